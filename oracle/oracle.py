@@ -1,0 +1,291 @@
+"""ctypes front-end of the CPU checkers.  TEST INFRASTRUCTURE ONLY.
+
+``Oracle``  loads oracle/_build/libtqoracle.so, the C restatement (tq_oracle.c).
+``RefLib``  loads oracle/_ref/libtqref.so, the reference's own CPU sources built
+            by oracle/Makefile (present only where the reference tree was
+            available at build time; it then travels with the built tree).
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs import
+this module.  The product library never does.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+sys.path.insert(0, os.path.join(ROOT, "tiny-llm_b200"))
+from tqb200 import abi  # noqa: E402
+
+ORACLE_SO = os.path.join(HERE, "_build", "libtqoracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libtqref.so")
+
+_f = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
+_u8 = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
+_u16 = np.ctypeslib.ndpointer(dtype=np.uint16, flags="C_CONTIGUOUS")
+_i32 = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
+_vp = C.c_void_p
+_i = C.c_int
+_fl = C.c_float
+
+
+def build_oracle(ref: bool = False) -> None:
+    """Compile the checkers (make -C oracle oracle [ref])."""
+    targets = ["oracle"] + (["ref"] if ref else [])
+    subprocess.check_call(["make", "-s", "-C", HERE, "-j8"] + targets)
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _u8a(a):
+    return np.ascontiguousarray(a, dtype=np.uint8)
+
+
+class _Common:
+    """Shared numpy-level wrappers; subclasses bind the C symbols."""
+
+    def matvec_i4(self, w, x, out_dim, in_dim, group_size):
+        y = np.zeros(out_dim, np.float32)
+        self._matvec_i4(_u8a(w), _f32(x), y, out_dim, in_dim, group_size)
+        return y
+
+    def matvec_vq2(self, w, x, out_dim, in_dim):
+        y = np.zeros(out_dim, np.float32)
+        self._matvec_vq2(_u8a(w), _f32(x), y, out_dim, in_dim)
+        return y
+
+    def matmul_i4(self, w, x_cols, M, K, N, group_size):
+        """x_cols: [N, K] (one token per row == column-major X[K, N]); returns [N, M]."""
+        y = np.zeros((N, M), np.float32)
+        self._matmul_i4(_u8a(w), _f32(x_cols), y, M, K, N, group_size)
+        return y
+
+    def biip_rotate(self, x, scale, sign, block_size):
+        x = _f32(x)
+        y = np.zeros_like(x)
+        self._biip(x, y, x.size, None if scale is None else _f32(scale).ctypes.data,
+                   _f32(sign).ctypes.data, block_size)
+        return y
+
+    def rmsnorm(self, x, w, eps):
+        x = _f32(x)
+        y = np.zeros_like(x)
+        self._rmsnorm(x, _f32(w), y, x.size, eps)
+        return y
+
+    def rope(self, q, k, n_heads, n_kv_heads, head_dim, pos, theta):
+        q = _f32(q).copy()
+        k = _f32(k).copy()
+        self._rope(q, k, n_heads, n_kv_heads, head_dim, pos, theta)
+        return q, k
+
+    def attention(self, q, kc, vc, seq_len, max_seq_len, n_heads, n_kv_heads, head_dim, scale):
+        out = np.zeros(n_heads * head_dim, np.float32)
+        self._attn(_f32(q), _f32(kc), _f32(vc), seq_len, max_seq_len, n_heads, n_kv_heads,
+                   head_dim, scale, out)
+        return out
+
+    def swiglu(self, g, u):
+        g = _f32(g).copy()
+        self._swiglu(g, _f32(u), g.size)
+        return g
+
+    def argmax(self, logits):
+        l = _f32(logits)
+        return int(self._argmax(l, l.size))
+
+    def topk_softmax(self, logits, k):
+        l = _f32(logits)
+        idx = np.zeros(k, np.int32)
+        w = np.zeros(k, np.float32)
+        self._topk(l, l.size, k, idx, w)
+        return idx, w
+
+
+class Oracle(_Common):
+    """The C restatement (oracle/tq_oracle.c)."""
+
+    def __init__(self, path: str = ORACLE_SO):
+        if not os.path.exists(path):
+            build_oracle()
+        L = C.CDLL(path)
+        self.lib = L
+
+        def sig(name, args, res=None):
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = res
+            return fn
+
+        self._matvec_i4 = sig("tqo_matvec_i4", [_u8, _f, _f, _i, _i, _i])
+        self._matvec_w4a8 = sig("tqo_matvec_i4_w4a8", [_u8, _f, _f, _i, _i, _i])
+        self._matmul_i4 = sig("tqo_matmul_i4", [_u8, _f, _f, _i, _i, _i, _i])
+        self._dequant = sig("tqo_dequant_i4", [_u8, _i, _i, _i, _f])
+        self._matvec_vq2 = sig("tqo_matvec_vq2", [_u8, _f, _f, _i, _i])
+        self._matvec_f32 = sig("tqo_matvec_f32", [_f, _f, _f, _i, _i])
+        self._biip = sig("tqo_biip_rotate", [_f, _f, _i, _vp, _vp, _i])
+        self._rmsnorm = sig("tqo_rmsnorm", [_f, _f, _f, _i, _fl])
+        self._rope = sig("tqo_rope", [_f, _f, _i, _i, _i, _i, _fl])
+        self._attn = sig("tqo_attention_decode", [_f, _f, _f, _i, _i, _i, _i, _i, _fl, _f])
+        self._attn16 = sig("tqo_attention_decode_f16kv",
+                           [_f, _u16, _u16, _i, _i, _i, _i, _i, _fl, _f])
+        self._swiglu = sig("tqo_swiglu", [_f, _f, _i])
+        self._argmax = sig("tqo_argmax", [_f, _i], _i)
+        self._topk = sig("tqo_topk_softmax", [_f, _i, _i, _i32, _f])
+        self._f2h = sig("tqo_float_to_half", [_fl], C.c_uint16)
+        self._h2f = sig("tqo_half_to_float", [C.c_uint16], _fl)
+        sig("tqo_set_threads", [_i])
+        sig("tqo_model_create", [C.POINTER(abi.ModelDesc), _i, _i], _vp)
+        sig("tqo_model_step", [_vp, _i], _i)
+        sig("tqo_model_logits", [_vp], C.POINTER(C.c_float))
+        sig("tqo_model_hidden", [_vp], C.POINTER(C.c_float))
+        sig("tqo_model_reset", [_vp])
+        sig("tqo_model_destroy", [_vp])
+        sig("tqo_model_set_partial", [_vp, _i, _i])
+
+    def set_threads(self, n: int):
+        self.lib.tqo_set_threads(n)
+
+    def matvec_i4_w4a8(self, w, x, out_dim, in_dim, group_size):
+        y = np.zeros(out_dim, np.float32)
+        self._matvec_w4a8(_u8a(w), _f32(x), y, out_dim, in_dim, group_size)
+        return y
+
+    def dequant_i4(self, w, rows, dim, group_size):
+        out = np.zeros((rows, dim), np.float32)
+        self._dequant(_u8a(w), rows, dim, group_size, out)
+        return out
+
+    def matvec_f32(self, w, x):
+        w = _f32(w)
+        y = np.zeros(w.shape[0], np.float32)
+        self._matvec_f32(w, _f32(x), y, w.shape[0], w.shape[1])
+        return y
+
+    def attention_f16kv(self, q, kc16, vc16, seq_len, max_seq_len, n_heads, n_kv_heads,
+                        head_dim, scale):
+        out = np.zeros(n_heads * head_dim, np.float32)
+        self._attn16(_f32(q), np.ascontiguousarray(kc16, np.uint16),
+                     np.ascontiguousarray(vc16, np.uint16), seq_len, max_seq_len, n_heads,
+                     n_kv_heads, head_dim, scale, out)
+        return out
+
+    def float_to_half(self, a) -> np.ndarray:
+        a = _f32(a).ravel()
+        return np.array([self._f2h(float(v)) for v in a], np.uint16)
+
+    def model(self, synth_model, max_seq_len: int, kv_fp16: bool = False) -> "OracleModel":
+        return OracleModel(self, synth_model, max_seq_len, kv_fp16)
+
+
+class OracleModel:
+    def __init__(self, orc: Oracle, sm, max_seq_len: int, kv_fp16: bool):
+        self.orc = orc
+        self.sm = sm  # keeps the weights alive
+        self.vocab = sm.spec.vocab
+        self.h = orc.lib.tqo_model_create(C.byref(sm.desc), max_seq_len, 1 if kv_fp16 else 0)
+
+    def step(self, token: int) -> int:
+        return int(self.orc.lib.tqo_model_step(self.h, token))
+
+    def logits(self) -> np.ndarray:
+        p = self.orc.lib.tqo_model_logits(self.h)
+        return np.ctypeslib.as_array(p, shape=(self.vocab,)).copy()
+
+    def set_partial(self, n_layers: int, head: bool):
+        self.orc.lib.tqo_model_set_partial(self.h, n_layers, 1 if head else 0)
+
+    def reset(self):
+        self.orc.lib.tqo_model_reset(self.h)
+
+    def close(self):
+        if self.h:
+            self.orc.lib.tqo_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+
+class RefLib(_Common):
+    """The reference's own CPU code (oracle/_ref/libtqref.so)."""
+
+    @staticmethod
+    def available(path: str = REF_SO) -> bool:
+        return os.path.exists(path)
+
+    def __init__(self, path: str = REF_SO):
+        L = C.CDLL(path)
+        self.lib = L
+
+        def sig(name, args, res=None):
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = res
+            return fn
+
+        self._matvec_i4 = sig("tqref_matvec_i4", [_u8, _f, _f, _i, _i, _i])
+        self._matmul_i4 = sig("tqref_matmul_i4", [_u8, _f, _f, _i, _i, _i, _i])
+        self._dequant_row = sig("tqref_dequant_i4_row", [_u8, _i, _i, _i, _f])
+        self._matvec_vq2 = sig("tqref_matvec_vq2", [_u8, _f, _f, _i, _i])
+        self._biip = sig("tqref_biip_rotate", [_f, _f, _i, _vp, _vp, _i])
+        self._rmsnorm = sig("tqref_rmsnorm", [_f, _f, _f, _i, _fl])
+        self._rope = sig("tqref_rope", [_f, _f, _i, _i, _i, _i, _fl])
+        self._attn = sig("tqref_attention_decode", [_f, _f, _f, _i, _i, _i, _i, _i, _fl, _f])
+        self._swiglu = sig("tqref_swiglu", [_f, _f, _i])
+        self._argmax = sig("tqref_argmax", [_f, _i], _i)
+        self._topk = sig("tqref_topk_softmax", [_f, _i, _i, _i32, _f])
+        self._f2h = sig("tqref_float_to_half", [_fl], C.c_uint16)
+        self._h2f = sig("tqref_half_to_float", [C.c_uint16], _fl)
+        sig("tqref_model_open", [C.c_char_p, _i, _i, C.c_char_p, _i], _vp)
+        sig("tqref_model_step", [_vp, _i], _i)
+        sig("tqref_model_logits", [_vp], C.POINTER(C.c_float))
+        sig("tqref_model_reset", [_vp])
+        sig("tqref_model_close", [_vp])
+
+    def dequant_i4(self, w, rows, dim, group_size):
+        out = np.zeros((rows, dim), np.float32)
+        w = _u8a(w)
+        row = np.zeros(dim, np.float32)
+        for r in range(rows):
+            self._dequant_row(w, r, dim, group_size, row)
+            out[r] = row
+        return out
+
+    def float_to_half(self, a) -> np.ndarray:
+        a = _f32(a).ravel()
+        return np.array([self._f2h(float(v)) for v in a], np.uint16)
+
+    def open_model(self, path: str, max_seq_len: int, vocab: int, kv_fp16: bool = False):
+        err = C.create_string_buffer(512)
+        h = self.lib.tqref_model_open(path.encode(), max_seq_len, 1 if kv_fp16 else 0, err, 512)
+        if not h:
+            raise RuntimeError("reference model load failed: " + err.value.decode())
+        return RefModelHandle(self, h, vocab)
+
+
+class RefModelHandle:
+    def __init__(self, lib: RefLib, h, vocab: int):
+        self.lib, self.h, self.vocab = lib, h, vocab
+
+    def step(self, token: int) -> int:
+        return int(self.lib.lib.tqref_model_step(self.h, token))
+
+    def logits(self) -> np.ndarray:
+        p = self.lib.lib.tqref_model_logits(self.h)
+        return np.ctypeslib.as_array(p, shape=(self.vocab,)).copy()
+
+    def close(self):
+        if self.h:
+            self.lib.lib.tqref_model_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
