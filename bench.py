@@ -1,0 +1,334 @@
+#!/usr/bin/env python3
+"""Benchmark of the tinyqwen quantised decode hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+Prints ONE JSON line (rank 0).  Workloads (synthetic seeded data of the
+BASELINE shapes):
+
+  matvec-i4   BASELINE config 1: i4 g64 matvec 4864x896.  A step is one CUDA-graph
+              replay of 64 launches, one per distinct copy of W (64 x 2.45 MB =
+              157 MB > the 126 MB L2, so every launch streams W from HBM).
+
+Timing: W warm-up steps, then K steps bracketed by a barrier and
+cudaDeviceSynchronize, CUDA events on the launching stream, max over ranks.
+nvidia-smi clocks are sampled during the timed region.  The oracle/_ref CPU
+build (the reference's own code) is timed on a bounded sample for
+``cpu_baseline``; ``--impl reference`` times only that.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "tiny-llm_b200"))
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+# ------------------------------------------------------------------ distributed plumbing
+def dist_init():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=None)
+        pg = dist
+    return world, rank, local, pg
+
+
+def barrier(pg):
+    if pg is not None:
+        pg.barrier()
+
+
+def max_over_ranks(pg, v: float) -> float:
+    if pg is None:
+        return v
+    import torch
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ CPU baseline
+def cpu_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def ref_matvec_rate(seconds: float, threads: int):
+    """Time the reference's matvec_i4_ref (oracle/_ref, the reference's own code) on
+    config 1, rows split across `threads` host threads.  Returns (GB/s, kind, sample)."""
+    from oracle.oracle import Oracle, RefLib
+    from tqb200 import synth
+    w, x = synth.config1_matvec(0)
+    M, K, G = 4864, 896, 64
+    rb = w.shape[1]
+    if RefLib.available():
+        lib, kind = RefLib(), "reference"
+        fn = lib._matvec_i4
+    else:
+        lib, kind = Oracle(), "port"
+        lib.set_threads(1)
+        fn = lib._matvec_i4
+    bounds = np.linspace(0, M, threads + 1).astype(int)
+    y = np.zeros(M, np.float32)
+
+    def one_call():
+        ts = []
+        for a, b in zip(bounds[:-1], bounds[1:]):
+            if b <= a:
+                continue
+            wa = np.ascontiguousarray(w[a:b])
+            ya = np.zeros(b - a, np.float32)
+            ts.append((wa, ya))
+        th = [threading.Thread(target=fn, args=(wa, x, ya, ya.size, K, G)) for wa, ya in ts]
+        t0 = time.perf_counter()
+        for t in th:
+            t.start()
+        for t in th:
+            t.join()
+        return time.perf_counter() - t0
+
+    one_call()
+    calls, spent = 0, 0.0
+    while spent < seconds:
+        spent += one_call()
+        calls += 1
+    bytes_per = M * rb + K * 4 + M * 4
+    gbs = bytes_per * calls / spent / 1e9
+    return gbs, kind, f"{calls} calls of matvec_i4_ref on config 1 (4864x896 g64) in {spent:.1f} s"
+
+
+# ------------------------------------------------------------------ workloads
+def bench_matvec(args, rank, pg, pk, pk_kind):
+    import torch
+    from tqb200 import lib, synth
+    tq = lib.load()
+    M, K, G = 4864, 896, 64
+    NCOPY = 64
+    w, x = synth.config1_matvec(0)
+    algo_bytes = w.nbytes + x.nbytes + M * 4
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(1)
+    ws = [torch.from_numpy(w).to(dev)]
+    for i in range(1, NCOPY):   # distinct copies (same distribution) so L2 never holds W
+        ws.append(torch.from_numpy(synth.random_i4(rng, M, K, G) if i < 4 else w).to(dev))
+    dx = torch.from_numpy(x).to(dev)
+    dy = torch.empty(M, device=dev)
+    stream = torch.cuda.Stream()
+    sp = stream.cuda_stream
+
+    def launch_all():
+        for wi in ws:
+            st = tq.tqb200_dev_matvec_i4(wi.data_ptr(), dx.data_ptr(), dy.data_ptr(), M, K, G, sp)
+            if st:
+                raise lib.TQB200Error(st, tq.tqb200_last_error().decode())
+
+    with torch.cuda.stream(stream):
+        launch_all()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        launch_all()
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
+    clocks.start()
+    barrier(pg)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(pg)
+    ms = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    ms = max_over_ranks(pg, ms)
+    ms_step = ms / args.steps
+    per_launch_s = ms_step / 1e3 / NCOPY
+    achieved = algo_bytes / per_launch_s / 1e9
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    value = achieved * world  # replicas: every rank streams its own copies
+
+    # e2e: the reference-facing host-pointer call (H2D of W and x, D2H of y per call)
+    e2e = None
+    if rank == 0:
+        tq.tqb200_set_resident_weights(0)
+        y = np.zeros(M, np.float32)
+        for _ in range(3):
+            lib.matvec_i4(w, x, M, K, G)
+        n = 50
+        t0 = time.perf_counter()
+        for _ in range(n):
+            st = tq.tqb200_matvec_i4(w, x, y, M, K, G)
+            assert st == 0
+        dt = (time.perf_counter() - t0) / n
+        e2e = {"value": algo_bytes / dt / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(w.nbytes + x.nbytes),
+               "d2h_bytes_per_step": int(M * 4), "note": "one tqb200_matvec_i4 host-pointer call per step"}
+    out = {
+        "metric": "i4 matvec HBM GB/s (BASELINE config 1, 4864x896 g64)",
+        "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u4 weights, f32 activations",
+        "data": "synthetic (seeded, BASELINE config 1 distributions)",
+        "config": {"workload": "matvec-i4 (config 1)", "rows": M, "cols": K, "group_size": G,
+                   "launches_per_step": NCOPY, "distinct_weight_copies": NCOPY,
+                   "l2": "inputs larger than L2 (64 distinct W copies, 157 MB)",
+                   "parallelism": f"replicas x{world}"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
+                     "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
+                     "traffic": None, "peak_source": pk_kind,
+                     "kernel": "i4_matvec_kernel<64,2>",
+                     "algorithmic_bytes_per_launch": int(algo_bytes)},
+        "clocks": clk,
+        "gpu_launches": NCOPY * args.steps,
+        "e2e": e2e,
+    }
+    return out
+
+
+def bench_reference_arm(args, rank):
+    """--impl reference: the reference's own CPU code on the host cores."""
+    if rank != 0:
+        return None
+    threads = cpu_threads()
+    gbs, kind, sample = ref_matvec_rate(max(2.0, 0.5 * args.steps), threads)
+    return {
+        "impl": "reference",
+        "metric": "i4 matvec HBM GB/s (BASELINE config 1, 4864x896 g64)",
+        "value": round(gbs, 4), "unit": "GB/s", "n_gpus": 0, "steps": args.steps,
+        "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "u4 weights, f32 activations (double accumulation)",
+        "data": "synthetic (seeded, BASELINE config 1 distributions)",
+        "config": {"workload": "matvec-i4 (config 1)", "rows": 4864, "cols": 896, "group_size": 64},
+        "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="matvec-i4")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    world, rank, local, pg = (int(os.environ.get("WORLD_SIZE", "1")),
+                              int(os.environ.get("RANK", "0")),
+                              int(os.environ.get("LOCAL_RANK", "0")), None)
+    if args.impl == "reference":
+        out = bench_reference_arm(args, rank)
+        if out is not None:
+            print(json.dumps(out), flush=True)
+        return
+
+    import torch
+    torch.cuda.set_device(local)
+    world, rank, local, pg = dist_init()
+    pk, pk_kind = peaks()
+    if args.workload == "matvec-i4":
+        out = bench_matvec(args, rank, pg, pk, pk_kind)
+    else:
+        raise SystemExit(f"unknown workload {args.workload}")
+    if rank == 0:
+        threads = cpu_threads()
+        gbs, kind, sample = ref_matvec_rate(args.cpu_seconds, 1)
+        out["cpu_baseline"] = {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": kind,
+                               "sample": sample + f" (host has {threads} threads)"}
+        print(json.dumps(out), flush=True)
+    if pg is not None:
+        pg.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,99 @@
+"""i4 matvec family on the GPU vs the oracle (max relative error, as
+benchmarks/bench_kernels.cpp:474-479 defines it).  Tolerance 1e-4: the
+north-star bound for fp32-accumulating kernels vs the double-accumulating
+reference.  Dequantised weights: bit-exact."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import golden_cases as gc
+from conftest import max_rel
+from tqb200 import synth
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-4
+
+
+@pytest.mark.parametrize("M,K,G", gc.I4_CASES + [(4864, 896, 64), (1, 64, 64), (7, 2560, 64),
+                                                 (300, 9728, 64), (129, 4096, 128), (5, 96, 32)])
+def test_matvec_i4_vs_oracle(tq, oracle, M, K, G):
+    rng = np.random.default_rng(M * 7 + K)
+    w = synth.random_i4(rng, M, K, G)
+    x = rng.normal(size=K).astype(np.float32)
+    y = tq.matvec_i4(w, x, M, K, G)
+    assert max_rel(y, oracle.matvec_i4(w, x, M, K, G)) < TOL
+
+
+def test_matvec_i4_golden_config1(tq, golden):
+    w, x = synth.config1_matvec(0)
+    assert max_rel(tq.matvec_i4(w, x, 4864, 896, 64), golden["cfg1_y"]) < TOL
+
+
+def test_matvec_i4_rtn_weights(tq, oracle):
+    rng = np.random.default_rng(5)
+    w = synth.quantize_i4_rtn(rng.normal(0, 0.02, (512, 2560)).astype(np.float32), 64)
+    x = rng.normal(size=2560).astype(np.float32)
+    assert max_rel(tq.matvec_i4(w, x, 512, 2560, 64), oracle.matvec_i4(w, x, 512, 2560, 64)) < TOL
+
+
+def test_pair_and_qkv_match_single(tq, oracle):
+    rng = np.random.default_rng(9)
+    K, G = 896, 64
+    wq, wk, wv = (synth.random_i4(rng, n, K, G) for n in (896, 128, 128))
+    x = rng.normal(size=K).astype(np.float32)
+    yq, yk, yv = tq.matvec_qkv_i4(wq, wk, wv, x, 896, 128, K, G)
+    assert max_rel(yq, oracle.matvec_i4(wq, x, 896, K, G)) < TOL
+    assert max_rel(yk, oracle.matvec_i4(wk, x, 128, K, G)) < TOL
+    assert max_rel(yv, oracle.matvec_i4(wv, x, 128, K, G)) < TOL
+    g1, g2 = synth.random_i4(rng, 4864, K, G), synth.random_i4(rng, 4864, K, G)
+    y1, y2 = tq.matvec_pair_i4(g1, g2, x, 4864, K, G)
+    assert max_rel(y1, oracle.matvec_i4(g1, x, 4864, K, G)) < TOL
+    assert max_rel(y2, oracle.matvec_i4(g2, x, 4864, K, G)) < TOL
+
+
+@pytest.mark.parametrize("M,K,G", gc.I4_CASES)
+def test_dequant_bit_exact(tq, golden, M, K, G):
+    w, x = gc.i4_case(M, K, G)
+    assert np.array_equal(tq.dequant_i4(w, M, K, G), golden[f"i4_{M}x{K}g{G}_deq"])
+
+
+def test_symmetric_w4a8_vs_naive(tq, oracle):
+    # tests/test_matvec_i4.cpp:441-477: sdot5 vs the symmetric W4A8 naive, abs err < 1e-4
+    rng = np.random.default_rng(9901)
+    for (M, K) in [(96, 384), (512, 896)]:
+        wf = rng.normal(size=(M, K)).astype(np.float32)
+        w = synth.quantize_i4_rtn(wf, 64, symmetric=True)
+        x = rng.normal(size=K).astype(np.float32)
+        y = tq.matvec_i4_sym(w, x, M, K, 64)
+        ref = oracle.matvec_i4_w4a8(w, x, M, K, 64)
+        assert np.abs(y.astype(np.float64) - ref).max() < 1e-4
+
+
+def test_resident_weight_cache(tq, oracle):
+    rng = np.random.default_rng(3)
+    w = synth.random_i4(rng, 256, 512, 64)
+    x = rng.normal(size=512).astype(np.float32)
+    tq.set_resident_weights(True)
+    try:
+        y1 = tq.matvec_i4(w, x, 256, 512, 64)
+        y2 = tq.matvec_i4(w, x, 256, 512, 64)
+        assert np.array_equal(y1, y2)
+        assert max_rel(y1, oracle.matvec_i4(w, x, 256, 512, 64)) < TOL
+    finally:
+        tq.set_resident_weights(False)
+        tq.clear_resident_weights()
+
+
+def test_device_pointer_path(tq, oracle):
+    import torch
+    rng = np.random.default_rng(4)
+    M, K, G = 2048, 2560, 64
+    w = synth.random_i4(rng, M, K, G)
+    x = rng.normal(size=K).astype(np.float32)
+    dw = torch.from_numpy(w).cuda()
+    dx = torch.from_numpy(x).cuda()
+    dy = torch.empty(M, device="cuda", dtype=torch.float32)
+    tq.dev_matvec_i4(dw.data_ptr(), dx.data_ptr(), dy.data_ptr(), M, K, G)
+    torch.cuda.synchronize()
+    assert max_rel(dy.cpu().numpy(), oracle.matvec_i4(w, x, M, K, G)) < TOL

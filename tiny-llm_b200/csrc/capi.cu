@@ -1,0 +1,306 @@
+// capi.cu — the extern "C" boundary of libtqb200.so (declared in include/tqb200.h).
+//
+// Host-pointer entry points mirror the reference's dispatch signatures
+// (kernels/dispatch.h) and are synchronous, like the reference's CPU
+// variants: upload, launch, download, synchronise.  Device-pointer twins
+// (tqb200_dev_*) are stream-ordered and never synchronise.
+#include <cstdarg>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace tqb200 {
+
+namespace {
+thread_local char g_err[1024] = "";
+}
+
+int set_error(int status, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+    return status;
+}
+
+// ------------------------------------------------------------------ device context
+namespace {
+
+struct DevBuf {
+    void *p = nullptr;
+    size_t cap = 0;
+};
+
+struct HostCtx {
+    int device = -1;
+    cudaStream_t stream = nullptr;
+    std::vector<DevBuf> scratch;                            // per-call argument slots
+    std::unordered_map<std::string, DevBuf> resident;       // (host ptr, bytes) -> device copy
+    bool resident_on = false;
+};
+
+std::mutex g_mu;
+HostCtx g_ctx;
+
+int ensure_device() {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return set_error(TQB200_ERR_NO_DEVICE, "no CUDA device visible");
+    }
+    int dev = 0;
+    TQ_CUDA_TRY(cudaGetDevice(&dev));
+    if (g_ctx.device != dev) {
+        if (g_ctx.stream) cudaStreamDestroy(g_ctx.stream);
+        for (auto &b : g_ctx.scratch)
+            if (b.p) cudaFree(b.p);
+        for (auto &kv : g_ctx.resident)
+            if (kv.second.p) cudaFree(kv.second.p);
+        g_ctx.scratch.clear();
+        g_ctx.resident.clear();
+        g_ctx.stream = nullptr;
+        g_ctx.device = dev;
+        TQ_CUDA_TRY(cudaStreamCreateWithFlags(&g_ctx.stream, cudaStreamNonBlocking));
+    }
+    return TQB200_OK;
+}
+
+// Growable device slot; contents undefined.  Allocations are 256-byte aligned.
+int scratch(int slot, size_t bytes, void **out) {
+    if ((int)g_ctx.scratch.size() <= slot) g_ctx.scratch.resize(slot + 1);
+    DevBuf &b = g_ctx.scratch[slot];
+    if (b.cap < bytes) {
+        if (b.p) cudaFree(b.p);
+        b.p = nullptr;
+        b.cap = 0;
+        const size_t cap = ((bytes + 255) / 256) * 256 + 256;
+        TQ_CUDA_TRY(cudaMalloc(&b.p, cap));
+        b.cap = cap;
+    }
+    *out = b.p;
+    return TQB200_OK;
+}
+
+int upload(int slot, const void *host, size_t bytes, void **dev) {
+    int st = scratch(slot, bytes ? bytes : 1, dev);
+    if (st) return st;
+    if (bytes) TQ_CUDA_TRY(cudaMemcpyAsync(*dev, host, bytes, cudaMemcpyHostToDevice, g_ctx.stream));
+    return TQB200_OK;
+}
+
+// Weight upload: resident cache keyed by (host pointer, size) when enabled.
+int upload_weight(int slot, const void *host, size_t bytes, void **dev) {
+    if (!g_ctx.resident_on) return upload(slot, host, bytes, dev);
+    char key[64];
+    snprintf(key, sizeof key, "%p:%zu", host, bytes);
+    auto it = g_ctx.resident.find(key);
+    if (it != g_ctx.resident.end()) {
+        *dev = it->second.p;
+        return TQB200_OK;
+    }
+    DevBuf b;
+    TQ_CUDA_TRY(cudaMalloc(&b.p, bytes + 256));
+    b.cap = bytes + 256;
+    TQ_CUDA_TRY(cudaMemcpy(b.p, host, bytes, cudaMemcpyHostToDevice));
+    g_ctx.resident[key] = b;
+    *dev = b.p;
+    return TQB200_OK;
+}
+
+int download(void *host, const void *dev, size_t bytes) {
+    if (bytes) TQ_CUDA_TRY(cudaMemcpyAsync(host, dev, bytes, cudaMemcpyDeviceToHost, g_ctx.stream));
+    return TQB200_OK;
+}
+
+int finish() {
+    TQ_CUDA_TRY(cudaStreamSynchronize(g_ctx.stream));
+    return TQB200_OK;
+}
+
+#define TQ_TRY(expr)            \
+    do {                        \
+        int s_ = (expr);        \
+        if (s_) return s_;      \
+    } while (0)
+
+size_t i4_bytes(int rows, int cols, int g) {
+    const size_t ng = (size_t)(cols + g - 1) / g;
+    return (size_t)rows * ng * (size_t)(4 + g / 2);
+}
+
+int check_i4(int rows, int cols, int g) {
+    TQ_CHECK_ARG(rows >= 0 && cols > 0, "bad i4 shape %d x %d", rows, cols);
+    TQ_CHECK_ARG(g > 0 && g % 2 == 0 && g <= 4096, "bad group_size %d", g);
+    return TQB200_OK;
+}
+
+}  // namespace
+}  // namespace tqb200
+
+using namespace tqb200;
+
+extern "C" {
+
+int tqb200_version(void) { return 10000; }
+
+const char *tqb200_last_error(void) { return g_err; }
+
+const char *tqb200_status_string(int status) {
+    switch (status) {
+        case TQB200_OK: return "ok";
+        case TQB200_ERR_INVALID_ARG: return "invalid argument";
+        case TQB200_ERR_CUDA: return "CUDA error";
+        case TQB200_ERR_UNSUPPORTED: return "unsupported";
+        case TQB200_ERR_NO_DEVICE: return "no CUDA device";
+        case TQB200_ERR_TIMEOUT: return "device wait timed out";
+        default: return "unknown status";
+    }
+}
+
+int tqb200_device_count(int *count) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+    }
+    if (count) *count = n;
+    return TQB200_OK;
+}
+
+int tqb200_set_resident_weights(int enabled) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    g_ctx.resident_on = enabled != 0;
+    return TQB200_OK;
+}
+
+int tqb200_clear_resident_weights(void) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    for (auto &kv : g_ctx.resident)
+        if (kv.second.p) cudaFree(kv.second.p);
+    g_ctx.resident.clear();
+    return TQB200_OK;
+}
+
+// ------------------------------------------------------------------ i4 (host pointers)
+int tqb200_matvec_i4(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim,
+                     int group_size) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    TQ_TRY(check_i4(out_dim, in_dim, group_size));
+    TQ_CHECK_ARG(w && x && y, "null pointer");
+    TQ_TRY(ensure_device());
+    void *dw, *dx, *dy;
+    TQ_TRY(upload_weight(0, w, i4_bytes(out_dim, in_dim, group_size), &dw));
+    TQ_TRY(upload(3, x, (size_t)in_dim * 4, &dx));
+    TQ_TRY(scratch(4, (size_t)out_dim * 4, &dy));
+    I4Job j{(const uint8_t *)dw, (float *)dy, nullptr, nullptr, out_dim};
+    TQ_TRY(launch_i4_matvec(&j, 1, (const float *)dx, in_dim, group_size, g_ctx.stream));
+    TQ_TRY(download(y, dy, (size_t)out_dim * 4));
+    return finish();
+}
+
+int tqb200_matvec_pair_i4(const uint8_t *w1, const uint8_t *w2, const float *x, float *y1,
+                          float *y2, int out_dim, int in_dim, int group_size) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    TQ_TRY(check_i4(out_dim, in_dim, group_size));
+    TQ_CHECK_ARG(w1 && w2 && x && y1 && y2, "null pointer");
+    TQ_TRY(ensure_device());
+    const size_t wb = i4_bytes(out_dim, in_dim, group_size);
+    void *dw1, *dw2, *dx, *dy1, *dy2;
+    TQ_TRY(upload_weight(0, w1, wb, &dw1));
+    TQ_TRY(upload_weight(1, w2, wb, &dw2));
+    TQ_TRY(upload(3, x, (size_t)in_dim * 4, &dx));
+    TQ_TRY(scratch(4, (size_t)out_dim * 4, &dy1));
+    TQ_TRY(scratch(5, (size_t)out_dim * 4, &dy2));
+    I4Job j[2] = {{(const uint8_t *)dw1, (float *)dy1, nullptr, nullptr, out_dim},
+                  {(const uint8_t *)dw2, (float *)dy2, nullptr, nullptr, out_dim}};
+    TQ_TRY(launch_i4_matvec(j, 2, (const float *)dx, in_dim, group_size, g_ctx.stream));
+    TQ_TRY(download(y1, dy1, (size_t)out_dim * 4));
+    TQ_TRY(download(y2, dy2, (size_t)out_dim * 4));
+    return finish();
+}
+
+int tqb200_matvec_qkv_i4(const uint8_t *wq, const uint8_t *wk, const uint8_t *wv,
+                         const float *x, float *yq, float *yk, float *yv, int q_dim, int kv_dim,
+                         int in_dim, int group_size) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    TQ_TRY(check_i4(q_dim, in_dim, group_size));
+    TQ_TRY(check_i4(kv_dim, in_dim, group_size));
+    TQ_CHECK_ARG(wq && wk && wv && x && yq && yk && yv, "null pointer");
+    TQ_TRY(ensure_device());
+    void *dq, *dk, *dv, *dx, *oq, *ok, *ov;
+    TQ_TRY(upload_weight(0, wq, i4_bytes(q_dim, in_dim, group_size), &dq));
+    TQ_TRY(upload_weight(1, wk, i4_bytes(kv_dim, in_dim, group_size), &dk));
+    TQ_TRY(upload_weight(2, wv, i4_bytes(kv_dim, in_dim, group_size), &dv));
+    TQ_TRY(upload(3, x, (size_t)in_dim * 4, &dx));
+    TQ_TRY(scratch(4, (size_t)q_dim * 4, &oq));
+    TQ_TRY(scratch(5, (size_t)kv_dim * 4, &ok));
+    TQ_TRY(scratch(6, (size_t)kv_dim * 4, &ov));
+    I4Job j[3] = {{(const uint8_t *)dq, (float *)oq, nullptr, nullptr, q_dim},
+                  {(const uint8_t *)dk, (float *)ok, nullptr, nullptr, kv_dim},
+                  {(const uint8_t *)dv, (float *)ov, nullptr, nullptr, kv_dim}};
+    TQ_TRY(launch_i4_matvec(j, 3, (const float *)dx, in_dim, group_size, g_ctx.stream));
+    TQ_TRY(download(yq, oq, (size_t)q_dim * 4));
+    TQ_TRY(download(yk, ok, (size_t)kv_dim * 4));
+    TQ_TRY(download(yv, ov, (size_t)kv_dim * 4));
+    return finish();
+}
+
+int tqb200_matvec_i4_sym(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim,
+                         int group_size) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    TQ_TRY(check_i4(out_dim, in_dim, group_size));
+    TQ_CHECK_ARG(w && x && y, "null pointer");
+    TQ_TRY(ensure_device());
+    void *dw, *dx, *dy;
+    TQ_TRY(upload_weight(0, w, i4_bytes(out_dim, in_dim, group_size), &dw));
+    TQ_TRY(upload(3, x, (size_t)in_dim * 4, &dx));
+    TQ_TRY(scratch(4, (size_t)out_dim * 4, &dy));
+    TQ_TRY(launch_i4_matvec_sym((const uint8_t *)dw, (const float *)dx, (float *)dy, out_dim,
+                                in_dim, group_size, g_ctx.stream));
+    TQ_TRY(download(y, dy, (size_t)out_dim * 4));
+    return finish();
+}
+
+int tqb200_dequant_i4(const uint8_t *w, int rows, int dim, int group_size, float *out) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    TQ_TRY(check_i4(rows, dim, group_size));
+    TQ_CHECK_ARG(w && out, "null pointer");
+    TQ_TRY(ensure_device());
+    void *dw, *dout;
+    TQ_TRY(upload_weight(0, w, i4_bytes(rows, dim, group_size), &dw));
+    TQ_TRY(scratch(4, (size_t)rows * dim * 4, &dout));
+    TQ_TRY(launch_i4_dequant((const uint8_t *)dw, rows, dim, group_size, (float *)dout,
+                             g_ctx.stream));
+    TQ_TRY(download(out, dout, (size_t)rows * dim * 4));
+    return finish();
+}
+
+// ------------------------------------------------------------------ i4 (device pointers)
+int tqb200_dev_matvec_i4(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim,
+                         int group_size, void *stream) {
+    TQ_TRY(check_i4(out_dim, in_dim, group_size));
+    TQ_CHECK_ARG(w && x && y, "null pointer");
+    I4Job j{w, y, nullptr, nullptr, out_dim};
+    return launch_i4_matvec(&j, 1, x, in_dim, group_size, (cudaStream_t)stream);
+}
+
+int tqb200_dev_matvec_i4_sym(const uint8_t *w, const float *x, float *y, int out_dim,
+                             int in_dim, int group_size, void *stream) {
+    TQ_TRY(check_i4(out_dim, in_dim, group_size));
+    TQ_CHECK_ARG(w && x && y, "null pointer");
+    return launch_i4_matvec_sym(w, x, y, out_dim, in_dim, group_size, (cudaStream_t)stream);
+}
+
+int tqb200_dev_dequant_i4(const uint8_t *w, int rows, int dim, int group_size, float *out,
+                          void *stream) {
+    TQ_TRY(check_i4(rows, dim, group_size));
+    TQ_CHECK_ARG(w && out, "null pointer");
+    return launch_i4_dequant(w, rows, dim, group_size, out, (cudaStream_t)stream);
+}
+
+}  // extern "C"
