@@ -271,11 +271,206 @@ def bench_matvec(args, rank, pg, pk, pk_kind):
     return out
 
 
+# ------------------------------------------------------------------ decode (config 4)
+DECODE_CTX = 4096
+
+
+def qwen3_4b_spec(max_seq: int):
+    from dataclasses import replace
+    from tqb200.model import QWEN3_4B
+    # random codes/scales/zeros (config-1 distributions) instead of RTN of N(0,0.02):
+    # same bytes and shapes, built in seconds
+    return replace(QWEN3_4B, weights="codes", max_seq_len=max_seq)
+
+
+def matvec_bytes_by_kind(spec) -> dict:
+    """Algorithmic bytes per decode step of every matvec kind: weights + x + y once."""
+    from tqb200.synth import i4_row_bytes
+    H, I, G = spec.hidden, spec.inter, spec.group_size
+    qd, kvd, L = spec.n_heads * spec.head_dim, spec.n_kv_heads * spec.head_dim, spec.n_layers
+
+    def mv(rows, cols):
+        return rows * i4_row_bytes(cols, G) + cols * 4 + rows * 4
+
+    return {"qkv": L * (mv(qd, H) + 2 * mv(kvd, H) - 2 * H * 4),
+            "o_proj": L * (mv(H, qd) + H * 4),               # + residual read
+            "gate_up": L * (2 * mv(I, H) - H * 4),
+            "down": L * (mv(H, I) + I * 4 + H * 4),           # + up read (SwiGLU) + residual
+            "lm_head": mv(spec.vocab, H)}
+
+
+def step_bytes(spec, ctx: int, kv_bytes: int) -> int:
+    mv = sum(matvec_bytes_by_kind(spec).values())
+    kv = 2 * spec.n_layers * spec.n_kv_heads * ctx * spec.head_dim * kv_bytes
+    return mv + kv
+
+
+def bench_decode(args, rank, pg, pk, pk_kind):
+    import torch
+    from tqb200 import lib
+    from tqb200.model import SynthModel
+    lib.load()
+    W, K = args.warmup, args.steps
+    ctx = args.ctx
+    max_seq = ctx + W + K + 8
+    spec = qwen3_4b_spec(max_seq)
+    t0 = time.time()
+    sm = SynthModel(spec, seed=0)
+    t_build = time.time() - t0
+    eng = lib.Engine(sm, max_seq_len=max_seq, kv_fp16=True)
+    del sm.tensors  # host copy no longer needed
+    # KV for context 4096: run the engine itself over positions 0..4095-W (greedy from token 1)
+    rng = np.random.default_rng(1)
+    first = int(rng.integers(0, spec.vocab))
+    toks, _ = eng.generate(first, ctx - W)
+    tok = toks[-1]
+    toks, _ = eng.generate(tok, W)   # warm-up steps (also captures the graph)
+    tok = toks[-1]
+    torch.cuda.synchronize()
+    clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
+    clocks.start()
+    barrier(pg)
+    torch.cuda.synchronize()
+    toks, dev_ms = eng.generate(tok, K)  # K steps at context 4096.., device-timed
+    torch.cuda.synchronize()
+    barrier(pg)
+    clk = clocks.stop()
+    dev_ms = max_over_ranks(pg, dev_ms)
+    ms_step = dev_ms / K
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+
+    # e2e: the C-ABI step call with host token in / host token out, every step
+    tok = toks[-1]
+    eng_steps = []
+    for _ in range(3):
+        tok = eng.step(tok)
+    n_e2e = min(K, 16)
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        tok = eng.step(tok)
+    e2e_ms = (time.perf_counter() - t0) * 1e3 / n_e2e
+    # live per-kernel times (one step launched kernel by kernel, CUDA events)
+    _, prof = eng.profile_step(tok)
+    mvb = matvec_bytes_by_kind(spec)
+    mv_ms = sum(prof[k] for k in mvb)
+    mv_bytes = sum(mvb.values())
+    achieved = mv_bytes / (mv_ms * 1e-3) / 1e9
+    total_bytes = step_bytes(spec, ctx, 2)
+    launches = 2 + 6 * spec.n_layers + 1  # + the device-side token feed
+    out = {
+        "metric": "decode ms/token, batch 1 (BASELINE config 4: Qwen3-4B-shaped i4 g64, fp16 KV, ctx 4096)",
+        "value": round(ms_step, 4), "unit": "ms/token", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": round(ms_step, 4), "higher_is_better": False, "scaling": "strong",
+        "vs_baseline": None, "dtype": "u4 weights, f32 activations, f16 KV",
+        "data": "synthetic (seeded random i4 codes/scales/zeros; KV filled by the engine's own "
+                "greedy decode over 4096 positions)",
+        "config": {"workload": "decode-qwen3-4b (config 4)", "layers": spec.n_layers,
+                   "hidden": spec.hidden, "inter": spec.inter, "heads": spec.n_heads,
+                   "kv_heads": spec.n_kv_heads, "head_dim": spec.head_dim, "vocab": spec.vocab,
+                   "context": ctx, "global_batch": 1,
+                   "l2": "inputs larger than L2 (%.2f GB read per step)" % (total_bytes / 1e9),
+                   "parallelism": "single GPU" if world == 1 else f"tp{world}",
+                   "bytes_per_step": int(total_bytes),
+                   "hbm_floor_ms": round(total_bytes / (pk["hbm_gbs"] * 1e9) * 1e3, 4),
+                   "model_build_s": round(t_build, 1)},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
+                     "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
+                     "peak_source": pk_kind, "kernel": "i4_mv_tma_kernel (all matvecs of a step)",
+                     "algorithmic_bytes_per_step": int(mv_bytes),
+                     "matvec_ms_per_step": round(mv_ms, 4),
+                     "step_vs_hbm_floor": round((total_bytes / (pk["hbm_gbs"] * 1e9) * 1e3) / ms_step, 4)},
+        "kernel_ms_by_kind": {k: round(v, 4) for k, v in prof.items()},
+        "clocks": clk,
+        "gpu_launches": launches * K,
+        "e2e": {"value": round(e2e_ms, 4), "unit": "ms/token", "h2d_bytes_per_step": 8,
+                "d2h_bytes_per_step": 8,
+                "note": "tqb200_engine_step per token: token+position H2D, next token+status D2H"},
+    }
+    eng.close()
+    return out
+
+
+def ref_decode_rate(threads_note: str = ""):
+    """Reference CPU decode cost per token for config 4 (oracle/_ref: the reference's own
+    QwenModel::forward_token and attention_decode_ref), bounded sample: 2- and 4-layer
+    models of the Qwen3-4B shape give the per-layer and head costs (the step is a sum over
+    layers plus the head, so it extrapolates exactly in layers); attention at context 4096
+    is timed separately with attention_decode_ref and added per layer."""
+    import tempfile
+    from dataclasses import replace
+    from oracle.oracle import Oracle, RefLib
+    from tqb200.model import SynthModel
+    base = qwen3_4b_spec(64)
+    have_ref = RefLib.available()
+    times = {}
+    with tempfile.TemporaryDirectory() as td:
+        for nl in (2, 6):
+            spec = replace(base, n_layers=nl)
+            sm = SynthModel(spec, seed=0)
+            if have_ref:
+                ref = RefLib()
+                path = os.path.join(td, f"m{nl}.tqwen")
+                sm.write_tqwen(path)
+                m = ref.open_model(path, 64, spec.vocab, False)
+            else:
+                orc = Oracle()
+                orc.set_threads(1)
+                m = orc.model(sm, 64, False)
+            m.step(1)
+            best = float("inf")
+            for i in range(3):
+                t0 = time.perf_counter()
+                m.step(2 + i)
+                best = min(best, time.perf_counter() - t0)
+            times[nl] = best
+            m.close()
+            del sm
+    t_layer = (times[6] - times[2]) / 4
+    t_head = times[2] - 2 * t_layer
+    # attention over the 4096-position KV of one layer vs the 4-position one above
+    lib = RefLib() if have_ref else Oracle()
+    H, KVH, hd = base.n_heads, base.n_kv_heads, base.head_dim
+    rng = np.random.default_rng(0)
+    q = rng.normal(size=H * hd).astype(np.float32)
+    kc = rng.normal(size=KVH * DECODE_CTX * hd).astype(np.float32)
+    vc = rng.normal(size=KVH * DECODE_CTX * hd).astype(np.float32)
+    t0 = time.perf_counter()
+    lib.attention(q, kc, vc, DECODE_CTX, DECODE_CTX, H, KVH, hd, 0.088)
+    t_attn = time.perf_counter() - t0
+    total = t_head + base.n_layers * (t_layer + t_attn)
+    kind = "reference" if have_ref else "port"
+    sample = (f"forward_token of 2- and 6-layer Qwen3-4B-shaped i4 models at context ~4 "
+              f"(best of 3: {times[2]*1e3:.0f} / {times[6]*1e3:.0f} ms per token) extrapolated to 36 layers, "
+              f"plus attention_decode_ref at context 4096 ({t_attn*1e3:.1f} ms per layer); 1 thread "
+              f"(the reference's x86 kernels are single-threaded){threads_note}")
+    return total * 1e3, kind, sample
+
+
 def bench_reference_arm(args, rank):
     """--impl reference: the reference's own CPU code on the host cores."""
     if rank != 0:
         return None
     threads = cpu_threads()
+    if args.workload.startswith("decode"):
+        per = []
+        for _ in range(max(1, min(args.steps, 2))):
+            ms, kind, sample = ref_decode_rate()
+            per.append(ms)
+        ms = float(np.median(per))
+        return {
+            "impl": "reference",
+            "metric": "decode ms/token, batch 1 (BASELINE config 4: Qwen3-4B-shaped i4 g64, fp16 KV, ctx 4096)",
+            "value": round(ms, 2), "unit": "ms/token", "n_gpus": 0, "steps": len(per),
+            "warmup": 0, "ms_per_step": round(ms, 2), "higher_is_better": False,
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": "u4 weights, f32 activations (double accumulation), f32 KV",
+            "data": "synthetic (seeded random i4 codes/scales/zeros)",
+            "config": {"workload": "decode-qwen3-4b (config 4)", "context": DECODE_CTX},
+            "cpu_baseline": {"value": round(ms, 2), "unit": "ms/token", "cores": 1, "kind": kind,
+                             "sample": sample + f"; host has {threads} threads"},
+            "e2e": {"value": round(ms, 2), "unit": "ms/token", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+        }
     gbs, kind, sample = ref_matvec_rate(max(2.0, 0.5 * args.steps), threads)
     return {
         "impl": "reference",
@@ -297,9 +492,11 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="matvec-i4")
+    ap.add_argument("--workload", default="decode-qwen3-4b",
+                    choices=["decode-qwen3-4b", "matvec-i4"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ctx", type=int, default=DECODE_CTX, help="decode context (KV positions)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -319,12 +516,17 @@ def main():
     if args.workload == "matvec-i4":
         out = bench_matvec(args, rank, pg, pk, pk_kind)
     else:
-        raise SystemExit(f"unknown workload {args.workload}")
+        out = bench_decode(args, rank, pg, pk, pk_kind)
     if rank == 0:
         threads = cpu_threads()
-        gbs, kind, sample = ref_matvec_rate(args.cpu_seconds, 1)
-        out["cpu_baseline"] = {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": kind,
-                               "sample": sample + f" (host has {threads} threads)"}
+        if args.workload == "matvec-i4":
+            gbs, kind, sample = ref_matvec_rate(args.cpu_seconds, 1)
+            out["cpu_baseline"] = {"value": round(gbs, 4), "unit": "GB/s", "cores": 1,
+                                   "kind": kind, "sample": sample + f" (host has {threads} threads)"}
+        elif args.cpu_seconds > 0:
+            ms, kind, sample = ref_decode_rate(f"; host has {threads} threads")
+            out["cpu_baseline"] = {"value": round(ms, 2), "unit": "ms/token", "cores": 1,
+                                   "kind": kind, "sample": sample}
         print(json.dumps(out), flush=True)
     if pg is not None:
         pg.destroy_process_group()

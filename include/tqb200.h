@@ -81,6 +81,85 @@ int tqb200_dev_matvec_i4_sym(const uint8_t *w, const float *x, float *y, int out
 int tqb200_dev_dequant_i4(const uint8_t *w, int rows, int dim, int group_size, float *out,
                           void *stream);
 
+/* -------------------------------------------------- decode ops (host pointers)
+ * Same signatures and meaning as the reference's ops dispatch entries
+ * (kernels/dispatch.h:298-307, shared --ops-impl name); status instead of abort. */
+
+/* RmsnormFn (kernels/dispatch.h:298); rmsnorm_ref, kernels/rmsnorm/rmsnorm_ref.cpp:48-78. In-place safe. */
+int tqb200_rmsnorm(const float *x, const float *weight, float *y, int n, float eps);
+/* RopeFn (kernels/dispatch.h:299); rope_ref, kernels/rope/rope_ref.cpp:56-117.  q, k in place. */
+int tqb200_rope(float *q, float *k, int n_heads, int n_kv_heads, int head_dim, int pos,
+                float theta);
+/* AttentionDecodeFn (kernels/dispatch.h:301); attention_decode_ref,
+ * kernels/attention/attention_decode_ref.cpp:53-143.  k/v: one layer, [KVH][max_seq_len][hd]. */
+int tqb200_attention_decode(const float *q, const float *k_cache, const float *v_cache,
+                            int seq_len, int max_seq_len, int n_heads, int n_kv_heads,
+                            int head_dim, float scale, float *out);
+/* IBackend::attention_decode_f16kv (runtime/backend.h:246-249): fp16 (binary16 bits) KV. */
+int tqb200_attention_decode_f16kv(const float *q, const uint16_t *k_cache,
+                                  const uint16_t *v_cache, int seq_len, int max_seq_len,
+                                  int n_heads, int n_kv_heads, int head_dim, float scale,
+                                  float *out);
+/* SwigluFn (kernels/dispatch.h:304); swiglu_ref, kernels/silu/swiglu_ref.cpp:41-52.  gate in place. */
+int tqb200_swiglu(float *gate, const float *up, int n);
+/* ArgmaxFn (kernels/dispatch.h:305) returns the index; here via *index (first maximum). */
+int tqb200_argmax(const float *logits, int n, int *index);
+/* TopKSoftmaxFn (kernels/dispatch.h:306); topk_softmax_ref,
+ * kernels/topk_softmax/topk_softmax_ref.cpp:41-78 (n <= 1024, k <= 64; ties -> lower index). */
+int tqb200_topk_softmax(const float *gate_logits, int n, int k, int *indices, float *weights);
+
+/* -------------------------------------------------- whole-step decode engine
+ * Replaces the GPU decode registry entry (GpuDecodeCreateFn / StepFn / ResetFn /
+ * DestroyFn / LogitsFn, kernels/dispatch.h:353-378; the reference's engine is
+ * kernels/cuda/gpu_engine.cu).  create() takes a tqb200_model_desc instead of a
+ * ModelFile; the adapter builds one from the ModelFile's tensor table.  The
+ * engine owns device copies of every weight, the KV arena and activations; a
+ * step runs one CUDA graph and returns the greedy next token
+ * (QwenModel::forward_token, runtime/qwen_forward_token.cpp:83-742). */
+typedef struct tqb200_engine tqb200_engine;
+
+typedef struct tqb200_engine_opts {
+    int max_seq_len;   /* KV positions (<= desc->max_seq_len when that is > 0) */
+    int kv_fp16;       /* 0 = fp32 KV (reference default), 1 = fp16 KV (RNE store, --kv-f16) */
+    int use_graph;     /* capture the step once and replay it (default 1) */
+    int pdl;           /* programmatic dependent launch between kernels (default 1) */
+    int device;        /* CUDA device ordinal; -1 = current */
+    int reserved[11];
+} tqb200_engine_opts;
+
+void tqb200_engine_default_opts(tqb200_engine_opts *opts);
+/* GpuDecodeCreateFn (kernels/dispatch.h:356). */
+int tqb200_engine_create(const tqb200_model_desc *desc, const tqb200_engine_opts *opts,
+                         tqb200_engine **out);
+/* GpuDecodeStepFn (kernels/dispatch.h:358): feeds token_id at the current position. */
+int tqb200_engine_step(tqb200_engine *e, int token_id, int *next_token);
+/* Greedy-decodes n_steps tokens with the produced token fed back on the device (no
+ * host round trip per token; main.cpp's decode loop, runtime/main.cpp:1038-1041, moved
+ * onto the GPU): step i feeds the token of step i-1, the first feeds token_id.
+ * out_tokens[n_steps] receives the produced ids; *device_ms (optional) the CUDA-event
+ * time of the n graph launches. */
+int tqb200_engine_generate(tqb200_engine *e, int token_id, int n_steps, int *out_tokens,
+                           float *device_ms);
+/* One step launched kernel by kernel (no graph, no PDL) with a CUDA event after every
+ * launch; ms_by_kind[k] sums the kernel time per kind: 0 embed, 1 qkv, 2 qk-norm/rope/
+ * kv-append, 3 attention, 4 o_proj, 5 gate/up, 6 down, 7 lm_head(+argmax). */
+int tqb200_engine_profile_step(tqb200_engine *e, int token_id, float *ms_by_kind, int n_kinds,
+                               int *next_token);
+/* GpuDecodeResetFn (kernels/dispatch.h:359): rewinds the position to 0. */
+int tqb200_engine_reset(tqb200_engine *e);
+/* GpuDecodeDestroyFn (kernels/dispatch.h:360). */
+int tqb200_engine_destroy(tqb200_engine *e);
+/* GpuDecodeLogitsFn (kernels/dispatch.h:361): DEVICE pointer to [vocab] logits. */
+const float *tqb200_engine_logits(const tqb200_engine *e);
+int tqb200_engine_copy_logits(const tqb200_engine *e, float *host, int n);
+int tqb200_engine_position(const tqb200_engine *e);
+/* Sets the position of the next step (positions below it must already hold KV). */
+int tqb200_engine_set_position(tqb200_engine *e, int pos);
+/* The engine's CUDA stream and KV arena ([K|V][L][KVH][max_seq][hd]), for harnesses. */
+int tqb200_engine_stream(const tqb200_engine *e, void **stream);
+int tqb200_engine_kv_cache(const tqb200_engine *e, void **kv, size_t *bytes);
+int tqb200_engine_weight_bytes(const tqb200_engine *e, size_t *bytes);
+
 #ifdef __cplusplus
 }
 #endif

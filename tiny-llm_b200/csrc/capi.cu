@@ -303,4 +303,149 @@ int tqb200_dev_dequant_i4(const uint8_t *w, int rows, int dim, int group_size, f
     return launch_i4_dequant(w, rows, dim, group_size, out, (cudaStream_t)stream);
 }
 
+// ------------------------------------------------------------------ decode ops (host pointers)
+int tqb200_rmsnorm(const float *x, const float *weight, float *y, int n, float eps) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    TQ_CHECK_ARG(x && weight && y && n > 0, "rmsnorm: bad arguments");
+    TQ_TRY(ensure_device());
+    void *dx, *dw;
+    TQ_TRY(upload(3, x, (size_t)n * 4, &dx));
+    TQ_TRY(upload(7, weight, (size_t)n * 4, &dw));
+    TQ_TRY(launch_rmsnorm((const float *)dx, (const float *)dw, (float *)dx, 1, n, eps,
+                          g_ctx.stream));
+    TQ_TRY(download(y, dx, (size_t)n * 4));
+    return finish();
+}
+
+int tqb200_rope(float *q, float *k, int n_heads, int n_kv_heads, int head_dim, int pos,
+                float theta) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    TQ_CHECK_ARG(q && k && n_heads >= 0 && n_kv_heads >= 0 && head_dim > 0 && pos >= 0,
+                 "rope: bad arguments");
+    TQ_TRY(ensure_device());
+    void *dq, *dk;
+    const size_t qb = (size_t)n_heads * head_dim * 4, kb = (size_t)n_kv_heads * head_dim * 4;
+    TQ_TRY(upload(3, q, qb, &dq));
+    TQ_TRY(upload(7, k, kb, &dk));
+    TQ_TRY(launch_rope((float *)dq, (float *)dk, n_heads, n_kv_heads, head_dim, pos, theta,
+                       g_ctx.stream));
+    TQ_TRY(download(q, dq, qb));
+    TQ_TRY(download(k, dk, kb));
+    return finish();
+}
+
+static int attention_host(const float *q, const void *kc, const void *vc, int elem, int seq_len,
+                          int max_seq_len, int n_heads, int n_kv_heads, int head_dim,
+                          float scale, float *out) {
+    TQ_CHECK_ARG(q && kc && vc && out, "attention: null pointer");
+    TQ_CHECK_ARG(seq_len >= 1 && seq_len <= max_seq_len && n_kv_heads > 0 &&
+                     n_heads % n_kv_heads == 0 && head_dim > 0,
+                 "attention: bad shape seq %d max %d heads %d/%d hd %d", seq_len, max_seq_len,
+                 n_heads, n_kv_heads, head_dim);
+    TQ_TRY(ensure_device());
+    // only the first seq_len positions of every KV head travel: [KVH][seq_len][hd]
+    const size_t row = (size_t)seq_len * head_dim * elem, pitch = (size_t)max_seq_len * head_dim * elem;
+    void *dq, *dk, *dv, *dout, *dpart, *dtick;
+    TQ_TRY(upload(3, q, (size_t)n_heads * head_dim * 4, &dq));
+    TQ_TRY(scratch(8, row * n_kv_heads, &dk));
+    TQ_TRY(scratch(9, row * n_kv_heads, &dv));
+    TQ_CUDA_TRY(cudaMemcpy2DAsync(dk, row, kc, pitch, row, n_kv_heads, cudaMemcpyHostToDevice,
+                                  g_ctx.stream));
+    TQ_CUDA_TRY(cudaMemcpy2DAsync(dv, row, vc, pitch, row, n_kv_heads, cudaMemcpyHostToDevice,
+                                  g_ctx.stream));
+    AttnArgs a{};
+    a.q = (const float *)dq;
+    a.k = dk;
+    a.v = dv;
+    a.kv_fp16 = elem == 2;
+    a.pos = nullptr;
+    a.seq_len = seq_len;
+    a.max_seq = seq_len;  // the device copy is packed to seq_len positions per head
+    a.n_heads = n_heads;
+    a.n_kv_heads = n_kv_heads;
+    a.head_dim = head_dim;
+    a.scale = scale;
+    TQ_TRY(attn_plan(n_kv_heads, seq_len, &a.nsplit, &a.chunk_max));
+    TQ_TRY(scratch(10, attn_partial_floats(n_heads, head_dim, a.nsplit) * 4, &dpart));
+    if ((int)g_ctx.scratch.size() <= 11 || g_ctx.scratch[11].cap < (size_t)n_kv_heads * 4) {
+        TQ_TRY(scratch(11, (size_t)n_kv_heads * 4, &dtick));
+        TQ_CUDA_TRY(cudaMemsetAsync(dtick, 0, g_ctx.scratch[11].cap, g_ctx.stream));
+    }
+    dtick = g_ctx.scratch[11].p;
+    TQ_TRY(scratch(4, (size_t)n_heads * head_dim * 4, &dout));
+    a.partial = (float *)dpart;
+    a.tickets = (unsigned int *)dtick;
+    a.out = (float *)dout;
+    TQ_TRY(launch_attention(a, g_ctx.stream));
+    TQ_TRY(download(out, dout, (size_t)n_heads * head_dim * 4));
+    return finish();
+}
+
+int tqb200_attention_decode(const float *q, const float *k_cache, const float *v_cache,
+                            int seq_len, int max_seq_len, int n_heads, int n_kv_heads,
+                            int head_dim, float scale, float *out) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    return attention_host(q, k_cache, v_cache, 4, seq_len, max_seq_len, n_heads, n_kv_heads,
+                          head_dim, scale, out);
+}
+
+int tqb200_attention_decode_f16kv(const float *q, const uint16_t *k_cache,
+                                  const uint16_t *v_cache, int seq_len, int max_seq_len,
+                                  int n_heads, int n_kv_heads, int head_dim, float scale,
+                                  float *out) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    return attention_host(q, k_cache, v_cache, 2, seq_len, max_seq_len, n_heads, n_kv_heads,
+                          head_dim, scale, out);
+}
+
+int tqb200_swiglu(float *gate, const float *up, int n) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    TQ_CHECK_ARG(gate && up && n >= 0, "swiglu: bad arguments");
+    if (n == 0) return TQB200_OK;
+    TQ_TRY(ensure_device());
+    void *dg, *du;
+    TQ_TRY(upload(3, gate, (size_t)n * 4, &dg));
+    TQ_TRY(upload(7, up, (size_t)n * 4, &du));
+    TQ_TRY(launch_swiglu((float *)dg, (const float *)du, n, g_ctx.stream));
+    TQ_TRY(download(gate, dg, (size_t)n * 4));
+    return finish();
+}
+
+int tqb200_argmax(const float *logits, int n, int *index) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    TQ_CHECK_ARG(logits && index && n > 0, "argmax: bad arguments");
+    TQ_TRY(ensure_device());
+    void *dl, *pv, *pi, *dt, *dout;
+    TQ_TRY(upload(3, logits, (size_t)n * 4, &dl));
+    const int nb = argmax_blocks(n);
+    TQ_TRY(scratch(12, (size_t)nb * 4, &pv));
+    TQ_TRY(scratch(13, (size_t)nb * 4, &pi));
+    if ((int)g_ctx.scratch.size() <= 14 || g_ctx.scratch[14].p == nullptr) {
+        TQ_TRY(scratch(14, 64, &dt));
+        TQ_CUDA_TRY(cudaMemsetAsync(dt, 0, 64, g_ctx.stream));
+    }
+    dt = g_ctx.scratch[14].p;
+    dout = (char *)dt + 16;
+    TQ_TRY(launch_argmax((const float *)dl, n, (float *)pv, (int *)pi, (unsigned int *)dt,
+                         (int *)dout, g_ctx.stream));
+    TQ_TRY(download(index, dout, 4));
+    return finish();
+}
+
+int tqb200_topk_softmax(const float *gate_logits, int n, int k, int *indices, float *weights) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    TQ_CHECK_ARG(gate_logits && indices && weights, "topk_softmax: null pointer");
+    if (k <= 0 || n <= 0) return TQB200_OK;  // the reference returns without writing
+    TQ_CHECK_ARG(n <= 1024 && k <= 64, "topk_softmax: n %d k %d beyond 1024/64", n, k);
+    TQ_TRY(ensure_device());
+    void *dl, *di, *dw;
+    TQ_TRY(upload(3, gate_logits, (size_t)n * 4, &dl));
+    TQ_TRY(scratch(4, (size_t)k * 4, &di));
+    TQ_TRY(scratch(5, (size_t)k * 4, &dw));
+    TQ_TRY(launch_topk_softmax((const float *)dl, n, k, (int *)di, (float *)dw, g_ctx.stream));
+    TQ_TRY(download(indices, di, (size_t)k * 4));
+    TQ_TRY(download(weights, dw, (size_t)k * 4));
+    return finish();
+}
+
 }  // extern "C"

@@ -113,11 +113,12 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
                  : "memory");
 }
 
-// Returns true once the phase with the given parity has completed, false after
-// `max_polls` unsuccessful polls (the caller records an error and stops).
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t max_polls) {
+// Returns true once the phase with the given parity has completed, false when
+// `max_cycles` SM clock cycles pass first (the caller records an error and stops).
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, long long max_cycles) {
     const uint32_t a = smem_u32(bar);
-    for (uint32_t i = 0; i < max_polls; ++i) {
+    const long long t0 = clock64();
+    while (true) {
         uint32_t done;
         asm volatile(
             "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
@@ -126,8 +127,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32
             : "r"(a), "r"(parity)
             : "memory");
         if (done) return true;
+        if (clock64() - t0 > max_cycles) return false;
     }
-    return false;
+}
+
+// ~1 s at B200 clocks: no legitimate wait on a bulk copy comes near it.
+constexpr long long kWaitCycles = 2000000000LL;
+
+// Programmatic dependent launch (sm_90+): no-ops when launched without the attribute.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+__device__ __forceinline__ uint32_t lds_u32(const uint8_t *p) {
+    return *reinterpret_cast<const uint32_t *>(p);
 }
 
 __device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gmem_src, uint32_t bytes,
@@ -139,11 +151,7 @@ __device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gmem_src, u
         : "memory");
 }
 
-// Device-side error word shared by kernels that can time out: the first failing
-// kernel stores its code; the host reads it after synchronising.
-struct DeviceStatus {
-    int code;     // 0 = ok
-    int where;    // kernel-specific detail
-};
+// Device error codes written to an int status word by kernels with bounded waits.
+enum : int { kDevOk = 0, kDevTimeoutTma = 1 };
 
 }  // namespace tqb200

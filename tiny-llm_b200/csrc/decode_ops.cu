@@ -1,0 +1,572 @@
+// decode_ops.cu — the non-matvec ops of one decode step, sm_100a.
+//
+//   rmsnorm        rmsnorm_ref          kernels/rmsnorm/rmsnorm_ref.cpp:48-78
+//   rope           rope_ref             kernels/rope/rope_ref.cpp:56-117
+//   qk-norm+rope+kv-append (engine)     runtime/qwen_forward_token.cpp:423-446,
+//                                       runtime/kv_cache.cpp:120-135
+//   attention      attention_decode_ref kernels/attention/attention_decode_ref.cpp:53-143
+//                  (fp16 KV: the same math on decoded halves)
+//   swiglu         swiglu_ref           kernels/silu/swiglu_ref.cpp:41-52
+//   argmax         argmax_ref           kernels/argmax/argmax_ref.cpp:42-54
+//   topk_softmax   topk_softmax_ref     kernels/topk_softmax/topk_softmax_ref.cpp:41-78
+//   embed          qwen_forward_token.cpp:121-164 (f32 copy / f16 decode / i4 dequant row)
+//
+// Rounding: where the reference rounds in fp32 the kernels use the _rn
+// intrinsics so nvcc cannot contract a multiply and an add into an FMA the
+// reference does not perform; reductions the reference does in double are
+// done in double.  Transcendentals call CUDA's expf/powf/cosf/sinf (full
+// precision, never the fast intrinsics), so those ops agree to a few ulp.
+#include <float.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace tqb200 {
+
+namespace {
+
+__device__ __forceinline__ double block_sum_d(double v, double *sh) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    v = warp_sum_d(v);
+    __syncthreads();
+    if (lane == 0) sh[warp] = v;
+    __syncthreads();
+    double r = 0.0;
+    if (warp == 0) {
+        r = lane < nw ? sh[lane] : 0.0;
+        r = warp_sum_d(r);
+        if (lane == 0) sh[0] = r;
+    }
+    __syncthreads();
+    return sh[0];
+}
+
+// y = rmsnorm(x) * w over `rows` independent rows of n (one CTA per row).
+__global__ void rmsnorm_rows_kernel(const float *__restrict__ x, const float *__restrict__ w,
+                                    float *__restrict__ y, int n, float eps) {
+    __shared__ double sh[32];
+    const float *xr = x + (size_t)blockIdx.x * n;
+    float *yr = y + (size_t)blockIdx.x * n;
+    double ss = 0.0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const double v = (double)xr[i];
+        ss += v * v;
+    }
+    ss = block_sum_d(ss, sh);
+    const float mean_sq = (float)(ss / n);
+    const float scale = 1.0f / sqrtf(__fadd_rn(mean_sq, eps));
+    for (int i = threadIdx.x; i < n; i += blockDim.x) yr[i] = __fmul_rn(__fmul_rn(xr[i], scale), w[i]);
+}
+
+// Rotate-half RoPE with cos/sin computed on the device (per-op entry point).
+__global__ void rope_kernel(float *__restrict__ q, float *__restrict__ k, int n_heads,
+                            int n_kv_heads, int head_dim, int pos, float theta) {
+    const int half = head_dim / 2;
+    const int h = blockIdx.x;
+    float *v = h < n_heads ? q + (size_t)h * head_dim : k + (size_t)(h - n_heads) * head_dim;
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+        const float exponent = -(float)(2 * i) / (float)head_dim;
+        const float inv_freq = powf(theta, exponent);
+        const float angle = __fmul_rn((float)pos, inv_freq);
+        const float c = cosf(angle), s = sinf(angle);
+        const float x0 = v[i], x1 = v[i + half];
+        v[i] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+        v[i + half] = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s));
+    }
+}
+
+// Engine: per-head QK-norm (optional), RoPE from a precomputed [max_seq][hd/2]
+// cos/sin table (host-computed with the reference's exact powf/cosf/sinf), and
+// the KV append at *pos.  One CTA per head: blocks [0, H) = q heads,
+// [H, H+KVH) = k heads (rope + store), [H+KVH, H+2KVH) = v heads (store).
+template <typename KV>
+__global__ void qk_rope_kv_kernel(float *__restrict__ q, const float *__restrict__ k,
+                                  const float *__restrict__ v, const float *__restrict__ q_norm,
+                                  const float *__restrict__ k_norm, float eps,
+                                  const float *__restrict__ cos_tab,
+                                  const float *__restrict__ sin_tab, const int *__restrict__ pos_p,
+                                  KV *__restrict__ kcache, KV *__restrict__ vcache, int n_heads,
+                                  int n_kv_heads, int head_dim, int max_seq) {
+    __shared__ double sh[32];
+    __shared__ float buf[512];
+    const int h = blockIdx.x;
+    const int pos = *pos_p;
+    const int half = head_dim / 2;
+    if (h >= n_heads + n_kv_heads) {  // value head: plain store
+        const int kh = h - n_heads - n_kv_heads;
+        KV *dst = vcache + ((size_t)kh * max_seq + pos) * head_dim;
+        for (int i = threadIdx.x; i < head_dim; i += blockDim.x) {
+            const float val = v[kh * head_dim + i];
+            if constexpr (sizeof(KV) == 2) dst[i] = f2h_ref(val);
+            else dst[i] = val;
+        }
+        return;
+    }
+    const bool is_q = h < n_heads;
+    const float *src = is_q ? q + (size_t)h * head_dim : k + (size_t)(h - n_heads) * head_dim;
+    const float *nw = is_q ? q_norm : k_norm;
+    for (int i = threadIdx.x; i < head_dim; i += blockDim.x) buf[i] = src[i];
+    if (nw) {
+        double ss = 0.0;
+        for (int i = threadIdx.x; i < head_dim; i += blockDim.x) ss += (double)buf[i] * (double)buf[i];
+        ss = block_sum_d(ss, sh);
+        const float mean_sq = (float)(ss / head_dim);
+        const float scale = 1.0f / sqrtf(__fadd_rn(mean_sq, eps));
+        for (int i = threadIdx.x; i < head_dim; i += blockDim.x)
+            buf[i] = __fmul_rn(__fmul_rn(buf[i], scale), nw[i]);
+    }
+    __syncthreads();
+    const float *cs = cos_tab + (size_t)pos * half;
+    const float *sn = sin_tab + (size_t)pos * half;
+    float r[2][4];
+    int cnt = 0;
+    for (int i = threadIdx.x; i < half; i += blockDim.x, ++cnt) {
+        const float x0 = buf[i], x1 = buf[i + half], c = cs[i], s = sn[i];
+        r[0][cnt & 3] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+        r[1][cnt & 3] = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s));
+    }
+    __syncthreads();
+    cnt = 0;
+    for (int i = threadIdx.x; i < half; i += blockDim.x, ++cnt) {
+        buf[i] = r[0][cnt & 3];
+        buf[i + half] = r[1][cnt & 3];
+    }
+    __syncthreads();
+    if (is_q) {
+        for (int i = threadIdx.x; i < head_dim; i += blockDim.x) q[(size_t)h * head_dim + i] = buf[i];
+    } else {
+        const int kh = h - n_heads;
+        KV *dst = kcache + ((size_t)kh * max_seq + pos) * head_dim;
+        for (int i = threadIdx.x; i < head_dim; i += blockDim.x) {
+            if constexpr (sizeof(KV) == 2) dst[i] = f2h_ref(buf[i]);
+            else dst[i] = buf[i];
+        }
+    }
+}
+
+// ------------------------------------------------------------------ attention
+__device__ __forceinline__ void load4(const float *p, float o[4]) {
+    const float4 v = *reinterpret_cast<const float4 *>(p);
+    o[0] = v.x, o[1] = v.y, o[2] = v.z, o[3] = v.w;
+}
+__device__ __forceinline__ void load4(const uint16_t *p, float o[4]) {
+    const uint2 v = *reinterpret_cast<const uint2 *>(p);
+    o[0] = h2f((uint16_t)(v.x & 0xFFFF)), o[1] = h2f((uint16_t)(v.x >> 16));
+    o[2] = h2f((uint16_t)(v.y & 0xFFFF)), o[3] = h2f((uint16_t)(v.y >> 16));
+}
+
+constexpr int kAttnThreads = 256;
+
+// Split-K (flash-decoding) GQA decode attention.  grid = (n_kv_heads, nsplit).
+// CTA (kh, s) handles the G = n_heads/n_kv_heads query heads of KV head kh over
+// positions [s*chunk, (s+1)*chunk) of [0, seq): it reads each K/V row once for
+// all G heads.  Scores -> smem, exact max/sum softmax over the chunk, P.V, then
+// the partial (m, l, o) goes to global scratch; the last CTA of the KV head (an
+// atomic ticket) merges the partials and writes out.  seq = *pos_p + 1 when
+// pos_p is set (CUDA-graph replays), else seq_len.
+template <typename KV, int HD, int G>
+__global__ void __launch_bounds__(kAttnThreads)
+    attn_split_kernel(const float *__restrict__ q, const KV *__restrict__ kc,
+                      const KV *__restrict__ vc, const int *__restrict__ pos_p, int seq_len,
+                      int max_seq, int nsplit, float scale, float *__restrict__ part,
+                      unsigned int *__restrict__ tickets, float *__restrict__ out) {
+    extern __shared__ float sm[];
+    float *qs = sm;                              // [G][HD]
+    constexpr int kTS = kAttnThreads / (HD / 4);  // position subsets of the P.V phase
+    float *red = qs + G * HD;                    // [kTS][G][HD] (P.V partials)
+    float *sc = red + kTS * G * HD;              // [chunk_max][G]
+    __shared__ float s_m[G], s_l[G];
+    __shared__ bool s_last;
+    const int kh = blockIdx.x, split = blockIdx.y;
+    const int tid = threadIdx.x;
+    const int seq = pos_p ? (*pos_p + 1) : seq_len;
+    const int chunk = (seq + nsplit - 1) / nsplit;
+    const int t0 = split * chunk;
+    const int t1 = min(seq, t0 + chunk);
+    const int n = max(0, t1 - t0);
+    const KV *kbase = kc + (size_t)kh * max_seq * HD;
+    const KV *vbase = vc + (size_t)kh * max_seq * HD;
+
+    for (int i = tid; i < G * HD; i += kAttnThreads) qs[i] = q[(size_t)kh * G * HD + i];
+    __syncthreads();
+    // scores: one position per thread, q broadcast from smem
+    for (int tt = tid; tt < n; tt += kAttnThreads) {
+        const KV *kr = kbase + (size_t)(t0 + tt) * HD;
+        float acc[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) acc[g] = 0.0f;
+#pragma unroll 4
+        for (int d = 0; d < HD; d += 4) {
+            float kv[4];
+            load4(kr + d, kv);
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const float4 qv = *reinterpret_cast<const float4 *>(qs + g * HD + d);
+                acc[g] = fmaf(qv.x, kv[0], acc[g]);
+                acc[g] = fmaf(qv.y, kv[1], acc[g]);
+                acc[g] = fmaf(qv.z, kv[2], acc[g]);
+                acc[g] = fmaf(qv.w, kv[3], acc[g]);
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) sc[tt * G + g] = acc[g] * scale;
+    }
+    __syncthreads();
+    // softmax statistics per head (warp g)
+    const int lane = tid & 31, warp = tid >> 5;
+    if (warp < G) {
+        float m = -INFINITY;
+        for (int tt = lane; tt < n; tt += 32) m = fmaxf(m, sc[tt * G + warp]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float l = 0.0f;
+        for (int tt = lane; tt < n; tt += 32) {
+            const float p = expf(sc[tt * G + warp] - m);
+            sc[tt * G + warp] = p;
+            l += p;
+        }
+        l = warp_sum(l);
+        if (lane == 0) {
+            s_m[warp] = m;
+            s_l[warp] = l;
+        }
+    }
+    __syncthreads();
+    // P.V: thread = (dim group of 4, position subset of 8)
+    {
+        const int dg = tid % (HD / 4), ts = tid / (HD / 4);
+        constexpr int TS = kAttnThreads / (HD / 4);
+        float acc[G][4];
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[g][j] = 0.0f;
+        for (int tt = ts; tt < n; tt += TS) {
+            float vv[4];
+            load4(vbase + (size_t)(t0 + tt) * HD + dg * 4, vv);
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const float p = sc[tt * G + g];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[g][j] = fmaf(p, vv[j], acc[g][j]);
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) red[(ts * G + g) * HD + dg * 4 + j] = acc[g][j];
+        __syncthreads();
+        float *my = part + ((size_t)kh * nsplit + split) * G * (HD + 2);
+        for (int i = tid; i < G * HD; i += kAttnThreads) {
+            float s = 0.0f;
+            for (int r = 0; r < TS; ++r) s += red[r * G * HD + i];
+            my[2 * G + i] = s;
+        }
+        if (tid < G) {
+            my[tid] = s_m[tid];
+            my[G + tid] = s_l[tid];
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const unsigned int t = atomicAdd(&tickets[kh], 1u);
+        s_last = (t == (unsigned)nsplit - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    // merge the nsplit partials of this KV head
+    const float *pk = part + (size_t)kh * nsplit * G * (HD + 2);
+    for (int i = tid; i < G * HD; i += kAttnThreads) {
+        const int g = i / HD;
+        float M = -INFINITY;
+        for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(pk + (size_t)s * G * (HD + 2) + g));
+        float L = 0.0f, O = 0.0f;
+        for (int s = 0; s < nsplit; ++s) {
+            const float *ps = pk + (size_t)s * G * (HD + 2);
+            const float ms = __ldcg(ps + g);
+            if (ms == -INFINITY) continue;
+            const float f = expf(ms - M);
+            L = fmaf(__ldcg(ps + G + g), f, L);
+            O = fmaf(__ldcg(ps + 2 * G + i), f, O);
+        }
+        out[(size_t)kh * G * HD + i] = O / L;
+    }
+    if (tid == 0) tickets[kh] = 0u;
+}
+
+// ------------------------------------------------------------------ swiglu
+__global__ void swiglu_kernel(float *__restrict__ g, const float *__restrict__ u, int n) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const float gv = g[i];
+        const float denom = __fadd_rn(1.0f, expf(-gv));
+        g[i] = __fmul_rn(__fdiv_rn(gv, denom), u[i]);
+    }
+}
+
+// ------------------------------------------------------------------ argmax
+// (value, index) pairs compare by value, then lower index wins: the first
+// maximum, as argmax_ref's strict '>' scan yields.
+__device__ __forceinline__ void better(float &bv, int &bi, float v, int i) {
+    if (v > bv || (v == bv && i < bi)) {
+        bv = v;
+        bi = i;
+    }
+}
+
+__device__ __forceinline__ void block_argmax(float &bv, int &bi, float *sv, int *si) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        better(bv, bi, ov, oi);
+    }
+    if (lane == 0) {
+        sv[warp] = bv;
+        si[warp] = bi;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        bv = lane < nw ? sv[lane] : -INFINITY;
+        bi = lane < nw ? si[lane] : INT_MAX;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            better(bv, bi, ov, oi);
+        }
+    }
+}
+
+__global__ void argmax_kernel(const float *__restrict__ l, int n, float *__restrict__ pv,
+                              int *__restrict__ pi, unsigned int *__restrict__ ticket,
+                              int *__restrict__ out) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    __shared__ bool last;
+    float bv = -INFINITY;
+    int bi = INT_MAX;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        better(bv, bi, l[i], i);
+    block_argmax(bv, bi, sv, si);
+    if (threadIdx.x == 0) {
+        pv[blockIdx.x] = bv;
+        pi[blockIdx.x] = bi;
+        __threadfence();
+        last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    bv = -INFINITY;
+    bi = INT_MAX;
+    for (int b = threadIdx.x; b < gridDim.x; b += blockDim.x) better(bv, bi, __ldcg(pv + b), __ldcg(pi + b));
+    __syncthreads();
+    block_argmax(bv, bi, sv, si);
+    if (threadIdx.x == 0) {
+        // every value NaN (or n == 0): argmax_ref returns index 0
+        *out = bi == INT_MAX ? 0 : bi;
+        *ticket = 0u;
+    }
+}
+
+// ------------------------------------------------------------------ top-k softmax
+// n <= 1024, k <= 64; one CTA.  Selection by (value desc, index asc); the
+// softmax over the selected logits runs in double exactly as topk_softmax_ref.
+__global__ void topk_softmax_kernel(const float *__restrict__ logits, int n, int k,
+                                    int *__restrict__ idx_out, float *__restrict__ w_out) {
+    __shared__ float vals[1024];
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    __shared__ int sel[64];
+    for (int i = threadIdx.x; i < n; i += blockDim.x) vals[i] = logits[i];
+    __syncthreads();
+    const int kk = min(k, n);
+    for (int t = 0; t < kk; ++t) {
+        float bv = -INFINITY;
+        int bi = INT_MAX;
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            bool taken = false;
+            for (int j = 0; j < t; ++j) taken |= (sel[j] == i);
+            if (!taken) {
+                const float v = vals[i];
+                if (bi == INT_MAX || v > bv || (v == bv && i < bi)) {
+                    bv = v;
+                    bi = i;
+                }
+            }
+        }
+        block_argmax(bv, bi, sv, si);
+        if (threadIdx.x == 0) sel[t] = bi;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        float m = vals[sel[0]];
+        for (int i = 1; i < kk; ++i) m = fmaxf(m, vals[sel[i]]);
+        float e[64];
+        double sum = 0.0;
+        for (int i = 0; i < kk; ++i) {
+            e[i] = (float)exp((double)vals[sel[i]] - (double)m);
+            sum += (double)e[i];
+        }
+        const double inv = sum > 0.0 ? 1.0 / sum : 0.0;
+        for (int i = 0; i < kk; ++i) {
+            idx_out[i] = sel[i];
+            w_out[i] = (float)((double)e[i] * inv);
+        }
+        for (int i = kk; i < k; ++i) {
+            idx_out[i] = -1;
+            w_out[i] = 0.0f;
+        }
+    }
+}
+
+// ------------------------------------------------------------------ embed
+__global__ void embed_kernel(const void *__restrict__ table, int dtype, const int *__restrict__ token,
+                             int dim, int group_size, float *__restrict__ out) {
+    const int tok = *token;
+    for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < dim; c += gridDim.x * blockDim.x) {
+        if (dtype == TQB200_DT_F32) {
+            out[c] = ((const float *)table)[(size_t)tok * dim + c];
+        } else if (dtype == TQB200_DT_F16) {
+            out[c] = h2f(((const uint16_t *)table)[(size_t)tok * dim + c]);
+        } else {
+            const int ng = (dim + group_size - 1) / group_size, GB = 4 + group_size / 2;
+            const uint8_t *gp = (const uint8_t *)table + ((size_t)tok * ng + c / group_size) * GB;
+            const int i = c % group_size;
+            const float s = h2f((uint16_t)(gp[0] | (gp[1] << 8)));
+            const float z = h2f((uint16_t)(gp[2] | (gp[3] << 8)));
+            const uint8_t b = gp[4 + (i >> 1)];
+            out[c] = __fmul_rn(__fsub_rn((float)((i & 1) ? (b >> 4) : (b & 15)), z), s);
+        }
+    }
+}
+
+template <typename KV, int HD, int G>
+int launch_attn_t(const AttnArgs &a, cudaStream_t st) {
+    const size_t smem = (size_t)(G * HD + (kAttnThreads / (HD / 4)) * G * HD) * 4 +
+                        (size_t)a.chunk_max * G * 4;
+    auto k = attn_split_kernel<KV, HD, G>;
+    if (smem > 48 * 1024) {
+        TQ_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    }
+    dim3 grid(a.n_kv_heads, a.nsplit);
+    k<<<grid, kAttnThreads, smem, st>>>(a.q, (const KV *)a.k, (const KV *)a.v, a.pos, a.seq_len,
+                                        a.max_seq, a.nsplit, a.scale, a.partial, a.tickets, a.out);
+    TQ_CUDA_TRY(cudaGetLastError());
+    return TQB200_OK;
+}
+
+template <typename KV>
+int launch_attn_kv(const AttnArgs &a, cudaStream_t st) {
+    const int G = a.n_heads / a.n_kv_heads;
+#define TQ_ATTN_CASE(HDV, GV) \
+    if (a.head_dim == HDV && G == GV) return launch_attn_t<KV, HDV, GV>(a, st);
+    TQ_ATTN_CASE(64, 1) TQ_ATTN_CASE(64, 2) TQ_ATTN_CASE(64, 4) TQ_ATTN_CASE(64, 7)
+    TQ_ATTN_CASE(64, 8) TQ_ATTN_CASE(128, 1) TQ_ATTN_CASE(128, 2) TQ_ATTN_CASE(128, 4)
+    TQ_ATTN_CASE(128, 8) TQ_ATTN_CASE(32, 1) TQ_ATTN_CASE(32, 2) TQ_ATTN_CASE(32, 4)
+    TQ_ATTN_CASE(32, 8)
+#undef TQ_ATTN_CASE
+    return set_error(TQB200_ERR_UNSUPPORTED, "attention: head_dim %d with %d heads per KV head",
+                     a.head_dim, G);
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ launchers
+int launch_rmsnorm(const float *x, const float *w, float *y, int rows, int n, float eps,
+                   cudaStream_t st) {
+    TQ_CHECK_ARG(n > 0 && rows > 0, "rmsnorm n %d rows %d", n, rows);
+    rmsnorm_rows_kernel<<<rows, 256, 0, st>>>(x, w, y, n, eps);
+    TQ_CUDA_TRY(cudaGetLastError());
+    return TQB200_OK;
+}
+
+int launch_rope(float *q, float *k, int n_heads, int n_kv_heads, int head_dim, int pos,
+                float theta, cudaStream_t st) {
+    TQ_CHECK_ARG(head_dim > 0 && head_dim % 2 == 0 && head_dim / 2 <= 256,
+                 "rope: unsupported head_dim %d", head_dim);
+    if (n_heads + n_kv_heads == 0) return TQB200_OK;
+    rope_kernel<<<n_heads + n_kv_heads, 128, 0, st>>>(q, k, n_heads, n_kv_heads, head_dim, pos,
+                                                      theta);
+    TQ_CUDA_TRY(cudaGetLastError());
+    return TQB200_OK;
+}
+
+int launch_qk_rope_kv(const QkRopeKvArgs &a, cudaStream_t st) {
+    TQ_CHECK_ARG(a.head_dim <= 512 && a.head_dim % 2 == 0 && a.head_dim / 2 <= 4 * 128,
+                 "head_dim %d", a.head_dim);
+    const int blocks = a.n_heads + 2 * a.n_kv_heads;
+    if (a.kv_fp16)
+        qk_rope_kv_kernel<uint16_t><<<blocks, 128, 0, st>>>(
+            a.q, a.k, a.v, a.q_norm, a.k_norm, a.eps, a.cos_tab, a.sin_tab, a.pos,
+            (uint16_t *)a.kcache, (uint16_t *)a.vcache, a.n_heads, a.n_kv_heads, a.head_dim,
+            a.max_seq);
+    else
+        qk_rope_kv_kernel<float><<<blocks, 128, 0, st>>>(
+            a.q, a.k, a.v, a.q_norm, a.k_norm, a.eps, a.cos_tab, a.sin_tab, a.pos,
+            (float *)a.kcache, (float *)a.vcache, a.n_heads, a.n_kv_heads, a.head_dim, a.max_seq);
+    TQ_CUDA_TRY(cudaGetLastError());
+    return TQB200_OK;
+}
+
+int attn_plan(int n_kv_heads, int max_seq, int *nsplit, int *chunk_max) {
+    // aim for >= 2 CTAs per SM at full context, chunks of at least 32 positions
+    const int target = 2 * num_sms();
+    int ns = std::max(1, (target + n_kv_heads - 1) / n_kv_heads);
+    ns = std::min(ns, std::max(1, (max_seq + 31) / 32));
+    *nsplit = ns;
+    *chunk_max = (max_seq + ns - 1) / ns;
+    return TQB200_OK;
+}
+
+size_t attn_partial_floats(int n_heads, int head_dim, int nsplit) {
+    return (size_t)nsplit * (n_heads * head_dim + 2 * n_heads);
+}
+
+int launch_attention(const AttnArgs &a, cudaStream_t st) {
+    TQ_CHECK_ARG(a.n_kv_heads > 0 && a.n_heads % a.n_kv_heads == 0, "heads %d / kv %d",
+                 a.n_heads, a.n_kv_heads);
+    TQ_CHECK_ARG(a.chunk_max >= (a.max_seq + a.nsplit - 1) / a.nsplit, "chunk plan");
+    return a.kv_fp16 ? launch_attn_kv<uint16_t>(a, st) : launch_attn_kv<float>(a, st);
+}
+
+int launch_swiglu(float *g, const float *u, int n, cudaStream_t st) {
+    if (n == 0) return TQB200_OK;
+    const int block = 256;
+    const int grid = std::min((n + block - 1) / block, num_sms() * 8);
+    swiglu_kernel<<<grid, block, 0, st>>>(g, u, n);
+    TQ_CUDA_TRY(cudaGetLastError());
+    return TQB200_OK;
+}
+
+int argmax_blocks(int n) { return std::max(1, std::min((n + 1023) / 1024, 2 * num_sms())); }
+
+int launch_argmax(const float *l, int n, float *pv, int *pi, unsigned int *ticket, int *out,
+                  cudaStream_t st) {
+    TQ_CHECK_ARG(n > 0, "argmax n %d", n);
+    argmax_kernel<<<argmax_blocks(n), 256, 0, st>>>(l, n, pv, pi, ticket, out);
+    TQ_CUDA_TRY(cudaGetLastError());
+    return TQB200_OK;
+}
+
+int launch_topk_softmax(const float *logits, int n, int k, int *idx, float *w, cudaStream_t st) {
+    TQ_CHECK_ARG(n > 0 && n <= 1024 && k > 0 && k <= 64, "topk n %d k %d", n, k);
+    topk_softmax_kernel<<<1, 256, 0, st>>>(logits, n, k, idx, w);
+    TQ_CUDA_TRY(cudaGetLastError());
+    return TQB200_OK;
+}
+
+int launch_embed(const void *table, int dtype, const int *token, int dim, int group_size,
+                 float *out, cudaStream_t st) {
+    const int grid = std::max(1, std::min((dim + 255) / 256, 16));
+    embed_kernel<<<grid, 256, 0, st>>>(table, dtype, token, dim, group_size, out);
+    TQ_CUDA_TRY(cudaGetLastError());
+    return TQB200_OK;
+}
+
+}  // namespace tqb200

@@ -1,0 +1,635 @@
+// engine.cu — GPU-resident batch-1 greedy decode engine (sm_100a).
+//
+// Replaces the reference's GPU decode registry entry (kernels/dispatch.h:353-378,
+// kernels/cuda/gpu_engine.cu) for quantised (i4) Qwen2/Qwen3-family models and
+// runs the same step as QwenModel::forward_token (runtime/qwen_forward_token.cpp:83-742):
+//
+//   embed -> per layer [ rmsnorm -> q/k/v (+bias) -> QK-norm -> RoPE -> KV append
+//            -> attention -> o_proj + residual -> rmsnorm -> gate/up -> SwiGLU
+//            -> down + residual ] -> final rmsnorm -> lm_head -> argmax
+//
+// as 2 + 6 * n_layers kernels:
+//   embed | qkv (RMSNorm prologue, bias epilogue) | qk-norm+rope+kv-append | split-K
+//   attention | o_proj (residual epilogue) | gate/up (RMSNorm prologue) | down (SwiGLU
+//   prologue, residual epilogue) | ... | lm_head (RMSNorm prologue, argmax epilogue)
+// captured once into a CUDA graph whose nodes are linked by programmatic
+// dependent launch, so each matvec streams its weights while its predecessor
+// finishes.  Per step the host moves 8 bytes in (token, position) and 8 bytes
+// out (next token, device status) through pinned memory, like the reference
+// engine's 2 x 4 B H2D + 4 B D2H (kernels/cuda/gpu_engine.cu:332-371).
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace tqb200 {
+namespace {
+
+struct DLayer {
+    const float *input_ln = nullptr, *post_ln = nullptr;
+    const uint8_t *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr;
+    const uint8_t *gate = nullptr, *up = nullptr, *down = nullptr;
+    const float *q_bias = nullptr, *k_bias = nullptr, *v_bias = nullptr;
+    const float *q_norm = nullptr, *k_norm = nullptr;
+};
+
+}  // namespace
+}  // namespace tqb200
+
+struct tqb200_engine {
+    tqb200_model_desc d{};
+    tqb200_engine_opts o{};
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::vector<void *> allocs;
+    std::vector<tqb200::DLayer> layers;
+    const void *embed = nullptr;
+    int embed_dtype = 0;
+    const uint8_t *lm_head = nullptr;
+    const float *final_norm = nullptr;
+    float *hidden = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr;
+    float *gate = nullptr, *up = nullptr, *logits = nullptr;
+    void *kv = nullptr;  // [K|V][L][KVH][max_seq][hd]
+    size_t layer_stride = 0;
+    float *cos_tab = nullptr, *sin_tab = nullptr;
+    int *io_in = nullptr;   // device [token, pos]
+    int *io_out = nullptr;  // device [next, status]
+    int *h_io = nullptr;    // pinned host [token, pos, next, status]
+    float *attn_part = nullptr;
+    unsigned int *attn_tickets = nullptr;
+    int attn_nsplit = 0, attn_chunk = 0;
+    float *am_v = nullptr;
+    int *am_i = nullptr;
+    unsigned int *am_ticket = nullptr;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;       // one step, host-fed token/position
+    cudaGraph_t loop_graph = nullptr;
+    cudaGraphExec_t loop_exec = nullptr;  // one step + device-side feed of the next token
+    int *gen_tokens = nullptr;            // device [max_seq] tokens of generate()
+    int *gen_count = nullptr;             // device step counter of generate()
+    cudaEvent_t ev[2] = {nullptr, nullptr};
+    // profiling: events after every launch, tagged with a kernel kind
+    bool prof = false;
+    std::vector<cudaEvent_t> prof_ev;
+    std::vector<int> prof_kind;
+    int pos = 0;
+    size_t weight_bytes = 0;
+};
+
+namespace tqb200 {
+namespace {
+
+int dev_alloc(tqb200_engine *e, size_t bytes, void **out) {
+    void *p = nullptr;
+    TQ_CUDA_TRY(cudaMalloc(&p, bytes + 256));  // +256: bulk copies may round up to 16 B
+    e->allocs.push_back(p);
+    *out = p;
+    return TQB200_OK;
+}
+
+int upload_bytes(tqb200_engine *e, const void *host, size_t bytes, const void **out) {
+    void *p;
+    int st = dev_alloc(e, bytes, &p);
+    if (st) return st;
+    TQ_CUDA_TRY(cudaMemcpy(p, host, bytes, cudaMemcpyHostToDevice));
+    e->weight_bytes += bytes;
+    *out = p;
+    return TQB200_OK;
+}
+
+size_t mat_bytes(const tqb200_matrix &m, int group) {
+    switch (m.dtype) {
+        case TQB200_DT_I4: return (size_t)m.rows * tqb200_i4_row_bytes(m.cols, group);
+        case TQB200_DT_VQ2: return tqb200_vq2_bytes(m.rows, m.cols);
+        case TQB200_DT_F16: return (size_t)m.rows * m.cols * 2;
+        default: return (size_t)m.rows * m.cols * 4;
+    }
+}
+
+#define TQ_TRY(expr)         \
+    do {                     \
+        int s_ = (expr);     \
+        if (s_) return s_;   \
+    } while (0)
+
+int need_i4(const tqb200_matrix &m, int rows, int cols, const char *what, int layer) {
+    if (!m.data) return set_error(TQB200_ERR_INVALID_ARG, "layer %d: %s missing", layer, what);
+    if (m.dtype != TQB200_DT_I4)
+        return set_error(TQB200_ERR_UNSUPPORTED, "layer %d: %s dtype %d (engine path is i4)",
+                         layer, what, m.dtype);
+    if (m.rows != rows || m.cols != cols)
+        return set_error(TQB200_ERR_INVALID_ARG, "layer %d: %s shape %dx%d, expected %dx%d",
+                         layer, what, m.rows, m.cols, rows, cols);
+    return TQB200_OK;
+}
+
+int up_i4(tqb200_engine *e, const tqb200_matrix &m, const uint8_t **out) {
+    const void *p;
+    TQ_TRY(upload_bytes(e, m.data, mat_bytes(m, e->d.group_size), &p));
+    *out = (const uint8_t *)p;
+    return TQB200_OK;
+}
+
+int up_vec(tqb200_engine *e, const float *h, int n, const float **out) {
+    if (!h) {
+        *out = nullptr;
+        return TQB200_OK;
+    }
+    const void *p;
+    TQ_TRY(upload_bytes(e, h, (size_t)n * 4, &p));
+    *out = (const float *)p;
+    return TQB200_OK;
+}
+
+int validate(const tqb200_model_desc &d, const tqb200_engine_opts &o) {
+    TQ_CHECK_ARG(d.model_type == TQB200_MODEL_QWEN2,
+                 "engine supports model_type Qwen2/Qwen3 dense (0), got %d", d.model_type);
+    TQ_CHECK_ARG(d.n_layers > 0 && d.hidden > 0 && d.inter > 0 && d.n_heads > 0 &&
+                     d.n_kv_heads > 0 && d.head_dim > 0 && d.vocab > 0 && d.layers,
+                 "model description has zero fields");
+    TQ_CHECK_ARG(d.n_heads % d.n_kv_heads == 0, "n_heads %% n_kv_heads != 0");
+    TQ_CHECK_ARG(d.group_size > 0 && d.group_size % 32 == 0,
+                 "engine needs group_size %% 32 == 0 (got %d)", d.group_size);
+    TQ_CHECK_ARG(d.hidden % 32 == 0 && d.inter % 32 == 0 && (d.n_heads * d.head_dim) % 32 == 0,
+                 "engine needs hidden/inter/q_dim multiples of 32");
+    TQ_CHECK_ARG(o.max_seq_len > 0 && (d.max_seq_len <= 0 || o.max_seq_len <= d.max_seq_len),
+                 "max_seq_len %d exceeds model max %d", o.max_seq_len, d.max_seq_len);
+    TQ_CHECK_ARG(d.head_dim % 2 == 0 && d.head_dim <= 512, "head_dim %d", d.head_dim);
+    TQ_CHECK_ARG(d.lm_head.data && d.lm_head.dtype == TQB200_DT_I4 && d.lm_head.rows == d.vocab &&
+                     d.lm_head.cols == d.hidden,
+                 "engine needs an i4 lm_head [vocab x hidden]");
+    TQ_CHECK_ARG(d.embed.data && d.embed.rows == d.vocab && d.embed.cols == d.hidden &&
+                     (d.embed.dtype == TQB200_DT_F32 || d.embed.dtype == TQB200_DT_F16 ||
+                      d.embed.dtype == TQB200_DT_I4),
+                 "embed must be f32/f16/i4 [vocab x hidden]");
+    TQ_CHECK_ARG(d.final_norm, "final_norm missing");
+    return TQB200_OK;
+}
+
+// RoPE tables with the reference's exact float operations (kernels/rope/rope_ref.cpp:74-85):
+// inv_freq = powf(theta, -(float)(2i)/(float)hd), angle = (float)pos * inv_freq.
+int build_rope_tables(tqb200_engine *e) {
+    const int half = e->d.head_dim / 2, S = e->o.max_seq_len;
+    std::vector<float> cs((size_t)S * half), sn((size_t)S * half), inv(half);
+    for (int i = 0; i < half; ++i) {
+        const float exponent = -(float)(2 * i) / (float)e->d.head_dim;
+        inv[i] = powf(e->d.rope_theta, exponent);
+    }
+    for (int p = 0; p < S; ++p)
+        for (int i = 0; i < half; ++i) {
+            volatile float angle = (float)p * inv[i];
+            cs[(size_t)p * half + i] = cosf(angle);
+            sn[(size_t)p * half + i] = sinf(angle);
+        }
+    const void *dc, *ds;
+    TQ_TRY(upload_bytes(e, cs.data(), cs.size() * 4, &dc));
+    TQ_TRY(upload_bytes(e, sn.data(), sn.size() * 4, &ds));
+    e->weight_bytes -= (cs.size() + sn.size()) * 4;
+    e->cos_tab = (float *)dc;
+    e->sin_tab = (float *)ds;
+    return TQB200_OK;
+}
+
+enum Kind { K_EMBED, K_QKV, K_ROPE_KV, K_ATTN, K_OPROJ, K_GATEUP, K_DOWN, K_LMHEAD, K_NKINDS };
+
+int mark(tqb200_engine *e, int kind) {
+    if (!e->prof) return TQB200_OK;
+    cudaEvent_t ev;
+    TQ_CUDA_TRY(cudaEventCreate(&ev));
+    TQ_CUDA_TRY(cudaEventRecord(ev, e->stream));
+    e->prof_ev.push_back(ev);
+    e->prof_kind.push_back(kind);
+    return TQB200_OK;
+}
+
+// Device-side token feed for generate(): records the produced token and makes it
+// (and position + 1) the input of the next step.
+__global__ void feed_next_kernel(int *io_in, const int *io_out, int *tokens, int *count) {
+    const int c = *count;
+    tokens[c] = io_out[0];
+    io_in[0] = io_out[0];
+    io_in[1] += 1;
+    *count = c + 1;
+}
+
+// One decode step's kernels, stream-ordered on e->stream.
+int launch_forward(tqb200_engine *e) {
+    const tqb200_model_desc &d = e->d;
+    cudaStream_t st = e->stream;
+    const int H = d.hidden, hd = d.head_dim;
+    const int qd = d.n_heads * hd, kvd = d.n_kv_heads * hd;
+    const bool pdl = e->o.pdl != 0;
+    int *status = e->io_out + 1;
+    TQ_TRY(mark(e, -1));
+    TQ_TRY(launch_embed(e->embed, e->embed_dtype, e->io_in, H, d.group_size, e->hidden, st));
+    TQ_TRY(mark(e, K_EMBED));
+    for (int l = 0; l < d.n_layers; ++l) {
+        const DLayer &w = e->layers[l];
+        {   // q/k/v with the input RMSNorm fused into the prologue, biases into the epilogue
+            I4Job j[3] = {{w.q, e->q, w.q_bias, nullptr, qd},
+                          {w.k, e->k, w.k_bias, nullptr, kvd},
+                          {w.v, e->v, w.v_bias, nullptr, kvd}};
+            I4LaunchOpts o;
+            o.x = {X_RMSNORM, e->hidden, w.input_ln, d.rms_eps, nullptr};
+            o.pdl = pdl;
+            o.status = status;
+            TQ_TRY(launch_i4_matvec_ex(j, 3, H, d.group_size, o, st));
+            TQ_TRY(mark(e, K_QKV));
+        }
+        char *kvb = (char *)e->kv;
+        const size_t es = e->o.kv_fp16 ? 2 : 4;
+        void *kc = kvb + (size_t)l * e->layer_stride * es;
+        void *vc = kvb + ((size_t)d.n_layers + l) * e->layer_stride * es;
+        {
+            QkRopeKvArgs a{};
+            a.q = e->q;
+            a.k = e->k;
+            a.v = e->v;
+            a.q_norm = w.q_norm;
+            a.k_norm = w.k_norm;
+            a.eps = d.rms_eps;
+            a.cos_tab = e->cos_tab;
+            a.sin_tab = e->sin_tab;
+            a.pos = e->io_in + 1;
+            a.kcache = kc;
+            a.vcache = vc;
+            a.kv_fp16 = e->o.kv_fp16;
+            a.n_heads = d.n_heads;
+            a.n_kv_heads = d.n_kv_heads;
+            a.head_dim = hd;
+            a.max_seq = e->o.max_seq_len;
+            TQ_TRY(launch_qk_rope_kv(a, st));
+            TQ_TRY(mark(e, K_ROPE_KV));
+        }
+        {
+            AttnArgs a{};
+            a.q = e->q;
+            a.k = kc;
+            a.v = vc;
+            a.kv_fp16 = e->o.kv_fp16;
+            a.pos = e->io_in + 1;
+            a.seq_len = 0;
+            a.max_seq = e->o.max_seq_len;
+            a.n_heads = d.n_heads;
+            a.n_kv_heads = d.n_kv_heads;
+            a.head_dim = hd;
+            a.scale = 1.0f / sqrtf((float)hd);
+            a.nsplit = e->attn_nsplit;
+            a.chunk_max = e->attn_chunk;
+            a.partial = e->attn_part;
+            a.tickets = e->attn_tickets;
+            a.out = e->attn;
+            TQ_TRY(launch_attention(a, st));
+            TQ_TRY(mark(e, K_ATTN));
+        }
+        {   // o_proj, residual fused: hidden = hidden + W_o attn
+            I4Job j{w.o, e->hidden, nullptr, e->hidden, H};
+            I4LaunchOpts o;
+            o.x = {X_PLAIN, e->attn, nullptr, 0.0f, nullptr};
+            o.pdl = pdl;
+            o.status = status;
+            TQ_TRY(launch_i4_matvec_ex(&j, 1, qd, d.group_size, o, st));
+            TQ_TRY(mark(e, K_OPROJ));
+        }
+        {   // gate/up with the post-attention RMSNorm fused into the prologue
+            I4Job j[2] = {{w.gate, e->gate, nullptr, nullptr, d.inter},
+                          {w.up, e->up, nullptr, nullptr, d.inter}};
+            I4LaunchOpts o;
+            o.x = {X_RMSNORM, e->hidden, w.post_ln, d.rms_eps, nullptr};
+            o.pdl = pdl;
+            o.status = status;
+            TQ_TRY(launch_i4_matvec_ex(j, 2, H, d.group_size, o, st));
+            TQ_TRY(mark(e, K_GATEUP));
+        }
+        {   // down with SwiGLU in the prologue and the residual in the epilogue
+            I4Job j{w.down, e->hidden, nullptr, e->hidden, H};
+            I4LaunchOpts o;
+            o.x = {X_SWIGLU, e->gate, nullptr, 0.0f, e->up};
+            o.pdl = pdl;
+            o.status = status;
+            TQ_TRY(launch_i4_matvec_ex(&j, 1, d.inter, d.group_size, o, st));
+            TQ_TRY(mark(e, K_DOWN));
+        }
+    }
+    {   // lm_head with the final RMSNorm in the prologue and the greedy argmax in the epilogue
+        I4Job j{e->lm_head, e->logits, nullptr, nullptr, d.vocab};
+        I4LaunchOpts o;
+        o.x = {X_RMSNORM, e->hidden, e->final_norm, d.rms_eps, nullptr};
+        o.argmax = {e->am_v, e->am_i, e->am_ticket, e->io_out};
+        o.pdl = pdl;
+        o.status = status;
+        TQ_TRY(launch_i4_matvec_ex(&j, 1, H, d.group_size, o, st));
+        TQ_TRY(mark(e, K_LMHEAD));
+    }
+    return TQB200_OK;
+}
+
+int capture(tqb200_engine *e, bool with_feed, cudaGraph_t *graph, cudaGraphExec_t *exec) {
+    TQ_CUDA_TRY(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+    int st = launch_forward(e);
+    if (st == TQB200_OK && with_feed) {
+        feed_next_kernel<<<1, 1, 0, e->stream>>>(e->io_in, e->io_out, e->gen_tokens, e->gen_count);
+        if (cudaGetLastError() != cudaSuccess) st = set_error(TQB200_ERR_CUDA, "feed launch failed");
+    }
+    cudaGraph_t g = nullptr;
+    const cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
+    if (st) {
+        if (g) cudaGraphDestroy(g);
+        return st;
+    }
+    TQ_CUDA_TRY(ce);
+    *graph = g;
+    TQ_CUDA_TRY(cudaGraphInstantiate(exec, g, 0));
+    return TQB200_OK;
+}
+
+int check_status(tqb200_engine *e) {
+    if (e->h_io[3] != 0) {
+        const int code = e->h_io[3];
+        e->h_io[3] = 0;
+        cudaMemsetAsync(e->io_out + 1, 0, 4, e->stream);
+        cudaStreamSynchronize(e->stream);
+        return set_error(TQB200_ERR_TIMEOUT, "device wait timed out (code %d) at position %d",
+                         code, e->pos);
+    }
+    return TQB200_OK;
+}
+
+void free_engine(tqb200_engine *e) {
+    if (!e) return;
+    if (e->exec) cudaGraphExecDestroy(e->exec);
+    if (e->graph) cudaGraphDestroy(e->graph);
+    if (e->loop_exec) cudaGraphExecDestroy(e->loop_exec);
+    if (e->loop_graph) cudaGraphDestroy(e->loop_graph);
+    for (auto ev : e->ev)
+        if (ev) cudaEventDestroy(ev);
+    for (auto ev : e->prof_ev) cudaEventDestroy(ev);
+    for (void *p : e->allocs) cudaFree(p);
+    if (e->h_io) cudaFreeHost(e->h_io);
+    if (e->stream) cudaStreamDestroy(e->stream);
+    delete e;
+}
+
+int create_impl(const tqb200_model_desc *desc, const tqb200_engine_opts *opts, tqb200_engine *e) {
+    e->d = *desc;
+    e->o = *opts;
+    const tqb200_model_desc &d = e->d;
+    TQ_TRY(validate(d, e->o));
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        return set_error(TQB200_ERR_NO_DEVICE, "no CUDA device visible");
+    }
+    if (e->o.device >= 0) TQ_CUDA_TRY(cudaSetDevice(e->o.device));
+    TQ_CUDA_TRY(cudaGetDevice(&e->device));
+    TQ_CUDA_TRY(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
+    const int H = d.hidden, hd = d.head_dim, qd = d.n_heads * hd, kvd = d.n_kv_heads * hd;
+    e->layers.resize(d.n_layers);
+    for (int l = 0; l < d.n_layers; ++l) {
+        const tqb200_layer &s = d.layers[l];
+        DLayer &w = e->layers[l];
+        TQ_TRY(need_i4(s.q_proj, qd, H, "q_proj", l));
+        TQ_TRY(need_i4(s.k_proj, kvd, H, "k_proj", l));
+        TQ_TRY(need_i4(s.v_proj, kvd, H, "v_proj", l));
+        TQ_TRY(need_i4(s.o_proj, H, qd, "o_proj", l));
+        TQ_TRY(need_i4(s.gate_proj, d.inter, H, "gate_proj", l));
+        TQ_TRY(need_i4(s.up_proj, d.inter, H, "up_proj", l));
+        TQ_TRY(need_i4(s.down_proj, H, d.inter, "down_proj", l));
+        TQ_CHECK_ARG(s.input_ln && s.post_ln, "layer %d: norms missing", l);
+        TQ_CHECK_ARG((s.q_norm == nullptr) == (s.k_norm == nullptr),
+                     "layer %d: q_norm/k_norm must both be present or both absent", l);
+        TQ_CHECK_ARG(!s.rot_q.sign && !s.rot_o.sign && !s.rot_gate.sign && !s.rot_down.sign,
+                     "layer %d: BiIP-rotated projections are not on the i4 engine path", l);
+        TQ_TRY(up_vec(e, s.input_ln, H, &w.input_ln));
+        TQ_TRY(up_vec(e, s.post_ln, H, &w.post_ln));
+        TQ_TRY(up_i4(e, s.q_proj, &w.q));
+        TQ_TRY(up_i4(e, s.k_proj, &w.k));
+        TQ_TRY(up_i4(e, s.v_proj, &w.v));
+        TQ_TRY(up_i4(e, s.o_proj, &w.o));
+        TQ_TRY(up_i4(e, s.gate_proj, &w.gate));
+        TQ_TRY(up_i4(e, s.up_proj, &w.up));
+        TQ_TRY(up_i4(e, s.down_proj, &w.down));
+        TQ_TRY(up_vec(e, s.q_bias, qd, &w.q_bias));
+        TQ_TRY(up_vec(e, s.k_bias, kvd, &w.k_bias));
+        TQ_TRY(up_vec(e, s.v_bias, kvd, &w.v_bias));
+        TQ_TRY(up_vec(e, s.q_norm, hd, &w.q_norm));
+        TQ_TRY(up_vec(e, s.k_norm, hd, &w.k_norm));
+    }
+    e->embed_dtype = d.embed.dtype;
+    TQ_TRY(upload_bytes(e, d.embed.data, mat_bytes(d.embed, d.group_size), &e->embed));
+    if (d.lm_head.data == d.embed.data && d.embed.dtype == TQB200_DT_I4)
+        e->lm_head = (const uint8_t *)e->embed;  // tied compact-i4 embedding
+    else
+        TQ_TRY(up_i4(e, d.lm_head, &e->lm_head));
+    TQ_TRY(up_vec(e, d.final_norm, H, &e->final_norm));
+    TQ_TRY(build_rope_tables(e));
+
+    void *p;
+    const size_t act = (size_t)H * 2 + qd * 2 + kvd * 2 + (size_t)d.inter * 2 + d.vocab;
+    TQ_TRY(dev_alloc(e, act * 4, &p));
+    float *f = (float *)p;
+    e->hidden = f, f += H;
+    e->q = f, f += qd;
+    e->k = f, f += kvd;
+    e->v = f, f += kvd;
+    e->attn = f, f += qd;
+    e->gate = f, f += d.inter;
+    e->up = f, f += d.inter;
+    e->logits = f;
+    e->layer_stride = (size_t)d.n_kv_heads * e->o.max_seq_len * hd;
+    const size_t kv_bytes = 2 * (size_t)d.n_layers * e->layer_stride * (e->o.kv_fp16 ? 2 : 4);
+    TQ_TRY(dev_alloc(e, kv_bytes, &e->kv));
+    TQ_CUDA_TRY(cudaMemset(e->kv, 0, kv_bytes));
+    TQ_TRY(attn_plan(d.n_kv_heads, e->o.max_seq_len, &e->attn_nsplit, &e->attn_chunk));
+    TQ_TRY(dev_alloc(e, attn_partial_floats(d.n_heads, hd, e->attn_nsplit) * 4, &p));
+    e->attn_part = (float *)p;
+    const int slots = i4_argmax_slots(d.vocab, H, d.group_size);
+    TQ_TRY(dev_alloc(e, (size_t)slots * 8 + 256 + (size_t)d.n_kv_heads * 4 + 64, &p));
+    TQ_CUDA_TRY(cudaMemset(p, 0, (size_t)slots * 8 + 256 + (size_t)d.n_kv_heads * 4 + 64));
+    e->am_v = (float *)p;
+    e->am_i = (int *)((char *)p + (size_t)slots * 4);
+    e->am_ticket = (unsigned int *)((char *)p + (size_t)slots * 8);
+    e->io_in = (int *)((char *)p + (size_t)slots * 8 + 64);
+    e->io_out = (int *)((char *)p + (size_t)slots * 8 + 128);
+    e->attn_tickets = (unsigned int *)((char *)p + (size_t)slots * 8 + 256);
+    TQ_TRY(dev_alloc(e, (size_t)(e->o.max_seq_len + 8) * 4, &p));
+    e->gen_count = (int *)p;
+    e->gen_tokens = (int *)p + 8;
+    TQ_CUDA_TRY(cudaMallocHost(&e->h_io, 64));
+    memset(e->h_io, 0, 64);
+    TQ_CUDA_TRY(cudaEventCreate(&e->ev[0]));
+    TQ_CUDA_TRY(cudaEventCreate(&e->ev[1]));
+    return TQB200_OK;
+}
+
+}  // namespace
+}  // namespace tqb200
+
+using namespace tqb200;
+
+extern "C" {
+
+void tqb200_engine_default_opts(tqb200_engine_opts *o) {
+    if (!o) return;
+    memset(o, 0, sizeof *o);
+    o->max_seq_len = 512;
+    o->kv_fp16 = 0;
+    o->use_graph = 1;
+    o->pdl = 1;
+    o->device = -1;
+}
+
+int tqb200_engine_create(const tqb200_model_desc *desc, const tqb200_engine_opts *opts,
+                         tqb200_engine **out) {
+    TQ_CHECK_ARG(desc && out, "null argument");
+    *out = nullptr;
+    tqb200_engine_opts o;
+    if (opts)
+        o = *opts;
+    else
+        tqb200_engine_default_opts(&o);
+    auto *e = new tqb200_engine();
+    const int st = create_impl(desc, &o, e);
+    if (st) {
+        free_engine(e);
+        return st;
+    }
+    *out = e;
+    return TQB200_OK;
+}
+
+int tqb200_engine_step(tqb200_engine *e, int token_id, int *next_token) {
+    TQ_CHECK_ARG(e, "null engine");
+    TQ_CHECK_ARG(token_id >= 0 && token_id < e->d.vocab, "token_id %d out of range [0, %d)",
+                 token_id, e->d.vocab);
+    TQ_CHECK_ARG(e->pos < e->o.max_seq_len, "position %d exceeds max_seq_len %d", e->pos,
+                 e->o.max_seq_len);
+    TQ_CUDA_TRY(cudaSetDevice(e->device));
+    e->h_io[0] = token_id;
+    e->h_io[1] = e->pos;
+    TQ_CUDA_TRY(cudaMemcpyAsync(e->io_in, e->h_io, 8, cudaMemcpyHostToDevice, e->stream));
+    if (e->o.use_graph) {
+        if (!e->exec) TQ_TRY(capture(e, false, &e->graph, &e->exec));
+        TQ_CUDA_TRY(cudaGraphLaunch(e->exec, e->stream));
+    } else {
+        TQ_TRY(launch_forward(e));
+    }
+    TQ_CUDA_TRY(cudaMemcpyAsync(e->h_io + 2, e->io_out, 8, cudaMemcpyDeviceToHost, e->stream));
+    TQ_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    TQ_TRY(check_status(e));
+    e->pos += 1;
+    if (next_token) *next_token = e->h_io[2];
+    return TQB200_OK;
+}
+
+int tqb200_engine_generate(tqb200_engine *e, int token_id, int n_steps, int *out_tokens,
+                           float *device_ms) {
+    TQ_CHECK_ARG(e && out_tokens && n_steps >= 0, "bad generate arguments");
+    TQ_CHECK_ARG(token_id >= 0 && token_id < e->d.vocab, "token_id %d out of range", token_id);
+    TQ_CHECK_ARG(e->pos + n_steps <= e->o.max_seq_len, "positions %d..%d exceed max_seq_len %d",
+                 e->pos, e->pos + n_steps, e->o.max_seq_len);
+    if (n_steps == 0) return TQB200_OK;
+    TQ_CUDA_TRY(cudaSetDevice(e->device));
+    if (!e->loop_exec) TQ_TRY(capture(e, true, &e->loop_graph, &e->loop_exec));
+    e->h_io[0] = token_id;
+    e->h_io[1] = e->pos;
+    TQ_CUDA_TRY(cudaMemcpyAsync(e->io_in, e->h_io, 8, cudaMemcpyHostToDevice, e->stream));
+    TQ_CUDA_TRY(cudaMemsetAsync(e->gen_count, 0, 4, e->stream));
+    TQ_CUDA_TRY(cudaEventRecord(e->ev[0], e->stream));
+    for (int i = 0; i < n_steps; ++i) TQ_CUDA_TRY(cudaGraphLaunch(e->loop_exec, e->stream));
+    TQ_CUDA_TRY(cudaEventRecord(e->ev[1], e->stream));
+    TQ_CUDA_TRY(cudaMemcpyAsync(out_tokens, e->gen_tokens, (size_t)n_steps * 4,
+                                cudaMemcpyDeviceToHost, e->stream));
+    TQ_CUDA_TRY(cudaMemcpyAsync(e->h_io + 2, e->io_out, 8, cudaMemcpyDeviceToHost, e->stream));
+    TQ_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    TQ_TRY(check_status(e));
+    if (device_ms) TQ_CUDA_TRY(cudaEventElapsedTime(device_ms, e->ev[0], e->ev[1]));
+    e->pos += n_steps;
+    return TQB200_OK;
+}
+
+int tqb200_engine_profile_step(tqb200_engine *e, int token_id, float *ms_by_kind, int n_kinds,
+                               int *next_token) {
+    TQ_CHECK_ARG(e && ms_by_kind && n_kinds > 0, "bad profile arguments");
+    TQ_CHECK_ARG(token_id >= 0 && token_id < e->d.vocab && e->pos < e->o.max_seq_len,
+                 "bad token/position");
+    TQ_CUDA_TRY(cudaSetDevice(e->device));
+    e->h_io[0] = token_id;
+    e->h_io[1] = e->pos;
+    TQ_CUDA_TRY(cudaMemcpyAsync(e->io_in, e->h_io, 8, cudaMemcpyHostToDevice, e->stream));
+    e->prof = true;
+    const int st = launch_forward(e);
+    e->prof = false;
+    if (st) return st;
+    TQ_CUDA_TRY(cudaMemcpyAsync(e->h_io + 2, e->io_out, 8, cudaMemcpyDeviceToHost, e->stream));
+    TQ_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    for (int k = 0; k < n_kinds; ++k) ms_by_kind[k] = 0.0f;
+    for (size_t i = 1; i < e->prof_ev.size(); ++i) {
+        float ms = 0.0f;
+        TQ_CUDA_TRY(cudaEventElapsedTime(&ms, e->prof_ev[i - 1], e->prof_ev[i]));
+        const int k = e->prof_kind[i];
+        if (k >= 0 && k < n_kinds) ms_by_kind[k] += ms;
+    }
+    for (auto ev : e->prof_ev) cudaEventDestroy(ev);
+    e->prof_ev.clear();
+    e->prof_kind.clear();
+    TQ_TRY(check_status(e));
+    e->pos += 1;
+    if (next_token) *next_token = e->h_io[2];
+    return TQB200_OK;
+}
+
+int tqb200_engine_reset(tqb200_engine *e) {
+    TQ_CHECK_ARG(e, "null engine");
+    e->pos = 0;  // KvCache::reset only rewinds seq_len (runtime/kv_cache.cpp:63-65)
+    return TQB200_OK;
+}
+
+int tqb200_engine_destroy(tqb200_engine *e) {
+    if (e) {
+        cudaSetDevice(e->device);
+        free_engine(e);
+    }
+    return TQB200_OK;
+}
+
+const float *tqb200_engine_logits(const tqb200_engine *e) { return e ? e->logits : nullptr; }
+
+int tqb200_engine_copy_logits(const tqb200_engine *e, float *host, int n) {
+    TQ_CHECK_ARG(e && host && n >= 0 && n <= e->d.vocab, "bad logits copy");
+    TQ_CUDA_TRY(cudaSetDevice(e->device));
+    TQ_CUDA_TRY(cudaMemcpy(host, e->logits, (size_t)n * 4, cudaMemcpyDeviceToHost));
+    return TQB200_OK;
+}
+
+int tqb200_engine_position(const tqb200_engine *e) { return e ? e->pos : -1; }
+
+int tqb200_engine_set_position(tqb200_engine *e, int pos) {
+    TQ_CHECK_ARG(e && pos >= 0 && pos < e->o.max_seq_len, "bad position");
+    e->pos = pos;
+    return TQB200_OK;
+}
+
+int tqb200_engine_stream(const tqb200_engine *e, void **stream) {
+    TQ_CHECK_ARG(e && stream, "null argument");
+    *stream = e->stream;
+    return TQB200_OK;
+}
+
+int tqb200_engine_kv_cache(const tqb200_engine *e, void **kv, size_t *bytes) {
+    TQ_CHECK_ARG(e && kv && bytes, "null argument");
+    *kv = e->kv;
+    *bytes = 2 * (size_t)e->d.n_layers * e->layer_stride * (e->o.kv_fp16 ? 2 : 4);
+    return TQB200_OK;
+}
+
+int tqb200_engine_weight_bytes(const tqb200_engine *e, size_t *bytes) {
+    TQ_CHECK_ARG(e && bytes, "null argument");
+    *bytes = e->weight_bytes;
+    return TQB200_OK;
+}
+
+}  // extern "C"

@@ -4,9 +4,12 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <stddef.h>
 #include <stdint.h>
 
 namespace tqb200 {
+
+int num_sms();
 
 // ------------------------------------------------------------------ i4
 // One matrix of a fused i4 matvec launch.  All jobs share x, in_dim and group.
@@ -18,19 +21,91 @@ struct I4Job {
     int rows;
 };
 
-// y_j = W_j x (+bias_j) for up to 3 jobs in one launch (q/k/v, gate/up, ...).
+// Where the kernel's activation vector comes from.
+enum XMode : int {
+    X_PLAIN = 0,    // x = src
+    X_RMSNORM = 1,  // x = rmsnorm(src) * norm_w      (rmsnorm_ref semantics)
+    X_SWIGLU = 2,   // x = src / (1 + expf(-src)) * up (swiglu_ref semantics)
+};
+
+struct XSource {
+    int mode = X_PLAIN;
+    const float *src = nullptr;
+    const float *norm_w = nullptr;
+    float eps = 0.0f;
+    const float *up = nullptr;
+};
+
+// Greedy-token epilogue: argmax over all rows of job 0 (first index of the max).
+struct ArgmaxOut {
+    float *part_v = nullptr;        // [>= grid] per-CTA partials
+    int *part_i = nullptr;
+    unsigned int *ticket = nullptr; // zero-initialised; reset by the last CTA
+    int *token = nullptr;           // result
+};
+
+struct I4LaunchOpts {
+    XSource x;
+    ArgmaxOut argmax;
+    bool pdl = false;               // launch with programmatic stream serialisation
+    int *status = nullptr;          // device error word (bounded-wait timeouts)
+};
+
+// y_j = W_j x (+bias_j / +resid_j) for up to 3 jobs in one launch (q/k/v, gate/up, ...).
 int launch_i4_matvec(const I4Job *jobs, int n_jobs, const float *x, int in_dim, int group_size,
                      cudaStream_t stream);
+int launch_i4_matvec_ex(const I4Job *jobs, int n_jobs, int in_dim, int group_size,
+                        const I4LaunchOpts &opts, cudaStream_t stream);
+int i4_argmax_slots(int rows, int in_dim, int group_size);  // partial slots the epilogue needs
 // Symmetric W4A8 ("sdot5") semantics.
 int launch_i4_matvec_sym(const uint8_t *w, const float *x, float *y, int rows, int in_dim,
                          int group_size, cudaStream_t stream);
 // Bit-exact dequant of `rows` rows to fp32.
 int launch_i4_dequant(const uint8_t *w, int rows, int dim, int group_size, float *out,
                       cudaStream_t stream);
-// One dequantised row (embedding lookup, dequant_i4_row) selected on device by *token.
-int launch_i4_embed_row(const uint8_t *w, const int *token, int dim, int group_size, float *out,
-                        cudaStream_t stream);
 
-int num_sms();
+// ------------------------------------------------------------------ decode ops
+int launch_rmsnorm(const float *x, const float *w, float *y, int rows, int n, float eps,
+                   cudaStream_t st);
+int launch_rope(float *q, float *k, int n_heads, int n_kv_heads, int head_dim, int pos,
+                float theta, cudaStream_t st);
+
+struct QkRopeKvArgs {
+    float *q;                 // [H*hd] in/out
+    const float *k, *v;       // [KVH*hd]
+    const float *q_norm, *k_norm;  // optional [hd]
+    float eps;
+    const float *cos_tab, *sin_tab;  // [max_seq][hd/2]
+    const int *pos;
+    void *kcache, *vcache;    // layer slices [KVH][max_seq][hd]
+    int kv_fp16;
+    int n_heads, n_kv_heads, head_dim, max_seq;
+};
+int launch_qk_rope_kv(const QkRopeKvArgs &a, cudaStream_t st);
+
+struct AttnArgs {
+    const float *q;           // [H*hd]
+    const void *k, *v;        // [KVH][max_seq][hd] fp32 or fp16
+    int kv_fp16;
+    const int *pos;           // seq = *pos + 1 (nullptr -> seq_len)
+    int seq_len, max_seq;
+    int n_heads, n_kv_heads, head_dim;
+    float scale;
+    int nsplit, chunk_max;
+    float *partial;           // attn_partial_floats(...)
+    unsigned int *tickets;    // [n_kv_heads], zero-initialised
+    float *out;               // [H*hd]
+};
+int attn_plan(int n_kv_heads, int max_seq, int *nsplit, int *chunk_max);
+size_t attn_partial_floats(int n_heads, int head_dim, int nsplit);
+int launch_attention(const AttnArgs &a, cudaStream_t st);
+
+int launch_swiglu(float *g, const float *u, int n, cudaStream_t st);
+int argmax_blocks(int n);
+int launch_argmax(const float *l, int n, float *pv, int *pi, unsigned int *ticket, int *out,
+                  cudaStream_t st);
+int launch_topk_softmax(const float *logits, int n, int k, int *idx, float *w, cudaStream_t st);
+int launch_embed(const void *table, int dtype, const int *token, int dim, int group_size,
+                 float *out, cudaStream_t st);
 
 }  // namespace tqb200

@@ -49,6 +49,27 @@ PROTOTYPES = {
     "tqb200_dev_matvec_i4": ([_vp, _vp, _vp, _i, _i, _i, _vp], _i),
     "tqb200_dev_matvec_i4_sym": ([_vp, _vp, _vp, _i, _i, _i, _vp], _i),
     "tqb200_dev_dequant_i4": ([_vp, _i, _i, _i, _vp, _vp], _i),
+    "tqb200_rmsnorm": ([_f, _f, _f, _i, _fl], _i),
+    "tqb200_rope": ([_f, _f, _i, _i, _i, _i, _fl], _i),
+    "tqb200_attention_decode": ([_f, _f, _f, _i, _i, _i, _i, _i, _fl, _f], _i),
+    "tqb200_attention_decode_f16kv": ([_f, _u16, _u16, _i, _i, _i, _i, _i, _fl, _f], _i),
+    "tqb200_swiglu": ([_f, _f, _i], _i),
+    "tqb200_argmax": ([_f, _i, C.POINTER(_i)], _i),
+    "tqb200_topk_softmax": ([_f, _i, _i, _i32, _f], _i),
+    "tqb200_engine_default_opts": ([_vp], None),
+    "tqb200_engine_create": ([C.POINTER(abi.ModelDesc), _vp, C.POINTER(_vp)], _i),
+    "tqb200_engine_step": ([_vp, _i, C.POINTER(_i)], _i),
+    "tqb200_engine_reset": ([_vp], _i),
+    "tqb200_engine_destroy": ([_vp], _i),
+    "tqb200_engine_logits": ([_vp], _vp),
+    "tqb200_engine_copy_logits": ([_vp, _f, _i], _i),
+    "tqb200_engine_position": ([_vp], _i),
+    "tqb200_engine_set_position": ([_vp, _i], _i),
+    "tqb200_engine_stream": ([_vp, C.POINTER(_vp)], _i),
+    "tqb200_engine_kv_cache": ([_vp, C.POINTER(_vp), C.POINTER(C.c_size_t)], _i),
+    "tqb200_engine_weight_bytes": ([_vp, C.POINTER(C.c_size_t)], _i),
+    "tqb200_engine_generate": ([_vp, _i, _i, _i32, C.POINTER(_fl)], _i),
+    "tqb200_engine_profile_step": ([_vp, _i, _f, _i, C.POINTER(_i)], _i),
 }
 
 _lib = None
@@ -158,3 +179,142 @@ def dev_matvec_i4_sym(w_ptr: int, x_ptr: int, y_ptr: int, out_dim: int, in_dim: 
 
 def dev_dequant_i4(w_ptr: int, rows: int, dim: int, group_size: int, out_ptr: int, stream=None):
     _check(load().tqb200_dev_dequant_i4(w_ptr, rows, dim, group_size, out_ptr, _stream(stream)))
+
+
+# ---------------------------------------------------------------- decode ops
+def rmsnorm(x, weight, eps: float) -> np.ndarray:
+    x = _f32(x)
+    y = np.zeros_like(x)
+    _check(load().tqb200_rmsnorm(x, _f32(weight), y, x.size, eps))
+    return y
+
+
+def rope(q, k, n_heads: int, n_kv_heads: int, head_dim: int, pos: int, theta: float):
+    q = _f32(q).copy()
+    k = _f32(k).copy()
+    _check(load().tqb200_rope(q, k, n_heads, n_kv_heads, head_dim, pos, theta))
+    return q, k
+
+
+def attention_decode(q, k_cache, v_cache, seq_len, max_seq_len, n_heads, n_kv_heads, head_dim,
+                     scale) -> np.ndarray:
+    out = np.zeros(n_heads * head_dim, np.float32)
+    _check(load().tqb200_attention_decode(_f32(q), _f32(k_cache), _f32(v_cache), seq_len,
+                                          max_seq_len, n_heads, n_kv_heads, head_dim, scale, out))
+    return out
+
+
+def attention_decode_f16kv(q, k_cache16, v_cache16, seq_len, max_seq_len, n_heads, n_kv_heads,
+                           head_dim, scale) -> np.ndarray:
+    out = np.zeros(n_heads * head_dim, np.float32)
+    _check(load().tqb200_attention_decode_f16kv(
+        _f32(q), np.ascontiguousarray(k_cache16, np.uint16),
+        np.ascontiguousarray(v_cache16, np.uint16), seq_len, max_seq_len, n_heads, n_kv_heads,
+        head_dim, scale, out))
+    return out
+
+
+def swiglu(gate, up) -> np.ndarray:
+    g = _f32(gate).copy()
+    _check(load().tqb200_swiglu(g, _f32(up), g.size))
+    return g
+
+
+def argmax(logits) -> int:
+    l = _f32(logits)
+    i = C.c_int(-1)
+    _check(load().tqb200_argmax(l, l.size, C.byref(i)))
+    return i.value
+
+
+def topk_softmax(logits, k: int):
+    l = _f32(logits)
+    idx = np.zeros(k, np.int32)
+    w = np.zeros(k, np.float32)
+    _check(load().tqb200_topk_softmax(l, l.size, k, idx, w))
+    return idx, w
+
+
+# ---------------------------------------------------------------- engine
+class EngineOpts(C.Structure):
+    _fields_ = [("max_seq_len", C.c_int), ("kv_fp16", C.c_int), ("use_graph", C.c_int),
+                ("pdl", C.c_int), ("device", C.c_int), ("reserved", C.c_int * 11)]
+
+
+class Engine:
+    """GPU decode engine (the reference's GpuDecode* registry entry, kernels/dispatch.h:353-378)."""
+
+    def __init__(self, model, max_seq_len: int = 512, kv_fp16: bool = False,
+                 use_graph: bool = True, pdl: bool = True, device: int = -1):
+        L = load()
+        self.model = model  # keeps the host weights alive through create()
+        self.vocab = model.spec.vocab
+        o = EngineOpts()
+        L.tqb200_engine_default_opts(C.byref(o))
+        o.max_seq_len, o.kv_fp16 = max_seq_len, 1 if kv_fp16 else 0
+        o.use_graph, o.pdl, o.device = 1 if use_graph else 0, 1 if pdl else 0, device
+        h = C.c_void_p()
+        _check(L.tqb200_engine_create(C.byref(model.desc), C.byref(o), C.byref(h)))
+        self.h = h
+
+    def step(self, token: int) -> int:
+        nxt = C.c_int(-1)
+        _check(load().tqb200_engine_step(self.h, int(token), C.byref(nxt)))
+        return nxt.value
+
+    def logits(self) -> np.ndarray:
+        out = np.zeros(self.vocab, np.float32)
+        _check(load().tqb200_engine_copy_logits(self.h, out, self.vocab))
+        return out
+
+    def logits_ptr(self) -> int:
+        return load().tqb200_engine_logits(self.h)
+
+    def generate(self, token: int, n_steps: int):
+        """n greedy steps with device-side token feedback; returns (tokens, device_ms)."""
+        out = np.zeros(max(1, n_steps), np.int32)
+        ms = C.c_float(0.0)
+        _check(load().tqb200_engine_generate(self.h, int(token), n_steps, out, C.byref(ms)))
+        return out[:n_steps].tolist(), ms.value
+
+    KINDS = ("embed", "qkv", "qk_rope_kv", "attention", "o_proj", "gate_up", "down", "lm_head")
+
+    def profile_step(self, token: int):
+        """One kernel-by-kernel step timed with CUDA events; returns (next, {kind: ms})."""
+        ms = np.zeros(len(self.KINDS), np.float32)
+        nxt = C.c_int(-1)
+        _check(load().tqb200_engine_profile_step(self.h, int(token), ms, ms.size, C.byref(nxt)))
+        return nxt.value, dict(zip(self.KINDS, ms.tolist()))
+
+    def reset(self):
+        _check(load().tqb200_engine_reset(self.h))
+
+    @property
+    def position(self) -> int:
+        return load().tqb200_engine_position(self.h)
+
+    def set_position(self, pos: int):
+        _check(load().tqb200_engine_set_position(self.h, pos))
+
+    def stream(self) -> int:
+        s = C.c_void_p()
+        _check(load().tqb200_engine_stream(self.h, C.byref(s)))
+        return s.value or 0
+
+    def kv_cache(self):
+        p, n = C.c_void_p(), C.c_size_t()
+        _check(load().tqb200_engine_kv_cache(self.h, C.byref(p), C.byref(n)))
+        return p.value, n.value
+
+    def weight_bytes(self) -> int:
+        n = C.c_size_t()
+        _check(load().tqb200_engine_weight_bytes(self.h, C.byref(n)))
+        return n.value
+
+    def close(self):
+        if getattr(self, "h", None):
+            load().tqb200_engine_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
