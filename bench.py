@@ -312,7 +312,7 @@ def bench_decode(args, rank, pg, pk, pk_kind):
     lib.load()
     W, K = args.warmup, args.steps
     ctx = args.ctx
-    max_seq = ctx + W + K + 8
+    max_seq = ctx + W + K + 32  # + the e2e (19) and profiled (1) steps after the timed region
     spec = qwen3_4b_spec(max_seq)
     t0 = time.time()
     sm = SynthModel(spec, seed=0)

@@ -81,6 +81,24 @@ int tqb200_dev_matvec_i4_sym(const uint8_t *w, const float *x, float *y, int out
 int tqb200_dev_dequant_i4(const uint8_t *w, int rows, int dim, int group_size, float *out,
                           void *stream);
 
+/* ------------------------------------------------------ VQ2 + BiIP rotation
+ * VQ2 tensor: [codebook 256x4 fp16 = 2048 B][one uint8 index per 4 weights, row-major]
+ * (runtime/tiny_format.h:91-103).  in_dim % 4 == 0. */
+
+/* MatvecVQ2Fn (kernels/dispatch.h:187); matvec_vq2_ref, kernels/matvec/matvec_vq2_ref.cpp:52-82. */
+int tqb200_matvec_vq2(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim);
+/* BiipRotateFn (kernels/dispatch.h:227); biip_rotate_activation_ref,
+ * kernels/biip/biip_rotate.cpp:36-69.  scale may be NULL; x == y allowed. */
+int tqb200_biip_rotate(const float *x, float *y, int dim, const float *scale, const float *sign,
+                       int block_size);
+/* Fused: y = W_vq2 * BiIP(x) in one launch (QwenModel::mv_rot, runtime/qwen_model.cpp:229-238);
+ * sign == NULL skips the rotation. */
+int tqb200_matvec_vq2_rot(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim,
+                          const float *scale, const float *sign, int block_size);
+int tqb200_dev_matvec_vq2_rot(const uint8_t *w, const float *x, float *y, int out_dim,
+                              int in_dim, const float *scale, const float *sign, int block_size,
+                              void *stream);
+
 /* -------------------------------------------------- decode ops (host pointers)
  * Same signatures and meaning as the reference's ops dispatch entries
  * (kernels/dispatch.h:298-307, shared --ops-impl name); status instead of abort. */

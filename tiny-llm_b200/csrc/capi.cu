@@ -303,6 +303,79 @@ int tqb200_dev_dequant_i4(const uint8_t *w, int rows, int dim, int group_size, f
     return launch_i4_dequant(w, rows, dim, group_size, out, (cudaStream_t)stream);
 }
 
+// ------------------------------------------------------------------ VQ2 + BiIP
+static int vq2_host(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim,
+                    const float *scale, const float *sign, int bs) {
+    TQ_CHECK_ARG(w && x && y && out_dim >= 0 && in_dim > 0 && in_dim % 4 == 0,
+                 "vq2: bad arguments (%d x %d)", out_dim, in_dim);
+    TQ_TRY(ensure_device());
+    void *dw, *dx, *dy, *dsg = nullptr, *dsc = nullptr;
+    TQ_TRY(upload_weight(0, w, 2048 + (size_t)out_dim * (in_dim / 4), &dw));
+    TQ_TRY(upload(3, x, (size_t)in_dim * 4, &dx));
+    TQ_TRY(scratch(4, (size_t)out_dim * 4, &dy));
+    if (sign) {
+        TQ_TRY(upload(7, sign, (size_t)in_dim * 4, &dsg));
+        if (scale) TQ_TRY(upload(8, scale, (size_t)in_dim * 4, &dsc));
+    }
+    VqLaunch a;
+    a.w = (const uint8_t *)dw;
+    a.y = (float *)dy;
+    a.rows = out_dim;
+    a.K = in_dim;
+    a.x.mode = X_PLAIN;
+    a.x.src = (const float *)dx;
+    a.rot_sign = (const float *)dsg;
+    a.rot_scale = (const float *)dsc;
+    a.rot_bs = bs;
+    TQ_TRY(launch_vq2_matvec(a, g_ctx.stream));
+    TQ_TRY(download(y, dy, (size_t)out_dim * 4));
+    return finish();
+}
+
+int tqb200_matvec_vq2(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    return vq2_host(w, x, y, out_dim, in_dim, nullptr, nullptr, 0);
+}
+
+int tqb200_matvec_vq2_rot(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim,
+                          const float *scale, const float *sign, int block_size) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    return vq2_host(w, x, y, out_dim, in_dim, scale, sign, block_size);
+}
+
+int tqb200_dev_matvec_vq2_rot(const uint8_t *w, const float *x, float *y, int out_dim,
+                              int in_dim, const float *scale, const float *sign, int block_size,
+                              void *stream) {
+    TQ_CHECK_ARG(w && x && y && in_dim % 4 == 0, "vq2: bad arguments");
+    VqLaunch a;
+    a.w = w;
+    a.y = y;
+    a.rows = out_dim;
+    a.K = in_dim;
+    a.x.mode = X_PLAIN;
+    a.x.src = x;
+    a.rot_sign = sign;
+    a.rot_scale = scale;
+    a.rot_bs = block_size;
+    return launch_vq2_matvec(a, (cudaStream_t)stream);
+}
+
+int tqb200_biip_rotate(const float *x, float *y, int dim, const float *scale, const float *sign,
+                       int block_size) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    TQ_CHECK_ARG(x && y && sign && dim > 0, "biip: bad arguments");
+    TQ_TRY(ensure_device());
+    void *dx, *dsg, *dsc = nullptr, *dy;
+    TQ_TRY(upload(3, x, (size_t)dim * 4, &dx));
+    TQ_TRY(upload(7, sign, (size_t)dim * 4, &dsg));
+    if (scale) TQ_TRY(upload(8, scale, (size_t)dim * 4, &dsc));
+    TQ_TRY(scratch(4, (size_t)dim * 4, &dy));
+    TQ_TRY(launch_biip((const float *)dx, (float *)dy, dim, (const float *)dsc, (const float *)dsg,
+                       block_size, g_ctx.stream));
+    TQ_TRY(download(y, dy, (size_t)dim * 4));
+    return finish();
+}
+
 // ------------------------------------------------------------------ decode ops (host pointers)
 int tqb200_rmsnorm(const float *x, const float *weight, float *y, int n, float eps) {
     std::lock_guard<std::mutex> lk(g_mu);

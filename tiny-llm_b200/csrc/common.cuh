@@ -152,6 +152,12 @@ __device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gmem_src, u
 }
 
 // Device error codes written to an int status word by kernels with bounded waits.
-enum : int { kDevOk = 0, kDevTimeoutTma = 1 };
+enum : int {
+    kDevOk = 0,
+    kDevTimeoutTma = 1,   // a TMA bulk copy did not complete within the wait bound
+    kDevBadStage = 2,     // a pass did not fit its shared-memory stage (host planning bug)
+    kDevBadToken = 3,     // token id outside [0, vocab)
+    kDevBadPosition = 4,  // position outside [0, max_seq)
+};
 
 }  // namespace tqb200

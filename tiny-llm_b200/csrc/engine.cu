@@ -73,6 +73,8 @@ struct tqb200_engine {
     cudaEvent_t ev[2] = {nullptr, nullptr};
     // profiling: events after every launch, tagged with a kernel kind
     bool prof = false;
+    bool debug_sync = false;  // TQB200_DEBUG_SYNC=1: no graph, check every kernel
+    int cur_layer = -1;
     std::vector<cudaEvent_t> prof_ev;
     std::vector<int> prof_kind;
     int pos = 0;
@@ -195,7 +197,25 @@ int build_rope_tables(tqb200_engine *e) {
 
 enum Kind { K_EMBED, K_QKV, K_ROPE_KV, K_ATTN, K_OPROJ, K_GATEUP, K_DOWN, K_LMHEAD, K_NKINDS };
 
+const char *kind_name(int k) {
+    static const char *n[] = {"embed", "qkv", "qk_rope_kv", "attention",
+                              "o_proj", "gate_up", "down", "lm_head"};
+    return (k >= 0 && k < K_NKINDS) ? n[k] : "start";
+}
+
 int mark(tqb200_engine *e, int kind) {
+    if (e->debug_sync) {
+        // diagnostic mode (TQB200_DEBUG_SYNC=1): finish every kernel and check it
+        const cudaError_t ce = cudaStreamSynchronize(e->stream);
+        if (ce != cudaSuccess)
+            return set_error(TQB200_ERR_CUDA, "after %s (layer %d, position %d): %s",
+                             kind_name(kind), e->cur_layer, e->pos, cudaGetErrorString(ce));
+        int stv = 0;
+        TQ_CUDA_TRY(cudaMemcpy(&stv, e->io_out + 1, 4, cudaMemcpyDeviceToHost));
+        if (stv)
+            return set_error(TQB200_ERR_TIMEOUT, "device status %d after %s (layer %d)", stv,
+                             kind_name(kind), e->cur_layer);
+    }
     if (!e->prof) return TQB200_OK;
     cudaEvent_t ev;
     TQ_CUDA_TRY(cudaEventCreate(&ev));
@@ -228,6 +248,7 @@ int launch_forward(tqb200_engine *e) {
     TQ_TRY(mark(e, K_EMBED));
     for (int l = 0; l < d.n_layers; ++l) {
         const DLayer &w = e->layers[l];
+        e->cur_layer = l;
         {   // q/k/v with the input RMSNorm fused into the prologue, biases into the epilogue
             I4Job j[3] = {{w.q, e->q, w.q_bias, nullptr, qd},
                           {w.k, e->k, w.k_bias, nullptr, kvd},
@@ -376,6 +397,11 @@ void free_engine(tqb200_engine *e) {
 int create_impl(const tqb200_model_desc *desc, const tqb200_engine_opts *opts, tqb200_engine *e) {
     e->d = *desc;
     e->o = *opts;
+    const char *dbg = getenv("TQB200_DEBUG_SYNC");
+    if (dbg && dbg[0] == '1') {
+        e->debug_sync = true;
+        e->o.use_graph = 0;
+    }
     const tqb200_model_desc &d = e->d;
     TQ_TRY(validate(d, e->o));
     int ndev = 0;
@@ -533,13 +559,22 @@ int tqb200_engine_generate(tqb200_engine *e, int token_id, int n_steps, int *out
                  e->pos, e->pos + n_steps, e->o.max_seq_len);
     if (n_steps == 0) return TQB200_OK;
     TQ_CUDA_TRY(cudaSetDevice(e->device));
-    if (!e->loop_exec) TQ_TRY(capture(e, true, &e->loop_graph, &e->loop_exec));
+    if (e->o.use_graph && !e->loop_exec) TQ_TRY(capture(e, true, &e->loop_graph, &e->loop_exec));
     e->h_io[0] = token_id;
     e->h_io[1] = e->pos;
     TQ_CUDA_TRY(cudaMemcpyAsync(e->io_in, e->h_io, 8, cudaMemcpyHostToDevice, e->stream));
     TQ_CUDA_TRY(cudaMemsetAsync(e->gen_count, 0, 4, e->stream));
     TQ_CUDA_TRY(cudaEventRecord(e->ev[0], e->stream));
-    for (int i = 0; i < n_steps; ++i) TQ_CUDA_TRY(cudaGraphLaunch(e->loop_exec, e->stream));
+    for (int i = 0; i < n_steps; ++i) {
+        if (e->o.use_graph) {
+            TQ_CUDA_TRY(cudaGraphLaunch(e->loop_exec, e->stream));
+        } else {
+            TQ_TRY(launch_forward(e));
+            feed_next_kernel<<<1, 1, 0, e->stream>>>(e->io_in, e->io_out, e->gen_tokens,
+                                                     e->gen_count);
+            TQ_CUDA_TRY(cudaGetLastError());
+        }
+    }
     TQ_CUDA_TRY(cudaEventRecord(e->ev[1], e->stream));
     TQ_CUDA_TRY(cudaMemcpyAsync(out_tokens, e->gen_tokens, (size_t)n_steps * 4,
                                 cudaMemcpyDeviceToHost, e->stream));

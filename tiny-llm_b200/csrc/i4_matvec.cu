@@ -86,17 +86,6 @@ __device__ __forceinline__ int round_half_away(float v) {
     return (int)(v >= 0.0f ? v + 0.5f : v - 0.5f);
 }
 
-// Activation value of column `col` under the fused prologue.
-__device__ __forceinline__ float x_value(const XSource &xs, int col, float rms_scale) {
-    if (xs.mode == X_RMSNORM) return __fmul_rn(__fmul_rn(xs.src[col], rms_scale), xs.norm_w[col]);
-    if (xs.mode == X_SWIGLU) {
-        const float g = xs.src[col];
-        const float denom = __fadd_rn(1.0f, expf(-g));
-        return __fmul_rn(__fdiv_rn(g, denom), xs.up[col]);
-    }
-    return __ldg(xs.src + col);
-}
-
 __device__ __forceinline__ void better(float &bv, int &bi, float v, int i) {
     if (v > bv || (v == bv && i < bi)) {
         bv = v;
@@ -140,18 +129,23 @@ __device__ void issue_pass(const MvParams &P, int p, int s, uint64_t *bars, uint
     const int row0 = (p - P.pass_begin[j]) * P.R;
     const int row1 = min(job.rows, row0 + P.R);
     const uintptr_t a = (uintptr_t)(job.w + (size_t)row0 * RB);
-    const uintptr_t b = (uintptr_t)(job.w + (size_t)row1 * RB);
+    uintptr_t b = (uintptr_t)(job.w + (size_t)row1 * RB);
     const uintptr_t mat_end16 = (uintptr_t)(job.w + (size_t)job.rows * RB) & ~(uintptr_t)15;
     const uintptr_t a16 = a & ~(uintptr_t)15;
     uintptr_t b16 = (b + 15) & ~(uintptr_t)15;
     if (b16 > mat_end16) b16 = mat_end16;
     if (b16 < a16) b16 = a16;
     uint8_t *dst = stage_base + (size_t)s * P.stage_bytes;
+    uint32_t bytes = (uint32_t)(b16 - a16);
+    if ((size_t)(b - a16) > P.stage_bytes) {  // self-check: never write past the stage buffer
+        if (P.status) atomicExch(P.status, kDevBadStage);
+        bytes = 0;
+        b = a16;
+    }
     // ragged tail of the matrix (< 16 bytes): plain loads, published by the arrive
     for (uintptr_t q = b16; q < b; ++q) dst[q - a16] = *(const uint8_t *)q;
     s_head[s] = (uint32_t)(a - a16);
     fence_proxy_async_smem();
-    const uint32_t bytes = (uint32_t)(b16 - a16);
     mbar_arrive_expect_tx(&bars[s], bytes);
     if (bytes) bulk_g2s(dst, (const void *)a16, bytes, &bars[s]);
 }
@@ -200,33 +194,53 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
     const uint32_t hdr_off = (uint32_t)g * GB;
     const uint32_t seg_off = hdr_off + 4u + (uint32_t)(sg - g * spg) * (SEG / 2);
 
-    // ---- activation prologue
-    float rms_scale = 0.0f;
-    if (P.x.mode == X_RMSNORM) {
+    // ---- activation prologue: the whole vector into shared memory with coalesced
+    // loads (RMSNorm / SwiGLU applied there), then each thread takes its segment
+    float *xsm = red + (((size_t)P.R * nt + 3) & ~(size_t)3);  // [K + SEG] floats, zero past K
+    {
+        const int KP = nt * SEG;  // every segment a thread can own (>= K)
         double ss = 0.0;
-        for (int i = t; i < K; i += blockDim.x) {
-            const double v = (double)P.x.src[i];
-            ss += v * v;
+        for (int i = t; i < KP; i += blockDim.x) {
+            float v = 0.0f;
+            if (i < K) {
+                if (P.x.mode == X_SWIGLU) {
+                    const float gv = P.x.src[i];
+                    v = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), P.x.up[i]);
+                } else {
+                    v = P.x.src[i];
+                }
+            }
+            if (P.x.mode == X_RMSNORM) ss += (double)v * (double)v;
+            xsm[i] = v;
         }
-        ss = warp_sum_d(ss);
-        if ((t & 31) == 0) s_rd[t >> 5] = ss;
-        __syncthreads();
-        if (t < 32) {
-            double v = t < (int)(blockDim.x >> 5) ? s_rd[t] : 0.0;
-            v = warp_sum_d(v);
-            if (t == 0) s_rd[0] = v;
+        if (P.x.mode == X_RMSNORM) {
+            ss = warp_sum_d(ss);
+            if ((t & 31) == 0) s_rd[t >> 5] = ss;
+            __syncthreads();
+            if (t < 32) {
+                double v = t < (int)(blockDim.x >> 5) ? s_rd[t] : 0.0;
+                v = warp_sum_d(v);
+                if (t == 0) s_rd[0] = v;
+            }
+            __syncthreads();
+            const float mean_sq = (float)(s_rd[0] / K);
+            const float rms_scale = 1.0f / sqrtf(__fadd_rn(mean_sq, P.x.eps));
+            for (int i = t; i < K; i += blockDim.x)
+                xsm[i] = __fmul_rn(__fmul_rn(xsm[i], rms_scale), P.x.norm_w[i]);
         }
         __syncthreads();
-        const float mean_sq = (float)(s_rd[0] / K);
-        rms_scale = 1.0f / sqrtf(__fadd_rn(mean_sq, P.x.eps));
     }
     float xv[SEG];
     float X = 0.0f;
 #pragma unroll
-    for (int i = 0; i < SEG; ++i) {
-        const int col = col0 + i;
-        xv[i] = (active && col < K) ? x_value(P.x, col, rms_scale) : 0.0f;
-        X += xv[i];
+    for (int i = 0; i < SEG; i += 4) {
+        const float4 v4 = active ? *reinterpret_cast<const float4 *>(xsm + col0 + i)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+        xv[i] = v4.x, xv[i + 1] = v4.y, xv[i + 2] = v4.z, xv[i + 3] = v4.w;
+        X += v4.x;
+        X += v4.y;
+        X += v4.z;
+        X += v4.w;
     }
     float xs[MATH == MATH_F32 ? SEG : 1];
     uint32_t xd[MATH == MATH_DP4A ? 6 * NW : 1];
@@ -566,8 +580,11 @@ Shape plan(int K, int G) {
     L.RP = (int)std::max<size_t>(1, std::min<size_t>(8, (target + L.S * RB - 1) / (L.S * RB)));
     L.R = L.S * L.RP;
     L.stage_bytes = (uint32_t)(((size_t)L.R * RB + 32 + 127) / 128 * 128);
-    L.stages = (int)std::max<size_t>(2, std::min<size_t>(kMaxStages, (64 * 1024) / L.stage_bytes));
-    L.smem = 128 + (size_t)L.stages * L.stage_bytes + (size_t)L.R * L.nt * 4;
+    // one or two persistent CTAs per SM: ~96 KB of weights in flight per SM
+    L.stages = (int)std::max<size_t>(2, std::min<size_t>(kMaxStages, (48 * 1024) / L.stage_bytes));
+    const size_t kp = (size_t)L.nt * L.seg;
+    L.smem = 128 + (size_t)L.stages * L.stage_bytes + (((size_t)L.R * L.nt + 3) & ~(size_t)3) * 4 +
+             kp * 4;
     return L;
 }
 
@@ -590,7 +607,8 @@ int launch_tma(const MvParams &P, const Shape &L, int passes, bool pdl, cudaStre
         TQ_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
         attr_set = true;
     }
-    const int grid = grid_for(k, L.block, L.smem, passes);
+    // persistent: at most two CTAs per SM, so the x prologue is paid once per CTA
+    const int grid = std::min(grid_for(k, L.block, L.smem, passes), 2 * num_sms());
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(L.block);

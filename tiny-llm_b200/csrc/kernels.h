@@ -64,6 +64,21 @@ int launch_i4_matvec_sym(const uint8_t *w, const float *x, float *y, int rows, i
 int launch_i4_dequant(const uint8_t *w, int rows, int dim, int group_size, float *out,
                       cudaStream_t stream);
 
+// ------------------------------------------------------------------ VQ2 + BiIP
+struct VqLaunch {
+    const uint8_t *w = nullptr;   // [codebook 256x4 f16][rows x K/4 indices]
+    float *y = nullptr;
+    const float *resid = nullptr; // optional: y = resid + dot
+    int rows = 0, K = 0;
+    XSource x;
+    const float *rot_sign = nullptr, *rot_scale = nullptr;  // BiIP of x (sign null: none)
+    int rot_bs = 0;
+    bool pdl = false;
+};
+int launch_vq2_matvec(const VqLaunch &a, cudaStream_t st);
+int launch_biip(const float *x, float *y, int dim, const float *scale, const float *sign, int bs,
+                cudaStream_t st);
+
 // ------------------------------------------------------------------ decode ops
 int launch_rmsnorm(const float *x, const float *w, float *y, int rows, int n, float eps,
                    cudaStream_t st);

@@ -49,6 +49,10 @@ PROTOTYPES = {
     "tqb200_dev_matvec_i4": ([_vp, _vp, _vp, _i, _i, _i, _vp], _i),
     "tqb200_dev_matvec_i4_sym": ([_vp, _vp, _vp, _i, _i, _i, _vp], _i),
     "tqb200_dev_dequant_i4": ([_vp, _i, _i, _i, _vp, _vp], _i),
+    "tqb200_matvec_vq2": ([_u8, _f, _f, _i, _i], _i),
+    "tqb200_biip_rotate": ([_f, _f, _i, _vp, _vp, _i], _i),
+    "tqb200_matvec_vq2_rot": ([_u8, _f, _f, _i, _i, _vp, _vp, _i], _i),
+    "tqb200_dev_matvec_vq2_rot": ([_vp, _vp, _vp, _i, _i, _vp, _vp, _i, _vp], _i),
     "tqb200_rmsnorm": ([_f, _f, _f, _i, _fl], _i),
     "tqb200_rope": ([_f, _f, _i, _i, _i, _i, _fl], _i),
     "tqb200_attention_decode": ([_f, _f, _f, _i, _i, _i, _i, _i, _fl, _f], _i),
@@ -179,6 +183,37 @@ def dev_matvec_i4_sym(w_ptr: int, x_ptr: int, y_ptr: int, out_dim: int, in_dim: 
 
 def dev_dequant_i4(w_ptr: int, rows: int, dim: int, group_size: int, out_ptr: int, stream=None):
     _check(load().tqb200_dev_dequant_i4(w_ptr, rows, dim, group_size, out_ptr, _stream(stream)))
+
+
+# ---------------------------------------------------------------- VQ2 + BiIP
+def matvec_vq2(w, x, out_dim: int, in_dim: int) -> np.ndarray:
+    y = np.zeros(out_dim, np.float32)
+    _check(load().tqb200_matvec_vq2(_u8a(w), _f32(x), y, out_dim, in_dim))
+    return y
+
+
+def _ptr_or_none(a):
+    return None if a is None else _f32(a).ctypes.data
+
+
+def biip_rotate(x, scale, sign, block_size: int) -> np.ndarray:
+    x = _f32(x)
+    y = np.zeros_like(x)
+    sc = None if scale is None else _f32(scale)
+    sg = _f32(sign)
+    _check(load().tqb200_biip_rotate(x, y, x.size, None if sc is None else sc.ctypes.data,
+                                     sg.ctypes.data, block_size))
+    return y
+
+
+def matvec_vq2_rot(w, x, out_dim: int, in_dim: int, scale, sign, block_size: int) -> np.ndarray:
+    y = np.zeros(out_dim, np.float32)
+    sc = None if scale is None else _f32(scale)
+    sg = None if sign is None else _f32(sign)
+    _check(load().tqb200_matvec_vq2_rot(_u8a(w), _f32(x), y, out_dim, in_dim,
+                                        None if sc is None else sc.ctypes.data,
+                                        None if sg is None else sg.ctypes.data, block_size))
+    return y
 
 
 # ---------------------------------------------------------------- decode ops
