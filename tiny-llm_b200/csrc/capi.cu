@@ -395,13 +395,18 @@ int tqb200_rope(float *q, float *k, int n_heads, int n_kv_heads, int head_dim, i
     std::lock_guard<std::mutex> lk(g_mu);
     TQ_CHECK_ARG(q && k && n_heads >= 0 && n_kv_heads >= 0 && head_dim > 0 && pos >= 0,
                  "rope: bad arguments");
+    TQ_CHECK_ARG(head_dim % 2 == 0 && head_dim / 2 <= 256, "rope_ref: unsupported head_dim %d",
+                 head_dim);
     TQ_TRY(ensure_device());
-    void *dq, *dk;
+    void *dq, *dk, *dt;
     const size_t qb = (size_t)n_heads * head_dim * 4, kb = (size_t)n_kv_heads * head_dim * 4;
+    std::vector<float> tab(head_dim);
+    rope_row(theta, head_dim, pos, tab.data(), tab.data() + head_dim / 2);
     TQ_TRY(upload(3, q, qb, &dq));
     TQ_TRY(upload(7, k, kb, &dk));
-    TQ_TRY(launch_rope((float *)dq, (float *)dk, n_heads, n_kv_heads, head_dim, pos, theta,
-                       g_ctx.stream));
+    TQ_TRY(upload(8, tab.data(), (size_t)head_dim * 4, &dt));
+    TQ_TRY(launch_rope((float *)dq, (float *)dk, n_heads, n_kv_heads, head_dim, (const float *)dt,
+                       (const float *)dt + head_dim / 2, g_ctx.stream));
     TQ_TRY(download(q, dq, qb));
     TQ_TRY(download(k, dk, kb));
     return finish();

@@ -60,17 +60,19 @@ __global__ void rmsnorm_rows_kernel(const float *__restrict__ x, const float *__
     for (int i = threadIdx.x; i < n; i += blockDim.x) yr[i] = __fmul_rn(__fmul_rn(xr[i], scale), w[i]);
 }
 
-// Rotate-half RoPE with cos/sin computed on the device (per-op entry point).
+// Rotate-half RoPE with the position's cos/sin row (per-op entry point).  The row
+// comes from rope_row() on the host: the angle pos * powf(theta, -2i/hd) is so
+// ill-conditioned at long positions (a 1-ulp difference in powf moves cos by
+// ~1e-4 at pos 4095) that the rotation is only bit-exact with the reference's
+// own libm values.
 __global__ void rope_kernel(float *__restrict__ q, float *__restrict__ k, int n_heads,
-                            int n_kv_heads, int head_dim, int pos, float theta) {
+                            int n_kv_heads, int head_dim, const float *__restrict__ cs,
+                            const float *__restrict__ sn) {
     const int half = head_dim / 2;
     const int h = blockIdx.x;
     float *v = h < n_heads ? q + (size_t)h * head_dim : k + (size_t)(h - n_heads) * head_dim;
     for (int i = threadIdx.x; i < half; i += blockDim.x) {
-        const float exponent = -(float)(2 * i) / (float)head_dim;
-        const float inv_freq = powf(theta, exponent);
-        const float angle = __fmul_rn((float)pos, inv_freq);
-        const float c = cosf(angle), s = sinf(angle);
+        const float c = cs[i], s = sn[i];
         const float x0 = v[i], x1 = v[i + half];
         v[i] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
         v[i + half] = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s));
@@ -486,13 +488,23 @@ int launch_rmsnorm(const float *x, const float *w, float *y, int rows, int n, fl
     return TQB200_OK;
 }
 
-int launch_rope(float *q, float *k, int n_heads, int n_kv_heads, int head_dim, int pos,
-                float theta, cudaStream_t st) {
+void rope_row(float theta, int head_dim, int pos, float *cs, float *sn) {
+    // kernels/rope/rope_ref.cpp:74-85, same float operations and libm calls
+    for (int i = 0; i < head_dim / 2; ++i) {
+        const float exponent = -(float)(2 * i) / (float)head_dim;
+        const float inv_freq = powf(theta, exponent);
+        volatile float angle = (float)pos * inv_freq;
+        cs[i] = cosf(angle);
+        sn[i] = sinf(angle);
+    }
+}
+
+int launch_rope(float *q, float *k, int n_heads, int n_kv_heads, int head_dim, const float *cs,
+                const float *sn, cudaStream_t st) {
     TQ_CHECK_ARG(head_dim > 0 && head_dim % 2 == 0 && head_dim / 2 <= 256,
                  "rope: unsupported head_dim %d", head_dim);
     if (n_heads + n_kv_heads == 0) return TQB200_OK;
-    rope_kernel<<<n_heads + n_kv_heads, 128, 0, st>>>(q, k, n_heads, n_kv_heads, head_dim, pos,
-                                                      theta);
+    rope_kernel<<<n_heads + n_kv_heads, 128, 0, st>>>(q, k, n_heads, n_kv_heads, head_dim, cs, sn);
     TQ_CUDA_TRY(cudaGetLastError());
     return TQB200_OK;
 }

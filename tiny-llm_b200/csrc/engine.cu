@@ -175,17 +175,10 @@ int validate(const tqb200_model_desc &d, const tqb200_engine_opts &o) {
 // inv_freq = powf(theta, -(float)(2i)/(float)hd), angle = (float)pos * inv_freq.
 int build_rope_tables(tqb200_engine *e) {
     const int half = e->d.head_dim / 2, S = e->o.max_seq_len;
-    std::vector<float> cs((size_t)S * half), sn((size_t)S * half), inv(half);
-    for (int i = 0; i < half; ++i) {
-        const float exponent = -(float)(2 * i) / (float)e->d.head_dim;
-        inv[i] = powf(e->d.rope_theta, exponent);
-    }
+    std::vector<float> cs((size_t)S * half), sn((size_t)S * half);
     for (int p = 0; p < S; ++p)
-        for (int i = 0; i < half; ++i) {
-            volatile float angle = (float)p * inv[i];
-            cs[(size_t)p * half + i] = cosf(angle);
-            sn[(size_t)p * half + i] = sinf(angle);
-        }
+        rope_row(e->d.rope_theta, e->d.head_dim, p, cs.data() + (size_t)p * half,
+                 sn.data() + (size_t)p * half);
     const void *dc, *ds;
     TQ_TRY(upload_bytes(e, cs.data(), cs.size() * 4, &dc));
     TQ_TRY(upload_bytes(e, sn.data(), sn.size() * 4, &ds));

@@ -82,8 +82,10 @@ int launch_biip(const float *x, float *y, int dim, const float *scale, const flo
 // ------------------------------------------------------------------ decode ops
 int launch_rmsnorm(const float *x, const float *w, float *y, int rows, int n, float eps,
                    cudaStream_t st);
-int launch_rope(float *q, float *k, int n_heads, int n_kv_heads, int head_dim, int pos,
-                float theta, cudaStream_t st);
+// Host: the cos/sin row of one position exactly as rope_ref computes it.
+void rope_row(float theta, int head_dim, int pos, float *cs, float *sn);
+int launch_rope(float *q, float *k, int n_heads, int n_kv_heads, int head_dim, const float *cs,
+                const float *sn, cudaStream_t st);
 
 struct QkRopeKvArgs {
     float *q;                 // [H*hd] in/out
