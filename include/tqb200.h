@@ -142,8 +142,19 @@ typedef struct tqb200_engine_opts {
     int use_graph;     /* capture the step once and replay it (default 1) */
     int pdl;           /* programmatic dependent launch between kernels (default 1) */
     int device;        /* CUDA device ordinal; -1 = current */
-    int reserved[11];
+    /* Column-parallel sharding over tp_size GPUs, one process per GPU (new in this build;
+     * the reference is single-device).  Every projection's output rows, the attention
+     * heads and lm_head's vocabulary rows are split; activations are all-gathered over
+     * NCCL at each layer boundary.  All ranks call create/step/generate in lockstep. */
+    int tp_size;       /* 1 = single GPU */
+    int tp_rank;
+    unsigned char nccl_id[128];  /* from tqb200_nccl_unique_id() on one rank, shared to all */
+    int reserved[8];
 } tqb200_engine_opts;
+
+/* An NCCL unique id for tqb200_engine_opts.nccl_id (TQB200_ERR_UNSUPPORTED when the
+ * library was built without NCCL). */
+int tqb200_nccl_unique_id(unsigned char id[128]);
 
 void tqb200_engine_default_opts(tqb200_engine_opts *opts);
 /* GpuDecodeCreateFn (kernels/dispatch.h:356). */

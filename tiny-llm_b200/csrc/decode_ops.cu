@@ -300,12 +300,71 @@ __global__ void __launch_bounds__(kAttnThreads)
     if (tid == 0) tickets[kh] = 0u;
 }
 
+// Any head_dim / group size: one CTA per query head, scores for every position in
+// shared memory, exact max/sum softmax, then P.V with one thread per dimension.
+template <typename KV>
+__global__ void attn_generic_kernel(const float *__restrict__ q, const KV *__restrict__ kc,
+                                    const KV *__restrict__ vc, const int *__restrict__ pos_p,
+                                    int seq_len, int max_seq, int n_heads, int n_kv_heads,
+                                    int head_dim, float scale, float *__restrict__ out) {
+    extern __shared__ float sc[];  // [seq]
+    __shared__ float s_red[32];
+    const int h = blockIdx.x, tid = threadIdx.x;
+    const int kvh = h / (n_heads / n_kv_heads);
+    const int seq = pos_p ? (*pos_p + 1) : seq_len;
+    const float *qh = q + (size_t)h * head_dim;
+    const KV *kb = kc + (size_t)kvh * max_seq * head_dim;
+    const KV *vb = vc + (size_t)kvh * max_seq * head_dim;
+    auto ld = [](const KV *p, size_t i) -> float {
+        if constexpr (sizeof(KV) == 2) return h2f(((const uint16_t *)p)[i]);
+        else return ((const float *)p)[i];
+    };
+    float m = -INFINITY;
+    for (int t = tid; t < seq; t += blockDim.x) {
+        float a = 0.0f;
+        for (int i = 0; i < head_dim; ++i) a = fmaf(qh[i], ld(kb, (size_t)t * head_dim + i), a);
+        sc[t] = a * scale;
+        m = fmaxf(m, sc[t]);
+    }
+    const int lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) s_red[warp] = m;
+    __syncthreads();
+    m = -INFINITY;
+    for (int w = 0; w < nw; ++w) m = fmaxf(m, s_red[w]);
+    __syncthreads();
+    float l = 0.0f;
+    for (int t = tid; t < seq; t += blockDim.x) {
+        sc[t] = expf(sc[t] - m);
+        l += sc[t];
+    }
+    l = warp_sum(l);
+    if (lane == 0) s_red[warp] = l;
+    __syncthreads();
+    l = 0.0f;
+    for (int w = 0; w < nw; ++w) l += s_red[w];
+    for (int d = tid; d < head_dim; d += blockDim.x) {
+        float o = 0.0f;
+        for (int t = 0; t < seq; ++t) o = fmaf(sc[t], ld(vb, (size_t)t * head_dim + d), o);
+        out[(size_t)h * head_dim + d] = o / l;
+    }
+}
+
 // ------------------------------------------------------------------ swiglu
 __global__ void swiglu_kernel(float *__restrict__ g, const float *__restrict__ u, int n) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const float gv = g[i];
         const float denom = __fadd_rn(1.0f, expf(-gv));
         g[i] = __fmul_rn(__fdiv_rn(gv, denom), u[i]);
+    }
+}
+
+__global__ void swiglu_out_kernel(const float *__restrict__ g, const float *__restrict__ u,
+                                  float *__restrict__ out, int n) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const float gv = g[i];
+        out[i] = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), u[i]);
     }
 }
 
@@ -374,6 +433,15 @@ __global__ void argmax_kernel(const float *__restrict__ l, int n, float *__restr
         *out = bi == INT_MAX ? 0 : bi;
         *ticket = 0u;
     }
+}
+
+// Global greedy token from per-rank (max, index) pairs: largest value, then lowest index.
+__global__ void argmax_pairs_kernel(const ArgPair *__restrict__ pairs, int n, int *__restrict__ out) {
+    if (threadIdx.x != 0) return;
+    float bv = -INFINITY;
+    int bi = INT_MAX;
+    for (int r = 0; r < n; ++r) better(bv, bi, pairs[r].v, pairs[r].i);
+    *out = bi == INT_MAX ? 0 : bi;
 }
 
 // ------------------------------------------------------------------ top-k softmax
@@ -473,8 +541,17 @@ int launch_attn_kv(const AttnArgs &a, cudaStream_t st) {
     TQ_ATTN_CASE(128, 8) TQ_ATTN_CASE(32, 1) TQ_ATTN_CASE(32, 2) TQ_ATTN_CASE(32, 4)
     TQ_ATTN_CASE(32, 8)
 #undef TQ_ATTN_CASE
-    return set_error(TQB200_ERR_UNSUPPORTED, "attention: head_dim %d with %d heads per KV head",
-                     a.head_dim, G);
+    // other shapes: the generic one-CTA-per-head kernel (no scratch, any head_dim)
+    const size_t smem = (size_t)a.max_seq * 4;
+    TQ_CHECK_ARG(smem <= 200 * 1024, "attention: max_seq %d too long for the generic kernel",
+                 a.max_seq);
+    auto k = attn_generic_kernel<KV>;
+    if (smem > 48 * 1024)
+        TQ_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    k<<<a.n_heads, 128, smem, st>>>(a.q, (const KV *)a.k, (const KV *)a.v, a.pos, a.seq_len,
+                                    a.max_seq, a.n_heads, a.n_kv_heads, a.head_dim, a.scale, a.out);
+    TQ_CUDA_TRY(cudaGetLastError());
+    return TQB200_OK;
 }
 
 }  // namespace
@@ -552,6 +629,21 @@ int launch_swiglu(float *g, const float *u, int n, cudaStream_t st) {
     const int block = 256;
     const int grid = std::min((n + block - 1) / block, num_sms() * 8);
     swiglu_kernel<<<grid, block, 0, st>>>(g, u, n);
+    TQ_CUDA_TRY(cudaGetLastError());
+    return TQB200_OK;
+}
+
+int launch_swiglu_out(const float *g, const float *u, float *out, int n, cudaStream_t st) {
+    if (n == 0) return TQB200_OK;
+    const int block = 256;
+    const int grid = std::min((n + block - 1) / block, num_sms() * 8);
+    swiglu_out_kernel<<<grid, block, 0, st>>>(g, u, out, n);
+    TQ_CUDA_TRY(cudaGetLastError());
+    return TQB200_OK;
+}
+
+int launch_argmax_pairs(const ArgPair *pairs, int n, int *out, cudaStream_t st) {
+    argmax_pairs_kernel<<<1, 32, 0, st>>>(pairs, n, out);
     TQ_CUDA_TRY(cudaGetLastError());
     return TQB200_OK;
 }

@@ -17,6 +17,15 @@
 // finishes.  Per step the host moves 8 bytes in (token, position) and 8 bytes
 // out (next token, device status) through pinned memory, like the reference
 // engine's 2 x 4 B H2D + 4 B D2H (kernels/cuda/gpu_engine.cu:332-371).
+//
+// Tensor parallelism (tp_size > 1, one process per GPU): every projection's
+// output rows are split evenly (q/k/v by head, o/down by hidden row, gate/up by
+// intermediate row, lm_head by vocabulary row); each rank runs the same kernels
+// on its rows and the activations are all-gathered in place over NCCL (inside
+// the CUDA graph) after attention, o_proj, SwiGLU and down.  Every output
+// element is computed by exactly the kernel and order the single-GPU engine
+// uses, so tokens and logits do not depend on the number of GPUs.  The greedy
+// token is the first maximum over the ranks' (max, index) pairs.
 #include <cmath>
 #include <cstring>
 #include <string>
@@ -24,6 +33,9 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#ifdef TQB200_HAVE_NCCL
+#include <nccl.h>
+#endif
 
 namespace tqb200 {
 namespace {
@@ -79,6 +91,13 @@ struct tqb200_engine {
     std::vector<int> prof_kind;
     int pos = 0;
     size_t weight_bytes = 0;
+    // tensor parallelism
+    int tp = 1, rank = 0;
+    float *act = nullptr;              // [inter] SwiGLU output, all-gathered (tp > 1)
+    tqb200::ArgPair *pairs = nullptr;  // [tp] per-rank (max, index)
+#ifdef TQB200_HAVE_NCCL
+    ncclComm_t comm = nullptr;
+#endif
 };
 
 namespace tqb200 {
@@ -131,6 +150,15 @@ int need_i4(const tqb200_matrix &m, int rows, int cols, const char *what, int la
 int up_i4(tqb200_engine *e, const tqb200_matrix &m, const uint8_t **out) {
     const void *p;
     TQ_TRY(upload_bytes(e, m.data, mat_bytes(m, e->d.group_size), &p));
+    *out = (const uint8_t *)p;
+    return TQB200_OK;
+}
+
+// Rows [r0, r0 + n) of an i4 matrix (a contiguous byte range of the interleaved layout).
+int up_i4_rows(tqb200_engine *e, const tqb200_matrix &m, int r0, int n, const uint8_t **out) {
+    const size_t rb = tqb200_i4_row_bytes(m.cols, e->d.group_size);
+    const void *p;
+    TQ_TRY(upload_bytes(e, (const uint8_t *)m.data + (size_t)r0 * rb, (size_t)n * rb, &p));
     *out = (const uint8_t *)p;
     return TQB200_OK;
 }
@@ -228,14 +256,35 @@ __global__ void feed_next_kernel(int *io_in, const int *io_out, int *tokens, int
     *count = c + 1;
 }
 
+// In-place all-gather of `count` floats per rank (rank r's slice at buf + r * count).
+int allgather(tqb200_engine *e, float *buf, size_t count) {
+    if (e->tp == 1) return TQB200_OK;
+#ifdef TQB200_HAVE_NCCL
+    const ncclResult_t nr =
+        ncclAllGather(buf + (size_t)e->rank * count, buf, count, ncclFloat, e->comm, e->stream);
+    if (nr != ncclSuccess)
+        return set_error(TQB200_ERR_CUDA, "ncclAllGather: %s", ncclGetErrorString(nr));
+    return TQB200_OK;
+#else
+    (void)buf;
+    (void)count;
+    return set_error(TQB200_ERR_UNSUPPORTED, "built without NCCL");
+#endif
+}
+
 // One decode step's kernels, stream-ordered on e->stream.
 int launch_forward(tqb200_engine *e) {
     const tqb200_model_desc &d = e->d;
     cudaStream_t st = e->stream;
+    const int G = e->tp, r = e->rank;
     const int H = d.hidden, hd = d.head_dim;
-    const int qd = d.n_heads * hd, kvd = d.n_kv_heads * hd;
+    const int qd = d.n_heads * hd;
+    const int Hl = d.n_heads / G, KVl = d.n_kv_heads / G;
+    const int qdl = Hl * hd, kvdl = KVl * hd, Hs = H / G, Is = d.inter / G, Vs = d.vocab / G;
     const bool pdl = e->o.pdl != 0;
     int *status = e->io_out + 1;
+    float *attn_mine = e->attn + (size_t)r * qdl;
+    float *hidden_mine = e->hidden + (size_t)r * Hs;
     TQ_TRY(mark(e, -1));
     TQ_TRY(launch_embed(e->embed, e->embed_dtype, e->io_in, H, d.group_size, e->hidden, st));
     TQ_TRY(mark(e, K_EMBED));
@@ -243,9 +292,9 @@ int launch_forward(tqb200_engine *e) {
         const DLayer &w = e->layers[l];
         e->cur_layer = l;
         {   // q/k/v with the input RMSNorm fused into the prologue, biases into the epilogue
-            I4Job j[3] = {{w.q, e->q, w.q_bias, nullptr, qd},
-                          {w.k, e->k, w.k_bias, nullptr, kvd},
-                          {w.v, e->v, w.v_bias, nullptr, kvd}};
+            I4Job j[3] = {{w.q, e->q, w.q_bias, nullptr, qdl},
+                          {w.k, e->k, w.k_bias, nullptr, kvdl},
+                          {w.v, e->v, w.v_bias, nullptr, kvdl}};
             I4LaunchOpts o;
             o.x = {X_RMSNORM, e->hidden, w.input_ln, d.rms_eps, nullptr};
             o.pdl = pdl;
@@ -271,8 +320,8 @@ int launch_forward(tqb200_engine *e) {
             a.kcache = kc;
             a.vcache = vc;
             a.kv_fp16 = e->o.kv_fp16;
-            a.n_heads = d.n_heads;
-            a.n_kv_heads = d.n_kv_heads;
+            a.n_heads = Hl;
+            a.n_kv_heads = KVl;
             a.head_dim = hd;
             a.max_seq = e->o.max_seq_len;
             TQ_TRY(launch_qk_rope_kv(a, st));
@@ -287,55 +336,75 @@ int launch_forward(tqb200_engine *e) {
             a.pos = e->io_in + 1;
             a.seq_len = 0;
             a.max_seq = e->o.max_seq_len;
-            a.n_heads = d.n_heads;
-            a.n_kv_heads = d.n_kv_heads;
+            a.n_heads = Hl;
+            a.n_kv_heads = KVl;
             a.head_dim = hd;
             a.scale = 1.0f / sqrtf((float)hd);
             a.nsplit = e->attn_nsplit;
             a.chunk_max = e->attn_chunk;
             a.partial = e->attn_part;
             a.tickets = e->attn_tickets;
-            a.out = e->attn;
+            a.out = attn_mine;
             TQ_TRY(launch_attention(a, st));
+            TQ_TRY(allgather(e, e->attn, qdl));
             TQ_TRY(mark(e, K_ATTN));
         }
-        {   // o_proj, residual fused: hidden = hidden + W_o attn
-            I4Job j{w.o, e->hidden, nullptr, e->hidden, H};
+        {   // o_proj, residual fused: hidden = hidden + W_o attn (this rank's rows)
+            I4Job j{w.o, hidden_mine, nullptr, hidden_mine, Hs};
             I4LaunchOpts o;
             o.x = {X_PLAIN, e->attn, nullptr, 0.0f, nullptr};
             o.pdl = pdl;
             o.status = status;
             TQ_TRY(launch_i4_matvec_ex(&j, 1, qd, d.group_size, o, st));
+            TQ_TRY(allgather(e, e->hidden, Hs));
             TQ_TRY(mark(e, K_OPROJ));
         }
-        {   // gate/up with the post-attention RMSNorm fused into the prologue
-            I4Job j[2] = {{w.gate, e->gate, nullptr, nullptr, d.inter},
-                          {w.up, e->up, nullptr, nullptr, d.inter}};
+        {   // gate/up in one pass per row block (post-attention RMSNorm in the prologue),
+            // SwiGLU of each (gate, up) row pair in the epilogue -> act
+            I4Job j[2] = {{w.gate, e->act + (size_t)r * Is, nullptr, nullptr, Is},
+                          {w.up, e->up, nullptr, nullptr, Is}};
             I4LaunchOpts o;
             o.x = {X_RMSNORM, e->hidden, w.post_ln, d.rms_eps, nullptr};
+            o.pair_swiglu = true;
             o.pdl = pdl;
             o.status = status;
             TQ_TRY(launch_i4_matvec_ex(j, 2, H, d.group_size, o, st));
+            TQ_TRY(allgather(e, e->act, Is));
             TQ_TRY(mark(e, K_GATEUP));
         }
-        {   // down with SwiGLU in the prologue and the residual in the epilogue
-            I4Job j{w.down, e->hidden, nullptr, e->hidden, H};
+        {   // down with the residual in the epilogue
+            I4Job j{w.down, hidden_mine, nullptr, hidden_mine, Hs};
             I4LaunchOpts o;
-            o.x = {X_SWIGLU, e->gate, nullptr, 0.0f, e->up};
+            o.x = {X_PLAIN, e->act, nullptr, 0.0f, nullptr};
             o.pdl = pdl;
             o.status = status;
             TQ_TRY(launch_i4_matvec_ex(&j, 1, d.inter, d.group_size, o, st));
+            TQ_TRY(allgather(e, e->hidden, Hs));
             TQ_TRY(mark(e, K_DOWN));
         }
     }
     {   // lm_head with the final RMSNorm in the prologue and the greedy argmax in the epilogue
-        I4Job j{e->lm_head, e->logits, nullptr, nullptr, d.vocab};
+        I4Job j{e->lm_head, e->logits + (size_t)r * Vs, nullptr, nullptr, Vs};
         I4LaunchOpts o;
         o.x = {X_RMSNORM, e->hidden, e->final_norm, d.rms_eps, nullptr};
-        o.argmax = {e->am_v, e->am_i, e->am_ticket, e->io_out};
+        o.argmax.part_v = e->am_v;
+        o.argmax.part_i = e->am_i;
+        o.argmax.ticket = e->am_ticket;
+        o.argmax.row_offset = r * Vs;
+        if (G == 1) {
+            o.argmax.token = e->io_out;
+        } else {
+            o.argmax.token = &e->pairs[r].i;
+            o.argmax.value = &e->pairs[r].v;
+        }
         o.pdl = pdl;
         o.status = status;
         TQ_TRY(launch_i4_matvec_ex(&j, 1, H, d.group_size, o, st));
+        if (G > 1) {
+            TQ_TRY(allgather(e, reinterpret_cast<float *>(e->pairs), 2));
+            TQ_TRY(allgather(e, e->logits, Vs));
+            TQ_TRY(launch_argmax_pairs(e->pairs, G, e->io_out, st));
+        }
         TQ_TRY(mark(e, K_LMHEAD));
     }
     return TQB200_OK;
@@ -381,6 +450,9 @@ void free_engine(tqb200_engine *e) {
     for (auto ev : e->ev)
         if (ev) cudaEventDestroy(ev);
     for (auto ev : e->prof_ev) cudaEventDestroy(ev);
+#ifdef TQB200_HAVE_NCCL
+    if (e->comm) ncclCommDestroy(e->comm);
+#endif
     for (void *p : e->allocs) cudaFree(p);
     if (e->h_io) cudaFreeHost(e->h_io);
     if (e->stream) cudaStreamDestroy(e->stream);
@@ -406,6 +478,28 @@ int create_impl(const tqb200_model_desc *desc, const tqb200_engine_opts *opts, t
     TQ_CUDA_TRY(cudaGetDevice(&e->device));
     TQ_CUDA_TRY(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
     const int H = d.hidden, hd = d.head_dim, qd = d.n_heads * hd, kvd = d.n_kv_heads * hd;
+    e->tp = e->o.tp_size > 0 ? e->o.tp_size : 1;
+    e->rank = e->o.tp_rank;
+    const int G = e->tp, r = e->rank;
+    TQ_CHECK_ARG(r >= 0 && r < G, "tp_rank %d outside tp_size %d", r, G);
+    TQ_CHECK_ARG(d.n_heads % G == 0 && d.n_kv_heads % G == 0 && H % G == 0 && d.inter % G == 0 &&
+                     d.vocab % G == 0,
+                 "tp_size %d must divide heads %d, kv heads %d, hidden %d, inter %d, vocab %d", G,
+                 d.n_heads, d.n_kv_heads, H, d.inter, d.vocab);
+    const int qdl = qd / G, kvdl = kvd / G, Hs = H / G, Is = d.inter / G, Vs = d.vocab / G;
+#ifdef TQB200_HAVE_NCCL
+    if (G > 1) {
+        ncclUniqueId id;
+        static_assert(sizeof(id) == sizeof(e->o.nccl_id), "NCCL id size");
+        memcpy(&id, e->o.nccl_id, sizeof(id));
+        const ncclResult_t nr = ncclCommInitRank(&e->comm, G, id, r);
+        if (nr != ncclSuccess)
+            return set_error(TQB200_ERR_CUDA, "ncclCommInitRank(rank %d of %d): %s", r, G,
+                             ncclGetErrorString(nr));
+    }
+#else
+    TQ_CHECK_ARG(G == 1, "this build has no NCCL: tp_size must be 1");
+#endif
     e->layers.resize(d.n_layers);
     for (int l = 0; l < d.n_layers; ++l) {
         const tqb200_layer &s = d.layers[l];
@@ -424,45 +518,49 @@ int create_impl(const tqb200_model_desc *desc, const tqb200_engine_opts *opts, t
                      "layer %d: BiIP-rotated projections are not on the i4 engine path", l);
         TQ_TRY(up_vec(e, s.input_ln, H, &w.input_ln));
         TQ_TRY(up_vec(e, s.post_ln, H, &w.post_ln));
-        TQ_TRY(up_i4(e, s.q_proj, &w.q));
-        TQ_TRY(up_i4(e, s.k_proj, &w.k));
-        TQ_TRY(up_i4(e, s.v_proj, &w.v));
-        TQ_TRY(up_i4(e, s.o_proj, &w.o));
-        TQ_TRY(up_i4(e, s.gate_proj, &w.gate));
-        TQ_TRY(up_i4(e, s.up_proj, &w.up));
-        TQ_TRY(up_i4(e, s.down_proj, &w.down));
-        TQ_TRY(up_vec(e, s.q_bias, qd, &w.q_bias));
-        TQ_TRY(up_vec(e, s.k_bias, kvd, &w.k_bias));
-        TQ_TRY(up_vec(e, s.v_bias, kvd, &w.v_bias));
+        // this rank's rows (all rows when tp == 1)
+        TQ_TRY(up_i4_rows(e, s.q_proj, r * qdl, qdl, &w.q));
+        TQ_TRY(up_i4_rows(e, s.k_proj, r * kvdl, kvdl, &w.k));
+        TQ_TRY(up_i4_rows(e, s.v_proj, r * kvdl, kvdl, &w.v));
+        TQ_TRY(up_i4_rows(e, s.o_proj, r * Hs, Hs, &w.o));
+        TQ_TRY(up_i4_rows(e, s.gate_proj, r * Is, Is, &w.gate));
+        TQ_TRY(up_i4_rows(e, s.up_proj, r * Is, Is, &w.up));
+        TQ_TRY(up_i4_rows(e, s.down_proj, r * Hs, Hs, &w.down));
+        TQ_TRY(up_vec(e, s.q_bias ? s.q_bias + r * qdl : nullptr, qdl, &w.q_bias));
+        TQ_TRY(up_vec(e, s.k_bias ? s.k_bias + r * kvdl : nullptr, kvdl, &w.k_bias));
+        TQ_TRY(up_vec(e, s.v_bias ? s.v_bias + r * kvdl : nullptr, kvdl, &w.v_bias));
         TQ_TRY(up_vec(e, s.q_norm, hd, &w.q_norm));
         TQ_TRY(up_vec(e, s.k_norm, hd, &w.k_norm));
     }
     e->embed_dtype = d.embed.dtype;
     TQ_TRY(upload_bytes(e, d.embed.data, mat_bytes(d.embed, d.group_size), &e->embed));
-    if (d.lm_head.data == d.embed.data && d.embed.dtype == TQB200_DT_I4)
+    if (G == 1 && d.lm_head.data == d.embed.data && d.embed.dtype == TQB200_DT_I4)
         e->lm_head = (const uint8_t *)e->embed;  // tied compact-i4 embedding
     else
-        TQ_TRY(up_i4(e, d.lm_head, &e->lm_head));
+        TQ_TRY(up_i4_rows(e, d.lm_head, r * Vs, Vs, &e->lm_head));
     TQ_TRY(up_vec(e, d.final_norm, H, &e->final_norm));
     TQ_TRY(build_rope_tables(e));
 
     void *p;
-    const size_t act = (size_t)H * 2 + qd * 2 + kvd * 2 + (size_t)d.inter * 2 + d.vocab;
+    const size_t act = (size_t)H * 2 + qd * 2 + kvd * 2 + (size_t)d.inter * 3 + d.vocab + 64;
     TQ_TRY(dev_alloc(e, act * 4, &p));
     float *f = (float *)p;
     e->hidden = f, f += H;
     e->q = f, f += qd;
     e->k = f, f += kvd;
     e->v = f, f += kvd;
-    e->attn = f, f += qd;
+    e->attn = f, f += qd;   // full width: rank r's heads at [r*qdl, (r+1)*qdl)
     e->gate = f, f += d.inter;
     e->up = f, f += d.inter;
-    e->logits = f;
-    e->layer_stride = (size_t)d.n_kv_heads * e->o.max_seq_len * hd;
+    e->act = f, f += d.inter;
+    e->logits = f, f += d.vocab;
+    e->pairs = reinterpret_cast<ArgPair *>(f);
+    TQ_CHECK_ARG(G <= 32, "tp_size %d above 32", G);
+    e->layer_stride = (size_t)(d.n_kv_heads / G) * e->o.max_seq_len * hd;
     const size_t kv_bytes = 2 * (size_t)d.n_layers * e->layer_stride * (e->o.kv_fp16 ? 2 : 4);
     TQ_TRY(dev_alloc(e, kv_bytes, &e->kv));
     TQ_CUDA_TRY(cudaMemset(e->kv, 0, kv_bytes));
-    TQ_TRY(attn_plan(d.n_kv_heads, e->o.max_seq_len, &e->attn_nsplit, &e->attn_chunk));
+    TQ_TRY(attn_plan(d.n_kv_heads / G, e->o.max_seq_len, &e->attn_nsplit, &e->attn_chunk));
     TQ_TRY(dev_alloc(e, attn_partial_floats(d.n_heads, hd, e->attn_nsplit) * 4, &p));
     e->attn_part = (float *)p;
     const int slots = i4_argmax_slots(d.vocab, H, d.group_size);
@@ -499,6 +597,22 @@ void tqb200_engine_default_opts(tqb200_engine_opts *o) {
     o->use_graph = 1;
     o->pdl = 1;
     o->device = -1;
+    o->tp_size = 1;
+    o->tp_rank = 0;
+}
+
+int tqb200_nccl_unique_id(unsigned char id[128]) {
+    TQ_CHECK_ARG(id, "null id buffer");
+#ifdef TQB200_HAVE_NCCL
+    ncclUniqueId u;
+    const ncclResult_t nr = ncclGetUniqueId(&u);
+    if (nr != ncclSuccess)
+        return set_error(TQB200_ERR_CUDA, "ncclGetUniqueId: %s", ncclGetErrorString(nr));
+    memcpy(id, &u, sizeof u);
+    return TQB200_OK;
+#else
+    return set_error(TQB200_ERR_UNSUPPORTED, "built without NCCL");
+#endif
 }
 
 int tqb200_engine_create(const tqb200_model_desc *desc, const tqb200_engine_opts *opts,

@@ -54,6 +54,7 @@ struct MvParams {
     int K, G, nt, S, RP, R;
     int stages;
     uint32_t stage_bytes;
+    int pair;  // jobs 0 and 1 (gate, up) share passes; y0 = silu(W0 x) * (W1 x)
     XSource x;
     ArgmaxOut am;
     int *status;
@@ -119,15 +120,12 @@ __device__ void block_argmax(float &bv, int &bi, float *sv, int *si) {
     }
 }
 
-// Thread 0: stream the rows of pass p into stage buffer s.
-__device__ void issue_pass(const MvParams &P, int p, int s, uint64_t *bars, uint8_t *stage_base,
-                           uint32_t *s_head) {
-    int j = 0;
-    while (j + 1 < P.n_jobs && p >= P.pass_begin[j + 1]) ++j;
-    const I4Job &job = P.job[j];
+// Rows [row0, row1) of one matrix -> a 16-byte aligned shared-memory region of `cap`
+// bytes: the 16-byte aligned interior goes by one bulk copy (returned byte count),
+// the ragged tail of the matrix (< 16 bytes) by plain loads.  *head = offset of row0.
+__device__ uint32_t stage_rows(const MvParams &P, const I4Job &job, int row0, int row1,
+                               uint8_t *dst, size_t cap, uint32_t *head, const uint8_t **src16) {
     const size_t RB = (size_t)((P.K + P.G - 1) / P.G) * (4 + P.G / 2);
-    const int row0 = (p - P.pass_begin[j]) * P.R;
-    const int row1 = min(job.rows, row0 + P.R);
     const uintptr_t a = (uintptr_t)(job.w + (size_t)row0 * RB);
     uintptr_t b = (uintptr_t)(job.w + (size_t)row1 * RB);
     const uintptr_t mat_end16 = (uintptr_t)(job.w + (size_t)job.rows * RB) & ~(uintptr_t)15;
@@ -135,19 +133,38 @@ __device__ void issue_pass(const MvParams &P, int p, int s, uint64_t *bars, uint
     uintptr_t b16 = (b + 15) & ~(uintptr_t)15;
     if (b16 > mat_end16) b16 = mat_end16;
     if (b16 < a16) b16 = a16;
-    uint8_t *dst = stage_base + (size_t)s * P.stage_bytes;
     uint32_t bytes = (uint32_t)(b16 - a16);
-    if ((size_t)(b - a16) > P.stage_bytes) {  // self-check: never write past the stage buffer
+    if ((size_t)(b - a16) > cap) {  // self-check: never write past the stage buffer
         if (P.status) atomicExch(P.status, kDevBadStage);
         bytes = 0;
         b = a16;
     }
-    // ragged tail of the matrix (< 16 bytes): plain loads, published by the arrive
     for (uintptr_t q = b16; q < b; ++q) dst[q - a16] = *(const uint8_t *)q;
-    s_head[s] = (uint32_t)(a - a16);
+    *head = (uint32_t)(a - a16);
+    *src16 = (const uint8_t *)a16;
+    return bytes;
+}
+
+// Thread 0: stream the rows of pass p into stage buffer s.  In paired mode the stage
+// holds the same rows of job 0 and job 1 (gate and up) in its two halves.
+__device__ void issue_pass(const MvParams &P, int p, int s, uint64_t *bars, uint8_t *stage_base,
+                           uint32_t *s_head) {
+    int j = 0;
+    while (j + 1 < P.n_jobs && p >= P.pass_begin[j + 1]) ++j;
+    const I4Job &job = P.job[j];
+    const int row0 = (p - P.pass_begin[j]) * P.R;
+    const int row1 = min(job.rows, row0 + P.R);
+    uint8_t *dst = stage_base + (size_t)s * P.stage_bytes;
+    const size_t cap = P.pair ? P.stage_bytes / 2 : P.stage_bytes;
+    const uint8_t *src0, *src1 = nullptr;
+    const uint32_t b0 = stage_rows(P, job, row0, row1, dst, cap, &s_head[s], &src0);
+    uint32_t b1 = 0;
+    if (P.pair)
+        b1 = stage_rows(P, P.job[1], row0, row1, dst + cap, cap, &s_head[kMaxStages + s], &src1);
     fence_proxy_async_smem();
-    mbar_arrive_expect_tx(&bars[s], bytes);
-    if (bytes) bulk_g2s(dst, (const void *)a16, bytes, &bars[s]);
+    mbar_arrive_expect_tx(&bars[s], b0 + b1);
+    if (b0) bulk_g2s(dst, src0, b0, &bars[s]);
+    if (b1) bulk_g2s(dst + cap, src1, b1, &bars[s]);
 }
 
 template <int SEG, int MATH>
@@ -157,7 +174,7 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
     uint8_t *stage_base = smem + 128;
     float *red = reinterpret_cast<float *>(stage_base + (size_t)P.stages * P.stage_bytes);
-    __shared__ uint32_t s_head[kMaxStages];
+    __shared__ uint32_t s_head[2 * kMaxStages];
     __shared__ int s_err;
     __shared__ double s_rd[32];
     __shared__ float s_bv[32];
@@ -196,7 +213,8 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
 
     // ---- activation prologue: the whole vector into shared memory with coalesced
     // loads (RMSNorm / SwiGLU applied there), then each thread takes its segment
-    float *xsm = red + (((size_t)P.R * nt + 3) & ~(size_t)3);  // [K + SEG] floats, zero past K
+    // [nt * SEG] floats, zero past K
+    float *xsm = red + (((size_t)(1 + P.pair) * P.R * nt + 3) & ~(size_t)3);
     {
         const int KP = nt * SEG;  // every segment a thread can own (>= K)
         double ss = 0.0;
@@ -230,18 +248,59 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
         }
         __syncthreads();
     }
-    float xv[SEG];
-    float X = 0.0f;
+    // ---- per-segment tables, built once per CTA by all warps together (one warp per
+    // segment, SEG/32 elements per lane): the segment sum X and, for dp4a, the three
+    // int8 digit planes packed to match the nibble order of a 32-bit word
+    // (lo word = even columns, hi word = odd columns) plus the digit scales.
+    float *seg_x = xsm + (size_t)nt * SEG;                                  // [nt]
+    float *seg_sc = seg_x + nt;                                             // [nt][3]
+    uint32_t *seg_dig = reinterpret_cast<uint32_t *>(seg_sc + 3 * nt + 3);  // [nt][6*NW]
+    seg_dig = reinterpret_cast<uint32_t *>(((uintptr_t)seg_dig + 15) & ~(uintptr_t)15);
+    {
+        const int lane_ = t & 31, warp_ = t >> 5, nw_ = blockDim.x >> 5;
+        constexpr int EPL = SEG / 32;  // elements per lane
+        for (int sgi = warp_; sgi < nt; sgi += nw_) {
+            float v[EPL];
+            float sum = 0.0f, amax = 0.0f;
 #pragma unroll
-    for (int i = 0; i < SEG; i += 4) {
-        const float4 v4 = active ? *reinterpret_cast<const float4 *>(xsm + col0 + i)
-                                 : make_float4(0.f, 0.f, 0.f, 0.f);
-        xv[i] = v4.x, xv[i + 1] = v4.y, xv[i + 2] = v4.z, xv[i + 3] = v4.w;
-        X += v4.x;
-        X += v4.y;
-        X += v4.z;
-        X += v4.w;
+            for (int e = 0; e < EPL; ++e) {
+                v[e] = xsm[sgi * SEG + lane_ * EPL + e];
+                sum += v[e];
+                amax = fmaxf(amax, fabsf(v[e]));
+            }
+            sum = warp_sum(sum);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            if constexpr (MATH == MATH_DP4A) {
+                const float s0 = amax > 0.0f ? amax / 127.0f : 1.0f;
+                const float s1 = s0 / 254.0f, s2 = s1 / 254.0f;
+                const float i0 = 1.0f / s0, i1 = 1.0f / s1, i2 = 1.0f / s2;
+                uint8_t *db = reinterpret_cast<uint8_t *>(seg_dig + (size_t)sgi * 6 * NW);
+#pragma unroll
+                for (int e = 0; e < EPL; ++e) {
+                    const int c = lane_ * EPL + e;               // column within the segment
+                    const int chunk = c >> 3, k = c & 7;
+                    const int word = 6 * chunk + (k & 1), byte = k >> 1;
+                    const int q0 = max(-127, min(127, round_half_away(v[e] * i0)));
+                    const float r1 = fmaf(-(float)q0, s0, v[e]);
+                    const int q1 = max(-127, min(127, round_half_away(r1 * i1)));
+                    const float r2 = fmaf(-(float)q1, s1, r1);
+                    const int q2 = max(-127, min(127, round_half_away(r2 * i2)));
+                    db[(word + 0) * 4 + byte] = (uint8_t)q0;
+                    db[(word + 2) * 4 + byte] = (uint8_t)q1;
+                    db[(word + 4) * 4 + byte] = (uint8_t)q2;
+                }
+                if (lane_ == 0) {
+                    seg_sc[3 * sgi + 0] = s0;
+                    seg_sc[3 * sgi + 1] = s1;
+                    seg_sc[3 * sgi + 2] = s2;
+                }
+            }
+            if (lane_ == 0) seg_x[sgi] = sum;
+        }
+        __syncthreads();
     }
+    const float X = seg_x[sg];
     float xs[MATH == MATH_F32 ? SEG : 1];
     uint32_t xd[MATH == MATH_DP4A ? 6 * NW : 1];
     float dsc0 = 0.0f, dsc1 = 0.0f, dsc2 = 0.0f;
@@ -251,35 +310,18 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
                 const int pos = k < 5 ? k : k - 3;
-                xs[8 * i + k] = xv[8 * i + k] * __uint_as_float((uint32_t)(127 - 4 * pos) << 23);
+                xs[8 * i + k] = xsm[col0 + 8 * i + k] * __uint_as_float((uint32_t)(127 - 4 * pos) << 23);
             }
     } else {
-        float amax = 0.0f;
+        const uint4 *src4 = reinterpret_cast<const uint4 *>(seg_dig + (size_t)sg * 6 * NW);
 #pragma unroll
-        for (int i = 0; i < SEG; ++i) amax = fmaxf(amax, fabsf(xv[i]));
-        dsc0 = amax > 0.0f ? amax / 127.0f : 1.0f;
-        dsc1 = dsc0 / 254.0f;
-        dsc2 = dsc1 / 254.0f;
-        const float i0 = 1.0f / dsc0, i1 = 1.0f / dsc1, i2 = 1.0f / dsc2;
-#pragma unroll
-        for (int i = 0; i < NW; ++i) {
-            uint32_t d[6] = {0, 0, 0, 0, 0, 0};
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const float v = xv[8 * i + k];
-                const int q0 = max(-127, min(127, round_half_away(v * i0)));
-                const float r1 = fmaf(-(float)q0, dsc0, v);
-                const int q1 = max(-127, min(127, round_half_away(r1 * i1)));
-                const float r2 = fmaf(-(float)q1, dsc1, r1);
-                const int q2 = max(-127, min(127, round_half_away(r2 * i2)));
-                const int half = k & 1, byte = k >> 1;  // even cols -> lo word, odd -> hi word
-                d[0 + half] |= ((uint32_t)q0 & 0xFFu) << (8 * byte);
-                d[2 + half] |= ((uint32_t)q1 & 0xFFu) << (8 * byte);
-                d[4 + half] |= ((uint32_t)q2 & 0xFFu) << (8 * byte);
-            }
-#pragma unroll
-            for (int m = 0; m < 6; ++m) xd[6 * i + m] = d[m];
+        for (int i = 0; i < 6 * NW / 4; ++i) {
+            const uint4 w4 = src4[i];
+            xd[4 * i + 0] = w4.x, xd[4 * i + 1] = w4.y, xd[4 * i + 2] = w4.z, xd[4 * i + 3] = w4.w;
         }
+        dsc0 = seg_sc[3 * sg + 0];
+        dsc1 = seg_sc[3 * sg + 1];
+        dsc2 = seg_sc[3 * sg + 2];
     }
 
     const int lane = t & 31, warp = t >> 5, nwarps = blockDim.x >> 5;
@@ -296,10 +338,13 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
         const I4Job &job = P.job[j];
         const int row0 = (p - P.pass_begin[j]) * P.R;
         if (!mbar_wait(&bars[s], parity, kWaitCycles)) s_err = 1;
-        const uint8_t *sb = stage_base + (size_t)s * P.stage_bytes + s_head[s];
+        const size_t half_bytes = P.stage_bytes / 2;
         if (active) {
-            for (int r = 0; r < P.RP; ++r) {
-                const int rl = slot + r * S;
+            for (int r = 0; r < P.RP * (1 + P.pair); ++r) {
+                const int jb = r >= P.RP;  // paired mode: second half = job 1
+                const int rl = slot + (r - jb * P.RP) * S;
+                const uint8_t *sb = stage_base + (size_t)s * P.stage_bytes +
+                                    (jb ? half_bytes + s_head[kMaxStages + s] : s_head[s]);
                 float part = 0.0f;
                 if (row0 + rl < job.rows) {
                     const uint8_t *rp = sb + (size_t)rl * RB;
@@ -328,7 +373,7 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
                         part = sc * fmaf(-zr, X, dot);
                     }
                 }
-                red[rl * nt + sg] = part;
+                red[(jb * P.R + rl) * nt + sg] = part;
             }
         }
         __syncthreads();
@@ -336,14 +381,27 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
         for (int rl = warp; rl < P.R; rl += nwarps) {
             const int row = row0 + rl;
             if (row >= job.rows) continue;
-            float v = 0.0f;
-            for (int i = lane; i < nt; i += 32) v += red[rl * nt + i];
-            v = warp_sum(v);
+            // segment partials summed in double, rounded once (the reference's row dot
+            // is a double sum rounded to float)
+            double vd = 0.0;
+            for (int i = lane; i < nt; i += 32) vd += (double)red[rl * nt + i];
+            float v = (float)warp_sum_d(vd);
+            float u = 0.0f;
+            if (P.pair) {
+                double ud = 0.0;
+                for (int i = lane; i < nt; i += 32) ud += (double)red[(P.R + rl) * nt + i];
+                u = (float)warp_sum_d(ud);
+            }
             if (lane == 0) {
-                if (job.bias) v += job.bias[row];
-                if (job.resid) v = job.resid[row] + v;
+                if (P.pair) {
+                    // swiglu_ref (kernels/silu/swiglu_ref.cpp:41-52) on (gate, up)
+                    v = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), u);
+                } else {
+                    if (job.bias) v += job.bias[row];
+                    if (job.resid) v = job.resid[row] + v;
+                }
                 job.y[row] = v;
-                if (P.am.token && j == 0) better(bv, bi, v, row);
+                if (P.am.token && j == 0) better(bv, bi, v, row + P.am.row_offset);
             }
         }
         __syncthreads();
@@ -381,7 +439,8 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
                 better(bv, bi, __ldcg(P.am.part_v + b), __ldcg(P.am.part_i + b));
             block_argmax(bv, bi, s_bv, s_bi);
             if (t == 0) {
-                *P.am.token = bi == INT_MAX ? 0 : bi;
+                *P.am.token = bi == INT_MAX ? P.am.row_offset : bi;
+                if (P.am.value) *P.am.value = bv;
                 *P.am.ticket = 0u;
             }
         }
@@ -564,7 +623,7 @@ struct Shape {
     size_t smem = 0;
 };
 
-Shape plan(int K, int G) {
+Shape plan(int K, int G, bool pair) {
     Shape L;
     L.seg = (G % 64 == 0) ? 64 : 32;
     const int ng = (K + G - 1) / G;
@@ -579,12 +638,14 @@ Shape plan(int K, int G) {
     const size_t target = 16 * 1024;
     L.RP = (int)std::max<size_t>(1, std::min<size_t>(8, (target + L.S * RB - 1) / (L.S * RB)));
     L.R = L.S * L.RP;
-    L.stage_bytes = (uint32_t)(((size_t)L.R * RB + 32 + 127) / 128 * 128);
+    const size_t region = ((size_t)L.R * RB + 32 + 127) / 128 * 128;
+    L.stage_bytes = (uint32_t)(pair ? 2 * region : region);
     // one or two persistent CTAs per SM: ~96 KB of weights in flight per SM
     L.stages = (int)std::max<size_t>(2, std::min<size_t>(kMaxStages, (48 * 1024) / L.stage_bytes));
     const size_t kp = (size_t)L.nt * L.seg;
-    L.smem = 128 + (size_t)L.stages * L.stage_bytes + (((size_t)L.R * L.nt + 3) & ~(size_t)3) * 4 +
-             kp * 4;
+    const size_t red = (((size_t)(pair ? 2 : 1) * L.R * L.nt + 3) & ~(size_t)3);
+    const size_t tables = (size_t)L.nt * 4 + 3 + 16 + (size_t)L.nt * 6 * (L.seg / 8);  // words
+    L.smem = 128 + (size_t)L.stages * L.stage_bytes + (red + kp + tables) * 4;
     return L;
 }
 
@@ -654,12 +715,15 @@ int launch_i4_matvec_ex(const I4Job *jobs, int n_jobs, int in_dim, int group_siz
     P.x = o.x;
     P.am = o.argmax;
     P.status = o.status;
-    const Shape L = plan(in_dim, group_size);
+    const bool pair = o.pair_swiglu;
+    TQ_CHECK_ARG(!pair || (n_jobs == 2 && jobs[0].rows == jobs[1].rows && !o.argmax.token),
+                 "paired SwiGLU needs two jobs with equal rows");
+    const Shape L = plan(in_dim, group_size, pair);
     bool aligned = true;  // the TMA path needs 16-byte aligned matrix bases
     for (int j = 0; j < n_jobs; ++j) aligned = aligned && ((uintptr_t)jobs[j].w % 16u == 0);
     const bool fast = (group_size % 32 == 0) && L.seg != 0 && aligned;
     if (!fast) {
-        TQ_CHECK_ARG(o.x.mode == X_PLAIN && !o.argmax.token,
+        TQ_CHECK_ARG(o.x.mode == X_PLAIN && !o.argmax.token && !pair,
                      "fused prologue/epilogue needs group_size %% 32 == 0 and aligned weights");
     }
     const int R = fast ? L.R : 1;
@@ -668,9 +732,10 @@ int launch_i4_matvec_ex(const I4Job *jobs, int n_jobs, int in_dim, int group_siz
         TQ_CHECK_ARG(jobs[j].rows >= 0, "rows %d", jobs[j].rows);
         P.job[j] = jobs[j];
         P.pass_begin[j] = acc;
-        acc += (jobs[j].rows + R - 1) / R;
+        if (!pair || j == 0) acc += (jobs[j].rows + R - 1) / R;
     }
     P.pass_begin[n_jobs] = acc;
+    P.pair = pair ? 1 : 0;
     if (acc == 0) return TQB200_OK;
     if (fast) {
         P.nt = L.nt;

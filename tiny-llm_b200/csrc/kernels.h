@@ -41,13 +41,16 @@ struct ArgmaxOut {
     float *part_v = nullptr;        // [>= grid] per-CTA partials
     int *part_i = nullptr;
     unsigned int *ticket = nullptr; // zero-initialised; reset by the last CTA
-    int *token = nullptr;           // result
+    int *token = nullptr;           // result index (row + row_offset)
+    float *value = nullptr;         // optional: the maximum itself
+    int row_offset = 0;             // global index of row 0 (vocabulary shard)
 };
 
 struct I4LaunchOpts {
     XSource x;
     ArgmaxOut argmax;
     bool pdl = false;               // launch with programmatic stream serialisation
+    bool pair_swiglu = false;       // jobs (gate, up): y_gate = silu(gate x) * (up x)
     int *status = nullptr;          // device error word (bounded-wait timeouts)
 };
 
@@ -118,6 +121,13 @@ size_t attn_partial_floats(int n_heads, int head_dim, int nsplit);
 int launch_attention(const AttnArgs &a, cudaStream_t st);
 
 int launch_swiglu(float *g, const float *u, int n, cudaStream_t st);
+int launch_swiglu_out(const float *g, const float *u, float *out, int n, cudaStream_t st);
+// (value, index) of every rank's vocabulary shard -> the global first maximum
+struct ArgPair {
+    float v;
+    int i;
+};
+int launch_argmax_pairs(const ArgPair *pairs, int n, int *out, cudaStream_t st);
 int argmax_blocks(int n);
 int launch_argmax(const float *l, int n, float *pv, int *pi, unsigned int *ticket, int *out,
                   cudaStream_t st);

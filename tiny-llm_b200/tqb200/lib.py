@@ -61,6 +61,7 @@ PROTOTYPES = {
     "tqb200_argmax": ([_f, _i, C.POINTER(_i)], _i),
     "tqb200_topk_softmax": ([_f, _i, _i, _i32, _f], _i),
     "tqb200_engine_default_opts": ([_vp], None),
+    "tqb200_nccl_unique_id": ([_vp], _i),
     "tqb200_engine_create": ([C.POINTER(abi.ModelDesc), _vp, C.POINTER(_vp)], _i),
     "tqb200_engine_step": ([_vp, _i, C.POINTER(_i)], _i),
     "tqb200_engine_reset": ([_vp], _i),
@@ -273,14 +274,22 @@ def topk_softmax(logits, k: int):
 # ---------------------------------------------------------------- engine
 class EngineOpts(C.Structure):
     _fields_ = [("max_seq_len", C.c_int), ("kv_fp16", C.c_int), ("use_graph", C.c_int),
-                ("pdl", C.c_int), ("device", C.c_int), ("reserved", C.c_int * 11)]
+                ("pdl", C.c_int), ("device", C.c_int), ("tp_size", C.c_int), ("tp_rank", C.c_int),
+                ("nccl_id", C.c_ubyte * 128), ("reserved", C.c_int * 8)]
+
+
+def nccl_unique_id() -> bytes:
+    buf = (C.c_ubyte * 128)()
+    _check(load().tqb200_nccl_unique_id(buf))
+    return bytes(buf)
 
 
 class Engine:
     """GPU decode engine (the reference's GpuDecode* registry entry, kernels/dispatch.h:353-378)."""
 
     def __init__(self, model, max_seq_len: int = 512, kv_fp16: bool = False,
-                 use_graph: bool = True, pdl: bool = True, device: int = -1):
+                 use_graph: bool = True, pdl: bool = True, device: int = -1,
+                 tp_size: int = 1, tp_rank: int = 0, nccl_id: bytes = b""):
         L = load()
         self.model = model  # keeps the host weights alive through create()
         self.vocab = model.spec.vocab
@@ -288,6 +297,10 @@ class Engine:
         L.tqb200_engine_default_opts(C.byref(o))
         o.max_seq_len, o.kv_fp16 = max_seq_len, 1 if kv_fp16 else 0
         o.use_graph, o.pdl, o.device = 1 if use_graph else 0, 1 if pdl else 0, device
+        o.tp_size, o.tp_rank = tp_size, tp_rank
+        if tp_size > 1:
+            assert len(nccl_id) == 128, "tensor parallel needs the 128-byte NCCL id"
+            C.memmove(o.nccl_id, nccl_id, 128)
         h = C.c_void_p()
         _check(L.tqb200_engine_create(C.byref(model.desc), C.byref(o), C.byref(h)))
         self.h = h
