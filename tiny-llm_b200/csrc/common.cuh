@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <cstdio>
 
 #include "../../include/tqb200.h"
@@ -27,6 +28,15 @@ int set_error(int status, const char *fmt, ...);
     do {                                                                                   \
         if (!(cond)) return ::tqb200::set_error(TQB200_ERR_INVALID_ARG, __VA_ARGS__);      \
     } while (0)
+
+// True the first time it is called on the current device for this mask (kernel
+// attributes such as the dynamic shared-memory limit are per device).
+inline bool first_on_device(std::atomic<unsigned long long> &mask) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return true;
+    const unsigned long long bit = 1ull << (dev & 63);
+    return (mask.fetch_or(bit) & bit) == 0;
+}
 
 // ---------------------------------------------------------------- fp16
 // Exact binary16 -> binary32 (hardware cvt; identical values to the reference's

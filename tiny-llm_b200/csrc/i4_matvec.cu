@@ -22,10 +22,15 @@
 //    OR'ed into the mantissa of 2^23, activations pre-scaled by 16^-k) and one
 //    FADD; then one FFMA per weight, using
 //        sum_i (q_i - z) s x_i = s * (sum_i q_i x_i - z * sum_i x_i).
-//    (MATH_DP4A): activations split into three int8 digits per segment
-//    (x ~ d0*s0 + d1*s0/254 + d2*s0/254^2, error <= 6e-8 * max|x|), and the
-//    nibble dots run as exact integer dp4a (2 unpack ops + 6 dp4a per 8
-//    weights).
+//    (MATH_DP4A): activations split into three int8 digits with one scale
+//    for the whole vector (x ~ (d0 + d1/254 + d2/254^2) * max|x|/127, error
+//    <= 3.1e-8 * max|x|), built elementwise once per CTA, and the nibble dots
+//    run as exact integer dp4a (2 unpack ops + 6 dp4a per 8 weights).
+//  * The activation vector (and the RMSNorm weight or SwiGLU up vector) comes in
+//    by bulk copy; one pass computes the sum of squares and max |x|, a second
+//    applies the norm and builds the digit planes; a pass of rows then needs one
+//    barrier (partials double-buffered), and the bias / residual of its rows are
+//    fetched before its weights are waited on.
 //  * Optional fused prologues (RMSNorm of the source, SwiGLU of gate/up) and
 //    epilogues (bias, residual add, greedy argmax over the rows).
 //  * Every mbarrier wait is bounded; on timeout the kernel records an error
@@ -55,6 +60,7 @@ struct MvParams {
     int stages;
     uint32_t stage_bytes;
     int pair;  // jobs 0 and 1 (gate, up) share passes; y0 = silu(W0 x) * (W1 x)
+    int x_bulk;  // activation vectors 16-byte aligned with K % 4 == 0: one bulk copy each
     XSource x;
     ArgmaxOut am;
     int *status;
@@ -81,10 +87,6 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
     int d;
     asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
     return d;
-}
-
-__device__ __forceinline__ int round_half_away(float v) {
-    return (int)(v >= 0.0f ? v + 0.5f : v - 0.5f);
 }
 
 __device__ __forceinline__ void better(float &bv, int &bi, float v, int i) {
@@ -171,35 +173,166 @@ template <int SEG, int MATH>
 __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ MvParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int NW = SEG / 8;
+    const int t = threadIdx.x;
+    const int total = P.pass_begin[P.n_jobs];
+    const int nt = P.nt, S = P.S, K = P.K, G = P.G, np = 1 + P.pair;
+    const int KP = nt * SEG;  // every column a segment can own (>= K), a multiple of 32
+    // shared memory: barriers | weight stages | red x2 | x | norm weight or up | digit
+    // planes (word-major: word w of segment g at w*nt + g) | 8-column chunk sums
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *xbar = bars + kMaxStages;      // activation copy
+    uint64_t *wbar = bars + kMaxStages + 1;  // norm-weight copy
     uint8_t *stage_base = smem + 128;
     float *red = reinterpret_cast<float *>(stage_base + (size_t)P.stages * P.stage_bytes);
+    const size_t red_n = (size_t)np * P.R * nt;  // one buffer
+    float *xsm = red + ((2 * red_n + 3) & ~(size_t)3);
+    float *wsm = xsm + KP;
+    uint32_t *dig = reinterpret_cast<uint32_t *>(wsm + (((size_t)K + 3) & ~(size_t)3));
+    float *csum = reinterpret_cast<float *>(dig + (size_t)6 * NW * nt);
     __shared__ uint32_t s_head[2 * kMaxStages];
     __shared__ int s_err;
     __shared__ double s_rd[32];
+    __shared__ float s_am[32];
     __shared__ float s_bv[32];
     __shared__ int s_bi[32];
     __shared__ bool s_last;
+    const bool bulk_x = P.x_bulk != 0;
+    const bool norm = P.x.mode == X_RMSNORM, swiglu = P.x.mode == X_SWIGLU;
 
-    const int t = threadIdx.x;
-    const int total = P.pass_begin[P.n_jobs];
     if (t == 0) {
         for (int s = 0; s < P.stages; ++s) mbar_init(&bars[s], 1);
+        mbar_init(xbar, 1);
+        mbar_init(wbar, 1);
         fence_mbar_init();
         s_err = 0;
-    }
-    __syncthreads();
-    if (t == 0) {
         for (int s = 0; s < P.stages; ++s) {
             const int p = blockIdx.x + s * gridDim.x;
             if (p < total) issue_pass(P, p, s, bars, stage_base, s_head);
         }
+        if (bulk_x && norm) {  // constant weights: before the dependency wait
+            mbar_arrive_expect_tx(wbar, (uint32_t)K * 4u);
+            bulk_g2s(wsm, P.x.norm_w, (uint32_t)K * 4u, wbar);
+        }
     }
+    __syncthreads();  // barrier initialisation visible to every thread
     // weights are in flight; now wait for the producer of x and let our dependents start
     griddep_wait();
     griddep_launch();
+    if (t == 0 && bulk_x) {
+        const uint32_t xb = (uint32_t)K * 4u;
+        mbar_arrive_expect_tx(xbar, swiglu ? 2 * xb : xb);
+        bulk_g2s(xsm, P.x.src, xb, xbar);
+        if (swiglu) bulk_g2s(wsm, P.x.up, xb, xbar);
+    }
 
-    const int nt = P.nt, S = P.S, K = P.K, G = P.G;
+    // ---- activation: whole vector in shared memory, zero past K.  One thread waits on
+    // the copies; the others park at the barrier.  Unaligned sources: batched loads.
+    for (int i = K + t; i < KP; i += blockDim.x) xsm[i] = 0.0f;
+    if (bulk_x) {
+        if (t == 0) {
+            if (!mbar_wait(xbar, 0, kWaitCycles)) s_err = 1;
+            if (norm && !mbar_wait(wbar, 0, kWaitCycles)) s_err = 1;
+        }
+    } else {
+        for (int i0 = t; i0 < K; i0 += 4 * blockDim.x) {  // 4 loads in flight per thread
+            float v[4], u[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int i = i0 + k * blockDim.x;
+                v[k] = i < K ? P.x.src[i] : 0.0f;
+                u[k] = (i < K && swiglu) ? P.x.up[i] : (i < K && norm) ? P.x.norm_w[i] : 0.0f;
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int i = i0 + k * blockDim.x;
+                if (i < K) xsm[i] = v[k], wsm[i] = u[k];
+            }
+        }
+    }
+    __syncthreads();
+    // pass A: SwiGLU in place; sum of squares (RMSNorm, in double as rmsnorm_ref);
+    // max |value| for the digit scale (RMSNorm: max |x*w|, scaled below)
+    {
+        double ss = 0.0;
+        float am = 0.0f;
+        for (int i = t; i < K; i += blockDim.x) {
+            float v = xsm[i];
+            if (swiglu) {
+                v = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), wsm[i]);
+                xsm[i] = v;
+            }
+            if (norm) {
+                ss += (double)v * (double)v;
+                am = fmaxf(am, fabsf(v * wsm[i]));
+            } else {
+                am = fmaxf(am, fabsf(v));
+            }
+        }
+        if (norm) ss = warp_sum_d(ss);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+        if ((t & 31) == 0) {
+            s_rd[t >> 5] = ss;
+            s_am[t >> 5] = am;
+        }
+    }
+    __syncthreads();
+    float rms_scale = 1.0f, amax = 0.0f;
+    {
+        double tot = 0.0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+            tot += s_rd[w];
+            amax = fmaxf(amax, s_am[w]);
+        }
+        if (norm) {
+            const float mean_sq = (float)(tot / K);
+            rms_scale = 1.0f / sqrtf(__fadd_rn(mean_sq, P.x.eps));
+            amax = amax * rms_scale * 1.0000005f;  // bound on |(x*r)*w| after rounding
+        }
+    }
+    // pass B, 8 columns (one weight word) per item: RMSNorm applied, the chunk sum, and
+    // the dp4a digit planes of the vector with ONE scale for all of it:
+    //   x ~ (d0 + d1/254 + d2/254^2) * s0,  s0 = max|x| / 127  (error <= 3.1e-8 max|x|);
+    // word order per chunk (lo, hi) x (d0, d1, d2), lo = even columns, hi = odd ones,
+    // matching the nibble order of a weight word
+    const float dsc0 = amax > 0.0f ? amax / 127.0f : 1.0f;
+    const float dsc1 = dsc0 / 254.0f, dsc2 = dsc1 / 254.0f;
+    {
+        const float i0 = 1.0f / dsc0, i1 = 1.0f / dsc1, i2 = 1.0f / dsc2;
+        for (int c = t; c < KP / 8; c += blockDim.x) {
+            float4 a = *reinterpret_cast<const float4 *>(xsm + 8 * c);
+            float4 b = *reinterpret_cast<const float4 *>(xsm + 8 * c + 4);
+            float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+            if (norm) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    v[k] = 8 * c + k < K ? __fmul_rn(__fmul_rn(v[k], rms_scale), wsm[8 * c + k]) : 0.0f;
+                *reinterpret_cast<float4 *>(xsm + 8 * c) = make_float4(v[0], v[1], v[2], v[3]);
+                *reinterpret_cast<float4 *>(xsm + 8 * c + 4) = make_float4(v[4], v[5], v[6], v[7]);
+            }
+            csum[c] = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+            if constexpr (MATH == MATH_DP4A) {
+                uint32_t wd[6] = {0u, 0u, 0u, 0u, 0u, 0u};
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const int q0 = max(-127, min(127, __float2int_rn(v[k] * i0)));
+                    const float r1 = fmaf(-(float)q0, dsc0, v[k]);
+                    const int q1 = max(-127, min(127, __float2int_rn(r1 * i1)));
+                    const float r2 = fmaf(-(float)q1, dsc1, r1);
+                    const int q2 = max(-127, min(127, __float2int_rn(r2 * i2)));
+                    const int sh = 8 * (k >> 1);
+                    wd[(k & 1) + 0] |= ((uint32_t)q0 & 0xFFu) << sh;
+                    wd[(k & 1) + 2] |= ((uint32_t)q1 & 0xFFu) << sh;
+                    wd[(k & 1) + 4] |= ((uint32_t)q2 & 0xFFu) << sh;
+                }
+                const int sgi = c / NW, ci = c - sgi * NW;
+#pragma unroll
+                for (int k = 0; k < 6; ++k) dig[(size_t)(6 * ci + k) * nt + sgi] = wd[k];
+            }
+        }
+    }
+    __syncthreads();
+
     const int slot = t / nt;
     const int sg = t - slot * nt;
     const bool active = slot < S;
@@ -210,118 +343,24 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
     const int col0 = sg * SEG;
     const uint32_t hdr_off = (uint32_t)g * GB;
     const uint32_t seg_off = hdr_off + 4u + (uint32_t)(sg - g * spg) * (SEG / 2);
-
-    // ---- activation prologue: the whole vector into shared memory with coalesced
-    // loads (RMSNorm / SwiGLU applied there), then each thread takes its segment
-    // [nt * SEG] floats, zero past K
-    float *xsm = red + (((size_t)(1 + P.pair) * P.R * nt + 3) & ~(size_t)3);
-    {
-        const int KP = nt * SEG;  // every segment a thread can own (>= K)
-        double ss = 0.0;
-        for (int i = t; i < KP; i += blockDim.x) {
-            float v = 0.0f;
-            if (i < K) {
-                if (P.x.mode == X_SWIGLU) {
-                    const float gv = P.x.src[i];
-                    v = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), P.x.up[i]);
-                } else {
-                    v = P.x.src[i];
-                }
-            }
-            if (P.x.mode == X_RMSNORM) ss += (double)v * (double)v;
-            xsm[i] = v;
-        }
-        if (P.x.mode == X_RMSNORM) {
-            ss = warp_sum_d(ss);
-            if ((t & 31) == 0) s_rd[t >> 5] = ss;
-            __syncthreads();
-            if (t < 32) {
-                double v = t < (int)(blockDim.x >> 5) ? s_rd[t] : 0.0;
-                v = warp_sum_d(v);
-                if (t == 0) s_rd[0] = v;
-            }
-            __syncthreads();
-            const float mean_sq = (float)(s_rd[0] / K);
-            const float rms_scale = 1.0f / sqrtf(__fadd_rn(mean_sq, P.x.eps));
-            for (int i = t; i < K; i += blockDim.x)
-                xsm[i] = __fmul_rn(__fmul_rn(xsm[i], rms_scale), P.x.norm_w[i]);
-        }
-        __syncthreads();
-    }
-    // ---- per-segment tables, built once per CTA by all warps together (one warp per
-    // segment, SEG/32 elements per lane): the segment sum X and, for dp4a, the three
-    // int8 digit planes packed to match the nibble order of a 32-bit word
-    // (lo word = even columns, hi word = odd columns) plus the digit scales.
-    float *seg_x = xsm + (size_t)nt * SEG;                                  // [nt]
-    float *seg_sc = seg_x + nt;                                             // [nt][3]
-    uint32_t *seg_dig = reinterpret_cast<uint32_t *>(seg_sc + 3 * nt + 3);  // [nt][6*NW]
-    seg_dig = reinterpret_cast<uint32_t *>(((uintptr_t)seg_dig + 15) & ~(uintptr_t)15);
-    {
-        const int lane_ = t & 31, warp_ = t >> 5, nw_ = blockDim.x >> 5;
-        constexpr int EPL = SEG / 32;  // elements per lane
-        for (int sgi = warp_; sgi < nt; sgi += nw_) {
-            float v[EPL];
-            float sum = 0.0f, amax = 0.0f;
-#pragma unroll
-            for (int e = 0; e < EPL; ++e) {
-                v[e] = xsm[sgi * SEG + lane_ * EPL + e];
-                sum += v[e];
-                amax = fmaxf(amax, fabsf(v[e]));
-            }
-            sum = warp_sum(sum);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-            if constexpr (MATH == MATH_DP4A) {
-                const float s0 = amax > 0.0f ? amax / 127.0f : 1.0f;
-                const float s1 = s0 / 254.0f, s2 = s1 / 254.0f;
-                const float i0 = 1.0f / s0, i1 = 1.0f / s1, i2 = 1.0f / s2;
-                uint8_t *db = reinterpret_cast<uint8_t *>(seg_dig + (size_t)sgi * 6 * NW);
-#pragma unroll
-                for (int e = 0; e < EPL; ++e) {
-                    const int c = lane_ * EPL + e;               // column within the segment
-                    const int chunk = c >> 3, k = c & 7;
-                    const int word = 6 * chunk + (k & 1), byte = k >> 1;
-                    const int q0 = max(-127, min(127, round_half_away(v[e] * i0)));
-                    const float r1 = fmaf(-(float)q0, s0, v[e]);
-                    const int q1 = max(-127, min(127, round_half_away(r1 * i1)));
-                    const float r2 = fmaf(-(float)q1, s1, r1);
-                    const int q2 = max(-127, min(127, round_half_away(r2 * i2)));
-                    db[(word + 0) * 4 + byte] = (uint8_t)q0;
-                    db[(word + 2) * 4 + byte] = (uint8_t)q1;
-                    db[(word + 4) * 4 + byte] = (uint8_t)q2;
-                }
-                if (lane_ == 0) {
-                    seg_sc[3 * sgi + 0] = s0;
-                    seg_sc[3 * sgi + 1] = s1;
-                    seg_sc[3 * sgi + 2] = s2;
-                }
-            }
-            if (lane_ == 0) seg_x[sgi] = sum;
-        }
-        __syncthreads();
-    }
-    const float X = seg_x[sg];
+    float X = 0.0f;  // segment sum (zero-point term)
     float xs[MATH == MATH_F32 ? SEG : 1];
     uint32_t xd[MATH == MATH_DP4A ? 6 * NW : 1];
-    float dsc0 = 0.0f, dsc1 = 0.0f, dsc2 = 0.0f;
-    if constexpr (MATH == MATH_F32) {
+    if (active) {
 #pragma unroll
-        for (int i = 0; i < NW; ++i)
+        for (int ci = 0; ci < NW; ++ci) X += csum[sg * NW + ci];
+        if constexpr (MATH == MATH_F32) {
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const int pos = k < 5 ? k : k - 3;
-                xs[8 * i + k] = xsm[col0 + 8 * i + k] * __uint_as_float((uint32_t)(127 - 4 * pos) << 23);
-            }
-    } else {
-        const uint4 *src4 = reinterpret_cast<const uint4 *>(seg_dig + (size_t)sg * 6 * NW);
+            for (int i = 0; i < NW; ++i)
 #pragma unroll
-        for (int i = 0; i < 6 * NW / 4; ++i) {
-            const uint4 w4 = src4[i];
-            xd[4 * i + 0] = w4.x, xd[4 * i + 1] = w4.y, xd[4 * i + 2] = w4.z, xd[4 * i + 3] = w4.w;
+                for (int k = 0; k < 8; ++k) {
+                    const int pos = k < 5 ? k : k - 3;
+                    xs[8 * i + k] = xsm[col0 + 8 * i + k] * __uint_as_float((uint32_t)(127 - 4 * pos) << 23);
+                }
+        } else {
+#pragma unroll
+            for (int w = 0; w < 6 * NW; ++w) xd[w] = dig[(size_t)w * nt + sg];
         }
-        dsc0 = seg_sc[3 * sg + 0];
-        dsc1 = seg_sc[3 * sg + 1];
-        dsc2 = seg_sc[3 * sg + 2];
     }
 
     const int lane = t & 31, warp = t >> 5, nwarps = blockDim.x >> 5;
@@ -337,12 +376,24 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
         while (j + 1 < P.n_jobs && p >= P.pass_begin[j + 1]) ++j;
         const I4Job &job = P.job[j];
         const int row0 = (p - P.pass_begin[j]) * P.R;
+        float *rb = red + (size_t)(i_pass & 1) * red_n;  // double-buffered partials
+        // bias / residual of this pass fetched before the weight wait: lane k of warp w
+        // holds row w + k*nwarps, the row that warp reduces in its k-th epilogue turn
+        float pre_b = 0.0f, pre_r = 0.0f;
+        if (!P.pair) {
+            const int rl = warp + lane * nwarps, row = row0 + rl;
+            if (rl < P.R && row < job.rows) {
+                if (job.bias) pre_b = job.bias[row];
+                if (job.resid) pre_r = job.resid[row];
+            }
+        }
         if (!mbar_wait(&bars[s], parity, kWaitCycles)) s_err = 1;
         const size_t half_bytes = P.stage_bytes / 2;
         if (active) {
-            for (int r = 0; r < P.RP * (1 + P.pair); ++r) {
+            for (int r = 0; r < P.RP * np; ++r) {
                 const int jb = r >= P.RP;  // paired mode: second half = job 1
                 const int rl = slot + (r - jb * P.RP) * S;
+                if (rl >= P.R) continue;
                 const uint8_t *sb = stage_base + (size_t)s * P.stage_bytes +
                                     (jb ? half_bytes + s_head[kMaxStages + s] : s_head[s]);
                 float part = 0.0f;
@@ -373,23 +424,33 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
                         part = sc * fmaf(-zr, X, dot);
                     }
                 }
-                red[(jb * P.R + rl) * nt + sg] = part;
+                rb[(jb * P.R + rl) * nt + sg] = part;
             }
         }
-        __syncthreads();
+        __syncthreads();  // stage s consumed, partials of this pass complete
         if (s_err) break;
-        for (int rl = warp; rl < P.R; rl += nwarps) {
+        if (t == 0) {  // refill stage s while the rows of this pass are reduced
+            const int pn = blockIdx.x + (i_pass + P.stages) * gridDim.x;
+            if (pn < total) issue_pass(P, pn, s, bars, stage_base, s_head);
+        }
+        for (int rl = warp, turn = 0; rl < P.R; rl += nwarps, ++turn) {
             const int row = row0 + rl;
             if (row >= job.rows) continue;
+            float b_ = __shfl_sync(0xffffffffu, pre_b, turn & 31);
+            float r_ = __shfl_sync(0xffffffffu, pre_r, turn & 31);
+            if (turn >= 32 && !P.pair) {  // more turns than lanes: plain loads
+                b_ = job.bias ? job.bias[row] : 0.0f;
+                r_ = job.resid ? job.resid[row] : 0.0f;
+            }
             // segment partials summed in double, rounded once (the reference's row dot
             // is a double sum rounded to float)
             double vd = 0.0;
-            for (int i = lane; i < nt; i += 32) vd += (double)red[rl * nt + i];
+            for (int i = lane; i < nt; i += 32) vd += (double)rb[rl * nt + i];
             float v = (float)warp_sum_d(vd);
             float u = 0.0f;
             if (P.pair) {
                 double ud = 0.0;
-                for (int i = lane; i < nt; i += 32) ud += (double)red[(P.R + rl) * nt + i];
+                for (int i = lane; i < nt; i += 32) ud += (double)rb[(P.R + rl) * nt + i];
                 u = (float)warp_sum_d(ud);
             }
             if (lane == 0) {
@@ -397,17 +458,12 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
                     // swiglu_ref (kernels/silu/swiglu_ref.cpp:41-52) on (gate, up)
                     v = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), u);
                 } else {
-                    if (job.bias) v += job.bias[row];
-                    if (job.resid) v = job.resid[row] + v;
+                    if (job.bias) v += b_;
+                    if (job.resid) v = r_ + v;
                 }
                 job.y[row] = v;
                 if (P.am.token && j == 0) better(bv, bi, v, row + P.am.row_offset);
             }
-        }
-        __syncthreads();
-        if (t == 0) {
-            const int pn = blockIdx.x + (i_pass + P.stages) * gridDim.x;
-            if (pn < total) issue_pass(P, pn, s, bars, stage_base, s_head);
         }
     }
     if (s_err) {
@@ -417,6 +473,10 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
                 const int ii = i_pass + k;
                 if (blockIdx.x + ii * gridDim.x >= total) break;
                 mbar_wait(&bars[ii % P.stages], (uint32_t)(ii / P.stages) & 1u, kWaitCycles);
+            }
+            if (bulk_x) {
+                mbar_wait(xbar, 0, kWaitCycles);
+                if (norm) mbar_wait(wbar, 0, kWaitCycles);
             }
             if (P.status) atomicExch(P.status, kDevTimeoutTma);
         }
@@ -623,7 +683,13 @@ struct Shape {
     size_t smem = 0;
 };
 
-Shape plan(int K, int G, bool pair) {
+// Launch shape.  One CTA per SM (block up to 512 threads: S row slots of nt segment
+// threads); a pass is R consecutive rows, one bulk copy (two in paired mode).  When a
+// CTA's share of the rows fits in <= 64 KB it is a single pass (R = rows / SMs, so the
+// passes spread evenly); otherwise passes of <= 32 KB stream through a ring of up to
+// 96 KB.  Shared memory stays near 110 KB or below for most shapes, so the next
+// kernel's CTA can become resident (and start its weight copies) before this one ends.
+Shape plan(int K, int G, bool pair, int rows_total) {
     Shape L;
     L.seg = (G % 64 == 0) ? 64 : 32;
     const int ng = (K + G - 1) / G;
@@ -633,19 +699,30 @@ Shape plan(int K, int G, bool pair) {
         return L;
     }
     const size_t RB = (size_t)ng * (4 + G / 2);
-    L.S = std::max(1, 256 / L.nt);
+    const int np = pair ? 2 : 1;
+    L.S = std::max(1, 512 / L.nt);
     L.block = ((L.nt * L.S + 31) / 32) * 32;
-    const size_t target = 16 * 1024;
-    L.RP = (int)std::max<size_t>(1, std::min<size_t>(8, (target + L.S * RB - 1) / (L.S * RB)));
-    L.R = L.S * L.RP;
+    const int per_cta = std::max(1, (rows_total + num_sms() - 1) / num_sms());
+    if ((size_t)per_cta * RB * np <= 64 * 1024) {
+        L.R = per_cta;
+    } else {
+        L.R = (int)std::max<size_t>(1, (32 * 1024) / (RB * np));
+    }
+    L.RP = (L.R + L.S - 1) / L.S;
     const size_t region = ((size_t)L.R * RB + 32 + 127) / 128 * 128;
-    L.stage_bytes = (uint32_t)(pair ? 2 * region : region);
-    // one or two persistent CTAs per SM: ~96 KB of weights in flight per SM
-    L.stages = (int)std::max<size_t>(2, std::min<size_t>(kMaxStages, (48 * 1024) / L.stage_bytes));
+    L.stage_bytes = (uint32_t)(np * region);
+    L.stages = (int)std::max<size_t>(2, std::min<size_t>(kMaxStages, (96 * 1024) / L.stage_bytes));
     const size_t kp = (size_t)L.nt * L.seg;
-    const size_t red = (((size_t)(pair ? 2 : 1) * L.R * L.nt + 3) & ~(size_t)3);
-    const size_t tables = (size_t)L.nt * 4 + 3 + 16 + (size_t)L.nt * 6 * (L.seg / 8);  // words
-    L.smem = 128 + (size_t)L.stages * L.stage_bytes + (red + kp + tables) * 4;
+    const size_t red = ((2 * (size_t)np * L.R * L.nt + 3) & ~(size_t)3);
+    const size_t wsm = ((size_t)K + 3) & ~(size_t)3;
+    const size_t dig = (size_t)L.nt * 6 * (L.seg / 8);
+    const size_t floats = red + kp + wsm + dig + kp / 8;
+    for (;;) {
+        L.smem = 128 + (size_t)L.stages * L.stage_bytes + floats * 4;
+        if (L.smem <= 220 * 1024 || L.stages <= 2) break;
+        --L.stages;
+    }
+    if (L.smem > 220 * 1024) L.seg = 0;  // no TMA shape: the generic kernel
     return L;
 }
 
@@ -663,13 +740,11 @@ int grid_for(Kern k, int block, size_t smem, int work) {
 template <int SEG, int MATH>
 int launch_tma(const MvParams &P, const Shape &L, int passes, bool pdl, cudaStream_t st) {
     auto k = i4_mv_tma_kernel<SEG, MATH>;
-    static bool attr_set = false;
-    if (!attr_set) {
-        TQ_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        attr_set = true;
-    }
-    // persistent: at most two CTAs per SM, so the x prologue is paid once per CTA
-    const int grid = std::min(grid_for(k, L.block, L.smem, passes), 2 * num_sms());
+    static std::atomic<unsigned long long> attr_set{0};
+    if (first_on_device(attr_set))
+        TQ_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
+    // persistent: at most one CTA per SM, so the x prologue is paid once per SM
+    const int grid = std::min(grid_for(k, L.block, L.smem, passes), num_sms());
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(L.block);
@@ -718,7 +793,10 @@ int launch_i4_matvec_ex(const I4Job *jobs, int n_jobs, int in_dim, int group_siz
     const bool pair = o.pair_swiglu;
     TQ_CHECK_ARG(!pair || (n_jobs == 2 && jobs[0].rows == jobs[1].rows && !o.argmax.token),
                  "paired SwiGLU needs two jobs with equal rows");
-    const Shape L = plan(in_dim, group_size, pair);
+    int rows_total = 0;
+    for (int j = 0; j < n_jobs; ++j)
+        if (!pair || j == 0) rows_total += std::max(0, jobs[j].rows);
+    const Shape L = plan(in_dim, group_size, pair, rows_total);
     bool aligned = true;  // the TMA path needs 16-byte aligned matrix bases
     for (int j = 0; j < n_jobs; ++j) aligned = aligned && ((uintptr_t)jobs[j].w % 16u == 0);
     const bool fast = (group_size % 32 == 0) && L.seg != 0 && aligned;
@@ -736,6 +814,9 @@ int launch_i4_matvec_ex(const I4Job *jobs, int n_jobs, int in_dim, int group_siz
     }
     P.pass_begin[n_jobs] = acc;
     P.pair = pair ? 1 : 0;
+    auto a16 = [](const void *p) { return ((uintptr_t)p & 15u) == 0; };
+    P.x_bulk = (in_dim % 4 == 0) && a16(o.x.src) && (o.x.mode != X_RMSNORM || a16(o.x.norm_w)) &&
+               (o.x.mode != X_SWIGLU || a16(o.x.up));
     if (acc == 0) return TQB200_OK;
     if (fast) {
         P.nt = L.nt;
