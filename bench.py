@@ -356,7 +356,10 @@ def bench_decode(args, rank, pg, pk, pk_kind):
     mv_bytes = sum(mvb.values())
     achieved = mv_bytes / (mv_ms * 1e-3) / 1e9
     total_bytes = step_bytes(spec, ctx, 2)
-    launches = 2 + 6 * spec.n_layers + 1  # + the device-side token feed
+    # embed, per layer qkv / attention (QK-norm, RoPE and KV append fused) / o_proj /
+    # gate_up / down, lm_head (+argmax), the device-side token feed, and with tensor
+    # parallelism the cross-rank argmax (NCCL's all-gather kernels are not counted)
+    launches = 2 + 5 * spec.n_layers + 1 + (1 if world > 1 else 0)
     out = {
         "metric": "decode ms/token, batch 1 (BASELINE config 4: Qwen3-4B-shaped i4 g64, fp16 KV, ctx 4096)",
         "value": round(ms_step, 4), "unit": "ms/token", "n_gpus": world, "steps": K, "warmup": W,

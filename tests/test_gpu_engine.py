@@ -80,11 +80,22 @@ def test_config2_qwen25_05b_64_steps(tq, oracle):
     assert worst < TOL
 
 
-def test_config4_qwen3_4b_fp16_kv(tq, oracle):
-    """BASELINE config 4 shape (36 layers, hidden 2560, 32/8 heads, fp16 KV), short run."""
+# fp16 KV at 36 layers: every K/V element is rounded to half precision, whose step
+# is 2^-11 of the value.  A last-bit float difference upstream (the engine sums a
+# matvec row in a different order than the oracle) can flip that rounding, a
+# relative change of up to ~4.9e-4 in one cached element; over 36 layers this lifts
+# the logits' max relative error to 1.5e-4 .. 2e-4 (it grows with depth, and is the
+# same with the engine's fp32-math matvec).  The fp16 case therefore keeps exact
+# greedy tokens and a 5e-4 bound; the fp32-KV case keeps 1e-4.
+TOL_F16KV_DEEP = 5e-4
+
+
+@pytest.mark.parametrize("kv16,tol", [(False, TOL), (True, TOL_F16KV_DEEP)], ids=["f32kv", "f16kv"])
+def test_config4_qwen3_4b(tq, oracle, kv16, tol):
+    """BASELINE config 4 shape (36 layers, hidden 2560, 32/8 heads), short run."""
     spec = replace(QWEN3_4B, weights="codes")
     sm = SynthModel(spec, seed=0)
     prompt = list(np.random.default_rng(1).integers(0, spec.vocab, 4))
-    toks, otoks, worst = _decode_compare(tq, oracle, sm, prompt, 4, 4096, True)
+    toks, otoks, worst = _decode_compare(tq, oracle, sm, prompt, 4, 4096, kv16)
     assert toks == otoks
-    assert worst < TOL
+    assert worst < tol, worst

@@ -1,0 +1,555 @@
+// attention_tma.cu — split-K GQA decode attention with the KV chunk staged in
+// shared memory by TMA bulk copies and the splits merged through distributed
+// shared memory, sm_100a.
+//
+// Semantics: attention_decode_ref (kernels/attention/attention_decode_ref.cpp:53-143),
+// fp16 KV as in the reference's KVCache (runtime/kv_cache.cpp:120-135).  In the
+// engine ("fused") mode the kernel also performs the step's QK-norm, RoPE and KV
+// append (runtime/qwen_forward_token.cpp:423-446), which removes one launch per
+// layer and lets every cached row be fetched before the previous kernel finishes.
+//
+// Grid (n_kv_heads, ns) in clusters of (1, ns): the ns CTAs of a KV head form one
+// thread-block cluster.  CTA rank s owns positions [s*chunk, s*chunk+n) of its KV
+// head for the G query heads that share it.  Thread 0 streams the chunk's K rows
+// and then its V rows through a ring of shared-memory tiles (one cp.async.bulk per
+// tile, completion on an mbarrier).  Scores: a warp per cached row, lanes over head
+// dimensions, the G dot products reduced across the warp with a reduce-scatter
+// (log2 G exchanges halve the values each lane holds).  Exact max/sum softmax over
+// the chunk, P.V with threads over (dimension quad, row subset).  Each CTA leaves
+// its (m, l, o) in its own shared memory; after a cluster barrier every CTA merges
+// a slice of the output by reading the other ranks' partials over DSMEM (weights
+// exp(m_s - M) per split and head), and a second cluster barrier keeps the
+// partials alive until every rank has read them.  No global scratch, no atomics.
+//
+// Ordering (programmatic dependent launch): rows [0, seq-1) of the cache were
+// written by earlier steps and *pos at the start of this step, both complete once
+// the kernel runs (the kernel before it waited on its own predecessor before
+// releasing this one), so in fused mode their copies, and those of the constant
+// vectors (RoPE row, QK-norm weights), are issued before griddepcontrol.wait; the
+// step's q/k/v come from the immediately preceding kernel and are copied after it.
+// In plain mode the whole chunk may come from the previous kernel, so every copy is
+// issued after the wait.
+#include <float.h>
+
+#include <algorithm>
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace tqb200 {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kStages = 8;         // max tiles in flight (all of a 4096-context chunk)
+constexpr int kTileBytes = 16384;  // target bytes per staged tile
+constexpr int kMaxSplit = 16;      // cluster size (non-portable above 8)
+
+struct TmaAttnParams {
+    const float *q;                 // [H*HD] (raw projection in fused mode)
+    uint8_t *kc, *vc;               // caches [KVH][max_seq][HD] (KV elements)
+    const float *k_new, *v_new;     // fused: this step's k, v [KVH*HD]; null = plain
+    const float *q_norm, *k_norm;   // fused, optional [HD]
+    float eps;
+    const float *cos_tab, *sin_tab; // fused: [max_seq][HD/2]
+    const int *pos;                 // seq = *pos + 1 (null -> seq_len)
+    int seq_len, max_seq, chunk_max;
+    float scale;
+    int tile_rows, stages, stage_region;  // rows per tile; tiles in the ring; ring bytes
+    int bulk_in;                    // q/k/v and constant vectors 16-byte aligned: bulk copies
+    float *out;
+    int *status;
+};
+
+template <typename KV>
+__device__ __forceinline__ KV to_kv(float v) {
+    if constexpr (sizeof(KV) == 2) return f2h_ref(v);
+    else return v;
+}
+
+// D consecutive KV elements from shared memory as floats (D = 1, 2, 4)
+template <int D>
+__device__ __forceinline__ void lds_kv(const float *p, float o[D]) {
+    if constexpr (D == 4) {
+        const float4 v = *reinterpret_cast<const float4 *>(p);
+        o[0] = v.x, o[1] = v.y, o[2] = v.z, o[3] = v.w;
+    } else if constexpr (D == 2) {
+        const float2 v = *reinterpret_cast<const float2 *>(p);
+        o[0] = v.x, o[1] = v.y;
+    } else {
+        o[0] = *p;
+    }
+}
+template <int D>
+__device__ __forceinline__ void lds_kv(const uint16_t *p, float o[D]) {
+    if constexpr (D == 4) {
+        const uint2 v = *reinterpret_cast<const uint2 *>(p);
+        o[0] = h2f((uint16_t)(v.x & 0xFFFFu)), o[1] = h2f((uint16_t)(v.x >> 16));
+        o[2] = h2f((uint16_t)(v.y & 0xFFFFu)), o[3] = h2f((uint16_t)(v.y >> 16));
+    } else if constexpr (D == 2) {
+        const uint32_t v = *reinterpret_cast<const uint32_t *>(p);
+        o[0] = h2f((uint16_t)(v & 0xFFFFu)), o[1] = h2f((uint16_t)(v >> 16));
+    } else {
+        o[0] = h2f(*p);
+    }
+}
+
+// Reduce-scatter of N per-lane values over the warp: after it, v[0] of lane l is
+// the warp-wide sum of value (l >> (5 - log2 N)); N is a power of two <= 32.
+template <int N, int OFF>
+__device__ __forceinline__ void warp_reduce_scatter(float *v, int lane) {
+    if constexpr (N > 1) {
+        const bool up = (lane & OFF) != 0;
+#pragma unroll
+        for (int i = 0; i < N / 2; ++i) {
+            const float send = up ? v[i] : v[i + N / 2];
+            const float keep = up ? v[i + N / 2] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, OFF);
+        }
+        warp_reduce_scatter<N / 2, OFF / 2>(v, lane);
+    } else {
+#pragma unroll
+        for (int o = OFF; o > 0; o >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+    }
+}
+
+template <int G> struct Pow2 { static constexpr int v = G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8; };
+template <int N> struct Log2 { static constexpr int v = N <= 1 ? 0 : N <= 2 ? 1 : N <= 4 ? 2 : 3; };
+
+// Scores of one cached row (warp-cooperative): sc[row*G + g] = scale * q_g . k
+template <typename KV, int HD, int G>
+__device__ __forceinline__ void score_row(const KV *kr, const float (&qr)[G][HD / 32], int lane,
+                                          float scale, float *sc_row) {
+    constexpr int D = HD / 32;
+    constexpr int GP = Pow2<G>::v;
+    float k[D];
+    lds_kv<D>(kr + lane * D, k);
+    float acc[GP];
+#pragma unroll
+    for (int g = 0; g < GP; ++g) {
+        acc[g] = 0.0f;
+        if (g < G) {
+#pragma unroll
+            for (int d = 0; d < D; ++d) acc[g] = fmaf(qr[g][d], k[d], acc[g]);
+        }
+    }
+    warp_reduce_scatter<GP, 16>(acc, lane);
+    constexpr int SH = 5 - Log2<GP>::v;
+    const int g = lane >> SH;
+    if ((lane & ((1 << SH) - 1)) == 0 && g < G) sc_row[g] = acc[0] * scale;
+}
+
+// Warp-level QK-norm (optional) + rotate-half RoPE of one head vector, in place in
+// shared memory; the same float operations as the per-head engine kernel.
+template <int HD>
+__device__ __forceinline__ void norm_rope_warp(float *x, const float *nw, float eps,
+                                               const float *cs, const float *sn, int lane) {
+    if (nw) {
+        double ss = 0.0;
+        for (int i = lane; i < HD; i += 32) ss += (double)x[i] * (double)x[i];
+        ss = warp_sum_d(ss);
+        const float mean_sq = (float)(ss / HD);
+        const float rs = 1.0f / sqrtf(__fadd_rn(mean_sq, eps));
+        for (int i = lane; i < HD; i += 32) x[i] = __fmul_rn(__fmul_rn(x[i], rs), nw[i]);
+        __syncwarp();
+    }
+    constexpr int half = HD / 2;
+    constexpr int E = (half + 31) / 32;
+    float r0[E], r1[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const int i = lane + 32 * e;
+        if (i < half) {
+            const float x0 = x[i], x1 = x[i + half], c = cs[i], s = sn[i];
+            r0[e] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+            r1[e] = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s));
+        }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const int i = lane + 32 * e;
+        if (i < half) {
+            x[i] = r0[e];
+            x[i + half] = r1[e];
+        }
+    }
+    __syncwarp();
+}
+
+template <typename KV, int HD, int G>
+__global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constant__ TmaAttnParams P) {
+    namespace cg = cooperative_groups;
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int RB = HD * (int)sizeof(KV);  // bytes per cached row
+    constexpr int D = HD / 32;                // dimensions per lane in the score phase
+    constexpr int DG = HD / 4;                // dimension quads in the P.V phase
+    constexpr int TS = kThreads / DG;         // row subsets in the P.V phase
+    constexpr int half = HD / 2;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem);  // [stages] tiles
+    uint64_t *bar_c = bars + kStages;                      // constant vectors
+    uint64_t *bar_q = bars + kStages + 1;                  // q (+ new k, v)
+    uint8_t *ring = smem + 128;
+    KV *lastk = reinterpret_cast<KV *>(ring + P.stage_region);  // [HD] new row (fused)
+    KV *lastv = lastk + HD;
+    float *krow = reinterpret_cast<float *>(
+        ((uintptr_t)(lastv + HD) + 15) & ~(uintptr_t)15);       // [HD] new k (fp32)
+    float *vrow = krow + HD;                                    // [HD] new v (fp32)
+    float *qs = vrow + HD;                                      // [G][HD]
+    float *cs = qs + G * HD;                                    // [HD/2] RoPE row
+    float *sn = cs + half;                                      // [HD/2]
+    float *qn = sn + half;                                      // [HD] QK-norm weights
+    float *kn = qn + HD;                                        // [HD]
+    float *sc = kn + HD;                                        // [chunk_max][G]
+    // after the last tile the ring holds the P.V reduction and this CTA's partial
+    float *red = reinterpret_cast<float *>(ring);               // [TS][G][HD]
+    float *po = red + TS * G * HD;                              // [G][HD] partial o
+    float *pm = po + G * HD;                                    // [G] partial m
+    float *pl = pm + G;                                         // [G] partial l
+    float *wgt = pl + G;                                        // [ns][G] merge weights
+    __shared__ float s_m[G], s_l[G];
+    __shared__ int s_err;
+
+    cg::cluster_group cluster = cg::this_cluster();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int kh = blockIdx.x;
+    const int ns = (int)cluster.num_blocks(), split = (int)cluster.block_rank();
+    const bool fused = P.k_new != nullptr;
+    const int seq = P.pos ? (*P.pos + 1) : P.seq_len;
+    if (seq < 1 || seq > P.max_seq) {  // uniform over the grid: no CTA reaches a cluster barrier
+        if (tid == 0 && kh == 0 && split == 0 && P.status) atomicExch(P.status, kDevBadPosition);
+        return;
+    }
+    const int chunk = (seq + ns - 1) / ns;
+    const int t0 = split * chunk;
+    const int n = max(0, min(seq, t0 + chunk) - t0);
+    const bool owner = fused && seq - 1 >= t0 && seq - 1 < t0 + n;  // holds the new row
+    const int n_copy = owner ? n - 1 : n;
+    const int T = P.tile_rows, NST = P.stages;
+    const int nk = (n_copy + T - 1) / T;
+    const int total = 2 * nk;  // K tiles, then V tiles
+    const size_t row0 = (size_t)kh * P.max_seq + t0;
+    const bool has_norm = P.q_norm != nullptr;
+    auto issue = [&](int i) {
+        const int j = i < nk ? i : i - nk;
+        const int r0 = j * T, rows = min(T, n_copy - r0);
+        const uint8_t *src = (i < nk ? P.kc : P.vc) + (row0 + r0) * RB;
+        uint64_t *bar = &bars[i % NST];
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(bar, (uint32_t)(rows * RB));
+        bulk_g2s(ring + (size_t)(i % NST) * T * RB, src, (uint32_t)(rows * RB), bar);
+    };
+    if (tid == 0) {
+        for (int s = 0; s < kStages + 2; ++s) mbar_init(&bars[s], 1);
+        fence_mbar_init();
+        s_err = 0;
+        if (fused) {
+            for (int i = 0; i < min(total, NST); ++i) issue(i);
+            if (P.bulk_in) {
+                const uint32_t hb = (uint32_t)half * 4u;
+                mbar_arrive_expect_tx(bar_c, 2 * hb + (has_norm ? 2u * HD * 4u : 0u));
+                bulk_g2s(cs, P.cos_tab + (size_t)(seq - 1) * half, hb, bar_c);
+                bulk_g2s(sn, P.sin_tab + (size_t)(seq - 1) * half, hb, bar_c);
+                if (has_norm) {
+                    bulk_g2s(qn, P.q_norm, HD * 4u, bar_c);
+                    bulk_g2s(kn, P.k_norm, HD * 4u, bar_c);
+                }
+            }
+        }
+    }
+    griddep_wait();
+    griddep_launch();
+    if (tid == 0) {
+        if (!fused)
+            for (int i = 0; i < min(total, NST); ++i) issue(i);
+        if (P.bulk_in) {
+            const uint32_t qb = (uint32_t)G * HD * 4u;
+            mbar_arrive_expect_tx(bar_q, qb + (owner ? 2u * HD * 4u : 0u));
+            bulk_g2s(qs, P.q + (size_t)kh * G * HD, qb, bar_q);
+            if (owner) {
+                bulk_g2s(krow, P.k_new + (size_t)kh * HD, HD * 4u, bar_q);
+                bulk_g2s(vrow, P.v_new + (size_t)kh * HD, HD * 4u, bar_q);
+            }
+        }
+    }
+    if (P.bulk_in) {
+        if (tid == 0) {
+            if (fused && !mbar_wait(bar_c, 0, kWaitCycles)) s_err = 1;
+            if (!mbar_wait(bar_q, 0, kWaitCycles)) s_err = 1;
+        }
+    } else {  // unaligned inputs: the same staging with plain loads
+        for (int i = tid; i < G * HD; i += kThreads) qs[i] = P.q[(size_t)kh * G * HD + i];
+        if (fused) {
+            for (int i = tid; i < half; i += kThreads) {
+                cs[i] = P.cos_tab[(size_t)(seq - 1) * half + i];
+                sn[i] = P.sin_tab[(size_t)(seq - 1) * half + i];
+            }
+            for (int i = tid; i < HD; i += kThreads) {
+                if (has_norm) qn[i] = P.q_norm[i], kn[i] = P.k_norm[i];
+                if (owner) krow[i] = P.k_new[(size_t)kh * HD + i], vrow[i] = P.v_new[(size_t)kh * HD + i];
+            }
+        }
+    }
+    __syncthreads();
+
+    // ---- fused mode: QK-norm + RoPE of the G query heads and, for the owner, of the
+    // new k row; the new k/v rounded to the cache type, kept in shared memory for this
+    // step and appended to the cache for the next ones
+    if (fused && !s_err) {
+        const int jobs = G + (owner ? 2 : 0);
+        for (int h = warp; h < jobs; h += kWarps) {
+            if (h < G) {
+                norm_rope_warp<HD>(qs + h * HD, has_norm ? qn : nullptr, P.eps, cs, sn, lane);
+            } else if (h == G) {
+                norm_rope_warp<HD>(krow, has_norm ? kn : nullptr, P.eps, cs, sn, lane);
+                KV *dst = reinterpret_cast<KV *>(P.kc) + ((size_t)kh * P.max_seq + seq - 1) * HD;
+                for (int i = lane; i < HD; i += 32) {
+                    const KV v = to_kv<KV>(krow[i]);
+                    lastk[i] = v;
+                    dst[i] = v;
+                }
+            } else {
+                KV *dst = reinterpret_cast<KV *>(P.vc) + ((size_t)kh * P.max_seq + seq - 1) * HD;
+                for (int i = lane; i < HD; i += 32) {
+                    const KV v = to_kv<KV>(vrow[i]);
+                    lastv[i] = v;
+                    dst[i] = v;
+                }
+            }
+        }
+        __syncthreads();
+    }
+    float qr[G][D];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int d = 0; d < D; ++d) qr[g][d] = qs[g * HD + lane * D + d];
+    if (owner && warp == 0 && !s_err)
+        score_row<KV, HD, G>(lastk, qr, lane, P.scale, sc + (size_t)(n - 1) * G);
+
+    // ---- K tiles -> scores
+    int it = 0;
+    for (; !s_err && it < nk; ++it) {
+        if (tid == 0 && !mbar_wait(&bars[it % NST], (uint32_t)(it / NST) & 1u, kWaitCycles))
+            s_err = 1;
+        __syncthreads();
+        if (s_err) break;
+        const KV *tile = reinterpret_cast<const KV *>(ring + (size_t)(it % NST) * T * RB);
+        const int r0 = it * T, rows = min(T, n_copy - r0);
+        for (int r = warp; r < rows; r += kWarps)
+            score_row<KV, HD, G>(tile + (size_t)r * HD, qr, lane, P.scale, sc + (size_t)(r0 + r) * G);
+        __syncthreads();
+        if (tid == 0 && it + NST < total) issue(it + NST);
+    }
+    __syncthreads();  // the new row's score (warp 0) when there was no K tile
+    // ---- softmax statistics per head (warp g); p overwrites the scores
+    if (!s_err && warp < G) {
+        float m = -INFINITY;
+        for (int tt = lane; tt < n; tt += 32) m = fmaxf(m, sc[tt * G + warp]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float l = 0.0f;
+        for (int tt = lane; tt < n; tt += 32) {
+            const float p = expf(sc[tt * G + warp] - m);
+            sc[tt * G + warp] = p;
+            l += p;
+        }
+        l = warp_sum(l);
+        if (lane == 0) {
+            s_m[warp] = m;
+            s_l[warp] = l;
+        }
+    }
+    __syncthreads();
+    // ---- V tiles -> P.V
+    const int dg = tid % DG, ts = tid / DG;
+    float acc[G][4];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[g][j] = 0.0f;
+    for (; !s_err && it < total; ++it) {
+        if (tid == 0 && !mbar_wait(&bars[it % NST], (uint32_t)(it / NST) & 1u, kWaitCycles))
+            s_err = 1;
+        __syncthreads();
+        if (s_err) break;
+        const KV *tile = reinterpret_cast<const KV *>(ring + (size_t)(it % NST) * T * RB);
+        const int r0 = (it - nk) * T, rows = min(T, n_copy - r0);
+        for (int r = ts; r < rows; r += TS) {
+            float vv[4];
+            lds_kv<4>(tile + (size_t)r * HD + dg * 4, vv);
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const float p = sc[(r0 + r) * G + g];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[g][j] = fmaf(p, vv[j], acc[g][j]);
+            }
+        }
+        __syncthreads();
+        if (tid == 0 && it + NST < total) issue(it + NST);
+    }
+    const bool err = s_err != 0;
+    if (err) {
+        // drain the copies still in flight and report; this CTA's partial is an empty
+        // split's (the merge gives it weight 0), so the cluster stays in step
+        if (tid == 0) {
+            for (int i = it; i < min(total, it + NST); ++i)
+                mbar_wait(&bars[i % NST], (uint32_t)(i / NST) & 1u, kWaitCycles);
+            if (P.bulk_in) {
+                mbar_wait(bar_q, 0, kWaitCycles);
+                if (fused) mbar_wait(bar_c, 0, kWaitCycles);
+            }
+            if (P.status) atomicExch(P.status, kDevTimeoutTma);
+        }
+        __syncthreads();
+    } else if (owner && ts == 0) {  // the new row's value
+        float vv[4];
+        lds_kv<4>(lastv + dg * 4, vv);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float p = sc[(n - 1) * G + g];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[g][j] = fmaf(p, vv[j], acc[g][j]);
+        }
+    }
+    // ---- this CTA's partial (m, l, o) into its own shared memory (the ring is free)
+    if (!err) {
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) red[(ts * G + g) * HD + dg * 4 + j] = acc[g][j];
+    }
+    __syncthreads();
+    for (int i = tid; i < G * HD; i += kThreads) {
+        float v = 0.0f;
+        if (!err)
+            for (int r = 0; r < TS; ++r) v += red[r * G * HD + i];
+        po[i] = v;
+    }
+    if (tid < G) {
+        pm[tid] = err ? -INFINITY : s_m[tid];
+        pl[tid] = err ? 0.0f : s_l[tid];
+    }
+    cluster.sync();  // every rank's partial is visible cluster-wide
+    // ---- merge over DSMEM: weights exp(m_s - M) per (split, head), then this rank's
+    // slice of the output elements; empty splits (m_s = -inf, o = 0) weigh 0
+    if (tid < G) {
+        float M = -INFINITY;
+        for (int s = 0; s < ns; ++s) M = fmaxf(M, *cluster.map_shared_rank(pm + tid, s));
+        float L = 0.0f;
+        for (int s = 0; s < ns; ++s) {
+            const float ms = *cluster.map_shared_rank(pm + tid, s);
+            const float w = ms == -INFINITY ? 0.0f : expf(ms - M);
+            wgt[s * G + tid] = w;
+            L = fmaf(*cluster.map_shared_rank(pl + tid, s), w, L);
+        }
+        s_l[tid] = L;
+    }
+    __syncthreads();
+    const int per = (G * HD + ns - 1) / ns;
+    for (int i = split * per + tid; i < min(G * HD, (split + 1) * per); i += kThreads) {
+        const int g = i / HD;
+        float O = 0.0f;
+#pragma unroll 4
+        for (int s = 0; s < ns; ++s) O = fmaf(*cluster.map_shared_rank(po + i, s), wgt[s * G + g], O);
+        P.out[(size_t)kh * G * HD + i] = O / s_l[g];
+    }
+    cluster.sync();  // no rank leaves while another still reads its partial
+}
+
+template <typename KV, int HD, int G>
+int launch_t(const AttnArgs &a, cudaStream_t st) {
+    constexpr int RB = HD * (int)sizeof(KV);
+    constexpr int TS = kThreads / (HD / 4);
+    auto k = attn_tma_kernel<KV, HD, G>;
+    static std::atomic<unsigned long long> attr{0};
+    if (first_on_device(attr)) {
+        TQ_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        TQ_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    }
+    auto a16 = [](const void *p) { return ((uintptr_t)p & 15u) == 0; };
+    // splits = cluster size: about one CTA per SM over all KV heads, at most 16, at
+    // least 32 positions per split; halved while a cluster of that size cannot be
+    // scheduled (a cluster must fit in one GPC)
+    int ns = std::max(1, std::min(kMaxSplit, (num_sms() + a.n_kv_heads - 1) / a.n_kv_heads));
+    ns = std::min(ns, std::max(1, (a.max_seq + 31) / 32));
+    for (; ns >= 1; ns /= 2) {
+        TmaAttnParams P{};
+        P.q = a.q;
+        P.kc = (uint8_t *)a.k;
+        P.vc = (uint8_t *)a.v;
+        P.k_new = a.k_new;
+        P.v_new = a.v_new;
+        P.q_norm = a.q_norm;
+        P.k_norm = a.k_norm;
+        P.eps = a.eps;
+        P.cos_tab = a.cos_tab;
+        P.sin_tab = a.sin_tab;
+        P.pos = a.pos;
+        P.seq_len = a.seq_len;
+        P.max_seq = a.max_seq;
+        P.chunk_max = (a.max_seq + ns - 1) / ns;
+        P.scale = a.scale;
+        P.tile_rows = std::max(1, std::min(kTileBytes / RB, P.chunk_max));
+        P.stages = std::max(1, std::min(kStages, 2 * ((P.chunk_max + P.tile_rows - 1) / P.tile_rows)));
+        const size_t ring = (size_t)P.stages * P.tile_rows * RB;
+        const size_t part = ((size_t)TS * G * HD + (size_t)G * HD + 2 * G + (size_t)kMaxSplit * G) * 4;
+        P.stage_region = (int)((std::max(ring, part) + 15) & ~(size_t)15);
+        P.bulk_in = a16(a.q) && (!a.k_new || (a16(a.k_new) && a16(a.v_new) && a16(a.cos_tab) &&
+                                              a16(a.sin_tab) &&
+                                              (!a.q_norm || (a16(a.q_norm) && a16(a.k_norm)))));
+        P.out = a.out;
+        P.status = a.status;
+        const size_t smem = 128 + (size_t)P.stage_region + ((2 * (size_t)RB + 15) & ~(size_t)15) +
+                            ((size_t)4 * HD + (size_t)G * HD) * 4 + (size_t)P.chunk_max * G * 4;
+        if (smem > 227 * 1024) continue;
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(a.n_kv_heads, ns);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr_l[2];
+        attr_l[0].id = cudaLaunchAttributeClusterDimension;
+        attr_l[0].val.clusterDim.x = 1;
+        attr_l[0].val.clusterDim.y = ns;
+        attr_l[0].val.clusterDim.z = 1;
+        attr_l[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr_l[1].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr_l;
+        cfg.numAttrs = 1;
+        int nclusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&nclusters, k, &cfg) != cudaSuccess || nclusters < 1) {
+            cudaGetLastError();
+            continue;
+        }
+        cfg.numAttrs = a.pdl ? 2 : 1;
+        TQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, k, P));
+        return TQB200_OK;
+    }
+    return TQB200_ERR_UNSUPPORTED;
+}
+
+template <typename KV>
+int launch_kv(const AttnArgs &a, cudaStream_t st) {
+    const int G = a.n_heads / a.n_kv_heads;
+#define TQ_TMA_CASE(HDV, GV) \
+    if (a.head_dim == HDV && G == GV) return launch_t<KV, HDV, GV>(a, st);
+    TQ_TMA_CASE(64, 1) TQ_TMA_CASE(64, 2) TQ_TMA_CASE(64, 4) TQ_TMA_CASE(64, 7)
+    TQ_TMA_CASE(64, 8) TQ_TMA_CASE(128, 1) TQ_TMA_CASE(128, 2) TQ_TMA_CASE(128, 4)
+    TQ_TMA_CASE(128, 8) TQ_TMA_CASE(32, 1) TQ_TMA_CASE(32, 2) TQ_TMA_CASE(32, 4)
+    TQ_TMA_CASE(32, 8)
+#undef TQ_TMA_CASE
+    return TQB200_ERR_UNSUPPORTED;
+}
+
+}  // namespace
+
+int launch_attention_tma(const AttnArgs &a, cudaStream_t st) {
+    if (a.n_kv_heads <= 0 || a.n_heads % a.n_kv_heads != 0) return TQB200_ERR_UNSUPPORTED;
+    if (((uintptr_t)a.k | (uintptr_t)a.v) & 15u) return TQB200_ERR_UNSUPPORTED;
+    return a.kv_fp16 ? launch_kv<uint16_t>(a, st) : launch_kv<float>(a, st);
+}
+
+}  // namespace tqb200

@@ -280,22 +280,45 @@ __global__ void __launch_bounds__(kAttnThreads)
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    // merge the nsplit partials of this KV head
+    // merge the nsplit partials of this KV head.  The per-split (m, l) pairs go to
+    // shared memory in one parallel pass (red is free now and holds >= 1024*G floats,
+    // nsplit <= 296), each (split, head) weight exp(m_s - M) is computed once, and
+    // every output element then sums its nsplit weighted partials with independent
+    // loads.  Empty splits (m_s = -inf, o = 0) get weight 0.
     const float *pk = part + (size_t)kh * nsplit * G * (HD + 2);
+    const size_t PS = (size_t)G * (HD + 2);
+    float *wf = red;                        // [nsplit][G] m_s, then the weights
+    float *wl = red + (size_t)nsplit * G;   // [nsplit][G] l_s
+    for (int i = tid; i < nsplit * G; i += kAttnThreads) {
+        const int s = i / G, g = i - s * G;
+        wf[i] = __ldcg(pk + s * PS + g);
+        wl[i] = __ldcg(pk + s * PS + G + g);
+    }
+    __syncthreads();
+    if (tid < G) {
+        float M = -INFINITY;
+        for (int s = 0; s < nsplit; ++s) M = fmaxf(M, wf[s * G + tid]);
+        s_m[tid] = M;
+    }
+    __syncthreads();
+    for (int i = tid; i < nsplit * G; i += kAttnThreads) {
+        const float ms = wf[i];
+        wf[i] = ms == -INFINITY ? 0.0f : expf(ms - s_m[i % G]);
+    }
+    __syncthreads();
+    if (tid < G) {
+        float L = 0.0f;
+        for (int s = 0; s < nsplit; ++s) L = fmaf(wl[s * G + tid], wf[s * G + tid], L);
+        s_l[tid] = L;
+    }
+    __syncthreads();
     for (int i = tid; i < G * HD; i += kAttnThreads) {
         const int g = i / HD;
-        float M = -INFINITY;
-        for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(pk + (size_t)s * G * (HD + 2) + g));
-        float L = 0.0f, O = 0.0f;
-        for (int s = 0; s < nsplit; ++s) {
-            const float *ps = pk + (size_t)s * G * (HD + 2);
-            const float ms = __ldcg(ps + g);
-            if (ms == -INFINITY) continue;
-            const float f = expf(ms - M);
-            L = fmaf(__ldcg(ps + G + g), f, L);
-            O = fmaf(__ldcg(ps + 2 * G + i), f, O);
-        }
-        out[(size_t)kh * G * HD + i] = O / L;
+        const float *po = pk + 2 * G + i;
+        float O = 0.0f;
+#pragma unroll 8
+        for (int s = 0; s < nsplit; ++s) O = fmaf(__ldcg(po + s * PS), wf[s * G + g], O);
+        out[(size_t)kh * G * HD + i] = O / s_l[g];
     }
     if (tid == 0) tickets[kh] = 0u;
 }
@@ -620,7 +643,33 @@ size_t attn_partial_floats(int n_heads, int head_dim, int nsplit) {
 int launch_attention(const AttnArgs &a, cudaStream_t st) {
     TQ_CHECK_ARG(a.n_kv_heads > 0 && a.n_heads % a.n_kv_heads == 0, "heads %d / kv %d",
                  a.n_heads, a.n_kv_heads);
+    TQ_CHECK_ARG(!a.k_new || (a.pos && a.v_new && a.cos_tab && a.sin_tab), "fused attention args");
+    const int rc = launch_attention_tma(a, st);
+    if (rc != TQB200_ERR_UNSUPPORTED) return rc;
+    // no TMA shape: the split kernel (global partials), after the per-head
+    // QK-norm / RoPE / KV-append kernel in fused mode
     TQ_CHECK_ARG(a.chunk_max >= (a.max_seq + a.nsplit - 1) / a.nsplit, "chunk plan");
+    if (a.k_new) {
+        QkRopeKvArgs r{};
+        r.q = const_cast<float *>(a.q);
+        r.k = a.k_new;
+        r.v = a.v_new;
+        r.q_norm = a.q_norm;
+        r.k_norm = a.k_norm;
+        r.eps = a.eps;
+        r.cos_tab = a.cos_tab;
+        r.sin_tab = a.sin_tab;
+        r.pos = a.pos;
+        r.kcache = const_cast<void *>(a.k);
+        r.vcache = const_cast<void *>(a.v);
+        r.kv_fp16 = a.kv_fp16;
+        r.n_heads = a.n_heads;
+        r.n_kv_heads = a.n_kv_heads;
+        r.head_dim = a.head_dim;
+        r.max_seq = a.max_seq;
+        const int rr = launch_qk_rope_kv(r, st);
+        if (rr != TQB200_OK) return rr;
+    }
     return a.kv_fp16 ? launch_attn_kv<uint16_t>(a, st) : launch_attn_kv<float>(a, st);
 }
 

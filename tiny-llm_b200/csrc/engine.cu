@@ -306,28 +306,7 @@ int launch_forward(tqb200_engine *e) {
         const size_t es = e->o.kv_fp16 ? 2 : 4;
         void *kc = kvb + (size_t)l * e->layer_stride * es;
         void *vc = kvb + ((size_t)d.n_layers + l) * e->layer_stride * es;
-        {
-            QkRopeKvArgs a{};
-            a.q = e->q;
-            a.k = e->k;
-            a.v = e->v;
-            a.q_norm = w.q_norm;
-            a.k_norm = w.k_norm;
-            a.eps = d.rms_eps;
-            a.cos_tab = e->cos_tab;
-            a.sin_tab = e->sin_tab;
-            a.pos = e->io_in + 1;
-            a.kcache = kc;
-            a.vcache = vc;
-            a.kv_fp16 = e->o.kv_fp16;
-            a.n_heads = Hl;
-            a.n_kv_heads = KVl;
-            a.head_dim = hd;
-            a.max_seq = e->o.max_seq_len;
-            TQ_TRY(launch_qk_rope_kv(a, st));
-            TQ_TRY(mark(e, K_ROPE_KV));
-        }
-        {
+        {   // QK-norm + RoPE + KV append fused into the attention launch
             AttnArgs a{};
             a.q = e->q;
             a.k = kc;
@@ -345,6 +324,15 @@ int launch_forward(tqb200_engine *e) {
             a.partial = e->attn_part;
             a.tickets = e->attn_tickets;
             a.out = attn_mine;
+            a.k_new = e->k;
+            a.v_new = e->v;
+            a.q_norm = w.q_norm;
+            a.k_norm = w.k_norm;
+            a.eps = d.rms_eps;
+            a.cos_tab = e->cos_tab;
+            a.sin_tab = e->sin_tab;
+            a.pdl = pdl;
+            a.status = status;
             TQ_TRY(launch_attention(a, st));
             TQ_TRY(allgather(e, e->attn, qdl));
             TQ_TRY(mark(e, K_ATTN));

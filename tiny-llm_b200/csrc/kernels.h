@@ -115,10 +115,23 @@ struct AttnArgs {
     float *partial;           // attn_partial_floats(...)
     unsigned int *tickets;    // [n_kv_heads], zero-initialised
     float *out;               // [H*hd]
+    // Engine ("fused") mode, k_new != nullptr: q/k_new/v_new are the step's raw
+    // projections; QK-norm (optional), RoPE from the [max_seq][hd/2] tables and
+    // the KV append at position seq-1 happen inside the attention launch (one
+    // kernel where the shape has a TMA instantiation, else qk_rope_kv first).
+    const float *k_new = nullptr, *v_new = nullptr;
+    const float *q_norm = nullptr, *k_norm = nullptr;
+    float eps = 0.0f;
+    const float *cos_tab = nullptr, *sin_tab = nullptr;
+    bool pdl = false;         // programmatic dependent launch (TMA kernel only)
+    int *status = nullptr;    // device error word (bounded waits, bad position)
 };
 int attn_plan(int n_kv_heads, int max_seq, int *nsplit, int *chunk_max);
 size_t attn_partial_floats(int n_heads, int head_dim, int nsplit);
 int launch_attention(const AttnArgs &a, cudaStream_t st);
+// The TMA-staged, cluster-merged kernel alone (no scratch: partial/tickets unused);
+// TQB200_ERR_UNSUPPORTED, with nothing launched, for shapes it does not cover.
+int launch_attention_tma(const AttnArgs &a, cudaStream_t st);
 
 int launch_swiglu(float *g, const float *u, int n, cudaStream_t st);
 int launch_swiglu_out(const float *g, const float *u, float *out, int n, cudaStream_t st);
