@@ -1,0 +1,43 @@
+"""The drop-in boundary itself: the reference's own decode loop
+(QwenModel::forward_token and the GPU decode registry), built from the reference
+sources with tiny-llm_b200/host/b200_variants.cpp registered, run three ways on the
+same .tqwen file: reference CPU kernels, the "b200" per-op variants inside
+forward_token (--matvec-impl b200 --ops-impl b200), and the "b200" whole-step
+engine (--engine b200).  Greedy tokens must be identical.  The checker binary is
+built where the reference tree exists (tiny-llm_b200/host/Makefile); the test is
+skipped where it was not built."""
+from __future__ import annotations
+
+import os
+import subprocess
+
+import pytest
+
+import golden_cases as gc
+from tqb200.model import SynthModel
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+BIN = os.path.join(ROOT, "tiny-llm_b200", "host", "_build", "drop_in_check")
+
+
+@pytest.mark.parametrize("case", [c for c in gc.MODEL_CASES if c[0] in ("qwen2_bias", "vq2_rot")],
+                         ids=lambda c: c[0])
+def test_reference_decode_loop_with_b200_variants(tmp_path, case):
+    if not os.path.exists(BIN):
+        pytest.skip("drop_in_check not built (needs the reference tree at build time)")
+    name, spec, kv16, seed = case
+    path = str(tmp_path / f"{name}.tqwen")
+    SynthModel(spec, seed=seed).write_tqwen(path)
+    args = ["64", "6"] + [str(t) for t in gc.PROMPT]
+    run = lambda mode: subprocess.run([BIN, path, mode] + args, capture_output=True, text=True,
+                                      timeout=300)
+    ref = run("ref")
+    assert ref.returncode == 0, ref.stderr
+    ops = run("ops")
+    assert ops.returncode == 0, ops.stderr
+    assert ops.stdout.split() == ref.stdout.split()
+    if spec.weight_dtype == "i4":
+        eng = run("engine")
+        assert eng.returncode == 0, eng.stderr
+        assert eng.stdout.split() == ref.stdout.split()
