@@ -37,7 +37,6 @@ def test_reference_decode_loop_with_b200_variants(tmp_path, case):
     ops = run("ops")
     assert ops.returncode == 0, ops.stderr
     assert ops.stdout.split() == ref.stdout.split()
-    if spec.weight_dtype == "i4":
-        eng = run("engine")
-        assert eng.returncode == 0, eng.stderr
-        assert eng.stdout.split() == ref.stdout.split()
+    eng = run("engine")
+    assert eng.returncode == 0, eng.stderr
+    assert eng.stdout.split() == ref.stdout.split()

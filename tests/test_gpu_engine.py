@@ -10,12 +10,13 @@ import pytest
 
 import golden_cases as gc
 from conftest import max_rel
-from tqb200.model import QWEN25_05B, QWEN3_4B, SynthModel
+from tqb200.model import QWEN25_05B, QWEN3_06B_VQ2, QWEN3_4B, SynthModel
 from dataclasses import replace
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-4
-ENGINE_CASES = [c for c in gc.MODEL_CASES if c[0] in ("qwen2_bias", "qwen3_f16kv", "untied_f32embed")]
+ENGINE_CASES = [c for c in gc.MODEL_CASES
+                if c[0] in ("qwen2_bias", "qwen3_f16kv", "untied_f32embed", "vq2_rot")]
 
 
 @pytest.mark.parametrize("case", ENGINE_CASES, ids=[c[0] for c in ENGINE_CASES])
@@ -99,3 +100,13 @@ def test_config4_qwen3_4b(tq, oracle, kv16, tol):
     toks, otoks, worst = _decode_compare(tq, oracle, sm, prompt, 4, 4096, kv16)
     assert toks == otoks
     assert worst < tol, worst
+
+
+def test_config3_qwen3_06b_vq2_step(tq, oracle):
+    """BASELINE config 3 full step: 28-layer Qwen3-0.6B-shaped VQ2 model with a BiIP
+    rotation on every projection input (7 per layer), tied i4 embed / lm_head."""
+    sm = SynthModel(QWEN3_06B_VQ2, seed=0)
+    prompt = list(np.random.default_rng(3).integers(0, QWEN3_06B_VQ2.vocab, 8))
+    toks, otoks, worst = _decode_compare(tq, oracle, sm, prompt, 8, 64, False)
+    assert toks == otoks
+    assert worst < TOL, worst

@@ -318,15 +318,15 @@ static int vq2_host(const uint8_t *w, const float *x, float *y, int out_dim, int
         if (scale) TQ_TRY(upload(8, scale, (size_t)in_dim * 4, &dsc));
     }
     VqLaunch a;
-    a.w = (const uint8_t *)dw;
-    a.y = (float *)dy;
-    a.rows = out_dim;
+    a.job[0].w = (const uint8_t *)dw;
+    a.job[0].y = (float *)dy;
+    a.job[0].rows = out_dim;
+    a.job[0].rot_sign = (const float *)dsg;
+    a.job[0].rot_scale = (const float *)dsc;
+    a.job[0].rot_bs = bs;
     a.K = in_dim;
     a.x.mode = X_PLAIN;
     a.x.src = (const float *)dx;
-    a.rot_sign = (const float *)dsg;
-    a.rot_scale = (const float *)dsc;
-    a.rot_bs = bs;
     TQ_TRY(launch_vq2_matvec(a, g_ctx.stream));
     TQ_TRY(download(y, dy, (size_t)out_dim * 4));
     return finish();
@@ -348,15 +348,15 @@ int tqb200_dev_matvec_vq2_rot(const uint8_t *w, const float *x, float *y, int ou
                               void *stream) {
     TQ_CHECK_ARG(w && x && y && in_dim % 4 == 0, "vq2: bad arguments");
     VqLaunch a;
-    a.w = w;
-    a.y = y;
-    a.rows = out_dim;
+    a.job[0].w = w;
+    a.job[0].y = y;
+    a.job[0].rows = out_dim;
+    a.job[0].rot_sign = sign;
+    a.job[0].rot_scale = scale;
+    a.job[0].rot_bs = block_size;
     a.K = in_dim;
     a.x.mode = X_PLAIN;
     a.x.src = x;
-    a.rot_sign = sign;
-    a.rot_scale = scale;
-    a.rot_bs = block_size;
     return launch_vq2_matvec(a, (cudaStream_t)stream);
 }
 

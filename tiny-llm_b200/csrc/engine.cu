@@ -40,12 +40,18 @@
 namespace tqb200 {
 namespace {
 
+// Projection order of the per-projection BiIP rotations.
+enum Proj { P_Q, P_K, P_V, P_O, P_GATE, P_UP, P_DOWN, P_N };
+
 struct DLayer {
+    bool vq2 = false;  // projections are VQ2 (else i4)
     const float *input_ln = nullptr, *post_ln = nullptr;
     const uint8_t *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr;
     const uint8_t *gate = nullptr, *up = nullptr, *down = nullptr;
     const float *q_bias = nullptr, *k_bias = nullptr, *v_bias = nullptr;
     const float *q_norm = nullptr, *k_norm = nullptr;
+    const float *rot_sign[P_N] = {}, *rot_scale[P_N] = {};  // VQ2 BiIP (sign null: none)
+    int rot_bs[P_N] = {};
 };
 
 }  // namespace
@@ -136,21 +142,16 @@ size_t mat_bytes(const tqb200_matrix &m, int group) {
         if (s_) return s_;   \
     } while (0)
 
-int need_i4(const tqb200_matrix &m, int rows, int cols, const char *what, int layer) {
+int need_mat(const tqb200_matrix &m, int rows, int cols, int dtype, const char *what, int layer) {
     if (!m.data) return set_error(TQB200_ERR_INVALID_ARG, "layer %d: %s missing", layer, what);
-    if (m.dtype != TQB200_DT_I4)
-        return set_error(TQB200_ERR_UNSUPPORTED, "layer %d: %s dtype %d (engine path is i4)",
-                         layer, what, m.dtype);
+    if (m.dtype != dtype)
+        return set_error(TQB200_ERR_UNSUPPORTED,
+                         "layer %d: %s dtype %d (the engine needs every projection i4 (3) or "
+                         "every projection VQ2 (4); layer 0 has %d)",
+                         layer, what, m.dtype, dtype);
     if (m.rows != rows || m.cols != cols)
         return set_error(TQB200_ERR_INVALID_ARG, "layer %d: %s shape %dx%d, expected %dx%d",
                          layer, what, m.rows, m.cols, rows, cols);
-    return TQB200_OK;
-}
-
-int up_i4(tqb200_engine *e, const tqb200_matrix &m, const uint8_t **out) {
-    const void *p;
-    TQ_TRY(upload_bytes(e, m.data, mat_bytes(m, e->d.group_size), &p));
-    *out = (const uint8_t *)p;
     return TQB200_OK;
 }
 
@@ -159,6 +160,19 @@ int up_i4_rows(tqb200_engine *e, const tqb200_matrix &m, int r0, int n, const ui
     const size_t rb = tqb200_i4_row_bytes(m.cols, e->d.group_size);
     const void *p;
     TQ_TRY(upload_bytes(e, (const uint8_t *)m.data + (size_t)r0 * rb, (size_t)n * rb, &p));
+    *out = (const uint8_t *)p;
+    return TQB200_OK;
+}
+
+// Rows [r0, r0 + n) of a VQ2 matrix: its codebook followed by those rows' indices.
+int up_vq2_rows(tqb200_engine *e, const tqb200_matrix &m, int r0, int n, const uint8_t **out) {
+    const size_t rb = (size_t)m.cols / 4, cb = 2048;
+    void *p;
+    TQ_TRY(dev_alloc(e, cb + (size_t)n * rb, &p));
+    TQ_CUDA_TRY(cudaMemcpy(p, m.data, cb, cudaMemcpyHostToDevice));
+    TQ_CUDA_TRY(cudaMemcpy((uint8_t *)p + cb, (const uint8_t *)m.data + cb + (size_t)r0 * rb,
+                           (size_t)n * rb, cudaMemcpyHostToDevice));
+    e->weight_bytes += cb + (size_t)n * rb;
     *out = (const uint8_t *)p;
     return TQB200_OK;
 }
@@ -291,7 +305,33 @@ int launch_forward(tqb200_engine *e) {
     for (int l = 0; l < d.n_layers; ++l) {
         const DLayer &w = e->layers[l];
         e->cur_layer = l;
-        {   // q/k/v with the input RMSNorm fused into the prologue, biases into the epilogue
+        auto vq = [&](const uint8_t *m, float *y, const float *resid, int rows, int p) {
+            VqJob jb;
+            jb.w = m;
+            jb.y = y;
+            jb.resid = resid;
+            jb.rows = rows;
+            jb.rot_sign = w.rot_sign[p];
+            jb.rot_scale = w.rot_scale[p];
+            jb.rot_bs = w.rot_bs[p];
+            return jb;
+        };
+        auto vq_launch = [&](VqLaunch &a) {
+            a.pdl = pdl;
+            a.status = status;
+            return launch_vq2_matvec(a, st);
+        };
+        if (w.vq2) {  // q/k/v (each with its own rotation) after the input RMSNorm
+            VqLaunch a;
+            a.job[0] = vq(w.q, e->q, nullptr, qdl, P_Q);
+            a.job[1] = vq(w.k, e->k, nullptr, kvdl, P_K);
+            a.job[2] = vq(w.v, e->v, nullptr, kvdl, P_V);
+            a.n_jobs = 3;
+            a.K = H;
+            a.x = {X_RMSNORM, e->hidden, w.input_ln, d.rms_eps, nullptr};
+            TQ_TRY(vq_launch(a));
+            TQ_TRY(mark(e, K_QKV));
+        } else {   // q/k/v with the input RMSNorm fused into the prologue, biases into the epilogue
             I4Job j[3] = {{w.q, e->q, w.q_bias, nullptr, qdl},
                           {w.k, e->k, w.k_bias, nullptr, kvdl},
                           {w.v, e->v, w.v_bias, nullptr, kvdl}};
@@ -337,7 +377,15 @@ int launch_forward(tqb200_engine *e) {
             TQ_TRY(allgather(e, e->attn, qdl));
             TQ_TRY(mark(e, K_ATTN));
         }
-        {   // o_proj, residual fused: hidden = hidden + W_o attn (this rank's rows)
+        if (w.vq2) {
+            VqLaunch a;
+            a.job[0] = vq(w.o, hidden_mine, hidden_mine, Hs, P_O);
+            a.K = qd;
+            a.x = {X_PLAIN, e->attn, nullptr, 0.0f, nullptr};
+            TQ_TRY(vq_launch(a));
+            TQ_TRY(allgather(e, e->hidden, Hs));
+            TQ_TRY(mark(e, K_OPROJ));
+        } else {   // o_proj, residual fused: hidden = hidden + W_o attn (this rank's rows)
             I4Job j{w.o, hidden_mine, nullptr, hidden_mine, Hs};
             I4LaunchOpts o;
             o.x = {X_PLAIN, e->attn, nullptr, 0.0f, nullptr};
@@ -347,7 +395,18 @@ int launch_forward(tqb200_engine *e) {
             TQ_TRY(allgather(e, e->hidden, Hs));
             TQ_TRY(mark(e, K_OPROJ));
         }
-        {   // gate/up in one pass per row block (post-attention RMSNorm in the prologue),
+        if (w.vq2) {
+            VqLaunch a;
+            a.job[0] = vq(w.gate, e->act + (size_t)r * Is, nullptr, Is, P_GATE);
+            a.job[1] = vq(w.up, e->up, nullptr, Is, P_UP);
+            a.n_jobs = 2;
+            a.pair_swiglu = true;
+            a.K = H;
+            a.x = {X_RMSNORM, e->hidden, w.post_ln, d.rms_eps, nullptr};
+            TQ_TRY(vq_launch(a));
+            TQ_TRY(allgather(e, e->act, Is));
+            TQ_TRY(mark(e, K_GATEUP));
+        } else {   // gate/up in one pass per row block (post-attention RMSNorm in the prologue),
             // SwiGLU of each (gate, up) row pair in the epilogue -> act
             I4Job j[2] = {{w.gate, e->act + (size_t)r * Is, nullptr, nullptr, Is},
                           {w.up, e->up, nullptr, nullptr, Is}};
@@ -360,7 +419,15 @@ int launch_forward(tqb200_engine *e) {
             TQ_TRY(allgather(e, e->act, Is));
             TQ_TRY(mark(e, K_GATEUP));
         }
-        {   // down with the residual in the epilogue
+        if (w.vq2) {
+            VqLaunch a;
+            a.job[0] = vq(w.down, hidden_mine, hidden_mine, Hs, P_DOWN);
+            a.K = d.inter;
+            a.x = {X_PLAIN, e->act, nullptr, 0.0f, nullptr};
+            TQ_TRY(vq_launch(a));
+            TQ_TRY(allgather(e, e->hidden, Hs));
+            TQ_TRY(mark(e, K_DOWN));
+        } else {   // down with the residual in the epilogue
             I4Job j{w.down, hidden_mine, nullptr, hidden_mine, Hs};
             I4LaunchOpts o;
             o.x = {X_PLAIN, e->act, nullptr, 0.0f, nullptr};
@@ -492,28 +559,53 @@ int create_impl(const tqb200_model_desc *desc, const tqb200_engine_opts *opts, t
     for (int l = 0; l < d.n_layers; ++l) {
         const tqb200_layer &s = d.layers[l];
         DLayer &w = e->layers[l];
-        TQ_TRY(need_i4(s.q_proj, qd, H, "q_proj", l));
-        TQ_TRY(need_i4(s.k_proj, kvd, H, "k_proj", l));
-        TQ_TRY(need_i4(s.v_proj, kvd, H, "v_proj", l));
-        TQ_TRY(need_i4(s.o_proj, H, qd, "o_proj", l));
-        TQ_TRY(need_i4(s.gate_proj, d.inter, H, "gate_proj", l));
-        TQ_TRY(need_i4(s.up_proj, d.inter, H, "up_proj", l));
-        TQ_TRY(need_i4(s.down_proj, H, d.inter, "down_proj", l));
+        const int wdt = d.layers[0].q_proj.dtype;
+        TQ_CHECK_ARG(wdt == TQB200_DT_I4 || wdt == TQB200_DT_VQ2,
+                     "projection dtype %d: the engine path is i4 or VQ2", wdt);
+        TQ_TRY(need_mat(s.q_proj, qd, H, wdt, "q_proj", l));
+        TQ_TRY(need_mat(s.k_proj, kvd, H, wdt, "k_proj", l));
+        TQ_TRY(need_mat(s.v_proj, kvd, H, wdt, "v_proj", l));
+        TQ_TRY(need_mat(s.o_proj, H, qd, wdt, "o_proj", l));
+        TQ_TRY(need_mat(s.gate_proj, d.inter, H, wdt, "gate_proj", l));
+        TQ_TRY(need_mat(s.up_proj, d.inter, H, wdt, "up_proj", l));
+        TQ_TRY(need_mat(s.down_proj, H, d.inter, wdt, "down_proj", l));
         TQ_CHECK_ARG(s.input_ln && s.post_ln, "layer %d: norms missing", l);
         TQ_CHECK_ARG((s.q_norm == nullptr) == (s.k_norm == nullptr),
                      "layer %d: q_norm/k_norm must both be present or both absent", l);
-        TQ_CHECK_ARG(!s.rot_q.sign && !s.rot_o.sign && !s.rot_gate.sign && !s.rot_down.sign,
-                     "layer %d: BiIP-rotated projections are not on the i4 engine path", l);
+        w.vq2 = wdt == TQB200_DT_VQ2;
+        const tqb200_rotation *rots[P_N] = {&s.rot_q, &s.rot_k, &s.rot_v, &s.rot_o,
+                                            &s.rot_gate, &s.rot_up, &s.rot_down};
+        if (!w.vq2) {
+            for (int p = 0; p < P_N; ++p)
+                TQ_CHECK_ARG(!rots[p]->sign && !rots[p]->scale,
+                             "layer %d: BiIP rotations are only on the engine's VQ2 path", l);
+        } else {
+            TQ_CHECK_ARG(!s.q_bias && !s.k_bias && !s.v_bias,
+                         "layer %d: q/k/v biases are not supported with VQ2 projections", l);
+            const int rot_dim[P_N] = {H, H, H, qd, H, H, d.inter};
+            for (int p = 0; p < P_N; ++p) {
+                TQ_CHECK_ARG(rots[p]->sign || !rots[p]->scale,
+                             "layer %d: rotation %d has a scale but no sign", l, p);
+                const int bs = rots[p]->block_size;
+                TQ_CHECK_ARG(bs >= 0 && (bs & (bs - 1)) == 0, "layer %d: rotation block %d", l, bs);
+                TQ_TRY(up_vec(e, rots[p]->sign, rot_dim[p], &w.rot_sign[p]));
+                TQ_TRY(up_vec(e, rots[p]->scale, rot_dim[p], &w.rot_scale[p]));
+                w.rot_bs[p] = bs;
+            }
+        }
         TQ_TRY(up_vec(e, s.input_ln, H, &w.input_ln));
         TQ_TRY(up_vec(e, s.post_ln, H, &w.post_ln));
         // this rank's rows (all rows when tp == 1)
-        TQ_TRY(up_i4_rows(e, s.q_proj, r * qdl, qdl, &w.q));
-        TQ_TRY(up_i4_rows(e, s.k_proj, r * kvdl, kvdl, &w.k));
-        TQ_TRY(up_i4_rows(e, s.v_proj, r * kvdl, kvdl, &w.v));
-        TQ_TRY(up_i4_rows(e, s.o_proj, r * Hs, Hs, &w.o));
-        TQ_TRY(up_i4_rows(e, s.gate_proj, r * Is, Is, &w.gate));
-        TQ_TRY(up_i4_rows(e, s.up_proj, r * Is, Is, &w.up));
-        TQ_TRY(up_i4_rows(e, s.down_proj, r * Hs, Hs, &w.down));
+        auto up_rows = [&](const tqb200_matrix &m, int r0, int n, const uint8_t **o) {
+            return w.vq2 ? up_vq2_rows(e, m, r0, n, o) : up_i4_rows(e, m, r0, n, o);
+        };
+        TQ_TRY(up_rows(s.q_proj, r * qdl, qdl, &w.q));
+        TQ_TRY(up_rows(s.k_proj, r * kvdl, kvdl, &w.k));
+        TQ_TRY(up_rows(s.v_proj, r * kvdl, kvdl, &w.v));
+        TQ_TRY(up_rows(s.o_proj, r * Hs, Hs, &w.o));
+        TQ_TRY(up_rows(s.gate_proj, r * Is, Is, &w.gate));
+        TQ_TRY(up_rows(s.up_proj, r * Is, Is, &w.up));
+        TQ_TRY(up_rows(s.down_proj, r * Hs, Hs, &w.down));
         TQ_TRY(up_vec(e, s.q_bias ? s.q_bias + r * qdl : nullptr, qdl, &w.q_bias));
         TQ_TRY(up_vec(e, s.k_bias ? s.k_bias + r * kvdl : nullptr, kvdl, &w.k_bias));
         TQ_TRY(up_vec(e, s.v_bias ? s.v_bias + r * kvdl : nullptr, kvdl, &w.v_bias));

@@ -68,15 +68,23 @@ int launch_i4_dequant(const uint8_t *w, int rows, int dim, int group_size, float
                       cudaStream_t stream);
 
 // ------------------------------------------------------------------ VQ2 + BiIP
-struct VqLaunch {
+// One VQ2 matrix of a launch; each job has its own codebook and BiIP rotation.
+struct VqJob {
     const uint8_t *w = nullptr;   // [codebook 256x4 f16][rows x K/4 indices]
     float *y = nullptr;
     const float *resid = nullptr; // optional: y = resid + dot
-    int rows = 0, K = 0;
-    XSource x;
+    int rows = 0;
     const float *rot_sign = nullptr, *rot_scale = nullptr;  // BiIP of x (sign null: none)
-    int rot_bs = 0;
+    int rot_bs = 0;               // 0: the reference's block size for the input width
+};
+struct VqLaunch {
+    VqJob job[3];
+    int n_jobs = 1;
+    bool pair_swiglu = false;     // jobs (gate, up), equal rows: y_gate = silu(gate) * up
+    int K = 0;
+    XSource x;
     bool pdl = false;
+    int *status = nullptr;        // device error word (bounded-wait timeouts)
 };
 int launch_vq2_matvec(const VqLaunch &a, cudaStream_t st);
 int launch_biip(const float *x, float *y, int dim, const float *scale, const float *sign, int bs,

@@ -8,16 +8,22 @@
 //     y = FWHT_bs((x / scale) * sign) / sqrt(bs) per block of bs elements, with the
 //     butterfly order h = 1, 2, 4, ... (pairs (j, j+h)); elements past the last full
 //     block keep (x / scale) * sign.
+//   applied per projection as QwenModel::mv_rot does (runtime/qwen_model.cpp:229-238).
 //
-// Design: VQ2 at batch 1 is gather-bound, not HBM-bound (a weight byte selects a
-// 16-byte codebook vector).  The codebook is decoded once per CTA into shared
-// memory as 8 interleaved fp32 copies, entry k of copy p at byte k*128 + p*16:
-// the 8 lanes of each LDS.128 phase (lane % 8 = p) always hit 8 distinct 16-byte
-// bank groups, so the random lookups are conflict free.  Thread (slot, seg) owns
-// 16 columns (4 index bytes, one coalesced 32-bit load per row) and keeps its 16
-// activations in registers; row sums reduce through shared memory.  The BiIP
-// rotation (optionally after an RMSNorm) runs in the prologue in shared memory
-// with the reference's butterfly order, so the rotated activations are bit-exact.
+// Design.  VQ2 at batch 1 is latency- and gather-bound, not HBM-bound: a whole
+// Qwen3-0.6B-shaped layer is 3.9 MB, and a weight byte selects a 16-byte codebook
+// vector.  So a launch carries up to three matrices (q/k/v, or gate/up paired with
+// the SwiGLU epilogue), each CTA owns one contiguous row block of one matrix, and
+// everything a CTA reads comes in by TMA bulk copies issued up front: its
+// codebook, its whole index block and the constant vectors (RMSNorm weight, BiIP
+// sign and scale) before griddepcontrol.wait, the activation vector after it.
+// The codebook is decoded into shared memory as 8 interleaved fp32 copies (entry
+// k of copy p at byte k*128 + p*16): the 8 lanes of each LDS.128 phase (lane % 8
+// = p) hit 8 distinct 16-byte bank groups, so random lookups are conflict free.
+// Thread (slot, seg) owns 16 columns (4 index bytes per row) and keeps its 16
+// (rotated) activations in registers; row sums reduce through shared memory.  The
+// BiIP rotation runs in shared memory with the reference's butterfly order, so the
+// rotated activations are bit-exact.
 #include <algorithm>
 
 #include "common.cuh"
@@ -27,20 +33,21 @@ namespace tqb200 {
 
 namespace {
 
-constexpr int kVqThreads = 256;
+constexpr int kVqMaxThreads = 256;
+constexpr int kCbBytes = 2048;            // 256 entries x 4 fp16
+constexpr int kCbDecoded = 256 * 8 * 16;  // 8 interleaved fp32 copies
 
 struct VqParams {
-    const uint8_t *w;     // [codebook][indices]
-    float *y;
-    const float *resid;   // optional residual: y = resid + dot
-    int rows, K;
-    XSource x;            // X_PLAIN / X_RMSNORM / X_SWIGLU source
-    const float *rot_sign, *rot_scale;  // BiIP (sign == nullptr: no rotation)
-    int rot_bs;
-    int nt, S;            // threads per row (K/16) and row slots
+    VqJob job[3];
+    int cta_begin[4];  // CTAs [cta_begin[j], cta_begin[j+1]) serve job j (pair: job 0)
+    int n_jobs, pair, K, nt, S, rpc;  // rpc: rows per CTA (a multiple of S)
+    int bulk;          // bases 16-byte aligned and K % 64 == 0: bulk copies
+    int region;        // bytes of one matrix's staging region (codebook + index block)
+    XSource x;
+    int *status;
 };
 
-// In-place BiIP of v[0..K) in shared memory by the whole CTA.
+// In-place BiIP of v[0..K) in shared memory by the whole CTA (sign/scale anywhere).
 __device__ void biip_smem(float *v, int K, const float *sign, const float *scale, int bs) {
     for (int j = threadIdx.x; j < K; j += blockDim.x)
         v[j] = scale ? __fmul_rn(__fdiv_rn(v[j], scale[j]), sign[j]) : __fmul_rn(v[j], sign[j]);
@@ -65,28 +72,128 @@ __device__ void biip_smem(float *v, int K, const float *sign, const float *scale
     __syncthreads();
 }
 
-__global__ void __launch_bounds__(kVqThreads) vq2_matvec_kernel(const __grid_constant__ VqParams P) {
-    extern __shared__ __align__(16) uint8_t smem[];
-    float4 *cb = reinterpret_cast<float4 *>(smem);            // [256][8] float4
-    float *xs = reinterpret_cast<float *>(smem + 256 * 8 * 16);   // [K]
-    float *red = xs + P.K;                                     // [S][nt]
+__global__ void __launch_bounds__(kVqMaxThreads) vq2_matvec_kernel(const __grid_constant__ VqParams P) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int t = threadIdx.x, K = P.K, nm = 1 + P.pair;  // matrices this CTA reads
+    const size_t K4 = ((size_t)K * 4 + 15) & ~(size_t)15;
+    uint64_t *bar_w = reinterpret_cast<uint64_t *>(smem);  // codebooks, indices, constants
+    uint64_t *bar_x = bar_w + 1;                            // activation (+ SwiGLU up)
+    uint8_t *cbf = smem + 128;                              // [nm][kCbDecoded]
+    uint8_t *raw = cbf + (size_t)nm * kCbDecoded;           // [nm][region]
+    float *xs = reinterpret_cast<float *>(raw + (size_t)nm * P.region);  // [K]
+    float *wsm = xs + K4 / 4;                               // [K] norm weight / up
+    float *xr = wsm + K4 / 4;                               // [nm][K] rotated
+    float *rot = xr + (size_t)nm * K4 / 4;                  // [nm][2][K] sign, scale
+    float *red = rot + (size_t)nm * 2 * K4 / 4;             // [nm][S][nt]
+    __shared__ int s_err;
     __shared__ double s_rd[32];
-    const int t = threadIdx.x, K = P.K;
-    // codebook -> 8 interleaved fp32 copies (weights: no dependency on the previous kernel)
-    for (int i = t; i < 256 * 8; i += blockDim.x) {
-        const int k = i >> 3;
-        const uint16_t *h = reinterpret_cast<const uint16_t *>(P.w) + k * 4;
-        cb[i] = make_float4(h2f(h[0]), h2f(h[1]), h2f(h[2]), h2f(h[3]));
+
+    int j = 0;
+    while (j + 1 < P.n_jobs && (int)blockIdx.x >= P.cta_begin[j + 1]) ++j;
+    const int r0 = ((int)blockIdx.x - P.cta_begin[j]) * P.rpc;
+    const int r1 = min(P.job[j].rows, r0 + P.rpc);
+    const int nb = K / 4;  // index bytes per row
+    const size_t idx_bytes = (size_t)max(0, r1 - r0) * nb;
+    const bool norm = P.x.mode == X_RMSNORM;
+
+    // ---- constant inputs (weights, norm weight, rotation vectors) before the wait
+    if (t == 0) {
+        mbar_init(bar_w, 1);
+        mbar_init(bar_x, 1);
+        fence_mbar_init();
+        s_err = 0;
+        if (P.bulk) {
+            uint32_t tx = 0;
+            for (int m = 0; m < nm; ++m) {
+                const VqJob &jb = P.job[P.pair ? m : j];
+                tx += kCbBytes + (uint32_t)idx_bytes;
+                if (jb.rot_sign) tx += (uint32_t)K * 4u * (jb.rot_scale ? 2u : 1u);
+            }
+            if (norm) tx += (uint32_t)K * 4u;
+            mbar_arrive_expect_tx(bar_w, tx);
+            for (int m = 0; m < nm; ++m) {
+                const VqJob &jb = P.job[P.pair ? m : j];
+                uint8_t *dst = raw + (size_t)m * P.region;
+                bulk_g2s(dst, jb.w, kCbBytes, bar_w);
+                if (idx_bytes) bulk_g2s(dst + kCbBytes, jb.w + kCbBytes + (size_t)r0 * nb,
+                                        (uint32_t)idx_bytes, bar_w);
+                if (jb.rot_sign) {
+                    bulk_g2s(rot + (size_t)(2 * m) * K4 / 4, jb.rot_sign, (uint32_t)K * 4u, bar_w);
+                    if (jb.rot_scale)
+                        bulk_g2s(rot + (size_t)(2 * m + 1) * K4 / 4, jb.rot_scale, (uint32_t)K * 4u,
+                                 bar_w);
+                }
+            }
+            if (norm) bulk_g2s(wsm, P.x.norm_w, (uint32_t)K * 4u, bar_w);
+        }
     }
     griddep_wait();
-    // activation prologue: source (+RMSNorm / SwiGLU), then BiIP
-    float rms_scale = 0.0f;
-    if (P.x.mode == X_RMSNORM) {
-        double ss = 0.0;
-        for (int i = t; i < K; i += blockDim.x) {
-            const double v = (double)P.x.src[i];
-            ss += v * v;
+    griddep_launch();
+    if (t == 0 && P.bulk) {
+        const uint32_t xb = (uint32_t)K * 4u;
+        mbar_arrive_expect_tx(bar_x, P.x.mode == X_SWIGLU ? 2 * xb : xb);
+        bulk_g2s(xs, P.x.src, xb, bar_x);
+        if (P.x.mode == X_SWIGLU) bulk_g2s(wsm, P.x.up, xb, bar_x);
+    }
+    if (!P.bulk) {
+        // unaligned inputs: the same staging with plain loads, 4 in flight per thread
+        for (int m = 0; m < nm; ++m) {
+            const VqJob &jb = P.job[P.pair ? m : j];
+            uint8_t *dst = raw + (size_t)m * P.region;
+            const size_t n = kCbBytes + idx_bytes;
+            for (size_t i0 = t; i0 < n; i0 += 4 * blockDim.x) {
+                uint8_t v[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const size_t i = i0 + (size_t)k * blockDim.x;
+                    v[k] = i < n ? jb.w[i < (size_t)kCbBytes ? i : i + (size_t)r0 * nb] : 0;
+                }
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const size_t i = i0 + (size_t)k * blockDim.x;
+                    if (i < n) dst[i] = v[k];
+                }
+            }
+            if (jb.rot_sign)
+                for (int i = t; i < K; i += blockDim.x) {
+                    rot[(size_t)(2 * m) * K4 / 4 + i] = jb.rot_sign[i];
+                    if (jb.rot_scale) rot[(size_t)(2 * m + 1) * K4 / 4 + i] = jb.rot_scale[i];
+                }
         }
+        for (int i = t; i < K; i += blockDim.x) {
+            xs[i] = P.x.src[i];
+            if (norm) wsm[i] = P.x.norm_w[i];
+            if (P.x.mode == X_SWIGLU) wsm[i] = P.x.up[i];
+        }
+    } else if (t == 0) {
+        if (!mbar_wait(bar_w, 0, kWaitCycles)) s_err = 1;
+        if (!mbar_wait(bar_x, 0, kWaitCycles)) s_err = 1;
+    }
+    __syncthreads();
+    if (s_err) {
+        if (t == 0) {  // drain before exit
+            mbar_wait(bar_w, 0, kWaitCycles);
+            mbar_wait(bar_x, 0, kWaitCycles);
+            if (P.status) atomicExch(P.status, kDevTimeoutTma);
+        }
+        return;
+    }
+    // ---- codebooks -> 8 interleaved fp32 copies (thread t decodes entry t)
+    for (int m = 0; m < nm; ++m) {
+        const uint8_t *cr = raw + (size_t)m * P.region;
+        float4 *cb = reinterpret_cast<float4 *>(cbf + (size_t)m * kCbDecoded);
+        for (int k = t; k < 256; k += blockDim.x) {
+            const uint2 h = *reinterpret_cast<const uint2 *>(cr + 8 * k);
+            const float4 c = make_float4(h2f((uint16_t)(h.x & 0xFFFFu)), h2f((uint16_t)(h.x >> 16)),
+                                         h2f((uint16_t)(h.y & 0xFFFFu)), h2f((uint16_t)(h.y >> 16)));
+#pragma unroll
+            for (int p = 0; p < 8; ++p) cb[k * 8 + p] = c;
+        }
+    }
+    // ---- activation: RMSNorm / SwiGLU in place, then each matrix's rotation
+    if (norm) {
+        double ss = 0.0;
+        for (int i = t; i < K; i += blockDim.x) ss += (double)xs[i] * (double)xs[i];
         ss = warp_sum_d(ss);
         if ((t & 31) == 0) s_rd[t >> 5] = ss;
         __syncthreads();
@@ -96,69 +203,90 @@ __global__ void __launch_bounds__(kVqThreads) vq2_matvec_kernel(const __grid_con
             if (t == 0) s_rd[0] = v;
         }
         __syncthreads();
-        rms_scale = 1.0f / sqrtf(__fadd_rn((float)(s_rd[0] / K), P.x.eps));
-    }
-    for (int i = t; i < K; i += blockDim.x) {
-        float v;
-        if (P.x.mode == X_RMSNORM) {
-            v = __fmul_rn(__fmul_rn(P.x.src[i], rms_scale), P.x.norm_w[i]);
-        } else if (P.x.mode == X_SWIGLU) {
-            const float g = P.x.src[i];
-            v = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), P.x.up[i]);
-        } else {
-            v = P.x.src[i];
+        const float rms = 1.0f / sqrtf(__fadd_rn((float)(s_rd[0] / K), P.x.eps));
+        for (int i = t; i < K; i += blockDim.x) xs[i] = __fmul_rn(__fmul_rn(xs[i], rms), wsm[i]);
+    } else if (P.x.mode == X_SWIGLU) {
+        for (int i = t; i < K; i += blockDim.x) {
+            const float g = xs[i];
+            xs[i] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), wsm[i]);
         }
-        xs[i] = v;
     }
     __syncthreads();
-    if (P.rot_sign) biip_smem(xs, K, P.rot_sign, P.rot_scale, P.rot_bs);
-    griddep_launch();
+    const float *xm0 = xs, *xm1 = xs;
+    for (int m = 0; m < nm; ++m) {
+        const VqJob &jb = P.job[P.pair ? m : j];
+        if (!jb.rot_sign) continue;
+        float *v = xr + (size_t)m * K4 / 4;
+        for (int i = t; i < K; i += blockDim.x) v[i] = xs[i];
+        __syncthreads();
+        biip_smem(v, K, rot + (size_t)(2 * m) * K4 / 4,
+                  jb.rot_scale ? rot + (size_t)(2 * m + 1) * K4 / 4 : nullptr, jb.rot_bs);
+        if (m == 0) xm0 = v;
+        else xm1 = v;
+    }
 
     const int nt = P.nt, S = P.S;
     const int slot = t / nt, sg = t - slot * nt;
     const bool active = slot < S;
     const int c0 = sg * 16;  // 4 blocks of 4 columns
-    float xv[16];
+    float xv[2][16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) xv[i] = (active && c0 + i < K) ? xs[c0 + i] : 0.0f;
+    for (int i = 0; i < 16; ++i) {
+        const bool in = active && c0 + i < K;
+        xv[0][i] = in ? xm0[c0 + i] : 0.0f;
+        xv[1][i] = (in && nm > 1) ? xm1[c0 + i] : 0.0f;
+    }
     const uint32_t lane_off = (uint32_t)(t & 7) * 16u;
-    const uint8_t *cbb = smem;
-    const int nb = K / 4;
-    const uint8_t *idx = P.w + 2048;
     const int lane = t & 31, warp = t >> 5, nwarps = blockDim.x >> 5;
-    for (int r0 = blockIdx.x * S; r0 < P.rows; r0 += gridDim.x * S) {
-        const int row = r0 + slot;
+    const VqJob &job = P.job[j];
+    for (int rb = r0; rb < r1; rb += S) {
+        const int row = rb + slot;
         if (active) {
-            float acc = 0.0f;
-            if (row < P.rows) {
-                const uint8_t *ip = idx + (size_t)row * nb + sg * 4;
-                uint32_t wd;
-                if (sg * 4 + 4 <= nb && (((uintptr_t)ip) & 3u) == 0) {
-                    wd = ldg_u32(ip);
-                } else {
-                    wd = 0;
-                    for (int b = 0; b < 4 && sg * 4 + b < nb; ++b) wd |= (uint32_t)ip[b] << (8 * b);
-                }
 #pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                    const uint32_t k = (wd >> (8 * b)) & 0xFFu;
-                    const float4 c = *reinterpret_cast<const float4 *>(cbb + (k << 7) + lane_off);
-                    acc = fmaf(c.x, xv[4 * b + 0], acc);
-                    acc = fmaf(c.y, xv[4 * b + 1], acc);
-                    acc = fmaf(c.z, xv[4 * b + 2], acc);
-                    acc = fmaf(c.w, xv[4 * b + 3], acc);
+            for (int m = 0; m < 2; ++m) {
+                if (m >= nm) break;
+                float acc = 0.0f;
+                if (row < r1) {
+                    const uint8_t *ip =
+                        raw + (size_t)m * P.region + kCbBytes + (size_t)(row - r0) * nb + sg * 4;
+                    uint32_t wd = 0;
+                    if (sg * 4 + 4 <= nb && ((uintptr_t)ip & 3u) == 0) {
+                        wd = *reinterpret_cast<const uint32_t *>(ip);
+                    } else {
+                        for (int b = 0; b < 4 && sg * 4 + b < nb; ++b) wd |= (uint32_t)ip[b] << (8 * b);
+                    }
+                    const uint8_t *cbb = cbf + (size_t)m * kCbDecoded;
+#pragma unroll
+                    for (int b = 0; b < 4; ++b) {
+                        const uint32_t k = (wd >> (8 * b)) & 0xFFu;
+                        const float4 c = *reinterpret_cast<const float4 *>(cbb + (k << 7) + lane_off);
+                        acc = fmaf(c.x, xv[m][4 * b + 0], acc);
+                        acc = fmaf(c.y, xv[m][4 * b + 1], acc);
+                        acc = fmaf(c.z, xv[m][4 * b + 2], acc);
+                        acc = fmaf(c.w, xv[m][4 * b + 3], acc);
+                    }
                 }
+                red[((size_t)m * S + slot) * nt + sg] = acc;
             }
-            red[slot * nt + sg] = acc;
         }
         __syncthreads();
         for (int rl = warp; rl < S; rl += nwarps) {
-            const int rr = r0 + rl;
-            if (rr >= P.rows) continue;
-            float v = 0.0f;
-            for (int i = lane; i < nt; i += 32) v += red[rl * nt + i];
+            const int rr = rb + rl;
+            if (rr >= r1) continue;
+            float v = 0.0f, u = 0.0f;
+            for (int i = lane; i < nt; i += 32) v += red[(size_t)rl * nt + i];
             v = warp_sum(v);
-            if (lane == 0) P.y[rr] = P.resid ? P.resid[rr] + v : v;
+            if (P.pair) {
+                for (int i = lane; i < nt; i += 32) u += red[((size_t)S + rl) * nt + i];
+                u = warp_sum(u);
+            }
+            if (lane == 0) {
+                if (P.pair) {  // swiglu_ref (kernels/silu/swiglu_ref.cpp:41-52) on (gate, up)
+                    job.y[rr] = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), u);
+                } else {
+                    job.y[rr] = job.resid ? job.resid[rr] + v : v;
+                }
+            }
         }
         __syncthreads();
     }
@@ -174,41 +302,71 @@ __global__ void biip_kernel(const float *__restrict__ x, float *__restrict__ y, 
     for (int j = threadIdx.x; j < dim; j += blockDim.x) y[j] = v[j];
 }
 
+int hadamard_bs(int dim) {  // runtime/qwen_model.cpp:61-67
+    for (int b = 256; b >= 2; b >>= 1)
+        if (dim % b == 0) return b;
+    return 1;
+}
+
 }  // namespace
 
 int launch_vq2_matvec(const VqLaunch &a, cudaStream_t st) {
-    TQ_CHECK_ARG(a.rows >= 0 && a.K > 0 && a.K % 4 == 0, "vq2: bad shape %d x %d", a.rows, a.K);
-    TQ_CHECK_ARG(!a.rot_sign || (a.rot_bs >= 1 && (a.rot_bs & (a.rot_bs - 1)) == 0),
-                 "vq2: rotation block %d", a.rot_bs);
-    if (a.rows == 0) return TQB200_OK;
+    TQ_CHECK_ARG(a.n_jobs >= 1 && a.n_jobs <= 3, "vq2: n_jobs %d", a.n_jobs);
+    TQ_CHECK_ARG(a.K > 0 && a.K % 4 == 0, "vq2: in_dim %d not a multiple of 4", a.K);
+    TQ_CHECK_ARG(!a.pair_swiglu || (a.n_jobs == 2 && a.job[0].rows == a.job[1].rows),
+                 "vq2: paired SwiGLU needs two jobs with equal rows");
     VqParams P{};
-    P.w = a.w;
-    P.y = a.y;
-    P.resid = a.resid;
-    P.rows = a.rows;
+    P.n_jobs = a.n_jobs;
+    P.pair = a.pair_swiglu ? 1 : 0;
     P.K = a.K;
     P.x = a.x;
-    P.rot_sign = a.rot_sign;
-    P.rot_scale = a.rot_scale;
-    P.rot_bs = a.rot_bs;
+    P.status = a.status;
     P.nt = (a.K + 15) / 16;
-    TQ_CHECK_ARG(P.nt <= kVqThreads, "vq2: in_dim %d above %d", a.K, 16 * kVqThreads);
-    P.S = std::max(1, kVqThreads / P.nt);
-    const size_t smem = 256 * 8 * 16 + (size_t)a.K * 4 + (size_t)P.S * P.nt * 4;
-    static bool attr = false;
-    if (!attr) {
-        TQ_CUDA_TRY(cudaFuncSetAttribute(vq2_matvec_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
-        attr = true;
+    TQ_CHECK_ARG(P.nt <= kVqMaxThreads, "vq2: in_dim %d above %d", a.K, 16 * kVqMaxThreads);
+    P.S = std::max(1, kVqMaxThreads / P.nt);
+    const int block = (P.S * P.nt + 31) / 32 * 32;
+    auto a16 = [](const void *p) { return ((uintptr_t)p & 15u) == 0; };
+    bool bulk = a.K % 64 == 0 && a16(a.x.src) && (a.x.mode != X_RMSNORM || a16(a.x.norm_w)) &&
+                (a.x.mode != X_SWIGLU || a16(a.x.up));
+    int total = 0;
+    for (int j = 0; j < a.n_jobs; ++j) {
+        const VqJob &jb = a.job[j];
+        TQ_CHECK_ARG(jb.rows >= 0 && (jb.rows == 0 || (jb.w && jb.y)), "vq2: job %d", j);
+        TQ_CHECK_ARG(!jb.rot_sign || jb.rot_bs == 0 || (jb.rot_bs & (jb.rot_bs - 1)) == 0,
+                     "vq2: rotation block %d", jb.rot_bs);
+        P.job[j] = jb;
+        if (jb.rot_sign && jb.rot_bs == 0) P.job[j].rot_bs = hadamard_bs(a.K);
+        bulk = bulk && a16(jb.w) &&
+               (!jb.rot_sign || (a16(jb.rot_sign) && (!jb.rot_scale || a16(jb.rot_scale))));
+        if (!P.pair || j == 0) total += jb.rows;
     }
-    TQ_CHECK_ARG(smem <= 160 * 1024, "vq2: in_dim %d needs too much shared memory", a.K);
-    int per_sm = 1;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, vq2_matvec_kernel, kVqThreads, smem);
-    const int passes = (a.rows + P.S - 1) / P.S;
-    const int grid = std::max(1, std::min(passes, std::max(1, per_sm) * num_sms()));
+    if (total == 0) return TQB200_OK;
+    P.bulk = bulk ? 1 : 0;
+    // rows per CTA: ~2 CTAs per SM over all the launch's rows, a multiple of S
+    const int target = 2 * num_sms();
+    int rpc = (total + target - 1) / target;
+    rpc = std::max(P.S, (rpc + P.S - 1) / P.S * P.S);
+    P.rpc = rpc;
+    int ctas = 0;
+    for (int j = 0; j < a.n_jobs; ++j) {
+        P.cta_begin[j] = ctas;
+        if (!P.pair || j == 0) ctas += (a.job[j].rows + rpc - 1) / rpc;
+    }
+    for (int j = a.n_jobs; j <= 3; ++j) P.cta_begin[j] = ctas;
+    if (P.pair) P.cta_begin[1] = P.cta_begin[2] = P.cta_begin[3] = ctas;
+    const int nm = 1 + P.pair;
+    P.region = (int)(((size_t)kCbBytes + (size_t)rpc * (a.K / 4) + 15) & ~(size_t)15);
+    const size_t K4 = ((size_t)a.K * 4 + 15) & ~(size_t)15;
+    const size_t smem = 128 + (size_t)nm * (kCbDecoded + P.region) + 2 * K4 + (size_t)nm * 3 * K4 +
+                        (size_t)nm * P.S * P.nt * 4;
+    TQ_CHECK_ARG(smem <= 200 * 1024, "vq2: in_dim %d needs too much shared memory", a.K);
+    static std::atomic<unsigned long long> attr{0};
+    if (first_on_device(attr))
+        TQ_CUDA_TRY(cudaFuncSetAttribute(vq2_matvec_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kVqThreads);
+    cfg.gridDim = dim3(ctas);
+    cfg.blockDim = dim3(block);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr_l[1];
@@ -224,12 +382,10 @@ int launch_biip(const float *x, float *y, int dim, const float *scale, const flo
                 cudaStream_t st) {
     TQ_CHECK_ARG(dim > 0 && sign && bs >= 1 && (bs & (bs - 1)) == 0, "biip: bad arguments");
     TQ_CHECK_ARG((size_t)dim * 4 <= 160 * 1024, "biip: dim %d too large", dim);
-    static bool attr = false;
-    if (!attr) {
+    static std::atomic<unsigned long long> attr{0};
+    if (first_on_device(attr))
         TQ_CUDA_TRY(cudaFuncSetAttribute(biip_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          160 * 1024));
-        attr = true;
-    }
     biip_kernel<<<1, 512, (size_t)dim * 4, st>>>(x, y, dim, sign, scale, bs);
     TQ_CUDA_TRY(cudaGetLastError());
     return TQB200_OK;
