@@ -59,6 +59,17 @@ def dist_init():
     return world, rank, local, pg
 
 
+def share_nccl_id(pg, rank: int) -> bytes:
+    """Rank 0's NCCL unique id (the engine's own communicator), broadcast to every rank."""
+    import torch
+    from tqb200 import lib
+    nid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+    if rank == 0:
+        nid.copy_(torch.frombuffer(bytearray(lib.nccl_unique_id()), dtype=torch.uint8))
+    pg.broadcast(nid, src=0)
+    return bytes(nid.cpu().numpy().tobytes())
+
+
 def barrier(pg):
     if pg is not None:
         pg.barrier()
@@ -317,7 +328,11 @@ def bench_decode(args, rank, pg, pk, pk_kind):
     t0 = time.time()
     sm = SynthModel(spec, seed=0)
     t_build = time.time() - t0
-    eng = lib.Engine(sm, max_seq_len=max_seq, kv_fp16=True)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    tp = {}
+    if world > 1:  # tensor parallel: every projection's output rows sharded over the ranks
+        tp = {"tp_size": world, "tp_rank": rank, "nccl_id": share_nccl_id(pg, rank)}
+    eng = lib.Engine(sm, max_seq_len=max_seq, kv_fp16=True, **tp)
     del sm.tensors  # host copy no longer needed
     # KV for context 4096: run the engine itself over positions 0..4095-W (greedy from token 1)
     rng = np.random.default_rng(1)
@@ -337,7 +352,6 @@ def bench_decode(args, rank, pg, pk, pk_kind):
     clk = clocks.stop()
     dev_ms = max_over_ranks(pg, dev_ms)
     ms_step = dev_ms / K
-    world = int(os.environ.get("WORLD_SIZE", "1"))
 
     # e2e: the C-ABI step call with host token in / host token out, every step
     tok = toks[-1]

@@ -1,0 +1,51 @@
+"""Tensor-parallel engine (tp_size 2, one process per GPU, NCCL all-gather per layer)
+against the single-GPU oracle: identical greedy tokens and logits within 1e-4 on
+every rank.  Needs two visible GPUs (skipped otherwise)."""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+import golden_cases as gc
+from conftest import max_rel
+from tqb200.model import SynthModel
+
+pytestmark = pytest.mark.gpu
+HERE = os.path.dirname(os.path.abspath(__file__))
+TP_CASES = [c for c in gc.MODEL_CASES if c[0] in ("qwen2_bias", "qwen3_f16kv", "vq2_rot")]
+
+
+@pytest.mark.parametrize("case", TP_CASES, ids=[c[0] for c in TP_CASES])
+def test_tp2_engine_matches_oracle(tq, oracle, tmp_path, case):
+    import torch
+    world = 2
+    if torch.cuda.device_count() < world:
+        pytest.skip("needs 2 GPUs")
+    name, spec, kv16, seed = case
+    nid = tq.nccl_unique_id().hex()
+    outs = [str(tmp_path / f"r{r}.npz") for r in range(world)]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    procs = [subprocess.Popen([sys.executable, os.path.join(HERE, "tp_worker.py"), str(r),
+                               str(world), nid, name, outs[r]], env=env,
+                              stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
+             for r in range(world)]
+    logs = []
+    for p in procs:
+        try:
+            logs.append(p.communicate(timeout=240)[0])
+        except subprocess.TimeoutExpired:
+            for q in procs:
+                q.kill()
+            pytest.fail("tensor-parallel ranks did not finish")
+    assert all(p.returncode == 0 for p in procs), logs
+    om = oracle.model(SynthModel(spec, seed=seed), 64, kv16)
+    otoks, ologits = gc.model_tokens(om, steps=10)
+    for r in range(world):
+        d = np.load(outs[r])
+        assert list(d["tokens"]) == otoks, (r, list(d["tokens"]), otoks)
+        for a, b in zip(d["logits"], ologits):
+            assert max_rel(a, b) < 1e-4
