@@ -466,7 +466,7 @@ int launch_t(const AttnArgs &a, cudaStream_t st) {
     auto k = attn_tma_kernel<KV, HD, G>;
     static std::atomic<unsigned long long> attr{0};
     if (first_on_device(attr)) {
-        TQ_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        TQ_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, max_dyn_smem()));
         TQ_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     }
     auto a16 = [](const void *p) { return ((uintptr_t)p & 15u) == 0; };
@@ -504,7 +504,7 @@ int launch_t(const AttnArgs &a, cudaStream_t st) {
         P.status = a.status;
         const size_t smem = 128 + (size_t)P.stage_region + ((2 * (size_t)RB + 15) & ~(size_t)15) +
                             ((size_t)4 * HD + (size_t)G * HD) * 4 + (size_t)P.chunk_max * G * 4;
-        if (smem > 227 * 1024) continue;
+        if (smem > (size_t)max_dyn_smem()) continue;
         cudaLaunchConfig_t cfg{};
         cfg.gridDim = dim3(a.n_kv_heads, ns);
         cfg.blockDim = dim3(kThreads);

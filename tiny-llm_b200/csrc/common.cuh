@@ -19,15 +19,28 @@ int set_error(int status, const char *fmt, ...);
 #define TQ_CUDA_TRY(expr)                                                                  \
     do {                                                                                   \
         cudaError_t e_ = (expr);                                                           \
-        if (e_ != cudaSuccess)                                                             \
+        if (e_ != cudaSuccess) {                                                           \
+            cudaGetLastError(); /* a non-sticky error must not surface at a later check */ \
             return ::tqb200::set_error(TQB200_ERR_CUDA, "%s:%d %s: %s", __FILE__, __LINE__, \
                                        #expr, cudaGetErrorString(e_));                     \
+        }                                                                                  \
     } while (0)
 
 #define TQ_CHECK_ARG(cond, ...)                                                            \
     do {                                                                                   \
         if (!(cond)) return ::tqb200::set_error(TQB200_ERR_INVALID_ARG, __VA_ARGS__);      \
     } while (0)
+
+// Largest dynamic shared memory a block may opt into on the current device.
+inline int max_dyn_smem() {
+    int dev = 0, v = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) {
+        cudaGetLastError();
+        return 227 * 1024 - 1024;
+    }
+    return v;
+}
 
 // True the first time it is called on the current device for this mask (kernel
 // attributes such as the dynamic shared-memory limit are per device).

@@ -169,28 +169,56 @@ __device__ void issue_pass(const MvParams &P, int p, int s, uint64_t *bars, uint
     if (b1) bulk_g2s(dst + cap, src1, b1, &bars[s]);
 }
 
+constexpr int kBarBytes = 256;  // 2*kMaxStages + 2 mbarriers, rounded up
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Named barrier 1 over the consumer warps, returning the OR of `pred` across them
+// (uniform: every consumer thread gets the same answer).
+__device__ __forceinline__ bool consumer_sync_or(int nthreads, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n bar.red.or.pred p, 1, %2, q;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(r)
+        : "r"((uint32_t)pred), "r"(nthreads)
+        : "memory");
+    return r != 0;
+}
+
+// dp4a digit planes of one segment: 6 words per 8 columns, then 4 words of padding
+// (a row stride of 6*NW+4 words keeps the 16-byte loads of 8 consecutive segments on
+// distinct bank groups)
+template <int NW> struct DigitLayout { static constexpr int stride = 6 * NW + 4; };
+
 template <int SEG, int MATH>
 __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ MvParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int NW = SEG / 8;
+    constexpr int DS = DigitLayout<NW>::stride;
     const int t = threadIdx.x;
+    const int lane = t & 31, warp = t >> 5;
     const int total = P.pass_begin[P.n_jobs];
     const int nt = P.nt, S = P.S, K = P.K, G = P.G, np = 1 + P.pair;
     const int KP = nt * SEG;  // every column a segment can own (>= K), a multiple of 32
-    // shared memory: barriers | weight stages | red x2 | x | norm weight or up | digit
-    // planes (word-major: word w of segment g at w*nt + g) | 8-column chunk sums
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
-    uint64_t *xbar = bars + kMaxStages;      // activation copy
-    uint64_t *wbar = bars + kMaxStages + 1;  // norm-weight copy
-    uint8_t *stage_base = smem + 128;
+    const int ncw = (int)(blockDim.x >> 5) - 1;  // consumer warps (warp 0 is the producer)
+    // shared memory: barriers | weight stages | red x2 | x | norm weight or up |
+    // digit planes [nt][DS] | 8-column chunk sums
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);  // [kMaxStages] weights landed
+    uint64_t *empty = full + kMaxStages;                   // [kMaxStages] stage consumed
+    uint64_t *xbar = full + 2 * kMaxStages;                // activation copy
+    uint64_t *wbar = xbar + 1;                             // norm-weight copy
+    uint8_t *stage_base = smem + kBarBytes;
     float *red = reinterpret_cast<float *>(stage_base + (size_t)P.stages * P.stage_bytes);
     const size_t red_n = (size_t)np * P.R * nt;  // one buffer
     float *xsm = red + ((2 * red_n + 3) & ~(size_t)3);
     float *wsm = xsm + KP;
     uint32_t *dig = reinterpret_cast<uint32_t *>(wsm + (((size_t)K + 3) & ~(size_t)3));
-    float *csum = reinterpret_cast<float *>(dig + (size_t)6 * NW * nt);
+    float *csum = reinterpret_cast<float *>(dig + (size_t)DS * nt);
     __shared__ uint32_t s_head[2 * kMaxStages];
-    __shared__ int s_err;
+    __shared__ int s_err, s_issued;  // s_issued: passes whose copies were issued
     __shared__ double s_rd[32];
     __shared__ float s_am[32];
     __shared__ float s_bv[32];
@@ -200,14 +228,21 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
     const bool norm = P.x.mode == X_RMSNORM, swiglu = P.x.mode == X_SWIGLU;
 
     if (t == 0) {
-        for (int s = 0; s < P.stages; ++s) mbar_init(&bars[s], 1);
+        for (int s = 0; s < P.stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], ncw);
+        }
         mbar_init(xbar, 1);
         mbar_init(wbar, 1);
         fence_mbar_init();
         s_err = 0;
+        s_issued = 0;
         for (int s = 0; s < P.stages; ++s) {
             const int p = blockIdx.x + s * gridDim.x;
-            if (p < total) issue_pass(P, p, s, bars, stage_base, s_head);
+            if (p < total) {
+                issue_pass(P, p, s, full, stage_base, s_head);
+                s_issued = s + 1;
+            }
         }
         if (bulk_x && norm) {  // constant weights: before the dependency wait
             mbar_arrive_expect_tx(wbar, (uint32_t)K * 4u);
@@ -271,9 +306,9 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
         if (norm) ss = warp_sum_d(ss);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-        if ((t & 31) == 0) {
-            s_rd[t >> 5] = ss;
-            s_am[t >> 5] = am;
+        if (lane == 0) {
+            s_rd[warp] = ss;
+            s_am[warp] = am;
         }
     }
     __syncthreads();
@@ -294,10 +329,13 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
     // the dp4a digit planes of the vector with ONE scale for all of it:
     //   x ~ (d0 + d1/254 + d2/254^2) * s0,  s0 = max|x| / 127  (error <= 3.1e-8 max|x|);
     // word order per chunk (lo, hi) x (d0, d1, d2), lo = even columns, hi = odd ones,
-    // matching the nibble order of a weight word
+    // matching the nibble order of a weight word.  Rounding to the nearest integer
+    // uses the 1.5*2^23 trick (one FFMA; the digit's byte is the low byte of the
+    // sum's bits), so no float/int conversions; |digit| <= 127 by construction.
     const float dsc0 = amax > 0.0f ? amax / 127.0f : 1.0f;
     const float dsc1 = dsc0 / 254.0f, dsc2 = dsc1 / 254.0f;
     {
+        constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
         const float i0 = 1.0f / dsc0, i1 = 1.0f / dsc1, i2 = 1.0f / dsc2;
         for (int c = t; c < KP / 8; c += blockDim.x) {
             float4 a = *reinterpret_cast<const float4 *>(xsm + 8 * c);
@@ -315,165 +353,216 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
                 uint32_t wd[6] = {0u, 0u, 0u, 0u, 0u, 0u};
 #pragma unroll
                 for (int k = 0; k < 8; ++k) {
-                    const int q0 = max(-127, min(127, __float2int_rn(v[k] * i0)));
-                    const float r1 = fmaf(-(float)q0, dsc0, v[k]);
-                    const int q1 = max(-127, min(127, __float2int_rn(r1 * i1)));
-                    const float r2 = fmaf(-(float)q1, dsc1, r1);
-                    const int q2 = max(-127, min(127, __float2int_rn(r2 * i2)));
+                    const float t0 = fmaf(v[k], i0, kRound);
+                    const float r1 = fmaf(-(t0 - kRound), dsc0, v[k]);
+                    const float t1 = fmaf(r1, i1, kRound);
+                    const float r2 = fmaf(-(t1 - kRound), dsc1, r1);
+                    const float t2 = fmaf(r2, i2, kRound);
                     const int sh = 8 * (k >> 1);
-                    wd[(k & 1) + 0] |= ((uint32_t)q0 & 0xFFu) << sh;
-                    wd[(k & 1) + 2] |= ((uint32_t)q1 & 0xFFu) << sh;
-                    wd[(k & 1) + 4] |= ((uint32_t)q2 & 0xFFu) << sh;
+                    wd[(k & 1) + 0] |= (__float_as_uint(t0) & 0xFFu) << sh;
+                    wd[(k & 1) + 2] |= (__float_as_uint(t1) & 0xFFu) << sh;
+                    wd[(k & 1) + 4] |= (__float_as_uint(t2) & 0xFFu) << sh;
                 }
                 const int sgi = c / NW, ci = c - sgi * NW;
-#pragma unroll
-                for (int k = 0; k < 6; ++k) dig[(size_t)(6 * ci + k) * nt + sgi] = wd[k];
+                uint2 *dst = reinterpret_cast<uint2 *>(dig + (size_t)sgi * DS + 6 * ci);
+                dst[0] = make_uint2(wd[0], wd[1]);
+                dst[1] = make_uint2(wd[2], wd[3]);
+                dst[2] = make_uint2(wd[4], wd[5]);
             }
         }
     }
     __syncthreads();
 
-    const int slot = t / nt;
-    const int sg = t - slot * nt;
-    const bool active = slot < S;
-    const int GB = 4 + G / 2;
-    const size_t RB = (size_t)((K + G - 1) / G) * GB;
-    const int spg = G / SEG;
-    const int g = sg / spg;
-    const int col0 = sg * SEG;
-    const uint32_t hdr_off = (uint32_t)g * GB;
-    const uint32_t seg_off = hdr_off + 4u + (uint32_t)(sg - g * spg) * (SEG / 2);
-    float X = 0.0f;  // segment sum (zero-point term)
-    float xs[MATH == MATH_F32 ? SEG : 1];
-    uint32_t xd[MATH == MATH_DP4A ? 6 * NW : 1];
-    if (active) {
-#pragma unroll
-        for (int ci = 0; ci < NW; ++ci) X += csum[sg * NW + ci];
-        if constexpr (MATH == MATH_F32) {
-#pragma unroll
-            for (int i = 0; i < NW; ++i)
-#pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    const int pos = k < 5 ? k : k - 3;
-                    xs[8 * i + k] = xsm[col0 + 8 * i + k] * __uint_as_float((uint32_t)(127 - 4 * pos) << 23);
-                }
-        } else {
-#pragma unroll
-            for (int w = 0; w < 6 * NW; ++w) xd[w] = dig[(size_t)w * nt + sg];
-        }
-    }
-
-    const int lane = t & 31, warp = t >> 5, nwarps = blockDim.x >> 5;
     float bv = -INFINITY;
     int bi = INT_MAX;
-    int i_pass = 0;
-    for (;; ++i_pass) {
-        const int p = blockIdx.x + i_pass * gridDim.x;
-        if (p >= total) break;
-        const int s = i_pass % P.stages;
-        const uint32_t parity = (uint32_t)(i_pass / P.stages) & 1u;
-        int j = 0;
-        while (j + 1 < P.n_jobs && p >= P.pass_begin[j + 1]) ++j;
-        const I4Job &job = P.job[j];
-        const int row0 = (p - P.pass_begin[j]) * P.R;
-        float *rb = red + (size_t)(i_pass & 1) * red_n;  // double-buffered partials
-        // bias / residual of this pass fetched before the weight wait: lane k of warp w
-        // holds row w + k*nwarps, the row that warp reduces in its k-th epilogue turn
-        float pre_b = 0.0f, pre_r = 0.0f;
-        if (!P.pair) {
-            const int rl = warp + lane * nwarps, row = row0 + rl;
-            if (rl < P.R && row < job.rows) {
-                if (job.bias) pre_b = job.bias[row];
-                if (job.resid) pre_r = job.resid[row];
+    bool c_err = false;  // consumer-side error (uniform across consumers)
+    if (warp == 0) {
+        // ---- producer: refill stage s with pass i once every consumer warp is done
+        // with pass i - stages there
+        if (lane == 0) {
+            for (int i = P.stages;; ++i) {
+                const int p = blockIdx.x + i * gridDim.x;
+                if (p >= total) break;
+                const int s = i % P.stages;
+                if (!mbar_wait(&empty[s], (uint32_t)(i / P.stages - 1) & 1u, kWaitCycles)) {
+                    s_err = 1;
+                    break;
+                }
+                issue_pass(P, p, s, full, stage_base, s_head);
+                s_issued = i + 1;
             }
         }
-        if (!mbar_wait(&bars[s], parity, kWaitCycles)) s_err = 1;
-        const size_t half_bytes = P.stage_bytes / 2;
+    } else {
+        // ---- consumers: thread (slot, seg) over the rows of every pass
+        const int tc = t - 32, cw = warp - 1;
+        const int slot = tc / nt;
+        const int sg = tc - slot * nt;
+        const bool active = slot < S;
+        const int GB = 4 + G / 2;
+        const size_t RB = (size_t)((K + G - 1) / G) * GB;
+        const int spg = G / SEG;
+        const int g = sg / spg;
+        const int col0 = sg * SEG;
+        const uint32_t hdr_off = (uint32_t)g * GB;
+        const uint32_t seg_off = hdr_off + 4u + (uint32_t)(sg - g * spg) * (SEG / 2);
+        const int ncons = ncw * 32;
+        float X = 0.0f;  // segment sum (zero-point term)
+        float xs[MATH == MATH_F32 ? SEG : 1];
+        uint32_t xd[MATH == MATH_DP4A ? 6 * NW : 1];
         if (active) {
-            for (int r = 0; r < P.RP * np; ++r) {
-                const int jb = r >= P.RP;  // paired mode: second half = job 1
-                const int rl = slot + (r - jb * P.RP) * S;
-                if (rl >= P.R) continue;
-                const uint8_t *sb = stage_base + (size_t)s * P.stage_bytes +
-                                    (jb ? half_bytes + s_head[kMaxStages + s] : s_head[s]);
-                float part = 0.0f;
-                if (row0 + rl < job.rows) {
-                    const uint8_t *rp = sb + (size_t)rl * RB;
-                    const uint32_t hv = lds_u32(rp + hdr_off);
-                    const float sc = h2f((uint16_t)(hv & 0xFFFFu));
-                    const float zr = h2f((uint16_t)(hv >> 16));
-                    if constexpr (MATH == MATH_F32) {
-                        float a0 = 0.0f, a1 = 0.0f;
 #pragma unroll
-                        for (int i = 0; i < NW; ++i) dot8(lds_u32(rp + seg_off + 4 * i), xs + 8 * i, a0, a1);
-                        part = sc * fmaf(-zr, X, a0 + a1);
-                    } else {
-                        int D0 = 0, D1 = 0, D2 = 0;
+            for (int ci = 0; ci < NW; ++ci) X += csum[sg * NW + ci];
+            if constexpr (MATH == MATH_F32) {
 #pragma unroll
-                        for (int i = 0; i < NW; ++i) {
-                            const uint32_t wd = lds_u32(rp + seg_off + 4 * i);
-                            const uint32_t lo = wd & 0x0F0F0F0Fu, hi = (wd >> 4) & 0x0F0F0F0Fu;
-                            D0 = dp4a_us(lo, xd[6 * i + 0], D0);
-                            D0 = dp4a_us(hi, xd[6 * i + 1], D0);
-                            D1 = dp4a_us(lo, xd[6 * i + 2], D1);
-                            D1 = dp4a_us(hi, xd[6 * i + 3], D1);
-                            D2 = dp4a_us(lo, xd[6 * i + 4], D2);
-                            D2 = dp4a_us(hi, xd[6 * i + 5], D2);
+                for (int i = 0; i < NW; ++i)
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const int pos = k < 5 ? k : k - 3;
+                        xs[8 * i + k] = xsm[col0 + 8 * i + k] * __uint_as_float((uint32_t)(127 - 4 * pos) << 23);
+                    }
+            } else {
+                const uint4 *src = reinterpret_cast<const uint4 *>(dig + (size_t)sg * DS);
+#pragma unroll
+                for (int w = 0; w < 6 * NW / 4; ++w) {
+                    const uint4 v4 = src[w];
+                    xd[4 * w + 0] = v4.x, xd[4 * w + 1] = v4.y, xd[4 * w + 2] = v4.z, xd[4 * w + 3] = v4.w;
+                }
+            }
+        }
+        for (int i_pass = 0;; ++i_pass) {
+            const int p = blockIdx.x + i_pass * gridDim.x;
+            if (p >= total) break;
+            const int s = i_pass % P.stages;
+            const uint32_t parity = (uint32_t)(i_pass / P.stages) & 1u;
+            int j = 0;
+            while (j + 1 < P.n_jobs && p >= P.pass_begin[j + 1]) ++j;
+            const I4Job &job = P.job[j];
+            const int row0 = (p - P.pass_begin[j]) * P.R;
+            float *rb = red + (size_t)(i_pass & 1) * red_n;  // double-buffered partials
+            // bias / residual of this pass fetched before the weight wait: lane k of
+            // consumer warp cw holds row cw + k*ncw, its k-th epilogue row
+            float pre_b = 0.0f, pre_r = 0.0f;
+            if (!P.pair) {
+                const int rl = cw + lane * ncw, row = row0 + rl;
+                if (rl < P.R && row < job.rows) {
+                    if (job.bias) pre_b = job.bias[row];
+                    if (job.resid) pre_r = job.resid[row];
+                }
+            }
+            const bool ok = mbar_wait(&full[s], parity, kWaitCycles);
+            const size_t half_bytes = P.stage_bytes / 2;
+            if (active && ok) {
+                for (int r = 0; r < P.RP * np; ++r) {
+                    const int jb = r >= P.RP;  // paired mode: second half = job 1
+                    const int rl = slot + (r - jb * P.RP) * S;
+                    if (rl >= P.R) continue;
+                    const uint8_t *sb = stage_base + (size_t)s * P.stage_bytes +
+                                        (jb ? half_bytes + s_head[kMaxStages + s] : s_head[s]);
+                    float part = 0.0f;
+                    if (row0 + rl < job.rows) {
+                        const uint8_t *rp = sb + (size_t)rl * RB;
+                        const uint32_t hv = lds_u32(rp + hdr_off);
+                        const float sc = h2f((uint16_t)(hv & 0xFFFFu));
+                        const float zr = h2f((uint16_t)(hv >> 16));
+                        if constexpr (MATH == MATH_F32) {
+                            float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll
+                            for (int i = 0; i < NW; ++i) dot8(lds_u32(rp + seg_off + 4 * i), xs + 8 * i, a0, a1);
+                            part = sc * fmaf(-zr, X, a0 + a1);
+                        } else {
+                            int D0 = 0, D1 = 0, D2 = 0;
+#pragma unroll
+                            for (int i = 0; i < NW; ++i) {
+                                const uint32_t wd = lds_u32(rp + seg_off + 4 * i);
+                                const uint32_t lo = wd & 0x0F0F0F0Fu, hi = (wd >> 4) & 0x0F0F0F0Fu;
+                                D0 = dp4a_us(lo, xd[6 * i + 0], D0);
+                                D0 = dp4a_us(hi, xd[6 * i + 1], D0);
+                                D1 = dp4a_us(lo, xd[6 * i + 2], D1);
+                                D1 = dp4a_us(hi, xd[6 * i + 3], D1);
+                                D2 = dp4a_us(lo, xd[6 * i + 4], D2);
+                                D2 = dp4a_us(hi, xd[6 * i + 5], D2);
+                            }
+                            const float dot = fmaf((float)D0, dsc0, fmaf((float)D1, dsc1, (float)D2 * dsc2));
+                            part = sc * fmaf(-zr, X, dot);
                         }
-                        const float dot = fmaf((float)D0, dsc0, fmaf((float)D1, dsc1, (float)D2 * dsc2));
-                        part = sc * fmaf(-zr, X, dot);
+                    }
+                    rb[(jb * P.R + rl) * nt + sg] = part;
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with stage s
+            // partials of this pass complete; an error anywhere stops every consumer
+            if (consumer_sync_or(ncons, !ok)) {
+                c_err = true;
+                break;
+            }
+            // rows of this pass: two at a time (independent reduction chains), segment
+            // partials summed in double and rounded once, as the reference's double row
+            // dot is
+            for (int ra = cw, turn = 0; ra < P.R; ra += 2 * ncw, turn += 2) {
+                const int rbw = ra + ncw;
+                const bool has_b = rbw < P.R;
+                double va = 0.0, vb = 0.0, ua = 0.0, ub = 0.0;
+                for (int i = lane; i < nt; i += 32) {
+                    va += (double)rb[ra * nt + i];
+                    if (has_b) vb += (double)rb[rbw * nt + i];
+                    if (P.pair) {
+                        ua += (double)rb[(P.R + ra) * nt + i];
+                        if (has_b) ub += (double)rb[(P.R + rbw) * nt + i];
                     }
                 }
-                rb[(jb * P.R + rl) * nt + sg] = part;
-            }
-        }
-        __syncthreads();  // stage s consumed, partials of this pass complete
-        if (s_err) break;
-        if (t == 0) {  // refill stage s while the rows of this pass are reduced
-            const int pn = blockIdx.x + (i_pass + P.stages) * gridDim.x;
-            if (pn < total) issue_pass(P, pn, s, bars, stage_base, s_head);
-        }
-        for (int rl = warp, turn = 0; rl < P.R; rl += nwarps, ++turn) {
-            const int row = row0 + rl;
-            if (row >= job.rows) continue;
-            float b_ = __shfl_sync(0xffffffffu, pre_b, turn & 31);
-            float r_ = __shfl_sync(0xffffffffu, pre_r, turn & 31);
-            if (turn >= 32 && !P.pair) {  // more turns than lanes: plain loads
-                b_ = job.bias ? job.bias[row] : 0.0f;
-                r_ = job.resid ? job.resid[row] : 0.0f;
-            }
-            // segment partials summed in double, rounded once (the reference's row dot
-            // is a double sum rounded to float)
-            double vd = 0.0;
-            for (int i = lane; i < nt; i += 32) vd += (double)rb[rl * nt + i];
-            float v = (float)warp_sum_d(vd);
-            float u = 0.0f;
-            if (P.pair) {
-                double ud = 0.0;
-                for (int i = lane; i < nt; i += 32) ud += (double)rb[(P.R + rl) * nt + i];
-                u = (float)warp_sum_d(ud);
-            }
-            if (lane == 0) {
-                if (P.pair) {
-                    // swiglu_ref (kernels/silu/swiglu_ref.cpp:41-52) on (gate, up)
-                    v = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), u);
-                } else {
-                    if (job.bias) v += b_;
-                    if (job.resid) v = r_ + v;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    va += __shfl_xor_sync(0xffffffffu, va, o);
+                    vb += __shfl_xor_sync(0xffffffffu, vb, o);
+                    if (P.pair) {
+                        ua += __shfl_xor_sync(0xffffffffu, ua, o);
+                        ub += __shfl_xor_sync(0xffffffffu, ub, o);
+                    }
                 }
-                job.y[row] = v;
-                if (P.am.token && j == 0) better(bv, bi, v, row + P.am.row_offset);
+                float pb[2], pr[2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int tt = turn + h;
+                    pb[h] = __shfl_sync(0xffffffffu, pre_b, tt & 31);
+                    pr[h] = __shfl_sync(0xffffffffu, pre_r, tt & 31);
+                }
+                if (lane == 0) {
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int rl = h ? rbw : ra;
+                        const int row = row0 + rl;
+                        if ((h && !has_b) || row >= job.rows) continue;
+                        float v = (float)(h ? vb : va);
+                        if (P.pair) {
+                            // swiglu_ref (kernels/silu/swiglu_ref.cpp:41-52) on (gate, up)
+                            const float u = (float)(h ? ub : ua);
+                            v = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), u);
+                        } else {
+                            float b_ = pb[h], r_ = pr[h];
+                            if (turn + h >= 32) {  // more turns than lanes: plain loads
+                                b_ = job.bias ? job.bias[row] : 0.0f;
+                                r_ = job.resid ? job.resid[row] : 0.0f;
+                            }
+                            if (job.bias) v += b_;
+                            if (job.resid) v = r_ + v;
+                        }
+                        job.y[row] = v;
+                        if (P.am.token && j == 0) better(bv, bi, v, row + P.am.row_offset);
+                    }
+                }
             }
         }
     }
+    if (c_err && t == 32) s_err = 1;
+    __syncthreads();  // producer and consumers done
     if (s_err) {
-        // drain every copy this CTA still has in flight before the CTA exits
+        // drain the copies this CTA may still have in flight (the most recent pass of
+        // every stage), report, exit
         if (t == 0) {
-            for (int k = 0; k < P.stages; ++k) {
-                const int ii = i_pass + k;
-                if (blockIdx.x + ii * gridDim.x >= total) break;
-                mbar_wait(&bars[ii % P.stages], (uint32_t)(ii / P.stages) & 1u, kWaitCycles);
-            }
+            const int issued = s_issued;
+            for (int i = max(0, issued - P.stages); i < issued; ++i)
+                mbar_wait(&full[i % P.stages], (uint32_t)(i / P.stages) & 1u, kWaitCycles);
             if (bulk_x) {
                 mbar_wait(xbar, 0, kWaitCycles);
                 if (norm) mbar_wait(wbar, 0, kWaitCycles);
@@ -700,8 +789,12 @@ Shape plan(int K, int G, bool pair, int rows_total) {
     }
     const size_t RB = (size_t)ng * (4 + G / 2);
     const int np = pair ? 2 : 1;
-    L.S = std::max(1, 512 / L.nt);
-    L.block = ((L.nt * L.S + 31) / 32) * 32;
+    if (L.nt > 480) {  // warp 0 is the producer: at most 480 segment threads
+        L.seg = 0;
+        return L;
+    }
+    L.S = std::max(1, 480 / L.nt);
+    L.block = 32 + ((L.nt * L.S + 31) / 32) * 32;
     const int per_cta = std::max(1, (rows_total + num_sms() - 1) / num_sms());
     if ((size_t)per_cta * RB * np <= 64 * 1024) {
         L.R = per_cta;
@@ -715,10 +808,10 @@ Shape plan(int K, int G, bool pair, int rows_total) {
     const size_t kp = (size_t)L.nt * L.seg;
     const size_t red = ((2 * (size_t)np * L.R * L.nt + 3) & ~(size_t)3);
     const size_t wsm = ((size_t)K + 3) & ~(size_t)3;
-    const size_t dig = (size_t)L.nt * 6 * (L.seg / 8);
+    const size_t dig = (size_t)L.nt * (6 * (L.seg / 8) + 4) + 4;
     const size_t floats = red + kp + wsm + dig + kp / 8;
     for (;;) {
-        L.smem = 128 + (size_t)L.stages * L.stage_bytes + floats * 4;
+        L.smem = kBarBytes + (size_t)L.stages * L.stage_bytes + floats * 4;
         if (L.smem <= 220 * 1024 || L.stages <= 2) break;
         --L.stages;
     }
