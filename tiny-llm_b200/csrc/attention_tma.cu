@@ -464,10 +464,17 @@ int launch_t(const AttnArgs &a, cudaStream_t st) {
     constexpr int RB = HD * (int)sizeof(KV);
     constexpr int TS = kThreads / (HD / 4);
     auto k = attn_tma_kernel<KV, HD, G>;
-    static std::atomic<unsigned long long> attr{0};
-    if (first_on_device(attr)) {
-        TQ_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, max_dyn_smem()));
-        TQ_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    static std::atomic<unsigned long long> attr{0}, cluster_attr{0};
+    int smem_max = 0;
+    TQ_CUDA_TRY(smem_limit_once(k, attr, &smem_max));
+    {
+        int dev = 0;
+        TQ_CUDA_TRY(cudaGetDevice(&dev));
+        const unsigned long long bit = 1ull << (dev & 63);
+        if (!(cluster_attr.load() & bit)) {
+            TQ_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+            cluster_attr.fetch_or(bit);
+        }
     }
     auto a16 = [](const void *p) { return ((uintptr_t)p & 15u) == 0; };
     // splits = cluster size: about one CTA per SM over all KV heads, at most 16, at
@@ -502,9 +509,10 @@ int launch_t(const AttnArgs &a, cudaStream_t st) {
                                               (!a.q_norm || (a16(a.q_norm) && a16(a.k_norm)))));
         P.out = a.out;
         P.status = a.status;
+        // barriers | ring | new k, v rows (cache type) | krow, vrow, qs, cs+sn, qn, kn | sc
         const size_t smem = 128 + (size_t)P.stage_region + ((2 * (size_t)RB + 15) & ~(size_t)15) +
-                            ((size_t)4 * HD + (size_t)G * HD) * 4 + (size_t)P.chunk_max * G * 4;
-        if (smem > (size_t)max_dyn_smem()) continue;
+                            ((size_t)5 * HD + (size_t)G * HD) * 4 + (size_t)P.chunk_max * G * 4;
+        if (smem > (size_t)smem_max) continue;
         cudaLaunchConfig_t cfg{};
         cfg.gridDim = dim3(a.n_kv_heads, ns);
         cfg.blockDim = dim3(kThreads);

@@ -42,13 +42,24 @@ inline int max_dyn_smem() {
     return v;
 }
 
-// True the first time it is called on the current device for this mask (kernel
-// attributes such as the dynamic shared-memory limit are per device).
-inline bool first_on_device(std::atomic<unsigned long long> &mask) {
+// Raises kernel k's dynamic shared-memory limit to the most it can use on the current
+// device (the opt-in limit minus its static shared memory), once per device; `mask`
+// records the devices done.  *limit receives that most.
+template <typename Kern>
+inline cudaError_t smem_limit_once(Kern k, std::atomic<unsigned long long> &mask, int *limit) {
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return true;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    cudaFuncAttributes fa;
+    e = cudaFuncGetAttributes(&fa, k);
+    if (e != cudaSuccess) return e;
+    const int lim = max_dyn_smem() - (int)fa.sharedSizeBytes;
+    *limit = lim;
     const unsigned long long bit = 1ull << (dev & 63);
-    return (mask.fetch_or(bit) & bit) == 0;
+    if (mask.load() & bit) return cudaSuccess;
+    e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    if (e == cudaSuccess) mask.fetch_or(bit);
+    return e;
 }
 
 // ---------------------------------------------------------------- fp16

@@ -834,8 +834,10 @@ template <int SEG, int MATH>
 int launch_tma(const MvParams &P, const Shape &L, int passes, bool pdl, cudaStream_t st) {
     auto k = i4_mv_tma_kernel<SEG, MATH>;
     static std::atomic<unsigned long long> attr_set{0};
-    if (first_on_device(attr_set))
-        TQ_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
+    int smem_max = 0;
+    TQ_CUDA_TRY(smem_limit_once(k, attr_set, &smem_max));
+    TQ_CHECK_ARG(L.smem <= (size_t)smem_max, "i4 matvec: %zu B of shared memory above the %d B limit",
+                 L.smem, smem_max);
     // persistent: at most one CTA per SM, so the x prologue is paid once per SM
     const int grid = std::min(grid_for(k, L.block, L.smem, passes), num_sms());
     cudaLaunchConfig_t cfg = {};

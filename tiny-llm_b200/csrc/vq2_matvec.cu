@@ -359,11 +359,10 @@ int launch_vq2_matvec(const VqLaunch &a, cudaStream_t st) {
     const size_t K4 = ((size_t)a.K * 4 + 15) & ~(size_t)15;
     const size_t smem = 128 + (size_t)nm * (kCbDecoded + P.region) + 2 * K4 + (size_t)nm * 3 * K4 +
                         (size_t)nm * P.S * P.nt * 4;
-    TQ_CHECK_ARG(smem <= 200 * 1024, "vq2: in_dim %d needs too much shared memory", a.K);
     static std::atomic<unsigned long long> attr{0};
-    if (first_on_device(attr))
-        TQ_CUDA_TRY(cudaFuncSetAttribute(vq2_matvec_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    int smem_max = 0;
+    TQ_CUDA_TRY(smem_limit_once(vq2_matvec_kernel, attr, &smem_max));
+    TQ_CHECK_ARG(smem <= (size_t)smem_max, "vq2: in_dim %d needs too much shared memory", a.K);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(ctas);
     cfg.blockDim = dim3(block);
@@ -381,11 +380,10 @@ int launch_vq2_matvec(const VqLaunch &a, cudaStream_t st) {
 int launch_biip(const float *x, float *y, int dim, const float *scale, const float *sign, int bs,
                 cudaStream_t st) {
     TQ_CHECK_ARG(dim > 0 && sign && bs >= 1 && (bs & (bs - 1)) == 0, "biip: bad arguments");
-    TQ_CHECK_ARG((size_t)dim * 4 <= 160 * 1024, "biip: dim %d too large", dim);
     static std::atomic<unsigned long long> attr{0};
-    if (first_on_device(attr))
-        TQ_CUDA_TRY(cudaFuncSetAttribute(biip_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         160 * 1024));
+    int smem_max = 0;
+    TQ_CUDA_TRY(smem_limit_once(biip_kernel, attr, &smem_max));
+    TQ_CHECK_ARG((size_t)dim * 4 <= (size_t)smem_max, "biip: dim %d too large", dim);
     biip_kernel<<<1, 512, (size_t)dim * 4, st>>>(x, y, dim, sign, scale, bs);
     TQ_CUDA_TRY(cudaGetLastError());
     return TQB200_OK;
