@@ -804,18 +804,21 @@ Shape plan(int K, int G, bool pair, int rows_total) {
     L.RP = (L.R + L.S - 1) / L.S;
     const size_t region = ((size_t)L.R * RB + 32 + 127) / 128 * 128;
     L.stage_bytes = (uint32_t)(np * region);
-    L.stages = (int)std::max<size_t>(2, std::min<size_t>(kMaxStages, (96 * 1024) / L.stage_bytes));
     const size_t kp = (size_t)L.nt * L.seg;
     const size_t red = ((2 * (size_t)np * L.R * L.nt + 3) & ~(size_t)3);
     const size_t wsm = ((size_t)K + 3) & ~(size_t)3;
     const size_t dig = (size_t)L.nt * (6 * (L.seg / 8) + 4) + 4;
     const size_t floats = red + kp + wsm + dig + kp / 8;
-    for (;;) {
-        L.smem = kBarBytes + (size_t)L.stages * L.stage_bytes + floats * 4;
-        if (L.smem <= 220 * 1024 || L.stages <= 2) break;
-        --L.stages;
-    }
-    if (L.smem > 220 * 1024) L.seg = 0;  // no TMA shape: the generic kernel
+    // the block holds the whole register file (512 threads), so nothing else shares
+    // the SM: every stage the shared memory can hold is in flight at once
+    const size_t cap = 200 * 1024, fixed = kBarBytes + floats * 4;
+    const size_t ring = cap > fixed ? cap - fixed : 0;
+    L.stages = (int)std::min<size_t>(kMaxStages, ring / L.stage_bytes);
+    const int passes_per_cta =
+        (int)(((size_t)(rows_total + L.R - 1) / L.R + num_sms() - 1) / num_sms());
+    L.stages = std::max(1, std::min(L.stages, passes_per_cta));
+    L.smem = fixed + (size_t)L.stages * L.stage_bytes;
+    if (L.stages < 1 || L.smem > cap) L.seg = 0;  // no TMA shape: the generic kernel
     return L;
 }
 
