@@ -208,7 +208,7 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
     float *po = red + TS * G * HD;                              // [G][HD] partial o
     float *pm = po + G * HD;                                    // [G] partial m
     float *pl = pm + G;                                         // [G] partial l
-    float *wgt = pl + G;                                        // [ns][G] merge weights
+    float *wgt = pl + G;                                        // [ns][G] merge weights (+ m, l copies)
     __shared__ float s_m[G], s_l[G];
     __shared__ int s_err;
 
@@ -433,17 +433,27 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
         pl[tid] = err ? 0.0f : s_l[tid];
     }
     cluster.sync();  // every rank's partial is visible cluster-wide
-    // ---- merge over DSMEM: weights exp(m_s - M) per (split, head), then this rank's
-    // slice of the output elements; empty splits (m_s = -inf, o = 0) weigh 0
+    // ---- merge over DSMEM.  One parallel pass copies every rank's (m, l) here; the
+    // weights exp(m_s - M) per (split, head) come from that local copy; then each
+    // thread of this rank's output slice reads its ns partials with independent
+    // remote loads.  Empty splits (m_s = -inf, o = 0) weigh 0.
+    float *rm = wgt + kMaxSplit * G;  // [ns][G] remote m
+    float *rl = rm + kMaxSplit * G;   // [ns][G] remote l
+    if (tid < ns * G) {
+        const int s = tid / G, g = tid - s * G;
+        rm[tid] = *cluster.map_shared_rank(pm + g, s);
+        rl[tid] = *cluster.map_shared_rank(pl + g, s);
+    }
+    __syncthreads();
     if (tid < G) {
         float M = -INFINITY;
-        for (int s = 0; s < ns; ++s) M = fmaxf(M, *cluster.map_shared_rank(pm + tid, s));
+        for (int s = 0; s < ns; ++s) M = fmaxf(M, rm[s * G + tid]);
         float L = 0.0f;
         for (int s = 0; s < ns; ++s) {
-            const float ms = *cluster.map_shared_rank(pm + tid, s);
+            const float ms = rm[s * G + tid];
             const float w = ms == -INFINITY ? 0.0f : expf(ms - M);
             wgt[s * G + tid] = w;
-            L = fmaf(*cluster.map_shared_rank(pl + tid, s), w, L);
+            L = fmaf(rl[s * G + tid], w, L);
         }
         s_l[tid] = L;
     }
@@ -451,9 +461,13 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
     const int per = (G * HD + ns - 1) / ns;
     for (int i = split * per + tid; i < min(G * HD, (split + 1) * per); i += kThreads) {
         const int g = i / HD;
+        float o[kMaxSplit];
+#pragma unroll
+        for (int s = 0; s < kMaxSplit; ++s) o[s] = s < ns ? *cluster.map_shared_rank(po + i, s) : 0.0f;
         float O = 0.0f;
-#pragma unroll 4
-        for (int s = 0; s < ns; ++s) O = fmaf(*cluster.map_shared_rank(po + i, s), wgt[s * G + g], O);
+#pragma unroll
+        for (int s = 0; s < kMaxSplit; ++s)
+            if (s < ns) O = fmaf(o[s], wgt[s * G + g], O);
         P.out[(size_t)kh * G * HD + i] = O / s_l[g];
     }
     cluster.sync();  // no rank leaves while another still reads its partial
@@ -502,7 +516,7 @@ int launch_t(const AttnArgs &a, cudaStream_t st) {
         P.tile_rows = std::max(1, std::min(kTileBytes / RB, P.chunk_max));
         P.stages = std::max(1, std::min(kStages, 2 * ((P.chunk_max + P.tile_rows - 1) / P.tile_rows)));
         const size_t ring = (size_t)P.stages * P.tile_rows * RB;
-        const size_t part = ((size_t)TS * G * HD + (size_t)G * HD + 2 * G + (size_t)kMaxSplit * G) * 4;
+        const size_t part = ((size_t)TS * G * HD + (size_t)G * HD + 2 * G + 3 * (size_t)kMaxSplit * G) * 4;
         P.stage_region = (int)((std::max(ring, part) + 15) & ~(size_t)15);
         P.bulk_in = a16(a.q) && (!a.k_new || (a16(a.k_new) && a16(a.v_new) && a16(a.cos_tab) &&
                                               a16(a.sin_tab) &&

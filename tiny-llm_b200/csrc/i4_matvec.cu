@@ -188,6 +188,20 @@ __device__ __forceinline__ bool consumer_sync_or(int nthreads, bool pred) {
     return r != 0;
 }
 
+// Sum of n segment partials in double (four interleaved accumulators), rounded once.
+__device__ __forceinline__ float row_sum_d(const float *p, int n) {
+    double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+    int i = 0;
+    for (; i + 4 <= n; i += 4) {
+        a0 += (double)p[i];
+        a1 += (double)p[i + 1];
+        a2 += (double)p[i + 2];
+        a3 += (double)p[i + 3];
+    }
+    for (; i < n; ++i) a0 += (double)p[i];
+    return (float)((a0 + a1) + (a2 + a3));
+}
+
 // dp4a digit planes of one segment: 6 words per 8 columns, then 4 words of padding
 // (a row stride of 6*NW+4 words keeps the 16-byte loads of 8 consecutive segments on
 // distinct bank groups)
@@ -212,7 +226,8 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
     uint64_t *wbar = xbar + 1;                             // norm-weight copy
     uint8_t *stage_base = smem + kBarBytes;
     float *red = reinterpret_cast<float *>(stage_base + (size_t)P.stages * P.stage_bytes);
-    const size_t red_n = (size_t)np * P.R * nt;  // one buffer
+    const int ntp = nt + 1;  // partial-row stride (odd: conflict-free per-lane row sums)
+    const size_t red_n = (size_t)np * P.R * ntp;  // one buffer
     float *xsm = red + ((2 * red_n + 3) & ~(size_t)3);
     float *wsm = xsm + KP;
     uint32_t *dig = reinterpret_cast<uint32_t *>(wsm + (((size_t)K + 3) & ~(size_t)3));
@@ -253,21 +268,37 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
     // weights are in flight; now wait for the producer of x and let our dependents start
     griddep_wait();
     griddep_launch();
-    if (t == 0 && bulk_x) {
-        const uint32_t xb = (uint32_t)K * 4u;
-        mbar_arrive_expect_tx(xbar, swiglu ? 2 * xb : xb);
-        bulk_g2s(xsm, P.x.src, xb, xbar);
-        if (swiglu) bulk_g2s(wsm, P.x.up, xb, xbar);
-    }
 
-    // ---- activation: whole vector in shared memory, zero past K.  One thread waits on
-    // the copies; the others park at the barrier.  Unaligned sources: batched loads.
+    // ---- activation: whole vector in shared memory, zero past K.  The activation is
+    // read with 16-byte loads by every thread (all issued before any is used), not by
+    // a bulk copy: a copy would queue behind this CTA's weight copies in the SM's copy
+    // engine.  The RMSNorm weight, a constant, came by bulk copy before the wait.
+    // Unaligned sources: batched scalar loads.
     for (int i = K + t; i < KP; i += blockDim.x) xsm[i] = 0.0f;
     if (bulk_x) {
-        if (t == 0) {
-            if (!mbar_wait(xbar, 0, kWaitCycles)) s_err = 1;
-            if (norm && !mbar_wait(wbar, 0, kWaitCycles)) s_err = 1;
+        const float4 *xs4 = reinterpret_cast<const float4 *>(P.x.src);
+        const float4 *up4 = reinterpret_cast<const float4 *>(P.x.up);
+        const int K4 = K / 4;
+        for (int i0 = t; i0 < K4; i0 += 4 * blockDim.x) {
+            float4 v[4], u[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int i = i0 + k * blockDim.x;
+                if (i < K4) {
+                    v[k] = xs4[i];
+                    if (swiglu) u[k] = up4[i];
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int i = i0 + k * blockDim.x;
+                if (i < K4) {
+                    reinterpret_cast<float4 *>(xsm)[i] = v[k];
+                    if (swiglu) reinterpret_cast<float4 *>(wsm)[i] = u[k];
+                }
+            }
         }
+        if (t == 0 && norm && !mbar_wait(wbar, 0, kWaitCycles)) s_err = 1;
     } else {
         for (int i0 = t; i0 < K; i0 += 4 * blockDim.x) {  // 4 loads in flight per thread
             float v[4], u[4];
@@ -439,54 +470,65 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
             const I4Job &job = P.job[j];
             const int row0 = (p - P.pass_begin[j]) * P.R;
             float *rb = red + (size_t)(i_pass & 1) * red_n;  // double-buffered partials
-            // bias / residual of this pass fetched before the weight wait: lane k of
-            // consumer warp cw holds row cw + k*ncw, its k-th epilogue row
-            float pre_b = 0.0f, pre_r = 0.0f;
+            // bias / residual of the rows this warp reduces (below), fetched before the
+            // weight wait; chunk c of 32 rows belongs to consumer warp (i_pass + c) % ncw
+            float pre_b[2] = {0.0f, 0.0f}, pre_r[2] = {0.0f, 0.0f};
             if (!P.pair) {
-                const int rl = cw + lane * ncw, row = row0 + rl;
-                if (rl < P.R && row < job.rows) {
-                    if (job.bias) pre_b = job.bias[row];
-                    if (job.resid) pre_r = job.resid[row];
+                for (int c = 0, k = 0; c * 32 < P.R && k < 2; ++c) {
+                    if ((i_pass + c) % ncw != cw) continue;
+                    const int rl = c * 32 + lane, row = row0 + rl;
+                    if (rl < P.R && row < job.rows) {
+                        if (job.bias) pre_b[k] = job.bias[row];
+                        if (job.resid) pre_r[k] = job.resid[row];
+                    }
+                    ++k;
                 }
             }
             const bool ok = mbar_wait(&full[s], parity, kWaitCycles);
             const size_t half_bytes = P.stage_bytes / 2;
-            if (active && ok) {
-                for (int r = 0; r < P.RP * np; ++r) {
-                    const int jb = r >= P.RP;  // paired mode: second half = job 1
-                    const int rl = slot + (r - jb * P.RP) * S;
-                    if (rl >= P.R) continue;
-                    const uint8_t *sb = stage_base + (size_t)s * P.stage_bytes +
-                                        (jb ? half_bytes + s_head[kMaxStages + s] : s_head[s]);
-                    float part = 0.0f;
-                    if (row0 + rl < job.rows) {
-                        const uint8_t *rp = sb + (size_t)rl * RB;
-                        const uint32_t hv = lds_u32(rp + hdr_off);
-                        const float sc = h2f((uint16_t)(hv & 0xFFFFu));
-                        const float zr = h2f((uint16_t)(hv >> 16));
-                        if constexpr (MATH == MATH_F32) {
-                            float a0 = 0.0f, a1 = 0.0f;
+            // one row's segment partial from the stage (0 past the matrix)
+            auto seg_part = [&](int jb, int rl) -> float {
+                const uint8_t *sb = stage_base + (size_t)s * P.stage_bytes +
+                                    (jb ? half_bytes + s_head[kMaxStages + s] : s_head[s]);
+                if (row0 + rl >= job.rows) return 0.0f;
+                const uint8_t *rp = sb + (size_t)rl * RB;
+                const uint32_t hv = lds_u32(rp + hdr_off);
+                const float sc = h2f((uint16_t)(hv & 0xFFFFu));
+                const float zr = h2f((uint16_t)(hv >> 16));
+                if constexpr (MATH == MATH_F32) {
+                    float a0 = 0.0f, a1 = 0.0f;
 #pragma unroll
-                            for (int i = 0; i < NW; ++i) dot8(lds_u32(rp + seg_off + 4 * i), xs + 8 * i, a0, a1);
-                            part = sc * fmaf(-zr, X, a0 + a1);
-                        } else {
-                            int D0 = 0, D1 = 0, D2 = 0;
+                    for (int i = 0; i < NW; ++i) dot8(lds_u32(rp + seg_off + 4 * i), xs + 8 * i, a0, a1);
+                    return sc * fmaf(-zr, X, a0 + a1);
+                } else {
+                    int D0 = 0, D1 = 0, D2 = 0;
 #pragma unroll
-                            for (int i = 0; i < NW; ++i) {
-                                const uint32_t wd = lds_u32(rp + seg_off + 4 * i);
-                                const uint32_t lo = wd & 0x0F0F0F0Fu, hi = (wd >> 4) & 0x0F0F0F0Fu;
-                                D0 = dp4a_us(lo, xd[6 * i + 0], D0);
-                                D0 = dp4a_us(hi, xd[6 * i + 1], D0);
-                                D1 = dp4a_us(lo, xd[6 * i + 2], D1);
-                                D1 = dp4a_us(hi, xd[6 * i + 3], D1);
-                                D2 = dp4a_us(lo, xd[6 * i + 4], D2);
-                                D2 = dp4a_us(hi, xd[6 * i + 5], D2);
-                            }
-                            const float dot = fmaf((float)D0, dsc0, fmaf((float)D1, dsc1, (float)D2 * dsc2));
-                            part = sc * fmaf(-zr, X, dot);
-                        }
+                    for (int i = 0; i < NW; ++i) {
+                        const uint32_t wd = lds_u32(rp + seg_off + 4 * i);
+                        const uint32_t lo = wd & 0x0F0F0F0Fu, hi = (wd >> 4) & 0x0F0F0F0Fu;
+                        D0 = dp4a_us(lo, xd[6 * i + 0], D0);
+                        D0 = dp4a_us(hi, xd[6 * i + 1], D0);
+                        D1 = dp4a_us(lo, xd[6 * i + 2], D1);
+                        D1 = dp4a_us(hi, xd[6 * i + 3], D1);
+                        D2 = dp4a_us(lo, xd[6 * i + 4], D2);
+                        D2 = dp4a_us(hi, xd[6 * i + 5], D2);
                     }
-                    rb[(jb * P.R + rl) * nt + sg] = part;
+                    const float dot = fmaf((float)D0, dsc0, fmaf((float)D1, dsc1, (float)D2 * dsc2));
+                    return sc * fmaf(-zr, X, dot);
+                }
+            };
+            if (active && ok) {
+                // rows slot, slot+S, ... of each job; two at a time for independent chains
+                for (int jb = 0; jb < np; ++jb) {
+                    for (int r = 0; r < P.RP; r += 2) {
+                        const int rl0 = slot + r * S, rl1 = rl0 + S;
+                        const bool h0 = rl0 < P.R, h1 = r + 1 < P.RP && rl1 < P.R;
+                        float p0 = 0.0f, p1 = 0.0f;
+                        if (h0) p0 = seg_part(jb, rl0);
+                        if (h1) p1 = seg_part(jb, rl1);
+                        if (h0) rb[(jb * P.R + rl0) * ntp + sg] = p0;
+                        if (h1) rb[(jb * P.R + rl1) * ntp + sg] = p1;
+                    }
                 }
             }
             __syncwarp();
@@ -496,61 +538,28 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
                 c_err = true;
                 break;
             }
-            // rows of this pass: two at a time (independent reduction chains), segment
-            // partials summed in double and rounded once, as the reference's double row
-            // dot is
-            for (int ra = cw, turn = 0; ra < P.R; ra += 2 * ncw, turn += 2) {
-                const int rbw = ra + ncw;
-                const bool has_b = rbw < P.R;
-                double va = 0.0, vb = 0.0, ua = 0.0, ub = 0.0;
-                for (int i = lane; i < nt; i += 32) {
-                    va += (double)rb[ra * nt + i];
-                    if (has_b) vb += (double)rb[rbw * nt + i];
-                    if (P.pair) {
-                        ua += (double)rb[(P.R + ra) * nt + i];
-                        if (has_b) ub += (double)rb[(P.R + rbw) * nt + i];
-                    }
+            // rows of this pass, 32 per warp (a lane per row): the row's segment partials
+            // summed in order in double and rounded once, as the reference's double row
+            // dot is.  Chunk c of 32 rows goes to consumer warp (i_pass + c) % ncw, so the
+            // reductions of consecutive passes spread over the warps.
+            for (int c = 0, k = 0; c * 32 < P.R; ++c) {
+                if ((i_pass + c) % ncw != cw) continue;
+                const int kk = k++;
+                const int rl = c * 32 + lane, row = row0 + rl;
+                if (rl >= P.R || row >= job.rows) continue;
+                float v = row_sum_d(rb + (size_t)rl * ntp, nt);
+                if (P.pair) {
+                    const float u = row_sum_d(rb + (size_t)(P.R + rl) * ntp, nt);
+                    // swiglu_ref (kernels/silu/swiglu_ref.cpp:41-52) on (gate, up)
+                    v = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), u);
+                } else {
+                    const float b_ = kk < 2 ? pre_b[kk] : (job.bias ? job.bias[row] : 0.0f);
+                    const float r_ = kk < 2 ? pre_r[kk] : (job.resid ? job.resid[row] : 0.0f);
+                    if (job.bias) v += b_;
+                    if (job.resid) v = r_ + v;
                 }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    va += __shfl_xor_sync(0xffffffffu, va, o);
-                    vb += __shfl_xor_sync(0xffffffffu, vb, o);
-                    if (P.pair) {
-                        ua += __shfl_xor_sync(0xffffffffu, ua, o);
-                        ub += __shfl_xor_sync(0xffffffffu, ub, o);
-                    }
-                }
-                float pb[2], pr[2];
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int tt = turn + h;
-                    pb[h] = __shfl_sync(0xffffffffu, pre_b, tt & 31);
-                    pr[h] = __shfl_sync(0xffffffffu, pre_r, tt & 31);
-                }
-                if (lane == 0) {
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int rl = h ? rbw : ra;
-                        const int row = row0 + rl;
-                        if ((h && !has_b) || row >= job.rows) continue;
-                        float v = (float)(h ? vb : va);
-                        if (P.pair) {
-                            // swiglu_ref (kernels/silu/swiglu_ref.cpp:41-52) on (gate, up)
-                            const float u = (float)(h ? ub : ua);
-                            v = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), u);
-                        } else {
-                            float b_ = pb[h], r_ = pr[h];
-                            if (turn + h >= 32) {  // more turns than lanes: plain loads
-                                b_ = job.bias ? job.bias[row] : 0.0f;
-                                r_ = job.resid ? job.resid[row] : 0.0f;
-                            }
-                            if (job.bias) v += b_;
-                            if (job.resid) v = r_ + v;
-                        }
-                        job.y[row] = v;
-                        if (P.am.token && j == 0) better(bv, bi, v, row + P.am.row_offset);
-                    }
-                }
+                job.y[row] = v;
+                if (P.am.token && j == 0) better(bv, bi, v, row + P.am.row_offset);
             }
         }
     }
@@ -563,10 +572,7 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
             const int issued = s_issued;
             for (int i = max(0, issued - P.stages); i < issued; ++i)
                 mbar_wait(&full[i % P.stages], (uint32_t)(i / P.stages) & 1u, kWaitCycles);
-            if (bulk_x) {
-                mbar_wait(xbar, 0, kWaitCycles);
-                if (norm) mbar_wait(wbar, 0, kWaitCycles);
-            }
+            if (bulk_x && norm) mbar_wait(wbar, 0, kWaitCycles);
             if (P.status) atomicExch(P.status, kDevTimeoutTma);
         }
         return;
@@ -805,7 +811,7 @@ Shape plan(int K, int G, bool pair, int rows_total) {
     const size_t region = ((size_t)L.R * RB + 32 + 127) / 128 * 128;
     L.stage_bytes = (uint32_t)(np * region);
     const size_t kp = (size_t)L.nt * L.seg;
-    const size_t red = ((2 * (size_t)np * L.R * L.nt + 3) & ~(size_t)3);
+    const size_t red = ((2 * (size_t)np * L.R * (L.nt + 1) + 3) & ~(size_t)3);
     const size_t wsm = ((size_t)K + 3) & ~(size_t)3;
     const size_t dig = (size_t)L.nt * (6 * (L.seg / 8) + 4) + 4;
     const size_t floats = red + kp + wsm + dig + kp / 8;
