@@ -118,6 +118,20 @@ int tqb200_attention_decode_f16kv(const float *q, const uint16_t *k_cache,
                                   const uint16_t *v_cache, int seq_len, int max_seq_len,
                                   int n_heads, int n_kv_heads, int head_dim, float scale,
                                   float *out);
+/* Decode attention on DEVICE pointers (fp32 KV, the arguments of AttentionDecodeFn plus a
+ * cudaStream_t) that allocates nothing.  It has no counterpart in the reference.  It is for
+ * callers that cannot allocate device memory on the call path: an allocator that forbids
+ * allocations it does not track, every device byte reserved up front, or a loop that cannot
+ * afford an allocation call.  Its split-K scratch is a fixed file-scope device array of 4 MiB
+ * plus 256 KV-head tickets per device, held until the process exits; shapes needing more than
+ * 4 MiB for one split or more than 256 KV heads are rejected with TQB200_ERR_INVALID_ARG, as
+ * are k/v caches that are not 16-byte aligned.  Every call clears the tickets on its stream.
+ * The first call on a device looks up the array's address, so make it outside any stream
+ * capture.  All calls share the array: calls that overlap on the GPU race. */
+int tqb200_dev_attention_decode_noalloc(const float *q, const float *k_cache,
+                                        const float *v_cache, int seq_len, int max_seq_len,
+                                        int n_heads, int n_kv_heads, int head_dim, float scale,
+                                        float *out, void *stream);
 /* SwigluFn (kernels/dispatch.h:304); swiglu_ref, kernels/silu/swiglu_ref.cpp:41-52.  gate in place. */
 int tqb200_swiglu(float *gate, const float *up, int n);
 /* ArgmaxFn (kernels/dispatch.h:305) returns the index; here via *index (first maximum). */

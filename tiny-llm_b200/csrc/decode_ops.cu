@@ -673,6 +673,13 @@ int launch_attention(const AttnArgs &a, cudaStream_t st) {
     return a.kv_fp16 ? launch_attn_kv<uint16_t>(a, st) : launch_attn_kv<float>(a, st);
 }
 
+int launch_attention_split(const AttnArgs &a, cudaStream_t st) {
+    TQ_CHECK_ARG(a.n_kv_heads > 0 && a.n_heads % a.n_kv_heads == 0 && !a.k_new,
+                 "split attention: heads %d / kv %d (plain mode only)", a.n_heads, a.n_kv_heads);
+    TQ_CHECK_ARG(a.chunk_max >= (a.max_seq + a.nsplit - 1) / a.nsplit, "chunk plan");
+    return a.kv_fp16 ? launch_attn_kv<uint16_t>(a, st) : launch_attn_kv<float>(a, st);
+}
+
 int launch_swiglu(float *g, const float *u, int n, cudaStream_t st) {
     if (n == 0) return TQB200_OK;
     const int block = 256;

@@ -140,6 +140,8 @@ int launch_attention(const AttnArgs &a, cudaStream_t st);
 // The TMA-staged, cluster-merged kernel alone (no scratch: partial/tickets unused);
 // TQB200_ERR_UNSUPPORTED, with nothing launched, for shapes it does not cover.
 int launch_attention_tma(const AttnArgs &a, cudaStream_t st);
+// The split kernel alone (plain mode), with AttnArgs' partial/tickets scratch.
+int launch_attention_split(const AttnArgs &a, cudaStream_t st);
 
 int launch_swiglu(float *g, const float *u, int n, cudaStream_t st);
 int launch_swiglu_out(const float *g, const float *u, float *out, int n, cudaStream_t st);

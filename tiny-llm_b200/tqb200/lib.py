@@ -56,6 +56,7 @@ PROTOTYPES = {
     "tqb200_rmsnorm": ([_f, _f, _f, _i, _fl], _i),
     "tqb200_rope": ([_f, _f, _i, _i, _i, _i, _fl], _i),
     "tqb200_attention_decode": ([_f, _f, _f, _i, _i, _i, _i, _i, _fl, _f], _i),
+    "tqb200_dev_attention_decode_noalloc": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _fl, _vp, _vp], _i),
     "tqb200_attention_decode_f16kv": ([_f, _u16, _u16, _i, _i, _i, _i, _i, _fl, _f], _i),
     "tqb200_swiglu": ([_f, _f, _i], _i),
     "tqb200_argmax": ([_f, _i, C.POINTER(_i)], _i),
