@@ -14,23 +14,21 @@
 //  * Weight prefetch is issued before griddepcontrol.wait: under programmatic
 //    dependent launch the next matvec's weights stream while the previous
 //    kernel still finishes; only the activation read waits for it.
-//  * Thread (slot, seg) owns one SEG-column segment (SEG = 32 or 64, dividing
-//    G) of rows slot, slot+S, ... of every pass and keeps its SEG activations
-//    in registers for the whole kernel.  Reads from shared memory are
-//    bank-conflict free (segment stride 9 or 5 words).
-//  * Math (MATH_F32): a nibble becomes an exact float with one LOP3 (bits
-//    OR'ed into the mantissa of 2^23, activations pre-scaled by 16^-k) and one
-//    FADD; then one FFMA per weight, using
+//  * Warp 0 is the producer (one lane issues the copies and refills a stage once
+//    every consumer warp has arrived on its "empty" mbarrier); consumer thread
+//    (slot, seg) owns one SEG-column segment (SEG = 32 or 64, dividing G) of
+//    rows slot, slot+S, ... of every pass.  512 threads, one CTA per SM.
+//  * Math: activations split into three int8 digits with one scale for the
+//    whole vector (x ~ (d0 + d1/254 + d2/254^2) * max|x|/127, error
+//    <= 3.1e-8 * max|x|), built once per CTA from activations held in
+//    registers, and the nibble dots run as exact integer dp4a (two masks, no
+//    shift: high nibbles enter as 16x bytes; 6 dp4a per 8 weights, six
+//    independent accumulators), using
 //        sum_i (q_i - z) s x_i = s * (sum_i q_i x_i - z * sum_i x_i).
-//    (MATH_DP4A): activations split into three int8 digits with one scale
-//    for the whole vector (x ~ (d0 + d1/254 + d2/254^2) * max|x|/127, error
-//    <= 3.1e-8 * max|x|), built elementwise once per CTA, and the nibble dots
-//    run as exact integer dp4a (2 unpack ops + 6 dp4a per 8 weights).
-//  * The activation vector (and the RMSNorm weight or SwiGLU up vector) comes in
-//    by bulk copy; one pass computes the sum of squares and max |x|, a second
-//    applies the norm and builds the digit planes; a pass of rows then needs one
-//    barrier (partials double-buffered), and the bias / residual of its rows are
-//    fetched before its weights are waited on.
+//    A pass needs one named barrier among the consumers (partials are
+//    double-buffered); a row's segment partials are summed in double by one
+//    lane, and the bias / residual of its rows are fetched before the weights
+//    are waited on.
 //  * Optional fused prologues (RMSNorm of the source, SwiGLU of gate/up) and
 //    epilogues (bias, residual add, greedy argmax over the rows).
 //  * Every mbarrier wait is bounded; on timeout the kernel records an error
@@ -46,11 +44,7 @@ namespace tqb200 {
 
 namespace {
 
-constexpr uint32_t kMagic = 0x4B000000u;  // 2^23
-constexpr float kMagicF = 8388608.0f;
 constexpr int kMaxStages = 8;
-constexpr int MATH_F32 = 0;
-constexpr int MATH_DP4A = 1;
 
 struct MvParams {
     I4Job job[3];
@@ -65,23 +59,6 @@ struct MvParams {
     ArgmaxOut am;
     int *status;
 };
-
-__device__ __forceinline__ float nib_f(uint32_t w, uint32_t mask) {
-    return __uint_as_float((w & mask) | kMagic) - kMagicF;
-}
-
-// One 32-bit word of 8 nibbles against 8 activations pre-scaled by 16^-pos.
-__device__ __forceinline__ void dot8(uint32_t w, const float *xs, float &a0, float &a1) {
-    const uint32_t w2 = w >> 12;
-    a0 = fmaf(nib_f(w, 0x0000000Fu), xs[0], a0);
-    a1 = fmaf(nib_f(w, 0x000000F0u), xs[1], a1);
-    a0 = fmaf(nib_f(w, 0x00000F00u), xs[2], a0);
-    a1 = fmaf(nib_f(w, 0x0000F000u), xs[3], a1);
-    a0 = fmaf(nib_f(w, 0x000F0000u), xs[4], a0);
-    a1 = fmaf(nib_f(w2, 0x00000F00u), xs[5], a1);
-    a0 = fmaf(nib_f(w2, 0x0000F000u), xs[6], a0);
-    a1 = fmaf(nib_f(w2, 0x000F0000u), xs[7], a1);
-}
 
 __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
     int d;
@@ -207,8 +184,11 @@ __device__ __forceinline__ float row_sum_d(const float *p, int n) {
 // distinct bank groups)
 template <int NW> struct DigitLayout { static constexpr int stride = 6 * NW + 4; };
 
-template <int SEG, int MATH>
-__global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ MvParams P) {
+constexpr int kI4Threads = 512;  // producer warp + 15 consumer warps, one CTA per SM
+constexpr int kI4MaxItems = 3;   // 8-column activation chunks per thread (K <= 12288)
+
+template <int SEG>
+__global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_constant__ MvParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int NW = SEG / 8;
     constexpr int DS = DigitLayout<NW>::stride;
@@ -218,20 +198,19 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
     const int nt = P.nt, S = P.S, K = P.K, G = P.G, np = 1 + P.pair;
     const int KP = nt * SEG;  // every column a segment can own (>= K), a multiple of 32
     const int ncw = (int)(blockDim.x >> 5) - 1;  // consumer warps (warp 0 is the producer)
-    // shared memory: barriers | weight stages | red x2 | x | norm weight or up |
-    // digit planes [nt][DS] | 8-column chunk sums
+    const bool norm = P.x.mode == X_RMSNORM, swiglu = P.x.mode == X_SWIGLU;
+    // shared memory: barriers | weight stages | red x2 | digit planes [nt][DS] |
+    // 8-column chunk sums | RMSNorm weight (norm mode only)
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);  // [kMaxStages] weights landed
     uint64_t *empty = full + kMaxStages;                   // [kMaxStages] stage consumed
-    uint64_t *xbar = full + 2 * kMaxStages;                // activation copy
-    uint64_t *wbar = xbar + 1;                             // norm-weight copy
+    uint64_t *wbar = full + 2 * kMaxStages;                // norm-weight copy
     uint8_t *stage_base = smem + kBarBytes;
     float *red = reinterpret_cast<float *>(stage_base + (size_t)P.stages * P.stage_bytes);
     const int ntp = nt + 1;  // partial-row stride (odd: conflict-free per-lane row sums)
     const size_t red_n = (size_t)np * P.R * ntp;  // one buffer
-    float *xsm = red + ((2 * red_n + 3) & ~(size_t)3);
-    float *wsm = xsm + KP;
-    uint32_t *dig = reinterpret_cast<uint32_t *>(wsm + (((size_t)K + 3) & ~(size_t)3));
+    uint32_t *dig = reinterpret_cast<uint32_t *>(red + ((2 * red_n + 3) & ~(size_t)3));
     float *csum = reinterpret_cast<float *>(dig + (size_t)DS * nt);
+    float *wsm = csum + (((size_t)KP / 8 + 3) & ~(size_t)3);
     __shared__ uint32_t s_head[2 * kMaxStages];
     __shared__ int s_err, s_issued;  // s_issued: passes whose copies were issued
     __shared__ double s_rd[32];
@@ -240,14 +219,12 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
     __shared__ int s_bi[32];
     __shared__ bool s_last;
     const bool bulk_x = P.x_bulk != 0;
-    const bool norm = P.x.mode == X_RMSNORM, swiglu = P.x.mode == X_SWIGLU;
 
     if (t == 0) {
         for (int s = 0; s < P.stages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], ncw);
         }
-        mbar_init(xbar, 1);
         mbar_init(wbar, 1);
         fence_mbar_init();
         s_err = 0;
@@ -269,69 +246,68 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
     griddep_wait();
     griddep_launch();
 
-    // ---- activation: whole vector in shared memory, zero past K.  The activation is
-    // read with 16-byte loads by every thread (all issued before any is used), not by
-    // a bulk copy: a copy would queue behind this CTA's weight copies in the SM's copy
-    // engine.  The RMSNorm weight, a constant, came by bulk copy before the wait.
-    // Unaligned sources: batched scalar loads.
-    for (int i = K + t; i < KP; i += blockDim.x) xsm[i] = 0.0f;
-    if (bulk_x) {
-        const float4 *xs4 = reinterpret_cast<const float4 *>(P.x.src);
-        const float4 *up4 = reinterpret_cast<const float4 *>(P.x.up);
-        const int K4 = K / 4;
-        for (int i0 = t; i0 < K4; i0 += 4 * blockDim.x) {
-            float4 v[4], u[4];
+    // ---- activation, 8-column chunks c = t, t + blockDim, ... held in registers: one
+    // round of 16-byte loads (unaligned sources: scalar loads), SwiGLU applied, the sum
+    // of squares (RMSNorm, in double as rmsnorm_ref) and max |value| for the digit scale
+    const int nchunks = KP / 8;
+    float xv[kI4MaxItems][8];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int i = i0 + k * blockDim.x;
-                if (i < K4) {
-                    v[k] = xs4[i];
-                    if (swiglu) u[k] = up4[i];
+    for (int it = 0; it < kI4MaxItems; ++it) {
+        const int c = t + it * (int)blockDim.x;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) xv[it][k] = 0.0f;
+        if (c >= nchunks) continue;
+        if (bulk_x && 8 * c + 8 <= K) {
+            const float4 *s4 = reinterpret_cast<const float4 *>(P.x.src) + 2 * c;
+            const float4 a = s4[0], b = s4[1];
+            xv[it][0] = a.x, xv[it][1] = a.y, xv[it][2] = a.z, xv[it][3] = a.w;
+            xv[it][4] = b.x, xv[it][5] = b.y, xv[it][6] = b.z, xv[it][7] = b.w;
+            if (swiglu) {
+                const float4 *u4 = reinterpret_cast<const float4 *>(P.x.up) + 2 * c;
+                const float4 ua = u4[0], ub = u4[1];
+                const float u[8] = {ua.x, ua.y, ua.z, ua.w, ub.x, ub.y, ub.z, ub.w};
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const float g = xv[it][k];
+                    xv[it][k] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u[k]);
                 }
             }
+        } else {
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int i = i0 + k * blockDim.x;
-                if (i < K4) {
-                    reinterpret_cast<float4 *>(xsm)[i] = v[k];
-                    if (swiglu) reinterpret_cast<float4 *>(wsm)[i] = u[k];
+            for (int k = 0; k < 8; ++k) {
+                const int i = 8 * c + k;
+                if (i < K) {
+                    float v = P.x.src[i];
+                    if (swiglu) v = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), P.x.up[i]);
+                    xv[it][k] = v;
                 }
-            }
-        }
-        if (t == 0 && norm && !mbar_wait(wbar, 0, kWaitCycles)) s_err = 1;
-    } else {
-        for (int i0 = t; i0 < K; i0 += 4 * blockDim.x) {  // 4 loads in flight per thread
-            float v[4], u[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int i = i0 + k * blockDim.x;
-                v[k] = i < K ? P.x.src[i] : 0.0f;
-                u[k] = (i < K && swiglu) ? P.x.up[i] : (i < K && norm) ? P.x.norm_w[i] : 0.0f;
-            }
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int i = i0 + k * blockDim.x;
-                if (i < K) xsm[i] = v[k], wsm[i] = u[k];
             }
         }
     }
-    __syncthreads();
-    // pass A: SwiGLU in place; sum of squares (RMSNorm, in double as rmsnorm_ref);
-    // max |value| for the digit scale (RMSNorm: max |x*w|, scaled below)
+    if (norm) {
+        if (bulk_x) {
+            if (t == 0 && !mbar_wait(wbar, 0, kWaitCycles)) s_err = 1;
+        } else {
+            for (int i = t; i < K; i += blockDim.x) wsm[i] = P.x.norm_w[i];
+        }
+        __syncthreads();  // norm weights in shared memory
+    }
     {
         double ss = 0.0;
         float am = 0.0f;
-        for (int i = t; i < K; i += blockDim.x) {
-            float v = xsm[i];
-            if (swiglu) {
-                v = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), wsm[i]);
-                xsm[i] = v;
-            }
-            if (norm) {
-                ss += (double)v * (double)v;
-                am = fmaxf(am, fabsf(v * wsm[i]));
-            } else {
-                am = fmaxf(am, fabsf(v));
+#pragma unroll
+        for (int it = 0; it < kI4MaxItems; ++it) {
+            const int c = t + it * (int)blockDim.x;
+            if (c >= nchunks) continue;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float v = xv[it][k];
+                if (norm) {
+                    ss += (double)v * (double)v;
+                    am = fmaxf(am, fabsf(v * (8 * c + k < K ? wsm[8 * c + k] : 0.0f)));
+                } else {
+                    am = fmaxf(am, fabsf(v));
+                }
             }
         }
         if (norm) ss = warp_sum_d(ss);
@@ -356,8 +332,8 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
             amax = amax * rms_scale * 1.0000005f;  // bound on |(x*r)*w| after rounding
         }
     }
-    // pass B, 8 columns (one weight word) per item: RMSNorm applied, the chunk sum, and
-    // the dp4a digit planes of the vector with ONE scale for all of it:
+    // pass B, per chunk: RMSNorm applied, the chunk sum, and the dp4a digit planes of
+    // the vector with ONE scale for all of it:
     //   x ~ (d0 + d1/254 + d2/254^2) * s0,  s0 = max|x| / 127  (error <= 3.1e-8 max|x|);
     // word order per chunk (lo, hi) x (d0, d1, d2), lo = even columns, hi = odd ones,
     // matching the nibble order of a weight word.  Rounding to the nearest integer
@@ -368,38 +344,36 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
     {
         constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
         const float i0 = 1.0f / dsc0, i1 = 1.0f / dsc1, i2 = 1.0f / dsc2;
-        for (int c = t; c < KP / 8; c += blockDim.x) {
-            float4 a = *reinterpret_cast<const float4 *>(xsm + 8 * c);
-            float4 b = *reinterpret_cast<const float4 *>(xsm + 8 * c + 4);
-            float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-            if (norm) {
 #pragma unroll
-                for (int k = 0; k < 8; ++k)
+        for (int it = 0; it < kI4MaxItems; ++it) {
+            const int c = t + it * (int)blockDim.x;
+            if (c >= nchunks) continue;
+            float v[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                v[k] = xv[it][k];
+                if (norm)
                     v[k] = 8 * c + k < K ? __fmul_rn(__fmul_rn(v[k], rms_scale), wsm[8 * c + k]) : 0.0f;
-                *reinterpret_cast<float4 *>(xsm + 8 * c) = make_float4(v[0], v[1], v[2], v[3]);
-                *reinterpret_cast<float4 *>(xsm + 8 * c + 4) = make_float4(v[4], v[5], v[6], v[7]);
             }
             csum[c] = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
-            if constexpr (MATH == MATH_DP4A) {
-                uint32_t wd[6] = {0u, 0u, 0u, 0u, 0u, 0u};
+            uint32_t wd[6] = {0u, 0u, 0u, 0u, 0u, 0u};
 #pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    const float t0 = fmaf(v[k], i0, kRound);
-                    const float r1 = fmaf(-(t0 - kRound), dsc0, v[k]);
-                    const float t1 = fmaf(r1, i1, kRound);
-                    const float r2 = fmaf(-(t1 - kRound), dsc1, r1);
-                    const float t2 = fmaf(r2, i2, kRound);
-                    const int sh = 8 * (k >> 1);
-                    wd[(k & 1) + 0] |= (__float_as_uint(t0) & 0xFFu) << sh;
-                    wd[(k & 1) + 2] |= (__float_as_uint(t1) & 0xFFu) << sh;
-                    wd[(k & 1) + 4] |= (__float_as_uint(t2) & 0xFFu) << sh;
-                }
-                const int sgi = c / NW, ci = c - sgi * NW;
-                uint2 *dst = reinterpret_cast<uint2 *>(dig + (size_t)sgi * DS + 6 * ci);
-                dst[0] = make_uint2(wd[0], wd[1]);
-                dst[1] = make_uint2(wd[2], wd[3]);
-                dst[2] = make_uint2(wd[4], wd[5]);
+            for (int k = 0; k < 8; ++k) {
+                const float t0 = fmaf(v[k], i0, kRound);
+                const float r1 = fmaf(-(t0 - kRound), dsc0, v[k]);
+                const float t1 = fmaf(r1, i1, kRound);
+                const float r2 = fmaf(-(t1 - kRound), dsc1, r1);
+                const float t2 = fmaf(r2, i2, kRound);
+                const int sh = 8 * (k >> 1);
+                wd[(k & 1) + 0] |= (__float_as_uint(t0) & 0xFFu) << sh;
+                wd[(k & 1) + 2] |= (__float_as_uint(t1) & 0xFFu) << sh;
+                wd[(k & 1) + 4] |= (__float_as_uint(t2) & 0xFFu) << sh;
             }
+            const int sgi = c / NW, ci = c - sgi * NW;
+            uint2 *dst = reinterpret_cast<uint2 *>(dig + (size_t)sgi * DS + 6 * ci);
+            dst[0] = make_uint2(wd[0], wd[1]);
+            dst[1] = make_uint2(wd[2], wd[3]);
+            dst[2] = make_uint2(wd[4], wd[5]);
         }
     }
     __syncthreads();
@@ -433,31 +407,19 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
         const size_t RB = (size_t)((K + G - 1) / G) * GB;
         const int spg = G / SEG;
         const int g = sg / spg;
-        const int col0 = sg * SEG;
         const uint32_t hdr_off = (uint32_t)g * GB;
         const uint32_t seg_off = hdr_off + 4u + (uint32_t)(sg - g * spg) * (SEG / 2);
         const int ncons = ncw * 32;
         float X = 0.0f;  // segment sum (zero-point term)
-        float xs[MATH == MATH_F32 ? SEG : 1];
-        uint32_t xd[MATH == MATH_DP4A ? 6 * NW : 1];
+        uint32_t xd[6 * NW];
         if (active) {
 #pragma unroll
             for (int ci = 0; ci < NW; ++ci) X += csum[sg * NW + ci];
-            if constexpr (MATH == MATH_F32) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(dig + (size_t)sg * DS);
 #pragma unroll
-                for (int i = 0; i < NW; ++i)
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) {
-                        const int pos = k < 5 ? k : k - 3;
-                        xs[8 * i + k] = xsm[col0 + 8 * i + k] * __uint_as_float((uint32_t)(127 - 4 * pos) << 23);
-                    }
-            } else {
-                const uint4 *src = reinterpret_cast<const uint4 *>(dig + (size_t)sg * DS);
-#pragma unroll
-                for (int w = 0; w < 6 * NW / 4; ++w) {
-                    const uint4 v4 = src[w];
-                    xd[4 * w + 0] = v4.x, xd[4 * w + 1] = v4.y, xd[4 * w + 2] = v4.z, xd[4 * w + 3] = v4.w;
-                }
+            for (int w = 0; w < 6 * NW / 4; ++w) {
+                const uint4 v4 = src[w];
+                xd[4 * w + 0] = v4.x, xd[4 * w + 1] = v4.y, xd[4 * w + 2] = v4.z, xd[4 * w + 3] = v4.w;
             }
         }
         for (int i_pass = 0;; ++i_pass) {
@@ -495,27 +457,23 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
                 const uint32_t hv = lds_u32(rp + hdr_off);
                 const float sc = h2f((uint16_t)(hv & 0xFFFFu));
                 const float zr = h2f((uint16_t)(hv >> 16));
-                if constexpr (MATH == MATH_F32) {
-                    float a0 = 0.0f, a1 = 0.0f;
+                // low nibbles as bytes, high nibbles as 16x bytes (one mask each, no
+                // shift): six independent accumulators, the high ones scaled back by 16
+                int L0 = 0, L1 = 0, L2 = 0, H0 = 0, H1 = 0, H2 = 0;
 #pragma unroll
-                    for (int i = 0; i < NW; ++i) dot8(lds_u32(rp + seg_off + 4 * i), xs + 8 * i, a0, a1);
-                    return sc * fmaf(-zr, X, a0 + a1);
-                } else {
-                    int D0 = 0, D1 = 0, D2 = 0;
-#pragma unroll
-                    for (int i = 0; i < NW; ++i) {
-                        const uint32_t wd = lds_u32(rp + seg_off + 4 * i);
-                        const uint32_t lo = wd & 0x0F0F0F0Fu, hi = (wd >> 4) & 0x0F0F0F0Fu;
-                        D0 = dp4a_us(lo, xd[6 * i + 0], D0);
-                        D0 = dp4a_us(hi, xd[6 * i + 1], D0);
-                        D1 = dp4a_us(lo, xd[6 * i + 2], D1);
-                        D1 = dp4a_us(hi, xd[6 * i + 3], D1);
-                        D2 = dp4a_us(lo, xd[6 * i + 4], D2);
-                        D2 = dp4a_us(hi, xd[6 * i + 5], D2);
-                    }
-                    const float dot = fmaf((float)D0, dsc0, fmaf((float)D1, dsc1, (float)D2 * dsc2));
-                    return sc * fmaf(-zr, X, dot);
+                for (int i = 0; i < NW; ++i) {
+                    const uint32_t wd = lds_u32(rp + seg_off + 4 * i);
+                    const uint32_t lo = wd & 0x0F0F0F0Fu, hi = wd & 0xF0F0F0F0u;
+                    L0 = dp4a_us(lo, xd[6 * i + 0], L0);
+                    H0 = dp4a_us(hi, xd[6 * i + 1], H0);
+                    L1 = dp4a_us(lo, xd[6 * i + 2], L1);
+                    H1 = dp4a_us(hi, xd[6 * i + 3], H1);
+                    L2 = dp4a_us(lo, xd[6 * i + 4], L2);
+                    H2 = dp4a_us(hi, xd[6 * i + 5], H2);
                 }
+                const int D0 = L0 + (H0 >> 4), D1 = L1 + (H1 >> 4), D2 = L2 + (H2 >> 4);
+                const float dot = fmaf((float)D0, dsc0, fmaf((float)D1, dsc1, (float)D2 * dsc2));
+                return sc * fmaf(-zr, X, dot);
             };
             if (active && ok) {
                 // rows slot, slot+S, ... of each job; two at a time for independent chains
@@ -539,8 +497,8 @@ __global__ void __launch_bounds__(512) i4_mv_tma_kernel(const __grid_constant__ 
                 break;
             }
             // rows of this pass, 32 per warp (a lane per row): the row's segment partials
-            // summed in order in double and rounded once, as the reference's double row
-            // dot is.  Chunk c of 32 rows goes to consumer warp (i_pass + c) % ncw, so the
+            // summed in double and rounded once, as the reference's double row dot is.
+            // Chunk c of 32 rows goes to consumer warp (i_pass + c) % ncw, so the
             // reductions of consecutive passes spread over the warps.
             for (int c = 0, k = 0; c * 32 < P.R; ++c) {
                 if ((i_pass + c) % ncw != cw) continue;
@@ -762,16 +720,6 @@ __global__ void i4_dequant_kernel(const uint8_t *__restrict__ w, int rows, int d
 }
 
 int g_num_sms = 0;
-int g_math = -1;  // MATH_F32 / MATH_DP4A, from TQB200_I4_MATH (default dp4a)
-
-int math_mode() {
-    if (g_math < 0) {
-        const char *e = getenv("TQB200_I4_MATH");
-        g_math = (e && e[0] == 'f') ? MATH_F32 : MATH_DP4A;
-    }
-    return g_math;
-}
-
 struct Shape {
     int seg = 0, nt = 0, S = 0, RP = 0, R = 0, block = 0, stages = 0;
     uint32_t stage_bytes = 0;
@@ -784,23 +732,26 @@ struct Shape {
 // passes spread evenly); otherwise passes of <= 32 KB stream through a ring of up to
 // 96 KB.  Shared memory stays near 110 KB or below for most shapes, so the next
 // kernel's CTA can become resident (and start its weight copies) before this one ends.
-Shape plan(int K, int G, bool pair, int rows_total) {
+// Launch shape.  One CTA per SM (512 threads: the producer warp and S row slots of
+// nt segment threads; the block takes the whole register file).  A pass is R
+// consecutive rows, one bulk copy (two in paired mode): a single pass when a CTA's
+// share of the rows fits in 64 KB (R = rows / SMs, so the passes spread evenly),
+// otherwise passes of up to 32 KB through a ring of up to ~200 KB, all in flight.
+Shape plan(int K, int G, bool pair, bool norm, int rows_total) {
     Shape L;
     L.seg = (G % 64 == 0) ? 64 : 32;
     const int ng = (K + G - 1) / G;
     L.nt = ng * (G / L.seg);
-    if (L.nt > 512) {
-        L.seg = 0;
+    const int consumers = kI4Threads - 32;
+    const size_t kp = (size_t)L.nt * L.seg;
+    if (L.nt > consumers || kp / 8 > (size_t)kI4Threads * kI4MaxItems) {
+        L.seg = 0;  // the generic kernel
         return L;
     }
     const size_t RB = (size_t)ng * (4 + G / 2);
     const int np = pair ? 2 : 1;
-    if (L.nt > 480) {  // warp 0 is the producer: at most 480 segment threads
-        L.seg = 0;
-        return L;
-    }
-    L.S = std::max(1, 480 / L.nt);
-    L.block = 32 + ((L.nt * L.S + 31) / 32) * 32;
+    L.S = std::max(1, consumers / L.nt);
+    L.block = kI4Threads;
     const int per_cta = std::max(1, (rows_total + num_sms() - 1) / num_sms());
     if ((size_t)per_cta * RB * np <= 64 * 1024) {
         L.R = per_cta;
@@ -810,21 +761,19 @@ Shape plan(int K, int G, bool pair, int rows_total) {
     L.RP = (L.R + L.S - 1) / L.S;
     const size_t region = ((size_t)L.R * RB + 32 + 127) / 128 * 128;
     L.stage_bytes = (uint32_t)(np * region);
-    const size_t kp = (size_t)L.nt * L.seg;
     const size_t red = ((2 * (size_t)np * L.R * (L.nt + 1) + 3) & ~(size_t)3);
-    const size_t wsm = ((size_t)K + 3) & ~(size_t)3;
-    const size_t dig = (size_t)L.nt * (6 * (L.seg / 8) + 4) + 4;
-    const size_t floats = red + kp + wsm + dig + kp / 8;
-    // the block holds the whole register file (512 threads), so nothing else shares
-    // the SM: every stage the shared memory can hold is in flight at once
-    const size_t cap = 200 * 1024, fixed = kBarBytes + floats * 4;
+    const size_t dig = (size_t)L.nt * (6 * (L.seg / 8) + 4);
+    const size_t csum = (kp / 8 + 3) & ~(size_t)3;
+    const size_t wsm = norm ? (((size_t)K + 3) & ~(size_t)3) : 0;
+    const size_t fixed = kBarBytes + (red + dig + csum + wsm) * 4;
+    const size_t cap = 200 * 1024;
     const size_t ring = cap > fixed ? cap - fixed : 0;
     L.stages = (int)std::min<size_t>(kMaxStages, ring / L.stage_bytes);
     const int passes_per_cta =
         (int)(((size_t)(rows_total + L.R - 1) / L.R + num_sms() - 1) / num_sms());
-    L.stages = std::max(1, std::min(L.stages, passes_per_cta));
-    L.smem = fixed + (size_t)L.stages * L.stage_bytes;
-    if (L.stages < 1 || L.smem > cap) L.seg = 0;  // no TMA shape: the generic kernel
+    L.stages = std::min(L.stages, passes_per_cta);
+    L.smem = fixed + (size_t)std::max(1, L.stages) * L.stage_bytes;
+    if (L.stages < 1) L.seg = 0;  // no TMA shape: the generic kernel
     return L;
 }
 
@@ -839,15 +788,16 @@ int grid_for(Kern k, int block, size_t smem, int work) {
     return std::max(1, std::min(work, per_sm * num_sms()));
 }
 
-template <int SEG, int MATH>
+template <int SEG>
 int launch_tma(const MvParams &P, const Shape &L, int passes, bool pdl, cudaStream_t st) {
-    auto k = i4_mv_tma_kernel<SEG, MATH>;
+    auto k = i4_mv_tma_kernel<SEG>;
     static std::atomic<unsigned long long> attr_set{0};
     int smem_max = 0;
     TQ_CUDA_TRY(smem_limit_once(k, attr_set, &smem_max));
     TQ_CHECK_ARG(L.smem <= (size_t)smem_max, "i4 matvec: %zu B of shared memory above the %d B limit",
                  L.smem, smem_max);
-    // persistent: at most one CTA per SM, so the x prologue is paid once per SM
+    // one CTA per SM for this kernel (the activation prologue is paid once per SM); the
+    // SM's second slot is for the next kernel
     const int grid = std::min(grid_for(k, L.block, L.smem, passes), num_sms());
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -900,7 +850,7 @@ int launch_i4_matvec_ex(const I4Job *jobs, int n_jobs, int in_dim, int group_siz
     int rows_total = 0;
     for (int j = 0; j < n_jobs; ++j)
         if (!pair || j == 0) rows_total += std::max(0, jobs[j].rows);
-    const Shape L = plan(in_dim, group_size, pair, rows_total);
+    const Shape L = plan(in_dim, group_size, pair, o.x.mode == X_RMSNORM, rows_total);
     bool aligned = true;  // the TMA path needs 16-byte aligned matrix bases
     for (int j = 0; j < n_jobs; ++j) aligned = aligned && ((uintptr_t)jobs[j].w % 16u == 0);
     const bool fast = (group_size % 32 == 0) && L.seg != 0 && aligned;
@@ -929,12 +879,8 @@ int launch_i4_matvec_ex(const I4Job *jobs, int n_jobs, int in_dim, int group_siz
         P.R = L.R;
         P.stages = L.stages;
         P.stage_bytes = L.stage_bytes;
-        const bool dp4a = math_mode() == MATH_DP4A;
-        if (L.seg == 64)
-            return dp4a ? launch_tma<64, MATH_DP4A>(P, L, acc, o.pdl, stream)
-                        : launch_tma<64, MATH_F32>(P, L, acc, o.pdl, stream);
-        return dp4a ? launch_tma<32, MATH_DP4A>(P, L, acc, o.pdl, stream)
-                    : launch_tma<32, MATH_F32>(P, L, acc, o.pdl, stream);
+        if (L.seg == 64) return launch_tma<64>(P, L, acc, o.pdl, stream);
+        return launch_tma<32>(P, L, acc, o.pdl, stream);
     }
     const int grid = std::max(1, std::min((acc + 7) / 8, num_sms() * 8));
     i4_matvec_generic_kernel<<<grid, 256, 0, stream>>>(P);
