@@ -12,9 +12,9 @@
 // thread-block cluster.  CTA rank s owns positions [s*chunk, s*chunk+n) of its KV
 // head for the G query heads that share it.  Thread 0 streams the chunk's K rows
 // and then its V rows through a ring of shared-memory tiles (one cp.async.bulk per
-// tile, completion on an mbarrier).  Scores: a warp per cached row, lanes over head
-// dimensions, the G dot products reduced across the warp with a reduce-scatter
-// (log2 G exchanges halve the values each lane holds).  Exact max/sum softmax over
+// tile, completion on an mbarrier).  Scores: a warp takes 32/G cached rows at a time,
+// lanes over head dimensions, and reduces their G dot products each (32 values)
+// across the warp with one reduce-scatter.  Exact max/sum softmax over
 // the chunk, P.V with threads over (dimension quad, row subset).  Each CTA leaves
 // its (m, l, o) in its own shared memory; after a cluster barrier every CTA merges
 // a slice of the output by reading the other ranks' partials over DSMEM (weights
@@ -139,6 +139,42 @@ __device__ __forceinline__ void score_row(const KV *kr, const float (&qr)[G][HD 
     constexpr int SH = 5 - Log2<GP>::v;
     const int g = lane >> SH;
     if ((lane & ((1 << SH) - 1)) == 0 && g < G) sc_row[g] = acc[0] * scale;
+}
+
+// Scores of RW = 32/GP consecutive cached rows at once (warp-cooperative): every lane
+// forms the partial dots of its HD/32 dimensions for all RW rows and G heads (32
+// values), and one 5-level reduce-scatter leaves lane l with the full dot of row
+// l / GP, head l % GP: 31 shuffles in 5 dependent steps for RW rows instead of
+// ~6 dependent steps per row.  Rows at or past `rows` are skipped.
+template <typename KV, int HD, int G>
+__device__ __forceinline__ void score_rows(const KV *kr, int rows, const float (&qr)[G][HD / 32],
+                                           int lane, float scale, float *sc_rows) {
+    constexpr int D = HD / 32;
+    constexpr int GP = Pow2<G>::v;
+    constexpr int RW = 32 / GP;
+    float acc[32];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+        float k[D];
+        if (r < rows) {
+            lds_kv<D>(kr + (size_t)r * HD + lane * D, k);
+        } else {
+#pragma unroll
+            for (int d = 0; d < D; ++d) k[d] = 0.0f;
+        }
+#pragma unroll
+        for (int g = 0; g < GP; ++g) {
+            float a = 0.0f;
+            if (g < G) {
+#pragma unroll
+                for (int d = 0; d < D; ++d) a = fmaf(qr[g][d], k[d], a);
+            }
+            acc[r * GP + g] = a;
+        }
+    }
+    warp_reduce_scatter<32, 16>(acc, lane);
+    const int r = lane / GP, g = lane - r * GP;
+    if (r < rows && g < G) sc_rows[r * G + g] = acc[0] * scale;
 }
 
 // Warp-level QK-norm (optional) + rotate-half RoPE of one head vector, in place in
@@ -338,8 +374,10 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
         if (s_err) break;
         const KV *tile = reinterpret_cast<const KV *>(ring + (size_t)(it % NST) * T * RB);
         const int r0 = it * T, rows = min(T, n_copy - r0);
-        for (int r = warp; r < rows; r += kWarps)
-            score_row<KV, HD, G>(tile + (size_t)r * HD, qr, lane, P.scale, sc + (size_t)(r0 + r) * G);
+        constexpr int RW = 32 / Pow2<G>::v;
+        for (int rb = warp * RW; rb < rows; rb += kWarps * RW)
+            score_rows<KV, HD, G>(tile + (size_t)rb * HD, rows - rb, qr, lane, P.scale,
+                                  sc + (size_t)(r0 + rb) * G);
         __syncthreads();
         if (tid == 0 && it + NST < total) issue(it + NST);
     }
