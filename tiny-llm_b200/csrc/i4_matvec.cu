@@ -26,9 +26,8 @@
 //    independent accumulators), using
 //        sum_i (q_i - z) s x_i = s * (sum_i q_i x_i - z * sum_i x_i).
 //    A pass needs one named barrier among the consumers (partials are
-//    double-buffered); a row's segment partials are summed in double by one
-//    lane, and the bias / residual of its rows are fetched before the weights
-//    are waited on.
+//    double-buffered); a row's segment partials are summed by one lane, and the
+//    bias / residual of its rows are fetched before the weights are waited on.
 //  * Optional fused prologues (RMSNorm of the source, SwiGLU of gate/up) and
 //    epilogues (bias, residual add, greedy argmax over the rows).
 //  * Every mbarrier wait is bounded; on timeout the kernel records an error
@@ -142,8 +141,12 @@ __device__ void issue_pass(const MvParams &P, int p, int s, uint64_t *bars, uint
         b1 = stage_rows(P, P.job[1], row0, row1, dst + cap, cap, &s_head[kMaxStages + s], &src1);
     fence_proxy_async_smem();
     mbar_arrive_expect_tx(&bars[s], b0 + b1);
-    if (b0) bulk_g2s(dst, src0, b0, &bars[s]);
-    if (b1) bulk_g2s(dst + cap, src1, b1, &bars[s]);
+    // pieces of <= 16 KB: one bulk copy is fetched at a limited rate per SM, several in
+    // flight reach the full rate
+    constexpr uint32_t kPiece = 16384;
+    for (uint32_t o = 0; o < b0; o += kPiece) bulk_g2s(dst + o, src0 + o, min(kPiece, b0 - o), &bars[s]);
+    for (uint32_t o = 0; o < b1; o += kPiece)
+        bulk_g2s(dst + cap + o, src1 + o, min(kPiece, b1 - o), &bars[s]);
 }
 
 constexpr int kBarBytes = 256;  // 2*kMaxStages + 2 mbarriers, rounded up
@@ -165,18 +168,20 @@ __device__ __forceinline__ bool consumer_sync_or(int nthreads, bool pred) {
     return r != 0;
 }
 
-// Sum of n segment partials in double (four interleaved accumulators), rounded once.
-__device__ __forceinline__ float row_sum_d(const float *p, int n) {
-    double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+// Sum of n segment partials (four interleaved fp32 accumulators; n <= 480 partials
+// of a row whose terms are already dp4a-exact per segment, so the sum's rounding error
+// stays near 1e-6 relative, far inside the 1e-4 bound).
+__device__ __forceinline__ float row_sum(const float *p, int n) {
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
     int i = 0;
     for (; i + 4 <= n; i += 4) {
-        a0 += (double)p[i];
-        a1 += (double)p[i + 1];
-        a2 += (double)p[i + 2];
-        a3 += (double)p[i + 3];
+        a0 += p[i];
+        a1 += p[i + 1];
+        a2 += p[i + 2];
+        a3 += p[i + 3];
     }
-    for (; i < n; ++i) a0 += (double)p[i];
-    return (float)((a0 + a1) + (a2 + a3));
+    for (; i < n; ++i) a0 += p[i];
+    return (a0 + a1) + (a2 + a3);
 }
 
 // dp4a digit planes of one segment: 6 words per 8 columns, then 4 words of padding
@@ -339,11 +344,13 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
     // matching the nibble order of a weight word.  Rounding to the nearest integer
     // uses the 1.5*2^23 trick (one FFMA; the digit's byte is the low byte of the
     // sum's bits), so no float/int conversions; |digit| <= 127 by construction.
-    const float dsc0 = amax > 0.0f ? amax / 127.0f : 1.0f;
-    const float dsc1 = dsc0 / 254.0f, dsc2 = dsc1 / 254.0f;
+    // (the scales need not be exact quotients: any s0 >= max|x| / 127 to within a
+    // few ulp keeps every digit within +-127)
+    const float dsc0 = amax > 0.0f ? amax * (1.0f / 127.0f) : 1.0f;
+    const float dsc1 = dsc0 * (1.0f / 254.0f), dsc2 = dsc1 * (1.0f / 254.0f);
     {
         constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
-        const float i0 = 1.0f / dsc0, i1 = 1.0f / dsc1, i2 = 1.0f / dsc2;
+        const float i0 = __frcp_rn(dsc0), i1 = __frcp_rn(dsc1), i2 = __frcp_rn(dsc2);
 #pragma unroll
         for (int it = 0; it < kI4MaxItems; ++it) {
             const int c = t + it * (int)blockDim.x;
@@ -356,7 +363,7 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
                     v[k] = 8 * c + k < K ? __fmul_rn(__fmul_rn(v[k], rms_scale), wsm[8 * c + k]) : 0.0f;
             }
             csum[c] = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
-            uint32_t wd[6] = {0u, 0u, 0u, 0u, 0u, 0u};
+            uint32_t d0[8], d1[8], d2[8];  // digit k of each column, in the low byte
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
                 const float t0 = fmaf(v[k], i0, kRound);
@@ -364,11 +371,18 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
                 const float t1 = fmaf(r1, i1, kRound);
                 const float r2 = fmaf(-(t1 - kRound), dsc1, r1);
                 const float t2 = fmaf(r2, i2, kRound);
-                const int sh = 8 * (k >> 1);
-                wd[(k & 1) + 0] |= (__float_as_uint(t0) & 0xFFu) << sh;
-                wd[(k & 1) + 2] |= (__float_as_uint(t1) & 0xFFu) << sh;
-                wd[(k & 1) + 4] |= (__float_as_uint(t2) & 0xFFu) << sh;
+                d0[k] = __float_as_uint(t0);
+                d1[k] = __float_as_uint(t1);
+                d2[k] = __float_as_uint(t2);
             }
+            // low bytes of columns (0,2,4,6) -> lo word, (1,3,5,7) -> hi word
+            auto pack = [](const uint32_t *d, int o) {
+                const uint32_t a = __byte_perm(d[o], d[o + 2], 0x0040);
+                const uint32_t b = __byte_perm(d[o + 4], d[o + 6], 0x0040);
+                return __byte_perm(a, b, 0x5410);
+            };
+            const uint32_t wd[6] = {pack(d0, 0), pack(d0, 1), pack(d1, 0),
+                                    pack(d1, 1), pack(d2, 0), pack(d2, 1)};
             const int sgi = c / NW, ci = c - sgi * NW;
             uint2 *dst = reinterpret_cast<uint2 *>(dig + (size_t)sgi * DS + 6 * ci);
             dst[0] = make_uint2(wd[0], wd[1]);
@@ -434,14 +448,16 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
             float *rb = red + (size_t)(i_pass & 1) * red_n;  // double-buffered partials
             // bias / residual of the rows this warp reduces (below), fetched before the
             // weight wait; chunk c of 32 rows belongs to consumer warp (i_pass + c) % ncw
-            float pre_b[2] = {0.0f, 0.0f}, pre_r[2] = {0.0f, 0.0f};
+            float pre_b0 = 0.0f, pre_b1 = 0.0f, pre_r0 = 0.0f, pre_r1 = 0.0f;
             if (!P.pair) {
                 for (int c = 0, k = 0; c * 32 < P.R && k < 2; ++c) {
                     if ((i_pass + c) % ncw != cw) continue;
                     const int rl = c * 32 + lane, row = row0 + rl;
                     if (rl < P.R && row < job.rows) {
-                        if (job.bias) pre_b[k] = job.bias[row];
-                        if (job.resid) pre_r[k] = job.resid[row];
+                        const float b = job.bias ? job.bias[row] : 0.0f;
+                        const float r = job.resid ? job.resid[row] : 0.0f;
+                        if (k == 0) pre_b0 = b, pre_r0 = r;
+                        else pre_b1 = b, pre_r1 = r;
                     }
                     ++k;
                 }
@@ -497,7 +513,7 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
                 break;
             }
             // rows of this pass, 32 per warp (a lane per row): the row's segment partials
-            // summed in double and rounded once, as the reference's double row dot is.
+            // summed by one lane.
             // Chunk c of 32 rows goes to consumer warp (i_pass + c) % ncw, so the
             // reductions of consecutive passes spread over the warps.
             for (int c = 0, k = 0; c * 32 < P.R; ++c) {
@@ -505,14 +521,14 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
                 const int kk = k++;
                 const int rl = c * 32 + lane, row = row0 + rl;
                 if (rl >= P.R || row >= job.rows) continue;
-                float v = row_sum_d(rb + (size_t)rl * ntp, nt);
+                float v = row_sum(rb + (size_t)rl * ntp, nt);
                 if (P.pair) {
-                    const float u = row_sum_d(rb + (size_t)(P.R + rl) * ntp, nt);
+                    const float u = row_sum(rb + (size_t)(P.R + rl) * ntp, nt);
                     // swiglu_ref (kernels/silu/swiglu_ref.cpp:41-52) on (gate, up)
                     v = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), u);
                 } else {
-                    const float b_ = kk < 2 ? pre_b[kk] : (job.bias ? job.bias[row] : 0.0f);
-                    const float r_ = kk < 2 ? pre_r[kk] : (job.resid ? job.resid[row] : 0.0f);
+                    const float b_ = kk == 0 ? pre_b0 : kk == 1 ? pre_b1 : (job.bias ? job.bias[row] : 0.0f);
+                    const float r_ = kk == 0 ? pre_r0 : kk == 1 ? pre_r1 : (job.resid ? job.resid[row] : 0.0f);
                     if (job.bias) v += b_;
                     if (job.resid) v = r_ + v;
                 }
