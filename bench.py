@@ -3,18 +3,27 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
 
-Prints ONE JSON line (rank 0).  Workloads (synthetic seeded data of the
-BASELINE shapes):
+Prints ONE JSON line (rank 0).  Workloads (synthetic seeded data of the BASELINE
+shapes; random weights of the named architecture, no checkpoint):
 
-  matvec-i4   BASELINE config 1: i4 g64 matvec 4864x896.  A step is one CUDA-graph
-              replay of 64 launches, one per distinct copy of W (64 x 2.45 MB =
-              157 MB > the 126 MB L2, so every launch streams W from HBM).
+  decode-qwen3-4b       (default) BASELINE config 4: Qwen3-4B-shaped i4 g64 model, fp16
+                        KV, context 4096 filled by the engine's own greedy decode.  A step
+                        is one decode token; value = device-timed ms/token of K
+                        generate() steps; e2e = tqb200_engine_step per token (host token
+                        in, host token out).  With --gpus N under torchrun the engine runs
+                        tensor-parallel over the N ranks.
+  decode-qwen2.5-0.5b   BASELINE config 2 shape (i4, fp32 KV, context 32).
+  decode-qwen3-0.6b-vq2 BASELINE config 3 full step (VQ2 + BiIP, fp32 KV, context 32).
+  matvec-i4             BASELINE config 1: i4 g64 matvec 4864x896.  A step is one
+                        CUDA-graph replay of 64 launches, one per distinct copy of W
+                        (64 x 2.45 MB = 157 MB > the 126 MB L2, so every launch streams W
+                        from HBM).
 
-Timing: W warm-up steps, then K steps bracketed by a barrier and
-cudaDeviceSynchronize, CUDA events on the launching stream, max over ranks.
-nvidia-smi clocks are sampled during the timed region.  The oracle/_ref CPU
-build (the reference's own code) is timed on a bounded sample for
-``cpu_baseline``; ``--impl reference`` times only that.
+Timing: W warm-up steps, then K steps bracketed by a barrier and a device sync, CUDA
+events on the launching stream, max over ranks.  nvidia-smi clocks are sampled during
+the timed region.  The reference's own CPU code (oracle/_ref, compiled from the
+reference sources) is timed on a bounded sample for ``cpu_baseline``;
+``--impl reference`` times only that.
 """
 from __future__ import annotations
 
@@ -286,28 +295,23 @@ def bench_matvec(args, rank, pg, pk, pk_kind):
 DECODE_CTX = 4096
 
 
-def qwen3_4b_spec(max_seq: int):
-    from dataclasses import replace
-    from tqb200.model import QWEN3_4B
-    # random codes/scales/zeros (config-1 distributions) instead of RTN of N(0,0.02):
-    # same bytes and shapes, built in seconds
-    return replace(QWEN3_4B, weights="codes", max_seq_len=max_seq)
-
-
 def matvec_bytes_by_kind(spec) -> dict:
-    """Algorithmic bytes per decode step of every matvec kind: weights + x + y once."""
+    """Algorithmic bytes per decode step of every matvec kind: weights + x + y once
+    (VQ2: codebook + one index byte per 4 weights; lm_head is i4 in every model here)."""
     from tqb200.synth import i4_row_bytes
     H, I, G = spec.hidden, spec.inter, spec.group_size
     qd, kvd, L = spec.n_heads * spec.head_dim, spec.n_kv_heads * spec.head_dim, spec.n_layers
+    vq2 = spec.weight_dtype == "vq2"
 
-    def mv(rows, cols):
-        return rows * i4_row_bytes(cols, G) + cols * 4 + rows * 4
+    def mv(rows, cols, i4=False):
+        w = rows * i4_row_bytes(cols, G) if (i4 or not vq2) else 2048 + rows * cols // 4
+        return w + cols * 4 + rows * 4
 
     return {"qkv": L * (mv(qd, H) + 2 * mv(kvd, H) - 2 * H * 4),
             "o_proj": L * (mv(H, qd) + H * 4),               # + residual read
             "gate_up": L * (2 * mv(I, H) - H * 4),
             "down": L * (mv(H, I) + I * 4 + H * 4),           # + up read (SwiGLU) + residual
-            "lm_head": mv(spec.vocab, H)}
+            "lm_head": mv(spec.vocab, H, i4=True)}
 
 
 def step_bytes(spec, ctx: int, kv_bytes: int) -> int:
@@ -316,15 +320,41 @@ def step_bytes(spec, ctx: int, kv_bytes: int) -> int:
     return mv + kv
 
 
+# decode workloads: BASELINE configs 2, 3 (full step) and 4
+DECODE_WORKLOADS = {
+    "decode-qwen3-4b": dict(
+        cfg="BASELINE config 4: Qwen3-4B-shaped i4 g64, fp16 KV", preset="QWEN3_4B", kv16=True,
+        ctx=DECODE_CTX, dtype="u4 weights, f32 activations, f16 KV"),
+    "decode-qwen2.5-0.5b": dict(
+        cfg="BASELINE config 2: Qwen2.5-0.5B-shaped i4 g64, fp32 KV", preset="QWEN25_05B",
+        kv16=False, ctx=32, dtype="u4 weights, f32 activations, f32 KV"),
+    "decode-qwen3-0.6b-vq2": dict(
+        cfg="BASELINE config 3 step: Qwen3-0.6B-shaped VQ2 + BiIP on every projection, fp32 KV",
+        preset="QWEN3_06B_VQ2", kv16=False, ctx=32,
+        dtype="2-bit VQ2 weights (i4 embed/lm_head), f32 activations, f32 KV"),
+}
+
+
+def decode_spec(wl: dict, max_seq: int):
+    from dataclasses import replace
+    from tqb200 import model as M
+    base = getattr(M, wl["preset"])
+    # i4 weights as random codes/scales/zeros (config-1 distributions) instead of RTN of
+    # N(0,0.02): same bytes and shapes, built in seconds
+    kw = {"weights": "codes"} if base.weight_dtype == "i4" else {}
+    return replace(base, max_seq_len=max_seq, **kw)
+
+
 def bench_decode(args, rank, pg, pk, pk_kind):
     import torch
     from tqb200 import lib
     from tqb200.model import SynthModel
     lib.load()
     W, K = args.warmup, args.steps
-    ctx = args.ctx
+    wl = DECODE_WORKLOADS[args.workload]
+    ctx = args.ctx if args.ctx is not None else wl["ctx"]
     max_seq = ctx + W + K + 32  # + the e2e (19) and profiled (1) steps after the timed region
-    spec = qwen3_4b_spec(max_seq)
+    spec = decode_spec(wl, max_seq)
     t0 = time.time()
     sm = SynthModel(spec, seed=0)
     t_build = time.time() - t0
@@ -332,9 +362,9 @@ def bench_decode(args, rank, pg, pk, pk_kind):
     tp = {}
     if world > 1:  # tensor parallel: every projection's output rows sharded over the ranks
         tp = {"tp_size": world, "tp_rank": rank, "nccl_id": share_nccl_id(pg, rank)}
-    eng = lib.Engine(sm, max_seq_len=max_seq, kv_fp16=True, **tp)
+    eng = lib.Engine(sm, max_seq_len=max_seq, kv_fp16=wl["kv16"], **tp)
     del sm.tensors  # host copy no longer needed
-    # KV for context 4096: run the engine itself over positions 0..4095-W (greedy from token 1)
+    # KV for the context: run the engine itself over positions 0..ctx-W-1 (greedy)
     rng = np.random.default_rng(1)
     first = int(rng.integers(0, spec.vocab))
     toks, _ = eng.generate(first, ctx - W)
@@ -346,7 +376,7 @@ def bench_decode(args, rank, pg, pk, pk_kind):
     clocks.start()
     barrier(pg)
     torch.cuda.synchronize()
-    toks, dev_ms = eng.generate(tok, K)  # K steps at context 4096.., device-timed
+    toks, dev_ms = eng.generate(tok, K)  # K steps at the context, device-timed
     torch.cuda.synchronize()
     barrier(pg)
     clk = clocks.stop()
@@ -369,19 +399,19 @@ def bench_decode(args, rank, pg, pk, pk_kind):
     mv_ms = sum(prof[k] for k in mvb)
     mv_bytes = sum(mvb.values())
     achieved = mv_bytes / (mv_ms * 1e-3) / 1e9
-    total_bytes = step_bytes(spec, ctx, 2)
+    total_bytes = step_bytes(spec, ctx, 2 if wl["kv16"] else 4)
     # embed, per layer qkv / attention (QK-norm, RoPE and KV append fused) / o_proj /
     # gate_up / down, lm_head (+argmax), the device-side token feed, and with tensor
     # parallelism the cross-rank argmax (NCCL's all-gather kernels are not counted)
     launches = 2 + 5 * spec.n_layers + 1 + (1 if world > 1 else 0)
     out = {
-        "metric": "decode ms/token, batch 1 (BASELINE config 4: Qwen3-4B-shaped i4 g64, fp16 KV, ctx 4096)",
+        "metric": f"decode ms/token, batch 1 ({wl['cfg']}, ctx {ctx})",
         "value": round(ms_step, 4), "unit": "ms/token", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": round(ms_step, 4), "higher_is_better": False, "scaling": "strong",
-        "vs_baseline": None, "dtype": "u4 weights, f32 activations, f16 KV",
-        "data": "synthetic (seeded random i4 codes/scales/zeros; KV filled by the engine's own "
-                "greedy decode over 4096 positions)",
-        "config": {"workload": "decode-qwen3-4b (config 4)", "layers": spec.n_layers,
+        "vs_baseline": None, "dtype": wl["dtype"],
+        "data": f"synthetic (seeded random weights of the named shape; KV filled by the engine's "
+                f"own greedy decode over {ctx} positions)",
+        "config": {"workload": args.workload, "layers": spec.n_layers,
                    "hidden": spec.hidden, "inter": spec.inter, "heads": spec.n_heads,
                    "kv_heads": spec.n_kv_heads, "head_dim": spec.head_dim, "vocab": spec.vocab,
                    "context": ctx, "global_batch": 1,
@@ -392,7 +422,9 @@ def bench_decode(args, rank, pg, pk, pk_kind):
                    "model_build_s": round(t_build, 1)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
                      "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
-                     "peak_source": pk_kind, "kernel": "i4_mv_tma_kernel (all matvecs of a step)",
+                     "peak_source": pk_kind,
+                     "kernel": ("vq2_matvec_kernel" if spec.weight_dtype == "vq2" else "i4_mv_tma_kernel")
+                               + " (all matvecs of a step)",
                      "algorithmic_bytes_per_step": int(mv_bytes),
                      "matvec_ms_per_step": round(mv_ms, 4),
                      "step_vs_hbm_floor": round((total_bytes / (pk["hbm_gbs"] * 1e9) * 1e3) / ms_step, 4)},
@@ -407,17 +439,19 @@ def bench_decode(args, rank, pg, pk, pk_kind):
     return out
 
 
-def ref_decode_rate(threads_note: str = ""):
-    """Reference CPU decode cost per token for config 4 (oracle/_ref: the reference's own
-    QwenModel::forward_token and attention_decode_ref), bounded sample: 2- and 4-layer
-    models of the Qwen3-4B shape give the per-layer and head costs (the step is a sum over
-    layers plus the head, so it extrapolates exactly in layers); attention at context 4096
-    is timed separately with attention_decode_ref and added per layer."""
+def ref_decode_rate(workload: str, ctx: int, threads_note: str = ""):
+    """Reference CPU decode cost per token for a decode workload (oracle/_ref: the
+    reference's own QwenModel::forward_token and attention_decode_ref), bounded sample:
+    2- and 6-layer models of the workload's shape give the per-layer and head costs (the
+    step is a sum over layers plus the head, so it extrapolates exactly in layers);
+    attention at the workload's context is timed separately with attention_decode_ref
+    (fp32 KV: the reference's fp16-KV attention is aarch64-only) and added per layer."""
     import tempfile
     from dataclasses import replace
     from oracle.oracle import Oracle, RefLib
     from tqb200.model import SynthModel
-    base = qwen3_4b_spec(64)
+    wl = DECODE_WORKLOADS[workload]
+    base = decode_spec(wl, 64)
     have_ref = RefLib.available()
     times = {}
     with tempfile.TemporaryDirectory() as td:
@@ -449,17 +483,18 @@ def ref_decode_rate(threads_note: str = ""):
     H, KVH, hd = base.n_heads, base.n_kv_heads, base.head_dim
     rng = np.random.default_rng(0)
     q = rng.normal(size=H * hd).astype(np.float32)
-    kc = rng.normal(size=KVH * DECODE_CTX * hd).astype(np.float32)
-    vc = rng.normal(size=KVH * DECODE_CTX * hd).astype(np.float32)
+    kc = rng.normal(size=KVH * ctx * hd).astype(np.float32)
+    vc = rng.normal(size=KVH * ctx * hd).astype(np.float32)
     t0 = time.perf_counter()
-    lib.attention(q, kc, vc, DECODE_CTX, DECODE_CTX, H, KVH, hd, 0.088)
+    lib.attention(q, kc, vc, ctx, ctx, H, KVH, hd, 0.088)
     t_attn = time.perf_counter() - t0
     total = t_head + base.n_layers * (t_layer + t_attn)
     kind = "reference" if have_ref else "port"
-    sample = (f"forward_token of 2- and 6-layer Qwen3-4B-shaped i4 models at context ~4 "
-              f"(best of 3: {times[2]*1e3:.0f} / {times[6]*1e3:.0f} ms per token) extrapolated to 36 layers, "
-              f"plus attention_decode_ref at context 4096 ({t_attn*1e3:.1f} ms per layer); 1 thread "
-              f"(the reference's x86 kernels are single-threaded){threads_note}")
+    sample = (f"forward_token of 2- and 6-layer {base.name} models at context ~4 "
+              f"(best of 3: {times[2]*1e3:.0f} / {times[6]*1e3:.0f} ms per token) extrapolated to "
+              f"{base.n_layers} layers, plus attention_decode_ref at context {ctx} "
+              f"({t_attn*1e3:.1f} ms per layer); 1 thread (the reference's x86 kernels are "
+              f"single-threaded){threads_note}")
     return total * 1e3, kind, sample
 
 
@@ -469,20 +504,22 @@ def bench_reference_arm(args, rank):
         return None
     threads = cpu_threads()
     if args.workload.startswith("decode"):
+        wl = DECODE_WORKLOADS[args.workload]
+        ctx = args.ctx if args.ctx is not None else wl["ctx"]
         per = []
         for _ in range(max(1, min(args.steps, 2))):
-            ms, kind, sample = ref_decode_rate()
+            ms, kind, sample = ref_decode_rate(args.workload, ctx)
             per.append(ms)
         ms = float(np.median(per))
         return {
             "impl": "reference",
-            "metric": "decode ms/token, batch 1 (BASELINE config 4: Qwen3-4B-shaped i4 g64, fp16 KV, ctx 4096)",
+            "metric": f"decode ms/token, batch 1 ({wl['cfg']}, ctx {ctx})",
             "value": round(ms, 2), "unit": "ms/token", "n_gpus": 0, "steps": len(per),
             "warmup": 0, "ms_per_step": round(ms, 2), "higher_is_better": False,
             "scaling": "strong", "vs_baseline": None,
-            "dtype": "u4 weights, f32 activations (double accumulation), f32 KV",
-            "data": "synthetic (seeded random i4 codes/scales/zeros)",
-            "config": {"workload": "decode-qwen3-4b (config 4)", "context": DECODE_CTX},
+            "dtype": "quantised weights, f32 activations (double accumulation), f32 KV",
+            "data": "synthetic (seeded random weights of the named shape)",
+            "config": {"workload": args.workload, "context": ctx},
             "cpu_baseline": {"value": round(ms, 2), "unit": "ms/token", "cores": 1, "kind": kind,
                              "sample": sample + f"; host has {threads} threads"},
             "e2e": {"value": round(ms, 2), "unit": "ms/token", "h2d_bytes_per_step": 0,
@@ -510,10 +547,11 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="decode-qwen3-4b",
-                    choices=["decode-qwen3-4b", "matvec-i4"])
+                    choices=list(DECODE_WORKLOADS) + ["matvec-i4"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--ctx", type=int, default=DECODE_CTX, help="decode context (KV positions)")
+    ap.add_argument("--ctx", type=int, default=None,
+                    help="decode context in KV positions (default: the workload's)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -541,7 +579,8 @@ def main():
             out["cpu_baseline"] = {"value": round(gbs, 4), "unit": "GB/s", "cores": 1,
                                    "kind": kind, "sample": sample + f" (host has {threads} threads)"}
         elif args.cpu_seconds > 0:
-            ms, kind, sample = ref_decode_rate(f"; host has {threads} threads")
+            ms, kind, sample = ref_decode_rate(args.workload, out["config"]["context"],
+                                               f"; host has {threads} threads")
             out["cpu_baseline"] = {"value": round(ms, 2), "unit": "ms/token", "cores": 1,
                                    "kind": kind, "sample": sample}
         print(json.dumps(out), flush=True)

@@ -415,15 +415,29 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
         if (s_err) break;
         const KV *tile = reinterpret_cast<const KV *>(ring + (size_t)(it % NST) * T * RB);
         const int r0 = (it - nk) * T, rows = min(T, n_copy - r0);
-        for (int r = ts; r < rows; r += TS) {
-            float vv[4];
-            lds_kv<4>(tile + (size_t)r * HD + dg * 4, vv);
+        // four rows per step: their loads are issued before any is used
+        for (int rq = ts; rq < rows; rq += 4 * TS) {
+            float vv[4][4], pp[4][G];
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                const float p = sc[(r0 + r) * G + g];
+            for (int u = 0; u < 4; ++u) {
+                const int r = rq + u * TS;
+                if (r < rows) {
+                    lds_kv<4>(tile + (size_t)r * HD + dg * 4, vv[u]);
 #pragma unroll
-                for (int j = 0; j < 4; ++j) acc[g][j] = fmaf(p, vv[j], acc[g][j]);
+                    for (int g = 0; g < G; ++g) pp[u][g] = sc[(r0 + r) * G + g];
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) vv[u][j] = 0.0f;
+#pragma unroll
+                    for (int g = 0; g < G; ++g) pp[u][g] = 0.0f;
+                }
             }
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+                for (int g = 0; g < G; ++g)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) acc[g][j] = fmaf(pp[u][g], vv[u][j], acc[g][j]);
         }
         __syncthreads();
         if (tid == 0 && it + NST < total) issue(it + NST);
@@ -471,33 +485,34 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
         pl[tid] = err ? 0.0f : s_l[tid];
     }
     cluster.sync();  // every rank's partial is visible cluster-wide
-    // ---- merge over DSMEM.  One parallel pass copies every rank's (m, l) here; the
-    // weights exp(m_s - M) per (split, head) come from that local copy; then each
-    // thread of this rank's output slice reads its ns partials with independent
-    // remote loads.  Empty splits (m_s = -inf, o = 0) weigh 0.
-    float *rm = wgt + kMaxSplit * G;  // [ns][G] remote m
-    float *rl = rm + kMaxSplit * G;   // [ns][G] remote l
-    if (tid < ns * G) {
-        const int s = tid / G, g = tid - s * G;
-        rm[tid] = *cluster.map_shared_rank(pm + g, s);
-        rl[tid] = *cluster.map_shared_rank(pl + g, s);
-    }
-    __syncthreads();
-    if (tid < G) {
-        float M = -INFINITY;
-        for (int s = 0; s < ns; ++s) M = fmaxf(M, rm[s * G + tid]);
-        float L = 0.0f;
-        for (int s = 0; s < ns; ++s) {
-            const float ms = rm[s * G + tid];
-            const float w = ms == -INFINITY ? 0.0f : expf(ms - M);
-            wgt[s * G + tid] = w;
-            L = fmaf(rl[s * G + tid], w, L);
+    // ---- merge over DSMEM.  Thread (g, s) of the first G half-warps reads rank s's
+    // (m, l) for head g; the max, the weights exp(m_s - M) and the weighted l sum are
+    // formed with shuffles inside the 16 lanes of head g.  Each thread of this rank's
+    // output slice then reads its ns partials with independent remote loads.  Empty
+    // splits (m_s = -inf, o = 0) weigh 0.
+    if (tid < (G * kMaxSplit + 31) / 32 * 32) {  // whole warps (the shuffles need all lanes)
+        const int g = tid / kMaxSplit, s = tid - g * kMaxSplit;
+        float m = -INFINITY, l = 0.0f;
+        if (g < G && s < ns) {
+            m = *cluster.map_shared_rank(pm + g, s);
+            l = *cluster.map_shared_rank(pl + g, s);
         }
-        s_l[tid] = L;
+        float M = m;
+#pragma unroll
+        for (int o = kMaxSplit / 2; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        const float w = m == -INFINITY ? 0.0f : expf(m - M);
+        if (g < G && s < ns) wgt[s * G + g] = w;
+        float L = l * w;
+#pragma unroll
+        for (int o = kMaxSplit / 2; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        if (g < G && s == 0) s_l[g] = L;
     }
     __syncthreads();
     const int per = (G * HD + ns - 1) / ns;
-    for (int i = split * per + tid; i < min(G * HD, (split + 1) * per); i += kThreads) {
+    const int i_end = min(G * HD, (split + 1) * per);
+    float res[(G * HD + kThreads - 1) / kThreads];
+    int nres = 0;
+    for (int i = split * per + tid; i < i_end; i += kThreads) {
         const int g = i / HD;
         float o[kMaxSplit];
 #pragma unroll
@@ -506,9 +521,14 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
 #pragma unroll
         for (int s = 0; s < kMaxSplit; ++s)
             if (s < ns) O = fmaf(o[s], wgt[s * G + g], O);
-        P.out[(size_t)kh * G * HD + i] = O / s_l[g];
+        res[nres++] = O / s_l[g];
     }
-    cluster.sync();  // no rank leaves while another still reads its partial
+    // every remote read of this thread is done: tell the cluster, write the output,
+    // and only then wait for the others (no rank leaves while another still reads it)
+    cluster.barrier_arrive();
+    nres = 0;
+    for (int i = split * per + tid; i < i_end; i += kThreads) P.out[(size_t)kh * G * HD + i] = res[nres++];
+    cluster.barrier_wait();
 }
 
 template <typename KV, int HD, int G>
@@ -552,7 +572,10 @@ int launch_t(const AttnArgs &a, cudaStream_t st) {
         P.chunk_max = (a.max_seq + ns - 1) / ns;
         P.scale = a.scale;
         P.tile_rows = std::max(1, std::min(kTileBytes / RB, P.chunk_max));
-        P.stages = std::max(1, std::min(kStages, 2 * ((P.chunk_max + P.tile_rows - 1) / P.tile_rows)));
+        // at most 64 KB of tiles in flight: two CTAs fit an SM, so the clusters of all
+        // KV heads are resident at once
+        P.stages = std::max(1, std::min({kStages, 65536 / (P.tile_rows * RB),
+                                         2 * ((P.chunk_max + P.tile_rows - 1) / P.tile_rows)}));
         const size_t ring = (size_t)P.stages * P.tile_rows * RB;
         const size_t part = ((size_t)TS * G * HD + (size_t)G * HD + 2 * G + 3 * (size_t)kMaxSplit * G) * 4;
         P.stage_region = (int)((std::max(ring, part) + 15) & ~(size_t)15);
@@ -579,11 +602,14 @@ int launch_t(const AttnArgs &a, cudaStream_t st) {
         attr_l[1].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr_l;
         cfg.numAttrs = 1;
+        // prefer a split count whose clusters (one per KV head) are all resident at
+        // once; otherwise take the largest schedulable one
         int nclusters = 0;
         if (cudaOccupancyMaxActiveClusters(&nclusters, k, &cfg) != cudaSuccess || nclusters < 1) {
             cudaGetLastError();
             continue;
         }
+        if (nclusters < a.n_kv_heads && ns > 4) continue;
         cfg.numAttrs = a.pdl ? 2 : 1;
         TQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, k, P));
         return TQB200_OK;
