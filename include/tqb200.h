@@ -81,6 +81,19 @@ int tqb200_dev_matvec_i4_sym(const uint8_t *w, const float *x, float *y, int out
 int tqb200_dev_dequant_i4(const uint8_t *w, int rows, int dim, int group_size, float *out,
                           void *stream);
 
+/* MatmulI4Fn (kernels/dispatch.h:248-249); semantics of matmul_i4_ref
+ * (kernels/matvec/matmul_i4_ref.cpp:53-114): Y[:, n] = W X[:, n] for n < N, X [in_dim x N]
+ * and Y [out_dim x N] column-major (one token per column).  Runs on the tensor cores
+ * (tcgen05, fp32 accumulation of bf16 hi/lo operand splits); group_size must be a
+ * multiple of 32 (TQB200_ERR_INVALID_ARG otherwise). */
+int tqb200_matmul_i4(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim, int n,
+                     int group_size);
+/* Device twin.  `scratch` (16-byte aligned) holds tqb200_matmul_i4_scratch_bytes(in_dim, n)
+ * bytes for the split activation planes; no reference counterpart. */
+size_t tqb200_matmul_i4_scratch_bytes(int in_dim, int n);
+int tqb200_dev_matmul_i4(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim,
+                         int n, int group_size, void *scratch, void *stream);
+
 /* ------------------------------------------------------ VQ2 + BiIP rotation
  * VQ2 tensor: [codebook 256x4 fp16 = 2048 B][one uint8 index per 4 weights, row-major]
  * (runtime/tiny_format.h:91-103).  in_dim % 4 == 0. */

@@ -75,3 +75,8 @@ def test_bad_arguments_rejected_before_device(built):
     assert st == 1  # odd group size
     assert b"group_size" in L.tqb200_last_error()
     assert L.tqb200_status_string(5) == b"device wait timed out"
+    # the tensor-core matmul needs whole 32-column groups
+    yy = np.zeros(8, np.float32)
+    st = L.tqb200_matmul_i4(np.zeros(64, np.uint8), np.ones(32, np.float32), yy, 1, 16, 2, 16)
+    assert st == 1 and b"multiple of 32" in L.tqb200_last_error()
+    assert L.tqb200_matmul_i4_scratch_bytes(2048, 37) == 2 * 32 * 64 * 48 * 2

@@ -303,6 +303,52 @@ int tqb200_dev_dequant_i4(const uint8_t *w, int rows, int dim, int group_size, f
     return launch_i4_dequant(w, rows, dim, group_size, out, (cudaStream_t)stream);
 }
 
+// ------------------------------------------------------------------ i4 matmul
+static int check_mm(int M, int K, int N, int G) {
+    TQ_TRY(check_i4(M, K, G));
+    TQ_CHECK_ARG(N >= 0, "matmul_i4: bad column count %d", N);
+    TQ_CHECK_ARG(G % 32 == 0, "matmul_i4: group_size %d is not a multiple of 32", G);
+    return TQB200_OK;
+}
+
+int tqb200_matmul_i4(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim, int n,
+                     int group_size) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    TQ_TRY(check_mm(out_dim, in_dim, n, group_size));
+    TQ_CHECK_ARG(w && x && y, "null pointer");
+    if (out_dim == 0 || n == 0) return TQB200_OK;
+    TQ_TRY(ensure_device());
+    void *dw, *dx, *dy, *ds, *dst;
+    TQ_TRY(upload_weight(0, w, i4_bytes(out_dim, in_dim, group_size), &dw));
+    TQ_TRY(upload(3, x, (size_t)in_dim * n * 4, &dx));
+    TQ_TRY(scratch(4, (size_t)out_dim * n * 4, &dy));
+    TQ_TRY(scratch(9, mm_x_planes_bytes(in_dim, n), &ds));
+    TQ_TRY(scratch(10, 16, &dst));
+    TQ_CUDA_TRY(cudaMemsetAsync(dst, 0, 4, g_ctx.stream));
+    TQ_TRY(launch_matmul_i4((const uint8_t *)dw, (const float *)dx, (float *)dy, out_dim, in_dim,
+                            n, group_size, ds, (int *)dst, g_ctx.stream));
+    TQ_TRY(download(y, dy, (size_t)out_dim * n * 4));
+    int hst = 0;
+    TQ_TRY(download(&hst, dst, 4));
+    TQ_TRY(finish());
+    if (hst != 0) return set_error(TQB200_ERR_TIMEOUT, "matmul_i4: device status %d", hst);
+    return TQB200_OK;
+}
+
+size_t tqb200_matmul_i4_scratch_bytes(int in_dim, int n) {
+    if (in_dim <= 0 || n < 0) return 0;
+    return mm_x_planes_bytes(in_dim, n);
+}
+
+int tqb200_dev_matmul_i4(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim,
+                         int n, int group_size, void *scratch, void *stream) {
+    TQ_TRY(check_mm(out_dim, in_dim, n, group_size));
+    TQ_CHECK_ARG(w && x && y && scratch, "null pointer");
+    TQ_CHECK_ARG(((uintptr_t)scratch & 15) == 0, "matmul_i4: scratch not 16-byte aligned");
+    return launch_matmul_i4(w, x, y, out_dim, in_dim, n, group_size, scratch, nullptr,
+                            (cudaStream_t)stream);
+}
+
 // ------------------------------------------------------------------ VQ2 + BiIP
 static int vq2_host(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim,
                     const float *scale, const float *sign, int bs) {

@@ -67,6 +67,28 @@ int launch_i4_matvec_sym(const uint8_t *w, const float *x, float *y, int rows, i
 int launch_i4_dequant(const uint8_t *w, int rows, int dim, int group_size, float *out,
                       cudaStream_t stream);
 
+// ------------------------------------------------------------------ i4 matmul (tensor cores)
+// One weight matrix of a (grouped) tcgen05 matmul: Y[:, n] = W X[:, n] for N columns.
+struct MmJob {
+    const uint8_t *w;     // [M] interleaved i4 rows
+    float *y;             // column n at y + n * ldy
+    int M, N, ldy;
+    int tile_begin;       // first CTA of this job (jobs in CTA order)
+    long long b_off;      // offset (bf16 elements) of this job's X planes
+};
+// bytes of the two bf16 X planes (hi, lo) for K x N
+size_t mm_x_planes_bytes(int K, int N);
+int mm_tile_width(int M, int N);
+// X [K x N] (column n at x + (cols ? cols[n] : n) * ldx) -> the bf16 hi/lo planes
+int launch_mm_pack_x(const float *x, const int *cols, int ldx, int K, int N, uint16_t *bhi,
+                     uint16_t *blo, cudaStream_t st);
+int launch_matmul_i4_grouped(const MmJob *host_jobs, const MmJob *dev_jobs, int n_jobs, int K,
+                             int G, int nt, const uint16_t *bhi, const uint16_t *blo,
+                             int total_tiles, int *status, cudaStream_t st);
+// Y = W X (matmul_i4_ref semantics); scratch holds mm_x_planes_bytes(K, N) bytes
+int launch_matmul_i4(const uint8_t *w, const float *x, float *y, int M, int K, int N, int G,
+                     void *scratch, int *status, cudaStream_t st);
+
 // ------------------------------------------------------------------ VQ2 + BiIP
 // One VQ2 matrix of a launch; each job has its own codebook and BiIP rotation.
 struct VqJob {

@@ -24,6 +24,10 @@
 #include "ref_ops.h"
 #include "tqb200.h"
 
+namespace tinyqwen {
+int g_matmul_calls = 0;  // calls that reached matmul_i4_b200 (read by drop_in_check)
+}
+
 namespace {
 
 [[noreturn]] void die(const char *what) {
@@ -46,6 +50,13 @@ void matvec_pair_i4_b200(const uint8_t *w1, const uint8_t *w2, const float *x, f
 void matvec_qkv_i4_b200(const uint8_t *wq, const uint8_t *wk, const uint8_t *wv, const float *x,
                         float *yq, float *yk, float *yv, int qd, int kvd, int in, int g) {
     if (tqb200_matvec_qkv_i4(wq, wk, wv, x, yq, yk, yv, qd, kvd, in, g)) die("matvec_qkv_i4");
+}
+// MatmulI4Fn (kernels/dispatch.h:248-249).  The reference has no by-name selector for
+// it: the first registration becomes current (kernels/dispatch.cpp:651-660), so this one
+// is current when this file is linked ahead of the reference's kernel objects.
+void matmul_i4_b200(const uint8_t *w, const float *x, float *y, int M, int K, int N, int g) {
+    ++tinyqwen::g_matmul_calls;
+    if (tqb200_matmul_i4(w, x, y, M, K, N, g)) die("matmul_i4");
 }
 void matvec_vq2_b200(const uint8_t *w, const float *x, float *y, int out, int in) {
     if (tqb200_matvec_vq2(w, x, y, out, in)) die("matvec_vq2");
@@ -217,6 +228,7 @@ TINYQWEN_MATVEC_I4_VARIANT(matvec_i4_b200, "b200");
 TINYQWEN_MATVEC_I4_PAIR_VARIANT(matvec_pair_i4_b200, "b200");
 TINYQWEN_MATVEC_QKV_I4_VARIANT(matvec_qkv_i4_b200, "b200");
 TINYQWEN_MATVEC_VQ2_VARIANT(matvec_vq2_b200, "b200");
+TINYQWEN_MATMUL_I4_VARIANT(matmul_i4_b200, "b200");
 TINYQWEN_BIIP_ROTATE_VARIANT(biip_b200, "b200");
 TINYQWEN_RMSNORM_VARIANT(rmsnorm_b200, "b200");
 TINYQWEN_ROPE_VARIANT(rope_b200, "b200");

@@ -6,6 +6,12 @@
 //         engine  the GPU decode registry with --engine b200 (gpu_decode_* entries)
 // Prints the greedy token after every fed token on one line, as main.cpp's decode
 // loop produces them (runtime/main.cpp:1009-1041).
+//
+//   drop_in_check <data.bin> matmul <M> <K> <N> <G>
+//   tinyqwen::matmul_i4 through the reference's dispatcher (the prefill contraction,
+//   QwenModel::mm -> CPUBackend::matmul) on data.bin = [W i4 rows][X, N columns of K
+//   floats]; writes Y (N columns of M floats) to data.bin.y and prints how many calls
+//   reached the b200 variant.
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -18,7 +24,38 @@
 #include "profiler.h"
 #include "qwen_model.h"
 
+namespace tinyqwen {
+extern int g_matmul_calls;  // b200_variants.cpp
+}
+
+static int run_matmul(const std::string &path, int M, int K, int N, int G) {
+    const size_t wb = (size_t)M * ((K + G - 1) / G) * (4 + G / 2);
+    std::vector<uint8_t> w(wb);
+    std::vector<float> x((size_t)K * N), y((size_t)M * N);
+    FILE *f = std::fopen(path.c_str(), "rb");
+    if (!f || std::fread(w.data(), 1, wb, f) != wb ||
+        std::fread(x.data(), 4, x.size(), f) != x.size()) {
+        std::fprintf(stderr, "matmul: cannot read %s\n", path.c_str());
+        if (f) std::fclose(f);
+        return 1;
+    }
+    std::fclose(f);
+    tinyqwen::matmul_i4(w.data(), x.data(), y.data(), M, K, N, G);
+    f = std::fopen((path + ".y").c_str(), "wb");
+    if (!f || std::fwrite(y.data(), 4, y.size(), f) != y.size()) {
+        std::fprintf(stderr, "matmul: cannot write %s.y\n", path.c_str());
+        if (f) std::fclose(f);
+        return 1;
+    }
+    std::fclose(f);
+    std::printf("b200 matmul calls %d\n", tinyqwen::g_matmul_calls);
+    return 0;
+}
+
 int main(int argc, char **argv) {
+    if (argc == 7 && std::strcmp(argv[2], "matmul") == 0)
+        return run_matmul(argv[1], std::atoi(argv[3]), std::atoi(argv[4]), std::atoi(argv[5]),
+                          std::atoi(argv[6]));
     if (argc < 6) {
         std::fprintf(stderr, "usage: %s model mode max_seq n_new tok...\n", argv[0]);
         return 2;

@@ -49,6 +49,9 @@ PROTOTYPES = {
     "tqb200_dev_matvec_i4": ([_vp, _vp, _vp, _i, _i, _i, _vp], _i),
     "tqb200_dev_matvec_i4_sym": ([_vp, _vp, _vp, _i, _i, _i, _vp], _i),
     "tqb200_dev_dequant_i4": ([_vp, _i, _i, _i, _vp, _vp], _i),
+    "tqb200_matmul_i4": ([_u8, _f, _f, _i, _i, _i, _i], _i),
+    "tqb200_matmul_i4_scratch_bytes": ([_i, _i], C.c_size_t),
+    "tqb200_dev_matmul_i4": ([_vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp], _i),
     "tqb200_matvec_vq2": ([_u8, _f, _f, _i, _i], _i),
     "tqb200_biip_rotate": ([_f, _f, _i, _vp, _vp, _i], _i),
     "tqb200_matvec_vq2_rot": ([_u8, _f, _f, _i, _i, _vp, _vp, _i], _i),
@@ -129,6 +132,13 @@ def matvec_i4(w, x, out_dim: int, in_dim: int, group_size: int) -> np.ndarray:
     y = np.zeros(out_dim, np.float32)
     _check(load().tqb200_matvec_i4(_u8a(w), _f32(x), y, out_dim, in_dim, group_size))
     return y
+
+
+def matmul_i4(w, x_cols, M: int, K: int, N: int, group_size: int) -> np.ndarray:
+    """MatmulI4Fn: x_cols is X column-major ([N][K] in memory); returns Y as [N][M]."""
+    y = np.zeros(M * N, np.float32)
+    _check(load().tqb200_matmul_i4(_u8a(w), _f32(x_cols), y, M, K, N, group_size))
+    return y.reshape(N, M)
 
 
 def matvec_pair_i4(w1, w2, x, out_dim: int, in_dim: int, group_size: int):
