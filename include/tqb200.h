@@ -84,13 +84,15 @@ int tqb200_dev_dequant_i4(const uint8_t *w, int rows, int dim, int group_size, f
 /* MatmulI4Fn (kernels/dispatch.h:248-249); semantics of matmul_i4_ref
  * (kernels/matvec/matmul_i4_ref.cpp:53-114): Y[:, n] = W X[:, n] for n < N, X [in_dim x N]
  * and Y [out_dim x N] column-major (one token per column).  Runs on the tensor cores
- * (tcgen05, fp32 accumulation of bf16 hi/lo operand splits); group_size must be a
- * multiple of 32 (TQB200_ERR_INVALID_ARG otherwise). */
+ * (tcgen05: exact bf16 codes against bf16 hi/lo activations, per-group partials in TMEM,
+ * fp32 accumulation); group_size 32, 64 or 128 (TQB200_ERR_INVALID_ARG otherwise). */
 int tqb200_matmul_i4(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim, int n,
                      int group_size);
-/* Device twin.  `scratch` (16-byte aligned) holds tqb200_matmul_i4_scratch_bytes(in_dim, n)
- * bytes for the split activation planes; no reference counterpart. */
-size_t tqb200_matmul_i4_scratch_bytes(int in_dim, int n);
+/* Device twin.  `scratch` (16-byte aligned) holds
+ * tqb200_matmul_i4_scratch_bytes(out_dim, in_dim, n, group_size) bytes for the weights in
+ * the kernel's tile order and the split activations (0 for an unsupported group size);
+ * no reference counterpart. */
+size_t tqb200_matmul_i4_scratch_bytes(int out_dim, int in_dim, int n, int group_size);
 int tqb200_dev_matmul_i4(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim,
                          int n, int group_size, void *scratch, void *stream);
 

@@ -78,5 +78,8 @@ def test_bad_arguments_rejected_before_device(built):
     # the tensor-core matmul needs whole 32-column groups
     yy = np.zeros(8, np.float32)
     st = L.tqb200_matmul_i4(np.zeros(64, np.uint8), np.ones(32, np.float32), yy, 1, 16, 2, 16)
-    assert st == 1 and b"multiple of 32" in L.tqb200_last_error()
-    assert L.tqb200_matmul_i4_scratch_bytes(2048, 37) == 2 * 32 * 64 * 48 * 2
+    assert st == 1 and b"not 32, 64 or 128" in L.tqb200_last_error()
+    # weights in 256-row tile blocks, then two bf16 planes of (G + 16) slots per group
+    # and 16-padded column
+    assert L.tqb200_matmul_i4_scratch_bytes(768, 2048, 37, 64) == 3 * 32 * 256 * 36 + 2 * 32 * 80 * 48 * 2
+    assert L.tqb200_matmul_i4_scratch_bytes(768, 2048, 37, 48) == 0

@@ -83,7 +83,7 @@ def test_dev_matmul_i4_device_pointers(tq, oracle):
     dx = torch.from_numpy(x).cuda()
     dy = torch.full((N, M), float("nan"), device="cuda")
     L = tq.load()
-    sb = L.tqb200_matmul_i4_scratch_bytes(K, N)
+    sb = L.tqb200_matmul_i4_scratch_bytes(M, K, N, G)
     scr = torch.empty(sb, dtype=torch.uint8, device="cuda")
     st = torch.cuda.current_stream().cuda_stream
     assert L.tqb200_dev_matmul_i4(dw.data_ptr(), dx.data_ptr(), dy.data_ptr(), M, K, N, G,

@@ -536,7 +536,8 @@ int launch_t(const AttnArgs &a, cudaStream_t st) {
     constexpr int RB = HD * (int)sizeof(KV);
     constexpr int TS = kThreads / (HD / 4);
     auto k = attn_tma_kernel<KV, HD, G>;
-    static std::atomic<unsigned long long> attr{0}, cluster_attr{0};
+    static KernelSmem attr;
+    static std::atomic<unsigned long long> cluster_attr{0};
     int smem_max = 0;
     TQ_CUDA_TRY(smem_limit_once(k, attr, &smem_max));
     {

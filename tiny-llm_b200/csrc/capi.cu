@@ -307,7 +307,7 @@ int tqb200_dev_dequant_i4(const uint8_t *w, int rows, int dim, int group_size, f
 static int check_mm(int M, int K, int N, int G) {
     TQ_TRY(check_i4(M, K, G));
     TQ_CHECK_ARG(N >= 0, "matmul_i4: bad column count %d", N);
-    TQ_CHECK_ARG(G % 32 == 0, "matmul_i4: group_size %d is not a multiple of 32", G);
+    TQ_CHECK_ARG(mm_group_supported(G), "matmul_i4: group_size %d is not 32, 64 or 128", G);
     return TQB200_OK;
 }
 
@@ -322,7 +322,7 @@ int tqb200_matmul_i4(const uint8_t *w, const float *x, float *y, int out_dim, in
     TQ_TRY(upload_weight(0, w, i4_bytes(out_dim, in_dim, group_size), &dw));
     TQ_TRY(upload(3, x, (size_t)in_dim * n * 4, &dx));
     TQ_TRY(scratch(4, (size_t)out_dim * n * 4, &dy));
-    TQ_TRY(scratch(9, mm_x_planes_bytes(in_dim, n), &ds));
+    TQ_TRY(scratch(9, mm_scratch_bytes(out_dim, in_dim, n, group_size), &ds));
     TQ_TRY(scratch(10, 16, &dst));
     TQ_CUDA_TRY(cudaMemsetAsync(dst, 0, 4, g_ctx.stream));
     TQ_TRY(launch_matmul_i4((const uint8_t *)dw, (const float *)dx, (float *)dy, out_dim, in_dim,
@@ -335,9 +335,9 @@ int tqb200_matmul_i4(const uint8_t *w, const float *x, float *y, int out_dim, in
     return TQB200_OK;
 }
 
-size_t tqb200_matmul_i4_scratch_bytes(int in_dim, int n) {
-    if (in_dim <= 0 || n < 0) return 0;
-    return mm_x_planes_bytes(in_dim, n);
+size_t tqb200_matmul_i4_scratch_bytes(int out_dim, int in_dim, int n, int group_size) {
+    if (out_dim < 0 || in_dim <= 0 || n < 0) return 0;
+    return mm_scratch_bytes(out_dim, in_dim, n, group_size);
 }
 
 int tqb200_dev_matmul_i4(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim,

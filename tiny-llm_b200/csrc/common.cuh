@@ -42,23 +42,36 @@ inline int max_dyn_smem() {
     return v;
 }
 
+// Per-kernel record of the devices whose dynamic shared-memory limit has been raised,
+// with the limit itself, so later launches skip the attribute queries.
+struct KernelSmem {
+    std::atomic<unsigned long long> mask{0};
+    std::atomic<int> limit[64] = {};
+};
+
 // Raises kernel k's dynamic shared-memory limit to the most it can use on the current
-// device (the opt-in limit minus its static shared memory), once per device; `mask`
-// records the devices done.  *limit receives that most.
+// device (the opt-in limit minus its static shared memory), once per device.  *limit
+// receives that most.
 template <typename Kern>
-inline cudaError_t smem_limit_once(Kern k, std::atomic<unsigned long long> &mask, int *limit) {
+inline cudaError_t smem_limit_once(Kern k, KernelSmem &ks, int *limit) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (ks.mask.load() & bit) {
+        *limit = ks.limit[dev & 63].load();
+        return cudaSuccess;
+    }
     cudaFuncAttributes fa;
     e = cudaFuncGetAttributes(&fa, k);
     if (e != cudaSuccess) return e;
     const int lim = max_dyn_smem() - (int)fa.sharedSizeBytes;
     *limit = lim;
-    const unsigned long long bit = 1ull << (dev & 63);
-    if (mask.load() & bit) return cudaSuccess;
     e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
-    if (e == cudaSuccess) mask.fetch_or(bit);
+    if (e == cudaSuccess) {
+        ks.limit[dev & 63].store(lim);
+        ks.mask.fetch_or(bit);
+    }
     return e;
 }
 
@@ -159,6 +172,26 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, long l
             " selp.u32 %0, 1, 0, p;\n}\n"
             : "=r"(done)
             : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if (clock64() - t0 > max_cycles) return false;
+    }
+}
+
+// As mbar_wait, but each probe may suspend the thread for up to `hint_ns` until the phase
+// completes (mbarrier.try_wait's suspend-time hint), so waiting warps leave the issue
+// slots of their scheduler to the warps that are working.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, long long max_cycles,
+                                                uint32_t hint_ns = 10000u) {
+    const uint32_t a = smem_u32(bar);
+    const long long t0 = clock64();
+    while (true) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+            " selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(a), "r"(parity), "r"(hint_ns)
             : "memory");
         if (done) return true;
         if (clock64() - t0 > max_cycles) return false;

@@ -807,7 +807,7 @@ int grid_for(Kern k, int block, size_t smem, int work) {
 template <int SEG>
 int launch_tma(const MvParams &P, const Shape &L, int passes, bool pdl, cudaStream_t st) {
     auto k = i4_mv_tma_kernel<SEG>;
-    static std::atomic<unsigned long long> attr_set{0};
+    static KernelSmem attr_set;
     int smem_max = 0;
     TQ_CUDA_TRY(smem_limit_once(k, attr_set, &smem_max));
     TQ_CHECK_ARG(L.smem <= (size_t)smem_max, "i4 matvec: %zu B of shared memory above the %d B limit",

@@ -70,22 +70,27 @@ int launch_i4_dequant(const uint8_t *w, int rows, int dim, int group_size, float
 // ------------------------------------------------------------------ i4 matmul (tensor cores)
 // One weight matrix of a (grouped) tcgen05 matmul: Y[:, n] = W X[:, n] for N columns.
 struct MmJob {
-    const uint8_t *w;     // [M] interleaved i4 rows
+    const uint8_t *w;     // tile-contiguous weights (launch_mm_repack_w)
     float *y;             // column n at y + n * ldy
     int M, N, ldy;
     int tile_begin;       // first CTA of this job (jobs in CTA order)
     long long b_off;      // offset (bf16 elements) of this job's X planes
 };
-// bytes of the two bf16 X planes (hi, lo) for K x N
-size_t mm_x_planes_bytes(int K, int N);
+bool mm_group_supported(int G);  // the tensor-core path covers G = 32, 64, 128
+// bytes of the two bf16 X planes (hi, lo) for K x N at group size G
+size_t mm_x_planes_bytes(int K, int N, int G);
+// interleaved i4 rows -> the GEMM's tile-contiguous weight blocks (same bytes, permuted)
+size_t mm_repacked_bytes(int M, int K, int G);
+int launch_mm_repack_w(const uint8_t *w, int M, int K, int G, uint8_t *out, cudaStream_t st);
+size_t mm_scratch_bytes(int M, int K, int N, int G);  // launch_matmul_i4's scratch
 int mm_tile_width(int M, int N);
 // X [K x N] (column n at x + (cols ? cols[n] : n) * ldx) -> the bf16 hi/lo planes
-int launch_mm_pack_x(const float *x, const int *cols, int ldx, int K, int N, uint16_t *bhi,
-                     uint16_t *blo, cudaStream_t st);
+int launch_mm_pack_x(const float *x, const int *cols, int ldx, int K, int N, int G,
+                     uint16_t *bhi, uint16_t *blo, cudaStream_t st);
 int launch_matmul_i4_grouped(const MmJob *host_jobs, const MmJob *dev_jobs, int n_jobs, int K,
                              int G, int nt, const uint16_t *bhi, const uint16_t *blo,
                              int total_tiles, int *status, cudaStream_t st);
-// Y = W X (matmul_i4_ref semantics); scratch holds mm_x_planes_bytes(K, N) bytes
+// Y = W X (matmul_i4_ref semantics); scratch holds mm_scratch_bytes(M, K, N, G) bytes
 int launch_matmul_i4(const uint8_t *w, const float *x, float *y, int M, int K, int N, int G,
                      void *scratch, int *status, cudaStream_t st);
 

@@ -1,5 +1,5 @@
 // matmul_i4_tc.cu — batched i4 (HQQ/RTN group-quantised) matmul on the sm_100a tensor
-// cores (tcgen05.mma, accumulator in TMEM).
+// cores (tcgen05.mma, accumulators in TMEM).
 //
 // Reference semantics: matmul_i4_ref (kernels/matvec/matmul_i4_ref.cpp:53-114):
 //   Y[:, n] = matvec_i4(W, X[:, n]) for every column n, X [K, N] and Y [M, N] column-major
@@ -7,25 +7,35 @@
 // and the products accumulated in double.
 //
 // Design (one CTA = a tile of 128 weight rows x NT token columns, all of K):
-//  * The tensor cores cannot apply a per-(row, group) scale inside the K reduction, so
-//    the weights are dequantised into the MMA operand: w = ((float)q - z) * s exactly as
-//    the reference (fp32), then split w = hi + lo into two bf16 values.  X is split the
-//    same way by a small pre-pass, and Y = Whi Xhi + Whi Xlo + Wlo Xhi with fp32
-//    accumulation in TMEM (three kind::f16 MMAs per K step; the dropped Wlo Xlo term and
-//    the two rounding residues are ~2^-17 of each product, far inside the 1e-4 bound).
-//  * Dequantisation by table: for each (row, group) the 16 possible weights are built
-//    once (hi|lo packed in one 32-bit word) in shared memory, and each nibble becomes
-//    one shared-memory lookup plus one byte permute for the hi and lo operand words.
-//  * Roles: warps 0-7 dequantise (thread = row r, K half h of a 64-wide stage) and
-//    afterwards drain TMEM in the epilogue; warp 8 allocates TMEM and one of its lanes
-//    issues the MMAs.  The X operand planes of a stage arrive by 1-D bulk copies (TMA)
-//    issued by thread 0; stages are handed over by mbarriers (full: 8 producer warps +
-//    the copy bytes; empty: tcgen05.commit after the stage's MMAs).
+//  * Group partials on the tensor cores.  With s, z the group's scale and zero,
+//        y = sum_g s_g * P_g,   P_g = sum_{k in g} q_k x_k - z_g X_g,   X_g = sum_{k in g} x_k.
+//    The codes q (0..15) are exact in bf16, so the A operand is the raw nibbles widened
+//    with one LOP3 (0x4300 | q is bf16 128 + q) and one packed bf16 subtract of 128: no
+//    dequantisation arithmetic and no rounding.  X is split into bf16 hi + lo (two MMAs
+//    per K step, the lo residue ~2^-17 of x).  The zero term rides in the same MMA as
+//    one extra K step of 16 slots per group: A = -(z1, z1, z1, z2, z2, z2) (z = z1 + z2
+//    exactly, z is binary16) against B = (X1, X2, X3, X1, X2, X3) (X_g = X1 + X2 + X3,
+//    three bf16 parts of the fp32 group sum), so each group's P_g lands in TMEM whole.
+//  * Epilogue per group: 8 warps read P_g from TMEM (double-buffered accumulators, so the
+//    MMAs of group g+1 overlap the read of group g) and fold y += s_g * P_g in fp32
+//    registers; one FFMA per output and group.
+//  * Roles: warps 0-3 build the A operand (thread = weight row) from nibble words fetched
+//    one group ahead; thread 0 also issues the two 1-D bulk copies (TMA) of the stage's
+//    X planes, which a pre-pass kernel lays out in the MMA's shared-memory order.
+//    Warps 4-11 are the epilogue; warp 12 allocates TMEM and one lane issues the MMAs.
+//    Stages (one quantisation group each) are handed over with mbarriers: full (4
+//    producer warps + the copy bytes), empty (tcgen05.commit), tmem_full (commit) and
+//    tmem_empty (8 epilogue warps).
 //  * Operand layout in shared memory: the canonical K-major, no-swizzle UMMA layout of
-//    8-row x 16-byte core matrices, core matrices of one 8-row group adjacent along K
-//    (leading byte offset 128) and 8-row groups 1024 bytes apart (stride byte offset).
-//  * Every mbarrier wait is bounded; on a timeout the kernel records an error word,
-//    stops issuing work, drains what it issued and frees its TMEM before returning.
+//    8-row x 16-byte core matrices, the core matrices of one 8-row group adjacent along
+//    K (leading byte offset 128), 8-row groups (G+16)*16 bytes apart (stride offset).
+//    Within every 16-byte core-matrix row the 8 K positions hold columns
+//    (0, 4, 1, 5, 2, 6, 3, 7) of that 8-column chunk, the order the nibble widening
+//    produces; X is stored in the same order, so the dot products are unchanged.
+//  * Every wait is bounded; on a timeout the kernel records an error word, stops issuing,
+//    waits (bounded) for what it issued and frees its TMEM before returning.
+// Accuracy: products carry the x residue (~2^-17 relative), the zero term ~2^-24, and
+// accumulation is fp32 (the reference's is double): ~1e-5 relative, inside 1e-4.
 #include <algorithm>
 #include <atomic>
 
@@ -39,22 +49,30 @@ namespace tqb200 {
 namespace {
 
 constexpr int kMmRows = 128;       // UMMA M
-constexpr int kMmKs = 64;          // K per pipeline stage
-constexpr int kMmProducers = 256;  // warps 0-7
-constexpr int kMmThreads = kMmProducers + 32;
+constexpr int kProdWarps = 8;      // warps 0-7: A operand, one weight row per thread
+constexpr int kEpiWarps = 8;       // warps 8-15: TMEM -> registers -> Y
+constexpr int kMmaWarp = kProdWarps + kEpiWarps;  // warp 16: TMEM allocation, MMA issue
+constexpr int kLoadWarp = kMmaWarp + 1;           // warp 17: bulk copies (TMA)
+constexpr int kMmThreads = (kLoadWarp + 1) * 32;
 constexpr int kMmMaxStages = 4;
-constexpr uint32_t kABytes = kMmRows * kMmKs * 2;  // one bf16 plane of a stage (16 KB)
-constexpr uint32_t kLutBytes = 16 * kMmProducers * 4;  // one buffer (16 KB)
+constexpr int kTileRows = 2 * kMmRows;  // weight rows per CTA: two accumulators share X
+constexpr int kMmMaxCols = 64;     // tile width limit (epilogue registers)
+// group scales handed from producers to the epilogue: a slot is rewritten only after the
+// epilogue has read it (the producer's stage wait orders it behind MMA i-S, which waited
+// for the epilogue's drain of group i-S-2)
+constexpr int kSclRing = kMmMaxStages + 3;
+constexpr int kMaxRaw = 4;         // weight blocks staged ahead, at most
 
 struct MmParams {
     MmJob job0;            // used when jobs == nullptr
     const MmJob *jobs;     // device array (grouped launch) or nullptr
     int n_jobs;
-    int K, G, ks;          // ks = ceil(K / 64) stages
-    int nt;                // tile width in columns (multiple of 16, <= 256)
+    int K, ng;             // ng = ceil(K / G) groups = pipeline stages of a tile
+    int nt;                // tile width in columns (multiple of 16, <= kMmMaxCols)
     const uint16_t *bhi, *blo;  // X planes (bf16 bits), see mm_pack_x_kernel
     int stages;
-    uint32_t stage_bytes;  // 2 * kABytes + 2 * nt * 128
+    uint32_t stage_bytes;
+    int raw_depth;         // groups of raw weight bytes staged ahead (2..4)
     uint32_t tmem_cols;
     int *status;
 };
@@ -112,17 +130,31 @@ __device__ __forceinline__ bool producers_sync_or(bool pred) {
         "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n bar.red.or.pred p, 1, %2, q;\n"
         " selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(r)
-        : "r"((uint32_t)pred), "n"(kMmProducers)
+        : "r"((uint32_t)pred), "n"(kProdWarps * 32)
         : "memory");
     return r != 0;
 }
 
-// bf16 hi | lo split of an fp32 value, hi in the low half of the word.
-__device__ __forceinline__ uint32_t split_bf16(float v) {
-    const __nv_bfloat16 hi = __float2bfloat16_rn(v);
-    const float r = __fsub_rn(v, __bfloat162float(hi));
-    const __nv_bfloat16 lo = __float2bfloat16_rn(r);
-    return (uint32_t)__bfloat16_as_ushort(hi) | ((uint32_t)__bfloat16_as_ushort(lo) << 16);
+// 8 TMEM columns of this warp's 32 lanes starting at `taddr`.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float *v) {
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                   "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr)
+                 : "memory");
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint16_t bf16_bits(float v) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+}
+__device__ __forceinline__ float bf16_val(uint16_t b) {
+    return __bfloat162float(__ushort_as_bfloat16(b));
 }
 
 __device__ __forceinline__ const MmJob &job_of(const MmParams &P, int j) {
@@ -131,54 +163,108 @@ __device__ __forceinline__ const MmJob &job_of(const MmParams &P, int j) {
 
 // ---------------------------------------------------------------- X pre-pass
 // X (column n at x + col(n) * ldx, K floats) -> two bf16 planes (hi, lo) laid out
-// [stage][n/8][kc][n%8][8]: stage = k/64, kc = (k%64)/8, i.e. every (stage, 8-column
-// block) is one kilobyte holding eight 8x16-byte core matrices of the K-major UMMA
-// layout.  Columns >= N and k >= K are zero.  One thread per 8-k chunk of a column.
+// [group g][n/8][kc][n%8][8 positions], kc < (G+16)/8: every (group, 8-column block) is
+// (G+16)*16 bytes of K-major core matrices.  Chunks kc < G/8 hold columns
+// g*G + 8*kc + (0,4,1,5,2,6,3,7); chunk G/8 of the hi plane holds the zero-term operand
+// (X1, X2, X3, X1, X2, X3, 0, 0) of the group sum X_g = sum x (fp32, k < K); everything
+// else (columns >= N, k >= K, the lo plane's extra chunks) is zero.
+// One thread per (group, column).
+template <int G>
 __global__ void mm_pack_x_kernel(const float *__restrict__ x, const int *__restrict__ cols, int ldx,
-                                 int K, int N, int npad, int ks, uint16_t *__restrict__ bhi,
+                                 int K, int N, int npad, int ng, uint16_t *__restrict__ bhi,
                                  uint16_t *__restrict__ blo) {
-    const long long total = (long long)npad * ks * 8;
+    constexpr int CK = (G + 16) / 8;
+    const long long total = (long long)npad * ng;
     for (long long c = blockIdx.x * (long long)blockDim.x + threadIdx.x; c < total;
          c += (long long)gridDim.x * blockDim.x) {
-        // c = ((stage * npad/8 + nb) * 8 + kc) * 8 + n%8: consecutive threads write
-        // consecutive 16-byte rows of a core matrix
-        const int n8 = (int)(c & 7);
-        const long long r = c >> 3;
-        const int kc = (int)(r & 7);
-        const long long sb = r >> 3;
-        const int nb = (int)(sb % (npad / 8));
-        const int st = (int)(sb / (npad / 8));
-        const int n = nb * 8 + n8;
-        const int k0 = st * kMmKs + kc * 8;
-        uint32_t w[8];
-        if (n < N) {
-            const float *src = x + (size_t)(cols ? cols[n] : n) * ldx;
+        const int n = (int)(c % npad);
+        const int g = (int)(c / npad);
+        const size_t base = ((size_t)g * (npad / 8) + n / 8) * CK * 64 + (size_t)(n % 8) * 8;
+        uint4 *dh = reinterpret_cast<uint4 *>(bhi + base);  // chunk kc at dh[kc * 8]
+        uint4 *dl = reinterpret_cast<uint4 *>(blo + base);
+        const float *src = n < N ? x + (size_t)(cols ? cols[n] : n) * ldx : nullptr;
+        float xs = 0.0f;
+#pragma unroll 1
+        for (int kc = 0; kc < G / 8; ++kc) {
+            uint32_t h[4], l[4];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) w[e] = k0 + e < K ? split_bf16(src[k0 + e]) : 0u;
-        } else {
+            for (int p = 0; p < 4; ++p) {
+                float v[2];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) w[e] = 0u;
+                for (int e = 0; e < 2; ++e) {  // position 2p+e holds column p + 4e
+                    const int k = g * G + 8 * kc + p + 4 * e;
+                    v[e] = (src && k < K) ? src[k] : 0.0f;
+                }
+                const uint16_t h0 = bf16_bits(v[0]), h1 = bf16_bits(v[1]);
+                const uint16_t l0 = bf16_bits(__fsub_rn(v[0], bf16_val(h0)));
+                const uint16_t l1 = bf16_bits(__fsub_rn(v[1], bf16_val(h1)));
+                h[p] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+                l[p] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+            }
+            dh[kc * 8] = make_uint4(h[0], h[1], h[2], h[3]);
+            dl[kc * 8] = make_uint4(l[0], l[1], l[2], l[3]);
         }
-        uint4 h, l;
-        h.x = __byte_perm(w[0], w[1], 0x5410), h.y = __byte_perm(w[2], w[3], 0x5410);
-        h.z = __byte_perm(w[4], w[5], 0x5410), h.w = __byte_perm(w[6], w[7], 0x5410);
-        l.x = __byte_perm(w[0], w[1], 0x7632), l.y = __byte_perm(w[2], w[3], 0x7632);
-        l.z = __byte_perm(w[4], w[5], 0x7632), l.w = __byte_perm(w[6], w[7], 0x7632);
-        reinterpret_cast<uint4 *>(bhi)[c] = h;
-        reinterpret_cast<uint4 *>(blo)[c] = l;
+        if (src) {  // group sum in column order, fp32
+            const int k0 = g * G, k1 = min(K, k0 + G);
+            for (int k = k0; k < k1; ++k) xs = __fadd_rn(xs, src[k]);
+        }
+        const uint16_t x1 = bf16_bits(xs);
+        const float r1 = __fsub_rn(xs, bf16_val(x1));
+        const uint16_t x2 = bf16_bits(r1);
+        const uint16_t x3 = bf16_bits(__fsub_rn(r1, bf16_val(x2)));
+        dh[(G / 8) * 8] = make_uint4((uint32_t)x1 | ((uint32_t)x2 << 16),
+                                     (uint32_t)x3 | ((uint32_t)x1 << 16),
+                                     (uint32_t)x2 | ((uint32_t)x3 << 16), 0u);
+        dh[(G / 8 + 1) * 8] = make_uint4(0u, 0u, 0u, 0u);
+        dl[(G / 8) * 8] = make_uint4(0u, 0u, 0u, 0u);
+        dl[(G / 8 + 1) * 8] = make_uint4(0u, 0u, 0u, 0u);
+    }
+}
+
+// ---------------------------------------------------------------- weight repack
+// Interleaved i4 rows (runtime/tiny_format.h:66-77) -> tile-contiguous blocks: for every
+// 256-row tile and group g, the 256 rows' group bytes ([scale][zero][G/2 nibble bytes])
+// back to back, rows past M zero.  Bytes are copied unchanged (a pure permutation of
+// 4-byte words), so the block of (tile, g) holds exactly what the row layout held.
+__global__ void mm_repack_w_kernel(const uint32_t *__restrict__ w, int M, int ng, int wr,
+                                   uint32_t *__restrict__ out, long long total) {
+    for (long long o = blockIdx.x * (long long)blockDim.x + threadIdx.x; o < total;
+         o += (long long)gridDim.x * blockDim.x) {
+        const int wd = (int)(o % wr);
+        const long long rest = o / wr;
+        const int r = (int)(rest % kTileRows);
+        const long long tg = rest / kTileRows;
+        const int g = (int)(tg % ng);
+        const long long tile = tg / ng;
+        const long long row = tile * kTileRows + r;
+        out[o] = row < M ? w[(size_t)row * ng * wr + (size_t)g * wr + wd] : 0u;
     }
 }
 
 // ---------------------------------------------------------------- the GEMM
+template <int G>
 __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_constant__ MmParams P) {
+    constexpr int CK = (G + 16) / 8;          // 16-byte chunks per row of a stage
+    constexpr uint32_t SBO = CK * 128;        // bytes between 8-row groups
+    constexpr uint32_t kAh = kMmRows * CK * 16;  // A bytes of one 128-row half
+    constexpr uint32_t kA = 2 * kAh;
+    constexpr int NW = G / 8;                 // nibble words per row of a group
+    constexpr int GB = 4 + G / 2;             // bytes per group of a weight row
+    constexpr int WR = GB / 4;                // words per row of a group (odd)
+    constexpr uint32_t kRawBytes = kTileRows * GB;
     extern __shared__ __align__(1024) uint8_t smem[];
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem);  // [kMmMaxStages]
-    uint64_t *empty = full + kMmMaxStages;                 // [kMmMaxStages]
-    uint64_t *done = empty + kMmMaxStages;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
-    uint32_t *lut = reinterpret_cast<uint32_t *>(smem + 1024);  // [2][16][256]
-    uint8_t *stage_base = smem + 1024 + 2 * kLutBytes;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);  // [kMmMaxStages] A built
+    uint64_t *bfull = full + kMmMaxStages;                 // [kMmMaxStages] X planes landed
+    uint64_t *empty = bfull + kMmMaxStages;                // [kMmMaxStages] stage consumed
+    uint64_t *tfull = empty + kMmMaxStages;                // [2] accumulators b ready
+    uint64_t *tempty = tfull + 2;                          // [2] accumulators b drained
+    uint64_t *done = tempty + 2;
+    uint64_t *rawbar = done + 1;                           // [kMaxRaw] weight block landed
+    uint64_t *rawfree = rawbar + kMaxRaw;                  // [kMaxRaw] weight block read
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(rawfree + kMaxRaw);
+    float *scl = reinterpret_cast<float *>(smem + 1024);   // [kSclRing][256] group scales
+    uint8_t *stage_base = smem + 1024 + kSclRing * kTileRows * 4;
     __shared__ int s_err;
 
     // ---- which tile: job j, rows m0.., columns n0..n0+nw
@@ -187,27 +273,35 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
     while (j + 1 < P.n_jobs && tile >= job_of(P, j + 1).tile_begin) ++j;
     const MmJob &job = job_of(P, j);
     const int local = tile - job.tile_begin;
-    const int mt = (job.M + kMmRows - 1) / kMmRows;
+    const int mt = (job.M + kTileRows - 1) / kTileRows;
     const int npad = (job.N + 15) & ~15;
-    const int m0 = (local % mt) * kMmRows;
+    const int m0 = (local % mt) * kTileRows;
     const int n0 = (local / mt) * P.nt;
-    const int nw = min(P.nt, npad - n0);  // this tile's MMA N (multiple of 16)
-    const uint32_t b_bytes = (uint32_t)nw * 128u;  // one X plane of a stage
+    const int nw = min(P.nt, npad - n0);           // this tile's MMA N (multiple of 16)
+    const uint32_t b_bytes = (uint32_t)nw * CK * 16u;  // one X plane of a stage
     const uint32_t stage_bytes = P.stage_bytes;
-    const int G = P.G, K = P.K, ks = P.ks;
-    const int GB = 4 + G / 2;
-    const size_t RB = (size_t)((K + G - 1) / G) * GB;
+    const int ng = P.ng, S = P.stages, RD = P.raw_depth;
+    uint8_t *raw = stage_base + (size_t)S * stage_bytes;  // [RD] weight blocks
 
     if (t == 0) {
-        for (int s = 0; s < P.stages; ++s) {
-            mbar_init(&full[s], kMmProducers / 32);
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], kProdWarps);
+            mbar_init(&bfull[s], 1);
             mbar_init(&empty[s], 1);
         }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], kEpiWarps);
+        }
         mbar_init(done, 1);
+        for (int r = 0; r < RD; ++r) {
+            mbar_init(&rawbar[r], 1);
+            mbar_init(&rawfree[r], kProdWarps);
+        }
         fence_mbar_init();
         s_err = 0;
     }
-    if (warp == 8) {  // TMEM accumulator: 128 lanes x tmem_cols fp32 columns
+    if (warp == kMmaWarp) {  // TMEM: 2 buffers x 2 row halves x nt fp32 columns x 128 lanes
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(tmem_slot)),
                      "r"(P.tmem_cols)
@@ -219,169 +313,176 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp < 8) {
-        // ---------------- producers: thread = (row r, half h) of every stage
-        const int r = t & (kMmRows - 1), h = t >> 7;
-        const int row = m0 + r;
-        const bool row_ok = row < job.M;
-        const uint8_t *wrow = job.w + (size_t)(row_ok ? row : 0) * RB;
-        const bool shared_lut = G >= kMmKs;  // both halves of a stage share the group
-        const int slot = shared_lut ? r : t;
-        int issued = 0;
-        bool abort = false;
-        // weight words of stage i (group header + 4 nibble words): fetched two stages
-        // ahead into registers so the global-load latency overlaps the work in between
-        auto fetch = [&](int i, uint32_t &hdr, uint32_t(&nb)[4]) {
-            hdr = 0u;
-            nb[0] = nb[1] = nb[2] = nb[3] = 0u;
-            const int k = i * kMmKs + 32 * h;
-            // the table's group exists (with a shared table the partner half may need it
-            // even when this half lies past K); same group for both halves when shared
-            if (i >= ks || !row_ok || (shared_lut ? i * kMmKs : k) >= K) return;
-            const uint8_t *gp = wrow + (size_t)(k / G) * GB;
-            hdr = ldg_u32(gp);
-            if (k < K) {
-                const uint8_t *np_ = gp + 4 + (k % G) / 2;
-#pragma unroll
-                for (int q = 0; q < 4; ++q) nb[q] = ldg_u32(np_ + 4 * q);
-            }
-        };
-        uint32_t hdr0, nib0[4], hdr1, nib1[4];
-        fetch(0, hdr0, nib0);
-        fetch(1, hdr1, nib1);
-        for (int i = 0; i < ks; ++i) {
-            const int s = i % P.stages;
-            const int k = i * kMmKs + 32 * h;  // first column of this thread's half
-            uint32_t hdr2, nib2[4];
-            fetch(i + 2, hdr2, nib2);
+    if (warp < kProdWarps) {
+        // ---------------- A operand: thread = weight row t of the tile, codes widened to
+        // bf16 from the tile-contiguous weight block of the group (mm_repack_w_kernel)
+        const uint32_t off = (uint32_t)(t >> 7) * kAh + (uint32_t)((t & 127) >> 3) * SBO +
+                             (uint32_t)(t & 7) * 16u;
+        const __nv_bfloat162 k128 = __floats2bfloat162_rn(128.0f, 128.0f);
+        for (int i = 0; i < ng; ++i) {
+            const int s = i % S, r = i % RD;
             bool ok = true;
-            if (i >= P.stages)
-                ok = mbar_wait(&empty[s], (uint32_t)((i / P.stages) - 1) & 1u, kWaitCycles);
-            // table of the 16 dequantised values of this (row, group) in buffer i & 1
-            uint32_t *lb = lut + (size_t)(i & 1) * (16 * kMmProducers);
-            const bool have = row_ok && k < K;  // this half holds weights
-            const bool full_half = k + 32 <= K;
-            const bool build = row_ok && (shared_lut ? i * kMmKs : k) < K;
-            uint32_t nib[4] = {nib0[0], nib0[1], nib0[2], nib0[3]};
-            if (build) {
-                const float sc = h2f((uint16_t)(hdr0 & 0xFFFFu));
-                const float z = h2f((uint16_t)(hdr0 >> 16));
-                const int q0 = shared_lut ? 8 * h : 0, q1 = shared_lut ? q0 + 8 : 16;
-                for (int q = q0; q < q1; ++q)
-                    lb[q * kMmProducers + slot] = split_bf16(__fmul_rn(__fsub_rn((float)q, z), sc));
+            if (i >= S) ok = mbar_wait_sleep(&empty[s], (uint32_t)((i / S) - 1) & 1u, kWaitCycles);
+            if (ok) ok = mbar_wait_sleep(&rawbar[r], (uint32_t)(i / RD) & 1u, kWaitCycles);
+            if (producers_sync_or(!ok)) {  // uniform: every producer stops together
+                if (t == 0) s_err = 1;
+                break;
             }
-            hdr0 = hdr1;
-            hdr1 = hdr2;
+            const uint32_t *d = reinterpret_cast<const uint32_t *>(raw + (size_t)r * kRawBytes) + t * WR;
+            uint32_t wv[WR];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                nib0[q] = nib1[q];
-                nib1[q] = nib2[q];
-            }
-            abort = producers_sync_or(!ok);  // also: the tables are complete
-            if (abort) break;
+            for (int q = 0; q < WR; ++q) wv[q] = d[q];  // [0] header, then nibble words
+            __syncwarp();
+            if (lane == 0) mbar_arrive_plain(&rawfree[r]);  // block slot r read
             uint8_t *st = stage_base + (size_t)s * stage_bytes;
-            if (t == 0) {  // X planes of this stage: two bulk copies
-                mbar_expect_tx(&full[s], 2u * b_bytes);
-                const size_t blk = ((size_t)i * (npad / 8) + n0 / 8) * 512;  // bf16 elements
-                bulk_g2s(st + 2 * kABytes, P.bhi + job.b_off + blk, b_bytes, &full[s]);
-                bulk_g2s(st + 2 * kABytes + b_bytes, P.blo + job.b_off + blk, b_bytes, &full[s]);
-                issued = i + 1;
-            }
-            // dequantise 32 weights: nibble -> table word -> (hi, lo) bf16 pairs
-            const uint32_t off = (uint32_t)(r >> 3) * 1024u + (uint32_t)(r & 7) * 16u;
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                uint4 hv = make_uint4(0u, 0u, 0u, 0u), lv = hv;
-                if (have) {
-                    uint32_t e[8];
-                    const uint32_t *lt = lb + slot;
+            for (int q = 0; q < NW; ++q) {  // 8 codes -> (q0,q4) (q1,q5) (q2,q6) (q3,q7)
+                const uint32_t w = wv[1 + q];
+                uint32_t o[4];
 #pragma unroll
-                    for (int n = 0; n < 8; ++n) {
-                        const int kk = k + 8 * q + n;
-                        e[n] = (full_half || kk < K) ? lt[((nib[q] >> (4 * n)) & 15u) * kMmProducers] : 0u;
-                    }
-                    hv.x = __byte_perm(e[0], e[1], 0x5410), hv.y = __byte_perm(e[2], e[3], 0x5410);
-                    hv.z = __byte_perm(e[4], e[5], 0x5410), hv.w = __byte_perm(e[6], e[7], 0x5410);
-                    lv.x = __byte_perm(e[0], e[1], 0x7632), lv.y = __byte_perm(e[2], e[3], 0x7632);
-                    lv.z = __byte_perm(e[4], e[5], 0x7632), lv.w = __byte_perm(e[6], e[7], 0x7632);
+                for (int p = 0; p < 4; ++p) {
+                    const uint32_t wide = ((w >> (4 * p)) & 0x000F000Fu) | 0x43004300u;  // 128 + q
+                    const __nv_bfloat162 v = __hsub2(*reinterpret_cast<const __nv_bfloat162 *>(&wide), k128);
+                    o[p] = *reinterpret_cast<const uint32_t *>(&v);
                 }
-                const uint32_t o = off + (uint32_t)(4 * h + q) * 128u;
-                *reinterpret_cast<uint4 *>(st + o) = hv;
-                *reinterpret_cast<uint4 *>(st + kABytes + o) = lv;
+                *reinterpret_cast<uint4 *>(st + off + (uint32_t)q * 128u) = make_uint4(o[0], o[1], o[2], o[3]);
             }
+            {  // zero term: -(z1, z1, z1, z2, z2, z2, 0, 0), z = z1 + z2 exactly
+                const float z = h2f((uint16_t)(wv[0] >> 16));
+                const uint16_t z1 = bf16_bits(-z);
+                const uint16_t z2 = bf16_bits(__fsub_rn(-z, bf16_val(z1)));
+                const uint32_t a = (uint32_t)z1 | ((uint32_t)z1 << 16);
+                const uint32_t b = (uint32_t)z1 | ((uint32_t)z2 << 16);
+                const uint32_t c = (uint32_t)z2 | ((uint32_t)z2 << 16);
+                *reinterpret_cast<uint4 *>(st + off + (uint32_t)NW * 128u) = make_uint4(a, b, c, 0u);
+                *reinterpret_cast<uint4 *>(st + off + (uint32_t)(NW + 1) * 128u) = make_uint4(0u, 0u, 0u, 0u);
+            }
+            scl[(i % kSclRing) * kTileRows + t] = h2f((uint16_t)(wv[0] & 0xFFFFu));  // for the epilogue
             fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
             __syncwarp();
             if (lane == 0) mbar_arrive_plain(&full[s]);
         }
-        if (abort && t == 0) s_err = 1;
-        // drain: the copies of the last issued stages have landed before smem is released
-        if (t == 0) {
-            for (int i = max(0, issued - P.stages); i < issued; ++i)
-                if (!mbar_wait(&full[i % P.stages], (uint32_t)(i / P.stages) & 1u, kWaitCycles))
-                    s_err = 1;
-        }
-        // ---------------- epilogue: TMEM -> Y (column-major), lanes 32*(warp%4).., columns
-        // split between warps w and w+4
-        // warp-uniform: tcgen05.ld below is a whole-warp instruction
-        const bool fin = __all_sync(0xffffffffu, mbar_wait(done, 0u, kWaitCycles));
-        tc_fence_after();
-        if (fin) {
-            const int lq = warp & 3;
-            const int half = nw / 2;  // multiple of 8
-            const int c0 = (warp >> 2) * half;
-            const int orow = m0 + 32 * lq + lane;
-            for (int c = c0; c < c0 + half; c += 8) {
-                uint32_t v[8];
-                asm volatile(
-                    "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
-                    "tcgen05.wait::ld.sync.aligned;\n"
-                    : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
-                      "=r"(v[6]), "=r"(v[7])
-                    : "r"(tmem + ((uint32_t)(32 * lq) << 16) + (uint32_t)c)
-                    : "memory");
-                if (orow < job.M) {
+    } else if (warp < kMmaWarp) {
+        // ---------------- epilogue: y += s_g * P_g per group, in registers; warp e owns
+        // row half e/4, TMEM lane quarter warp%4, all nw columns
+        const int e = warp - kProdWarps;
+        const int half = e >> 2;
+        const int quarter = warp & 3;  // TMEM lanes this warp may access
+        const int rl = 128 * half + 32 * quarter + lane;  // row within the tile
+        const int row = m0 + rl;
+        const uint32_t lane_addr = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(half * P.nt);
+        float y[kMmMaxCols];
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const int n = n0 + c + e;
-                        if (n < job.N) job.y[(size_t)n * job.ldy + orow] = __uint_as_float(v[e]);
-                    }
-                }
-            }
-        } else if (t == 0) {
-            s_err = 1;
-        }
-    } else if (lane == 0) {
-        // ---------------- MMA issuer
-        bool ok = true;
-        const uint32_t idesc = umma_idesc_bf16(nw);
-        for (int i = 0; i < ks && ok; ++i) {
-            const int s = i % P.stages;
-            if (!mbar_wait(&full[s], (uint32_t)(i / P.stages) & 1u, kWaitCycles)) {
-                ok = false;
+        for (int c = 0; c < kMmMaxCols; ++c) y[c] = 0.0f;
+        for (int i = 0; i < ng; ++i) {
+            const int b = i & 1;
+            if (!__all_sync(0xffffffffu, mbar_wait_sleep(&tfull[b], (uint32_t)(i >> 1) & 1u, kWaitCycles))) {
+                if (lane == 0) s_err = 1;
                 break;
             }
             tc_fence_after();
-            const uint32_t a_hi = smem_u32(stage_base + (size_t)s * stage_bytes);
-            const uint32_t a_lo = a_hi + kABytes;
-            const uint32_t b_hi = a_hi + 2 * kABytes;
-            const uint32_t b_lo = b_hi + b_bytes;
+            const float sc = scl[(i % kSclRing) * kTileRows + rl];
+            const uint32_t ta = lane_addr + (uint32_t)(b * 2 * P.nt);
 #pragma unroll
-            for (int kk = 0; kk < kMmKs / 16; ++kk) {
-                const uint32_t o = (uint32_t)kk * 256u;  // two 16-byte core-matrix columns
-                const uint64_t ah = umma_desc(a_hi + o, 128, 1024), al = umma_desc(a_lo + o, 128, 1024);
-                const uint64_t bh = umma_desc(b_hi + o, 128, 1024), bl = umma_desc(b_lo + o, 128, 1024);
-                umma_bf16(tmem, ah, bh, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-                umma_bf16(tmem, ah, bl, idesc, 1u);
-                umma_bf16(tmem, al, bh, idesc, 1u);
+            for (int h = 0; h < kMmMaxCols / 16; ++h) {  // 16 columns at a time
+                float v[16];
+#pragma unroll
+                for (int c = 0; c < 2; ++c)
+                    if (h * 16 + c * 8 < nw) tmem_ld8(ta + (uint32_t)(h * 16 + c * 8), v + c * 8);
+                tmem_wait_ld();
+#pragma unroll
+                for (int c = 0; c < 16; ++c)
+                    if (h * 16 + c < nw) y[h * 16 + c] = fmaf(sc, v[c], y[h * 16 + c]);
             }
-            umma_commit(&empty[s]);  // stage s free once these MMAs have read it
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_plain(&tempty[b]);
+        }
+        if (row < job.M) {
+#pragma unroll
+            for (int c = 0; c < kMmMaxCols; ++c) {
+                const int n = n0 + c;
+                if (c < nw && n < job.N) job.y[(size_t)n * job.ldy + row] = y[c];
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) {
+            // ---------------- MMA issuer: per group, for each row half, G/16 K steps of
+            // (codes x X hi) + (codes x X lo), then the zero term
+            bool ok = true;
+            const uint32_t idesc = umma_idesc_bf16(nw);
+            for (int i = 0; i < ng && ok; ++i) {
+                const int s = i % S, b = i & 1;
+                ok = mbar_wait_sleep(&full[s], (uint32_t)(i / S) & 1u, kWaitCycles);
+                if (ok) ok = mbar_wait_sleep(&bfull[s], (uint32_t)(i / S) & 1u, kWaitCycles);
+                if (ok && i >= 2) ok = mbar_wait_sleep(&tempty[b], (uint32_t)((i >> 1) - 1) & 1u, kWaitCycles);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t a0 = smem_u32(stage_base + (size_t)s * stage_bytes);
+                const uint32_t bh = a0 + kA, bl = bh + b_bytes;
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                    const uint32_t a = a0 + (uint32_t)hf * kAh;
+                    const uint32_t dd = tmem + (uint32_t)((b * 2 + hf) * P.nt);
+#pragma unroll
+                    for (int kk = 0; kk < G / 16; ++kk) {
+                        const uint32_t o = (uint32_t)kk * 256u;  // two 16-byte core-matrix columns
+                        const uint64_t ad = umma_desc(a + o, 128, SBO);
+                        umma_bf16(dd, ad, umma_desc(bh + o, 128, SBO), idesc, kk > 0 ? 1u : 0u);
+                        umma_bf16(dd, ad, umma_desc(bl + o, 128, SBO), idesc, 1u);
+                    }
+                    const uint32_t oz = (uint32_t)(G / 16) * 256u;  // zero term
+                    umma_bf16(dd, umma_desc(a + oz, 128, SBO), umma_desc(bh + oz, 128, SBO), idesc, 1u);
+                }
+                umma_commit(&empty[s]);  // stage s free once these MMAs have read it
+                umma_commit(&tfull[b]);  // accumulators b hold P_i
+            }
+            if (!ok) s_err = 1;
+            umma_commit(done);  // every MMA issued above has completed
+            if (!mbar_wait_sleep(done, 0u, kWaitCycles)) s_err = 1;
+        }
+    } else if (lane == 0) {
+        // ---------------- loader: weight blocks RD - 1 groups ahead, X planes per stage
+        const uint8_t *wblk = job.w + (size_t)(local % mt) * ng * kRawBytes;  // this row tile
+        auto issue_raw = [&](int g) {
+            uint64_t *bar = &rawbar[g % RD];
+            uint8_t *dst = raw + (size_t)(g % RD) * kRawBytes;
+            const uint8_t *src = wblk + (size_t)g * kRawBytes;
+            mbar_arrive_expect_tx(bar, kRawBytes);
+            for (uint32_t o = 0; o < kRawBytes; o += 16384u)
+                bulk_g2s(dst + o, src + o, min(16384u, kRawBytes - o), bar);
+        };
+        int raw_issued = 0, b_issued = 0;
+        bool ok = true;
+        for (int g = 0; g < RD - 1 && g < ng; ++g) issue_raw(g), raw_issued = g + 1;
+        for (int g = 0; g < ng && ok; ++g) {
+            const int gr = g + RD - 1;  // weight block into the slot group g - 1 used
+            if (gr < ng) {
+                if (g >= 1) ok = mbar_wait_sleep(&rawfree[(g - 1) % RD], (uint32_t)((g - 1) / RD) & 1u, kWaitCycles);
+                if (!ok) break;
+                issue_raw(gr);
+                raw_issued = gr + 1;
+            }
+            const int s = g % S;  // X planes of group g into stage s
+            if (g >= S) ok = mbar_wait_sleep(&empty[s], (uint32_t)((g / S) - 1) & 1u, kWaitCycles);
+            if (!ok) break;
+            uint8_t *st = stage_base + (size_t)s * stage_bytes;
+            const size_t blk = ((size_t)g * (npad / 8) + n0 / 8) * (CK * 64);  // bf16 elements
+            mbar_arrive_expect_tx(&bfull[s], 2u * b_bytes);
+            bulk_g2s(st + kA, P.bhi + job.b_off + blk, b_bytes, &bfull[s]);
+            bulk_g2s(st + kA + b_bytes, P.blo + job.b_off + blk, b_bytes, &bfull[s]);
+            b_issued = g + 1;
         }
         if (!ok) s_err = 1;
-        umma_commit(done);  // every MMA issued above has completed
+        // copies still in flight land before shared memory is released
+        for (int g = max(0, raw_issued - RD); g < raw_issued; ++g)
+            if (!mbar_wait_sleep(&rawbar[g % RD], (uint32_t)(g / RD) & 1u, kWaitCycles)) s_err = 1;
+        for (int g = max(0, b_issued - S); g < b_issued; ++g)
+            if (!mbar_wait_sleep(&bfull[g % S], (uint32_t)(g / S) & 1u, kWaitCycles)) s_err = 1;
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 8) {
+    if (warp == kMmaWarp) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                      "r"(P.tmem_cols)
@@ -390,35 +491,95 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
     if (t == 0 && s_err && P.status) atomicExch(P.status, kDevTimeoutTma);
 }
 
-std::atomic<unsigned long long> g_mm_smem_set{0};
+KernelSmem g_mm_smem_set[3];
+
+template <int G>
+uint32_t mm_stage_bytes(int nt) {
+    return (uint32_t)(kTileRows + 2 * nt) * ((G + 16) / 8) * 16u;
+}
+
+template <int G>
+int launch_grouped_g(MmParams &P, int total_tiles, cudaStream_t st, int gi) {
+    P.stage_bytes = mm_stage_bytes<G>(P.nt);
+    int limit = 0;
+    TQ_CUDA_TRY(smem_limit_once(mm_i4_tc_kernel<G>, g_mm_smem_set[gi], &limit));
+    const int fixed = 1024 + kSclRing * kTileRows * 4;
+    const int raw_group = kTileRows * (4 + G / 2);  // bytes of one staged weight block
+    // deepest pipeline that fits: operand stages first (2 wanted), then the weight ring
+    int stages = 0, rd = 0;
+    for (int s = std::min(kMmMaxStages, P.ng); s >= 1 && !stages; --s)
+        for (int r = kMaxRaw; r >= 2; --r)
+            if (fixed + s * (int)P.stage_bytes + r * raw_group <= limit && (s >= 2 || r == 2)) {
+                stages = s;
+                rd = r;
+                break;
+            }
+    TQ_CHECK_ARG(stages >= 1, "matmul_i4: tile of %d columns does not fit shared memory", P.nt);
+    P.stages = stages;
+    P.raw_depth = rd;
+    const size_t smem = fixed + (size_t)stages * P.stage_bytes + (size_t)rd * raw_group;
+    mm_i4_tc_kernel<G><<<total_tiles, kMmThreads, smem, st>>>(P);
+    TQ_CUDA_TRY(cudaGetLastError());
+    return TQB200_OK;
+}
 
 }  // namespace
 
-size_t mm_x_planes_bytes(int K, int N) {
-    const size_t ks = (size_t)(K + kMmKs - 1) / kMmKs;
+bool mm_group_supported(int G) { return G == 32 || G == 64 || G == 128; }
+
+size_t mm_x_planes_bytes(int K, int N, int G) {
+    if (!mm_group_supported(G)) return 0;
+    const size_t ng = (size_t)(K + G - 1) / G;
     const size_t npad = (size_t)(N + 15) & ~(size_t)15;
-    return 2 * ks * kMmKs * npad * 2;  // hi + lo bf16
+    return 2 * ng * (size_t)(G + 16) * npad * 2;  // hi + lo bf16
 }
 
-// Widest column tile (fewest re-dequantisations of a weight tile) that still gives every
-// SM a CTA; the narrowest that covers the columns when nothing fills the SMs.
+size_t mm_repacked_bytes(int M, int K, int G) {
+    if (!mm_group_supported(G)) return 0;
+    const size_t ng = (size_t)(K + G - 1) / G;
+    const size_t mt = (size_t)(M + kTileRows - 1) / kTileRows;
+    return mt * ng * kTileRows * (size_t)(4 + G / 2);
+}
+
+int launch_mm_repack_w(const uint8_t *w, int M, int K, int G, uint8_t *out, cudaStream_t st) {
+    TQ_CHECK_ARG(mm_group_supported(G), "matmul_i4: group_size %d not 32, 64 or 128", G);
+    TQ_CHECK_ARG((((uintptr_t)w) & 3) == 0 && (((uintptr_t)out) & 15) == 0,
+                 "matmul_i4: weights not 4-byte / repack buffer not 16-byte aligned");
+    const int ng = (K + G - 1) / G, wr = (4 + G / 2) / 4;
+    const long long total = (long long)(mm_repacked_bytes(M, K, G) / 4);
+    if (total == 0) return TQB200_OK;
+    const int threads = 256;
+    const int blocks = (int)std::min<long long>((total + threads - 1) / threads, 148LL * 16);
+    mm_repack_w_kernel<<<blocks, threads, 0, st>>>(reinterpret_cast<const uint32_t *>(w), M, ng,
+                                                   wr, reinterpret_cast<uint32_t *>(out), total);
+    TQ_CUDA_TRY(cudaGetLastError());
+    return TQB200_OK;
+}
+
+size_t mm_scratch_bytes(int M, int K, int N, int G) {
+    if (!mm_group_supported(G)) return 0;
+    const size_t a = (mm_repacked_bytes(M, K, G) + 255) & ~(size_t)255;
+    return a + mm_x_planes_bytes(K, N, G);
+}
+
+// Widest column tile (fewest re-reads of a weight tile) that still gives every SM a CTA;
+// the widest that covers the columns when nothing fills the SMs.
 int mm_tile_width(int M, int N) {
     const int npad = (N + 15) & ~15;
-    const int mt = (M + kMmRows - 1) / kMmRows;
+    const int mt = (M + kTileRows - 1) / kTileRows;
+    const int widest = std::min(npad, kMmMaxCols);
     const int sms = num_sms();
-    for (int nt = 256; nt >= 16; nt >>= 1) {
-        if (nt > npad && nt > 16) continue;
-        if (mt * ((npad + nt - 1) / nt) >= sms) return nt;
-    }
-    return std::min(npad, 128);
+    for (int nt = widest; nt >= 16; nt = (nt / 2 + 15) & ~15)
+        if (mt * ((npad + nt - 1) / nt) >= sms || nt == 16) return nt;
+    return widest;
 }
 
 int launch_matmul_i4_grouped(const MmJob *host_jobs, const MmJob *dev_jobs, int n_jobs, int K,
                              int G, int nt, const uint16_t *bhi, const uint16_t *blo, int total_tiles,
                              int *status, cudaStream_t st) {
     TQ_CHECK_ARG(n_jobs >= 1, "matmul_i4: no jobs");
-    TQ_CHECK_ARG(G % 32 == 0 && G >= 32, "matmul_i4 (tensor cores): group_size %d not a multiple of 32", G);
-    TQ_CHECK_ARG(nt % 16 == 0 && nt >= 16 && nt <= 256, "matmul_i4: bad tile width %d", nt);
+    TQ_CHECK_ARG(mm_group_supported(G), "matmul_i4 (tensor cores): group_size %d not 32, 64 or 128", G);
+    TQ_CHECK_ARG(nt % 16 == 0 && nt >= 16 && nt <= kMmMaxCols, "matmul_i4: bad tile width %d", nt);
     TQ_CHECK_ARG(((uintptr_t)bhi & 15) == 0 && ((uintptr_t)blo & 15) == 0, "matmul_i4: X planes not 16-byte aligned");
     if (total_tiles == 0) return TQB200_OK;
     MmParams P{};
@@ -426,64 +587,67 @@ int launch_matmul_i4_grouped(const MmJob *host_jobs, const MmJob *dev_jobs, int 
     P.jobs = dev_jobs;
     P.n_jobs = dev_jobs ? n_jobs : 1;
     P.K = K;
-    P.G = G;
-    P.ks = (K + kMmKs - 1) / kMmKs;
+    P.ng = (K + G - 1) / G;
     P.nt = nt;
     P.bhi = bhi;
     P.blo = blo;
-    P.stage_bytes = 2 * kABytes + 2u * (uint32_t)nt * 128u;
     uint32_t cols = 32;
-    while ((int)cols < nt) cols <<= 1;
+    while ((int)cols < 4 * nt) cols <<= 1;
     P.tmem_cols = cols;
     P.status = status;
-    int limit = 0;
-    TQ_CUDA_TRY(smem_limit_once(mm_i4_tc_kernel, g_mm_smem_set, &limit));
-    const int fixed = 1024 + 2 * (int)kLutBytes;
-    int stages = std::min(kMmMaxStages, (limit - fixed) / (int)P.stage_bytes);
-    stages = std::min(stages, P.ks);
-    TQ_CHECK_ARG(stages >= 1, "matmul_i4: tile of %d columns does not fit shared memory", nt);
-    P.stages = stages;
-    const size_t smem = (size_t)fixed + (size_t)stages * P.stage_bytes;
-    mm_i4_tc_kernel<<<total_tiles, kMmThreads, smem, st>>>(P);
-    TQ_CUDA_TRY(cudaGetLastError());
-    return TQB200_OK;
+    if (G == 32) return launch_grouped_g<32>(P, total_tiles, st, 0);
+    if (G == 64) return launch_grouped_g<64>(P, total_tiles, st, 1);
+    return launch_grouped_g<128>(P, total_tiles, st, 2);
 }
 
-int launch_mm_pack_x(const float *x, const int *cols, int ldx, int K, int N, uint16_t *bhi,
+int launch_mm_pack_x(const float *x, const int *cols, int ldx, int K, int N, int G, uint16_t *bhi,
                      uint16_t *blo, cudaStream_t st) {
+    TQ_CHECK_ARG(mm_group_supported(G), "matmul_i4: group_size %d not 32, 64 or 128", G);
     const int npad = (N + 15) & ~15;
-    const int ks = (K + kMmKs - 1) / kMmKs;
-    const long long total = (long long)npad * ks * 8;
+    const int ng = (K + G - 1) / G;
+    const long long total = (long long)npad * ng;
     if (total == 0) return TQB200_OK;
-    const int threads = 256;
-    const long long blocks = std::min<long long>((total + threads - 1) / threads, 148LL * 16);
-    mm_pack_x_kernel<<<(int)blocks, threads, 0, st>>>(x, cols, ldx, K, N, npad, ks, bhi, blo);
+    const int threads = 128;
+    const int blocks = (int)std::min<long long>((total + threads - 1) / threads, 148LL * 32);
+    if (G == 32)
+        mm_pack_x_kernel<32><<<blocks, threads, 0, st>>>(x, cols, ldx, K, N, npad, ng, bhi, blo);
+    else if (G == 64)
+        mm_pack_x_kernel<64><<<blocks, threads, 0, st>>>(x, cols, ldx, K, N, npad, ng, bhi, blo);
+    else
+        mm_pack_x_kernel<128><<<blocks, threads, 0, st>>>(x, cols, ldx, K, N, npad, ng, bhi, blo);
     TQ_CUDA_TRY(cudaGetLastError());
     return TQB200_OK;
 }
 
-// Y = W X for one matrix: X planes from the caller's scratch (mm_x_planes_bytes(K, N)).
+// Y = W X for one matrix.  scratch (mm_scratch_bytes(M, K, N, G)) receives the
+// tile-contiguous weights and the X planes.
 int launch_matmul_i4(const uint8_t *w, const float *x, float *y, int M, int K, int N, int G,
                      void *scratch, int *status, cudaStream_t st) {
     TQ_CHECK_ARG(M >= 0 && K > 0 && N >= 0, "matmul_i4: bad shape %d x %d x %d", M, K, N);
+    TQ_CHECK_ARG(mm_group_supported(G), "matmul_i4: group_size %d not 32, 64 or 128", G);
     if (M == 0 || N == 0) return TQB200_OK;
     TQ_CHECK_ARG(((uintptr_t)w & 3) == 0, "matmul_i4: weights not 4-byte aligned");
+    TQ_CHECK_ARG(((uintptr_t)scratch & 15) == 0, "matmul_i4: scratch not 16-byte aligned");
     const int npad = (N + 15) & ~15;
-    const size_t plane = mm_x_planes_bytes(K, N) / 2;
-    uint16_t *bhi = static_cast<uint16_t *>(scratch);
-    uint16_t *blo = reinterpret_cast<uint16_t *>(static_cast<uint8_t *>(scratch) + plane);
-    int r = launch_mm_pack_x(x, nullptr, K, K, N, bhi, blo, st);
+    uint8_t *wt = static_cast<uint8_t *>(scratch);
+    const size_t wbytes = (mm_repacked_bytes(M, K, G) + 255) & ~(size_t)255;
+    const size_t plane = mm_x_planes_bytes(K, N, G) / 2;
+    uint16_t *bhi = reinterpret_cast<uint16_t *>(wt + wbytes);
+    uint16_t *blo = reinterpret_cast<uint16_t *>(wt + wbytes + plane);
+    int r = launch_mm_repack_w(w, M, K, G, wt, st);
+    if (r != TQB200_OK) return r;
+    r = launch_mm_pack_x(x, nullptr, K, K, N, G, bhi, blo, st);
     if (r != TQB200_OK) return r;
     const int nt = mm_tile_width(M, N);
     MmJob j{};
-    j.w = w;
+    j.w = wt;
     j.y = y;
     j.M = M;
     j.N = N;
     j.ldy = M;
     j.tile_begin = 0;
     j.b_off = 0;
-    const int tiles = ((M + kMmRows - 1) / kMmRows) * ((npad + nt - 1) / nt);
+    const int tiles = ((M + kTileRows - 1) / kTileRows) * ((npad + nt - 1) / nt);
     return launch_matmul_i4_grouped(&j, nullptr, 1, K, G, nt, bhi, blo, tiles, status, st);
 }
 

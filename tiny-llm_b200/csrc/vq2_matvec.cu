@@ -359,7 +359,7 @@ int launch_vq2_matvec(const VqLaunch &a, cudaStream_t st) {
     const size_t K4 = ((size_t)a.K * 4 + 15) & ~(size_t)15;
     const size_t smem = 128 + (size_t)nm * (kCbDecoded + P.region) + 2 * K4 + (size_t)nm * 3 * K4 +
                         (size_t)nm * P.S * P.nt * 4;
-    static std::atomic<unsigned long long> attr{0};
+    static KernelSmem attr;
     int smem_max = 0;
     TQ_CUDA_TRY(smem_limit_once(vq2_matvec_kernel, attr, &smem_max));
     TQ_CHECK_ARG(smem <= (size_t)smem_max, "vq2: in_dim %d needs too much shared memory", a.K);
@@ -380,7 +380,7 @@ int launch_vq2_matvec(const VqLaunch &a, cudaStream_t st) {
 int launch_biip(const float *x, float *y, int dim, const float *scale, const float *sign, int bs,
                 cudaStream_t st) {
     TQ_CHECK_ARG(dim > 0 && sign && bs >= 1 && (bs & (bs - 1)) == 0, "biip: bad arguments");
-    static std::atomic<unsigned long long> attr{0};
+    static KernelSmem attr;
     int smem_max = 0;
     TQ_CUDA_TRY(smem_limit_once(biip_kernel, attr, &smem_max));
     TQ_CHECK_ARG((size_t)dim * 4 <= (size_t)smem_max, "biip: dim %d too large", dim);

@@ -50,7 +50,7 @@ PROTOTYPES = {
     "tqb200_dev_matvec_i4_sym": ([_vp, _vp, _vp, _i, _i, _i, _vp], _i),
     "tqb200_dev_dequant_i4": ([_vp, _i, _i, _i, _vp, _vp], _i),
     "tqb200_matmul_i4": ([_u8, _f, _f, _i, _i, _i, _i], _i),
-    "tqb200_matmul_i4_scratch_bytes": ([_i, _i], C.c_size_t),
+    "tqb200_matmul_i4_scratch_bytes": ([_i, _i, _i, _i], C.c_size_t),
     "tqb200_dev_matmul_i4": ([_vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp], _i),
     "tqb200_matvec_vq2": ([_u8, _f, _f, _i, _i], _i),
     "tqb200_biip_rotate": ([_f, _f, _i, _vp, _vp, _i], _i),
