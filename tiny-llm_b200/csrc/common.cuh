@@ -225,6 +225,7 @@ enum : int {
     kDevBadStage = 2,     // a pass did not fit its shared-memory stage (host planning bug)
     kDevBadToken = 3,     // token id outside [0, vocab)
     kDevBadPosition = 4,  // position outside [0, max_seq)
+    kDevBadExpert = 5,    // expert index outside [0, n_experts)
 };
 
 }  // namespace tqb200

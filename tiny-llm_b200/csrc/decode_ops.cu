@@ -470,8 +470,8 @@ __global__ void argmax_pairs_kernel(const ArgPair *__restrict__ pairs, int n, in
 // ------------------------------------------------------------------ top-k softmax
 // n <= 1024, k <= 64; one CTA.  Selection by (value desc, index asc); the
 // softmax over the selected logits runs in double exactly as topk_softmax_ref.
-__global__ void topk_softmax_kernel(const float *__restrict__ logits, int n, int k,
-                                    int *__restrict__ idx_out, float *__restrict__ w_out) {
+__device__ void topk_softmax_block(const float *__restrict__ logits, int n, int k,
+                                   int *__restrict__ idx_out, float *__restrict__ w_out) {
     __shared__ float vals[1024];
     __shared__ float sv[32];
     __shared__ int si[32];
@@ -515,6 +515,67 @@ __global__ void topk_softmax_kernel(const float *__restrict__ logits, int n, int
             idx_out[i] = -1;
             w_out[i] = 0.0f;
         }
+    }
+}
+
+__global__ void topk_softmax_kernel(const float *__restrict__ logits, int n, int k,
+                                    int *__restrict__ idx_out, float *__restrict__ w_out) {
+    topk_softmax_block(logits, n, k, idx_out, w_out);
+}
+
+// ------------------------------------------------------------------ MoE router + combine
+// MoE router of one decode step (runtime/qwen_forward_token.cpp:478-491 with an f32
+// router): normed = rmsnorm(h) * post_ln (rmsnorm_ref semantics), logits[e] = W[e] . normed
+// in double as matvec_f32_ref (kernels/matvec/matvec_f32_ref.cpp), then, in the last CTA
+// to finish, top-k softmax (topk_softmax_ref).  One warp per router row; every CTA
+// normalises the (small) hidden vector itself.
+__global__ void moe_router_kernel(const float *__restrict__ h, const float *__restrict__ norm_w,
+                                  float eps, int H, const float *__restrict__ W, int E, int k,
+                                  float *__restrict__ logits, int *__restrict__ idx,
+                                  float *__restrict__ wts, unsigned int *ticket) {
+    extern __shared__ float xn[];  // [H]
+    __shared__ double s_red[32];
+    __shared__ bool s_last;
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5, nw = blockDim.x >> 5;
+    double ss = 0.0;
+    for (int i = t; i < H; i += blockDim.x) {
+        const float v = h[i];
+        ss += (double)v * (double)v;
+    }
+    ss = warp_sum_d(ss);
+    if (lane == 0) s_red[warp] = ss;
+    __syncthreads();
+    double tot = 0.0;
+    for (int w = 0; w < nw; ++w) tot += s_red[w];
+    const float scale = 1.0f / sqrtf(__fadd_rn((float)(tot / H), eps));
+    for (int i = t; i < H; i += blockDim.x) xn[i] = __fmul_rn(__fmul_rn(h[i], scale), norm_w[i]);
+    __syncthreads();
+    const int e = blockIdx.x * nw + warp;
+    if (e < E) {
+        const float *row = W + (size_t)e * H;
+        double acc = 0.0;
+        for (int i = lane; i < H; i += 32) acc += (double)row[i] * (double)xn[i];
+        acc = warp_sum_d(acc);
+        if (lane == 0) logits[e] = (float)acc;
+    }
+    __threadfence();
+    __syncthreads();
+    if (t == 0) s_last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    topk_softmax_block(logits, E, k, idx, wts);
+    if (t == 0) *ticket = 0u;  // ready for the next launch (graph replay)
+}
+
+// acc = sum_t w_t * o_t in router order, then h += acc, with the reference's fp32
+// rounding points (runtime/qwen_forward_token.cpp:604-609, :627-631).
+__global__ void moe_combine_kernel(float *__restrict__ h, const float *__restrict__ o,
+                                   const float *__restrict__ wts, int k, int H) {
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < H; j += gridDim.x * blockDim.x) {
+        float acc = 0.0f;
+        for (int t = 0; t < k; ++t) acc = __fadd_rn(acc, __fmul_rn(wts[t], o[(size_t)t * H + j]));
+        h[j] = __fadd_rn(h[j], acc);
     }
 }
 
@@ -710,6 +771,28 @@ int launch_argmax(const float *l, int n, float *pv, int *pi, unsigned int *ticke
                   cudaStream_t st) {
     TQ_CHECK_ARG(n > 0, "argmax n %d", n);
     argmax_kernel<<<argmax_blocks(n), 256, 0, st>>>(l, n, pv, pi, ticket, out);
+    TQ_CUDA_TRY(cudaGetLastError());
+    return TQB200_OK;
+}
+
+int launch_moe_router(const float *h, const float *norm_w, float eps, int H, const float *W, int E,
+                      int k, float *logits, int *idx, float *wts, unsigned int *ticket,
+                      cudaStream_t st) {
+    TQ_CHECK_ARG(E > 0 && E <= 1024 && k > 0 && k <= 64 && k <= E && H > 0,
+                 "moe router: E %d k %d H %d", E, k, H);
+    const int threads = 256, rows_per = threads / 32;
+    const size_t smem = (size_t)H * 4;
+    TQ_CHECK_ARG(smem <= 48 * 1024, "moe router: hidden %d too large", H);
+    moe_router_kernel<<<(E + rows_per - 1) / rows_per, threads, smem, st>>>(
+        h, norm_w, eps, H, W, E, k, logits, idx, wts, ticket);
+    TQ_CUDA_TRY(cudaGetLastError());
+    return TQB200_OK;
+}
+
+int launch_moe_combine(float *h, const float *o, const float *wts, int k, int H, cudaStream_t st) {
+    TQ_CHECK_ARG(k > 0 && H > 0, "moe combine: k %d H %d", k, H);
+    const int threads = 256;
+    moe_combine_kernel<<<(H + threads - 1) / threads, threads, 0, st>>>(h, o, wts, k, H);
     TQ_CUDA_TRY(cudaGetLastError());
     return TQB200_OK;
 }

@@ -52,6 +52,12 @@ struct DLayer {
     const float *q_norm = nullptr, *k_norm = nullptr;
     const float *rot_sign[P_N] = {}, *rot_scale[P_N] = {};  // VQ2 BiIP (sign null: none)
     int rot_bs[P_N] = {};
+    // MoE FFN: router (f32 or i4) and every expert's matrices back to back
+    bool moe = false;
+    const float *router_f32 = nullptr;
+    const uint8_t *router_i4 = nullptr;
+    const uint8_t *ex_gate = nullptr, *ex_up = nullptr, *ex_down = nullptr;
+    size_t ex_gu_stride = 0, ex_down_stride = 0;  // bytes between experts
 };
 
 }  // namespace
@@ -101,6 +107,11 @@ struct tqb200_engine {
     int tp = 1, rank = 0;
     float *act = nullptr;              // [inter] SwiGLU output, all-gathered (tp > 1)
     tqb200::ArgPair *pairs = nullptr;  // [tp] per-rank (max, index)
+    // MoE decode state: router logits, chosen experts and weights, expert activations
+    float *moe_logits = nullptr, *moe_w = nullptr, *moe_h = nullptr, *moe_u = nullptr,
+          *moe_o = nullptr;
+    int *moe_idx = nullptr;
+    unsigned int *moe_ticket = nullptr;
 #ifdef TQB200_HAVE_NCCL
     ncclComm_t comm = nullptr;
 #endif
@@ -188,12 +199,52 @@ int up_vec(tqb200_engine *e, const float *h, int n, const float **out) {
     return TQB200_OK;
 }
 
+// Every expert's gate, up and down matrices into one device buffer per kind, expert x at
+// x * stride (stride = the matrix bytes rounded up to 16), and the router.
+int up_experts(tqb200_engine *e, const tqb200_layer &s, const tqb200_model_desc &d, DLayer &w) {
+    const int E = d.n_experts;
+    const size_t gu = (mat_bytes(s.expert_gate[0], d.group_size) + 15) & ~(size_t)15;
+    const size_t dn = (mat_bytes(s.expert_down[0], d.group_size) + 15) & ~(size_t)15;
+    void *pg, *pu, *pd;
+    TQ_TRY(dev_alloc(e, gu * E, &pg));
+    TQ_TRY(dev_alloc(e, gu * E, &pu));
+    TQ_TRY(dev_alloc(e, dn * E, &pd));
+    for (int x = 0; x < E; ++x) {
+        const size_t b = mat_bytes(s.expert_gate[x], d.group_size);
+        const size_t bd = mat_bytes(s.expert_down[x], d.group_size);
+        TQ_CUDA_TRY(cudaMemcpy((uint8_t *)pg + x * gu, s.expert_gate[x].data, b, cudaMemcpyHostToDevice));
+        TQ_CUDA_TRY(cudaMemcpy((uint8_t *)pu + x * gu, s.expert_up[x].data, b, cudaMemcpyHostToDevice));
+        TQ_CUDA_TRY(cudaMemcpy((uint8_t *)pd + x * dn, s.expert_down[x].data, bd, cudaMemcpyHostToDevice));
+        e->weight_bytes += 2 * b + bd;
+    }
+    w.ex_gate = (const uint8_t *)pg;
+    w.ex_up = (const uint8_t *)pu;
+    w.ex_down = (const uint8_t *)pd;
+    w.ex_gu_stride = gu;
+    w.ex_down_stride = dn;
+    const void *pr;
+    TQ_TRY(upload_bytes(e, s.router.data, mat_bytes(s.router, d.group_size), &pr));
+    if (s.router.dtype == TQB200_DT_F32) w.router_f32 = (const float *)pr;
+    else w.router_i4 = (const uint8_t *)pr;
+    return TQB200_OK;
+}
+
 int validate(const tqb200_model_desc &d, const tqb200_engine_opts &o) {
-    TQ_CHECK_ARG(d.model_type == TQB200_MODEL_QWEN2,
-                 "engine supports model_type Qwen2/Qwen3 dense (0), got %d", d.model_type);
-    TQ_CHECK_ARG(d.n_layers > 0 && d.hidden > 0 && d.inter > 0 && d.n_heads > 0 &&
+    const bool moe = d.model_type == TQB200_MODEL_QWEN3_MOE;
+    TQ_CHECK_ARG(d.model_type == TQB200_MODEL_QWEN2 || moe,
+                 "engine supports model_type Qwen2/Qwen3 dense (0) and Qwen3-MoE (3), got %d",
+                 d.model_type);
+    TQ_CHECK_ARG(d.n_layers > 0 && d.hidden > 0 && (moe || d.inter > 0) && d.n_heads > 0 &&
                      d.n_kv_heads > 0 && d.head_dim > 0 && d.vocab > 0 && d.layers,
                  "model description has zero fields");
+    if (moe) {
+        TQ_CHECK_ARG(d.n_experts > 0 && d.n_experts <= 1024 && d.experts_per_tok > 0 &&
+                         d.experts_per_tok <= 64 && d.experts_per_tok <= d.n_experts &&
+                         d.moe_inter > 0 && d.moe_inter % 32 == 0,
+                     "MoE: n_experts %d, experts_per_tok %d, moe_inter %d", d.n_experts,
+                     d.experts_per_tok, d.moe_inter);
+        TQ_CHECK_ARG(o.tp_size <= 1, "MoE models run on one GPU per engine (tp_size %d)", o.tp_size);
+    }
     TQ_CHECK_ARG(d.n_heads % d.n_kv_heads == 0, "n_heads %% n_kv_heads != 0");
     TQ_CHECK_ARG(d.group_size > 0 && d.group_size % 32 == 0,
                  "engine needs group_size %% 32 == 0 (got %d)", d.group_size);
@@ -230,11 +281,14 @@ int build_rope_tables(tqb200_engine *e) {
     return TQB200_OK;
 }
 
-enum Kind { K_EMBED, K_QKV, K_ROPE_KV, K_ATTN, K_OPROJ, K_GATEUP, K_DOWN, K_LMHEAD, K_NKINDS };
+enum Kind {
+    K_EMBED, K_QKV, K_ROPE_KV, K_ATTN, K_OPROJ, K_GATEUP, K_DOWN, K_LMHEAD, K_ROUTER, K_COMBINE,
+    K_NKINDS
+};
 
 const char *kind_name(int k) {
-    static const char *n[] = {"embed", "qkv", "qk_rope_kv", "attention",
-                              "o_proj", "gate_up", "down", "lm_head"};
+    static const char *n[] = {"embed", "qkv", "qk_rope_kv", "attention", "o_proj",
+                              "gate_up", "down", "lm_head", "router", "moe_combine"};
     return (k >= 0 && k < K_NKINDS) ? n[k] : "start";
 }
 
@@ -394,6 +448,60 @@ int launch_forward(tqb200_engine *e) {
             TQ_TRY(launch_i4_matvec_ex(&j, 1, qd, d.group_size, o, st));
             TQ_TRY(allgather(e, e->hidden, Hs));
             TQ_TRY(mark(e, K_OPROJ));
+        }
+        if (w.moe) {
+            // MoE FFN (runtime/qwen_forward_token.cpp:478-631, no shared expert): router over
+            // the post-attention RMSNorm -> top-k softmax -> gate/up of the chosen experts
+            // (RMSNorm prologue, SwiGLU epilogue) -> down of each on its own activation ->
+            // weighted sum in router order + residual
+            const int k = d.experts_per_tok, mi = d.moe_inter, E = d.n_experts;
+            if (w.router_f32) {
+                TQ_TRY(launch_moe_router(e->hidden, w.post_ln, d.rms_eps, H, w.router_f32, E, k,
+                                         e->moe_logits, e->moe_idx, e->moe_w, e->moe_ticket, st));
+            } else {
+                I4Job j{w.router_i4, e->moe_logits, nullptr, nullptr, E};
+                I4LaunchOpts o;
+                o.x = {X_RMSNORM, e->hidden, w.post_ln, d.rms_eps, nullptr};
+                o.pdl = pdl;
+                o.status = status;
+                TQ_TRY(launch_i4_matvec_ex(&j, 1, H, d.group_size, o, st));
+                TQ_TRY(launch_topk_softmax(e->moe_logits, E, k, e->moe_idx, e->moe_w, st));
+            }
+            TQ_TRY(mark(e, K_ROUTER));
+            {
+                I4Job j[2] = {{w.ex_gate, e->moe_h, nullptr, nullptr, k * mi},
+                              {w.ex_up, e->moe_u, nullptr, nullptr, k * mi}};
+                I4LaunchOpts o;
+                o.x = {X_RMSNORM, e->hidden, w.post_ln, d.rms_eps, nullptr};
+                o.pair_swiglu = true;
+                o.eidx = e->moe_idx;
+                o.estride = (long long)w.ex_gu_stride;
+                o.erows = mi;
+                o.nslots = k;
+                o.n_experts = E;
+                o.pdl = pdl;
+                o.status = status;
+                TQ_TRY(launch_i4_matvec_ex(j, 2, H, d.group_size, o, st));
+                TQ_TRY(mark(e, K_GATEUP));
+            }
+            {
+                I4Job j{w.ex_down, e->moe_o, nullptr, nullptr, k * H};
+                I4LaunchOpts o;
+                o.x = {X_PLAIN, e->moe_h, nullptr, 0.0f, nullptr};
+                o.eidx = e->moe_idx;
+                o.estride = (long long)w.ex_down_stride;
+                o.erows = H;
+                o.nslots = k;
+                o.n_experts = E;
+                o.xslots = true;
+                o.pdl = pdl;
+                o.status = status;
+                TQ_TRY(launch_i4_matvec_ex(&j, 1, mi, d.group_size, o, st));
+                TQ_TRY(mark(e, K_DOWN));
+            }
+            TQ_TRY(launch_moe_combine(e->hidden, e->moe_o, e->moe_w, k, H, st));
+            TQ_TRY(mark(e, K_COMBINE));
+            continue;
         }
         if (w.vq2) {
             VqLaunch a;
@@ -566,9 +674,23 @@ int create_impl(const tqb200_model_desc *desc, const tqb200_engine_opts *opts, t
         TQ_TRY(need_mat(s.k_proj, kvd, H, wdt, "k_proj", l));
         TQ_TRY(need_mat(s.v_proj, kvd, H, wdt, "v_proj", l));
         TQ_TRY(need_mat(s.o_proj, H, qd, wdt, "o_proj", l));
-        TQ_TRY(need_mat(s.gate_proj, d.inter, H, wdt, "gate_proj", l));
-        TQ_TRY(need_mat(s.up_proj, d.inter, H, wdt, "up_proj", l));
-        TQ_TRY(need_mat(s.down_proj, H, d.inter, wdt, "down_proj", l));
+        w.moe = d.model_type == TQB200_MODEL_QWEN3_MOE;
+        if (w.moe) {
+            TQ_CHECK_ARG(wdt == TQB200_DT_I4, "layer %d: MoE layers need i4 projections", l);
+            TQ_CHECK_ARG(s.router.data && s.router.rows == d.n_experts && s.router.cols == H &&
+                             (s.router.dtype == TQB200_DT_F32 || s.router.dtype == TQB200_DT_I4),
+                         "layer %d: router must be f32 or i4 [n_experts x hidden]", l);
+            TQ_CHECK_ARG(s.expert_gate && s.expert_up && s.expert_down, "layer %d: experts missing", l);
+            for (int x = 0; x < d.n_experts; ++x) {
+                TQ_TRY(need_mat(s.expert_gate[x], d.moe_inter, H, TQB200_DT_I4, "expert gate", l));
+                TQ_TRY(need_mat(s.expert_up[x], d.moe_inter, H, TQB200_DT_I4, "expert up", l));
+                TQ_TRY(need_mat(s.expert_down[x], H, d.moe_inter, TQB200_DT_I4, "expert down", l));
+            }
+        } else {
+            TQ_TRY(need_mat(s.gate_proj, d.inter, H, wdt, "gate_proj", l));
+            TQ_TRY(need_mat(s.up_proj, d.inter, H, wdt, "up_proj", l));
+            TQ_TRY(need_mat(s.down_proj, H, d.inter, wdt, "down_proj", l));
+        }
         TQ_CHECK_ARG(s.input_ln && s.post_ln, "layer %d: norms missing", l);
         TQ_CHECK_ARG((s.q_norm == nullptr) == (s.k_norm == nullptr),
                      "layer %d: q_norm/k_norm must both be present or both absent", l);
@@ -603,9 +725,13 @@ int create_impl(const tqb200_model_desc *desc, const tqb200_engine_opts *opts, t
         TQ_TRY(up_rows(s.k_proj, r * kvdl, kvdl, &w.k));
         TQ_TRY(up_rows(s.v_proj, r * kvdl, kvdl, &w.v));
         TQ_TRY(up_rows(s.o_proj, r * Hs, Hs, &w.o));
-        TQ_TRY(up_rows(s.gate_proj, r * Is, Is, &w.gate));
-        TQ_TRY(up_rows(s.up_proj, r * Is, Is, &w.up));
-        TQ_TRY(up_rows(s.down_proj, r * Hs, Hs, &w.down));
+        if (w.moe) {
+            TQ_TRY(up_experts(e, s, d, w));
+        } else {
+            TQ_TRY(up_rows(s.gate_proj, r * Is, Is, &w.gate));
+            TQ_TRY(up_rows(s.up_proj, r * Is, Is, &w.up));
+            TQ_TRY(up_rows(s.down_proj, r * Hs, Hs, &w.down));
+        }
         TQ_TRY(up_vec(e, s.q_bias ? s.q_bias + r * qdl : nullptr, qdl, &w.q_bias));
         TQ_TRY(up_vec(e, s.k_bias ? s.k_bias + r * kvdl : nullptr, kvdl, &w.k_bias));
         TQ_TRY(up_vec(e, s.v_bias ? s.v_bias + r * kvdl : nullptr, kvdl, &w.v_bias));
@@ -636,6 +762,20 @@ int create_impl(const tqb200_model_desc *desc, const tqb200_engine_opts *opts, t
     e->logits = f, f += d.vocab;
     e->pairs = reinterpret_cast<ArgPair *>(f);
     TQ_CHECK_ARG(G <= 32, "tp_size %d above 32", G);
+    if (d.model_type == TQB200_MODEL_QWEN3_MOE) {
+        const int k = d.experts_per_tok, mi = d.moe_inter;
+        const size_t n = (size_t)d.n_experts + 2 * (size_t)k * mi + (size_t)k * H + 3 * 64;
+        TQ_TRY(dev_alloc(e, n * 4 + 256, &p));
+        TQ_CUDA_TRY(cudaMemset(p, 0, n * 4 + 256));
+        float *m = (float *)p;
+        e->moe_h = m, m += (size_t)k * mi;       // 16-byte aligned rows of mi floats
+        e->moe_u = m, m += (size_t)k * mi;
+        e->moe_o = m, m += (size_t)k * H;
+        e->moe_logits = m, m += ((d.n_experts + 63) / 64) * 64;
+        e->moe_w = m, m += 64;
+        e->moe_idx = (int *)m, m += 64;
+        e->moe_ticket = (unsigned int *)m;
+    }
     e->layer_stride = (size_t)(d.n_kv_heads / G) * e->o.max_seq_len * hd;
     const size_t kv_bytes = 2 * (size_t)d.n_layers * e->layer_stride * (e->o.kv_fp16 ? 2 : 4);
     TQ_TRY(dev_alloc(e, kv_bytes, &e->kv));

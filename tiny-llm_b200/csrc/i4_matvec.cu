@@ -57,7 +57,25 @@ struct MvParams {
     XSource x;
     ArgmaxOut am;
     int *status;
+    // MoE experts.  Expert mode (eidx != nullptr): the rows of job j form nslots blocks
+    // of erows rows, block b being expert eidx[b] at job.w + eidx[b] * estride (passes
+    // never straddle blocks: R divides erows).  Slot mode (nslots > 0 with xslots):
+    // CTA c serves block c % nslots only, with x = x.src + (c % nslots) * K.
+    const int *eidx;
+    long long estride;
+    int erows, nslots, n_experts;
+    int xslots;
 };
+
+// Pass index of a CTA's i-th pass (>= total when it has none).
+__device__ __forceinline__ int pass_of(const MvParams &P, int i) {
+    if (!P.xslots) return blockIdx.x + i * gridDim.x;
+    const int nsub = gridDim.x / P.nslots;
+    const int slot = blockIdx.x % P.nslots, sub = blockIdx.x / P.nslots;
+    const int pps = P.erows / P.R;
+    const int pl = sub + i * nsub;
+    return (pl < pps && sub < nsub) ? slot * pps + pl : INT_MAX;
+}
 
 __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
     int d;
@@ -104,9 +122,23 @@ __device__ void block_argmax(float &bv, int &bi, float *sv, int *si) {
 __device__ uint32_t stage_rows(const MvParams &P, const I4Job &job, int row0, int row1,
                                uint8_t *dst, size_t cap, uint32_t *head, const uint8_t **src16) {
     const size_t RB = (size_t)((P.K + P.G - 1) / P.G) * (4 + P.G / 2);
-    const uintptr_t a = (uintptr_t)(job.w + (size_t)row0 * RB);
-    uintptr_t b = (uintptr_t)(job.w + (size_t)row1 * RB);
-    const uintptr_t mat_end16 = (uintptr_t)(job.w + (size_t)job.rows * RB) & ~(uintptr_t)15;
+    const uint8_t *base = job.w;
+    int rows_end = job.rows;
+    if (P.eidx) {  // the block's expert: rows relative to its own matrix
+        const int blk = row0 / P.erows;
+        int e = P.eidx[blk];
+        if (e < 0 || e >= P.n_experts) {  // self-check: never read outside the experts
+            if (P.status) atomicExch(P.status, kDevBadExpert);
+            e = 0;
+        }
+        base = job.w + (size_t)e * (size_t)P.estride;
+        row0 -= blk * P.erows;
+        row1 -= blk * P.erows;
+        rows_end = P.erows;
+    }
+    const uintptr_t a = (uintptr_t)(base + (size_t)row0 * RB);
+    uintptr_t b = (uintptr_t)(base + (size_t)row1 * RB);
+    const uintptr_t mat_end16 = (uintptr_t)(base + (size_t)rows_end * RB) & ~(uintptr_t)15;
     const uintptr_t a16 = a & ~(uintptr_t)15;
     uintptr_t b16 = (b + 15) & ~(uintptr_t)15;
     if (b16 > mat_end16) b16 = mat_end16;
@@ -234,11 +266,13 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
         fence_mbar_init();
         s_err = 0;
         s_issued = 0;
-        for (int s = 0; s < P.stages; ++s) {
-            const int p = blockIdx.x + s * gridDim.x;
-            if (p < total) {
-                issue_pass(P, p, s, full, stage_base, s_head);
-                s_issued = s + 1;
+        if (!P.eidx) {  // constant weights: before the dependency wait
+            for (int s = 0; s < P.stages; ++s) {
+                const int p = pass_of(P, s);
+                if (p < total) {
+                    issue_pass(P, p, s, full, stage_base, s_head);
+                    s_issued = s + 1;
+                }
             }
         }
         if (bulk_x && norm) {  // constant weights: before the dependency wait
@@ -250,6 +284,17 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
     // weights are in flight; now wait for the producer of x and let our dependents start
     griddep_wait();
     griddep_launch();
+    if (P.eidx && t == 0) {  // expert weights: which ones is known only now
+        for (int s = 0; s < P.stages; ++s) {
+            const int p = pass_of(P, s);
+            if (p < total) {
+                issue_pass(P, p, s, full, stage_base, s_head);
+                s_issued = s + 1;
+            }
+        }
+    }
+    // this CTA's activation vector (slot mode: its block's own)
+    const float *xsrc = P.x.src + (P.xslots ? (size_t)(blockIdx.x % P.nslots) * K : 0);
 
     // ---- activation, 8-column chunks c = t, t + blockDim, ... held in registers: one
     // round of 16-byte loads (unaligned sources: scalar loads), SwiGLU applied, the sum
@@ -263,7 +308,7 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
         for (int k = 0; k < 8; ++k) xv[it][k] = 0.0f;
         if (c >= nchunks) continue;
         if (bulk_x && 8 * c + 8 <= K) {
-            const float4 *s4 = reinterpret_cast<const float4 *>(P.x.src) + 2 * c;
+            const float4 *s4 = reinterpret_cast<const float4 *>(xsrc) + 2 * c;
             const float4 a = s4[0], b = s4[1];
             xv[it][0] = a.x, xv[it][1] = a.y, xv[it][2] = a.z, xv[it][3] = a.w;
             xv[it][4] = b.x, xv[it][5] = b.y, xv[it][6] = b.z, xv[it][7] = b.w;
@@ -282,7 +327,7 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
             for (int k = 0; k < 8; ++k) {
                 const int i = 8 * c + k;
                 if (i < K) {
-                    float v = P.x.src[i];
+                    float v = xsrc[i];
                     if (swiglu) v = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), P.x.up[i]);
                     xv[it][k] = v;
                 }
@@ -400,7 +445,7 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
         // with pass i - stages there
         if (lane == 0) {
             for (int i = P.stages;; ++i) {
-                const int p = blockIdx.x + i * gridDim.x;
+                const int p = pass_of(P, i);
                 if (p >= total) break;
                 const int s = i % P.stages;
                 if (!mbar_wait(&empty[s], (uint32_t)(i / P.stages - 1) & 1u, kWaitCycles)) {
@@ -437,7 +482,7 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
             }
         }
         for (int i_pass = 0;; ++i_pass) {
-            const int p = blockIdx.x + i_pass * gridDim.x;
+            const int p = pass_of(P, i_pass);
             if (p >= total) break;
             const int s = i_pass % P.stages;
             const uint32_t parity = (uint32_t)(i_pass / P.stages) & 1u;
@@ -753,7 +798,7 @@ struct Shape {
 // consecutive rows, one bulk copy (two in paired mode): a single pass when a CTA's
 // share of the rows fits in 64 KB (R = rows / SMs, so the passes spread evenly),
 // otherwise passes of up to 32 KB through a ring of up to ~200 KB, all in flight.
-Shape plan(int K, int G, bool pair, bool norm, int rows_total) {
+Shape plan(int K, int G, bool pair, bool norm, int rows_total, int r_div = 0) {
     Shape L;
     L.seg = (G % 64 == 0) ? 64 : 32;
     const int ng = (K + G - 1) / G;
@@ -773,6 +818,10 @@ Shape plan(int K, int G, bool pair, bool norm, int rows_total) {
         L.R = per_cta;
     } else {
         L.R = (int)std::max<size_t>(1, (32 * 1024) / (RB * np));
+    }
+    if (r_div > 0) {  // passes must not straddle r_div-row blocks
+        L.R = std::min(L.R, r_div);
+        while (r_div % L.R) --L.R;
     }
     L.RP = (L.R + L.S - 1) / L.S;
     const size_t region = ((size_t)L.R * RB + 32 + 127) / 128 * 128;
@@ -805,7 +854,8 @@ int grid_for(Kern k, int block, size_t smem, int work) {
 }
 
 template <int SEG>
-int launch_tma(const MvParams &P, const Shape &L, int passes, bool pdl, cudaStream_t st) {
+int launch_tma(const MvParams &P, const Shape &L, int passes, bool pdl, cudaStream_t st,
+               int grid_fixed = 0) {
     auto k = i4_mv_tma_kernel<SEG>;
     static KernelSmem attr_set;
     int smem_max = 0;
@@ -814,7 +864,7 @@ int launch_tma(const MvParams &P, const Shape &L, int passes, bool pdl, cudaStre
                  L.smem, smem_max);
     // one CTA per SM for this kernel (the activation prologue is paid once per SM); the
     // SM's second slot is for the next kernel
-    const int grid = std::min(grid_for(k, L.block, L.smem, passes), num_sms());
+    const int grid = grid_fixed > 0 ? grid_fixed : std::min(grid_for(k, L.block, L.smem, passes), num_sms());
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(L.block);
@@ -866,13 +916,32 @@ int launch_i4_matvec_ex(const I4Job *jobs, int n_jobs, int in_dim, int group_siz
     int rows_total = 0;
     for (int j = 0; j < n_jobs; ++j)
         if (!pair || j == 0) rows_total += std::max(0, jobs[j].rows);
-    const Shape L = plan(in_dim, group_size, pair, o.x.mode == X_RMSNORM, rows_total);
+    if (o.eidx) {
+        TQ_CHECK_ARG(o.erows > 0 && o.nslots > 0 && o.n_experts > 0 && !o.argmax.token,
+                     "expert matvec: bad erows %d / nslots %d / n_experts %d", o.erows, o.nslots,
+                     o.n_experts);
+        for (int j = 0; j < n_jobs; ++j)
+            TQ_CHECK_ARG(jobs[j].rows == o.nslots * o.erows && (uintptr_t)jobs[j].w % 16u == 0 &&
+                             o.estride % 16 == 0,
+                         "expert matvec: job %d is not nslots x erows aligned rows", j);
+        TQ_CHECK_ARG(!o.xslots || (n_jobs == 1 && !pair && o.x.mode == X_PLAIN),
+                     "per-slot activations need one plain job");
+    }
+    P.eidx = o.eidx;
+    P.estride = o.estride;
+    P.erows = o.erows;
+    P.nslots = o.nslots;
+    P.n_experts = o.n_experts;
+    P.xslots = o.xslots ? 1 : 0;
+    const Shape L = plan(in_dim, group_size, pair, o.x.mode == X_RMSNORM, rows_total,
+                         o.eidx ? o.erows : 0);
     bool aligned = true;  // the TMA path needs 16-byte aligned matrix bases
     for (int j = 0; j < n_jobs; ++j) aligned = aligned && ((uintptr_t)jobs[j].w % 16u == 0);
     const bool fast = (group_size % 32 == 0) && L.seg != 0 && aligned;
     if (!fast) {
-        TQ_CHECK_ARG(o.x.mode == X_PLAIN && !o.argmax.token && !pair,
-                     "fused prologue/epilogue needs group_size %% 32 == 0 and aligned weights");
+        TQ_CHECK_ARG(o.x.mode == X_PLAIN && !o.argmax.token && !pair && !o.eidx,
+                     "fused prologue/epilogue and expert mode need group_size %% 32 == 0 and "
+                     "aligned weights");
     }
     const int R = fast ? L.R : 1;
     int acc = 0;
@@ -887,6 +956,7 @@ int launch_i4_matvec_ex(const I4Job *jobs, int n_jobs, int in_dim, int group_siz
     auto a16 = [](const void *p) { return ((uintptr_t)p & 15u) == 0; };
     P.x_bulk = (in_dim % 4 == 0) && a16(o.x.src) && (o.x.mode != X_RMSNORM || a16(o.x.norm_w)) &&
                (o.x.mode != X_SWIGLU || a16(o.x.up));
+    TQ_CHECK_ARG(!o.xslots || P.x_bulk, "per-slot activations need 16-byte aligned rows of x");
     if (acc == 0) return TQB200_OK;
     if (fast) {
         P.nt = L.nt;
@@ -895,8 +965,10 @@ int launch_i4_matvec_ex(const I4Job *jobs, int n_jobs, int in_dim, int group_siz
         P.R = L.R;
         P.stages = L.stages;
         P.stage_bytes = L.stage_bytes;
-        if (L.seg == 64) return launch_tma<64>(P, L, acc, o.pdl, stream);
-        return launch_tma<32>(P, L, acc, o.pdl, stream);
+        // slot mode: a multiple of nslots CTAs, every block served by the same count
+        const int grid = o.xslots ? o.nslots * std::max(1, num_sms() / o.nslots) : 0;
+        if (L.seg == 64) return launch_tma<64>(P, L, acc, o.pdl, stream, grid);
+        return launch_tma<32>(P, L, acc, o.pdl, stream, grid);
     }
     const int grid = std::max(1, std::min((acc + 7) / 8, num_sms() * 8));
     i4_matvec_generic_kernel<<<grid, 256, 0, stream>>>(P);

@@ -52,6 +52,13 @@ struct I4LaunchOpts {
     bool pdl = false;               // launch with programmatic stream serialisation
     bool pair_swiglu = false;       // jobs (gate, up): y_gate = silu(gate x) * (up x)
     int *status = nullptr;          // device error word (bounded-wait timeouts)
+    // MoE experts chosen on the device: every job's rows are nslots blocks of erows
+    // rows; block b reads expert eidx[b] (device int) at job.w + eidx[b] * estride.
+    const int *eidx = nullptr;
+    long long estride = 0;
+    int erows = 0, nslots = 0, n_experts = 0;
+    // per-block activations (one plain job): block b uses x.src + b * in_dim
+    bool xslots = false;
 };
 
 // y_j = W_j x (+bias_j / +resid_j) for up to 3 jobs in one launch (q/k/v, gate/up, ...).
@@ -182,6 +189,12 @@ int argmax_blocks(int n);
 int launch_argmax(const float *l, int n, float *pv, int *pi, unsigned int *ticket, int *out,
                   cudaStream_t st);
 int launch_topk_softmax(const float *logits, int n, int k, int *idx, float *w, cudaStream_t st);
+// MoE decode: f32 router over rmsnorm(h) * norm_w, then top-k softmax (ticket: zeroed
+// device word, reset by the kernel); and h += sum_t wts[t] * o[t] in router order.
+int launch_moe_router(const float *h, const float *norm_w, float eps, int H, const float *W, int E,
+                      int k, float *logits, int *idx, float *wts, unsigned int *ticket,
+                      cudaStream_t st);
+int launch_moe_combine(float *h, const float *o, const float *wts, int k, int H, cudaStream_t st);
 int launch_embed(const void *table, int dtype, const int *token, int dim, int group_size,
                  float *out, cudaStream_t st);
 

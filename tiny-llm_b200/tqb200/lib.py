@@ -336,7 +336,8 @@ class Engine:
         _check(load().tqb200_engine_generate(self.h, int(token), n_steps, out, C.byref(ms)))
         return out[:n_steps].tolist(), ms.value
 
-    KINDS = ("embed", "qkv", "qk_rope_kv", "attention", "o_proj", "gate_up", "down", "lm_head")
+    KINDS = ("embed", "qkv", "qk_rope_kv", "attention", "o_proj", "gate_up", "down", "lm_head",
+             "router", "moe_combine")
 
     def profile_step(self, token: int):
         """One kernel-by-kernel step timed with CUDA events; returns (next, {kind: ms})."""
