@@ -307,11 +307,17 @@ def matvec_bytes_by_kind(spec) -> dict:
         w = rows * i4_row_bytes(cols, G) if (i4 or not vq2) else 2048 + rows * cols // 4
         return w + cols * 4 + rows * 4
 
-    return {"qkv": L * (mv(qd, H) + 2 * mv(kvd, H) - 2 * H * 4),
-            "o_proj": L * (mv(H, qd) + H * 4),               # + residual read
-            "gate_up": L * (2 * mv(I, H) - H * 4),
-            "down": L * (mv(H, I) + I * 4 + H * 4),           # + up read (SwiGLU) + residual
-            "lm_head": mv(spec.vocab, H, i4=True)}
+    out = {"qkv": L * (mv(qd, H) + 2 * mv(kvd, H) - 2 * H * 4),
+           "o_proj": L * (mv(H, qd) + H * 4),               # + residual read
+           "gate_up": L * (2 * mv(I, H) - H * 4),
+           "down": L * (mv(H, I) + I * 4 + H * 4),           # + up read (SwiGLU) + residual
+           "lm_head": mv(spec.vocab, H, i4=True)}
+    if spec.n_experts:  # MoE: the router and the k chosen experts' matrices per layer
+        k, mi, E = spec.experts_per_tok, spec.moe_inter, spec.n_experts
+        out["router"] = L * (E * H * 4 + H * 4 + E * 4)
+        out["gate_up"] = L * (2 * mv(mi, H) * k - (2 * k - 1) * H * 4)
+        out["down"] = L * k * mv(H, mi)
+    return out
 
 
 def step_bytes(spec, ctx: int, kv_bytes: int) -> int:
@@ -328,6 +334,10 @@ DECODE_WORKLOADS = {
     "decode-qwen2.5-0.5b": dict(
         cfg="BASELINE config 2: Qwen2.5-0.5B-shaped i4 g64, fp32 KV", preset="QWEN25_05B",
         kv16=False, ctx=32, dtype="u4 weights, f32 activations, f32 KV"),
+    "decode-qwen3-30b-a3b": dict(
+        cfg="BASELINE config 5 decode: Qwen3-30B-A3B-shaped MoE, i4 g64 experts, top-8 of 128, "
+            "fp32 KV", preset="QWEN3_30B_A3B", kv16=False, ctx=576,
+        dtype="u4 weights, f32 activations, f32 KV"),
     "decode-qwen3-0.6b-vq2": dict(
         cfg="BASELINE config 3 step: Qwen3-0.6B-shaped VQ2 + BiIP on every projection, fp32 KV",
         preset="QWEN3_06B_VQ2", kv16=False, ctx=32,
@@ -342,6 +352,8 @@ def decode_spec(wl: dict, max_seq: int):
     # i4 weights as random codes/scales/zeros (config-1 distributions) instead of RTN of
     # N(0,0.02): same bytes and shapes, built in seconds
     kw = {"weights": "codes"} if base.weight_dtype == "i4" else {}
+    if base.n_experts:  # one layer's worth of expert tensors on the host, repeated (every
+        kw["expert_layers"] = 1  # layer still gets its own device copy)
     return replace(base, max_seq_len=max_seq, **kw)
 
 
@@ -403,7 +415,9 @@ def bench_decode(args, rank, pg, pk, pk_kind):
     # embed, per layer qkv / attention (QK-norm, RoPE and KV append fused) / o_proj /
     # gate_up / down, lm_head (+argmax), the device-side token feed, and with tensor
     # parallelism the cross-rank argmax (NCCL's all-gather kernels are not counted)
-    launches = 2 + 5 * spec.n_layers + 1 + (1 if world > 1 else 0)
+    # MoE layers: qkv, attention, o_proj, router (+ top-k), gate/up, down, combine
+    per_layer = 7 if spec.n_experts else 5
+    launches = 2 + per_layer * spec.n_layers + 1 + (1 if world > 1 else 0)
     out = {
         "metric": f"decode ms/token, batch 1 ({wl['cfg']}, ctx {ctx})",
         "value": round(ms_step, 4), "unit": "ms/token", "n_gpus": world, "steps": K, "warmup": W,
@@ -454,8 +468,9 @@ def ref_decode_rate(workload: str, ctx: int, threads_note: str = ""):
     base = decode_spec(wl, 64)
     have_ref = RefLib.available()
     times = {}
+    la, lb = (2, 3) if base.n_experts else (2, 6)
     with tempfile.TemporaryDirectory() as td:
-        for nl in (2, 6):
+        for nl in (la, lb):
             spec = replace(base, n_layers=nl)
             sm = SynthModel(spec, seed=0)
             if have_ref:
@@ -476,8 +491,8 @@ def ref_decode_rate(workload: str, ctx: int, threads_note: str = ""):
             times[nl] = best
             m.close()
             del sm
-    t_layer = (times[6] - times[2]) / 4
-    t_head = times[2] - 2 * t_layer
+    t_layer = (times[lb] - times[la]) / (lb - la)
+    t_head = times[la] - la * t_layer
     # attention over the 4096-position KV of one layer vs the 4-position one above
     lib = RefLib() if have_ref else Oracle()
     H, KVH, hd = base.n_heads, base.n_kv_heads, base.head_dim
@@ -490,8 +505,8 @@ def ref_decode_rate(workload: str, ctx: int, threads_note: str = ""):
     t_attn = time.perf_counter() - t0
     total = t_head + base.n_layers * (t_layer + t_attn)
     kind = "reference" if have_ref else "port"
-    sample = (f"forward_token of 2- and 6-layer {base.name} models at context ~4 "
-              f"(best of 3: {times[2]*1e3:.0f} / {times[6]*1e3:.0f} ms per token) extrapolated to "
+    sample = (f"forward_token of {la}- and {lb}-layer {base.name} models at context ~4 "
+              f"(best of 3: {times[la]*1e3:.0f} / {times[lb]*1e3:.0f} ms per token) extrapolated to "
               f"{base.n_layers} layers, plus attention_decode_ref at context {ctx} "
               f"({t_attn*1e3:.1f} ms per layer); 1 thread (the reference's x86 kernels are "
               f"single-threaded){threads_note}")

@@ -524,19 +524,93 @@ __global__ void topk_softmax_kernel(const float *__restrict__ logits, int n, int
 }
 
 // ------------------------------------------------------------------ MoE router + combine
+// Top-k softmax of n <= 32 * kRouterPer logits by one warp: the k largest (value, then
+// lowest index, as topk_softmax_ref's partial_sort on distinct values) by k rounds of a
+// warp-wide (value, index) maximum, then softmax over them with exp and the sum in double
+// (kernels/topk_softmax/topk_softmax_ref.cpp:41-78).
+constexpr int kRouterPer = 32;  // logits per lane (n <= 1024)
+
+__device__ void topk_softmax_warp(const float *__restrict__ logits, int n, int k,
+                                  int *__restrict__ idx_out, float *__restrict__ w_out) {
+    const int lane = threadIdx.x & 31;
+    float v[kRouterPer];
+#pragma unroll
+    for (int j = 0; j < kRouterPer; ++j) {
+        const int i = lane + 32 * j;
+        v[j] = i < n ? logits[i] : -INFINITY;
+    }
+    uint32_t taken = 0;  // bit j: v[j] already chosen
+    float sel_v = 0.0f, vmax = 0.0f;
+    int sel_i = 0;
+    const int kk = min(k, n);
+    for (int t = 0; t < kk; ++t) {
+        float bv = -INFINITY;
+        int bi = INT_MAX;
+#pragma unroll
+        for (int j = 0; j < kRouterPer; ++j) {
+            const int i = lane + 32 * j;
+            if (i < n && !((taken >> j) & 1u) && (bi == INT_MAX || v[j] > bv)) {
+                bv = v[j];
+                bi = i;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (oi != INT_MAX && (bi == INT_MAX || ov > bv || (ov == bv && oi < bi))) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+        if (t == 0) vmax = bv;
+        if (lane == t) {
+            sel_v = bv;
+            sel_i = bi;
+        }
+    }
+    // lane t < kk holds the t-th choice
+    const float e = lane < kk ? (float)exp((double)sel_v - (double)vmax) : 0.0f;
+    double sum = (double)e;
+    for (int t = 1; t < kk; ++t) sum += __shfl_sync(0xffffffffu, (double)e, t) * (lane == 0);
+    sum = __shfl_sync(0xffffffffu, sum, 0);
+    if (lane < k) {
+        const double inv = sum > 0.0 ? 1.0 / sum : 0.0;
+        idx_out[lane] = lane < kk ? sel_i : -1;
+        w_out[lane] = lane < kk ? (float)((double)e * inv) : 0.0f;
+    }
+}
+
 // MoE router of one decode step (runtime/qwen_forward_token.cpp:478-491 with an f32
 // router): normed = rmsnorm(h) * post_ln (rmsnorm_ref semantics), logits[e] = W[e] . normed
 // in double as matvec_f32_ref (kernels/matvec/matvec_f32_ref.cpp), then, in the last CTA
-// to finish, top-k softmax (topk_softmax_ref).  One warp per router row; every CTA
-// normalises the (small) hidden vector itself.
-__global__ void moe_router_kernel(const float *__restrict__ h, const float *__restrict__ norm_w,
-                                  float eps, int H, const float *__restrict__ W, int E, int k,
-                                  float *__restrict__ logits, int *__restrict__ idx,
-                                  float *__restrict__ wts, unsigned int *ticket) {
-    extern __shared__ float xn[];  // [H]
-    __shared__ double s_red[32];
+// to finish, top-k softmax.  One warp per router row, its whole row loaded up front
+// (float4, many loads in flight); every CTA normalises the (small) hidden vector itself.
+constexpr int kRouterWarps = 4;
+constexpr int kRouterChunk = 32 * 4 * 16;  // floats of a row one warp loads at once
+
+__global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(
+    const float *__restrict__ h, const float *__restrict__ norm_w, float eps, int H,
+    const float *__restrict__ W, int E, int k, float *__restrict__ logits, int *__restrict__ idx,
+    float *__restrict__ wts, unsigned int *ticket) {
+    extern __shared__ __align__(16) float xn[];  // [H]
+    __shared__ double s_red[kRouterWarps];
     __shared__ bool s_last;
-    const int t = threadIdx.x, lane = t & 31, warp = t >> 5, nw = blockDim.x >> 5;
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int e = blockIdx.x * kRouterWarps + warp;
+    const float *row = W + (size_t)min(e, E - 1) * H;
+    const bool vec = (H % 4 == 0) && (((uintptr_t)W & 15) == 0);
+    // the router row does not depend on the previous kernel: its first chunk is loaded
+    // before the dependency wait
+    float4 wv[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        const int c = 4 * (lane + 32 * j);
+        wv[j] = (vec && c < H) ? *reinterpret_cast<const float4 *>(row + c) : make_float4(0, 0, 0, 0);
+    }
+    griddep_wait();
+    griddep_launch();
     double ss = 0.0;
     for (int i = t; i < H; i += blockDim.x) {
         const float v = h[i];
@@ -546,15 +620,36 @@ __global__ void moe_router_kernel(const float *__restrict__ h, const float *__re
     if (lane == 0) s_red[warp] = ss;
     __syncthreads();
     double tot = 0.0;
-    for (int w = 0; w < nw; ++w) tot += s_red[w];
+    for (int w = 0; w < kRouterWarps; ++w) tot += s_red[w];
     const float scale = 1.0f / sqrtf(__fadd_rn((float)(tot / H), eps));
     for (int i = t; i < H; i += blockDim.x) xn[i] = __fmul_rn(__fmul_rn(h[i], scale), norm_w[i]);
     __syncthreads();
-    const int e = blockIdx.x * nw + warp;
     if (e < E) {
-        const float *row = W + (size_t)e * H;
         double acc = 0.0;
-        for (int i = lane; i < H; i += 32) acc += (double)row[i] * (double)xn[i];
+        if (vec) {
+            for (int c0 = 0; c0 < H; c0 += kRouterChunk) {
+                if (c0 > 0) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int c = c0 + 4 * (lane + 32 * j);
+                        wv[j] = c < H ? *reinterpret_cast<const float4 *>(row + c) : make_float4(0, 0, 0, 0);
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int c = c0 + 4 * (lane + 32 * j);
+                    if (c < H) {
+                        const float4 x4 = *reinterpret_cast<const float4 *>(xn + c);
+                        acc += (double)wv[j].x * (double)x4.x;
+                        acc += (double)wv[j].y * (double)x4.y;
+                        acc += (double)wv[j].z * (double)x4.z;
+                        acc += (double)wv[j].w * (double)x4.w;
+                    }
+                }
+            }
+        } else {
+            for (int i = lane; i < H; i += 32) acc += (double)row[i] * (double)xn[i];
+        }
         acc = warp_sum_d(acc);
         if (lane == 0) logits[e] = (float)acc;
     }
@@ -564,7 +659,7 @@ __global__ void moe_router_kernel(const float *__restrict__ h, const float *__re
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    topk_softmax_block(logits, E, k, idx, wts);
+    if (warp == 0) topk_softmax_warp(logits, E, k, idx, wts);
     if (t == 0) *ticket = 0u;  // ready for the next launch (graph replay)
 }
 
@@ -572,6 +667,8 @@ __global__ void moe_router_kernel(const float *__restrict__ h, const float *__re
 // rounding points (runtime/qwen_forward_token.cpp:604-609, :627-631).
 __global__ void moe_combine_kernel(float *__restrict__ h, const float *__restrict__ o,
                                    const float *__restrict__ wts, int k, int H) {
+    griddep_wait();
+    griddep_launch();
     for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < H; j += gridDim.x * blockDim.x) {
         float acc = 0.0f;
         for (int t = 0; t < k; ++t) acc = __fadd_rn(acc, __fmul_rn(wts[t], o[(size_t)t * H + j]));
@@ -775,26 +872,39 @@ int launch_argmax(const float *l, int n, float *pv, int *pi, unsigned int *ticke
     return TQB200_OK;
 }
 
-int launch_moe_router(const float *h, const float *norm_w, float eps, int H, const float *W, int E,
-                      int k, float *logits, int *idx, float *wts, unsigned int *ticket,
-                      cudaStream_t st) {
-    TQ_CHECK_ARG(E > 0 && E <= 1024 && k > 0 && k <= 64 && k <= E && H > 0,
-                 "moe router: E %d k %d H %d", E, k, H);
-    const int threads = 256, rows_per = threads / 32;
-    const size_t smem = (size_t)H * 4;
-    TQ_CHECK_ARG(smem <= 48 * 1024, "moe router: hidden %d too large", H);
-    moe_router_kernel<<<(E + rows_per - 1) / rows_per, threads, smem, st>>>(
-        h, norm_w, eps, H, W, E, k, logits, idx, wts, ticket);
-    TQ_CUDA_TRY(cudaGetLastError());
+template <typename Kern, typename... Args>
+int launch_pdl(Kern k, int grid, int block, size_t smem, bool pdl, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    TQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, k, args...));
     return TQB200_OK;
 }
 
-int launch_moe_combine(float *h, const float *o, const float *wts, int k, int H, cudaStream_t st) {
+int launch_moe_router(const float *h, const float *norm_w, float eps, int H, const float *W, int E,
+                      int k, float *logits, int *idx, float *wts, unsigned int *ticket, bool pdl,
+                      cudaStream_t st) {
+    TQ_CHECK_ARG(E > 0 && E <= 32 * kRouterPer && k > 0 && k <= 32 && k <= E && H > 0,
+                 "moe router: E %d k %d H %d", E, k, H);
+    const size_t smem = (size_t)H * 4;
+    TQ_CHECK_ARG(smem <= 48 * 1024, "moe router: hidden %d too large", H);
+    return launch_pdl(moe_router_kernel, (E + kRouterWarps - 1) / kRouterWarps, kRouterWarps * 32,
+                      smem, pdl, st, h, norm_w, eps, H, W, E, k, logits, idx, wts, ticket);
+}
+
+int launch_moe_combine(float *h, const float *o, const float *wts, int k, int H, bool pdl,
+                       cudaStream_t st) {
     TQ_CHECK_ARG(k > 0 && H > 0, "moe combine: k %d H %d", k, H);
     const int threads = 256;
-    moe_combine_kernel<<<(H + threads - 1) / threads, threads, 0, st>>>(h, o, wts, k, H);
-    TQ_CUDA_TRY(cudaGetLastError());
-    return TQB200_OK;
+    return launch_pdl(moe_combine_kernel, (H + threads - 1) / threads, threads, 0, pdl, st, h, o,
+                      wts, k, H);
 }
 
 int launch_topk_softmax(const float *logits, int n, int k, int *idx, float *w, cudaStream_t st) {

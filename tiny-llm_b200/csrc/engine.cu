@@ -457,7 +457,8 @@ int launch_forward(tqb200_engine *e) {
             const int k = d.experts_per_tok, mi = d.moe_inter, E = d.n_experts;
             if (w.router_f32) {
                 TQ_TRY(launch_moe_router(e->hidden, w.post_ln, d.rms_eps, H, w.router_f32, E, k,
-                                         e->moe_logits, e->moe_idx, e->moe_w, e->moe_ticket, st));
+                                         e->moe_logits, e->moe_idx, e->moe_w, e->moe_ticket, pdl,
+                                         st));
             } else {
                 I4Job j{w.router_i4, e->moe_logits, nullptr, nullptr, E};
                 I4LaunchOpts o;
@@ -499,7 +500,7 @@ int launch_forward(tqb200_engine *e) {
                 TQ_TRY(launch_i4_matvec_ex(&j, 1, mi, d.group_size, o, st));
                 TQ_TRY(mark(e, K_DOWN));
             }
-            TQ_TRY(launch_moe_combine(e->hidden, e->moe_o, e->moe_w, k, H, st));
+            TQ_TRY(launch_moe_combine(e->hidden, e->moe_o, e->moe_w, k, H, pdl, st));
             TQ_TRY(mark(e, K_COMBINE));
             continue;
         }

@@ -192,9 +192,10 @@ int launch_topk_softmax(const float *logits, int n, int k, int *idx, float *w, c
 // MoE decode: f32 router over rmsnorm(h) * norm_w, then top-k softmax (ticket: zeroed
 // device word, reset by the kernel); and h += sum_t wts[t] * o[t] in router order.
 int launch_moe_router(const float *h, const float *norm_w, float eps, int H, const float *W, int E,
-                      int k, float *logits, int *idx, float *wts, unsigned int *ticket,
+                      int k, float *logits, int *idx, float *wts, unsigned int *ticket, bool pdl,
                       cudaStream_t st);
-int launch_moe_combine(float *h, const float *o, const float *wts, int k, int H, cudaStream_t st);
+int launch_moe_combine(float *h, const float *o, const float *wts, int k, int H, bool pdl,
+                       cudaStream_t st);
 int launch_embed(const void *table, int dtype, const int *token, int dim, int group_size,
                  float *out, cudaStream_t st);
 

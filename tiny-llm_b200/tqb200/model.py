@@ -48,6 +48,8 @@ class ModelSpec:
     router_dtype: str = "f32"         # MoE router matrix dtype
     norm_noise: float = 0.0           # 0 -> norm weights exactly 1 (make_fake_model.py)
     weights: str = "rtn"              # "rtn" (N(0,.02) -> RTN) | "codes" (direct random codes)
+    expert_layers: int = 0            # > 0: layer l reuses the expert tensors of layer
+                                      # l % expert_layers (host memory of a large MoE model)
 
 
 # The BASELINE shapes; vocab 151936 everywhere.
@@ -174,8 +176,14 @@ class SynthModel:
                                 self._rng(nxt()).normal(0.0, 1.0 / np.sqrt(H), (s.n_experts, H))
                                 .astype(np.float32))
                 self._add(p + "mlp.gate.weight", rt)
+                src = li % s.expert_layers if s.expert_layers > 0 else li
                 for e in range(s.n_experts):
                     pe = p + f"mlp.experts.{e}."
+                    if src != li:  # the same tensors (bytes) as layer `src`
+                        ps = f"model.layers.{src}.mlp.experts.{e}."
+                        for nm in ("gate_proj.weight", "up_proj.weight", "down_proj.weight"):
+                            self._add(pe + nm, replace(self.tensors[ps + nm]))
+                        continue
                     self._add(pe + "gate_proj.weight", self._quant(nxt(), s.moe_inter, H))
                     self._add(pe + "up_proj.weight", self._quant(nxt(), s.moe_inter, H))
                     self._add(pe + "down_proj.weight", self._quant(nxt(), H, s.moe_inter))
