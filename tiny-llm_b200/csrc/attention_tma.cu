@@ -177,6 +177,39 @@ __device__ __forceinline__ void score_rows(const KV *kr, int rows, const float (
     if (r < rows && g < G) sc_rows[r * G + g] = acc[0] * scale;
 }
 
+// As score_rows, but each lane returns its value (scale * q_g . k of row lane / GP,
+// head lane % GP), -inf for lanes past `rows` or G.
+template <typename KV, int HD, int G>
+__device__ __forceinline__ float score_lane(const KV *kr, int rows, const float (&qr)[G][HD / 32],
+                                            int lane, float scale) {
+    constexpr int D = HD / 32;
+    constexpr int GP = Pow2<G>::v;
+    constexpr int RW = 32 / GP;
+    float acc[32];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+        float k[D];
+        if (r < rows) {
+            lds_kv<D>(kr + (size_t)r * HD + lane * D, k);
+        } else {
+#pragma unroll
+            for (int d = 0; d < D; ++d) k[d] = 0.0f;
+        }
+#pragma unroll
+        for (int g = 0; g < GP; ++g) {
+            float a = 0.0f;
+            if (g < G) {
+#pragma unroll
+                for (int d = 0; d < D; ++d) a = fmaf(qr[g][d], k[d], a);
+            }
+            acc[r * GP + g] = a;
+        }
+    }
+    warp_reduce_scatter<32, 16>(acc, lane);
+    const int r = lane / GP, g = lane - r * GP;
+    return (r < rows && g < G) ? acc[0] * scale : -INFINITY;
+}
+
 // Warp-level QK-norm (optional) + rotate-half RoPE of one head vector, in place in
 // shared memory; the same float operations as the per-head engine kernel.
 template <int HD>
@@ -221,8 +254,6 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int RB = HD * (int)sizeof(KV);  // bytes per cached row
     constexpr int D = HD / 32;                // dimensions per lane in the score phase
-    constexpr int DG = HD / 4;                // dimension quads in the P.V phase
-    constexpr int TS = kThreads / DG;         // row subsets in the P.V phase
     constexpr int half = HD / 2;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);  // [stages] tiles
     uint64_t *bar_c = bars + kStages;                      // constant vectors
@@ -238,15 +269,17 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
     float *sn = cs + half;                                      // [HD/2]
     float *qn = sn + half;                                      // [HD] QK-norm weights
     float *kn = qn + HD;                                        // [HD]
-    float *sc = kn + HD;                                        // [chunk_max][G]
-    // after the last tile the ring holds the P.V reduction and this CTA's partial
-    float *red = reinterpret_cast<float *>(ring);               // [TS][G][HD]
-    float *po = red + TS * G * HD;                              // [G][HD] partial o
+    // after the last tile the ring holds the warps' partials and this CTA's partial
+    float *wpo = reinterpret_cast<float *>(ring);               // [warps][G][HD]
+    float *wpm = wpo + kWarps * G * HD;                         // [warps][G]
+    float *wpl = wpm + kWarps * G;                              // [warps][G]
+    float *po = wpl + kWarps * G;                               // [G][HD] partial o
     float *pm = po + G * HD;                                    // [G] partial m
     float *pl = pm + G;                                         // [G] partial l
     float *wgt = pl + G;                                        // [ns][G] merge weights (+ m, l copies)
     __shared__ float s_m[G], s_l[G];
-    __shared__ int s_err;
+    __shared__ int s_err, s_issued;
+    __shared__ int s_done[kStages];  // warps finished with the slot's current tile
 
     cg::cluster_group cluster = cg::this_cluster();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -264,23 +297,25 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
     const bool owner = fused && seq - 1 >= t0 && seq - 1 < t0 + n;  // holds the new row
     const int n_copy = owner ? n - 1 : n;
     const int T = P.tile_rows, NST = P.stages;
-    const int nk = (n_copy + T - 1) / T;
-    const int total = 2 * nk;  // K tiles, then V tiles
+    const int total = (n_copy + T - 1) / T;  // tiles: K and V of T rows in one slot
     const size_t row0 = (size_t)kh * P.max_seq + t0;
     const bool has_norm = P.q_norm != nullptr;
     auto issue = [&](int i) {
-        const int j = i < nk ? i : i - nk;
-        const int r0 = j * T, rows = min(T, n_copy - r0);
-        const uint8_t *src = (i < nk ? P.kc : P.vc) + (row0 + r0) * RB;
+        const int r0 = i * T, rows = min(T, n_copy - r0);
         uint64_t *bar = &bars[i % NST];
+        uint8_t *slot = ring + (size_t)(i % NST) * 2 * T * RB;
         fence_proxy_async_smem();
-        mbar_arrive_expect_tx(bar, (uint32_t)(rows * RB));
-        bulk_g2s(ring + (size_t)(i % NST) * T * RB, src, (uint32_t)(rows * RB), bar);
+        mbar_arrive_expect_tx(bar, (uint32_t)(2 * rows * RB));
+        bulk_g2s(slot, P.kc + (row0 + r0) * RB, (uint32_t)(rows * RB), bar);
+        bulk_g2s(slot + (size_t)T * RB, P.vc + (row0 + r0) * RB, (uint32_t)(rows * RB), bar);
+        atomicMax(&s_issued, i + 1);
     };
     if (tid == 0) {
         for (int s = 0; s < kStages + 2; ++s) mbar_init(&bars[s], 1);
         fence_mbar_init();
         s_err = 0;
+        s_issued = 0;
+        for (int s = 0; s < kStages; ++s) s_done[s] = 0;
         if (fused) {
             for (int i = 0; i < min(total, NST); ++i) issue(i);
             if (P.bulk_in) {
@@ -362,92 +397,91 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
     for (int g = 0; g < G; ++g)
 #pragma unroll
         for (int d = 0; d < D; ++d) qr[g][d] = qs[g * HD + lane * D + d];
-    if (owner && warp == 0 && !s_err)
-        score_row<KV, HD, G>(lastk, qr, lane, P.scale, sc + (size_t)(n - 1) * G);
 
-    // ---- K tiles -> scores
-    int it = 0;
-    for (; !s_err && it < nk; ++it) {
-        if (tid == 0 && !mbar_wait(&bars[it % NST], (uint32_t)(it / NST) & 1u, kWaitCycles))
-            s_err = 1;
-        __syncthreads();
-        if (s_err) break;
-        const KV *tile = reinterpret_cast<const KV *>(ring + (size_t)(it % NST) * T * RB);
-        const int r0 = it * T, rows = min(T, n_copy - r0);
-        constexpr int RW = 32 / Pow2<G>::v;
-        for (int rb = warp * RW; rb < rows; rb += kWarps * RW)
-            score_rows<KV, HD, G>(tile + (size_t)rb * HD, rows - rb, qr, lane, P.scale,
-                                  sc + (size_t)(r0 + rb) * G);
-        __syncthreads();
-        if (tid == 0 && it + NST < total) issue(it + NST);
+    // ---- rows -> (m, l, o) per warp, flash-decoding style: warp w takes rows
+    // [w*RPW, (w+1)*RPW) of every tile, RW at a time (one reduce-scatter for their
+    // scores), and keeps an online softmax per head: m, l and o = sum p v with lanes
+    // over head dimensions.  No block barrier per tile: each warp waits for the tile
+    // itself and the last warp done with a slot refills it.
+    constexpr int GP = Pow2<G>::v;
+    constexpr int RW = 32 / GP;
+    const int RPW = T / kWarps;
+    float m_[G], l_[G], acc[G][D];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        m_[g] = -INFINITY;
+        l_[g] = 0.0f;
+#pragma unroll
+        for (int d = 0; d < D; ++d) acc[g][d] = 0.0f;
     }
-    __syncthreads();  // the new row's score (warp 0) when there was no K tile
-    // ---- softmax statistics per head (warp g); p overwrites the scores
-    if (!s_err && warp < G) {
-        float m = -INFINITY;
-        for (int tt = lane; tt < n; tt += 32) m = fmaxf(m, sc[tt * G + warp]);
+    // one group of nrows <= RW rows (K rows kr, V rows vr): scores, online update, P.V
+    auto group = [&](const KV *kr, const KV *vr, int nrows) {
+        const float s = score_lane<KV, HD, G>(kr, nrows, qr, lane, P.scale);  // -inf: no row
+        const int gl = lane & (GP - 1);
+        float mx = s;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        float l = 0.0f;
-        for (int tt = lane; tt < n; tt += 32) {
-            const float p = expf(sc[tt * G + warp] - m);
-            sc[tt * G + warp] = p;
-            l += p;
+        for (int o = GP; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float mn[G], alpha[G];
+        float m_own = -INFINITY;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            mn[g] = fmaxf(m_[g], __shfl_sync(0xffffffffu, mx, g));
+            alpha[g] = m_[g] == -INFINITY ? 0.0f : expf(m_[g] - mn[g]);
+            if (gl == g) m_own = mn[g];
         }
-        l = warp_sum(l);
-        if (lane == 0) {
-            s_m[warp] = m;
-            s_l[warp] = l;
+        const float p = s == -INFINITY ? 0.0f : expf(s - m_own);
+        float ps = p;
+#pragma unroll
+        for (int o = GP; o < 32; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            l_[g] = fmaf(l_[g], alpha[g], __shfl_sync(0xffffffffu, ps, g));
+            m_[g] = mn[g];
+#pragma unroll
+            for (int d = 0; d < D; ++d) acc[g][d] *= alpha[g];
         }
-    }
-    __syncthreads();
-    // ---- V tiles -> P.V
-    const int dg = tid % DG, ts = tid / DG;
-    float acc[G][4];
+        for (int r = 0; r < nrows; ++r) {
+            float v[D];
+            lds_kv<D>(vr + (size_t)r * HD + lane * D, v);
 #pragma unroll
-    for (int g = 0; g < G; ++g)
+            for (int g = 0; g < G; ++g) {
+                const float pr = __shfl_sync(0xffffffffu, p, r * GP + g);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[g][j] = 0.0f;
-    for (; !s_err && it < total; ++it) {
-        if (tid == 0 && !mbar_wait(&bars[it % NST], (uint32_t)(it / NST) & 1u, kWaitCycles))
-            s_err = 1;
-        __syncthreads();
-        if (s_err) break;
-        const KV *tile = reinterpret_cast<const KV *>(ring + (size_t)(it % NST) * T * RB);
-        const int r0 = (it - nk) * T, rows = min(T, n_copy - r0);
-        // four rows per step: their loads are issued before any is used
-        for (int rq = ts; rq < rows; rq += 4 * TS) {
-            float vv[4][4], pp[4][G];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int r = rq + u * TS;
-                if (r < rows) {
-                    lds_kv<4>(tile + (size_t)r * HD + dg * 4, vv[u]);
-#pragma unroll
-                    for (int g = 0; g < G; ++g) pp[u][g] = sc[(r0 + r) * G + g];
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) vv[u][j] = 0.0f;
-#pragma unroll
-                    for (int g = 0; g < G; ++g) pp[u][g] = 0.0f;
+                for (int d = 0; d < D; ++d) acc[g][d] = fmaf(pr, v[d], acc[g][d]);
+            }
+        }
+    };
+    if (!s_err) {
+        for (int it = 0; it < total; ++it) {
+            const int sl = it % NST;
+            if (!__all_sync(0xffffffffu, mbar_wait(&bars[sl], (uint32_t)(it / NST) & 1u, kWaitCycles))) {
+                if (lane == 0) s_err = 1;
+                break;
+            }
+            const KV *kt = reinterpret_cast<const KV *>(ring + (size_t)sl * 2 * T * RB);
+            const KV *vt = kt + (size_t)T * HD;
+            const int rows = min(T, n_copy - it * T);
+            for (int rb = warp * RPW; rb < min(rows, (warp + 1) * RPW); rb += RW)
+                group(kt + (size_t)rb * HD, vt + (size_t)rb * HD, min(RW, min(rows, (warp + 1) * RPW) - rb));
+            __syncwarp();
+            if (lane == 0) {
+                __threadfence_block();
+                if (atomicAdd(&s_done[sl], 1) == kWarps - 1) {  // last warp on this slot
+                    s_done[sl] = 0;
+                    if (it + NST < total) issue(it + NST);
                 }
             }
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-#pragma unroll
-                for (int g = 0; g < G; ++g)
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) acc[g][j] = fmaf(pp[u][g], vv[u][j], acc[g][j]);
         }
-        __syncthreads();
-        if (tid == 0 && it + NST < total) issue(it + NST);
+        if (owner && warp == kWarps - 1 && !s_err) group(lastk, lastv, 1);  // the new row
     }
+    __syncthreads();  // every warp is past the ring: it now holds the partials
     const bool err = s_err != 0;
     if (err) {
         // drain the copies still in flight and report; this CTA's partial is an empty
         // split's (the merge gives it weight 0), so the cluster stays in step
         if (tid == 0) {
-            for (int i = it; i < min(total, it + NST); ++i)
+            const int issued = s_issued;
+            for (int i = max(0, issued - NST); i < issued; ++i)
                 mbar_wait(&bars[i % NST], (uint32_t)(i / NST) & 1u, kWaitCycles);
             if (P.bulk_in) {
                 mbar_wait(bar_q, 0, kWaitCycles);
@@ -456,33 +490,38 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
             if (P.status) atomicExch(P.status, kDevTimeoutTma);
         }
         __syncthreads();
-    } else if (owner && ts == 0) {  // the new row's value
-        float vv[4];
-        lds_kv<4>(lastv + dg * 4, vv);
+    }
+    // ---- warps' partials -> this CTA's partial (m, l, o) in its own shared memory
+    if (lane == 0) {
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-            const float p = sc[(n - 1) * G + g];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) acc[g][j] = fmaf(p, vv[j], acc[g][j]);
+            wpm[warp * G + g] = err ? -INFINITY : m_[g];
+            wpl[warp * G + g] = err ? 0.0f : l_[g];
         }
     }
-    // ---- this CTA's partial (m, l, o) into its own shared memory (the ring is free)
-    if (!err) {
 #pragma unroll
-        for (int g = 0; g < G; ++g)
+    for (int g = 0; g < G; ++g)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) red[(ts * G + g) * HD + dg * 4 + j] = acc[g][j];
-    }
+        for (int d = 0; d < D; ++d) wpo[(warp * G + g) * HD + lane * D + d] = err ? 0.0f : acc[g][d];
     __syncthreads();
     for (int i = tid; i < G * HD; i += kThreads) {
-        float v = 0.0f;
-        if (!err)
-            for (int r = 0; r < TS; ++r) v += red[r * G * HD + i];
-        po[i] = v;
-    }
-    if (tid < G) {
-        pm[tid] = err ? -INFINITY : s_m[tid];
-        pl[tid] = err ? 0.0f : s_l[tid];
+        const int g = i / HD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, wpm[w * G + g]);
+        float O = 0.0f, Lsum = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) {
+            const float mw = wpm[w * G + g];
+            const float e = mw == -INFINITY ? 0.0f : expf(mw - M);
+            O = fmaf(e, wpo[(w * G + g) * HD + (i - g * HD)], O);
+            Lsum = fmaf(e, wpl[w * G + g], Lsum);
+        }
+        po[i] = O;
+        if (i - g * HD == 0) {
+            pm[g] = M;
+            pl[g] = Lsum;
+        }
     }
     cluster.sync();  // every rank's partial is visible cluster-wide
     // ---- merge over DSMEM.  Thread (g, s) of the first G half-warps reads rank s's
@@ -534,7 +573,6 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
 template <typename KV, int HD, int G>
 int launch_t(const AttnArgs &a, cudaStream_t st) {
     constexpr int RB = HD * (int)sizeof(KV);
-    constexpr int TS = kThreads / (HD / 4);
     auto k = attn_tma_kernel<KV, HD, G>;
     static KernelSmem attr;
     static std::atomic<unsigned long long> cluster_attr{0};
@@ -572,22 +610,27 @@ int launch_t(const AttnArgs &a, cudaStream_t st) {
         P.max_seq = a.max_seq;
         P.chunk_max = (a.max_seq + ns - 1) / ns;
         P.scale = a.scale;
-        P.tile_rows = std::max(1, std::min(kTileBytes / RB, P.chunk_max));
+        // a tile is the K and V rows of tile_rows positions (<= 32 KB, a multiple of the
+        // warp count: every warp takes the same share of it)
+        int T = std::max(kWarps, 2 * kTileBytes / (2 * RB) / kWarps * kWarps);
+        T = std::min(T, (P.chunk_max + kWarps - 1) / kWarps * kWarps);
+        P.tile_rows = T;
         // at most 64 KB of tiles in flight: two CTAs fit an SM, so the clusters of all
         // KV heads are resident at once
-        P.stages = std::max(1, std::min({kStages, 65536 / (P.tile_rows * RB),
-                                         2 * ((P.chunk_max + P.tile_rows - 1) / P.tile_rows)}));
-        const size_t ring = (size_t)P.stages * P.tile_rows * RB;
-        const size_t part = ((size_t)TS * G * HD + (size_t)G * HD + 2 * G + 3 * (size_t)kMaxSplit * G) * 4;
+        P.stages = std::max(1, std::min({kStages, 65536 / (2 * T * RB),
+                                         (P.chunk_max + T - 1) / T}));
+        const size_t ring = (size_t)P.stages * 2 * T * RB;
+        const size_t part = ((size_t)kWarps * G * HD + 2 * (size_t)kWarps * G + (size_t)G * HD +
+                             2 * G + 3 * (size_t)kMaxSplit * G) * 4;
         P.stage_region = (int)((std::max(ring, part) + 15) & ~(size_t)15);
         P.bulk_in = a16(a.q) && (!a.k_new || (a16(a.k_new) && a16(a.v_new) && a16(a.cos_tab) &&
                                               a16(a.sin_tab) &&
                                               (!a.q_norm || (a16(a.q_norm) && a16(a.k_norm)))));
         P.out = a.out;
         P.status = a.status;
-        // barriers | ring | new k, v rows (cache type) | krow, vrow, qs, cs+sn, qn, kn | sc
+        // barriers | ring | new k, v rows (cache type) | krow, vrow, qs, cs+sn, qn, kn
         const size_t smem = 128 + (size_t)P.stage_region + ((2 * (size_t)RB + 15) & ~(size_t)15) +
-                            ((size_t)5 * HD + (size_t)G * HD) * 4 + (size_t)P.chunk_max * G * 4;
+                            ((size_t)5 * HD + (size_t)G * HD) * 4;
         if (smem > (size_t)smem_max) continue;
         cudaLaunchConfig_t cfg{};
         cfg.gridDim = dim3(a.n_kv_heads, ns);
