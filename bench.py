@@ -291,6 +291,117 @@ def bench_matvec(args, rank, pg, pk, pk_kind):
     return out
 
 
+# ------------------------------------------------------------------ prefill matmul
+MM_SHAPE = (4096, 2048, 512, 64)  # config 5 q_proj over a 512-token prefill: M, K, N, G
+MM_COPIES = 32                    # distinct weight copies per step (151 MB > L2)
+
+
+def ref_matmul_rate(seconds: float):
+    """The reference's matmul_i4_ref (oracle/_ref) on a column sample of MM_SHAPE, 1 core."""
+    from oracle.oracle import Oracle, RefLib
+    from tqb200 import synth
+    M, K, N, G = MM_SHAPE
+    rng = np.random.default_rng(7)
+    w = synth.random_i4_fast(rng, M, K, G)
+    n = 2
+    x = rng.normal(size=(n, K)).astype(np.float32)
+    lib, kind = (RefLib(), "reference") if RefLib.available() else (Oracle(), "port")
+    lib.matmul_i4(w, x, M, K, n, G)
+    calls, spent = 0, 0.0
+    while spent < seconds:
+        t0 = time.perf_counter()
+        lib.matmul_i4(w, x, M, K, n, G)
+        spent += time.perf_counter() - t0
+        calls += 1
+    tflops = 2.0 * M * K * n * calls / spent / 1e12
+    return tflops, kind, (f"{calls} calls of matmul_i4_ref on {M}x{K} g{G} with {n} columns "
+                          f"(of the workload's {N}) in {spent:.1f} s, 1 thread")
+
+
+def bench_matmul(args, rank, pg, pk, pk_kind):
+    """Tensor-core matmul_i4 (MatmulI4Fn) on the config-5 prefill q_proj shape."""
+    import torch
+    from tqb200 import lib, synth
+    tq = lib.load()
+    M, K, N, G = MM_SHAPE
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(3)
+    w0 = synth.random_i4_fast(rng, M, K, G)
+    ws = [torch.from_numpy(w0).to(dev)]
+    for _ in range(1, MM_COPIES):
+        ws.append(torch.from_numpy(synth.random_i4_fast(rng, M, K, G)).to(dev))
+    x = rng.normal(size=(N, K)).astype(np.float32)
+    dx = torch.from_numpy(x).to(dev)
+    dy = torch.empty(N, M, device=dev)
+    scr = torch.empty(tq.tqb200_matmul_i4_scratch_bytes(M, K, N, G), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream()
+    sp = stream.cuda_stream
+
+    def step():
+        for wi in ws:
+            st = tq.tqb200_dev_matmul_i4(wi.data_ptr(), dx.data_ptr(), dy.data_ptr(), M, K, N, G,
+                                         scr.data_ptr(), sp)
+            if st:
+                raise lib.TQB200Error(st, tq.tqb200_last_error().decode())
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
+    clocks.start()
+    barrier(pg)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(pg)
+    ms = max_over_ranks(pg, e0.elapsed_time(e1))
+    clk = clocks.stop()
+    per_call_s = ms / 1e3 / (args.steps * MM_COPIES)
+    flops = 2.0 * M * N * K
+    achieved = flops / per_call_s / 1e12
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    e2e = None
+    if rank == 0:
+        tq.tqb200_set_resident_weights(0)
+        lib.matmul_i4(w0, x, M, K, N, G)
+        n = 5
+        t0 = time.perf_counter()
+        for _ in range(n):
+            lib.matmul_i4(w0, x, M, K, N, G)
+        dt = (time.perf_counter() - t0) / n
+        e2e = {"value": round(flops / dt / 1e12, 3), "unit": "TFLOP/s",
+               "h2d_bytes_per_step": int(w0.nbytes + x.nbytes), "d2h_bytes_per_step": int(M * N * 4),
+               "note": "one tqb200_matmul_i4 host-pointer call per step"}
+    peak = pk.get("bf16_tflops", 1590.0)
+    return {
+        "metric": "i4 matmul TFLOP/s (tensor cores; BASELINE config 5 prefill q_proj, 4096x2048 g64, 512 tokens)",
+        "value": round(achieved * world, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "u4 weights (exact bf16 codes), bf16 hi/lo activations, f32 accumulation",
+        "data": "synthetic (seeded random codes/scales/zeros, N(0,1) activations)",
+        "config": {"workload": "matmul-i4", "M": M, "K": K, "N": N, "group_size": G,
+                   "calls_per_step": MM_COPIES,
+                   "l2": f"inputs larger than L2 ({MM_COPIES} distinct weight copies, "
+                         f"{MM_COPIES * w0.nbytes / 1e6:.0f} MB)",
+                   "parallelism": f"replicas x{world}"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
+                     "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": None,
+                     "peak_source": pk_kind, "kernel": "mm_i4_tc_kernel<64>",
+                     "note": "algorithmic 2*M*N*K flops over the whole call (weight repack and "
+                             "activation pre-pass included); the MMAs issue 2.25x these flops"},
+        "clocks": clk,
+        "gpu_launches": 3 * MM_COPIES * args.steps,
+        "e2e": e2e,
+    }
+
+
 # ------------------------------------------------------------------ decode (config 4)
 DECODE_CTX = 4096
 
@@ -325,6 +436,12 @@ def step_bytes(spec, ctx: int, kv_bytes: int) -> int:
     kv = 2 * spec.n_layers * spec.n_kv_heads * ctx * spec.head_dim * kv_bytes
     return mv + kv
 
+
+# DRAM bytes (read + written) of one step's matvec launches, from an ncu capture of one
+# whole step (dram__bytes_read.sum + dram__bytes_write.sum over the step's
+# i4_mv_tma_kernel launches, context 64: the matvec traffic does not depend on the
+# context).  Reported per step, like `achieved`.
+MATVEC_TRAFFIC_PER_STEP = {"decode-qwen3-4b": 2280930000}
 
 # decode workloads: BASELINE configs 2, 3 (full step) and 4
 DECODE_WORKLOADS = {
@@ -435,7 +552,8 @@ def bench_decode(args, rank, pg, pk, pk_kind):
                    "hbm_floor_ms": round(total_bytes / (pk["hbm_gbs"] * 1e9) * 1e3, 4),
                    "model_build_s": round(t_build, 1)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
-                     "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
+                     "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
+                     "traffic": MATVEC_TRAFFIC_PER_STEP.get(args.workload),
                      "peak_source": pk_kind,
                      "kernel": ("vq2_matvec_kernel" if spec.weight_dtype == "vq2" else "i4_mv_tma_kernel")
                                + " (all matvecs of a step)",
@@ -540,6 +658,22 @@ def bench_reference_arm(args, rank):
             "e2e": {"value": round(ms, 2), "unit": "ms/token", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
         }
+    if args.workload == "matmul-i4":
+        tf, kind, sample = ref_matmul_rate(max(2.0, 0.5 * args.steps))
+        M, K, N, G = MM_SHAPE
+        return {
+            "impl": "reference",
+            "metric": "i4 matmul TFLOP/s (tensor cores; BASELINE config 5 prefill q_proj, 4096x2048 g64, 512 tokens)",
+            "value": round(tf, 6), "unit": "TFLOP/s", "n_gpus": 0, "steps": 1, "warmup": 0,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "u4 weights, f32 activations (double accumulation)",
+            "data": "synthetic (seeded random codes/scales/zeros, N(0,1) activations)",
+            "config": {"workload": "matmul-i4", "M": M, "K": K, "N": N, "group_size": G},
+            "cpu_baseline": {"value": round(tf, 6), "unit": "TFLOP/s", "cores": 1, "kind": kind,
+                             "sample": sample},
+            "e2e": {"value": round(tf, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+        }
     gbs, kind, sample = ref_matvec_rate(max(2.0, 0.5 * args.steps), threads)
     return {
         "impl": "reference",
@@ -562,7 +696,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="decode-qwen3-4b",
-                    choices=list(DECODE_WORKLOADS) + ["matvec-i4"])
+                    choices=list(DECODE_WORKLOADS) + ["matvec-i4", "matmul-i4"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ctx", type=int, default=None,
@@ -585,6 +719,8 @@ def main():
     pk, pk_kind = peaks()
     if args.workload == "matvec-i4":
         out = bench_matvec(args, rank, pg, pk, pk_kind)
+    elif args.workload == "matmul-i4":
+        out = bench_matmul(args, rank, pg, pk, pk_kind)
     else:
         out = bench_decode(args, rank, pg, pk, pk_kind)
     if rank == 0:
@@ -592,6 +728,10 @@ def main():
         if args.workload == "matvec-i4":
             gbs, kind, sample = ref_matvec_rate(args.cpu_seconds, 1)
             out["cpu_baseline"] = {"value": round(gbs, 4), "unit": "GB/s", "cores": 1,
+                                   "kind": kind, "sample": sample + f" (host has {threads} threads)"}
+        elif args.workload == "matmul-i4":
+            tf, kind, sample = ref_matmul_rate(max(1.0, args.cpu_seconds))
+            out["cpu_baseline"] = {"value": round(tf, 6), "unit": "TFLOP/s", "cores": 1,
                                    "kind": kind, "sample": sample + f" (host has {threads} threads)"}
         elif args.cpu_seconds > 0:
             ms, kind, sample = ref_decode_rate(args.workload, out["config"]["context"],
