@@ -484,6 +484,9 @@ def bench_decode(args, rank, pg, pk, pk_kind):
     ctx = args.ctx if args.ctx is not None else wl["ctx"]
     max_seq = ctx + W + K + 32  # + the e2e (19) and profiled (1) steps after the timed region
     spec = decode_spec(wl, max_seq)
+    if args.layers:
+        from dataclasses import replace as _replace
+        spec = _replace(spec, n_layers=args.layers)
     t0 = time.time()
     sm = SynthModel(spec, seed=0)
     t_build = time.time() - t0
@@ -701,6 +704,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ctx", type=int, default=None,
                     help="decode context in KV positions (default: the workload's)")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="decode workloads: fewer layers than the model (small profiling cases)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 

@@ -588,6 +588,7 @@ __device__ void topk_softmax_warp(const float *__restrict__ logits, int n, int k
 // to finish, top-k softmax.  One warp per router row, its whole row loaded up front
 // (float4, many loads in flight); every CTA normalises the (small) hidden vector itself.
 constexpr int kRouterWarps = 4;
+constexpr int kRouterHid = 16;  // hidden elements per thread and chunk (H <= 2048 in one)
 constexpr int kRouterChunk = 32 * 4 * 16;  // floats of a row one warp loads at once
 
 __global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(
@@ -611,10 +612,18 @@ __global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(
     }
     griddep_wait();
     griddep_launch();
+    // the hidden vector and the norm weights, every load issued before any is used
+    // (a chunk of kRouterHid per thread at a time)
     double ss = 0.0;
-    for (int i = t; i < H; i += blockDim.x) {
-        const float v = h[i];
-        ss += (double)v * (double)v;
+    for (int c0 = 0; c0 < H; c0 += kRouterHid * kRouterWarps * 32) {
+        float hv[kRouterHid];
+#pragma unroll
+        for (int j = 0; j < kRouterHid; ++j) {
+            const int i = c0 + t + j * kRouterWarps * 32;
+            hv[j] = i < H ? h[i] : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < kRouterHid; ++j) ss += (double)hv[j] * (double)hv[j];
     }
     ss = warp_sum_d(ss);
     if (lane == 0) s_red[warp] = ss;
@@ -622,7 +631,20 @@ __global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(
     double tot = 0.0;
     for (int w = 0; w < kRouterWarps; ++w) tot += s_red[w];
     const float scale = 1.0f / sqrtf(__fadd_rn((float)(tot / H), eps));
-    for (int i = t; i < H; i += blockDim.x) xn[i] = __fmul_rn(__fmul_rn(h[i], scale), norm_w[i]);
+    for (int c0 = 0; c0 < H; c0 += kRouterHid * kRouterWarps * 32) {
+        float hv[kRouterHid], nv[kRouterHid];
+#pragma unroll
+        for (int j = 0; j < kRouterHid; ++j) {
+            const int i = c0 + t + j * kRouterWarps * 32;
+            hv[j] = i < H ? h[i] : 0.0f;
+            nv[j] = i < H ? norm_w[i] : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < kRouterHid; ++j) {
+            const int i = c0 + t + j * kRouterWarps * 32;
+            if (i < H) xn[i] = __fmul_rn(__fmul_rn(hv[j], scale), nv[j]);
+        }
+    }
     __syncthreads();
     if (e < E) {
         double acc = 0.0;
@@ -669,10 +691,23 @@ __global__ void moe_combine_kernel(float *__restrict__ h, const float *__restric
                                    const float *__restrict__ wts, int k, int H) {
     griddep_wait();
     griddep_launch();
+    constexpr int kMax = 16;  // expert outputs loaded at once (k is at most 32)
     for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < H; j += gridDim.x * blockDim.x) {
         float acc = 0.0f;
-        for (int t = 0; t < k; ++t) acc = __fadd_rn(acc, __fmul_rn(wts[t], o[(size_t)t * H + j]));
-        h[j] = __fadd_rn(h[j], acc);
+        const float hj = h[j];
+        for (int t0 = 0; t0 < k; t0 += kMax) {
+            float ov[kMax], wv[kMax];
+#pragma unroll
+            for (int u = 0; u < kMax; ++u) {
+                const int t = t0 + u;
+                ov[u] = t < k ? o[(size_t)t * H + j] : 0.0f;
+                wv[u] = t < k ? wts[t] : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < kMax; ++u)
+                if (t0 + u < k) acc = __fadd_rn(acc, __fmul_rn(wv[u], ov[u]));
+        }
+        h[j] = __fadd_rn(hj, acc);
     }
 }
 
