@@ -817,7 +817,11 @@ Shape plan(int K, int G, bool pair, bool norm, int rows_total, int r_div = 0) {
     if ((size_t)per_cta * RB * np <= 64 * 1024) {
         L.R = per_cta;
     } else {
-        L.R = (int)std::max<size_t>(1, (32 * 1024) / (RB * np));
+        // two passes per CTA when they fit (the second streams while the first is
+        // computed; each pass costs a consumer barrier and a reduction), else passes of
+        // at most 96 KB
+        const size_t cap = 96 * 1024 / (RB * np);
+        L.R = (int)std::max<size_t>(1, std::min<size_t>((per_cta + 1) / 2, cap));
     }
     if (r_div > 0) {  // passes must not straddle r_div-row blocks
         L.R = std::min(L.R, r_div);
