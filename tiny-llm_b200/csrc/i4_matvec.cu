@@ -787,17 +787,11 @@ struct Shape {
     size_t smem = 0;
 };
 
-// Launch shape.  One CTA per SM (block up to 512 threads: S row slots of nt segment
-// threads); a pass is R consecutive rows, one bulk copy (two in paired mode).  When a
-// CTA's share of the rows fits in <= 64 KB it is a single pass (R = rows / SMs, so the
-// passes spread evenly); otherwise passes of <= 32 KB stream through a ring of up to
-// 96 KB.  Shared memory stays near 110 KB or below for most shapes, so the next
-// kernel's CTA can become resident (and start its weight copies) before this one ends.
 // Launch shape.  One CTA per SM (512 threads: the producer warp and S row slots of
 // nt segment threads; the block takes the whole register file).  A pass is R
-// consecutive rows, one bulk copy (two in paired mode): a single pass when a CTA's
-// share of the rows fits in 64 KB (R = rows / SMs, so the passes spread evenly),
-// otherwise passes of up to 32 KB through a ring of up to ~200 KB, all in flight.
+// consecutive rows, one bulk copy (two in paired mode; copies split in 16 KB pieces),
+// R = rows / SMs (one pass) or half of it (two passes), through a ring of up to
+// ~200 KB, all in flight.
 Shape plan(int K, int G, bool pair, bool norm, int rows_total, int r_div = 0) {
     Shape L;
     L.seg = (G % 64 == 0) ? 64 : 32;
@@ -814,12 +808,12 @@ Shape plan(int K, int G, bool pair, bool norm, int rows_total, int r_div = 0) {
     L.S = std::max(1, consumers / L.nt);
     L.block = kI4Threads;
     const int per_cta = std::max(1, (rows_total + num_sms() - 1) / num_sms());
-    if ((size_t)per_cta * RB * np <= 64 * 1024) {
+    // A pass costs a consumer barrier and a reduction, so a CTA's share of up to 100 KB
+    // is one pass; larger shares go in two passes when they fit (the second streams
+    // while the first is computed), else in passes of at most 96 KB.
+    if ((size_t)per_cta * RB * np <= 100 * 1024) {
         L.R = per_cta;
     } else {
-        // two passes per CTA when they fit (the second streams while the first is
-        // computed; each pass costs a consumer barrier and a reduction), else passes of
-        // at most 96 KB
         const size_t cap = 96 * 1024 / (RB * np);
         L.R = (int)std::max<size_t>(1, std::min<size_t>((per_cta + 1) / 2, cap));
     }
