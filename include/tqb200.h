@@ -191,6 +191,14 @@ int tqb200_engine_create(const tqb200_model_desc *desc, const tqb200_engine_opts
                          tqb200_engine **out);
 /* GpuDecodeStepFn (kernels/dispatch.h:358): feeds token_id at the current position. */
 int tqb200_engine_step(tqb200_engine *e, int token_id, int *next_token);
+/* QwenModel::forward_prefill (runtime/qwen_model.h:169, runtime/qwen_forward_prefill.cpp:74):
+ * feeds the n prompt tokens at positions pos .. pos+n-1 as one batch (projections and
+ * experts on the tensor-core matmul, causal attention over the cache), leaves their K/V
+ * in the cache and the last token's logits in the engine, and returns the greedy next
+ * token.  Falls back to n decode steps where the batched path does not apply (tp_size > 1,
+ * VQ2 projections, head_dim other than 64/128), as the reference falls back to
+ * forward_token. */
+int tqb200_engine_prefill(tqb200_engine *e, const int *tokens, int n, int *next_token);
 /* Greedy-decodes n_steps tokens with the produced token fed back on the device (no
  * host round trip per token; main.cpp's decode loop, runtime/main.cpp:1038-1041, moved
  * onto the GPU): step i feeds the token of step i-1, the first feeds token_id.

@@ -94,8 +94,11 @@ __global__ void qk_rope_kv_kernel(float *__restrict__ q, const float *__restrict
     __shared__ double sh[32];
     __shared__ float buf[512];
     const int h = blockIdx.x;
-    const int pos = *pos_p;
+    const int pos = *pos_p + blockIdx.y;  // batched: token blockIdx.y of consecutive rows
     const int half = head_dim / 2;
+    q += (size_t)blockIdx.y * n_heads * head_dim;
+    k += (size_t)blockIdx.y * n_kv_heads * head_dim;
+    v += (size_t)blockIdx.y * n_kv_heads * head_dim;
     if (h >= n_heads + n_kv_heads) {  // value head: plain store
         const int kh = h - n_heads - n_kv_heads;
         KV *dst = vcache + ((size_t)kh * max_seq + pos) * head_dim;
@@ -714,7 +717,8 @@ __global__ void moe_combine_kernel(float *__restrict__ h, const float *__restric
 // ------------------------------------------------------------------ embed
 __global__ void embed_kernel(const void *__restrict__ table, int dtype, const int *__restrict__ token,
                              int dim, int group_size, float *__restrict__ out) {
-    const int tok = *token;
+    const int tok = token[blockIdx.y];  // batched: row blockIdx.y
+    out += (size_t)blockIdx.y * dim;
     for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < dim; c += gridDim.x * blockDim.x) {
         if (dtype == TQB200_DT_F32) {
             out[c] = ((const float *)table)[(size_t)tok * dim + c];
@@ -729,6 +733,83 @@ __global__ void embed_kernel(const void *__restrict__ table, int dtype, const in
             const uint8_t b = gp[4 + (i >> 1)];
             out[c] = __fmul_rn(__fsub_rn((float)((i & 1) ? (b >> 4) : (b & 15)), z), s);
         }
+    }
+}
+
+// ------------------------------------------------------------------ MoE prefill
+// Router logits of many tokens (f32 router): logits[t][e] = W[e] . xn[t] with the
+// products and the sum in double (matvec_f32_ref, kernels/matvec/matvec_f32_ref.cpp),
+// xn already normalised.  CTA = 16 tokens x 32 experts, K staged through shared memory
+// in chunks; thread = one token, two experts.
+constexpr int kRrTok = 16, kRrExp = 32, kRrK = 128;
+
+__global__ void __launch_bounds__(256) router_rows_kernel(const float *__restrict__ xn, int n, int H,
+                                                          const float *__restrict__ W, int E,
+                                                          float *__restrict__ logits) {
+    __shared__ float xs[kRrTok][kRrK + 1];
+    __shared__ float ws[kRrExp][kRrK + 1];
+    const int tid = threadIdx.x;
+    const int t0 = blockIdx.y * kRrTok, e0 = blockIdx.x * kRrExp;
+    const int tt = tid & 15, te = tid >> 4;
+    double a0 = 0.0, a1 = 0.0;
+    for (int k0 = 0; k0 < H; k0 += kRrK) {
+        __syncthreads();
+#pragma unroll
+        for (int r = 0; r < kRrTok * kRrK / 256; ++r) {
+            const int i = tid + 256 * r, row = i / kRrK, c = i % kRrK;
+            xs[row][c] = (t0 + row < n && k0 + c < H) ? xn[(size_t)(t0 + row) * H + k0 + c] : 0.0f;
+        }
+#pragma unroll
+        for (int r = 0; r < kRrExp * kRrK / 256; ++r) {
+            const int i = tid + 256 * r, row = i / kRrK, c = i % kRrK;
+            ws[row][c] = (e0 + row < E && k0 + c < H) ? W[(size_t)(e0 + row) * H + k0 + c] : 0.0f;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int c = 0; c < kRrK; ++c) {
+            const double x = (double)xs[tt][c];
+            a0 = fma((double)ws[te][c], x, a0);
+            a1 = fma((double)ws[te + 16][c], x, a1);
+        }
+    }
+    const int t = t0 + tt;
+    if (t < n) {
+        if (e0 + te < E) logits[(size_t)t * E + e0 + te] = (float)a0;
+        if (e0 + te + 16 < E) logits[(size_t)t * E + e0 + te + 16] = (float)a1;
+    }
+}
+
+// Top-k softmax of every token's router logits: one warp per token.
+__global__ void topk_rows_kernel(const float *__restrict__ logits, int n, int E, int k,
+                                 int *__restrict__ idx, float *__restrict__ wts) {
+    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (t >= n) return;
+    topk_softmax_warp(logits + (size_t)t * E, E, k, idx + (size_t)t * k, wts + (size_t)t * k);
+}
+
+// h[t] += sum_j wts[t][j] * o[slot[t*k + j]] in router order for every token, with the
+// decode combine's rounding points (moe_combine_kernel).
+__global__ void moe_combine_rows_kernel(float *__restrict__ h, const float *__restrict__ o,
+                                        const float *__restrict__ wts, const int *__restrict__ slot,
+                                        int k, int H) {
+    const int t = blockIdx.y;
+    constexpr int kMax = 16;
+    for (int jx = blockIdx.x * blockDim.x + threadIdx.x; jx < H; jx += gridDim.x * blockDim.x) {
+        float acc = 0.0f;
+        const float hj = h[(size_t)t * H + jx];
+        for (int u0 = 0; u0 < k; u0 += kMax) {
+            float ov[kMax], wv[kMax];
+#pragma unroll
+            for (int u = 0; u < kMax; ++u) {
+                const int a = u0 + u;
+                ov[u] = a < k ? o[(size_t)slot[(size_t)t * k + a] * H + jx] : 0.0f;
+                wv[u] = a < k ? wts[(size_t)t * k + a] : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < kMax; ++u)
+                if (u0 + u < k) acc = __fadd_rn(acc, __fmul_rn(wv[u], ov[u]));
+        }
+        h[(size_t)t * H + jx] = __fadd_rn(hj, acc);
     }
 }
 
@@ -805,7 +886,8 @@ int launch_rope(float *q, float *k, int n_heads, int n_kv_heads, int head_dim, c
 int launch_qk_rope_kv(const QkRopeKvArgs &a, cudaStream_t st) {
     TQ_CHECK_ARG(a.head_dim <= 512 && a.head_dim % 2 == 0 && a.head_dim / 2 <= 4 * 128,
                  "head_dim %d", a.head_dim);
-    const int blocks = a.n_heads + 2 * a.n_kv_heads;
+    TQ_CHECK_ARG(a.n_tokens >= 1 && a.n_tokens <= 65535, "qk_rope_kv: %d tokens", a.n_tokens);
+    const dim3 blocks(a.n_heads + 2 * a.n_kv_heads, a.n_tokens);
     if (a.kv_fp16)
         qk_rope_kv_kernel<uint16_t><<<blocks, 128, 0, st>>>(
             a.q, a.k, a.v, a.q_norm, a.k_norm, a.eps, a.cos_tab, a.sin_tab, a.pos,
@@ -949,9 +1031,36 @@ int launch_topk_softmax(const float *logits, int n, int k, int *idx, float *w, c
     return TQB200_OK;
 }
 
+int launch_router_rows(const float *xn, int n, int H, const float *W, int E, float *logits,
+                       cudaStream_t st) {
+    TQ_CHECK_ARG(n > 0 && n <= 65535 * kRrTok && E > 0 && H > 0, "router rows: n %d E %d H %d", n, E, H);
+    const dim3 grid((E + kRrExp - 1) / kRrExp, (n + kRrTok - 1) / kRrTok);
+    router_rows_kernel<<<grid, 256, 0, st>>>(xn, n, H, W, E, logits);
+    TQ_CUDA_TRY(cudaGetLastError());
+    return TQB200_OK;
+}
+
+int launch_topk_rows(const float *logits, int n, int E, int k, int *idx, float *wts, cudaStream_t st) {
+    TQ_CHECK_ARG(n > 0 && E > 0 && E <= 32 * kRouterPer && k > 0 && k <= 32 && k <= E,
+                 "topk rows: n %d E %d k %d", n, E, k);
+    topk_rows_kernel<<<(n + 3) / 4, 128, 0, st>>>(logits, n, E, k, idx, wts);
+    TQ_CUDA_TRY(cudaGetLastError());
+    return TQB200_OK;
+}
+
+int launch_moe_combine_rows(float *h, const float *o, const float *wts, const int *slot, int n,
+                            int k, int H, cudaStream_t st) {
+    TQ_CHECK_ARG(n > 0 && n <= 65535 && k > 0 && H > 0, "moe combine rows: n %d k %d H %d", n, k, H);
+    const dim3 grid((H + 255) / 256, n);
+    moe_combine_rows_kernel<<<grid, 256, 0, st>>>(h, o, wts, slot, k, H);
+    TQ_CUDA_TRY(cudaGetLastError());
+    return TQB200_OK;
+}
+
 int launch_embed(const void *table, int dtype, const int *token, int dim, int group_size,
-                 float *out, cudaStream_t st) {
-    const int grid = std::max(1, std::min((dim + 255) / 256, 16));
+                 float *out, cudaStream_t st, int n_tokens) {
+    TQ_CHECK_ARG(n_tokens >= 1 && n_tokens <= 65535, "embed: %d tokens", n_tokens);
+    const dim3 grid(std::max(1, std::min((dim + 255) / 256, 16)), n_tokens);
     embed_kernel<<<grid, 256, 0, st>>>(table, dtype, token, dim, group_size, out);
     TQ_CUDA_TRY(cudaGetLastError());
     return TQB200_OK;

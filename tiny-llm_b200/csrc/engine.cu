@@ -26,6 +26,7 @@
 // element is computed by exactly the kernel and order the single-GPU engine
 // uses, so tokens and logits do not depend on the number of GPUs.  The greedy
 // token is the first maximum over the ranks' (max, index) pairs.
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <string>
@@ -58,6 +59,40 @@ struct DLayer {
     const uint8_t *router_i4 = nullptr;
     const uint8_t *ex_gate = nullptr, *ex_up = nullptr, *ex_down = nullptr;
     size_t ex_gu_stride = 0, ex_down_stride = 0;  // bytes between experts
+};
+
+// Prefill copies of a layer's i4 matrices in the tensor-core matmul's tile-contiguous
+// order (launch_mm_repack_w); experts back to back, expert x at x * stride.
+struct PLayer {
+    const uint8_t *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr;
+    const uint8_t *gate = nullptr, *up = nullptr, *down = nullptr, *router = nullptr;
+    const uint8_t *ex_gate = nullptr, *ex_up = nullptr, *ex_down = nullptr;
+    size_t ex_gu_stride = 0, ex_down_stride = 0;
+};
+
+// Batched prompt state (allocated by the first prefill): activations of up to `cap`
+// tokens, row t of token t, and the X planes of the tensor-core matmul.
+struct Prefill {
+    bool ready = false;
+    int cap = 0;
+    std::vector<PLayer> layers;
+    float *hidden = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr,
+          *attn = nullptr, *gate = nullptr, *up = nullptr, *act = nullptr;
+    int *io = nullptr;  // device [p0, tokens...]
+    uint16_t *bhi = nullptr, *blo = nullptr;
+    // host-planned jobs of the current chunk size (7 per layer), on the device
+    std::vector<MmJob> hjobs;
+    MmJob *jobs = nullptr;
+    int jobs_n = -1;
+    std::vector<int> nt, tiles;  // per job launch: tile width and CTAs (4 launches per layer)
+    // MoE
+    float *logits = nullptr, *wts = nullptr, *mh = nullptr, *mu = nullptr, *mact = nullptr,
+          *mo = nullptr;
+    int *idx = nullptr, *rows = nullptr, *slot = nullptr, *ntiles = nullptr;
+    int *tile_gu = nullptr, *tile_dn = nullptr;
+    MmJob *jobs_gu = nullptr, *jobs_dn = nullptr;
+    MmPackJob *pack_gu = nullptr, *pack_dn = nullptr;
+    int max_tiles_gu = 0, max_tiles_dn = 0, moe_nt = 64;
 };
 
 }  // namespace
@@ -112,6 +147,7 @@ struct tqb200_engine {
           *moe_o = nullptr;
     int *moe_idx = nullptr;
     unsigned int *moe_ticket = nullptr;
+    tqb200::Prefill pf;
 #ifdef TQB200_HAVE_NCCL
     ncclComm_t comm = nullptr;
 #endif
@@ -340,6 +376,8 @@ int allgather(tqb200_engine *e, float *buf, size_t count) {
 #endif
 }
 
+int launch_lm_head(tqb200_engine *e);
+
 // One decode step's kernels, stream-ordered on e->stream.
 int launch_forward(tqb200_engine *e) {
     const tqb200_model_desc &d = e->d;
@@ -547,7 +585,19 @@ int launch_forward(tqb200_engine *e) {
             TQ_TRY(mark(e, K_DOWN));
         }
     }
-    {   // lm_head with the final RMSNorm in the prologue and the greedy argmax in the epilogue
+    return launch_lm_head(e);
+}
+
+// lm_head over e->hidden with the final RMSNorm in the prologue and the greedy argmax in
+// the epilogue (token -> io_out[0]).
+int launch_lm_head(tqb200_engine *e) {
+    const tqb200_model_desc &d = e->d;
+    cudaStream_t st = e->stream;
+    const int G = e->tp, r = e->rank;
+    const int H = d.hidden, Vs = d.vocab / G;
+    const bool pdl = e->o.pdl != 0;
+    int *status = e->io_out + 1;
+    {
         I4Job j{e->lm_head, e->logits + (size_t)r * Vs, nullptr, nullptr, Vs};
         I4LaunchOpts o;
         o.x = {X_RMSNORM, e->hidden, e->final_norm, d.rms_eps, nullptr};
@@ -803,6 +853,349 @@ int create_impl(const tqb200_model_desc *desc, const tqb200_engine_opts *opts, t
     return TQB200_OK;
 }
 
+// ------------------------------------------------------------------ prefill
+// A prompt runs in chunks of up to Prefill::cap tokens.  Per layer and chunk:
+//   rmsnorm rows -> q/k/v (one grouped tensor-core matmul, bias in the epilogue)
+//   -> QK-norm + RoPE + KV append (batched) -> causal attention over the cache
+//   -> o_proj (residual in the epilogue) -> rmsnorm rows -> FFN:
+//      dense: gate/up (grouped) -> SwiGLU -> down (residual in the epilogue)
+//      MoE:   router logits -> top-k softmax -> device plan (bucket by expert) ->
+//             gate/up of every expert with tokens in one planned launch -> SwiGLU
+//             -> down likewise -> weighted sum per token in router order + residual
+// then, after the last chunk, the decode lm_head on the last token's hidden state.
+// Every projection uses the tile-contiguous copies made by the first prefill.
+constexpr int kPrefillChunk = 512;
+
+bool prefill_batched(const tqb200_engine *e) {
+    const tqb200_model_desc &d = e->d;
+    return e->tp == 1 && !e->layers[0].vq2 && mm_group_supported(d.group_size) &&
+           attn_prefill_supported(d.n_heads, d.n_kv_heads, d.head_dim);
+}
+
+int repack(tqb200_engine *e, const uint8_t *w, int M, int K, const uint8_t **out) {
+    const int G = e->d.group_size;
+    void *p;
+    TQ_TRY(dev_alloc(e, mm_repacked_bytes(M, K, G), &p));
+    TQ_TRY(launch_mm_repack_w(w, M, K, G, (uint8_t *)p, e->stream));
+    *out = (const uint8_t *)p;
+    return TQB200_OK;
+}
+
+// E experts of M x K at `stride` bytes apart -> one buffer, expert x at x * *ostride.
+int repack_experts(tqb200_engine *e, const uint8_t *w, size_t stride, int E, int M, int K,
+                   const uint8_t **out, size_t *ostride) {
+    const int G = e->d.group_size;
+    const size_t one = (mm_repacked_bytes(M, K, G) + 255) & ~(size_t)255;
+    const size_t rb = tqb200_i4_row_bytes(K, G);
+    void *p;
+    TQ_TRY(dev_alloc(e, one * E, &p));
+    if (stride == (size_t)M * rb && M % kMmTileRows == 0 && one == mm_repacked_bytes(M, K, G)) {
+        // rows of consecutive experts are contiguous and no tile straddles two experts
+        TQ_TRY(launch_mm_repack_w(w, M * E, K, G, (uint8_t *)p, e->stream));
+    } else {
+        for (int x = 0; x < E; ++x)
+            TQ_TRY(launch_mm_repack_w(w + (size_t)x * stride, M, K, G, (uint8_t *)p + (size_t)x * one,
+                                      e->stream));
+    }
+    *out = (const uint8_t *)p;
+    *ostride = one;
+    return TQB200_OK;
+}
+
+int prefill_setup(tqb200_engine *e) {
+    Prefill &P = e->pf;
+    if (P.ready) return TQB200_OK;
+    const tqb200_model_desc &d = e->d;
+    const int H = d.hidden, qd = d.n_heads * d.head_dim, kvd = d.n_kv_heads * d.head_dim;
+    const int G = d.group_size;
+    const bool moe = d.model_type == TQB200_MODEL_QWEN3_MOE;
+    const int k = moe ? d.experts_per_tok : 1, E = moe ? d.n_experts : 0, mi = d.moe_inter;
+    P.cap = std::min(kPrefillChunk, e->o.max_seq_len);
+    if (moe) P.cap = std::min(P.cap, 24 * 1024 / k);  // plan kernel: n*k assignments in shared memory
+    const int cap = P.cap;
+    P.layers.resize(d.n_layers);
+    for (int l = 0; l < d.n_layers; ++l) {
+        const DLayer &w = e->layers[l];
+        PLayer &pl = P.layers[l];
+        TQ_TRY(repack(e, w.q, qd, H, &pl.q));
+        TQ_TRY(repack(e, w.k, kvd, H, &pl.k));
+        TQ_TRY(repack(e, w.v, kvd, H, &pl.v));
+        TQ_TRY(repack(e, w.o, H, qd, &pl.o));
+        if (w.moe) {
+            TQ_TRY(repack_experts(e, w.ex_gate, w.ex_gu_stride, E, mi, H, &pl.ex_gate, &pl.ex_gu_stride));
+            TQ_TRY(repack_experts(e, w.ex_up, w.ex_gu_stride, E, mi, H, &pl.ex_up, &pl.ex_gu_stride));
+            TQ_TRY(repack_experts(e, w.ex_down, w.ex_down_stride, E, H, mi, &pl.ex_down,
+                                  &pl.ex_down_stride));
+            if (w.router_i4) TQ_TRY(repack(e, w.router_i4, E, H, &pl.router));
+        } else {
+            TQ_TRY(repack(e, w.gate, d.inter, H, &pl.gate));
+            TQ_TRY(repack(e, w.up, d.inter, H, &pl.up));
+            TQ_TRY(repack(e, w.down, H, d.inter, &pl.down));
+        }
+    }
+    const int I = moe ? 0 : d.inter;
+    const size_t f = (size_t)cap * (2 * (size_t)H + 2 * (size_t)qd + 2 * (size_t)kvd + 3 * (size_t)I);
+    void *p;
+    TQ_TRY(dev_alloc(e, f * 4 + 16 * 64, &p));
+    float *a = (float *)p;
+    auto take = [&](size_t n) {  // 64-byte aligned carve
+        float *r = a;
+        a += (n + 15) & ~(size_t)15;
+        return r;
+    };
+    P.hidden = take((size_t)cap * H);
+    P.xn = take((size_t)cap * H);
+    P.q = take((size_t)cap * qd);
+    P.attn = take((size_t)cap * qd);
+    P.k = take((size_t)cap * kvd);
+    P.v = take((size_t)cap * kvd);
+    if (I) {
+        P.gate = take((size_t)cap * I);
+        P.up = take((size_t)cap * I);
+        P.act = take((size_t)cap * I);
+    }
+    TQ_TRY(dev_alloc(e, (size_t)(cap + 16) * 4, &p));
+    P.io = (int *)p;
+    long long pe = std::max({mm_plane_elems(H, cap, G), mm_plane_elems(qd, cap, G),
+                             I ? mm_plane_elems(I, cap, G) : 0LL});
+    if (moe) {
+        P.moe_nt = 64;
+        pe = std::max({pe, moe_plan_plane_elems(cap, k, E, H, G), moe_plan_plane_elems(cap, k, E, mi, G)});
+        const size_t A = (size_t)cap * k;
+        P.max_tiles_gu = 2 * moe_plan_max_tiles(cap, k, E, mi, P.moe_nt);
+        P.max_tiles_dn = moe_plan_max_tiles(cap, k, E, H, P.moe_nt);
+        const size_t mf = (size_t)cap * E + 2 * A + 3 * A * mi + A * H + 64 * 8;
+        TQ_TRY(dev_alloc(e, mf * 4, &p));
+        float *m = (float *)p;
+        auto mt = [&](size_t n) {
+            float *r = m;
+            m += (n + 15) & ~(size_t)15;
+            return r;
+        };
+        P.logits = mt((size_t)cap * E);
+        P.wts = mt(A);
+        P.idx = (int *)mt(A);
+        P.mh = mt(A * mi);
+        P.mu = mt(A * mi);
+        P.mact = mt(A * mi);
+        P.mo = mt(A * H);
+        const size_t ib = (2 * A + 2 + (size_t)P.max_tiles_gu + P.max_tiles_dn) * 4 + 256;
+        TQ_TRY(dev_alloc(e, ib, &p));
+        int *ip = (int *)p;
+        P.rows = ip, ip += A;
+        P.slot = ip, ip += A;
+        P.ntiles = ip, ip += 2;
+        P.tile_gu = ip, ip += P.max_tiles_gu;
+        P.tile_dn = ip;
+        TQ_TRY(dev_alloc(e, sizeof(MmJob) * 3 * E + sizeof(MmPackJob) * 2 * E + 256, &p));
+        P.jobs_gu = (MmJob *)p;
+        P.jobs_dn = P.jobs_gu + 2 * E;
+        P.pack_gu = (MmPackJob *)(P.jobs_dn + E);
+        P.pack_dn = P.pack_gu + E;
+    }
+    TQ_TRY(dev_alloc(e, (size_t)pe * 2 * 2 + 256, &p));
+    P.bhi = (uint16_t *)p;
+    P.blo = (uint16_t *)((char *)p + (((size_t)pe * 2 + 255) & ~(size_t)255));
+    TQ_TRY(dev_alloc(e, sizeof(MmJob) * 7 * d.n_layers, &p));
+    P.jobs = (MmJob *)p;
+    P.ready = true;
+    return TQB200_OK;
+}
+
+// Host-planned jobs of every layer for a chunk of n tokens: per layer 7 slots,
+// [q, k, v] [o] [gate, up | router] [down], and 4 launches (tile width, CTAs).
+int prefill_plan(tqb200_engine *e, int n) {
+    Prefill &P = e->pf;
+    if (P.jobs_n == n) return TQB200_OK;
+    const tqb200_model_desc &d = e->d;
+    const int H = d.hidden, qd = d.n_heads * d.head_dim, kvd = d.n_kv_heads * d.head_dim;
+    P.hjobs.assign((size_t)7 * d.n_layers, MmJob{});
+    P.nt.assign((size_t)4 * d.n_layers, 16);
+    P.tiles.assign((size_t)4 * d.n_layers, 0);
+    for (int l = 0; l < d.n_layers; ++l) {
+        const DLayer &w = e->layers[l];
+        const PLayer &pl = P.layers[l];
+        MmJob *j = &P.hjobs[(size_t)7 * l];
+        auto group = [&](MmJob *js, int nj, int launch) {
+            int mtot = 0;
+            for (int i = 0; i < nj; ++i) mtot += js[i].M;
+            const int nt = mm_tile_width(mtot, n);
+            int t = 0;
+            for (int i = 0; i < nj; ++i) {
+                js[i].N = n;
+                js[i].tile_begin = t;
+                js[i].b_off = 0;
+                t += mm_job_tiles(js[i].M, n, nt);
+            }
+            P.nt[(size_t)4 * l + launch] = nt;
+            P.tiles[(size_t)4 * l + launch] = t;
+        };
+        auto job = [](const uint8_t *wt, float *y, int M, const float *resid, const float *bias) {
+            MmJob x{};
+            x.w = wt;
+            x.y = y;
+            x.M = M;
+            x.ldy = M;
+            x.resid = resid;
+            x.bias = bias;
+            return x;
+        };
+        j[0] = job(pl.q, P.q, qd, nullptr, w.q_bias);
+        j[1] = job(pl.k, P.k, kvd, nullptr, w.k_bias);
+        j[2] = job(pl.v, P.v, kvd, nullptr, w.v_bias);
+        group(j, 3, 0);
+        j[3] = job(pl.o, P.hidden, H, P.hidden, nullptr);
+        group(j + 3, 1, 1);
+        if (w.moe) {
+            if (pl.router) {
+                j[4] = job(pl.router, P.logits, d.n_experts, nullptr, nullptr);
+                group(j + 4, 1, 2);
+            }
+        } else {
+            j[4] = job(pl.gate, P.gate, d.inter, nullptr, nullptr);
+            j[5] = job(pl.up, P.up, d.inter, nullptr, nullptr);
+            group(j + 4, 2, 2);
+            j[6] = job(pl.down, P.hidden, H, P.hidden, nullptr);
+            group(j + 6, 1, 3);
+        }
+    }
+    TQ_CUDA_TRY(cudaMemcpyAsync(P.jobs, P.hjobs.data(), sizeof(MmJob) * P.hjobs.size(),
+                                cudaMemcpyHostToDevice, e->stream));
+    P.jobs_n = n;
+    return TQB200_OK;
+}
+
+// One chunk of n tokens at positions p0..p0+n-1 (P.io already holds p0 and the tokens).
+int prefill_chunk(tqb200_engine *e, int n, int p0) {
+    Prefill &P = e->pf;
+    const tqb200_model_desc &d = e->d;
+    cudaStream_t st = e->stream;
+    const int H = d.hidden, hd = d.head_dim, G = d.group_size;
+    const int qd = d.n_heads * hd;
+    int *status = e->io_out + 1;
+    TQ_TRY(prefill_plan(e, n));
+    TQ_TRY(launch_embed(e->embed, e->embed_dtype, P.io + 1, H, G, P.hidden, st, n));
+    auto mm = [&](int l, int slot, int nj, int launch, int K) {
+        const MmJob *hj = &P.hjobs[(size_t)7 * l + slot];
+        return launch_matmul_i4_grouped(hj, nj > 1 ? P.jobs + (size_t)7 * l + slot : nullptr, nj, K,
+                                        G, P.nt[(size_t)4 * l + launch], P.bhi, P.blo,
+                                        P.tiles[(size_t)4 * l + launch], status, st);
+    };
+    auto pack = [&](const float *x, int K) {
+        return launch_mm_pack_x(x, nullptr, K, K, n, G, P.bhi, P.blo, st);
+    };
+    for (int l = 0; l < d.n_layers; ++l) {
+        const DLayer &w = e->layers[l];
+        const PLayer &pl = P.layers[l];
+        e->cur_layer = l;
+        TQ_TRY(launch_rmsnorm(P.hidden, w.input_ln, P.xn, n, H, d.rms_eps, st));
+        TQ_TRY(pack(P.xn, H));
+        TQ_TRY(mm(l, 0, 3, 0, H));
+        const size_t es = e->o.kv_fp16 ? 2 : 4;
+        char *kvb = (char *)e->kv;
+        void *kc = kvb + (size_t)l * e->layer_stride * es;
+        void *vc = kvb + ((size_t)d.n_layers + l) * e->layer_stride * es;
+        {
+            QkRopeKvArgs r{};
+            r.q = P.q;
+            r.k = P.k;
+            r.v = P.v;
+            r.q_norm = w.q_norm;
+            r.k_norm = w.k_norm;
+            r.eps = d.rms_eps;
+            r.cos_tab = e->cos_tab;
+            r.sin_tab = e->sin_tab;
+            r.pos = P.io;
+            r.kcache = kc;
+            r.vcache = vc;
+            r.kv_fp16 = e->o.kv_fp16;
+            r.n_heads = d.n_heads;
+            r.n_kv_heads = d.n_kv_heads;
+            r.head_dim = hd;
+            r.max_seq = e->o.max_seq_len;
+            r.n_tokens = n;
+            TQ_TRY(launch_qk_rope_kv(r, st));
+        }
+        {
+            AttnPrefillArgs a{};
+            a.q = P.q;
+            a.k = kc;
+            a.v = vc;
+            a.kv_fp16 = e->o.kv_fp16;
+            a.p0 = p0;
+            a.n = n;
+            a.max_seq = e->o.max_seq_len;
+            a.n_heads = d.n_heads;
+            a.n_kv_heads = d.n_kv_heads;
+            a.head_dim = hd;
+            a.scale = 1.0f / sqrtf((float)hd);
+            a.out = P.attn;
+            TQ_TRY(launch_attn_prefill(a, st));
+        }
+        TQ_TRY(pack(P.attn, qd));
+        TQ_TRY(mm(l, 3, 1, 1, qd));
+        TQ_TRY(launch_rmsnorm(P.hidden, w.post_ln, P.xn, n, H, d.rms_eps, st));
+        if (!w.moe) {
+            TQ_TRY(pack(P.xn, H));
+            TQ_TRY(mm(l, 4, 2, 2, H));
+            TQ_TRY(launch_swiglu_out(P.gate, P.up, P.act, n * d.inter, st));
+            TQ_TRY(pack(P.act, d.inter));
+            TQ_TRY(mm(l, 6, 1, 3, d.inter));
+            continue;
+        }
+        const int k = d.experts_per_tok, E = d.n_experts, mi = d.moe_inter;
+        if (pl.router) {
+            TQ_TRY(pack(P.xn, H));
+            TQ_TRY(mm(l, 4, 1, 2, H));
+        } else {
+            TQ_TRY(launch_router_rows(P.xn, n, H, w.router_f32, E, P.logits, st));
+        }
+        TQ_TRY(launch_topk_rows(P.logits, n, E, k, P.idx, P.wts, st));
+        MoePlanArgs a{};
+        a.idx = P.idx;
+        a.n = n;
+        a.k = k;
+        a.E = E;
+        a.G = G;
+        a.H = H;
+        a.mi = mi;
+        a.nt = P.moe_nt;
+        a.wg = pl.ex_gate;
+        a.wu = pl.ex_up;
+        a.wd = pl.ex_down;
+        a.wgu_stride = (long long)pl.ex_gu_stride;
+        a.wd_stride = (long long)pl.ex_down_stride;
+        a.xn = P.xn;
+        a.act = P.mact;
+        a.hbuf = P.mh;
+        a.ubuf = P.mu;
+        a.obuf = P.mo;
+        a.rows = P.rows;
+        a.slot = P.slot;
+        a.jobs_gu = P.jobs_gu;
+        a.jobs_dn = P.jobs_dn;
+        a.tile_gu = P.tile_gu;
+        a.tile_dn = P.tile_dn;
+        a.ntiles = P.ntiles;
+        a.pack_gu = P.pack_gu;
+        a.pack_dn = P.pack_dn;
+        a.status = status;
+        TQ_TRY(launch_moe_plan(a, st));
+        const int npad = (n + 15) & ~15;  // a token picks an expert at most once
+        const int tgu = 2 * moe_plan_max_tiles(n, k, E, mi, P.moe_nt);
+        const int tdn = moe_plan_max_tiles(n, k, E, H, P.moe_nt);
+        TQ_TRY(launch_mm_pack_x_grouped(P.pack_gu, E, H, G, npad, P.bhi, P.blo, st));
+        TQ_TRY(launch_matmul_i4_planned(P.jobs_gu, P.tile_gu, P.ntiles, tgu, H, G, P.moe_nt, P.bhi,
+                                        P.blo, status, st));
+        TQ_TRY(launch_swiglu_out(P.mh, P.mu, P.mact, n * k * mi, st));
+        TQ_TRY(launch_mm_pack_x_grouped(P.pack_dn, E, mi, G, npad, P.bhi, P.blo, st));
+        TQ_TRY(launch_matmul_i4_planned(P.jobs_dn, P.tile_dn, P.ntiles + 1, tdn, mi, G, P.moe_nt,
+                                        P.bhi, P.blo, status, st));
+        TQ_TRY(launch_moe_combine_rows(P.hidden, P.mo, P.wts, P.slot, n, k, H, st));
+    }
+    return TQB200_OK;
+}
+
 }  // namespace
 }  // namespace tqb200
 
@@ -875,6 +1268,45 @@ int tqb200_engine_step(tqb200_engine *e, int token_id, int *next_token) {
     TQ_CUDA_TRY(cudaStreamSynchronize(e->stream));
     TQ_TRY(check_status(e));
     e->pos += 1;
+    if (next_token) *next_token = e->h_io[2];
+    return TQB200_OK;
+}
+
+int tqb200_engine_prefill(tqb200_engine *e, const int *tokens, int n, int *next_token) {
+    TQ_CHECK_ARG(e && tokens && n > 0, "bad prefill arguments");
+    TQ_CHECK_ARG(e->pos + n <= e->o.max_seq_len, "positions %d..%d exceed max_seq_len %d", e->pos,
+                 e->pos + n, e->o.max_seq_len);
+    for (int i = 0; i < n; ++i)
+        TQ_CHECK_ARG(tokens[i] >= 0 && tokens[i] < e->d.vocab, "token %d (%d) out of range [0, %d)",
+                     i, tokens[i], e->d.vocab);
+    if (!prefill_batched(e)) {  // token by token through the decode step
+        int next = 0;
+        for (int i = 0; i < n; ++i) TQ_TRY(tqb200_engine_step(e, tokens[i], &next));
+        if (next_token) *next_token = next;
+        return TQB200_OK;
+    }
+    TQ_CUDA_TRY(cudaSetDevice(e->device));
+    TQ_TRY(prefill_setup(e));
+    Prefill &P = e->pf;
+    std::vector<int> io((size_t)P.cap + 1);
+    for (int c0 = 0; c0 < n; c0 += P.cap) {
+        const int m = std::min(P.cap, n - c0);
+        io[0] = e->pos + c0;
+        std::copy(tokens + c0, tokens + c0 + m, io.begin() + 1);
+        // pageable source: the call returns once the bytes are staged, so `io` is reusable
+        TQ_CUDA_TRY(cudaMemcpyAsync(P.io, io.data(), (size_t)(m + 1) * 4, cudaMemcpyHostToDevice,
+                                    e->stream));
+        TQ_TRY(prefill_chunk(e, m, e->pos + c0));
+        if (c0 + m == n) {  // the prompt's last token -> logits and the greedy next token
+            TQ_CUDA_TRY(cudaMemcpyAsync(e->hidden, P.hidden + (size_t)(m - 1) * e->d.hidden,
+                                        (size_t)e->d.hidden * 4, cudaMemcpyDeviceToDevice, e->stream));
+            TQ_TRY(launch_lm_head(e));
+        }
+    }
+    TQ_CUDA_TRY(cudaMemcpyAsync(e->h_io + 2, e->io_out, 8, cudaMemcpyDeviceToHost, e->stream));
+    TQ_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    TQ_TRY(check_status(e));
+    e->pos += n;
     if (next_token) *next_token = e->h_io[2];
     return TQB200_OK;
 }

@@ -82,6 +82,16 @@ struct MmJob {
     int M, N, ldy;
     int tile_begin;       // first CTA of this job (jobs in CTA order)
     long long b_off;      // offset (bf16 elements) of this job's X planes
+    const float *resid = nullptr;  // optional: y = resid + W x (same layout as y)
+    const float *bias = nullptr;   // optional: y = W x + bias[row]
+};
+constexpr int kMmTileRows = 256;  // weight rows per matmul CTA
+// One source of a grouped X pack: column n of the job is x + (cols ? cols[n] : n) * ldx.
+struct MmPackJob {
+    const float *x;
+    const int *cols;
+    int ldx, N;
+    long long b_off;      // bf16 elements into the planes
 };
 bool mm_group_supported(int G);  // the tensor-core path covers G = 32, 64, 128
 // bytes of the two bf16 X planes (hi, lo) for K x N at group size G
@@ -97,6 +107,59 @@ int launch_mm_pack_x(const float *x, const int *cols, int ldx, int K, int N, int
 int launch_matmul_i4_grouped(const MmJob *host_jobs, const MmJob *dev_jobs, int n_jobs, int K,
                              int G, int nt, const uint16_t *bhi, const uint16_t *blo,
                              int total_tiles, int *status, cudaStream_t st);
+// Device-planned launch: the job of tile i is dev_tile_job[i]; tiles at or beyond
+// *dev_n_tiles (written on the device, <= max_tiles) return at once.
+int launch_matmul_i4_planned(const MmJob *dev_jobs, const int *dev_tile_job, const int *dev_n_tiles,
+                             int max_tiles, int K, int G, int nt, const uint16_t *bhi,
+                             const uint16_t *blo, int *status, cudaStream_t st);
+// ---- prefill (prompt) pieces
+// Causal GQA attention of n new tokens at positions p0 .. p0+n-1 whose keys and values
+// are already in the cache: out[t] = softmax(q[t] K[0..p0+t]^T * scale) V[0..p0+t].
+struct AttnPrefillArgs {
+    const float *q;        // [n][n_heads * head_dim] (QK-normed, rotated)
+    const void *k, *v;     // [n_kv_heads][max_seq][head_dim] fp32 or fp16
+    int kv_fp16;
+    int p0, n, max_seq;
+    int n_heads, n_kv_heads, head_dim;
+    float scale;
+    float *out;            // [n][n_heads * head_dim]
+};
+int launch_attn_prefill(const AttnPrefillArgs &a, cudaStream_t st);
+bool attn_prefill_supported(int n_heads, int n_kv_heads, int head_dim);
+
+// MoE layer plan (one CTA on the device): bucket the n*k (token, choice) assignments by
+// expert and write the grouped GEMM jobs, pack jobs and tile maps of gate/up and down.
+constexpr int kMoePlanMaxExperts = 1024;
+struct MoePlanArgs {
+    const int *idx;        // [n*k] chosen experts
+    int n, k, E;
+    int G, H, mi, nt;      // group size, hidden, expert intermediate, tile width
+    const uint8_t *wg, *wu, *wd;  // tile-contiguous expert weights, expert e at e * stride
+    long long wgu_stride, wd_stride;
+    const float *xn;       // [n][H] normalised hidden rows (gate/up input)
+    const float *act;      // [n*k][mi] SwiGLU rows in bucket order (down input)
+    float *hbuf, *ubuf;    // [n*k][mi] gate / up outputs in bucket order
+    float *obuf;           // [n*k][H] down outputs in bucket order
+    int *rows, *slot;      // [n*k] token of bucket row; bucket row of assignment
+    MmJob *jobs_gu, *jobs_dn;     // [2E], [E]
+    int *tile_gu, *tile_dn;       // tile -> job maps (moe_plan_max_tiles entries)
+    int *ntiles;                  // [2] tiles in use: gate/up, down
+    MmPackJob *pack_gu, *pack_dn; // [E] each
+    int *status;
+};
+int launch_moe_plan(const MoePlanArgs &a, cudaStream_t st);
+// upper bounds for the buffers of a plan: tiles of one job kind of M rows at width nt,
+// and X-plane elements (one plane) for K
+int moe_plan_max_tiles(int n, int k, int E, int M, int nt);
+long long moe_plan_plane_elems(int n, int k, int E, int K, int G);
+
+// X planes of several jobs in one launch (dev_jobs: device array of n_jobs entries)
+int launch_mm_pack_x_grouped(const MmPackJob *dev_jobs, int n_jobs, int K, int G, int max_npad,
+                             uint16_t *bhi, uint16_t *blo, cudaStream_t st);
+// tiles of one job of M rows and N columns at tile width nt
+int mm_job_tiles(int M, int N, int nt);
+// bf16 elements of one plane for N columns (the b_off step between jobs)
+long long mm_plane_elems(int K, int N, int G);
 // Y = W X (matmul_i4_ref semantics); scratch holds mm_scratch_bytes(M, K, N, G) bytes
 int launch_matmul_i4(const uint8_t *w, const float *x, float *y, int M, int K, int N, int G,
                      void *scratch, int *status, cudaStream_t st);
@@ -142,6 +205,7 @@ struct QkRopeKvArgs {
     void *kcache, *vcache;    // layer slices [KVH][max_seq][hd]
     int kv_fp16;
     int n_heads, n_kv_heads, head_dim, max_seq;
+    int n_tokens = 1;         // consecutive tokens (rows of q/k/v) at *pos, *pos + 1, ...
 };
 int launch_qk_rope_kv(const QkRopeKvArgs &a, cudaStream_t st);
 
@@ -197,6 +261,13 @@ int launch_moe_router(const float *h, const float *norm_w, float eps, int H, con
 int launch_moe_combine(float *h, const float *o, const float *wts, int k, int H, bool pdl,
                        cudaStream_t st);
 int launch_embed(const void *table, int dtype, const int *token, int dim, int group_size,
-                 float *out, cudaStream_t st);
+                 float *out, cudaStream_t st, int n_tokens = 1);
+// MoE prefill: router logits of n tokens (f32 router, xn normalised rows), top-k softmax
+// per token, and h[t] += sum_j wts[t][j] * o[slot[t*k+j]] per token.
+int launch_router_rows(const float *xn, int n, int H, const float *W, int E, float *logits,
+                       cudaStream_t st);
+int launch_topk_rows(const float *logits, int n, int E, int k, int *idx, float *wts, cudaStream_t st);
+int launch_moe_combine_rows(float *h, const float *o, const float *wts, const int *slot, int n,
+                            int k, int H, cudaStream_t st);
 
 }  // namespace tqb200

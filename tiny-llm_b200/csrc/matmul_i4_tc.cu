@@ -56,6 +56,7 @@ constexpr int kLoadWarp = kMmaWarp + 1;           // warp 17: bulk copies (TMA)
 constexpr int kMmThreads = (kLoadWarp + 1) * 32;
 constexpr int kMmMaxStages = 4;
 constexpr int kTileRows = 2 * kMmRows;  // weight rows per CTA: two accumulators share X
+static_assert(kTileRows == kMmTileRows, "tile rows");
 constexpr int kMmMaxCols = 64;     // tile width limit (epilogue registers)
 // group scales handed from producers to the epilogue: a slot is rewritten only after the
 // epilogue has read it (the producer's stage wait orders it behind MMA i-S, which waited
@@ -67,6 +68,8 @@ struct MmParams {
     MmJob job0;            // used when jobs == nullptr
     const MmJob *jobs;     // device array (grouped launch) or nullptr
     int n_jobs;
+    const int *tile_job;   // device-planned launch: job of every tile (else binary search)
+    const int *n_tiles;    // device-planned launch: tiles in use
     int K, ng;             // ng = ceil(K / G) groups = pipeline stages of a tile
     int nt;                // tile width in columns (multiple of 16, <= kMmMaxCols)
     const uint16_t *bhi, *blo;  // X planes (bf16 bits), see mm_pack_x_kernel
@@ -221,6 +224,60 @@ __global__ void mm_pack_x_kernel(const float *__restrict__ x, const int *__restr
     }
 }
 
+// Several jobs' X planes in one launch: blockIdx.y is the job.
+template <int G>
+__global__ void mm_pack_x_grouped_kernel(const MmPackJob *__restrict__ jobs, int K, int ng,
+                                         uint16_t *__restrict__ bhi, uint16_t *__restrict__ blo) {
+    constexpr int CK = (G + 16) / 8;
+    const MmPackJob jb = jobs[blockIdx.y];
+    const int npad = (jb.N + 15) & ~15;
+    const long long total = (long long)npad * ng;
+    for (long long c = blockIdx.x * (long long)blockDim.x + threadIdx.x; c < total;
+         c += (long long)gridDim.x * blockDim.x) {
+        const int n = (int)(c % npad);
+        const int g = (int)(c / npad);
+        const size_t base = (size_t)jb.b_off + ((size_t)g * (npad / 8) + n / 8) * CK * 64 + (size_t)(n % 8) * 8;
+        uint4 *dh = reinterpret_cast<uint4 *>(bhi + base);
+        uint4 *dl = reinterpret_cast<uint4 *>(blo + base);
+        const float *src = n < jb.N ? jb.x + (size_t)(jb.cols ? jb.cols[n] : n) * jb.ldx : nullptr;
+        float xs = 0.0f;
+#pragma unroll 1
+        for (int kc = 0; kc < G / 8; ++kc) {
+            uint32_t h[4], l[4];
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+                float v[2];
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int k = g * G + 8 * kc + p + 4 * e;
+                    v[e] = (src && k < K) ? src[k] : 0.0f;
+                }
+                const uint16_t h0 = bf16_bits(v[0]), h1 = bf16_bits(v[1]);
+                const uint16_t l0 = bf16_bits(__fsub_rn(v[0], bf16_val(h0)));
+                const uint16_t l1 = bf16_bits(__fsub_rn(v[1], bf16_val(h1)));
+                h[p] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+                l[p] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+            }
+            dh[kc * 8] = make_uint4(h[0], h[1], h[2], h[3]);
+            dl[kc * 8] = make_uint4(l[0], l[1], l[2], l[3]);
+        }
+        if (src) {
+            const int k0 = g * G, k1 = min(K, k0 + G);
+            for (int k = k0; k < k1; ++k) xs = __fadd_rn(xs, src[k]);
+        }
+        const uint16_t x1 = bf16_bits(xs);
+        const float r1 = __fsub_rn(xs, bf16_val(x1));
+        const uint16_t x2 = bf16_bits(r1);
+        const uint16_t x3 = bf16_bits(__fsub_rn(r1, bf16_val(x2)));
+        dh[(G / 8) * 8] = make_uint4((uint32_t)x1 | ((uint32_t)x2 << 16),
+                                     (uint32_t)x3 | ((uint32_t)x1 << 16),
+                                     (uint32_t)x2 | ((uint32_t)x3 << 16), 0u);
+        dh[(G / 8 + 1) * 8] = make_uint4(0u, 0u, 0u, 0u);
+        dl[(G / 8) * 8] = make_uint4(0u, 0u, 0u, 0u);
+        dl[(G / 8 + 1) * 8] = make_uint4(0u, 0u, 0u, 0u);
+    }
+}
+
 // ---------------------------------------------------------------- weight repack
 // Interleaved i4 rows (runtime/tiny_format.h:66-77) -> tile-contiguous blocks: for every
 // 256-row tile and group g, the 256 rows' group bytes ([scale][zero][G/2 nibble bytes])
@@ -270,7 +327,17 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
     // ---- which tile: job j, rows m0.., columns n0..n0+nw
     int j = 0;
     const int tile = blockIdx.x;
-    while (j + 1 < P.n_jobs && tile >= job_of(P, j + 1).tile_begin) ++j;
+    if (P.tile_job) {
+        if (tile >= *P.n_tiles) return;  // uniform: before any barrier or TMEM use
+        j = P.tile_job[tile];
+    } else {  // last job whose first tile is at or before this one
+        int hi = P.n_jobs - 1;
+        while (j < hi) {
+            const int mid = (j + hi + 1) >> 1;
+            if (tile >= job_of(P, mid).tile_begin) j = mid;
+            else hi = mid - 1;
+        }
+    }
     const MmJob &job = job_of(P, j);
     const int local = tile - job.tile_begin;
     const int mt = (job.M + kTileRows - 1) / kTileRows;
@@ -402,7 +469,12 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
 #pragma unroll
             for (int c = 0; c < kMmMaxCols; ++c) {
                 const int n = n0 + c;
-                if (c < nw && n < job.N) job.y[(size_t)n * job.ldy + row] = y[c];
+                if (c < nw && n < job.N) {
+                    const size_t o = (size_t)n * job.ldy + row;
+                    float v = y[c];
+                    if (job.bias) v = v + job.bias[row];
+                    job.y[o] = job.resid ? job.resid[o] + v : v;
+                }
             }
         }
     } else if (warp == kMmaWarp) {
@@ -600,6 +672,33 @@ int launch_matmul_i4_grouped(const MmJob *host_jobs, const MmJob *dev_jobs, int 
     return launch_grouped_g<128>(P, total_tiles, st, 2);
 }
 
+int launch_matmul_i4_planned(const MmJob *dev_jobs, const int *dev_tile_job, const int *dev_n_tiles,
+                             int max_tiles, int K, int G, int nt, const uint16_t *bhi,
+                             const uint16_t *blo, int *status, cudaStream_t st) {
+    TQ_CHECK_ARG(dev_jobs && dev_tile_job && dev_n_tiles, "matmul_i4: planned launch needs its plan");
+    TQ_CHECK_ARG(mm_group_supported(G), "matmul_i4 (tensor cores): group_size %d not 32, 64 or 128", G);
+    TQ_CHECK_ARG(nt % 16 == 0 && nt >= 16 && nt <= kMmMaxCols, "matmul_i4: bad tile width %d", nt);
+    TQ_CHECK_ARG(((uintptr_t)bhi & 15) == 0 && ((uintptr_t)blo & 15) == 0, "matmul_i4: X planes not 16-byte aligned");
+    if (max_tiles <= 0) return TQB200_OK;
+    MmParams P{};
+    P.jobs = dev_jobs;
+    P.n_jobs = 0;
+    P.tile_job = dev_tile_job;
+    P.n_tiles = dev_n_tiles;
+    P.K = K;
+    P.ng = (K + G - 1) / G;
+    P.nt = nt;
+    P.bhi = bhi;
+    P.blo = blo;
+    uint32_t cols = 32;
+    while ((int)cols < 4 * nt) cols <<= 1;
+    P.tmem_cols = cols;
+    P.status = status;
+    if (G == 32) return launch_grouped_g<32>(P, max_tiles, st, 0);
+    if (G == 64) return launch_grouped_g<64>(P, max_tiles, st, 1);
+    return launch_grouped_g<128>(P, max_tiles, st, 2);
+}
+
 int launch_mm_pack_x(const float *x, const int *cols, int ldx, int K, int N, int G, uint16_t *bhi,
                      uint16_t *blo, cudaStream_t st) {
     TQ_CHECK_ARG(mm_group_supported(G), "matmul_i4: group_size %d not 32, 64 or 128", G);
@@ -615,6 +714,33 @@ int launch_mm_pack_x(const float *x, const int *cols, int ldx, int K, int N, int
         mm_pack_x_kernel<64><<<blocks, threads, 0, st>>>(x, cols, ldx, K, N, npad, ng, bhi, blo);
     else
         mm_pack_x_kernel<128><<<blocks, threads, 0, st>>>(x, cols, ldx, K, N, npad, ng, bhi, blo);
+    TQ_CUDA_TRY(cudaGetLastError());
+    return TQB200_OK;
+}
+
+int mm_job_tiles(int M, int N, int nt) {
+    const int npad = (N + 15) & ~15;
+    return ((M + kTileRows - 1) / kTileRows) * ((npad + nt - 1) / nt);
+}
+
+long long mm_plane_elems(int K, int N, int G) {
+    const long long ng = (K + G - 1) / G;
+    const long long npad = (N + 15) & ~15;
+    return ng * (G + 16) * npad;
+}
+
+int launch_mm_pack_x_grouped(const MmPackJob *dev_jobs, int n_jobs, int K, int G, int max_npad,
+                             uint16_t *bhi, uint16_t *blo, cudaStream_t st) {
+    TQ_CHECK_ARG(mm_group_supported(G), "matmul_i4: group_size %d not 32, 64 or 128", G);
+    if (n_jobs <= 0 || max_npad <= 0) return TQB200_OK;
+    const int ng = (K + G - 1) / G;
+    const int threads = 128;
+    const long long per_job = (long long)max_npad * ng;
+    const int bx = (int)std::max<long long>(1, std::min<long long>((per_job + threads - 1) / threads, 64));
+    dim3 grid(bx, n_jobs);
+    if (G == 32) mm_pack_x_grouped_kernel<32><<<grid, threads, 0, st>>>(dev_jobs, K, ng, bhi, blo);
+    else if (G == 64) mm_pack_x_grouped_kernel<64><<<grid, threads, 0, st>>>(dev_jobs, K, ng, bhi, blo);
+    else mm_pack_x_grouped_kernel<128><<<grid, threads, 0, st>>>(dev_jobs, K, ng, bhi, blo);
     TQ_CUDA_TRY(cudaGetLastError());
     return TQB200_OK;
 }

@@ -78,6 +78,7 @@ PROTOTYPES = {
     "tqb200_engine_kv_cache": ([_vp, C.POINTER(_vp), C.POINTER(C.c_size_t)], _i),
     "tqb200_engine_weight_bytes": ([_vp, C.POINTER(C.c_size_t)], _i),
     "tqb200_engine_generate": ([_vp, _i, _i, _i32, C.POINTER(_fl)], _i),
+    "tqb200_engine_prefill": ([_vp, _i32, _i, C.POINTER(_i)], _i),
     "tqb200_engine_profile_step": ([_vp, _i, _f, _i, C.POINTER(_i)], _i),
 }
 
@@ -319,6 +320,13 @@ class Engine:
     def step(self, token: int) -> int:
         nxt = C.c_int(-1)
         _check(load().tqb200_engine_step(self.h, int(token), C.byref(nxt)))
+        return nxt.value
+
+    def prefill(self, tokens) -> int:
+        """QwenModel::forward_prefill: the prompt as one batch; returns the greedy next token."""
+        toks = np.ascontiguousarray(tokens, dtype=np.int32)
+        nxt = C.c_int(-1)
+        _check(load().tqb200_engine_prefill(self.h, toks, len(toks), C.byref(nxt)))
         return nxt.value
 
     def logits(self) -> np.ndarray:
