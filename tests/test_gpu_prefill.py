@@ -64,7 +64,7 @@ def test_prefill_matches_token_by_token(tq, oracle, name, spec, kv16):
     prompt = _prompt(45, spec.vocab, 7)
     nxt = eng.prefill(prompt)
     onxt = _oracle_feed(om, prompt)
-    assert eng.position() == len(prompt)
+    assert eng.position == len(prompt)
     assert max_rel(eng.logits(), om.logits()) < TOL
     assert nxt == onxt
     toks, logits = _continue(eng, nxt, 8)
@@ -79,7 +79,7 @@ def test_prefill_matches_token_by_token(tq, oracle, name, spec, kv16):
 def test_prefill_after_decode_and_in_chunks(tq, oracle):
     """A prompt that starts after decoded positions (p0 > 0) and spans two chunks
     (512 + 100 tokens): the second chunk attends to the first chunk's cache."""
-    spec = CASES[1][1]
+    spec = replace(CASES[1][1], max_seq_len=1024)
     sm = SynthModel(spec, seed=32)
     eng = tq.Engine(sm, max_seq_len=640)
     om = oracle.model(sm, 640, False)
@@ -90,7 +90,7 @@ def test_prefill_after_decode_and_in_chunks(tq, oracle):
     prompt = _prompt(612, spec.vocab, 9)
     nxt = eng.prefill(prompt)
     onxt = _oracle_feed(om, prompt)
-    assert eng.position() == 615
+    assert eng.position == 615
     assert max_rel(eng.logits(), om.logits()) < TOL
     assert nxt == onxt
     toks, _ = _continue(eng, nxt, 4)
@@ -142,5 +142,5 @@ def test_prefill_rejects_bad_input(tq):
         eng.prefill([1, 2, 10**6])
     with pytest.raises(Exception):
         eng.prefill(list(range(40)))  # beyond max_seq_len
-    assert eng.position() == 0
+    assert eng.position == 0
     eng.close()
