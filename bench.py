@@ -28,6 +28,7 @@ reference sources) is timed on a bounded sample for ``cpu_baseline``;
 from __future__ import annotations
 
 import argparse
+import ctypes as C
 import json
 import os
 import subprocess
@@ -574,6 +575,144 @@ def bench_decode(args, rank, pg, pk, pk_kind):
     return out
 
 
+# ------------------------------------------------------------------ prefill (config 5)
+PREFILL_TOKENS = 512
+PREFILL_DECODE_STEPS = 64
+MATMUL_KINDS = ("qkv", "o_proj", "gate_up", "down")
+
+
+def prefill_flops(spec, n: int) -> dict:
+    """Algorithmic FLOPs of one n-token prefill at position 0, by part: the matmuls
+    (2*M*K per token and matrix; experts: k chosen per token), the router, causal
+    attention (QK^T and PV over n(n+1)/2 (query, key) pairs per head) and the last
+    token's lm_head."""
+    H, hd = spec.hidden, spec.head_dim
+    qd, kvd = spec.n_heads * hd, spec.n_kv_heads * hd
+    proj = 2.0 * n * (qd * H + 2 * kvd * H + H * qd)
+    if spec.n_experts:
+        ffn = 2.0 * n * spec.experts_per_tok * 3 * spec.moe_inter * H
+        router = 2.0 * n * spec.n_experts * H
+    else:
+        ffn, router = 2.0 * n * 3 * spec.inter * H, 0.0
+    attn = 4.0 * spec.n_heads * hd * (n * (n + 1) / 2)
+    L = spec.n_layers
+    return {"matmul": L * (proj + ffn), "router": L * router, "attention": L * attn,
+            "lm_head": 2.0 * spec.vocab * H}
+
+
+def bench_prefill(args, rank, pg, pk, pk_kind):
+    """a 512-token prompt through the engine's batched prefill (every
+    projection and the grouped experts on the tensor-core matmul), then 64 decode steps."""
+    import torch
+    from tqb200 import lib
+    from tqb200.model import SynthModel
+    lib.load()
+    W, K = args.warmup, args.steps
+    n = PREFILL_TOKENS
+    wl = DECODE_WORKLOADS["decode-qwen3-30b-a3b"]
+    spec = decode_spec(wl, n + PREFILL_DECODE_STEPS + 8)
+    if args.layers:
+        from dataclasses import replace as _replace
+        spec = _replace(spec, n_layers=args.layers)
+    t0 = time.time()
+    sm = SynthModel(spec, seed=0)
+    t_build = time.time() - t0
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    eng = lib.Engine(sm, max_seq_len=spec.max_seq_len, kv_fp16=False)
+    del sm.tensors
+    rng = np.random.default_rng(2)
+    prompt = rng.integers(0, spec.vocab, n).astype(np.int32)
+    ptr = C.c_void_p()
+    lib._check(lib.load().tqb200_engine_stream(eng.h, C.byref(ptr)))
+    stream = torch.cuda.ExternalStream(ptr.value)
+    for _ in range(W):  # the first one also makes the tile-contiguous weight copies
+        eng.reset()
+        eng.prefill(prompt)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
+    clocks.start()
+    barrier(pg)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(K):
+        eng.reset()
+        nxt = eng.prefill(prompt)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(pg)
+    clk = clocks.stop()
+    ms = max_over_ranks(pg, e0.elapsed_time(e1)) / K
+    # e2e: the same C-ABI call timed on the host (token ids H2D, next token + status D2H)
+    t0 = time.perf_counter()
+    for _ in range(K):
+        eng.reset()
+        eng.prefill(prompt)
+    e2e_ms = (time.perf_counter() - t0) * 1e3 / K
+    # the config's 64 decode steps after the prompt
+    toks, dec_ms = eng.generate(nxt, PREFILL_DECODE_STEPS)
+    # live per-kind times of one prefill launched kernel by kernel
+    eng.reset()
+    _, prof = eng.profile_prefill(prompt)
+    fl = prefill_flops(spec, n)
+    mm_ms = sum(prof[k] for k in MATMUL_KINDS)
+    achieved = fl["matmul"] / (mm_ms * 1e-3) / 1e12
+    total_fl = sum(fl.values())
+    peak = pk.get("bf16_tflops", 1590.0)
+    L = spec.n_layers
+    # embed; per MoE layer rmsnorm, pack, qkv, rope+kv, attention, pack, o_proj, rmsnorm,
+    # router, top-k, plan, pack, gate/up, swiglu, pack, down, combine; lm_head
+    launches = 1 + 17 * L + 1
+    out = {
+        "metric": "prefill ms per 512-token prompt, batch 1 (BASELINE config 5: Qwen3-30B-A3B-"
+                  "shaped MoE, i4 g64 experts, top-8 of 128, fp32 KV)",
+        "value": round(ms, 3), "unit": "ms/prompt", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": round(ms, 3), "higher_is_better": False, "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "u4 weights (exact bf16 codes), bf16 hi/lo activations, f32 accumulation; "
+                 "f32 attention and KV",
+        "data": "synthetic (seeded random weights of the named shape, 512 uniform random prompt ids)",
+        "config": {"workload": args.workload, "layers": L, "hidden": spec.hidden,
+                   "experts": spec.n_experts, "top_k": spec.experts_per_tok,
+                   "expert_inter": spec.moe_inter, "heads": spec.n_heads,
+                   "kv_heads": spec.n_kv_heads, "head_dim": spec.head_dim, "vocab": spec.vocab,
+                   "prompt_tokens": n, "global_batch": 1,
+                   "l2": "inputs larger than L2 (%.1f GB of expert weights read per prompt)"
+                         % (L * spec.n_experts * 3 * spec.moe_inter * spec.hidden * 0.5625 / 1e9),
+                   "parallelism": "single GPU", "model_build_s": round(t_build, 1),
+                   "prefill_tflop": round(total_fl / 1e12, 4),
+                   "prefill_tflops_whole_step": round(total_fl / (ms * 1e-3) / 1e12, 2),
+                   "decode_after_prefill_ms_per_token": round(dec_ms / PREFILL_DECODE_STEPS, 4)},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
+                     "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": None,
+                     "peak_source": pk_kind,
+                     "kernel": "mm_i4_tc_kernel<64> (every projection and expert GEMM of a prompt)",
+                     "algorithmic_flops_per_step": fl["matmul"],
+                     "matmul_ms_per_step": round(mm_ms, 3),
+                     "note": "algorithmic 2*M*N*K flops of the matmul launches over their summed "
+                             "CUDA-event times; the MMAs issue 2.5x these flops (bf16 hi + lo "
+                             "halves of X and the zero-term K step)"},
+        "kernel_ms_by_kind": {k: round(v, 4) for k, v in prof.items() if v > 0},
+        "clocks": clk,
+        "gpu_launches": launches * K,
+        "e2e": {"value": round(e2e_ms, 3), "unit": "ms/prompt", "h2d_bytes_per_step": 4 * (n + 1),
+                "d2h_bytes_per_step": 8,
+                "note": "tqb200_engine_prefill per prompt: position + ids H2D, next token + status D2H"},
+    }
+    eng.close()
+    return out
+
+
+def ref_prefill_rate(threads_note: str = ""):
+    """Reference CPU cost of a 512-token config-5 prompt: forward_prefill of an i4 MoE model
+    runs forward_token per token (runtime/qwen_forward_prefill.cpp:91-104; the batched MoE
+    path is GPTQ-only), so the cost is 512 decode steps at contexts 0..511, sampled as
+    the decode cost at the mean context 256."""
+    ms, kind, sample = ref_decode_rate("decode-qwen3-30b-a3b", PREFILL_TOKENS // 2, threads_note)
+    return ms * PREFILL_TOKENS, kind, (f"{PREFILL_TOKENS} x the per-token forward_token cost at "
+                                       f"the mean context {PREFILL_TOKENS // 2}: " + sample)
+
+
 def ref_decode_rate(workload: str, ctx: int, threads_note: str = ""):
     """Reference CPU decode cost per token for a decode workload (oracle/_ref: the
     reference's own QwenModel::forward_token and attention_decode_ref), bounded sample:
@@ -661,6 +800,23 @@ def bench_reference_arm(args, rank):
             "e2e": {"value": round(ms, 2), "unit": "ms/token", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
         }
+    if args.workload == "prefill-qwen3-30b-a3b":
+        ms, kind, sample = ref_prefill_rate(f"; host has {threads} threads")
+        return {
+            "impl": "reference",
+            "metric": "prefill ms per 512-token prompt, batch 1 (BASELINE config 5: Qwen3-30B-A3B-"
+                      "shaped MoE, i4 g64 experts, top-8 of 128, fp32 KV)",
+            "value": round(ms, 1), "unit": "ms/prompt", "n_gpus": 0, "steps": 1, "warmup": 0,
+            "ms_per_step": round(ms, 1), "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "quantised weights, f32 activations (double accumulation), f32 KV",
+            "data": "synthetic (seeded random weights of the named shape)",
+            "config": {"workload": args.workload, "prompt_tokens": PREFILL_TOKENS},
+            "cpu_baseline": {"value": round(ms, 1), "unit": "ms/prompt", "cores": 1, "kind": kind,
+                             "sample": sample},
+            "e2e": {"value": round(ms, 1), "unit": "ms/prompt", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+        }
     if args.workload == "matmul-i4":
         tf, kind, sample = ref_matmul_rate(max(2.0, 0.5 * args.steps))
         M, K, N, G = MM_SHAPE
@@ -699,7 +855,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="decode-qwen3-4b",
-                    choices=list(DECODE_WORKLOADS) + ["matvec-i4", "matmul-i4"])
+                    choices=list(DECODE_WORKLOADS) + ["matvec-i4", "matmul-i4",
+                                                      "prefill-qwen3-30b-a3b"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ctx", type=int, default=None,
@@ -726,6 +883,8 @@ def main():
         out = bench_matvec(args, rank, pg, pk, pk_kind)
     elif args.workload == "matmul-i4":
         out = bench_matmul(args, rank, pg, pk, pk_kind)
+    elif args.workload == "prefill-qwen3-30b-a3b":
+        out = bench_prefill(args, rank, pg, pk, pk_kind)
     else:
         out = bench_decode(args, rank, pg, pk, pk_kind)
     if rank == 0:
@@ -738,6 +897,11 @@ def main():
             tf, kind, sample = ref_matmul_rate(max(1.0, args.cpu_seconds))
             out["cpu_baseline"] = {"value": round(tf, 6), "unit": "TFLOP/s", "cores": 1,
                                    "kind": kind, "sample": sample + f" (host has {threads} threads)"}
+        elif args.workload == "prefill-qwen3-30b-a3b":
+            if args.cpu_seconds > 0:
+                ms, kind, sample = ref_prefill_rate(f"; host has {threads} threads")
+                out["cpu_baseline"] = {"value": round(ms, 1), "unit": "ms/prompt", "cores": 1,
+                                       "kind": kind, "sample": sample}
         elif args.cpu_seconds > 0:
             ms, kind, sample = ref_decode_rate(args.workload, out["config"]["context"],
                                                f"; host has {threads} threads")

@@ -199,6 +199,12 @@ int tqb200_engine_step(tqb200_engine *e, int token_id, int *next_token);
  * VQ2 projections, head_dim other than 64/128), as the reference falls back to
  * forward_token. */
 int tqb200_engine_prefill(tqb200_engine *e, const int *tokens, int n, int *next_token);
+/* tqb200_engine_prefill launched kernel by kernel with a CUDA event after each launch:
+ * ms_by_kind[k] sums the times of kind k (the kinds of tqb200_engine_profile_step, then
+ * rmsnorm, x_pack, moe_plan, swiglu).  Batched prefill only (TQB200_ERR_INVALID_ARG
+ * otherwise). */
+int tqb200_engine_profile_prefill(tqb200_engine *e, const int *tokens, int n, float *ms_by_kind,
+                                  int n_kinds, int *next_token);
 /* Greedy-decodes n_steps tokens with the produced token fed back on the device (no
  * host round trip per token; main.cpp's decode loop, runtime/main.cpp:1038-1041, moved
  * onto the GPU): step i feeds the token of step i-1, the first feeds token_id.

@@ -319,12 +319,13 @@ int build_rope_tables(tqb200_engine *e) {
 
 enum Kind {
     K_EMBED, K_QKV, K_ROPE_KV, K_ATTN, K_OPROJ, K_GATEUP, K_DOWN, K_LMHEAD, K_ROUTER, K_COMBINE,
-    K_NKINDS
+    K_NORM, K_PACK, K_PLAN, K_SWIGLU, K_NKINDS
 };
 
 const char *kind_name(int k) {
     static const char *n[] = {"embed", "qkv", "qk_rope_kv", "attention", "o_proj",
-                              "gate_up", "down", "lm_head", "router", "moe_combine"};
+                              "gate_up", "down", "lm_head", "router", "moe_combine",
+                              "rmsnorm", "x_pack", "moe_plan", "swiglu"};
     return (k >= 0 && k < K_NKINDS) ? n[k] : "start";
 }
 
@@ -1075,6 +1076,7 @@ int prefill_chunk(tqb200_engine *e, int n, int p0) {
     int *status = e->io_out + 1;
     TQ_TRY(prefill_plan(e, n));
     TQ_TRY(launch_embed(e->embed, e->embed_dtype, P.io + 1, H, G, P.hidden, st, n));
+    TQ_TRY(mark(e, K_EMBED));
     auto mm = [&](int l, int slot, int nj, int launch, int K) {
         const MmJob *hj = &P.hjobs[(size_t)7 * l + slot];
         return launch_matmul_i4_grouped(hj, nj > 1 ? P.jobs + (size_t)7 * l + slot : nullptr, nj, K,
@@ -1089,8 +1091,11 @@ int prefill_chunk(tqb200_engine *e, int n, int p0) {
         const PLayer &pl = P.layers[l];
         e->cur_layer = l;
         TQ_TRY(launch_rmsnorm(P.hidden, w.input_ln, P.xn, n, H, d.rms_eps, st));
+        TQ_TRY(mark(e, K_NORM));
         TQ_TRY(pack(P.xn, H));
+        TQ_TRY(mark(e, K_PACK));
         TQ_TRY(mm(l, 0, 3, 0, H));
+        TQ_TRY(mark(e, K_QKV));
         const size_t es = e->o.kv_fp16 ? 2 : 4;
         char *kvb = (char *)e->kv;
         void *kc = kvb + (size_t)l * e->layer_stride * es;
@@ -1115,6 +1120,7 @@ int prefill_chunk(tqb200_engine *e, int n, int p0) {
             r.max_seq = e->o.max_seq_len;
             r.n_tokens = n;
             TQ_TRY(launch_qk_rope_kv(r, st));
+            TQ_TRY(mark(e, K_ROPE_KV));
         }
         {
             AttnPrefillArgs a{};
@@ -1131,26 +1137,37 @@ int prefill_chunk(tqb200_engine *e, int n, int p0) {
             a.scale = 1.0f / sqrtf((float)hd);
             a.out = P.attn;
             TQ_TRY(launch_attn_prefill(a, st));
+            TQ_TRY(mark(e, K_ATTN));
         }
         TQ_TRY(pack(P.attn, qd));
+        TQ_TRY(mark(e, K_PACK));
         TQ_TRY(mm(l, 3, 1, 1, qd));
+        TQ_TRY(mark(e, K_OPROJ));
         TQ_TRY(launch_rmsnorm(P.hidden, w.post_ln, P.xn, n, H, d.rms_eps, st));
+        TQ_TRY(mark(e, K_NORM));
         if (!w.moe) {
             TQ_TRY(pack(P.xn, H));
+            TQ_TRY(mark(e, K_PACK));
             TQ_TRY(mm(l, 4, 2, 2, H));
+            TQ_TRY(mark(e, K_GATEUP));
             TQ_TRY(launch_swiglu_out(P.gate, P.up, P.act, n * d.inter, st));
+            TQ_TRY(mark(e, K_SWIGLU));
             TQ_TRY(pack(P.act, d.inter));
+            TQ_TRY(mark(e, K_PACK));
             TQ_TRY(mm(l, 6, 1, 3, d.inter));
+            TQ_TRY(mark(e, K_DOWN));
             continue;
         }
         const int k = d.experts_per_tok, E = d.n_experts, mi = d.moe_inter;
         if (pl.router) {
             TQ_TRY(pack(P.xn, H));
+            TQ_TRY(mark(e, K_PACK));
             TQ_TRY(mm(l, 4, 1, 2, H));
         } else {
             TQ_TRY(launch_router_rows(P.xn, n, H, w.router_f32, E, P.logits, st));
         }
         TQ_TRY(launch_topk_rows(P.logits, n, E, k, P.idx, P.wts, st));
+        TQ_TRY(mark(e, K_ROUTER));
         MoePlanArgs a{};
         a.idx = P.idx;
         a.n = n;
@@ -1181,17 +1198,24 @@ int prefill_chunk(tqb200_engine *e, int n, int p0) {
         a.pack_dn = P.pack_dn;
         a.status = status;
         TQ_TRY(launch_moe_plan(a, st));
+        TQ_TRY(mark(e, K_PLAN));
         const int npad = (n + 15) & ~15;  // a token picks an expert at most once
         const int tgu = 2 * moe_plan_max_tiles(n, k, E, mi, P.moe_nt);
         const int tdn = moe_plan_max_tiles(n, k, E, H, P.moe_nt);
         TQ_TRY(launch_mm_pack_x_grouped(P.pack_gu, E, H, G, npad, P.bhi, P.blo, st));
+        TQ_TRY(mark(e, K_PACK));
         TQ_TRY(launch_matmul_i4_planned(P.jobs_gu, P.tile_gu, P.ntiles, tgu, H, G, P.moe_nt, P.bhi,
                                         P.blo, status, st));
+        TQ_TRY(mark(e, K_GATEUP));
         TQ_TRY(launch_swiglu_out(P.mh, P.mu, P.mact, n * k * mi, st));
+        TQ_TRY(mark(e, K_SWIGLU));
         TQ_TRY(launch_mm_pack_x_grouped(P.pack_dn, E, mi, G, npad, P.bhi, P.blo, st));
+        TQ_TRY(mark(e, K_PACK));
         TQ_TRY(launch_matmul_i4_planned(P.jobs_dn, P.tile_dn, P.ntiles + 1, tdn, mi, G, P.moe_nt,
                                         P.bhi, P.blo, status, st));
+        TQ_TRY(mark(e, K_DOWN));
         TQ_TRY(launch_moe_combine_rows(P.hidden, P.mo, P.wts, P.slot, n, k, H, st));
+        TQ_TRY(mark(e, K_COMBINE));
     }
     return TQB200_OK;
 }
@@ -1272,6 +1296,33 @@ int tqb200_engine_step(tqb200_engine *e, int token_id, int *next_token) {
     return TQB200_OK;
 }
 
+int tqb200_engine_profile_prefill(tqb200_engine *e, const int *tokens, int n, float *ms_by_kind,
+                                  int n_kinds, int *next_token) {
+    TQ_CHECK_ARG(e && ms_by_kind && n_kinds > 0, "bad profile arguments");
+    TQ_CHECK_ARG(prefill_batched(e), "this engine's prefill runs as decode steps");
+    TQ_CUDA_TRY(cudaSetDevice(e->device));
+    TQ_TRY(prefill_setup(e));  // first-use weight repack stays outside the timed launches
+    e->prof = true;
+    TQ_TRY(mark(e, -1));
+    const int st = tqb200_engine_prefill(e, tokens, n, next_token);
+    e->prof = false;
+    for (int k = 0; k < n_kinds; ++k) ms_by_kind[k] = 0.0f;
+    int rc = st;
+    for (size_t i = 1; i < e->prof_ev.size() && rc == TQB200_OK; ++i) {
+        float ms = 0.0f;
+        if (cudaEventElapsedTime(&ms, e->prof_ev[i - 1], e->prof_ev[i]) != cudaSuccess) {
+            rc = set_error(TQB200_ERR_CUDA, "profile events");
+            break;
+        }
+        const int k = e->prof_kind[i];
+        if (k >= 0 && k < n_kinds) ms_by_kind[k] += ms;
+    }
+    for (auto ev : e->prof_ev) cudaEventDestroy(ev);
+    e->prof_ev.clear();
+    e->prof_kind.clear();
+    return rc;
+}
+
 int tqb200_engine_prefill(tqb200_engine *e, const int *tokens, int n, int *next_token) {
     TQ_CHECK_ARG(e && tokens && n > 0, "bad prefill arguments");
     TQ_CHECK_ARG(e->pos + n <= e->o.max_seq_len, "positions %d..%d exceed max_seq_len %d", e->pos,
@@ -1301,6 +1352,7 @@ int tqb200_engine_prefill(tqb200_engine *e, const int *tokens, int n, int *next_
             TQ_CUDA_TRY(cudaMemcpyAsync(e->hidden, P.hidden + (size_t)(m - 1) * e->d.hidden,
                                         (size_t)e->d.hidden * 4, cudaMemcpyDeviceToDevice, e->stream));
             TQ_TRY(launch_lm_head(e));
+            TQ_TRY(mark(e, K_LMHEAD));
         }
     }
     TQ_CUDA_TRY(cudaMemcpyAsync(e->h_io + 2, e->io_out, 8, cudaMemcpyDeviceToHost, e->stream));

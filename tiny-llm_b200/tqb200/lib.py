@@ -79,6 +79,7 @@ PROTOTYPES = {
     "tqb200_engine_weight_bytes": ([_vp, C.POINTER(C.c_size_t)], _i),
     "tqb200_engine_generate": ([_vp, _i, _i, _i32, C.POINTER(_fl)], _i),
     "tqb200_engine_prefill": ([_vp, _i32, _i, C.POINTER(_i)], _i),
+    "tqb200_engine_profile_prefill": ([_vp, _i32, _i, _f, _i, C.POINTER(_i)], _i),
     "tqb200_engine_profile_step": ([_vp, _i, _f, _i, C.POINTER(_i)], _i),
 }
 
@@ -345,7 +346,17 @@ class Engine:
         return out[:n_steps].tolist(), ms.value
 
     KINDS = ("embed", "qkv", "qk_rope_kv", "attention", "o_proj", "gate_up", "down", "lm_head",
-             "router", "moe_combine")
+             "router", "moe_combine", "rmsnorm", "x_pack", "moe_plan", "swiglu")
+
+    def profile_prefill(self, tokens):
+        """A prefill launched kernel by kernel, CUDA events between launches; returns
+        (next token, {kind: ms})."""
+        toks = np.ascontiguousarray(tokens, dtype=np.int32)
+        ms = np.zeros(len(self.KINDS), np.float32)
+        nxt = C.c_int(-1)
+        _check(load().tqb200_engine_profile_prefill(self.h, toks, len(toks), ms, len(self.KINDS),
+                                                    C.byref(nxt)))
+        return nxt.value, dict(zip(self.KINDS, ms.tolist()))
 
     def profile_step(self, token: int):
         """One kernel-by-kernel step timed with CUDA events; returns (next, {kind: ms})."""
