@@ -740,42 +740,55 @@ __global__ void embed_kernel(const void *__restrict__ table, int dtype, const in
 // Router logits of many tokens (f32 router): logits[t][e] = W[e] . xn[t] with the
 // products and the sum in double (matvec_f32_ref, kernels/matvec/matvec_f32_ref.cpp),
 // xn already normalised.  CTA = 16 tokens x 32 experts, K staged through shared memory
-// in chunks; thread = one token, two experts.
-constexpr int kRrTok = 16, kRrExp = 32, kRrK = 128;
+// in chunks, widened to double once at staging (conversions are slow); thread = one
+// token, two experts, two accumulation chains each.
+constexpr int kRrTok = 16, kRrExp = 32, kRrK = 64;
 
 __global__ void __launch_bounds__(256) router_rows_kernel(const float *__restrict__ xn, int n, int H,
                                                           const float *__restrict__ W, int E,
                                                           float *__restrict__ logits) {
-    __shared__ float xs[kRrTok][kRrK + 1];
-    __shared__ float ws[kRrExp][kRrK + 1];
+    __shared__ double xs[kRrTok][kRrK + 1];
+    __shared__ double ws[kRrExp][kRrK + 1];
     const int tid = threadIdx.x;
     const int t0 = blockIdx.y * kRrTok, e0 = blockIdx.x * kRrExp;
     const int tt = tid & 15, te = tid >> 4;
-    double a0 = 0.0, a1 = 0.0;
+    constexpr int RX = kRrTok * kRrK / 256, RW = kRrExp * kRrK / 256;
+    float px[RX], pw[RW];  // the next chunk, loaded while this one is consumed
+    auto fetch = [&](int k0) {
+#pragma unroll
+        for (int r = 0; r < RX; ++r) {
+            const int i = tid + 256 * r, row = i / kRrK, c = i % kRrK;
+            px[r] = (t0 + row < n && k0 + c < H) ? xn[(size_t)(t0 + row) * H + k0 + c] : 0.0f;
+        }
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            const int i = tid + 256 * r, row = i / kRrK, c = i % kRrK;
+            pw[r] = (e0 + row < E && k0 + c < H) ? W[(size_t)(e0 + row) * H + k0 + c] : 0.0f;
+        }
+    };
+    fetch(0);
+    double a0 = 0.0, a1 = 0.0, b0 = 0.0, b1 = 0.0;  // two chains per output
     for (int k0 = 0; k0 < H; k0 += kRrK) {
         __syncthreads();
 #pragma unroll
-        for (int r = 0; r < kRrTok * kRrK / 256; ++r) {
-            const int i = tid + 256 * r, row = i / kRrK, c = i % kRrK;
-            xs[row][c] = (t0 + row < n && k0 + c < H) ? xn[(size_t)(t0 + row) * H + k0 + c] : 0.0f;
-        }
+        for (int r = 0; r < RX; ++r) xs[(tid + 256 * r) / kRrK][(tid + 256 * r) % kRrK] = (double)px[r];
 #pragma unroll
-        for (int r = 0; r < kRrExp * kRrK / 256; ++r) {
-            const int i = tid + 256 * r, row = i / kRrK, c = i % kRrK;
-            ws[row][c] = (e0 + row < E && k0 + c < H) ? W[(size_t)(e0 + row) * H + k0 + c] : 0.0f;
-        }
+        for (int r = 0; r < RW; ++r) ws[(tid + 256 * r) / kRrK][(tid + 256 * r) % kRrK] = (double)pw[r];
         __syncthreads();
+        if (k0 + kRrK < H) fetch(k0 + kRrK);
 #pragma unroll 8
-        for (int c = 0; c < kRrK; ++c) {
-            const double x = (double)xs[tt][c];
-            a0 = fma((double)ws[te][c], x, a0);
-            a1 = fma((double)ws[te + 16][c], x, a1);
+        for (int c = 0; c < kRrK; c += 2) {
+            const double x0 = xs[tt][c], x1 = xs[tt][c + 1];
+            a0 = fma(ws[te][c], x0, a0);
+            a1 = fma(ws[te][c + 1], x1, a1);
+            b0 = fma(ws[te + 16][c], x0, b0);
+            b1 = fma(ws[te + 16][c + 1], x1, b1);
         }
     }
     const int t = t0 + tt;
     if (t < n) {
-        if (e0 + te < E) logits[(size_t)t * E + e0 + te] = (float)a0;
-        if (e0 + te + 16 < E) logits[(size_t)t * E + e0 + te + 16] = (float)a1;
+        if (e0 + te < E) logits[(size_t)t * E + e0 + te] = (float)(a0 + a1);
+        if (e0 + te + 16 < E) logits[(size_t)t * E + e0 + te + 16] = (float)(b0 + b1);
     }
 }
 

@@ -89,7 +89,7 @@ struct Prefill {
     float *logits = nullptr, *wts = nullptr, *mh = nullptr, *mu = nullptr, *mact = nullptr,
           *mo = nullptr;
     int *idx = nullptr, *rows = nullptr, *slot = nullptr, *ntiles = nullptr;
-    int *tile_gu = nullptr, *tile_dn = nullptr;
+    int *tile_gu = nullptr, *tile_dn = nullptr, *pack_map = nullptr;
     MmJob *jobs_gu = nullptr, *jobs_dn = nullptr;
     MmPackJob *pack_gu = nullptr, *pack_dn = nullptr;
     int max_tiles_gu = 0, max_tiles_dn = 0, moe_nt = 64;
@@ -912,7 +912,8 @@ int prefill_setup(tqb200_engine *e) {
     const bool moe = d.model_type == TQB200_MODEL_QWEN3_MOE;
     const int k = moe ? d.experts_per_tok : 1, E = moe ? d.n_experts : 0, mi = d.moe_inter;
     P.cap = std::min(kPrefillChunk, e->o.max_seq_len);
-    if (moe) P.cap = std::min(P.cap, 24 * 1024 / k);  // plan kernel: n*k assignments in shared memory
+    if (moe)  // the plan kernel holds the chunk's n*k assignments in shared memory
+        while (P.cap > 1 && moe_plan_smem_bytes(P.cap, k, E) > kMoePlanMaxSmem) P.cap /= 2;
     const int cap = P.cap;
     P.layers.resize(d.n_layers);
     for (int l = 0; l < d.n_layers; ++l) {
@@ -980,14 +981,16 @@ int prefill_setup(tqb200_engine *e) {
         P.mu = mt(A * mi);
         P.mact = mt(A * mi);
         P.mo = mt(A * H);
-        const size_t ib = (2 * A + 2 + (size_t)P.max_tiles_gu + P.max_tiles_dn) * 4 + 256;
+        const size_t mb = (size_t)moe_plan_max_cols(cap, k, E) / 8;
+        const size_t ib = (2 * A + 4 + (size_t)P.max_tiles_gu + P.max_tiles_dn + mb) * 4 + 256;
         TQ_TRY(dev_alloc(e, ib, &p));
         int *ip = (int *)p;
         P.rows = ip, ip += A;
         P.slot = ip, ip += A;
-        P.ntiles = ip, ip += 2;
+        P.ntiles = ip, ip += 4;
         P.tile_gu = ip, ip += P.max_tiles_gu;
-        P.tile_dn = ip;
+        P.tile_dn = ip, ip += P.max_tiles_dn;
+        P.pack_map = ip;
         TQ_TRY(dev_alloc(e, sizeof(MmJob) * 3 * E + sizeof(MmPackJob) * 2 * E + 256, &p));
         P.jobs_gu = (MmJob *)p;
         P.jobs_dn = P.jobs_gu + 2 * E;
@@ -1196,20 +1199,21 @@ int prefill_chunk(tqb200_engine *e, int n, int p0) {
         a.ntiles = P.ntiles;
         a.pack_gu = P.pack_gu;
         a.pack_dn = P.pack_dn;
+        a.pack_map = P.pack_map;
         a.status = status;
         TQ_TRY(launch_moe_plan(a, st));
         TQ_TRY(mark(e, K_PLAN));
-        const int npad = (n + 15) & ~15;  // a token picks an expert at most once
+        const int nbk = moe_plan_max_cols(n, k, E) / 8;
         const int tgu = 2 * moe_plan_max_tiles(n, k, E, mi, P.moe_nt);
         const int tdn = moe_plan_max_tiles(n, k, E, H, P.moe_nt);
-        TQ_TRY(launch_mm_pack_x_grouped(P.pack_gu, E, H, G, npad, P.bhi, P.blo, st));
+        TQ_TRY(launch_mm_pack_x_mapped(P.pack_gu, P.pack_map, P.ntiles + 2, nbk, H, G, P.bhi, P.blo, st));
         TQ_TRY(mark(e, K_PACK));
         TQ_TRY(launch_matmul_i4_planned(P.jobs_gu, P.tile_gu, P.ntiles, tgu, H, G, P.moe_nt, P.bhi,
                                         P.blo, status, st));
         TQ_TRY(mark(e, K_GATEUP));
         TQ_TRY(launch_swiglu_out(P.mh, P.mu, P.mact, n * k * mi, st));
         TQ_TRY(mark(e, K_SWIGLU));
-        TQ_TRY(launch_mm_pack_x_grouped(P.pack_dn, E, mi, G, npad, P.bhi, P.blo, st));
+        TQ_TRY(launch_mm_pack_x_mapped(P.pack_dn, P.pack_map, P.ntiles + 2, nbk, mi, G, P.bhi, P.blo, st));
         TQ_TRY(mark(e, K_PACK));
         TQ_TRY(launch_matmul_i4_planned(P.jobs_dn, P.tile_dn, P.ntiles + 1, tdn, mi, G, P.moe_nt,
                                         P.bhi, P.blo, status, st));

@@ -92,6 +92,7 @@ struct MmPackJob {
     const int *cols;
     int ldx, N;
     long long b_off;      // bf16 elements into the planes
+    int col0;             // mapped launch: first padded column of this job among all jobs
 };
 bool mm_group_supported(int G);  // the tensor-core path covers G = 32, 64, 128
 // bytes of the two bf16 X planes (hi, lo) for K x N at group size G
@@ -143,19 +144,25 @@ struct MoePlanArgs {
     int *rows, *slot;      // [n*k] token of bucket row; bucket row of assignment
     MmJob *jobs_gu, *jobs_dn;     // [2E], [E]
     int *tile_gu, *tile_dn;       // tile -> job maps (moe_plan_max_tiles entries)
-    int *ntiles;                  // [2] tiles in use: gate/up, down
+    int *ntiles;                  // [3] tiles in use: gate/up, down; 8-column blocks
     MmPackJob *pack_gu, *pack_dn; // [E] each
+    int *pack_map;                // 8-column block -> expert (moe_plan_max_cols / 8 entries)
     int *status;
 };
 int launch_moe_plan(const MoePlanArgs &a, cudaStream_t st);
 // upper bounds for the buffers of a plan: tiles of one job kind of M rows at width nt,
 // and X-plane elements (one plane) for K
 int moe_plan_max_tiles(int n, int k, int E, int M, int nt);
+int moe_plan_max_cols(int n, int k, int E);  // padded columns over all experts
+// dynamic shared memory of the plan kernel (at most kMoePlanMaxSmem)
+size_t moe_plan_smem_bytes(int n, int k, int E);
+constexpr size_t kMoePlanMaxSmem = 160 * 1024;
 long long moe_plan_plane_elems(int n, int k, int E, int K, int G);
 
-// X planes of several jobs in one launch (dev_jobs: device array of n_jobs entries)
-int launch_mm_pack_x_grouped(const MmPackJob *dev_jobs, int n_jobs, int K, int G, int max_npad,
-                             uint16_t *bhi, uint16_t *blo, cudaStream_t st);
+// X planes of several jobs in one launch: 8-column block b (< *dev_count <= max_blocks)
+// belongs to job dev_map[b]; all on the device
+int launch_mm_pack_x_mapped(const MmPackJob *dev_jobs, const int *dev_map, const int *dev_count,
+                            int max_blocks, int K, int G, uint16_t *bhi, uint16_t *blo, cudaStream_t st);
 // tiles of one job of M rows and N columns at tile width nt
 int mm_job_tiles(int M, int N, int nt);
 // bf16 elements of one plane for N columns (the b_off step between jobs)

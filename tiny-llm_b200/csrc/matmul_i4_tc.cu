@@ -11,21 +11,24 @@
 //        y = sum_g s_g * P_g,   P_g = sum_{k in g} q_k x_k - z_g X_g,   X_g = sum_{k in g} x_k.
 //    The codes q (0..15) are exact in bf16, so the A operand is the raw nibbles widened
 //    with one LOP3 (0x4300 | q is bf16 128 + q) and one packed bf16 subtract of 128: no
-//    dequantisation arithmetic and no rounding.  X is split into bf16 hi + lo (two MMAs
-//    per K step, the lo residue ~2^-17 of x).  The zero term rides in the same MMA as
-//    one extra K step of 16 slots per group: A = -(z1, z1, z1, z2, z2, z2) (z = z1 + z2
-//    exactly, z is binary16) against B = (X1, X2, X3, X1, X2, X3) (X_g = X1 + X2 + X3,
-//    three bf16 parts of the fp32 group sum), so each group's P_g lands in TMEM whole.
-//  * Epilogue per group: 8 warps read P_g from TMEM (double-buffered accumulators, so the
-//    MMAs of group g+1 overlap the read of group g) and fold y += s_g * P_g in fp32
-//    registers; one FFMA per output and group.
-//  * Roles: warps 0-3 build the A operand (thread = weight row) from nibble words fetched
-//    one group ahead; thread 0 also issues the two 1-D bulk copies (TMA) of the stage's
-//    X planes, which a pre-pass kernel lays out in the MMA's shared-memory order.
-//    Warps 4-11 are the epilogue; warp 12 allocates TMEM and one lane issues the MMAs.
-//    Stages (one quantisation group each) are handed over with mbarriers: full (4
-//    producer warps + the copy bytes), empty (tcgen05.commit), tmem_full (commit) and
-//    tmem_empty (8 epilogue warps).
+//    dequantisation arithmetic and no rounding.  X is split into bf16 hi + lo (the lo
+//    residue ~2^-17 of x), stored as rows [0, nw) and [nw, 2nw) of the B operand, so one
+//    MMA of N = 2nw per K step yields the hi and lo partial sums side by side in TMEM.
+//    The zero term rides in the same MMAs as one extra K step of 16 slots per group:
+//    A = -(z1, z1, z1, z2, z2, z2) (z = z1 + z2 exactly, z is binary16) against
+//    B = (X1, X2, X3, X1, X2, X3) in the hi rows (X_g = X1 + X2 + X3, three bf16 parts of
+//    the fp32 group sum; zeros in the lo rows), so each group's P_g lands in TMEM whole.
+//  * Epilogue per group: 8 warps read P_g's two halves from TMEM (double-buffered
+//    accumulators, so the MMAs of group g+1 overlap the read of group g) and fold
+//    y += s_g * (P_hi + P_lo) in fp32 registers.
+//  * Roles: warps 0-7 build the A operand (thread = weight row of the 256-row tile) from
+//    the weight blocks that warp 17 stages with 1-D bulk copies (TMA) a few groups ahead,
+//    together with the stage's X planes, which a pre-pass kernel lays out in the MMA's
+//    shared-memory order.  Warps 8-15 are the epilogue; warp 16 allocates TMEM and one
+//    lane issues the MMAs.  Stages (one quantisation group each) are handed over with
+//    mbarriers: full (8 producer warps), bfull (copy bytes), empty (tcgen05.commit),
+//    tmem_full (commit) and tmem_empty (8 epilogue warps); rawbar/rawfree for the
+//    weight blocks.
 //  * Operand layout in shared memory: the canonical K-major, no-swizzle UMMA layout of
 //    8-row x 16-byte core matrices, the core matrices of one 8-row group adjacent along
 //    K (leading byte offset 128), 8-row groups (G+16)*16 bytes apart (stride offset).
@@ -171,110 +174,78 @@ __device__ __forceinline__ const MmJob &job_of(const MmParams &P, int j) {
 // g*G + 8*kc + (0,4,1,5,2,6,3,7); chunk G/8 of the hi plane holds the zero-term operand
 // (X1, X2, X3, X1, X2, X3, 0, 0) of the group sum X_g = sum x (fp32, k < K); everything
 // else (columns >= N, k >= K, the lo plane's extra chunks) is zero.
-// One thread per (group, column).
-template <int G>
-__global__ void mm_pack_x_kernel(const float *__restrict__ x, const int *__restrict__ cols, int ldx,
-                                 int K, int N, int npad, int ng, uint16_t *__restrict__ bhi,
-                                 uint16_t *__restrict__ blo) {
-    constexpr int CK = (G + 16) / 8;
-    const long long total = (long long)npad * ng;
-    for (long long c = blockIdx.x * (long long)blockDim.x + threadIdx.x; c < total;
-         c += (long long)gridDim.x * blockDim.x) {
-        const int n = (int)(c % npad);
-        const int g = (int)(c / npad);
-        const size_t base = ((size_t)g * (npad / 8) + n / 8) * CK * 64 + (size_t)(n % 8) * 8;
-        uint4 *dh = reinterpret_cast<uint4 *>(bhi + base);  // chunk kc at dh[kc * 8]
-        uint4 *dl = reinterpret_cast<uint4 *>(blo + base);
-        const float *src = n < N ? x + (size_t)(cols ? cols[n] : n) * ldx : nullptr;
-        float xs = 0.0f;
-#pragma unroll 1
-        for (int kc = 0; kc < G / 8; ++kc) {
-            uint32_t h[4], l[4];
-#pragma unroll
-            for (int p = 0; p < 4; ++p) {
-                float v[2];
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {  // position 2p+e holds column p + 4e
-                    const int k = g * G + 8 * kc + p + 4 * e;
-                    v[e] = (src && k < K) ? src[k] : 0.0f;
-                }
-                const uint16_t h0 = bf16_bits(v[0]), h1 = bf16_bits(v[1]);
-                const uint16_t l0 = bf16_bits(__fsub_rn(v[0], bf16_val(h0)));
-                const uint16_t l1 = bf16_bits(__fsub_rn(v[1], bf16_val(h1)));
-                h[p] = (uint32_t)h0 | ((uint32_t)h1 << 16);
-                l[p] = (uint32_t)l0 | ((uint32_t)l1 << 16);
-            }
-            dh[kc * 8] = make_uint4(h[0], h[1], h[2], h[3]);
-            dl[kc * 8] = make_uint4(l[0], l[1], l[2], l[3]);
-        }
-        if (src) {  // group sum in column order, fp32
-            const int k0 = g * G, k1 = min(K, k0 + G);
-            for (int k = k0; k < k1; ++k) xs = __fadd_rn(xs, src[k]);
-        }
-        const uint16_t x1 = bf16_bits(xs);
-        const float r1 = __fsub_rn(xs, bf16_val(x1));
-        const uint16_t x2 = bf16_bits(r1);
-        const uint16_t x3 = bf16_bits(__fsub_rn(r1, bf16_val(x2)));
-        dh[(G / 8) * 8] = make_uint4((uint32_t)x1 | ((uint32_t)x2 << 16),
-                                     (uint32_t)x3 | ((uint32_t)x1 << 16),
-                                     (uint32_t)x2 | ((uint32_t)x3 << 16), 0u);
-        dh[(G / 8 + 1) * 8] = make_uint4(0u, 0u, 0u, 0u);
-        dl[(G / 8) * 8] = make_uint4(0u, 0u, 0u, 0u);
-        dl[(G / 8 + 1) * 8] = make_uint4(0u, 0u, 0u, 0u);
-    }
-}
+// CTA = one (group, 8-column block) of one job: warp c reads column c's G values
+// (coalesced along K), the block is assembled in shared memory and stored as whole
+// 16-byte words of the two contiguous (G+16)*16-byte regions.
+constexpr int kPackThreads = 256;
 
-// Several jobs' X planes in one launch: blockIdx.y is the job.
+// Grouped form: the 8-column blocks of all jobs are numbered together (job j's first
+// block is col0/8), map[b] is the job of block b and *count the blocks in use.
 template <int G>
-__global__ void mm_pack_x_grouped_kernel(const MmPackJob *__restrict__ jobs, int K, int ng,
-                                         uint16_t *__restrict__ bhi, uint16_t *__restrict__ blo) {
+__global__ void __launch_bounds__(kPackThreads) mm_pack_x_kernel(const MmPackJob job0,
+                                                                 const MmPackJob *__restrict__ jobs,
+                                                                 const int *__restrict__ map,
+                                                                 const int *__restrict__ count,
+                                                                 int K, int ng, int nb_grid,
+                                                                 uint16_t *__restrict__ bhi,
+                                                                 uint16_t *__restrict__ blo) {
     constexpr int CK = (G + 16) / 8;
-    const MmPackJob jb = jobs[blockIdx.y];
+    constexpr int PER = G / 32;  // values per lane
+    __shared__ __align__(16) uint16_t th[CK * 64], tl[CK * 64];
+    const int g = blockIdx.x / nb_grid, gb = blockIdx.x % nb_grid;
+    MmPackJob jb;
+    int nb;
+    if (map) {
+        if (gb >= *count) return;  // uniform
+        jb = jobs[map[gb]];
+        nb = gb - jb.col0 / 8;
+    } else {
+        jb = job0;
+        nb = gb;
+    }
     const int npad = (jb.N + 15) & ~15;
-    const long long total = (long long)npad * ng;
-    for (long long c = blockIdx.x * (long long)blockDim.x + threadIdx.x; c < total;
-         c += (long long)gridDim.x * blockDim.x) {
-        const int n = (int)(c % npad);
-        const int g = (int)(c / npad);
-        const size_t base = (size_t)jb.b_off + ((size_t)g * (npad / 8) + n / 8) * CK * 64 + (size_t)(n % 8) * 8;
-        uint4 *dh = reinterpret_cast<uint4 *>(bhi + base);
-        uint4 *dl = reinterpret_cast<uint4 *>(blo + base);
-        const float *src = n < jb.N ? jb.x + (size_t)(jb.cols ? jb.cols[n] : n) * jb.ldx : nullptr;
-        float xs = 0.0f;
-#pragma unroll 1
-        for (int kc = 0; kc < G / 8; ++kc) {
-            uint32_t h[4], l[4];
+    if (nb >= npad / 8) return;  // uniform
+    const int t = threadIdx.x, c = t >> 5, lane = t & 31;
+    const int n = nb * 8 + c;
+    const float *src = n < jb.N ? jb.x + (size_t)(jb.cols ? jb.cols[n] : n) * jb.ldx : nullptr;
+    float v[PER];
 #pragma unroll
-            for (int p = 0; p < 4; ++p) {
-                float v[2];
+    for (int i = 0; i < PER; ++i) {
+        const int k = g * G + lane * PER + i;
+        v[i] = (src && k < K) ? src[k] : 0.0f;
+    }
+    float xs = 0.0f;
 #pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const int k = g * G + 8 * kc + p + 4 * e;
-                    v[e] = (src && k < K) ? src[k] : 0.0f;
-                }
-                const uint16_t h0 = bf16_bits(v[0]), h1 = bf16_bits(v[1]);
-                const uint16_t l0 = bf16_bits(__fsub_rn(v[0], bf16_val(h0)));
-                const uint16_t l1 = bf16_bits(__fsub_rn(v[1], bf16_val(h1)));
-                h[p] = (uint32_t)h0 | ((uint32_t)h1 << 16);
-                l[p] = (uint32_t)l0 | ((uint32_t)l1 << 16);
-            }
-            dh[kc * 8] = make_uint4(h[0], h[1], h[2], h[3]);
-            dl[kc * 8] = make_uint4(l[0], l[1], l[2], l[3]);
+    for (int i = 0; i < PER; ++i) {
+        const int kl = lane * PER + i, r = kl & 7;
+        const int o = (kl >> 3) * 64 + c * 8 + 2 * (r & 3) + (r >> 2);
+        const uint16_t h = bf16_bits(v[i]);
+        th[o] = h;
+        tl[o] = bf16_bits(__fsub_rn(v[i], bf16_val(h)));
+        xs = __fadd_rn(xs, v[i]);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) xs = __fadd_rn(xs, __shfl_xor_sync(0xffffffffu, xs, off));
+    if (lane < 16) {  // the two extra chunks of column c: zero term in hi, zeros elsewhere
+        const int o = (G / 8) * 64 + (lane >> 3) * 64 + c * 8 + (lane & 7);
+        uint16_t hv = 0;
+        if (lane < 6) {
+            const uint16_t x1 = bf16_bits(xs);
+            const float r1 = __fsub_rn(xs, bf16_val(x1));
+            const uint16_t x2 = bf16_bits(r1);
+            const uint16_t x3 = bf16_bits(__fsub_rn(r1, bf16_val(x2)));
+            const int m = lane % 3;
+            hv = m == 0 ? x1 : (m == 1 ? x2 : x3);
         }
-        if (src) {
-            const int k0 = g * G, k1 = min(K, k0 + G);
-            for (int k = k0; k < k1; ++k) xs = __fadd_rn(xs, src[k]);
-        }
-        const uint16_t x1 = bf16_bits(xs);
-        const float r1 = __fsub_rn(xs, bf16_val(x1));
-        const uint16_t x2 = bf16_bits(r1);
-        const uint16_t x3 = bf16_bits(__fsub_rn(r1, bf16_val(x2)));
-        dh[(G / 8) * 8] = make_uint4((uint32_t)x1 | ((uint32_t)x2 << 16),
-                                     (uint32_t)x3 | ((uint32_t)x1 << 16),
-                                     (uint32_t)x2 | ((uint32_t)x3 << 16), 0u);
-        dh[(G / 8 + 1) * 8] = make_uint4(0u, 0u, 0u, 0u);
-        dl[(G / 8) * 8] = make_uint4(0u, 0u, 0u, 0u);
-        dl[(G / 8 + 1) * 8] = make_uint4(0u, 0u, 0u, 0u);
+        th[o] = hv;
+        tl[o] = 0;
+    }
+    __syncthreads();
+    const size_t base = (size_t)jb.b_off + ((size_t)g * (npad / 8) + nb) * CK * 64;
+    for (int i = t; i < 2 * CK * 8; i += kPackThreads) {
+        const int pl = i / (CK * 8), w = i % (CK * 8);
+        const uint4 val = reinterpret_cast<const uint4 *>(pl ? tl : th)[w];
+        reinterpret_cast<uint4 *>((pl ? blo : bhi) + base)[w] = val;
     }
 }
 
@@ -437,7 +408,9 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
         const int quarter = warp & 3;  // TMEM lanes this warp may access
         const int rl = 128 * half + 32 * quarter + lane;  // row within the tile
         const int row = m0 + rl;
-        const uint32_t lane_addr = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(half * P.nt);
+        // accumulator (buffer b, half h) = TMEM columns [(2b + h) * 2nt, +2nw): P of the
+        // hi plane in the first nw columns, of the lo plane in the next nw
+        const uint32_t lane_addr = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(half * 2 * P.nt);
         float y[kMmMaxCols];
 #pragma unroll
         for (int c = 0; c < kMmMaxCols; ++c) y[c] = 0.0f;
@@ -449,17 +422,17 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
             }
             tc_fence_after();
             const float sc = scl[(i % kSclRing) * kTileRows + rl];
-            const uint32_t ta = lane_addr + (uint32_t)(b * 2 * P.nt);
+            const uint32_t ta = lane_addr + (uint32_t)(b * 4 * P.nt);
 #pragma unroll
-            for (int h = 0; h < kMmMaxCols / 16; ++h) {  // 16 columns at a time
-                float v[16];
+            for (int h = 0; h < kMmMaxCols / 8; ++h) {  // 8 columns (hi and lo) at a time
+                if (h * 8 < nw) {
+                    float v[8], u[8];
+                    tmem_ld8(ta + (uint32_t)(h * 8), v);
+                    tmem_ld8(ta + (uint32_t)(nw + h * 8), u);
+                    tmem_wait_ld();
 #pragma unroll
-                for (int c = 0; c < 2; ++c)
-                    if (h * 16 + c * 8 < nw) tmem_ld8(ta + (uint32_t)(h * 16 + c * 8), v + c * 8);
-                tmem_wait_ld();
-#pragma unroll
-                for (int c = 0; c < 16; ++c)
-                    if (h * 16 + c < nw) y[h * 16 + c] = fmaf(sc, v[c], y[h * 16 + c]);
+                    for (int c = 0; c < 8; ++c) y[h * 8 + c] = fmaf(sc, v[c] + u[c], y[h * 8 + c]);
+                }
             }
             tc_fence_before();
             __syncwarp();
@@ -480,9 +453,10 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
     } else if (warp == kMmaWarp) {
         if (lane == 0) {
             // ---------------- MMA issuer: per group, for each row half, G/16 K steps of
-            // (codes x X hi) + (codes x X lo), then the zero term
+            // codes x [X hi | X lo] (one MMA of N = 2nw: the lo plane's rows follow the hi
+            // plane's in shared memory with the same 8-row stride), then the zero term
             bool ok = true;
-            const uint32_t idesc = umma_idesc_bf16(nw);
+            const uint32_t idesc = umma_idesc_bf16(2 * nw);
             for (int i = 0; i < ng && ok; ++i) {
                 const int s = i % S, b = i & 1;
                 ok = mbar_wait_sleep(&full[s], (uint32_t)(i / S) & 1u, kWaitCycles);
@@ -491,17 +465,16 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t a0 = smem_u32(stage_base + (size_t)s * stage_bytes);
-                const uint32_t bh = a0 + kA, bl = bh + b_bytes;
+                const uint32_t bh = a0 + kA;  // hi rows [0, nw), lo rows [nw, 2nw)
 #pragma unroll
                 for (int hf = 0; hf < 2; ++hf) {
                     const uint32_t a = a0 + (uint32_t)hf * kAh;
-                    const uint32_t dd = tmem + (uint32_t)((b * 2 + hf) * P.nt);
+                    const uint32_t dd = tmem + (uint32_t)((b * 2 + hf) * 2 * P.nt);
 #pragma unroll
                     for (int kk = 0; kk < G / 16; ++kk) {
                         const uint32_t o = (uint32_t)kk * 256u;  // two 16-byte core-matrix columns
-                        const uint64_t ad = umma_desc(a + o, 128, SBO);
-                        umma_bf16(dd, ad, umma_desc(bh + o, 128, SBO), idesc, kk > 0 ? 1u : 0u);
-                        umma_bf16(dd, ad, umma_desc(bl + o, 128, SBO), idesc, 1u);
+                        umma_bf16(dd, umma_desc(a + o, 128, SBO), umma_desc(bh + o, 128, SBO), idesc,
+                                  kk > 0 ? 1u : 0u);
                     }
                     const uint32_t oz = (uint32_t)(G / 16) * 256u;  // zero term
                     umma_bf16(dd, umma_desc(a + oz, 128, SBO), umma_desc(bh + oz, 128, SBO), idesc, 1u);
@@ -634,16 +607,25 @@ size_t mm_scratch_bytes(int M, int K, int N, int G) {
     return a + mm_x_planes_bytes(K, N, G);
 }
 
-// Widest column tile (fewest re-reads of a weight tile) that still gives every SM a CTA;
-// the widest that covers the columns when nothing fills the SMs.
+// Column tile width by a cost model: a CTA's time per group is about (64 + nt) units (the
+// A operand's shared-memory reads cost as much as 64 columns of B), and the launch takes
+// as many such CTA times as it has waves over the SMs.  Ties go to the wider tile.
 int mm_tile_width(int M, int N) {
     const int npad = (N + 15) & ~15;
     const int mt = (M + kTileRows - 1) / kTileRows;
     const int widest = std::min(npad, kMmMaxCols);
     const int sms = num_sms();
-    for (int nt = widest; nt >= 16; nt = (nt / 2 + 15) & ~15)
-        if (mt * ((npad + nt - 1) / nt) >= sms || nt == 16) return nt;
-    return widest;
+    int best = widest;
+    long long best_cost = -1;
+    for (int nt = widest; nt >= 16; nt -= 16) {
+        const long long tiles = (long long)mt * ((npad + nt - 1) / nt);
+        const long long cost = ((tiles + sms - 1) / sms) * (64 + nt);
+        if (best_cost < 0 || cost < best_cost) {
+            best = nt;
+            best_cost = cost;
+        }
+    }
+    return best;
 }
 
 int launch_matmul_i4_grouped(const MmJob *host_jobs, const MmJob *dev_jobs, int n_jobs, int K,
@@ -664,7 +646,7 @@ int launch_matmul_i4_grouped(const MmJob *host_jobs, const MmJob *dev_jobs, int 
     P.bhi = bhi;
     P.blo = blo;
     uint32_t cols = 32;
-    while ((int)cols < 4 * nt) cols <<= 1;
+    while ((int)cols < 8 * nt) cols <<= 1;
     P.tmem_cols = cols;
     P.status = status;
     if (G == 32) return launch_grouped_g<32>(P, total_tiles, st, 0);
@@ -691,7 +673,7 @@ int launch_matmul_i4_planned(const MmJob *dev_jobs, const int *dev_tile_job, con
     P.bhi = bhi;
     P.blo = blo;
     uint32_t cols = 32;
-    while ((int)cols < 4 * nt) cols <<= 1;
+    while ((int)cols < 8 * nt) cols <<= 1;
     P.tmem_cols = cols;
     P.status = status;
     if (G == 32) return launch_grouped_g<32>(P, max_tiles, st, 0);
@@ -699,23 +681,33 @@ int launch_matmul_i4_planned(const MmJob *dev_jobs, const int *dev_tile_job, con
     return launch_grouped_g<128>(P, max_tiles, st, 2);
 }
 
-int launch_mm_pack_x(const float *x, const int *cols, int ldx, int K, int N, int G, uint16_t *bhi,
-                     uint16_t *blo, cudaStream_t st) {
+int launch_pack(const MmPackJob &job0, const MmPackJob *jobs, const int *map, const int *count,
+                int K, int G, int nb_grid, uint16_t *bhi, uint16_t *blo, cudaStream_t st) {
     TQ_CHECK_ARG(mm_group_supported(G), "matmul_i4: group_size %d not 32, 64 or 128", G);
-    const int npad = (N + 15) & ~15;
+    if (nb_grid <= 0) return TQB200_OK;
     const int ng = (K + G - 1) / G;
-    const long long total = (long long)npad * ng;
-    if (total == 0) return TQB200_OK;
-    const int threads = 128;
-    const int blocks = (int)std::min<long long>((total + threads - 1) / threads, 148LL * 32);
+    const long long bx = (long long)ng * nb_grid;
+    TQ_CHECK_ARG(bx < (1LL << 31), "matmul_i4: X pack grid %lld", bx);
     if (G == 32)
-        mm_pack_x_kernel<32><<<blocks, threads, 0, st>>>(x, cols, ldx, K, N, npad, ng, bhi, blo);
+        mm_pack_x_kernel<32><<<(unsigned)bx, kPackThreads, 0, st>>>(job0, jobs, map, count, K, ng, nb_grid, bhi, blo);
     else if (G == 64)
-        mm_pack_x_kernel<64><<<blocks, threads, 0, st>>>(x, cols, ldx, K, N, npad, ng, bhi, blo);
+        mm_pack_x_kernel<64><<<(unsigned)bx, kPackThreads, 0, st>>>(job0, jobs, map, count, K, ng, nb_grid, bhi, blo);
     else
-        mm_pack_x_kernel<128><<<blocks, threads, 0, st>>>(x, cols, ldx, K, N, npad, ng, bhi, blo);
+        mm_pack_x_kernel<128><<<(unsigned)bx, kPackThreads, 0, st>>>(job0, jobs, map, count, K, ng, nb_grid, bhi, blo);
     TQ_CUDA_TRY(cudaGetLastError());
     return TQB200_OK;
+}
+
+int launch_mm_pack_x(const float *x, const int *cols, int ldx, int K, int N, int G, uint16_t *bhi,
+                     uint16_t *blo, cudaStream_t st) {
+    MmPackJob j{};
+    j.x = x;
+    j.cols = cols;
+    j.ldx = ldx;
+    j.N = N;
+    j.b_off = 0;
+    j.col0 = 0;
+    return launch_pack(j, nullptr, nullptr, nullptr, K, G, ((N + 15) & ~15) / 8, bhi, blo, st);
 }
 
 int mm_job_tiles(int M, int N, int nt) {
@@ -729,20 +721,10 @@ long long mm_plane_elems(int K, int N, int G) {
     return ng * (G + 16) * npad;
 }
 
-int launch_mm_pack_x_grouped(const MmPackJob *dev_jobs, int n_jobs, int K, int G, int max_npad,
-                             uint16_t *bhi, uint16_t *blo, cudaStream_t st) {
-    TQ_CHECK_ARG(mm_group_supported(G), "matmul_i4: group_size %d not 32, 64 or 128", G);
-    if (n_jobs <= 0 || max_npad <= 0) return TQB200_OK;
-    const int ng = (K + G - 1) / G;
-    const int threads = 128;
-    const long long per_job = (long long)max_npad * ng;
-    const int bx = (int)std::max<long long>(1, std::min<long long>((per_job + threads - 1) / threads, 64));
-    dim3 grid(bx, n_jobs);
-    if (G == 32) mm_pack_x_grouped_kernel<32><<<grid, threads, 0, st>>>(dev_jobs, K, ng, bhi, blo);
-    else if (G == 64) mm_pack_x_grouped_kernel<64><<<grid, threads, 0, st>>>(dev_jobs, K, ng, bhi, blo);
-    else mm_pack_x_grouped_kernel<128><<<grid, threads, 0, st>>>(dev_jobs, K, ng, bhi, blo);
-    TQ_CUDA_TRY(cudaGetLastError());
-    return TQB200_OK;
+int launch_mm_pack_x_mapped(const MmPackJob *dev_jobs, const int *dev_map, const int *dev_count,
+                            int max_blocks, int K, int G, uint16_t *bhi, uint16_t *blo, cudaStream_t st) {
+    TQ_CHECK_ARG(dev_jobs && dev_map && dev_count, "matmul_i4: mapped X pack needs its map");
+    return launch_pack(MmPackJob{}, dev_jobs, dev_map, dev_count, K, G, max_blocks, bhi, blo, st);
 }
 
 // Y = W X for one matrix.  scratch (mm_scratch_bytes(M, K, N, G)) receives the

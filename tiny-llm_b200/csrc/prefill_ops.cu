@@ -45,12 +45,12 @@ __device__ __forceinline__ float4 ld4(const uint16_t *p) {
 }
 
 template <typename KV, int HD>
-__global__ void __launch_bounds__(kApThreads, 2)
-attn_prefill_kernel(const float *__restrict__ q, const KV *__restrict__ kc, const KV *__restrict__ vc,
-                    int p0, int n, int H, int KVH, int max_seq, float scale, float *__restrict__ out) {
+__device__ __forceinline__ void attn_block(const float *__restrict__ q, const KV *__restrict__ kc,
+                                           const KV *__restrict__ vc, int p0, int n, int H, int KVH,
+                                           int max_seq, float scale, float *__restrict__ out, int qb,
+                                           float *sm) {
     constexpr int LD = ApSmem<HD>::LD;
     constexpr int NU = HD / 64;  // float4 column blocks per thread in P.V
-    extern __shared__ __align__(16) float sm[];
     float *Qs = sm;                          // [kApRows][LD]
     float *Ks = Qs + kApRows * LD;           // [kApKeys][LD]
     float *Vs = Ks + kApKeys * LD;           // [kApKeys][LD]
@@ -59,7 +59,7 @@ attn_prefill_kernel(const float *__restrict__ q, const KV *__restrict__ kc, cons
     const int g = H / KVH;
     const int tq = kApRows / g;              // tokens per CTA
     const int kh = blockIdx.y;
-    const int t0 = blockIdx.x * tq;
+    const int t0 = qb * tq;
     const int rows = min(tq, n - t0) * g;    // live rows; row r = token t0 + r/g, head kh*g + r%g
     const size_t qld = (size_t)H * HD;
     for (int i = tid; i < kApRows * (HD / 4); i += kApThreads) {
@@ -171,6 +171,21 @@ attn_prefill_kernel(const float *__restrict__ q, const KV *__restrict__ kc, cons
     }
 }
 
+// Causal work grows with the token index, so CTA j takes query blocks j and nb-1-j.
+template <typename KV, int HD>
+__global__ void __launch_bounds__(kApThreads, 2)
+attn_prefill_kernel(const float *__restrict__ q, const KV *__restrict__ kc, const KV *__restrict__ vc,
+                    int p0, int n, int H, int KVH, int max_seq, float scale, float *__restrict__ out) {
+    extern __shared__ __align__(16) float sm[];
+    const int nb = (n + kApRows / (H / KVH) - 1) / (kApRows / (H / KVH));
+    const int j = blockIdx.x;
+    attn_block<KV, HD>(q, kc, vc, p0, n, H, KVH, max_seq, scale, out, j, sm);
+    if (nb - 1 - j != j) {
+        __syncthreads();  // the first block's shared-memory reads are done
+        attn_block<KV, HD>(q, kc, vc, p0, n, H, KVH, max_seq, scale, out, nb - 1 - j, sm);
+    }
+}
+
 template <typename KV, int HD>
 int launch_ap(const AttnPrefillArgs &a, cudaStream_t st) {
     const size_t smem = ApSmem<HD>::bytes;
@@ -180,7 +195,8 @@ int launch_ap(const AttnPrefillArgs &a, cudaStream_t st) {
     TQ_CHECK_ARG((int)smem <= limit, "attention prefill: %zu B shared memory", smem);
     const int g = a.n_heads / a.n_kv_heads;
     const int tq = kApRows / g;
-    const dim3 grid((a.n + tq - 1) / tq, a.n_kv_heads);
+    const int nb = (a.n + tq - 1) / tq;
+    const dim3 grid((nb + 1) / 2, a.n_kv_heads);
     attn_prefill_kernel<KV, HD><<<grid, kApThreads, smem, st>>>(
         a.q, (const KV *)a.k, (const KV *)a.v, a.p0, a.n, a.n_heads, a.n_kv_heads, a.max_seq,
         a.scale, a.out);
@@ -195,19 +211,66 @@ int launch_ap(const AttnPrefillArgs &a, cudaStream_t st) {
 // grouped GEMM jobs (gate and up per expert with tokens, then down), their X-pack jobs
 // and the tile -> job maps, all on the device, so a MoE layer needs no host round trip.
 constexpr int kPlanThreads = 1024;
+constexpr int kPlanWarps = kPlanThreads / 32;
 
-__global__ void __launch_bounds__(kPlanThreads) moe_plan_kernel(const MoePlanArgs a) {
-    extern __shared__ int s_idx[];  // [A]
-    __shared__ int s_cnt[kMoePlanMaxExperts];
-    __shared__ int s_off[kMoePlanMaxExperts];
-    __shared__ int s_npre[kMoePlanMaxExperts];   // padded columns before expert e
-    __shared__ int s_tgu[kMoePlanMaxExperts];    // first gate/up tile of expert e
-    __shared__ int s_tdn[kMoePlanMaxExperts];    // first down tile of expert e
-    __shared__ int s_job[kMoePlanMaxExperts];    // compacted index of expert e (-1: no tokens)
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int A = a.n * a.k, E = a.E;
-    for (int e = tid; e < E; e += kPlanThreads) s_cnt[e] = 0;
+// Exclusive prefix sums over e < E (E <= kPlanThreads) of four per-expert values, by
+// every thread of the CTA (thread e holds expert e's values).
+__device__ void plan_scan4(int v[4], int tot[4], int (*wt)[4]) {
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    int inc[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        inc[q] = v[q];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int u = __shfl_up_sync(0xffffffffu, inc[q], o);
+            if (lane >= o) inc[q] += u;
+        }
+    }
+    if (lane == 31)
+        for (int q = 0; q < 4; ++q) wt[warp][q] = inc[q];
     __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            int x = wt[lane][q];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int u = __shfl_up_sync(0xffffffffu, x, o);
+                if (lane >= o) x += u;
+            }
+            wt[lane][q] = x;  // inclusive over warps
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const int before = warp ? wt[warp - 1][q] : 0;
+        const int excl = before + inc[q] - v[q];
+        tot[q] = wt[kPlanWarps - 1][q];
+        v[q] = excl;
+    }
+    __syncthreads();  // wt reusable
+}
+
+// One CTA.  The n*k assignments (token t, choice j) -> expert idx[t*k+j] are bucketed by
+// expert, in assignment order inside a bucket; bucket row `row` holds token rows[row],
+// and assignment a sits at bucket row slot[a].  From the bucket sizes it writes the
+// grouped GEMM jobs (gate and up per expert with tokens, then down), their X-pack jobs
+// and the tile -> job maps, all on the device, so a MoE layer needs no host round trip.
+// Ranking: warp w takes a contiguous slice of the assignments and ranks each within
+// (slice, expert) with __match_any_sync 32 at a time; a per-expert scan over the slices
+// then places every slice's run after the previous slices' runs.
+__global__ void __launch_bounds__(kPlanThreads) moe_plan_kernel(const MoePlanArgs a) {
+    extern __shared__ int sm_plan[];
+    const int A = a.n * a.k, E = a.E;
+    int *s_idx = sm_plan;            // [A] expert of assignment
+    int *s_rank = s_idx + A;         // [A] rank inside (slice, expert)
+    int *s_wc = s_rank + A;          // [kPlanWarps][E] slice counts, then slice offsets
+    __shared__ int s_off[kMoePlanMaxExperts], s_npre[kMoePlanMaxExperts];
+    __shared__ int s_tgu[kMoePlanMaxExperts], s_tdn[kMoePlanMaxExperts], s_job[kMoePlanMaxExperts];
+    __shared__ int s_wt[kPlanWarps][4];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     for (int i = tid; i < A; i += kPlanThreads) {
         int e = a.idx[i];
         if (e < 0 || e >= E) {  // cannot come from the top-k kernel; keep the plan in bounds
@@ -215,57 +278,93 @@ __global__ void __launch_bounds__(kPlanThreads) moe_plan_kernel(const MoePlanArg
             e = 0;
         }
         s_idx[i] = e;
-        atomicAdd(&s_cnt[e], 1);
+    }
+    for (int i = tid; i < kPlanWarps * E; i += kPlanThreads) s_wc[i] = 0;
+    __syncthreads();
+    const int S = (((A + kPlanWarps - 1) / kPlanWarps) + 31) & ~31;  // slice length
+    {
+        int *wc = s_wc + warp * E;
+        const int i1 = min(A, (warp + 1) * S);
+        for (int a0 = warp * S; a0 < i1; a0 += 32) {
+            const int i = a0 + lane;
+            const int e = i < i1 ? s_idx[i] : -1 - lane;  // idle lanes: keys of their own
+            const unsigned peers = __match_any_sync(0xffffffffu, e);
+            const int leader = __ffs(peers) - 1;
+            int base = 0;
+            if (lane == leader && i < i1) {
+                base = wc[e];
+                wc[e] = base + __popc(peers);
+            }
+            base = __shfl_sync(0xffffffffu, base, leader);
+            if (i < i1) s_rank[i] = base + __popc(peers & ((1u << lane) - 1u));
+            __syncwarp();
+        }
     }
     __syncthreads();
+    int v[4] = {0, 0, 0, 0}, tot[4];
     const int mt_gu = (a.mi + kMmTileRows - 1) / kMmTileRows;
     const int mt_dn = (a.H + kMmTileRows - 1) / kMmTileRows;
-    if (tid == 0) {
-        int off = 0, npre = 0, tgu = 0, tdn = 0, nj = 0;
-        for (int e = 0; e < E; ++e) {
-            const int c = s_cnt[e], npad = (c + 15) & ~15, ct = (npad + a.nt - 1) / a.nt;
-            s_off[e] = off;
-            s_npre[e] = npre;
-            s_tgu[e] = tgu;
-            s_tdn[e] = tdn;
-            s_job[e] = c > 0 ? nj++ : -1;
-            off += c;
-            npre += npad;
-            tgu += 2 * mt_gu * ct;
-            tdn += mt_dn * ct;
+    int c = 0;
+    if (tid < E) {  // slice offsets inside the bucket, and the bucket size
+        for (int w = 0; w < kPlanWarps; ++w) {
+            const int x = s_wc[w * E + tid];
+            s_wc[w * E + tid] = c;
+            c += x;
         }
-        a.ntiles[0] = tgu;
-        a.ntiles[1] = tdn;
+        const int npad = (c + 15) & ~15, ct = (npad + a.nt - 1) / a.nt;
+        v[0] = c;
+        v[1] = npad;
+        v[2] = 2 * mt_gu * ct;
+        v[3] = mt_dn * ct;
+    }
+    plan_scan4(v, tot, s_wt);
+    int jv[4] = {tid < E && c > 0 ? 1 : 0, 0, 0, 0}, jt[4];
+    plan_scan4(jv, jt, s_wt);
+    if (tid < E) {
+        s_off[tid] = v[0];
+        s_npre[tid] = v[1];
+        s_tgu[tid] = v[2];
+        s_tdn[tid] = v[3];
+        s_job[tid] = c > 0 ? jv[0] : -1;
+    }
+    if (tid == 0) {
+        a.ntiles[0] = tot[2];
+        a.ntiles[1] = tot[3];
+        a.ntiles[2] = tot[1] / 8;
     }
     __syncthreads();
     const long long cs_gu = (long long)((a.H + a.G - 1) / a.G) * (a.G + 16);   // plane elems per column
     const long long cs_dn = (long long)((a.mi + a.G - 1) / a.G) * (a.G + 16);
     for (int e = tid; e < E; e += kPlanThreads) {
-        const int c = s_cnt[e], off = s_off[e];
+        const int off = s_off[e];
+        const int cnt = (e + 1 < E ? s_off[e + 1] : tot[0]) - off;
         const long long bgu = cs_gu * s_npre[e], bdn = cs_dn * s_npre[e];
         MmPackJob pg;
         pg.x = a.xn;
         pg.cols = a.rows + off;
         pg.ldx = a.H;
-        pg.N = c;
+        pg.N = cnt;
         pg.b_off = bgu;
+        pg.col0 = s_npre[e];
         a.pack_gu[e] = pg;
         MmPackJob pd;
         pd.x = a.act + (size_t)off * a.mi;
         pd.cols = nullptr;
         pd.ldx = a.mi;
-        pd.N = c;
+        pd.N = cnt;
         pd.b_off = bdn;
+        pd.col0 = s_npre[e];
         a.pack_dn[e] = pd;
+        for (int b = 0; b < ((cnt + 15) & ~15) / 8; ++b) a.pack_map[s_npre[e] / 8 + b] = e;
         const int jx = s_job[e];
         if (jx < 0) continue;
-        const int ct = (((c + 15) & ~15) + a.nt - 1) / a.nt;
+        const int ct = (((cnt + 15) & ~15) + a.nt - 1) / a.nt;
         for (int h = 0; h < 2; ++h) {
             MmJob j;
             j.w = (h ? a.wu : a.wg) + (size_t)e * a.wgu_stride;
             j.y = (h ? a.ubuf : a.hbuf) + (size_t)off * a.mi;
             j.M = a.mi;
-            j.N = c;
+            j.N = cnt;
             j.ldy = a.mi;
             j.tile_begin = s_tgu[e] + h * mt_gu * ct;
             j.b_off = bgu;
@@ -278,7 +377,7 @@ __global__ void __launch_bounds__(kPlanThreads) moe_plan_kernel(const MoePlanArg
         j.w = a.wd + (size_t)e * a.wd_stride;
         j.y = a.obuf + (size_t)off * a.H;
         j.M = a.H;
-        j.N = c;
+        j.N = cnt;
         j.ldy = a.H;
         j.tile_begin = s_tdn[e];
         j.b_off = bdn;
@@ -287,20 +386,11 @@ __global__ void __launch_bounds__(kPlanThreads) moe_plan_kernel(const MoePlanArg
         a.jobs_dn[jx] = j;
         for (int i = 0; i < mt_dn * ct; ++i) a.tile_dn[j.tile_begin + i] = jx;
     }
-    // stable scatter: a warp per expert, assignments in order, ranks by ballot
-    for (int e = warp; e < E; e += kPlanThreads / 32) {
-        int run = s_off[e];
-        for (int a0 = 0; a0 < A; a0 += 32) {
-            const int i = a0 + lane;
-            const bool hit = i < A && s_idx[i] == e;
-            const unsigned mask = __ballot_sync(0xffffffffu, hit);
-            if (hit) {
-                const int row = run + __popc(mask & ((1u << lane) - 1u));
-                a.rows[row] = i / a.k;
-                a.slot[i] = row;
-            }
-            run += __popc(mask);
-        }
+    for (int i = tid; i < A; i += kPlanThreads) {  // bucket row of every assignment
+        const int e = s_idx[i], w = i / S;
+        const int row = s_off[e] + s_wc[w * E + e] + s_rank[i];
+        a.rows[row] = i / a.k;
+        a.slot[i] = row;
     }
 }
 
@@ -328,6 +418,15 @@ bool attn_prefill_supported(int n_heads, int n_kv_heads, int head_dim) {
     return (head_dim == 64 || head_dim == 128) && g <= kApRows && kApRows % g == 0;
 }
 
+size_t moe_plan_smem_bytes(int n, int k, int E) {
+    return (size_t)n * k * 8 + (size_t)kPlanWarps * E * 4;
+}
+
+int moe_plan_max_cols(int n, int k, int E) {
+    const long long A = (long long)n * k, live = std::min<long long>(E, A);
+    return (int)(A + 15 * live);
+}
+
 int moe_plan_max_tiles(int n, int k, int E, int M, int nt) {
     const long long A = (long long)n * k, live = std::min<long long>(E, A);
     const long long cols = A + 15 * live;  // padded columns over all experts
@@ -343,8 +442,8 @@ long long moe_plan_plane_elems(int n, int k, int E, int K, int G) {
 int launch_moe_plan(const MoePlanArgs &a, cudaStream_t st) {
     TQ_CHECK_ARG(a.E > 0 && a.E <= kMoePlanMaxExperts && a.k > 0 && a.n > 0,
                  "moe plan: E %d k %d n %d", a.E, a.k, a.n);
-    const size_t smem = (size_t)a.n * a.k * 4;
-    TQ_CHECK_ARG(smem <= 96 * 1024, "moe plan: %d assignments", a.n * a.k);
+    const size_t smem = moe_plan_smem_bytes(a.n, a.k, a.E);
+    TQ_CHECK_ARG(smem <= kMoePlanMaxSmem, "moe plan: %d assignments over %d experts", a.n * a.k, a.E);
     static KernelSmem once;
     int limit = 0;
     TQ_CUDA_TRY(smem_limit_once(moe_plan_kernel, once, &limit));
