@@ -661,8 +661,8 @@ def bench_prefill(args, rank, pg, pk, pk_kind):
     peak = pk.get("bf16_tflops", 1590.0)
     L = spec.n_layers
     # embed; per MoE layer rmsnorm, pack, qkv, rope+kv, attention, pack, o_proj, rmsnorm,
-    # router, top-k, plan, pack, gate/up, swiglu, pack, down, combine; lm_head
-    launches = 1 + 17 * L + 1
+    # router, top-k, plan, pack, gate/up, pack (+SwiGLU), down, combine; lm_head
+    launches = 1 + 16 * L + 1
     out = {
         "metric": "prefill ms per 512-token prompt, batch 1 (BASELINE config 5: Qwen3-30B-A3B-"
                   "shaped MoE, i4 g64 experts, top-8 of 128, fp32 KV)",

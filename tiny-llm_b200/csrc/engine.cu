@@ -77,7 +77,7 @@ struct Prefill {
     int cap = 0;
     std::vector<PLayer> layers;
     float *hidden = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr,
-          *attn = nullptr, *gate = nullptr, *up = nullptr, *act = nullptr;
+          *attn = nullptr, *gate = nullptr, *up = nullptr;
     int *io = nullptr;  // device [p0, tokens...]
     uint16_t *bhi = nullptr, *blo = nullptr;
     // host-planned jobs of the current chunk size (7 per layer), on the device
@@ -86,8 +86,7 @@ struct Prefill {
     int jobs_n = -1;
     std::vector<int> nt, tiles;  // per job launch: tile width and CTAs (4 launches per layer)
     // MoE
-    float *logits = nullptr, *wts = nullptr, *mh = nullptr, *mu = nullptr, *mact = nullptr,
-          *mo = nullptr;
+    float *logits = nullptr, *wts = nullptr, *mh = nullptr, *mu = nullptr, *mo = nullptr;
     int *idx = nullptr, *rows = nullptr, *slot = nullptr, *ntiles = nullptr;
     int *tile_gu = nullptr, *tile_dn = nullptr, *pack_map = nullptr;
     MmJob *jobs_gu = nullptr, *jobs_dn = nullptr;
@@ -936,7 +935,7 @@ int prefill_setup(tqb200_engine *e) {
         }
     }
     const int I = moe ? 0 : d.inter;
-    const size_t f = (size_t)cap * (2 * (size_t)H + 2 * (size_t)qd + 2 * (size_t)kvd + 3 * (size_t)I);
+    const size_t f = (size_t)cap * (2 * (size_t)H + 2 * (size_t)qd + 2 * (size_t)kvd + 2 * (size_t)I);
     void *p;
     TQ_TRY(dev_alloc(e, f * 4 + 16 * 64, &p));
     float *a = (float *)p;
@@ -954,7 +953,6 @@ int prefill_setup(tqb200_engine *e) {
     if (I) {
         P.gate = take((size_t)cap * I);
         P.up = take((size_t)cap * I);
-        P.act = take((size_t)cap * I);
     }
     TQ_TRY(dev_alloc(e, (size_t)(cap + 16) * 4, &p));
     P.io = (int *)p;
@@ -966,7 +964,7 @@ int prefill_setup(tqb200_engine *e) {
         const size_t A = (size_t)cap * k;
         P.max_tiles_gu = 2 * moe_plan_max_tiles(cap, k, E, mi, P.moe_nt);
         P.max_tiles_dn = moe_plan_max_tiles(cap, k, E, H, P.moe_nt);
-        const size_t mf = (size_t)cap * E + 2 * A + 3 * A * mi + A * H + 64 * 8;
+        const size_t mf = (size_t)cap * E + 2 * A + 2 * A * mi + A * H + 64 * 8;
         TQ_TRY(dev_alloc(e, mf * 4, &p));
         float *m = (float *)p;
         auto mt = [&](size_t n) {
@@ -979,7 +977,6 @@ int prefill_setup(tqb200_engine *e) {
         P.idx = (int *)mt(A);
         P.mh = mt(A * mi);
         P.mu = mt(A * mi);
-        P.mact = mt(A * mi);
         P.mo = mt(A * H);
         const size_t mb = (size_t)moe_plan_max_cols(cap, k, E) / 8;
         const size_t ib = (2 * A + 4 + (size_t)P.max_tiles_gu + P.max_tiles_dn + mb) * 4 + 256;
@@ -1086,8 +1083,8 @@ int prefill_chunk(tqb200_engine *e, int n, int p0) {
                                         G, P.nt[(size_t)4 * l + launch], P.bhi, P.blo,
                                         P.tiles[(size_t)4 * l + launch], status, st);
     };
-    auto pack = [&](const float *x, int K) {
-        return launch_mm_pack_x(x, nullptr, K, K, n, G, P.bhi, P.blo, st);
+    auto pack = [&](const float *x, int K, const float *u = nullptr) {
+        return launch_mm_pack_x(x, nullptr, K, K, n, G, P.bhi, P.blo, st, u);
     };
     for (int l = 0; l < d.n_layers; ++l) {
         const DLayer &w = e->layers[l];
@@ -1153,9 +1150,7 @@ int prefill_chunk(tqb200_engine *e, int n, int p0) {
             TQ_TRY(mark(e, K_PACK));
             TQ_TRY(mm(l, 4, 2, 2, H));
             TQ_TRY(mark(e, K_GATEUP));
-            TQ_TRY(launch_swiglu_out(P.gate, P.up, P.act, n * d.inter, st));
-            TQ_TRY(mark(e, K_SWIGLU));
-            TQ_TRY(pack(P.act, d.inter));
+            TQ_TRY(pack(P.gate, d.inter, P.up));  // SwiGLU formed by the pack
             TQ_TRY(mark(e, K_PACK));
             TQ_TRY(mm(l, 6, 1, 3, d.inter));
             TQ_TRY(mark(e, K_DOWN));
@@ -1186,7 +1181,6 @@ int prefill_chunk(tqb200_engine *e, int n, int p0) {
         a.wgu_stride = (long long)pl.ex_gu_stride;
         a.wd_stride = (long long)pl.ex_down_stride;
         a.xn = P.xn;
-        a.act = P.mact;
         a.hbuf = P.mh;
         a.ubuf = P.mu;
         a.obuf = P.mo;
@@ -1211,8 +1205,6 @@ int prefill_chunk(tqb200_engine *e, int n, int p0) {
         TQ_TRY(launch_matmul_i4_planned(P.jobs_gu, P.tile_gu, P.ntiles, tgu, H, G, P.moe_nt, P.bhi,
                                         P.blo, status, st));
         TQ_TRY(mark(e, K_GATEUP));
-        TQ_TRY(launch_swiglu_out(P.mh, P.mu, P.mact, n * k * mi, st));
-        TQ_TRY(mark(e, K_SWIGLU));
         TQ_TRY(launch_mm_pack_x_mapped(P.pack_dn, P.pack_map, P.ntiles + 2, nbk, mi, G, P.bhi, P.blo, st));
         TQ_TRY(mark(e, K_PACK));
         TQ_TRY(launch_matmul_i4_planned(P.jobs_dn, P.tile_dn, P.ntiles + 1, tdn, mi, G, P.moe_nt,

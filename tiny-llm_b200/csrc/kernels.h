@@ -89,6 +89,7 @@ constexpr int kMmTileRows = 256;  // weight rows per matmul CTA
 // One source of a grouped X pack: column n of the job is x + (cols ? cols[n] : n) * ldx.
 struct MmPackJob {
     const float *x;
+    const float *u;       // optional: pack SwiGLU(x, u) (u in x's layout) instead of x
     const int *cols;
     int ldx, N;
     long long b_off;      // bf16 elements into the planes
@@ -104,7 +105,7 @@ size_t mm_scratch_bytes(int M, int K, int N, int G);  // launch_matmul_i4's scra
 int mm_tile_width(int M, int N);
 // X [K x N] (column n at x + (cols ? cols[n] : n) * ldx) -> the bf16 hi/lo planes
 int launch_mm_pack_x(const float *x, const int *cols, int ldx, int K, int N, int G,
-                     uint16_t *bhi, uint16_t *blo, cudaStream_t st);
+                     uint16_t *bhi, uint16_t *blo, cudaStream_t st, const float *u = nullptr);
 int launch_matmul_i4_grouped(const MmJob *host_jobs, const MmJob *dev_jobs, int n_jobs, int K,
                              int G, int nt, const uint16_t *bhi, const uint16_t *blo,
                              int total_tiles, int *status, cudaStream_t st);
@@ -138,8 +139,8 @@ struct MoePlanArgs {
     const uint8_t *wg, *wu, *wd;  // tile-contiguous expert weights, expert e at e * stride
     long long wgu_stride, wd_stride;
     const float *xn;       // [n][H] normalised hidden rows (gate/up input)
-    const float *act;      // [n*k][mi] SwiGLU rows in bucket order (down input)
-    float *hbuf, *ubuf;    // [n*k][mi] gate / up outputs in bucket order
+    float *hbuf, *ubuf;    // [n*k][mi] gate / up outputs in bucket order (down's input is
+                           // SwiGLU(h, u), formed by its X pack)
     float *obuf;           // [n*k][H] down outputs in bucket order
     int *rows, *slot;      // [n*k] token of bucket row; bucket row of assignment
     MmJob *jobs_gu, *jobs_dn;     // [2E], [E]

@@ -174,25 +174,33 @@ __device__ __forceinline__ const MmJob &job_of(const MmParams &P, int j) {
 // g*G + 8*kc + (0,4,1,5,2,6,3,7); chunk G/8 of the hi plane holds the zero-term operand
 // (X1, X2, X3, X1, X2, X3, 0, 0) of the group sum X_g = sum x (fp32, k < K); everything
 // else (columns >= N, k >= K, the lo plane's extra chunks) is zero.
-// CTA = one (group, 8-column block) of one job: warp c reads column c's G values
-// (coalesced along K), the block is assembled in shared memory and stored as whole
-// 16-byte words of the two contiguous (G+16)*16-byte regions.
-constexpr int kPackThreads = 256;
+// With u set, the column's values are SwiGLU(x, u) = x / (1 + exp(-x)) * u (the
+// reference's silu and product roundings) instead of x.
+// One warp per (group, 8-column block): lane l takes column l/4 and the G/4 consecutive
+// K values (l%4)*G/4 .. (coalesced), which are whole 8-position chunks, so each lane
+// builds its 16-byte chunk words in registers and the 8 lanes of a chunk store 128
+// contiguous bytes.  A CTA's 8 warps take 8 consecutive groups of one column block.
+constexpr int kPackWarps = 8;
+
+__device__ __forceinline__ float pack_value(float g, const float *u, size_t i) {
+    if (!u) return g;
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u[i]);
+}
 
 // Grouped form: the 8-column blocks of all jobs are numbered together (job j's first
 // block is col0/8), map[b] is the job of block b and *count the blocks in use.
 template <int G>
-__global__ void __launch_bounds__(kPackThreads) mm_pack_x_kernel(const MmPackJob job0,
-                                                                 const MmPackJob *__restrict__ jobs,
-                                                                 const int *__restrict__ map,
-                                                                 const int *__restrict__ count,
-                                                                 int K, int ng, int nb_grid,
-                                                                 uint16_t *__restrict__ bhi,
-                                                                 uint16_t *__restrict__ blo) {
+__global__ void __launch_bounds__(kPackWarps * 32) mm_pack_x_kernel(const MmPackJob job0,
+                                                                    const MmPackJob *__restrict__ jobs,
+                                                                    const int *__restrict__ map,
+                                                                    const int *__restrict__ count,
+                                                                    int K, int ng, int nb_grid,
+                                                                    uint16_t *__restrict__ bhi,
+                                                                    uint16_t *__restrict__ blo) {
     constexpr int CK = (G + 16) / 8;
-    constexpr int PER = G / 32;  // values per lane
-    __shared__ __align__(16) uint16_t th[CK * 64], tl[CK * 64];
-    const int g = blockIdx.x / nb_grid, gb = blockIdx.x % nb_grid;
+    constexpr int PER = G / 4;   // values per lane: PER / 8 whole chunks
+    constexpr int NCH = PER / 8;
+    const int gq = blockIdx.x / nb_grid, gb = blockIdx.x % nb_grid;
     MmPackJob jb;
     int nb;
     if (map) {
@@ -205,47 +213,66 @@ __global__ void __launch_bounds__(kPackThreads) mm_pack_x_kernel(const MmPackJob
     }
     const int npad = (jb.N + 15) & ~15;
     if (nb >= npad / 8) return;  // uniform
-    const int t = threadIdx.x, c = t >> 5, lane = t & 31;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = gq * kPackWarps + warp;
+    if (g >= ng) return;  // warp-uniform; no CTA barrier below
+    const int c = lane >> 2, part = lane & 3;
     const int n = nb * 8 + c;
-    const float *src = n < jb.N ? jb.x + (size_t)(jb.cols ? jb.cols[n] : n) * jb.ldx : nullptr;
+    const size_t row = n < jb.N ? (size_t)(jb.cols ? jb.cols[n] : n) * jb.ldx : 0;
+    const float *src = n < jb.N ? jb.x + row : nullptr;
+    const int k0 = g * G + part * PER;
     float v[PER];
+    if (src && k0 + PER <= K && (((uintptr_t)(src + k0)) & 15) == 0 &&
+        (!jb.u || (((uintptr_t)(jb.u + row + k0)) & 15) == 0)) {
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
-        const int k = g * G + lane * PER + i;
-        v[i] = (src && k < K) ? src[k] : 0.0f;
+        for (int i = 0; i < PER; i += 4) {
+            const float4 f = *reinterpret_cast<const float4 *>(src + k0 + i);
+            v[i] = f.x, v[i + 1] = f.y, v[i + 2] = f.z, v[i + 3] = f.w;
+        }
+        if (jb.u) {
+#pragma unroll
+            for (int i = 0; i < PER; ++i) v[i] = pack_value(v[i], jb.u, row + k0 + i);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < PER; ++i)
+            v[i] = (src && k0 + i < K) ? pack_value(src[k0 + i], jb.u, row + k0 + i) : 0.0f;
     }
     float xs = 0.0f;
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
-        const int kl = lane * PER + i, r = kl & 7;
-        const int o = (kl >> 3) * 64 + c * 8 + 2 * (r & 3) + (r >> 2);
-        const uint16_t h = bf16_bits(v[i]);
-        th[o] = h;
-        tl[o] = bf16_bits(__fsub_rn(v[i], bf16_val(h)));
-        xs = __fadd_rn(xs, v[i]);
-    }
+    for (int i = 0; i < PER; ++i) xs = __fadd_rn(xs, v[i]);
+    xs = __fadd_rn(xs, __shfl_xor_sync(0xffffffffu, xs, 1));
+    xs = __fadd_rn(xs, __shfl_xor_sync(0xffffffffu, xs, 2));
+    const size_t base = (size_t)jb.b_off + ((size_t)g * (npad / 8) + nb) * CK * 64 + (size_t)c * 8;
+    uint4 *dh = reinterpret_cast<uint4 *>(bhi + base);  // chunk kc at dh[kc * 8]
+    uint4 *dl = reinterpret_cast<uint4 *>(blo + base);
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) xs = __fadd_rn(xs, __shfl_xor_sync(0xffffffffu, xs, off));
-    if (lane < 16) {  // the two extra chunks of column c: zero term in hi, zeros elsewhere
-        const int o = (G / 8) * 64 + (lane >> 3) * 64 + c * 8 + (lane & 7);
-        uint16_t hv = 0;
-        if (lane < 6) {
-            const uint16_t x1 = bf16_bits(xs);
-            const float r1 = __fsub_rn(xs, bf16_val(x1));
-            const uint16_t x2 = bf16_bits(r1);
-            const uint16_t x3 = bf16_bits(__fsub_rn(r1, bf16_val(x2)));
-            const int m = lane % 3;
-            hv = m == 0 ? x1 : (m == 1 ? x2 : x3);
+    for (int q = 0; q < NCH; ++q) {  // position 2p+e of a chunk holds its column p + 4e
+        uint32_t h[4], l[4];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            const float a = v[8 * q + p], b = v[8 * q + p + 4];
+            const uint16_t h0 = bf16_bits(a), h1 = bf16_bits(b);
+            const uint16_t l0 = bf16_bits(__fsub_rn(a, bf16_val(h0)));
+            const uint16_t l1 = bf16_bits(__fsub_rn(b, bf16_val(h1)));
+            h[p] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+            l[p] = (uint32_t)l0 | ((uint32_t)l1 << 16);
         }
-        th[o] = hv;
-        tl[o] = 0;
+        const int kc = part * NCH + q;
+        dh[kc * 8] = make_uint4(h[0], h[1], h[2], h[3]);
+        dl[kc * 8] = make_uint4(l[0], l[1], l[2], l[3]);
     }
-    __syncthreads();
-    const size_t base = (size_t)jb.b_off + ((size_t)g * (npad / 8) + nb) * CK * 64;
-    for (int i = t; i < 2 * CK * 8; i += kPackThreads) {
-        const int pl = i / (CK * 8), w = i % (CK * 8);
-        const uint4 val = reinterpret_cast<const uint4 *>(pl ? tl : th)[w];
-        reinterpret_cast<uint4 *>((pl ? blo : bhi) + base)[w] = val;
+    if (part == 0) {  // the zero-term chunk and the padding chunk of this column
+        const uint16_t x1 = bf16_bits(xs);
+        const float r1 = __fsub_rn(xs, bf16_val(x1));
+        const uint16_t x2 = bf16_bits(r1);
+        const uint16_t x3 = bf16_bits(__fsub_rn(r1, bf16_val(x2)));
+        dh[(G / 8) * 8] = make_uint4((uint32_t)x1 | ((uint32_t)x2 << 16),
+                                     (uint32_t)x3 | ((uint32_t)x1 << 16),
+                                     (uint32_t)x2 | ((uint32_t)x3 << 16), 0u);
+        dh[(G / 8 + 1) * 8] = make_uint4(0u, 0u, 0u, 0u);
+        dl[(G / 8) * 8] = make_uint4(0u, 0u, 0u, 0u);
+        dl[(G / 8 + 1) * 8] = make_uint4(0u, 0u, 0u, 0u);
     }
 }
 
@@ -686,22 +713,24 @@ int launch_pack(const MmPackJob &job0, const MmPackJob *jobs, const int *map, co
     TQ_CHECK_ARG(mm_group_supported(G), "matmul_i4: group_size %d not 32, 64 or 128", G);
     if (nb_grid <= 0) return TQB200_OK;
     const int ng = (K + G - 1) / G;
-    const long long bx = (long long)ng * nb_grid;
+    const long long bx = (long long)((ng + kPackWarps - 1) / kPackWarps) * nb_grid;
     TQ_CHECK_ARG(bx < (1LL << 31), "matmul_i4: X pack grid %lld", bx);
+    const int threads = kPackWarps * 32;
     if (G == 32)
-        mm_pack_x_kernel<32><<<(unsigned)bx, kPackThreads, 0, st>>>(job0, jobs, map, count, K, ng, nb_grid, bhi, blo);
+        mm_pack_x_kernel<32><<<(unsigned)bx, threads, 0, st>>>(job0, jobs, map, count, K, ng, nb_grid, bhi, blo);
     else if (G == 64)
-        mm_pack_x_kernel<64><<<(unsigned)bx, kPackThreads, 0, st>>>(job0, jobs, map, count, K, ng, nb_grid, bhi, blo);
+        mm_pack_x_kernel<64><<<(unsigned)bx, threads, 0, st>>>(job0, jobs, map, count, K, ng, nb_grid, bhi, blo);
     else
-        mm_pack_x_kernel<128><<<(unsigned)bx, kPackThreads, 0, st>>>(job0, jobs, map, count, K, ng, nb_grid, bhi, blo);
+        mm_pack_x_kernel<128><<<(unsigned)bx, threads, 0, st>>>(job0, jobs, map, count, K, ng, nb_grid, bhi, blo);
     TQ_CUDA_TRY(cudaGetLastError());
     return TQB200_OK;
 }
 
 int launch_mm_pack_x(const float *x, const int *cols, int ldx, int K, int N, int G, uint16_t *bhi,
-                     uint16_t *blo, cudaStream_t st) {
+                     uint16_t *blo, cudaStream_t st, const float *u) {
     MmPackJob j{};
     j.x = x;
+    j.u = u;
     j.cols = cols;
     j.ldx = ldx;
     j.N = N;

@@ -29,11 +29,17 @@ constexpr int kApRows = 64;
 constexpr int kApKeys = 32;
 constexpr int kApThreads = 256;
 
-template <int HD>
+// Shared memory: Q [kApRows][HD+4] f32, K/V tiles double-buffered in the cache's own type
+// ([2][K|V][kApKeys][HD + 16 B]), P [kApRows][kApKeys+1] f32.  The next tile's K/V rows
+// stream in with cp.async (16-byte pieces, zero-filled past the causal end) while the
+// current tile is consumed.
+template <typename KV, int HD>
 struct ApSmem {
-    static constexpr int LD = HD + 4;  // row pitch (floats): conflict-free 128-bit loads
-    static constexpr size_t bytes =
-        ((size_t)kApRows * LD + 2 * (size_t)kApKeys * LD + (size_t)kApRows * (kApKeys + 1)) * 4;
+    static constexpr int LD = HD + 4;                  // Q row pitch (floats)
+    static constexpr int LDK = HD + 16 / (int)sizeof(KV);  // K/V row pitch (elements)
+    static constexpr size_t q_bytes = (size_t)kApRows * LD * 4;
+    static constexpr size_t kv_bytes = 2 * 2 * (size_t)kApKeys * LDK * sizeof(KV);
+    static constexpr size_t bytes = q_bytes + kv_bytes + (size_t)kApRows * (kApKeys + 1) * 4;
 };
 
 __device__ __forceinline__ float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
@@ -44,17 +50,27 @@ __device__ __forceinline__ float4 ld4(const uint16_t *p) {
                        h2f((uint16_t)(u.y & 0xFFFFu)), h2f((uint16_t)(u.y >> 16)));
 }
 
+__device__ __forceinline__ void cp16(void *dst, const void *src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+                 "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 template <typename KV, int HD>
 __device__ __forceinline__ void attn_block(const float *__restrict__ q, const KV *__restrict__ kc,
                                            const KV *__restrict__ vc, int p0, int n, int H, int KVH,
                                            int max_seq, float scale, float *__restrict__ out, int qb,
-                                           float *sm) {
-    constexpr int LD = ApSmem<HD>::LD;
+                                           uint8_t *sm) {
+    using S = ApSmem<KV, HD>;
+    constexpr int LD = S::LD, LDK = S::LDK;
     constexpr int NU = HD / 64;  // float4 column blocks per thread in P.V
-    float *Qs = sm;                          // [kApRows][LD]
-    float *Ks = Qs + kApRows * LD;           // [kApKeys][LD]
-    float *Vs = Ks + kApKeys * LD;           // [kApKeys][LD]
-    float *Ps = Vs + kApKeys * LD;           // [kApRows][kApKeys + 1]
+    constexpr int CPR = HD * (int)sizeof(KV) / 16;  // 16-byte pieces per K/V row
+    float *Qs = reinterpret_cast<float *>(sm);                          // [kApRows][LD]
+    KV *Kr = reinterpret_cast<KV *>(sm + S::q_bytes);                   // [2][2][kApKeys][LDK]
+    float *Ps = reinterpret_cast<float *>(sm + S::q_bytes + S::kv_bytes);  // [kApRows][kApKeys + 1]
     const int tid = threadIdx.x;
     const int g = H / KVH;
     const int tq = kApRows / g;              // tokens per CTA
@@ -62,6 +78,24 @@ __device__ __forceinline__ void attn_block(const float *__restrict__ q, const KV
     const int t0 = qb * tq;
     const int rows = min(tq, n - t0) * g;    // live rows; row r = token t0 + r/g, head kh*g + r%g
     const size_t qld = (size_t)H * HD;
+    const int kv_end = p0 + min(t0 + tq, n);  // keys [0, kv_end)
+    const KV *kb_base = kc + (size_t)kh * max_seq * HD;
+    const KV *vb_base = vc + (size_t)kh * max_seq * HD;
+    const int ntile = (kv_end + kApKeys - 1) / kApKeys;
+    auto issue = [&](int t) {  // K/V rows of tile t into buffer t & 1
+        KV *Kb = Kr + (size_t)(t & 1) * 2 * kApKeys * LDK;
+        KV *Vb = Kb + kApKeys * LDK;
+        const int kb = t * kApKeys;
+        for (int i = tid; i < kApKeys * CPR; i += kApThreads) {
+            const int r = i / CPR, c = (i % CPR) * (16 / (int)sizeof(KV));
+            const bool ok = kb + r < kv_end;
+            const size_t off = (size_t)(ok ? kb + r : 0) * HD + c;
+            cp16(Kb + r * LDK + c, kb_base + off, ok);
+            cp16(Vb + r * LDK + c, vb_base + off, ok);
+        }
+        cp_commit();
+    };
+    issue(0);
     for (int i = tid; i < kApRows * (HD / 4); i += kApThreads) {
         const int r = i / (HD / 4), c = 4 * (i % (HD / 4));
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -80,28 +114,23 @@ __device__ __forceinline__ void attn_block(const float *__restrict__ q, const KV
 #pragma unroll
         for (int c = 0; c < 4 * NU; ++c) acc[i][c] = 0.0f;
     }
-    const int kv_end = p0 + min(t0 + tq, n);  // keys [0, kv_end)
-    const KV *kb_base = kc + (size_t)kh * max_seq * HD;
-    const KV *vb_base = vc + (size_t)kh * max_seq * HD;
-    for (int kb = 0; kb < kv_end; kb += kApKeys) {
-        __syncthreads();  // previous tile's K/V reads done (and Q staged, first time)
-        for (int i = tid; i < kApKeys * (HD / 4); i += kApThreads) {
-            const int r = i / (HD / 4), c = 4 * (i % (HD / 4));
-            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-            if (kb + r < kv_end) {
-                kv = ld4(kb_base + (size_t)(kb + r) * HD + c);
-                vv = ld4(vb_base + (size_t)(kb + r) * HD + c);
-            }
-            *reinterpret_cast<float4 *>(Ks + r * LD + c) = kv;
-            *reinterpret_cast<float4 *>(Vs + r * LD + c) = vv;
+    for (int t = 0; t < ntile; ++t) {
+        if (t + 1 < ntile) {
+            issue(t + 1);
+            cp_wait<1>();
+        } else {
+            cp_wait<0>();
         }
-        __syncthreads();
+        __syncthreads();  // tile t (and Q, the first time) visible to every thread
+        const KV *Ks = Kr + (size_t)(t & 1) * 2 * kApKeys * LDK;
+        const KV *Vs = Ks + kApKeys * LDK;
+        const int kb = t * kApKeys;
         float s[4][2];
 #pragma unroll
         for (int i = 0; i < 4; ++i) s[i][0] = s[i][1] = 0.0f;
 #pragma unroll 4
         for (int d = 0; d < HD; d += 4) {
-            const float4 k0 = ld4(Ks + tc * LD + d), k1 = ld4(Ks + (tc + 16) * LD + d);
+            const float4 k0 = ld4(Ks + tc * LDK + d), k1 = ld4(Ks + (tc + 16) * LDK + d);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const float4 qv = ld4(Qs + (4 * tr + i) * LD + d);
@@ -145,7 +174,7 @@ __device__ __forceinline__ void attn_block(const float *__restrict__ q, const KV
             for (int i = 0; i < 4; ++i) p[i] = Ps[(4 * tr + i) * (kApKeys + 1) + j];
 #pragma unroll
             for (int u = 0; u < NU; ++u) {
-                const float4 vv = ld4(Vs + j * LD + 4 * tc + 64 * u);
+                const float4 vv = ld4(Vs + j * LDK + 4 * tc + 64 * u);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     acc[i][4 * u + 0] = fmaf(p[i], vv.x, acc[i][4 * u + 0]);
@@ -155,7 +184,7 @@ __device__ __forceinline__ void attn_block(const float *__restrict__ q, const KV
                 }
             }
         }
-        __syncwarp();  // P of this tile read before the next tile rewrites it
+        __syncthreads();  // buffer t & 1 and P consumed before they are refilled
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -176,7 +205,7 @@ template <typename KV, int HD>
 __global__ void __launch_bounds__(kApThreads, 2)
 attn_prefill_kernel(const float *__restrict__ q, const KV *__restrict__ kc, const KV *__restrict__ vc,
                     int p0, int n, int H, int KVH, int max_seq, float scale, float *__restrict__ out) {
-    extern __shared__ __align__(16) float sm[];
+    extern __shared__ __align__(16) uint8_t sm[];
     const int nb = (n + kApRows / (H / KVH) - 1) / (kApRows / (H / KVH));
     const int j = blockIdx.x;
     attn_block<KV, HD>(q, kc, vc, p0, n, H, KVH, max_seq, scale, out, j, sm);
@@ -188,7 +217,7 @@ attn_prefill_kernel(const float *__restrict__ q, const KV *__restrict__ kc, cons
 
 template <typename KV, int HD>
 int launch_ap(const AttnPrefillArgs &a, cudaStream_t st) {
-    const size_t smem = ApSmem<HD>::bytes;
+    const size_t smem = ApSmem<KV, HD>::bytes;
     static KernelSmem once;
     int limit = 0;
     TQ_CUDA_TRY(smem_limit_once(attn_prefill_kernel<KV, HD>, once, &limit));
@@ -341,6 +370,7 @@ __global__ void __launch_bounds__(kPlanThreads) moe_plan_kernel(const MoePlanArg
         const long long bgu = cs_gu * s_npre[e], bdn = cs_dn * s_npre[e];
         MmPackJob pg;
         pg.x = a.xn;
+        pg.u = nullptr;
         pg.cols = a.rows + off;
         pg.ldx = a.H;
         pg.N = cnt;
@@ -348,7 +378,8 @@ __global__ void __launch_bounds__(kPlanThreads) moe_plan_kernel(const MoePlanArg
         pg.col0 = s_npre[e];
         a.pack_gu[e] = pg;
         MmPackJob pd;
-        pd.x = a.act + (size_t)off * a.mi;
+        pd.x = a.hbuf + (size_t)off * a.mi;
+        pd.u = a.ubuf + (size_t)off * a.mi;
         pd.cols = nullptr;
         pd.ldx = a.mi;
         pd.N = cnt;
