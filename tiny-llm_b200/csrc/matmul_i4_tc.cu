@@ -25,10 +25,10 @@
 //    the weight blocks that warp 17 stages with 1-D bulk copies (TMA) a few groups ahead,
 //    together with the stage's X planes, which a pre-pass kernel lays out in the MMA's
 //    shared-memory order.  Warps 8-15 are the epilogue; warp 16 allocates TMEM and one
-//    lane issues the MMAs.  Stages (one quantisation group each) are handed over with
-//    mbarriers: full (8 producer warps), bfull (copy bytes), empty (tcgen05.commit),
-//    tmem_full (commit) and tmem_empty (8 epilogue warps); rawbar/rawfree for the
-//    weight blocks.
+//    lane issues the MMAs; warp 18 does the MMA warp's barrier waits.  Stages (one quantisation group each) are handed over with
+//    mbarriers: full (8 producer warps + the X-plane copy bytes), empty (tcgen05.commit),
+//    tmem_full per row half (commit) and tmem_empty per row half (its 4 epilogue warps);
+//    rawbar/rawfree for the weight blocks.
 //  * Operand layout in shared memory: the canonical K-major, no-swizzle UMMA layout of
 //    8-row x 16-byte core matrices, the core matrices of one 8-row group adjacent along
 //    K (leading byte offset 128), 8-row groups (G+16)*16 bytes apart (stride offset).
@@ -56,7 +56,13 @@ constexpr int kProdWarps = 8;      // warps 0-7: A operand, one weight row per t
 constexpr int kEpiWarps = 8;       // warps 8-15: TMEM -> registers -> Y
 constexpr int kMmaWarp = kProdWarps + kEpiWarps;  // warp 16: TMEM allocation, MMA issue
 constexpr int kLoadWarp = kMmaWarp + 1;           // warp 17: bulk copies (TMA)
-constexpr int kMmThreads = (kLoadWarp + 1) * 32;
+constexpr int kGateWarp = kLoadWarp + 1;           // warp 18: waits on behalf of the MMA warp
+constexpr int kMmThreads = (kGateWarp + 1) * 32;
+// Named barriers between the gate warp and the MMA warp (0 is __syncthreads): stage
+// ready, then row half 0 / 1 drained.  A shared-memory wait issued by the MMA thread right
+// after its MMAs stalls until they have read their operands, so the MMA warp only meets
+// the gate warp at hardware barriers.
+constexpr int kBarStage = 1, kBarHalf0 = 2;
 constexpr int kMmMaxStages = 4;
 constexpr int kTileRows = 2 * kMmRows;  // weight rows per CTA: two accumulators share X
 static_assert(kTileRows == kMmTileRows, "tile rows");
@@ -65,7 +71,8 @@ constexpr int kMmMaxCols = 64;     // tile width limit (epilogue registers)
 // epilogue has read it (the producer's stage wait orders it behind MMA i-S, which waited
 // for the epilogue's drain of group i-S-2)
 constexpr int kSclRing = kMmMaxStages + 3;
-constexpr int kMaxRaw = 4;         // weight blocks staged ahead, at most
+constexpr int kMaxRaw = 8;         // weight blocks staged ahead, at most
+constexpr int kTmemCols = 512;     // the CTA's TMEM allocation (one CTA per SM: registers)
 
 struct MmParams {
     MmJob job0;            // used when jobs == nullptr
@@ -80,6 +87,7 @@ struct MmParams {
     uint32_t stage_bytes;
     int raw_depth;         // groups of raw weight bytes staged ahead (2..4)
     uint32_t tmem_cols;
+    int a_col;             // first TMEM column of the A stages (after the accumulators)
     int *status;
 };
 
@@ -106,6 +114,26 @@ __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t a, uint64_t 
         : "memory");
 }
 
+// D (TMEM) (+)= A (TMEM, lane = row, 8 columns = 16 bf16 of K) x B (shared memory).
+__device__ __forceinline__ void umma_bf16_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t b,
+                                             uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// 8 consecutive TMEM columns of this warp's 32 lanes <- 8 words per thread.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t *v) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};\n" ::"r"(taddr),
+                 "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                      smem_u32(bar))
@@ -129,14 +157,14 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
                  : "memory");
 }
 
-// Named barrier 1 over the producer warps; returns the OR of `pred` across them.
-__device__ __forceinline__ bool producers_sync_or(bool pred) {
+// Named barrier `id` over the gate and MMA warps (64 threads); returns the OR of `pred`.
+__device__ __forceinline__ bool gate_sync_or(int id, bool pred) {
     uint32_t r;
     asm volatile(
-        "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n bar.red.or.pred p, 1, %2, q;\n"
+        "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n bar.red.or.pred p, %2, 64, q;\n"
         " selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(r)
-        : "r"((uint32_t)pred), "n"(kProdWarps * 32)
+        : "r"((uint32_t)pred), "r"(id)
         : "memory");
     return r != 0;
 }
@@ -300,9 +328,8 @@ __global__ void mm_repack_w_kernel(const uint32_t *__restrict__ w, int M, int ng
 template <int G>
 __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_constant__ MmParams P) {
     constexpr int CK = (G + 16) / 8;          // 16-byte chunks per row of a stage
-    constexpr uint32_t SBO = CK * 128;        // bytes between 8-row groups
-    constexpr uint32_t kAh = kMmRows * CK * 16;  // A bytes of one 128-row half
-    constexpr uint32_t kA = 2 * kAh;
+    constexpr uint32_t SBO = CK * 128;        // bytes between 8-row groups (B operand)
+    constexpr int KS = G / 16 + 1;            // MMA K steps per group (the last: zero term)
     constexpr int NW = G / 8;                 // nibble words per row of a group
     constexpr int GB = 4 + G / 2;             // bytes per group of a weight row
     constexpr int WR = GB / 4;                // words per row of a group (odd)
@@ -310,10 +337,10 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
     extern __shared__ __align__(1024) uint8_t smem[];
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);  // [kMmMaxStages] A built
-    uint64_t *bfull = full + kMmMaxStages;                 // [kMmMaxStages] X planes landed
+    uint64_t *bfull = full + kMmMaxStages;                 // (unused slot)
     uint64_t *empty = bfull + kMmMaxStages;                // [kMmMaxStages] stage consumed
-    uint64_t *tfull = empty + kMmMaxStages;                // [2] accumulators b ready
-    uint64_t *tempty = tfull + 2;                          // [2] accumulators b drained
+    uint64_t *tfull = empty + kMmMaxStages;                // [2] accumulator of row half h ready
+    uint64_t *tempty = tfull + 2;                          // [2] accumulator of row half h drained
     uint64_t *done = tempty + 2;
     uint64_t *rawbar = done + 1;                           // [kMaxRaw] weight block landed
     uint64_t *rawfree = rawbar + kMaxRaw;                  // [kMaxRaw] weight block read
@@ -350,13 +377,13 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
 
     if (t == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(&full[s], kProdWarps);
-            mbar_init(&bfull[s], 1);
+            mbar_init(&full[s], kProdWarps + 1);  // 8 producer warps + the X-plane copies
+            mbar_init(&bfull[s], 1);  // keeps the layout; full[s] also takes the copy bytes
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], kEpiWarps);
+            mbar_init(&tempty[b], kEpiWarps / 2);
         }
         mbar_init(done, 1);
         for (int r = 0; r < RD; ++r) {
@@ -380,50 +407,56 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
 
     if (warp < kProdWarps) {
         // ---------------- A operand: thread = weight row t of the tile, codes widened to
-        // bf16 from the tile-contiguous weight block of the group (mm_repack_w_kernel)
-        const uint32_t off = (uint32_t)(t >> 7) * kAh + (uint32_t)((t & 127) >> 3) * SBO +
-                             (uint32_t)(t & 7) * 16u;
+        // bf16 from the tile-contiguous weight block of the group (mm_repack_w_kernel) and
+        // stored to the stage's TMEM columns of its row half (lane = row; warp w may reach
+        // lanes 32 * (w % 4) ..); K step kk = 8 columns, K positions 2c, 2c+1 in column c
+        const uint32_t a_lane = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+        const int half = t >> 7;
         const __nv_bfloat162 k128 = __floats2bfloat162_rn(128.0f, 128.0f);
         for (int i = 0; i < ng; ++i) {
             const int s = i % S, r = i % RD;
             bool ok = true;
             if (i >= S) ok = mbar_wait_sleep(&empty[s], (uint32_t)((i / S) - 1) & 1u, kWaitCycles);
             if (ok) ok = mbar_wait_sleep(&rawbar[r], (uint32_t)(i / RD) & 1u, kWaitCycles);
-            if (producers_sync_or(!ok)) {  // uniform: every producer stops together
-                if (t == 0) s_err = 1;
+            if (!__all_sync(0xffffffffu, ok)) {  // warp-uniform stop; the MMA side times out
+                if (lane == 0) s_err = 1;
                 break;
             }
+            tc_fence_after();  // the MMAs that read this stage's TMEM columns are complete
             const uint32_t *d = reinterpret_cast<const uint32_t *>(raw + (size_t)r * kRawBytes) + t * WR;
             uint32_t wv[WR];
 #pragma unroll
             for (int q = 0; q < WR; ++q) wv[q] = d[q];  // [0] header, then nibble words
             __syncwarp();
             if (lane == 0) mbar_arrive_plain(&rawfree[r]);  // block slot r read
-            uint8_t *st = stage_base + (size_t)s * stage_bytes;
+            const uint32_t ta = a_lane + (uint32_t)(P.a_col + (s * 2 + half) * KS * 8);
 #pragma unroll
-            for (int q = 0; q < NW; ++q) {  // 8 codes -> (q0,q4) (q1,q5) (q2,q6) (q3,q7)
-                const uint32_t w = wv[1 + q];
-                uint32_t o[4];
+            for (int kk = 0; kk < G / 16; ++kk) {  // 16 codes -> 8 words: (q0,q4) (q1,q5) ...
+                uint32_t o[8];
 #pragma unroll
-                for (int p = 0; p < 4; ++p) {
-                    const uint32_t wide = ((w >> (4 * p)) & 0x000F000Fu) | 0x43004300u;  // 128 + q
-                    const __nv_bfloat162 v = __hsub2(*reinterpret_cast<const __nv_bfloat162 *>(&wide), k128);
-                    o[p] = *reinterpret_cast<const uint32_t *>(&v);
+                for (int h = 0; h < 2; ++h) {
+                    const uint32_t w = wv[1 + 2 * kk + h];
+#pragma unroll
+                    for (int p = 0; p < 4; ++p) {
+                        const uint32_t wide = ((w >> (4 * p)) & 0x000F000Fu) | 0x43004300u;  // 128 + q
+                        const __nv_bfloat162 v = __hsub2(*reinterpret_cast<const __nv_bfloat162 *>(&wide), k128);
+                        o[4 * h + p] = *reinterpret_cast<const uint32_t *>(&v);
+                    }
                 }
-                *reinterpret_cast<uint4 *>(st + off + (uint32_t)q * 128u) = make_uint4(o[0], o[1], o[2], o[3]);
+                tmem_st8(ta + (uint32_t)(kk * 8), o);
             }
-            {  // zero term: -(z1, z1, z1, z2, z2, z2, 0, 0), z = z1 + z2 exactly
+            {  // zero term: -(z1, z1, z1, z2, z2, z2, 0, ...), z = z1 + z2 exactly
                 const float z = h2f((uint16_t)(wv[0] >> 16));
                 const uint16_t z1 = bf16_bits(-z);
                 const uint16_t z2 = bf16_bits(__fsub_rn(-z, bf16_val(z1)));
-                const uint32_t a = (uint32_t)z1 | ((uint32_t)z1 << 16);
-                const uint32_t b = (uint32_t)z1 | ((uint32_t)z2 << 16);
-                const uint32_t c = (uint32_t)z2 | ((uint32_t)z2 << 16);
-                *reinterpret_cast<uint4 *>(st + off + (uint32_t)NW * 128u) = make_uint4(a, b, c, 0u);
-                *reinterpret_cast<uint4 *>(st + off + (uint32_t)(NW + 1) * 128u) = make_uint4(0u, 0u, 0u, 0u);
+                const uint32_t o[8] = {(uint32_t)z1 | ((uint32_t)z1 << 16),
+                                       (uint32_t)z1 | ((uint32_t)z2 << 16),
+                                       (uint32_t)z2 | ((uint32_t)z2 << 16), 0u, 0u, 0u, 0u, 0u};
+                tmem_st8(ta + (uint32_t)((G / 16) * 8), o);
             }
             scl[(i % kSclRing) * kTileRows + t] = h2f((uint16_t)(wv[0] & 0xFFFFu));  // for the epilogue
-            fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+            tmem_wait_st();
+            tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_plain(&full[s]);
         }
@@ -435,27 +468,25 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
         const int quarter = warp & 3;  // TMEM lanes this warp may access
         const int rl = 128 * half + 32 * quarter + lane;  // row within the tile
         const int row = m0 + rl;
-        // accumulator (buffer b, half h) = TMEM columns [(2b + h) * 2nt, +2nw): P of the
-        // hi plane in the first nw columns, of the lo plane in the next nw
+        // accumulator of row half h = TMEM columns [2h * nt, + 2nw): P of the hi plane in
+        // the first nw columns, of the lo plane in the next nw
         const uint32_t lane_addr = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(half * 2 * P.nt);
         float y[kMmMaxCols];
 #pragma unroll
         for (int c = 0; c < kMmMaxCols; ++c) y[c] = 0.0f;
         for (int i = 0; i < ng; ++i) {
-            const int b = i & 1;
-            if (!__all_sync(0xffffffffu, mbar_wait_sleep(&tfull[b], (uint32_t)(i >> 1) & 1u, kWaitCycles))) {
+            if (!__all_sync(0xffffffffu, mbar_wait_sleep(&tfull[half], (uint32_t)i & 1u, kWaitCycles))) {
                 if (lane == 0) s_err = 1;
                 break;
             }
             tc_fence_after();
             const float sc = scl[(i % kSclRing) * kTileRows + rl];
-            const uint32_t ta = lane_addr + (uint32_t)(b * 4 * P.nt);
 #pragma unroll
             for (int h = 0; h < kMmMaxCols / 8; ++h) {  // 8 columns (hi and lo) at a time
                 if (h * 8 < nw) {
                     float v[8], u[8];
-                    tmem_ld8(ta + (uint32_t)(h * 8), v);
-                    tmem_ld8(ta + (uint32_t)(nw + h * 8), u);
+                    tmem_ld8(lane_addr + (uint32_t)(h * 8), v);
+                    tmem_ld8(lane_addr + (uint32_t)(nw + h * 8), u);
                     tmem_wait_ld();
 #pragma unroll
                     for (int c = 0; c < 8; ++c) y[h * 8 + c] = fmaf(sc, v[c] + u[c], y[h * 8 + c]);
@@ -463,7 +494,7 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_plain(&tempty[b]);
+            if (lane == 0) mbar_arrive_plain(&tempty[half]);
         }
         if (row < job.M) {
 #pragma unroll
@@ -478,41 +509,60 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
             }
         }
     } else if (warp == kMmaWarp) {
-        if (lane == 0) {
-            // ---------------- MMA issuer: per group, for each row half, G/16 K steps of
-            // codes x [X hi | X lo] (one MMA of N = 2nw: the lo plane's rows follow the hi
-            // plane's in shared memory with the same 8-row stride), then the zero term
-            bool ok = true;
-            const uint32_t idesc = umma_idesc_bf16(2 * nw);
-            for (int i = 0; i < ng && ok; ++i) {
-                const int s = i % S, b = i & 1;
-                ok = mbar_wait_sleep(&full[s], (uint32_t)(i / S) & 1u, kWaitCycles);
-                if (ok) ok = mbar_wait_sleep(&bfull[s], (uint32_t)(i / S) & 1u, kWaitCycles);
-                if (ok && i >= 2) ok = mbar_wait_sleep(&tempty[b], (uint32_t)((i >> 1) - 1) & 1u, kWaitCycles);
-                if (!ok) break;
-                tc_fence_after();
-                const uint32_t a0 = smem_u32(stage_base + (size_t)s * stage_bytes);
-                const uint32_t bh = a0 + kA;  // hi rows [0, nw), lo rows [nw, 2nw)
+        // ---------------- MMA issuer (lane 0): per group and row half, G/16 K steps of
+        // codes (TMEM) x [X hi | X lo] (shared memory; one MMA of N = 2nw, the lo plane's
+        // rows following the hi plane's), then the zero term.  Each half has one
+        // accumulator: the epilogue drains half 0 of group i while the MMAs of half 1 run,
+        // and the reverse.  The gate warp has done the waiting when each barrier opens.
+        const uint32_t idesc = umma_idesc_bf16(2 * nw);
+        bool bad = false;
+        for (int i = 0; i < ng; ++i) {
+            const int s = i % S;
+            bad = gate_sync_or(kBarStage, bad);  // A and X planes of group i in place
+            const uint32_t bh = smem_u32(stage_base + (size_t)s * stage_bytes);
 #pragma unroll
-                for (int hf = 0; hf < 2; ++hf) {
-                    const uint32_t a = a0 + (uint32_t)hf * kAh;
-                    const uint32_t dd = tmem + (uint32_t)((b * 2 + hf) * 2 * P.nt);
+            for (int hf = 0; hf < 2; ++hf) {
+                bad = gate_sync_or(kBarHalf0 + hf, bad);  // half hf of group i-1 drained
+                if (!bad && lane == 0) {
+                    tc_fence_after();
+                    const uint32_t ta = tmem + (uint32_t)(P.a_col + (s * 2 + hf) * KS * 8);
+                    const uint32_t dd = tmem + (uint32_t)(hf * 2 * P.nt);
 #pragma unroll
                     for (int kk = 0; kk < G / 16; ++kk) {
                         const uint32_t o = (uint32_t)kk * 256u;  // two 16-byte core-matrix columns
-                        umma_bf16(dd, umma_desc(a + o, 128, SBO), umma_desc(bh + o, 128, SBO), idesc,
-                                  kk > 0 ? 1u : 0u);
+                        umma_bf16_ta(dd, ta + (uint32_t)(kk * 8), umma_desc(bh + o, 128, SBO), idesc,
+                                     kk > 0 ? 1u : 0u);
                     }
                     const uint32_t oz = (uint32_t)(G / 16) * 256u;  // zero term
-                    umma_bf16(dd, umma_desc(a + oz, 128, SBO), umma_desc(bh + oz, 128, SBO), idesc, 1u);
+                    umma_bf16_ta(dd, ta + (uint32_t)((G / 16) * 8), umma_desc(bh + oz, 128, SBO), idesc, 1u);
+                    umma_commit(&tfull[hf]);  // half hf holds P_i
                 }
-                umma_commit(&empty[s]);  // stage s free once these MMAs have read it
-                umma_commit(&tfull[b]);  // accumulators b hold P_i
+                __syncwarp();
             }
-            if (!ok) s_err = 1;
+            if (!bad && lane == 0) umma_commit(&empty[s]);  // stage s free once read
+            __syncwarp();
+        }
+        if (lane == 0) {
+            if (bad) s_err = 1;
             umma_commit(done);  // every MMA issued above has completed
             if (!mbar_wait_sleep(done, 0u, kWaitCycles)) s_err = 1;
         }
+    } else if (warp == kGateWarp) {
+        // ---------------- gate: the MMA warp's waits, met at the named barriers in the
+        // same order; after a timeout it keeps meeting them without waiting
+        bool bad = false;
+        for (int i = 0; i < ng; ++i) {
+            const int s = i % S;
+            if (!bad && lane == 0) bad = !mbar_wait_sleep(&full[s], (uint32_t)(i / S) & 1u, kWaitCycles);
+            bad = gate_sync_or(kBarStage, __shfl_sync(0xffffffffu, bad, 0));
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                if (!bad && i >= 1 && lane == 0)
+                    bad = !mbar_wait_sleep(&tempty[hf], (uint32_t)(i - 1) & 1u, kWaitCycles);
+                bad = gate_sync_or(kBarHalf0 + hf, __shfl_sync(0xffffffffu, bad, 0));
+            }
+        }
+        if (bad && lane == 0) s_err = 1;
     } else if (lane == 0) {
         // ---------------- loader: weight blocks RD - 1 groups ahead, X planes per stage
         const uint8_t *wblk = job.w + (size_t)(local % mt) * ng * kRawBytes;  // this row tile
@@ -540,9 +590,9 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
             if (!ok) break;
             uint8_t *st = stage_base + (size_t)s * stage_bytes;
             const size_t blk = ((size_t)g * (npad / 8) + n0 / 8) * (CK * 64);  // bf16 elements
-            mbar_arrive_expect_tx(&bfull[s], 2u * b_bytes);
-            bulk_g2s(st + kA, P.bhi + job.b_off + blk, b_bytes, &bfull[s]);
-            bulk_g2s(st + kA + b_bytes, P.blo + job.b_off + blk, b_bytes, &bfull[s]);
+            mbar_arrive_expect_tx(&full[s], 2u * b_bytes);
+            bulk_g2s(st, P.bhi + job.b_off + blk, b_bytes, &full[s]);
+            bulk_g2s(st + b_bytes, P.blo + job.b_off + blk, b_bytes, &full[s]);
             b_issued = g + 1;
         }
         if (!ok) s_err = 1;
@@ -550,7 +600,7 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
         for (int g = max(0, raw_issued - RD); g < raw_issued; ++g)
             if (!mbar_wait_sleep(&rawbar[g % RD], (uint32_t)(g / RD) & 1u, kWaitCycles)) s_err = 1;
         for (int g = max(0, b_issued - S); g < b_issued; ++g)
-            if (!mbar_wait_sleep(&bfull[g % S], (uint32_t)(g / S) & 1u, kWaitCycles)) s_err = 1;
+            if (!mbar_wait_sleep(&full[g % S], (uint32_t)(g / S) & 1u, kWaitCycles)) s_err = 1;
     }
     tc_fence_before();
     __syncthreads();
@@ -566,8 +616,8 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
 KernelSmem g_mm_smem_set[3];
 
 template <int G>
-uint32_t mm_stage_bytes(int nt) {
-    return (uint32_t)(kTileRows + 2 * nt) * ((G + 16) / 8) * 16u;
+uint32_t mm_stage_bytes(int nt) {  // the X hi and lo planes of one group (B operand)
+    return (uint32_t)(2 * nt) * ((G + 16) / 8) * 16u;
 }
 
 template <int G>
@@ -577,9 +627,16 @@ int launch_grouped_g(MmParams &P, int total_tiles, cudaStream_t st, int gi) {
     TQ_CUDA_TRY(smem_limit_once(mm_i4_tc_kernel<G>, g_mm_smem_set[gi], &limit));
     const int fixed = 1024 + kSclRing * kTileRows * 4;
     const int raw_group = kTileRows * (4 + G / 2);  // bytes of one staged weight block
+    // TMEM: 4 nt accumulator columns (two row halves of [hi | lo]), then per stage two row
+    // halves of (G/16 + 1) K steps of 8 columns of A
+    const int a_stage_cols = 2 * (G / 16 + 1) * 8;
+    const int tmem_stages = (kTmemCols - 4 * P.nt) / a_stage_cols;
+    TQ_CHECK_ARG(tmem_stages >= 1, "matmul_i4: tile of %d columns leaves no TMEM for A", P.nt);
+    P.tmem_cols = kTmemCols;
+    P.a_col = 4 * P.nt;
     // deepest pipeline that fits: operand stages first (2 wanted), then the weight ring
     int stages = 0, rd = 0;
-    for (int s = std::min(kMmMaxStages, P.ng); s >= 1 && !stages; --s)
+    for (int s = std::min({kMmMaxStages, P.ng, tmem_stages}); s >= 1 && !stages; --s)
         for (int r = kMaxRaw; r >= 2; --r)
             if (fixed + s * (int)P.stage_bytes + r * raw_group <= limit && (s >= 2 || r == 2)) {
                 stages = s;
@@ -634,9 +691,9 @@ size_t mm_scratch_bytes(int M, int K, int N, int G) {
     return a + mm_x_planes_bytes(K, N, G);
 }
 
-// Column tile width by a cost model: a CTA's time per group is about (64 + nt) units (the
-// A operand's shared-memory reads cost as much as 64 columns of B), and the launch takes
-// as many such CTA times as it has waves over the SMs.  Ties go to the wider tile.
+// Column tile width by a cost model: a CTA's time per group is about (36 + nt) units (each
+// MMA instruction has a fixed cost of about 36 columns' worth; measured), and the launch
+// takes as many such CTA times as it has waves over the SMs.  Ties go to the wider tile.
 int mm_tile_width(int M, int N) {
     const int npad = (N + 15) & ~15;
     const int mt = (M + kTileRows - 1) / kTileRows;
@@ -646,7 +703,7 @@ int mm_tile_width(int M, int N) {
     long long best_cost = -1;
     for (int nt = widest; nt >= 16; nt -= 16) {
         const long long tiles = (long long)mt * ((npad + nt - 1) / nt);
-        const long long cost = ((tiles + sms - 1) / sms) * (64 + nt);
+        const long long cost = ((tiles + sms - 1) / sms) * (36 + nt);
         if (best_cost < 0 || cost < best_cost) {
             best = nt;
             best_cost = cost;
@@ -672,9 +729,6 @@ int launch_matmul_i4_grouped(const MmJob *host_jobs, const MmJob *dev_jobs, int 
     P.nt = nt;
     P.bhi = bhi;
     P.blo = blo;
-    uint32_t cols = 32;
-    while ((int)cols < 8 * nt) cols <<= 1;
-    P.tmem_cols = cols;
     P.status = status;
     if (G == 32) return launch_grouped_g<32>(P, total_tiles, st, 0);
     if (G == 64) return launch_grouped_g<64>(P, total_tiles, st, 1);
@@ -699,9 +753,6 @@ int launch_matmul_i4_planned(const MmJob *dev_jobs, const int *dev_tile_job, con
     P.nt = nt;
     P.bhi = bhi;
     P.blo = blo;
-    uint32_t cols = 32;
-    while ((int)cols < 8 * nt) cols <<= 1;
-    P.tmem_cols = cols;
     P.status = status;
     if (G == 32) return launch_grouped_g<32>(P, max_tiles, st, 0);
     if (G == 64) return launch_grouped_g<64>(P, max_tiles, st, 1);
