@@ -332,35 +332,24 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
     }
     griddep_wait();
     griddep_launch();
-    if (tid == 0) {
-        if (!fused)
-            for (int i = 0; i < min(total, NST); ++i) issue(i);
-        if (P.bulk_in) {
-            const uint32_t qb = (uint32_t)G * HD * 4u;
-            mbar_arrive_expect_tx(bar_q, qb + (owner ? 2u * HD * 4u : 0u));
-            bulk_g2s(qs, P.q + (size_t)kh * G * HD, qb, bar_q);
-            if (owner) {
-                bulk_g2s(krow, P.k_new + (size_t)kh * HD, HD * 4u, bar_q);
-                bulk_g2s(vrow, P.v_new + (size_t)kh * HD, HD * 4u, bar_q);
-            }
-        }
-    }
+    if (tid == 0 && !fused)
+        for (int i = 0; i < min(total, NST); ++i) issue(i);
+    // q (and the owner's new k, v) were just written by the projection kernel: plain
+    // loads by every thread reach them sooner than a bulk copy and its barrier
+    for (int i = tid; i < G * HD; i += kThreads) qs[i] = P.q[(size_t)kh * G * HD + i];
+    if (owner)
+        for (int i = tid; i < HD; i += kThreads)
+            krow[i] = P.k_new[(size_t)kh * HD + i], vrow[i] = P.v_new[(size_t)kh * HD + i];
     if (P.bulk_in) {
-        if (tid == 0) {
-            if (fused && !mbar_wait(bar_c, 0, kWaitCycles)) s_err = 1;
-            if (!mbar_wait(bar_q, 0, kWaitCycles)) s_err = 1;
-        }
-    } else {  // unaligned inputs: the same staging with plain loads
-        for (int i = tid; i < G * HD; i += kThreads) qs[i] = P.q[(size_t)kh * G * HD + i];
+        if (tid == 0 && fused && !mbar_wait(bar_c, 0, kWaitCycles)) s_err = 1;
+    } else {  // unaligned constant vectors: plain loads
         if (fused) {
             for (int i = tid; i < half; i += kThreads) {
                 cs[i] = P.cos_tab[(size_t)(seq - 1) * half + i];
                 sn[i] = P.sin_tab[(size_t)(seq - 1) * half + i];
             }
-            for (int i = tid; i < HD; i += kThreads) {
-                if (has_norm) qn[i] = P.q_norm[i], kn[i] = P.k_norm[i];
-                if (owner) krow[i] = P.k_new[(size_t)kh * HD + i], vrow[i] = P.v_new[(size_t)kh * HD + i];
-            }
+            if (has_norm)
+                for (int i = tid; i < HD; i += kThreads) qn[i] = P.q_norm[i], kn[i] = P.k_norm[i];
         }
     }
     __syncthreads();
@@ -483,10 +472,7 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
             const int issued = s_issued;
             for (int i = max(0, issued - NST); i < issued; ++i)
                 mbar_wait(&bars[i % NST], (uint32_t)(i / NST) & 1u, kWaitCycles);
-            if (P.bulk_in) {
-                mbar_wait(bar_q, 0, kWaitCycles);
-                if (fused) mbar_wait(bar_c, 0, kWaitCycles);
-            }
+            if (P.bulk_in && fused) mbar_wait(bar_c, 0, kWaitCycles);
             if (P.status) atomicExch(P.status, kDevTimeoutTma);
         }
         __syncthreads();

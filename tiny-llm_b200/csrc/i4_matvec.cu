@@ -370,12 +370,13 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
     }
     __syncthreads();
     float rms_scale = 1.0f, amax = 0.0f;
-    {
-        double tot = 0.0;
-        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
-            tot += s_rd[w];
-            amax = fmaxf(amax, s_am[w]);
-        }
+    {  // the warps' partials, summed across a warp's lanes (every warp, no extra barrier)
+        const int nwp = (int)(blockDim.x >> 5);
+        double tot = lane < nwp ? s_rd[lane] : 0.0;
+        amax = lane < nwp ? s_am[lane] : 0.0f;
+        if (norm) tot = warp_sum_d(tot);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
         if (norm) {
             const float mean_sq = (float)(tot / K);
             rms_scale = 1.0f / sqrtf(__fadd_rn(mean_sq, P.x.eps));
