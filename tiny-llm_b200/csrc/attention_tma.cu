@@ -278,6 +278,7 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
     float *pl = pm + G;                                         // [G] partial l
     float *wgt = pl + G;                                        // [ns][G] merge weights (+ m, l copies)
     __shared__ float s_m[G], s_l[G];
+    __shared__ float s_cw[kWarps * G];  // CTA merge weights
     __shared__ int s_err, s_issued;
     __shared__ int s_done[kStages];  // warps finished with the slot's current tile
 
@@ -490,24 +491,29 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
 #pragma unroll
         for (int d = 0; d < D; ++d) wpo[(warp * G + g) * HD + lane * D + d] = err ? 0.0f : acc[g][d];
     __syncthreads();
-    for (int i = tid; i < G * HD; i += kThreads) {
-        const int g = i / HD;
+    if (tid < G) {  // the warps' weights exp(m_w - M) of head g, once
+        const int g = tid;
         float M = -INFINITY;
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) M = fmaxf(M, wpm[w * G + g]);
-        float O = 0.0f, Lsum = 0.0f;
+        float Lsum = 0.0f;
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) {
             const float mw = wpm[w * G + g];
             const float e = mw == -INFINITY ? 0.0f : expf(mw - M);
-            O = fmaf(e, wpo[(w * G + g) * HD + (i - g * HD)], O);
+            s_cw[w * G + g] = e;
             Lsum = fmaf(e, wpl[w * G + g], Lsum);
         }
+        pm[g] = M;
+        pl[g] = Lsum;
+    }
+    __syncthreads();
+    for (int i = tid; i < G * HD; i += kThreads) {
+        const int g = i / HD;
+        float O = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) O = fmaf(s_cw[w * G + g], wpo[(w * G + g) * HD + (i - g * HD)], O);
         po[i] = O;
-        if (i - g * HD == 0) {
-            pm[g] = M;
-            pl[g] = Lsum;
-        }
     }
     cluster.sync();  // every rank's partial is visible cluster-wide
     // ---- merge over DSMEM.  Thread (g, s) of the first G half-warps reads rank s's
