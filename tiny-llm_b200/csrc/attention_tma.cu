@@ -269,6 +269,9 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
     float *sn = cs + half;                                      // [HD/2]
     float *qn = sn + half;                                      // [HD] QK-norm weights
     float *kn = qn + HD;                                        // [HD]
+    float *rcv_o = kn + HD;                                     // [ns][per] pushed partial o
+    float *rcv_m = rcv_o + G * HD + kMaxSplit;                  // [ns][G] pushed m
+    float *rcv_l = rcv_m + kMaxSplit * G;                       // [ns][G] pushed l
     // after the last tile the ring holds the warps' partials and this CTA's partial
     float *wpo = reinterpret_cast<float *>(ring);               // [warps][G][HD]
     float *wpm = wpo + kWarps * G * HD;                         // [warps][G]
@@ -515,51 +518,44 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
         for (int w = 0; w < kWarps; ++w) O = fmaf(s_cw[w * G + g], wpo[(w * G + g) * HD + (i - g * HD)], O);
         po[i] = O;
     }
-    cluster.sync();  // every rank's partial is visible cluster-wide
-    // ---- merge over DSMEM.  Thread (g, s) of the first G half-warps reads rank s's
-    // (m, l) for head g; the max, the weights exp(m_s - M) and the weighted l sum are
-    // formed with shuffles inside the 16 lanes of head g.  Each thread of this rank's
-    // output slice then reads its ns partials with independent remote loads.  Empty
-    // splits (m_s = -inf, o = 0) weigh 0.
-    if (tid < (G * kMaxSplit + 31) / 32 * 32) {  // whole warps (the shuffles need all lanes)
-        const int g = tid / kMaxSplit, s = tid - g * kMaxSplit;
-        float m = -INFINITY, l = 0.0f;
-        if (g < G && s < ns) {
-            m = *cluster.map_shared_rank(pm + g, s);
-            l = *cluster.map_shared_rank(pl + g, s);
+    // ---- merge over DSMEM, pushed: output slice r (per values) belongs to rank r; every
+    // rank stores its partial of slice r, and its (m, l), into rank r's receive area
+    // (remote stores, no round trip), then one cluster barrier (release / acquire) makes
+    // them visible and each rank merges its own slice from local shared memory.  Empty
+    // splits (m = -inf, o = 0) weigh 0.
+    const int per = (G * HD + ns - 1) / ns;
+    __syncthreads();  // po, pm, pl complete
+    for (int i = tid; i < G * HD; i += kThreads) {
+        const int r = i / per;
+        *cluster.map_shared_rank(rcv_o + split * per + (i - r * per), r) = po[i];
+    }
+    for (int i = tid; i < G * ns; i += kThreads) {
+        const int r = i / G, g = i - r * G;
+        *cluster.map_shared_rank(rcv_m + split * G + g, r) = pm[g];
+        *cluster.map_shared_rank(rcv_l + split * G + g, r) = pl[g];
+    }
+    cluster.sync();  // every push has landed
+    if (tid < G) {
+        const int g = tid;
+        float M = -INFINITY;
+        for (int s2 = 0; s2 < ns; ++s2) M = fmaxf(M, rcv_m[s2 * G + g]);
+        float L = 0.0f;
+        for (int s2 = 0; s2 < ns; ++s2) {
+            const float m = rcv_m[s2 * G + g];
+            const float w = m == -INFINITY ? 0.0f : expf(m - M);
+            wgt[s2 * G + g] = w;
+            L = fmaf(rcv_l[s2 * G + g], w, L);
         }
-        float M = m;
-#pragma unroll
-        for (int o = kMaxSplit / 2; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-        const float w = m == -INFINITY ? 0.0f : expf(m - M);
-        if (g < G && s < ns) wgt[s * G + g] = w;
-        float L = l * w;
-#pragma unroll
-        for (int o = kMaxSplit / 2; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-        if (g < G && s == 0) s_l[g] = L;
+        s_l[g] = L;
     }
     __syncthreads();
-    const int per = (G * HD + ns - 1) / ns;
     const int i_end = min(G * HD, (split + 1) * per);
-    float res[(G * HD + kThreads - 1) / kThreads];
-    int nres = 0;
     for (int i = split * per + tid; i < i_end; i += kThreads) {
-        const int g = i / HD;
-        float o[kMaxSplit];
-#pragma unroll
-        for (int s = 0; s < kMaxSplit; ++s) o[s] = s < ns ? *cluster.map_shared_rank(po + i, s) : 0.0f;
+        const int g = i / HD, j = i - split * per;
         float O = 0.0f;
-#pragma unroll
-        for (int s = 0; s < kMaxSplit; ++s)
-            if (s < ns) O = fmaf(o[s], wgt[s * G + g], O);
-        res[nres++] = O / s_l[g];
+        for (int s2 = 0; s2 < ns; ++s2) O = fmaf(rcv_o[s2 * per + j], wgt[s2 * G + g], O);
+        P.out[(size_t)kh * G * HD + i] = O / s_l[g];
     }
-    // every remote read of this thread is done: tell the cluster, write the output,
-    // and only then wait for the others (no rank leaves while another still reads it)
-    cluster.barrier_arrive();
-    nres = 0;
-    for (int i = split * per + tid; i < i_end; i += kThreads) P.out[(size_t)kh * G * HD + i] = res[nres++];
-    cluster.barrier_wait();
 }
 
 template <typename KV, int HD, int G>
@@ -622,7 +618,8 @@ int launch_t(const AttnArgs &a, cudaStream_t st) {
         P.status = a.status;
         // barriers | ring | new k, v rows (cache type) | krow, vrow, qs, cs+sn, qn, kn
         const size_t smem = 128 + (size_t)P.stage_region + ((2 * (size_t)RB + 15) & ~(size_t)15) +
-                            ((size_t)5 * HD + (size_t)G * HD) * 4;
+                            ((size_t)5 * HD + (size_t)G * HD) * 4 +
+                            ((size_t)G * HD + kMaxSplit + 2 * (size_t)kMaxSplit * G) * 4;
         if (smem > (size_t)smem_max) continue;
         cudaLaunchConfig_t cfg{};
         cfg.gridDim = dim3(a.n_kv_heads, ns);
