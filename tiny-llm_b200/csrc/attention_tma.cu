@@ -335,7 +335,6 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
         }
     }
     griddep_wait();
-    griddep_launch();
     if (tid == 0 && !fused)
         for (int i = 0; i < min(total, NST); ++i) issue(i);
     // q (and the owner's new k, v) were just written by the projection kernel: plain
@@ -468,6 +467,9 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
         if (owner && warp == kWarps - 1 && !s_err) group(lastk, lastv, 1);  // the new row
     }
     __syncthreads();  // every warp is past the ring: it now holds the partials
+    // dependents (the next projection) start their weight prefetch now, not earlier:
+    // their copies would compete with this kernel's cache reads
+    griddep_launch();
     const bool err = s_err != 0;
     if (err) {
         // drain the copies still in flight and report; this CTA's partial is an empty
