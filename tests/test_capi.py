@@ -83,3 +83,16 @@ def test_bad_arguments_rejected_before_device(built):
     # and 16-padded column
     assert L.tqb200_matmul_i4_scratch_bytes(768, 2048, 37, 64) == 3 * 32 * 256 * 36 + 2 * 32 * 80 * 48 * 2
     assert L.tqb200_matmul_i4_scratch_bytes(768, 2048, 37, 48) == 0
+
+
+def test_prefill_arguments_rejected_before_device(built):
+    """tqb200_engine_prefill / _profile_prefill validate their arguments on the host."""
+    import ctypes as C
+    from tqb200 import lib
+    L = lib.load()
+    toks = np.array([1, 2, 3], np.int32)
+    nxt = C.c_int(-1)
+    assert L.tqb200_engine_prefill(None, toks, 3, C.byref(nxt)) == 1
+    assert b"prefill" in L.tqb200_last_error()
+    ms = np.zeros(14, np.float32)
+    assert L.tqb200_engine_profile_prefill(None, toks, 3, ms, 14, C.byref(nxt)) == 1
