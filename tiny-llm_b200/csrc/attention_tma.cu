@@ -418,10 +418,12 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
 #pragma unroll
         for (int g = 0; g < G; ++g) {
             mn[g] = fmaxf(m_[g], __shfl_sync(0xffffffffu, mx, g));
-            alpha[g] = m_[g] == -INFINITY ? 0.0f : expf(m_[g] - mn[g]);
+            alpha[g] = m_[g] == -INFINITY ? 0.0f : __expf(m_[g] - mn[g]);
             if (gl == g) m_own = mn[g];
         }
-        const float p = s == -INFINITY ? 0.0f : expf(s - m_own);
+        // fast exponentials (ex2.approx, ~2^-21 relative): the online softmax's terms only
+        // need fp32-level accuracy, not the last bit of expf
+        const float p = s == -INFINITY ? 0.0f : __expf(s - m_own);
         float ps = p;
 #pragma unroll
         for (int o = GP; o < 32; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
