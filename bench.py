@@ -890,7 +890,7 @@ def main():
     if rank == 0:
         threads = cpu_threads()
         if args.workload == "matvec-i4":
-            gbs, kind, sample = ref_matvec_rate(args.cpu_seconds, 1)
+            gbs, kind, sample = ref_matvec_rate(max(0.5, args.cpu_seconds), 1)
             out["cpu_baseline"] = {"value": round(gbs, 4), "unit": "GB/s", "cores": 1,
                                    "kind": kind, "sample": sample + f" (host has {threads} threads)"}
         elif args.workload == "matmul-i4":
