@@ -47,8 +47,69 @@ struct VqParams {
     int *status;
 };
 
+// One Hadamard block of BS = 32 * E elements in registers (lane l holds elements
+// l*E .. l*E+E-1): butterfly levels h = 1, 2, 4, ... in the reference's order, the pairs
+// inside a lane first, then across lanes (partner l ^ (h / E)); every butterfly is the
+// reference's (a + b, a - b) on the same operands, so the result is bit-exact.
+template <int E>
+__device__ __forceinline__ void fwht_warp(float (&e)[E], int lane) {
+#pragma unroll
+    for (int h = 1; h < E; h <<= 1) {
+#pragma unroll
+        for (int j = 0; j < E; ++j)
+            if ((j & h) == 0) {
+                const float a = e[j], c = e[j + h];
+                e[j] = __fadd_rn(a, c);
+                e[j + h] = __fsub_rn(a, c);
+            }
+    }
+#pragma unroll
+    for (int hl = 1; hl < 32; hl <<= 1) {
+        const bool upper = (lane & hl) != 0;
+#pragma unroll
+        for (int j = 0; j < E; ++j) {
+            const float o = __shfl_xor_sync(0xffffffffu, e[j], hl);
+            e[j] = upper ? __fsub_rn(o, e[j]) : __fadd_rn(e[j], o);
+        }
+    }
+}
+
+template <int E>
+__device__ void biip_blocks_warp(float *v, int nblk, const float *sign, const float *scale) {
+    constexpr int BS = 32 * E;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const float inv = 1.0f / sqrtf((float)BS);
+    for (int b = warp; b < nblk; b += nw) {
+        float e[E];
+        const int base = b * BS + lane * E;
+#pragma unroll
+        for (int i = 0; i < E; ++i) {
+            const int j = base + i;
+            e[i] = scale ? __fmul_rn(__fdiv_rn(v[j], scale[j]), sign[j]) : __fmul_rn(v[j], sign[j]);
+        }
+        fwht_warp<E>(e, lane);
+#pragma unroll
+        for (int i = 0; i < E; ++i) v[base + i] = __fmul_rn(e[i], inv);
+    }
+}
+
 // In-place BiIP of v[0..K) in shared memory by the whole CTA (sign/scale anywhere).
+// Blocks of 32..256 elements run one per warp in registers; other sizes through shared
+// memory with a barrier per butterfly level.
 __device__ void biip_smem(float *v, int K, const float *sign, const float *scale, int bs) {
+    if (bs >= 32 && bs <= 256) {
+        const int nblk = K / bs;
+        for (int j = nblk * bs + threadIdx.x; j < K; j += blockDim.x)  // tail: sign/scale only
+            v[j] = scale ? __fmul_rn(__fdiv_rn(v[j], scale[j]), sign[j]) : __fmul_rn(v[j], sign[j]);
+        switch (bs) {
+            case 32: biip_blocks_warp<1>(v, nblk, sign, scale); break;
+            case 64: biip_blocks_warp<2>(v, nblk, sign, scale); break;
+            case 128: biip_blocks_warp<4>(v, nblk, sign, scale); break;
+            default: biip_blocks_warp<8>(v, nblk, sign, scale); break;
+        }
+        __syncthreads();
+        return;
+    }
     for (int j = threadIdx.x; j < K; j += blockDim.x)
         v[j] = scale ? __fmul_rn(__fdiv_rn(v[j], scale[j]), sign[j]) : __fmul_rn(v[j], sign[j]);
     __syncthreads();
