@@ -1,5 +1,5 @@
-"""Tensor-parallel engine (tp_size 2, one process per GPU, NCCL all-gather per layer)
-against the single-GPU oracle: identical greedy tokens and logits within 1e-4 on
+"""Tensor-parallel engine (tp_size 2, one process per GPU, NCCL all-gather per layer;
+MoE layers expert-parallel) against the single-GPU oracle: identical greedy tokens and logits within 1e-4 on
 every rank.  Needs two visible GPUs (skipped otherwise)."""
 from __future__ import annotations
 
@@ -16,7 +16,9 @@ from tqb200.model import SynthModel
 
 pytestmark = pytest.mark.gpu
 HERE = os.path.dirname(os.path.abspath(__file__))
-TP_CASES = [c for c in gc.MODEL_CASES if c[0] in ("qwen2_bias", "qwen3_f16kv", "vq2_rot")]
+# "moe": attention sharded as in the dense cases, experts split across the ranks (expert
+# parallelism: 8 of the 16 experts per rank, a cross-rank sum of the chosen experts' slots)
+TP_CASES = [c for c in gc.MODEL_CASES if c[0] in ("qwen2_bias", "qwen3_f16kv", "vq2_rot", "moe")]
 
 
 @pytest.mark.parametrize("case", TP_CASES, ids=[c[0] for c in TP_CASES])

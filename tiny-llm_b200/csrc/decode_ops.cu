@@ -714,6 +714,21 @@ __global__ void moe_combine_kernel(float *__restrict__ h, const float *__restric
     }
 }
 
+// Expert parallelism: the chosen experts as this rank's local indices (-1: another
+// rank's expert, e outside [e0, e0 + e_local)), and the expert-output slots zeroed so
+// that the cross-rank sum of the slots is each slot's owner's value exactly.
+__global__ void moe_ep_local_kernel(const int *__restrict__ idx, int k, int e0, int e_local,
+                                    int *__restrict__ local, float *__restrict__ o, int n) {
+    griddep_wait();
+    griddep_launch();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < k) {
+        const int e = idx[i] - e0;
+        local[i] = (e >= 0 && e < e_local) ? e : -1;
+    }
+    for (int j = i; j < n; j += gridDim.x * blockDim.x) o[j] = 0.0f;
+}
+
 // ------------------------------------------------------------------ embed
 __global__ void embed_kernel(const void *__restrict__ table, int dtype, const int *__restrict__ token,
                              int dim, int group_size, float *__restrict__ out) {
@@ -1068,6 +1083,14 @@ int launch_moe_combine_rows(float *h, const float *o, const float *wts, const in
     moe_combine_rows_kernel<<<grid, 256, 0, st>>>(h, o, wts, slot, k, H);
     TQ_CUDA_TRY(cudaGetLastError());
     return TQB200_OK;
+}
+
+int launch_moe_ep_local(const int *idx, int k, int e0, int e_local, int *local, float *o, int H,
+                        bool pdl, cudaStream_t st) {
+    TQ_CHECK_ARG(k > 0 && k <= 1024 && H > 0 && e_local > 0, "moe ep: k %d H %d", k, H);
+    const int n = k * H, threads = 256;
+    const int grid = std::max(1, std::min((n + threads - 1) / threads, 64));
+    return launch_pdl(moe_ep_local_kernel, grid, threads, 0, pdl, st, idx, k, e0, e_local, local, o, n);
 }
 
 int launch_embed(const void *table, int dtype, const int *token, int dim, int group_size,

@@ -145,6 +145,7 @@ struct tqb200_engine {
     float *moe_logits = nullptr, *moe_w = nullptr, *moe_h = nullptr, *moe_u = nullptr,
           *moe_o = nullptr;
     int *moe_idx = nullptr;
+    int *moe_local = nullptr;  // expert parallelism: chosen experts as local indices (-1: remote)
     unsigned int *moe_ticket = nullptr;
     tqb200::Prefill pf;
 #ifdef TQB200_HAVE_NCCL
@@ -237,7 +238,7 @@ int up_vec(tqb200_engine *e, const float *h, int n, const float **out) {
 // Every expert's gate, up and down matrices into one device buffer per kind, expert x at
 // x * stride (stride = the matrix bytes rounded up to 16), and the router.
 int up_experts(tqb200_engine *e, const tqb200_layer &s, const tqb200_model_desc &d, DLayer &w) {
-    const int E = d.n_experts;
+    const int E = d.n_experts / e->tp, x0 = e->rank * E;  // this rank's experts (all if tp == 1)
     const size_t gu = (mat_bytes(s.expert_gate[0], d.group_size) + 15) & ~(size_t)15;
     const size_t dn = (mat_bytes(s.expert_down[0], d.group_size) + 15) & ~(size_t)15;
     void *pg, *pu, *pd;
@@ -245,11 +246,11 @@ int up_experts(tqb200_engine *e, const tqb200_layer &s, const tqb200_model_desc 
     TQ_TRY(dev_alloc(e, gu * E, &pu));
     TQ_TRY(dev_alloc(e, dn * E, &pd));
     for (int x = 0; x < E; ++x) {
-        const size_t b = mat_bytes(s.expert_gate[x], d.group_size);
-        const size_t bd = mat_bytes(s.expert_down[x], d.group_size);
-        TQ_CUDA_TRY(cudaMemcpy((uint8_t *)pg + x * gu, s.expert_gate[x].data, b, cudaMemcpyHostToDevice));
-        TQ_CUDA_TRY(cudaMemcpy((uint8_t *)pu + x * gu, s.expert_up[x].data, b, cudaMemcpyHostToDevice));
-        TQ_CUDA_TRY(cudaMemcpy((uint8_t *)pd + x * dn, s.expert_down[x].data, bd, cudaMemcpyHostToDevice));
+        const size_t b = mat_bytes(s.expert_gate[x0 + x], d.group_size);
+        const size_t bd = mat_bytes(s.expert_down[x0 + x], d.group_size);
+        TQ_CUDA_TRY(cudaMemcpy((uint8_t *)pg + x * gu, s.expert_gate[x0 + x].data, b, cudaMemcpyHostToDevice));
+        TQ_CUDA_TRY(cudaMemcpy((uint8_t *)pu + x * gu, s.expert_up[x0 + x].data, b, cudaMemcpyHostToDevice));
+        TQ_CUDA_TRY(cudaMemcpy((uint8_t *)pd + x * dn, s.expert_down[x0 + x].data, bd, cudaMemcpyHostToDevice));
         e->weight_bytes += 2 * b + bd;
     }
     w.ex_gate = (const uint8_t *)pg;
@@ -278,7 +279,9 @@ int validate(const tqb200_model_desc &d, const tqb200_engine_opts &o) {
                          d.moe_inter > 0 && d.moe_inter % 32 == 0,
                      "MoE: n_experts %d, experts_per_tok %d, moe_inter %d", d.n_experts,
                      d.experts_per_tok, d.moe_inter);
-        TQ_CHECK_ARG(o.tp_size <= 1, "MoE models run on one GPU per engine (tp_size %d)", o.tp_size);
+        TQ_CHECK_ARG(o.tp_size <= 1 || d.n_experts % o.tp_size == 0,
+                     "expert parallelism: tp_size %d must divide n_experts %d", o.tp_size,
+                     d.n_experts);
     }
     TQ_CHECK_ARG(d.n_heads % d.n_kv_heads == 0, "n_heads %% n_kv_heads != 0");
     TQ_CHECK_ARG(d.group_size > 0 && d.group_size % 32 == 0,
@@ -368,6 +371,21 @@ int allgather(tqb200_engine *e, float *buf, size_t count) {
         ncclAllGather(buf + (size_t)e->rank * count, buf, count, ncclFloat, e->comm, e->stream);
     if (nr != ncclSuccess)
         return set_error(TQB200_ERR_CUDA, "ncclAllGather: %s", ncclGetErrorString(nr));
+    return TQB200_OK;
+#else
+    (void)buf;
+    (void)count;
+    return set_error(TQB200_ERR_UNSUPPORTED, "built without NCCL");
+#endif
+}
+
+// In-place sum over the ranks of `count` floats.
+int allreduce_sum(tqb200_engine *e, float *buf, size_t count) {
+    if (e->tp == 1) return TQB200_OK;
+#ifdef TQB200_HAVE_NCCL
+    const ncclResult_t nr = ncclAllReduce(buf, buf, count, ncclFloat, ncclSum, e->comm, e->stream);
+    if (nr != ncclSuccess)
+        return set_error(TQB200_ERR_CUDA, "ncclAllReduce: %s", ncclGetErrorString(nr));
     return TQB200_OK;
 #else
     (void)buf;
@@ -493,6 +511,13 @@ int launch_forward(tqb200_engine *e) {
             // (RMSNorm prologue, SwiGLU epilogue) -> down of each on its own activation ->
             // weighted sum in router order + residual
             const int k = d.experts_per_tok, mi = d.moe_inter, E = d.n_experts;
+            // expert parallelism (tp > 1): this rank holds experts [r * El, (r + 1) * El);
+            // the router runs whole on every rank (identical choices), each rank computes
+            // the chosen experts it holds into zeroed slots, and a cross-rank sum of the
+            // slots (exact: one non-zero term each) gives every rank all k outputs for the
+            // combine in router order
+            const int El = E / G;
+            const int *eidx = G > 1 ? e->moe_local : e->moe_idx;
             if (w.router_f32) {
                 TQ_TRY(launch_moe_router(e->hidden, w.post_ln, d.rms_eps, H, w.router_f32, E, k,
                                          e->moe_logits, e->moe_idx, e->moe_w, e->moe_ticket, pdl,
@@ -506,6 +531,8 @@ int launch_forward(tqb200_engine *e) {
                 TQ_TRY(launch_i4_matvec_ex(&j, 1, H, d.group_size, o, st));
                 TQ_TRY(launch_topk_softmax(e->moe_logits, E, k, e->moe_idx, e->moe_w, st));
             }
+            if (G > 1)
+                TQ_TRY(launch_moe_ep_local(e->moe_idx, k, r * El, El, e->moe_local, e->moe_o, H, pdl, st));
             TQ_TRY(mark(e, K_ROUTER));
             {
                 I4Job j[2] = {{w.ex_gate, e->moe_h, nullptr, nullptr, k * mi},
@@ -513,11 +540,11 @@ int launch_forward(tqb200_engine *e) {
                 I4LaunchOpts o;
                 o.x = {X_RMSNORM, e->hidden, w.post_ln, d.rms_eps, nullptr};
                 o.pair_swiglu = true;
-                o.eidx = e->moe_idx;
+                o.eidx = eidx;
                 o.estride = (long long)w.ex_gu_stride;
                 o.erows = mi;
                 o.nslots = k;
-                o.n_experts = E;
+                o.n_experts = El;
                 o.pdl = pdl;
                 o.status = status;
                 TQ_TRY(launch_i4_matvec_ex(j, 2, H, d.group_size, o, st));
@@ -527,15 +554,16 @@ int launch_forward(tqb200_engine *e) {
                 I4Job j{w.ex_down, e->moe_o, nullptr, nullptr, k * H};
                 I4LaunchOpts o;
                 o.x = {X_PLAIN, e->moe_h, nullptr, 0.0f, nullptr};
-                o.eidx = e->moe_idx;
+                o.eidx = eidx;
                 o.estride = (long long)w.ex_down_stride;
                 o.erows = H;
                 o.nslots = k;
-                o.n_experts = E;
+                o.n_experts = El;
                 o.xslots = true;
                 o.pdl = pdl;
                 o.status = status;
                 TQ_TRY(launch_i4_matvec_ex(&j, 1, mi, d.group_size, o, st));
+                TQ_TRY(allreduce_sum(e, e->moe_o, (size_t)k * H));
                 TQ_TRY(mark(e, K_DOWN));
             }
             TQ_TRY(launch_moe_combine(e->hidden, e->moe_o, e->moe_w, k, H, pdl, st));
@@ -815,7 +843,7 @@ int create_impl(const tqb200_model_desc *desc, const tqb200_engine_opts *opts, t
     TQ_CHECK_ARG(G <= 32, "tp_size %d above 32", G);
     if (d.model_type == TQB200_MODEL_QWEN3_MOE) {
         const int k = d.experts_per_tok, mi = d.moe_inter;
-        const size_t n = (size_t)d.n_experts + 2 * (size_t)k * mi + (size_t)k * H + 3 * 64;
+        const size_t n = (size_t)d.n_experts + 2 * (size_t)k * mi + (size_t)k * H + 4 * 64;
         TQ_TRY(dev_alloc(e, n * 4 + 256, &p));
         TQ_CUDA_TRY(cudaMemset(p, 0, n * 4 + 256));
         float *m = (float *)p;
@@ -825,6 +853,7 @@ int create_impl(const tqb200_model_desc *desc, const tqb200_engine_opts *opts, t
         e->moe_logits = m, m += ((d.n_experts + 63) / 64) * 64;
         e->moe_w = m, m += 64;
         e->moe_idx = (int *)m, m += 64;
+        e->moe_local = (int *)m, m += 64;
         e->moe_ticket = (unsigned int *)m;
     }
     e->layer_stride = (size_t)(d.n_kv_heads / G) * e->o.max_seq_len * hd;

@@ -59,7 +59,8 @@ struct MvParams {
     int *status;
     // MoE experts.  Expert mode (eidx != nullptr): the rows of job j form nslots blocks
     // of erows rows, block b being expert eidx[b] at job.w + eidx[b] * estride (passes
-    // never straddle blocks: R divides erows).  Slot mode (nslots > 0 with xslots):
+    // never straddle blocks: R divides erows); eidx[b] == -1 marks another rank's expert
+    // (expert parallelism): its block is neither staged nor written.  Slot mode (nslots > 0 with xslots):
     // CTA c serves block c % nslots only, with x = x.src + (c % nslots) * K.
     const int *eidx;
     long long estride;
@@ -124,10 +125,14 @@ __device__ uint32_t stage_rows(const MvParams &P, const I4Job &job, int row0, in
     const size_t RB = (size_t)((P.K + P.G - 1) / P.G) * (4 + P.G / 2);
     const uint8_t *base = job.w;
     int rows_end = job.rows;
+    bool skip = false;
     if (P.eidx) {  // the block's expert: rows relative to its own matrix
         const int blk = row0 / P.erows;
         int e = P.eidx[blk];
-        if (e < 0 || e >= P.n_experts) {  // self-check: never read outside the experts
+        if (e == -1) {  // another rank's expert (expert parallelism): nothing to stage
+            skip = true;
+            e = 0;
+        } else if (e < 0 || e >= P.n_experts) {  // self-check: never read outside the experts
             if (P.status) atomicExch(P.status, kDevBadExpert);
             e = 0;
         }
@@ -144,6 +149,10 @@ __device__ uint32_t stage_rows(const MvParams &P, const I4Job &job, int row0, in
     if (b16 > mat_end16) b16 = mat_end16;
     if (b16 < a16) b16 = a16;
     uint32_t bytes = (uint32_t)(b16 - a16);
+    if (skip) {
+        bytes = 0;
+        b = a16;
+    }
     if ((size_t)(b - a16) > cap) {  // self-check: never write past the stage buffer
         if (P.status) atomicExch(P.status, kDevBadStage);
         bytes = 0;
@@ -578,6 +587,7 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
                     if (job.bias) v += b_;
                     if (job.resid) v = r_ + v;
                 }
+                if (P.eidx && P.eidx[row / P.erows] == -1) continue;  // another rank's expert
                 job.y[row] = v;
                 if (P.am.token && j == 0) better(bv, bi, v, row + P.am.row_offset);
             }

@@ -270,6 +270,10 @@ int launch_moe_combine(float *h, const float *o, const float *wts, int k, int H,
                        cudaStream_t st);
 int launch_embed(const void *table, int dtype, const int *token, int dim, int group_size,
                  float *out, cudaStream_t st, int n_tokens = 1);
+// Expert parallelism: local[j] = idx[j] - e0 when this rank owns that expert, else -1;
+// o[0 .. k*H) = 0 (the cross-rank sum of the slots then equals each owner's output).
+int launch_moe_ep_local(const int *idx, int k, int e0, int e_local, int *local, float *o, int H,
+                        bool pdl, cudaStream_t st);
 // MoE prefill: router logits of n tokens (f32 router, xn normalised rows), top-k softmax
 // per token, and h[t] += sum_j wts[t][j] * o[slot[t*k+j]] per token.
 int launch_router_rows(const float *xn, int n, int H, const float *W, int E, float *logits,
