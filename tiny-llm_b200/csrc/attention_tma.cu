@@ -257,7 +257,6 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
     constexpr int half = HD / 2;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);  // [stages] tiles
     uint64_t *bar_c = bars + kStages;                      // constant vectors
-    uint64_t *bar_q = bars + kStages + 1;                  // q (+ new k, v)
     uint8_t *ring = smem + 128;
     KV *lastk = reinterpret_cast<KV *>(ring + P.stage_region);  // [HD] new row (fused)
     KV *lastv = lastk + HD;

@@ -151,12 +151,6 @@ __device__ __forceinline__ void mbar_arrive_plain(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)),
-                 "r"(bytes)
-                 : "memory");
-}
-
 // Named barrier `id` over the gate and MMA warps (64 threads); returns the OR of `pred`.
 __device__ __forceinline__ bool gate_sync_or(int id, bool pred) {
     uint32_t r;
@@ -337,8 +331,7 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
     extern __shared__ __align__(1024) uint8_t smem[];
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);  // [kMmMaxStages] A built
-    uint64_t *bfull = full + kMmMaxStages;                 // (unused slot)
-    uint64_t *empty = bfull + kMmMaxStages;                // [kMmMaxStages] stage consumed
+    uint64_t *empty = full + kMmMaxStages;                 // [kMmMaxStages] stage consumed
     uint64_t *tfull = empty + kMmMaxStages;                // [2] accumulator of row half h ready
     uint64_t *tempty = tfull + 2;                          // [2] accumulator of row half h drained
     uint64_t *done = tempty + 2;
@@ -378,7 +371,6 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
     if (t == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], kProdWarps + 1);  // 8 producer warps + the X-plane copies
-            mbar_init(&bfull[s], 1);  // keeps the layout; full[s] also takes the copy bytes
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
