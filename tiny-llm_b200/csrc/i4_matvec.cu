@@ -820,13 +820,13 @@ Shape plan(int K, int G, bool pair, bool norm, int rows_total, int r_div = 0) {
     L.block = kI4Threads;
     const int per_cta = std::max(1, (rows_total + num_sms() - 1) / num_sms());
     // A pass costs a consumer barrier and a reduction, so a CTA's share of up to 100 KB
-    // is one pass; larger shares go in three passes of at most 64 KB (the first lands
-    // sooner and the later ones stream while it is computed; measured against two
-    // passes of 96 KB and against 64 KB single passes on the config 4 step).
+    // is one pass; larger shares go in at least three passes of at most 80 KB (the first
+    // lands sooner and the later ones stream while it is computed; measured against two
+    // passes of 96 KB, four of 48 KB and 64 KB single passes on the config 4 step).
     if ((size_t)per_cta * RB * np <= 100 * 1024) {
         L.R = per_cta;
     } else {
-        const size_t cap = 64 * 1024 / (RB * np);
+        const size_t cap = 80 * 1024 / (RB * np);
         L.R = (int)std::max<size_t>(1, std::min<size_t>((per_cta + 2) / 3, cap));
     }
     if (r_div > 0) {  // passes must not straddle r_div-row blocks
