@@ -45,10 +45,12 @@ def test_attention_fp32_kv(tq, oracle, H, KVH, hd, seq, maxs):
     assert max_rel(out, oracle.attention(q, kc, vc, seq, maxs, H, KVH, hd, scale)) < 1e-5
 
 
-def test_attention_fp16_kv(tq, oracle):
+@pytest.mark.parametrize("H,KVH,hd,seq,maxs", [(32, 8, 128, 4095, 4096), (32, 8, 128, 77, 4096),
+                                              (8, 2, 64, 301, 512), (28, 4, 64, 333, 512),
+                                              (16, 8, 128, 1000, 1024), (8, 8, 32, 5, 64)])
+def test_attention_fp16_kv(tq, oracle, H, KVH, hd, seq, maxs):
     # the reference's fp16-KV check: store halves, decode, attention_decode_ref
-    # (tests/test_attention.cpp:192-226)
-    H, KVH, hd, seq, maxs = 32, 8, 128, 4095, 4096
+    # (tests/test_attention.cpp:192-226); shapes with partial tiles and groups of 1-8 heads
     q, kc, vc = gc.attn_case(H, KVH, hd, seq, maxs)
     k16, v16 = kc.astype(np.float16).view(np.uint16), vc.astype(np.float16).view(np.uint16)
     scale = float(np.float32(1.0) / np.sqrt(np.float32(hd)))

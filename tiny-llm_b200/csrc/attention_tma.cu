@@ -96,6 +96,26 @@ __device__ __forceinline__ void lds_kv(const uint16_t *p, float o[D]) {
     }
 }
 
+// D consecutive 16-bit cache elements as one register load (staged rows)
+template <int D> struct Raw16 { using T = uint16_t; };
+template <> struct Raw16<2> { using T = uint32_t; };
+template <> struct Raw16<4> { using T = uint2; };
+template <int D>
+__device__ __forceinline__ typename Raw16<D>::T ld_raw16(const uint16_t *p) {
+    return *reinterpret_cast<const typename Raw16<D>::T *>(p);
+}
+template <int D>
+__device__ __forceinline__ void raw16_to_f(typename Raw16<D>::T v, float o[D]) {
+    if constexpr (D == 4) {
+        o[0] = h2f((uint16_t)(v.x & 0xFFFFu)), o[1] = h2f((uint16_t)(v.x >> 16));
+        o[2] = h2f((uint16_t)(v.y & 0xFFFFu)), o[3] = h2f((uint16_t)(v.y >> 16));
+    } else if constexpr (D == 2) {
+        o[0] = h2f((uint16_t)(v & 0xFFFFu)), o[1] = h2f((uint16_t)(v >> 16));
+    } else {
+        o[0] = h2f(v);
+    }
+}
+
 // Reduce-scatter of N per-lane values over the warp: after it, v[0] of lane l is
 // the warp-wide sum of value (l >> (5 - log2 N)); N is a power of two <= 32.
 template <int N, int OFF>
@@ -249,7 +269,7 @@ __device__ __forceinline__ void norm_rope_warp(float *x, const float *nw, float 
 }
 
 template <typename KV, int HD, int G>
-__global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constant__ TmaAttnParams P) {
+__global__ void __launch_bounds__(kThreads, 2) attn_tma_kernel(const __grid_constant__ TmaAttnParams P) {
     namespace cg = cooperative_groups;
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int RB = HD * (int)sizeof(KV);  // bytes per cached row
@@ -281,6 +301,7 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
     float *wgt = pl + G;                                        // [ns][G] merge weights (+ m, l copies)
     __shared__ float s_m[G], s_l[G];
     __shared__ float s_cw[kWarps * G];  // CTA merge weights
+    __shared__ __align__(16) float s_p[kWarps][32];  // each warp's p values, read as broadcasts
     __shared__ int s_err, s_issued;
     __shared__ int s_done[kStages];  // warps finished with the slot's current tile
 
@@ -391,57 +412,130 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
 
     // ---- rows -> (m, l, o) per warp, flash-decoding style: warp w takes rows
     // [w*RPW, (w+1)*RPW) of every tile, RW at a time (one reduce-scatter for their
-    // scores), and keeps an online softmax per head: m, l and o = sum p v with lanes
-    // over head dimensions.  No block barrier per tile: each warp waits for the tile
-    // itself and the last warp done with a slot refills it.
+    // scores), and keeps an online softmax per head.  Lane l serves head l % GP: it holds
+    // the head's running max m (the same in all of the head's lanes) and its own share of
+    // the head's sum l (the shares are added once, after the last tile); o = sum p v has
+    // lanes over head dimensions.  No block barrier per tile: each warp waits for the tile
+    // itself and the last warp done with a slot refills it.  With a 16-bit cache (and a
+    // group that fits 32 registers) a warp first copies its rows to registers and gives
+    // the slot back, so the refill's latency overlaps the arithmetic.
     constexpr int GP = Pow2<G>::v;
     constexpr int RW = 32 / GP;
+    constexpr bool kStage = sizeof(KV) == 2 && 2 * RW * ((D + 1) / 2) <= 32;  // <= 32 registers
     const int RPW = T / kWarps;
-    float m_[G], l_[G], acc[G][D];
+    const int gl = lane & (GP - 1);
+    float m_lane = -INFINITY, l_lane = 0.0f, acc[G][D];
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-        m_[g] = -INFINITY;
-        l_[g] = 0.0f;
+    for (int g = 0; g < G; ++g)
 #pragma unroll
         for (int d = 0; d < D; ++d) acc[g][d] = 0.0f;
-    }
-    // one group of nrows <= RW rows (K rows kr, V rows vr): scores, online update, P.V
-    auto group = [&](const KV *kr, const KV *vr, int nrows) {
-        const float s = score_lane<KV, HD, G>(kr, nrows, qr, lane, P.scale);  // -inf: no row
-        const int gl = lane & (GP - 1);
+    float *pbuf = s_p[warp];
+    // the last warp done with slot sl refills it with tile it + NST
+    auto release = [&](int sl, int it) {
+        __syncwarp();
+        if (lane == 0) {
+            __threadfence_block();
+            if (atomicAdd(&s_done[sl], 1) == kWarps - 1) {
+                s_done[sl] = 0;
+                if (it + NST < total) issue(it + NST);
+            }
+        }
+    };
+    // online update with this lane's score s (row lane / GP, head gl; -inf: no row):
+    // returns p = exp(s - m) and rescales o.  Fast exponentials (ex2.approx, ~2^-21
+    // relative): the online softmax's terms only need fp32-level accuracy.
+    auto online = [&](float s) -> float {
         float mx = s;
 #pragma unroll
         for (int o = GP; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        float mn[G], alpha[G];
-        float m_own = -INFINITY;
+        const float mn = fmaxf(m_lane, mx);
+        const float alpha = m_lane == -INFINITY ? 0.0f : __expf(m_lane - mn);
+        const float p = s == -INFINITY ? 0.0f : __expf(s - mn);
+        l_lane = fmaf(l_lane, alpha, p);
+        m_lane = mn;
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-            mn[g] = fmaxf(m_[g], __shfl_sync(0xffffffffu, mx, g));
-            alpha[g] = m_[g] == -INFINITY ? 0.0f : __expf(m_[g] - mn[g]);
-            if (gl == g) m_own = mn[g];
+            const float ag = __shfl_sync(0xffffffffu, alpha, g);
+#pragma unroll
+            for (int d = 0; d < D; ++d) acc[g][d] *= ag;
         }
-        // fast exponentials (ex2.approx, ~2^-21 relative): the online softmax's terms only
-        // need fp32-level accuracy, not the last bit of expf
-        const float p = s == -INFINITY ? 0.0f : __expf(s - m_own);
-        float ps = p;
+        __syncwarp();  // the previous group's reads of pbuf are done
+        pbuf[lane] = p;
+        __syncwarp();
+        return p;
+    };
+    // o += p(row r, g) * v for every head g; p read back from pbuf as broadcasts
+    auto pv_row = [&](int r, const float (&v)[D]) {
+        float pr[GP];
+        if constexpr (GP >= 4) {
 #pragma unroll
-        for (int o = GP; o < 32; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-            l_[g] = fmaf(l_[g], alpha[g], __shfl_sync(0xffffffffu, ps, g));
-            m_[g] = mn[g];
-#pragma unroll
-            for (int d = 0; d < D; ++d) acc[g][d] *= alpha[g];
-        }
-        for (int r = 0; r < nrows; ++r) {
-            float v[D];
-            lds_kv<D>(vr + (size_t)r * HD + lane * D, v);
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-                const float pr = __shfl_sync(0xffffffffu, p, r * GP + g);
-#pragma unroll
-                for (int d = 0; d < D; ++d) acc[g][d] = fmaf(pr, v[d], acc[g][d]);
+            for (int j = 0; j < GP; j += 4) {
+                const float4 t = *reinterpret_cast<const float4 *>(pbuf + r * GP + j);
+                pr[j] = t.x, pr[j + 1] = t.y, pr[j + 2] = t.z, pr[j + 3] = t.w;
             }
+        } else if constexpr (GP == 2) {
+            const float2 t = *reinterpret_cast<const float2 *>(pbuf + r * 2);
+            pr[0] = t.x, pr[1] = t.y;
+        } else {
+            pr[0] = pbuf[r];
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int d = 0; d < D; ++d) acc[g][d] = fmaf(pr[g], v[d], acc[g][d]);
+    };
+    // one group of nrows <= RW rows (K rows kr, V rows vr): scores, online update, P.V;
+    // rel_sl >= 0: give ring slot rel_sl back (tile rel_it) once the rows are read
+    auto group = [&](const KV *kr, const KV *vr, int nrows, int rel_sl, int rel_it) {
+        if constexpr (kStage) {
+            using R = typename Raw16<D>::T;
+            R kw[RW], vw[RW];
+#pragma unroll
+            for (int r = 0; r < RW; ++r) {
+                if (r < nrows) {
+                    kw[r] = ld_raw16<D>(reinterpret_cast<const uint16_t *>(kr) + (size_t)r * HD + lane * D);
+                    vw[r] = ld_raw16<D>(reinterpret_cast<const uint16_t *>(vr) + (size_t)r * HD + lane * D);
+                } else {
+                    kw[r] = R{};
+                    vw[r] = R{};
+                }
+            }
+            if (rel_sl >= 0) release(rel_sl, rel_it);
+            float a32[32];
+#pragma unroll
+            for (int r = 0; r < RW; ++r) {
+                float k[D];
+                raw16_to_f<D>(kw[r], k);
+#pragma unroll
+                for (int g = 0; g < GP; ++g) {
+                    float a = 0.0f;
+                    if (g < G) {
+#pragma unroll
+                        for (int d = 0; d < D; ++d) a = fmaf(qr[g][d], k[d], a);
+                    }
+                    a32[r * GP + g] = a;
+                }
+            }
+            warp_reduce_scatter<32, 16>(a32, lane);
+            const float s = (lane / GP < nrows && gl < G) ? a32[0] * P.scale : -INFINITY;
+            online(s);
+#pragma unroll
+            for (int r = 0; r < RW; ++r) {
+                if (r < nrows) {
+                    float v[D];
+                    raw16_to_f<D>(vw[r], v);
+                    pv_row(r, v);
+                }
+            }
+        } else {
+            const float s = score_lane<KV, HD, G>(kr, nrows, qr, lane, P.scale);  // -inf: no row
+            online(s);
+            for (int r = 0; r < nrows; ++r) {
+                float v[D];
+                lds_kv<D>(vr + (size_t)r * HD + lane * D, v);
+                pv_row(r, v);
+            }
+            if (rel_sl >= 0) release(rel_sl, rel_it);
         }
     };
     if (!s_err) {
@@ -454,19 +548,18 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
             const KV *kt = reinterpret_cast<const KV *>(ring + (size_t)sl * 2 * T * RB);
             const KV *vt = kt + (size_t)T * HD;
             const int rows = min(T, n_copy - it * T);
-            for (int rb = warp * RPW; rb < min(rows, (warp + 1) * RPW); rb += RW)
-                group(kt + (size_t)rb * HD, vt + (size_t)rb * HD, min(RW, min(rows, (warp + 1) * RPW) - rb));
-            __syncwarp();
-            if (lane == 0) {
-                __threadfence_block();
-                if (atomicAdd(&s_done[sl], 1) == kWarps - 1) {  // last warp on this slot
-                    s_done[sl] = 0;
-                    if (it + NST < total) issue(it + NST);
-                }
-            }
+            const int r_beg = warp * RPW, r_end = min(rows, (warp + 1) * RPW);
+            for (int rb = r_beg; rb < r_end; rb += RW)
+                group(kt + (size_t)rb * HD, vt + (size_t)rb * HD, min(RW, r_end - rb),
+                      rb + RW >= r_end ? sl : -1, it);
+            if (r_beg >= r_end) release(sl, it);  // no rows of this tile for this warp
         }
-        if (owner && warp == kWarps - 1 && !s_err) group(lastk, lastv, 1);  // the new row
+        if (owner && warp == kWarps - 1 && !s_err) group(lastk, lastv, 1, -1, 0);  // the new row
     }
+    // the head's lanes' shares of l; lanes g < G then hold head g's (m, l)
+    float l_head = l_lane;
+#pragma unroll
+    for (int o = GP; o < 32; o <<= 1) l_head += __shfl_xor_sync(0xffffffffu, l_head, o);
     __syncthreads();  // every warp is past the ring: it now holds the partials
     // dependents (the next projection) start their weight prefetch now, not earlier:
     // their copies would compete with this kernel's cache reads
@@ -485,12 +578,9 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const __grid_constan
         __syncthreads();
     }
     // ---- warps' partials -> this CTA's partial (m, l, o) in its own shared memory
-    if (lane == 0) {
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-            wpm[warp * G + g] = err ? -INFINITY : m_[g];
-            wpl[warp * G + g] = err ? 0.0f : l_[g];
-        }
+    if (lane < G) {
+        wpm[warp * G + lane] = err ? -INFINITY : m_lane;
+        wpl[warp * G + lane] = err ? 0.0f : l_head;
     }
 #pragma unroll
     for (int g = 0; g < G; ++g)
