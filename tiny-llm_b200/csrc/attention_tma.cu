@@ -10,16 +10,17 @@
 //
 // Grid (n_kv_heads, ns) in clusters of (1, ns): the ns CTAs of a KV head form one
 // thread-block cluster.  CTA rank s owns positions [s*chunk, s*chunk+n) of its KV
-// head for the G query heads that share it.  Thread 0 streams the chunk's K rows
-// and then its V rows through a ring of shared-memory tiles (one cp.async.bulk per
-// tile, completion on an mbarrier).  Scores: a warp takes 32/G cached rows at a time,
-// lanes over head dimensions, and reduces their G dot products each (32 values)
-// across the warp with one reduce-scatter.  Exact max/sum softmax over
-// the chunk, P.V with threads over (dimension quad, row subset).  Each CTA leaves
-// its (m, l, o) in its own shared memory; after a cluster barrier every CTA merges
-// a slice of the output by reading the other ranks' partials over DSMEM (weights
-// exp(m_s - M) per split and head), and a second cluster barrier keeps the
-// partials alive until every rank has read them.  No global scratch, no atomics.
+// head for the G query heads that share it.  The chunk streams through a ring of
+// shared-memory tiles, a tile being the K and V rows of T positions (two
+// cp.async.bulk copies, completion on the slot's mbarrier); the last warp done with
+// a slot issues its next tile.  Flash-decoding inside the CTA: each warp takes its
+// rows of every tile 32/G at a time, forms their G dot products per row with lanes
+// over head dimensions and one warp reduce-scatter, and keeps an online softmax and
+// o = sum p v per head.  The warps' (m, l, o) are combined in shared memory; each CTA
+// then pushes its partial of output slice r, and its (m, l), into cluster rank r's
+// shared memory (DSMEM stores), and after one cluster barrier every rank merges its
+// own slice (weights exp(m_s - M) per split and head).  No global scratch, no atomics
+// on data.
 //
 // Ordering (programmatic dependent launch): rows [0, seq-1) of the cache were
 // written by earlier steps and *pos at the start of this step, both complete once
@@ -138,67 +139,11 @@ __device__ __forceinline__ void warp_reduce_scatter(float *v, int lane) {
 template <int G> struct Pow2 { static constexpr int v = G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8; };
 template <int N> struct Log2 { static constexpr int v = N <= 1 ? 0 : N <= 2 ? 1 : N <= 4 ? 2 : 3; };
 
-// Scores of one cached row (warp-cooperative): sc[row*G + g] = scale * q_g . k
-template <typename KV, int HD, int G>
-__device__ __forceinline__ void score_row(const KV *kr, const float (&qr)[G][HD / 32], int lane,
-                                          float scale, float *sc_row) {
-    constexpr int D = HD / 32;
-    constexpr int GP = Pow2<G>::v;
-    float k[D];
-    lds_kv<D>(kr + lane * D, k);
-    float acc[GP];
-#pragma unroll
-    for (int g = 0; g < GP; ++g) {
-        acc[g] = 0.0f;
-        if (g < G) {
-#pragma unroll
-            for (int d = 0; d < D; ++d) acc[g] = fmaf(qr[g][d], k[d], acc[g]);
-        }
-    }
-    warp_reduce_scatter<GP, 16>(acc, lane);
-    constexpr int SH = 5 - Log2<GP>::v;
-    const int g = lane >> SH;
-    if ((lane & ((1 << SH) - 1)) == 0 && g < G) sc_row[g] = acc[0] * scale;
-}
-
 // Scores of RW = 32/GP consecutive cached rows at once (warp-cooperative): every lane
 // forms the partial dots of its HD/32 dimensions for all RW rows and G heads (32
 // values), and one 5-level reduce-scatter leaves lane l with the full dot of row
-// l / GP, head l % GP: 31 shuffles in 5 dependent steps for RW rows instead of
-// ~6 dependent steps per row.  Rows at or past `rows` are skipped.
-template <typename KV, int HD, int G>
-__device__ __forceinline__ void score_rows(const KV *kr, int rows, const float (&qr)[G][HD / 32],
-                                           int lane, float scale, float *sc_rows) {
-    constexpr int D = HD / 32;
-    constexpr int GP = Pow2<G>::v;
-    constexpr int RW = 32 / GP;
-    float acc[32];
-#pragma unroll
-    for (int r = 0; r < RW; ++r) {
-        float k[D];
-        if (r < rows) {
-            lds_kv<D>(kr + (size_t)r * HD + lane * D, k);
-        } else {
-#pragma unroll
-            for (int d = 0; d < D; ++d) k[d] = 0.0f;
-        }
-#pragma unroll
-        for (int g = 0; g < GP; ++g) {
-            float a = 0.0f;
-            if (g < G) {
-#pragma unroll
-                for (int d = 0; d < D; ++d) a = fmaf(qr[g][d], k[d], a);
-            }
-            acc[r * GP + g] = a;
-        }
-    }
-    warp_reduce_scatter<32, 16>(acc, lane);
-    const int r = lane / GP, g = lane - r * GP;
-    if (r < rows && g < G) sc_rows[r * G + g] = acc[0] * scale;
-}
-
-// As score_rows, but each lane returns its value (scale * q_g . k of row lane / GP,
-// head lane % GP), -inf for lanes past `rows` or G.
+// l / GP, head l % GP: 31 shuffles in 5 dependent steps for RW rows.  Each lane returns
+// its value scaled, -inf for lanes past `rows` or G.
 template <typename KV, int HD, int G>
 __device__ __forceinline__ float score_lane(const KV *kr, int rows, const float (&qr)[G][HD / 32],
                                             int lane, float scale) {
