@@ -754,19 +754,30 @@ __global__ void embed_kernel(const void *__restrict__ table, int dtype, const in
 // ------------------------------------------------------------------ MoE prefill
 // Router logits of many tokens (f32 router): logits[t][e] = W[e] . xn[t] with the
 // products and the sum in double (matvec_f32_ref, kernels/matvec/matvec_f32_ref.cpp),
-// xn already normalised.  CTA = 16 tokens x 32 experts, K staged through shared memory
-// in chunks, widened to double once at staging (conversions are slow); thread = one
-// token, two experts, two accumulation chains each.
+// xn already normalised.  On the FP64 tensor cores: a product of two floats is exact in
+// double and the m8n8k4 f64 MMA accumulates in double, so only the summation order
+// differs from the reference's (relative 1e-16 before the final rounding to float).
+// CTA = 16 tokens x 32 experts, K staged through shared memory in chunks of 64, widened
+// to double once at staging; warp w owns the 8 x 8 output block (tokens (w & 1) * 8,
+// experts (w >> 1) * 8) with two accumulator pairs (even and odd k steps).
 constexpr int kRrTok = 16, kRrExp = 32, kRrK = 64;
+constexpr int kRrPad = kRrK + 4;  // row stride in doubles: the 8 x 4 fragment loads hit 16 bank pairs
+
+__device__ __forceinline__ void dmma_8x8x4(double (&d)[2], double a, double b) {
+    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};\n"
+                 : "+d"(d[0]), "+d"(d[1])
+                 : "d"(a), "d"(b));
+}
 
 __global__ void __launch_bounds__(256) router_rows_kernel(const float *__restrict__ xn, int n, int H,
                                                           const float *__restrict__ W, int E,
                                                           float *__restrict__ logits) {
-    __shared__ double xs[kRrTok][kRrK + 1];
-    __shared__ double ws[kRrExp][kRrK + 1];
-    const int tid = threadIdx.x;
+    __shared__ double xs[kRrTok][kRrPad];
+    __shared__ double ws[kRrExp][kRrPad];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int t0 = blockIdx.y * kRrTok, e0 = blockIdx.x * kRrExp;
-    const int tt = tid & 15, te = tid >> 4;
+    const int tb = (warp & 1) * 8, eb = (warp >> 1) * 8;
+    const int fr = lane >> 2, fc = lane & 3;  // fragment row (token / expert), k column
     constexpr int RX = kRrTok * kRrK / 256, RW = kRrExp * kRrK / 256;
     float px[RX], pw[RW];  // the next chunk, loaded while this one is consumed
     auto fetch = [&](int k0) {
@@ -782,7 +793,7 @@ __global__ void __launch_bounds__(256) router_rows_kernel(const float *__restric
         }
     };
     fetch(0);
-    double a0 = 0.0, a1 = 0.0, b0 = 0.0, b1 = 0.0;  // two chains per output
+    double acc0[2] = {0.0, 0.0}, acc1[2] = {0.0, 0.0};
     for (int k0 = 0; k0 < H; k0 += kRrK) {
         __syncthreads();
 #pragma unroll
@@ -791,19 +802,20 @@ __global__ void __launch_bounds__(256) router_rows_kernel(const float *__restric
         for (int r = 0; r < RW; ++r) ws[(tid + 256 * r) / kRrK][(tid + 256 * r) % kRrK] = (double)pw[r];
         __syncthreads();
         if (k0 + kRrK < H) fetch(k0 + kRrK);
-#pragma unroll 8
-        for (int c = 0; c < kRrK; c += 2) {
-            const double x0 = xs[tt][c], x1 = xs[tt][c + 1];
-            a0 = fma(ws[te][c], x0, a0);
-            a1 = fma(ws[te][c + 1], x1, a1);
-            b0 = fma(ws[te + 16][c], x0, b0);
-            b1 = fma(ws[te + 16][c + 1], x1, b1);
+#pragma unroll
+        for (int kk = 0; kk < kRrK; kk += 8) {
+            dmma_8x8x4(acc0, xs[tb + fr][kk + fc], ws[eb + fr][kk + fc]);
+            dmma_8x8x4(acc1, xs[tb + fr][kk + 4 + fc], ws[eb + fr][kk + 4 + fc]);
         }
     }
-    const int t = t0 + tt;
+    // D fragment: row lane >> 2 (token), columns (lane & 3) * 2 + {0, 1} (experts)
+    const int t = t0 + tb + fr;
     if (t < n) {
-        if (e0 + te < E) logits[(size_t)t * E + e0 + te] = (float)(a0 + a1);
-        if (e0 + te + 16 < E) logits[(size_t)t * E + e0 + te + 16] = (float)(b0 + b1);
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int e = e0 + eb + fc * 2 + i;
+            if (e < E) logits[(size_t)t * E + e] = (float)(acc0[i] + acc1[i]);
+        }
     }
 }
 
