@@ -151,6 +151,88 @@ __global__ void qk_rope_kv_kernel(float *__restrict__ q, const float *__restrict
     }
 }
 
+// The same step with one warp per head (head_dim <= 256), eight heads per CTA: the
+// lane holds elements i and i + head_dim/2 for i = lane + 32e in registers, the
+// sum of squares is a warp sum in double, and the norm and rotation are the same
+// float operations as the per-CTA form.  Grid (ceil(heads / 8), tokens).
+constexpr int kQrWarps = 8, kQrMaxE = 4;
+
+template <typename KV>
+__global__ void __launch_bounds__(kQrWarps * 32) qk_rope_kv_warp_kernel(
+    float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
+    const float *__restrict__ q_norm, const float *__restrict__ k_norm, float eps,
+    const float *__restrict__ cos_tab, const float *__restrict__ sin_tab,
+    const int *__restrict__ pos_p, KV *__restrict__ kcache, KV *__restrict__ vcache, int n_heads,
+    int n_kv_heads, int head_dim, int max_seq) {
+    const int lane = threadIdx.x & 31;
+    const int h = blockIdx.x * kQrWarps + (threadIdx.x >> 5);
+    if (h >= n_heads + 2 * n_kv_heads) return;
+    const int pos = *pos_p + blockIdx.y;  // token blockIdx.y of consecutive rows
+    q += (size_t)blockIdx.y * n_heads * head_dim;
+    k += (size_t)blockIdx.y * n_kv_heads * head_dim;
+    v += (size_t)blockIdx.y * n_kv_heads * head_dim;
+    if (h >= n_heads + n_kv_heads) {  // value head: plain store
+        const int kh = h - n_heads - n_kv_heads;
+        KV *dst = vcache + ((size_t)kh * max_seq + pos) * head_dim;
+        for (int i = lane; i < head_dim; i += 32) {
+            const float val = v[kh * head_dim + i];
+            if constexpr (sizeof(KV) == 2) dst[i] = f2h_ref(val);
+            else dst[i] = val;
+        }
+        return;
+    }
+    const bool is_q = h < n_heads;
+    const float *src = is_q ? q + (size_t)h * head_dim : k + (size_t)(h - n_heads) * head_dim;
+    const float *nw = is_q ? q_norm : k_norm;
+    const int half = head_dim / 2;
+    float x0[kQrMaxE], x1[kQrMaxE];
+#pragma unroll
+    for (int e = 0; e < kQrMaxE; ++e) {
+        const int i = lane + 32 * e;
+        x0[e] = i < half ? src[i] : 0.0f;
+        x1[e] = i < half ? src[i + half] : 0.0f;
+    }
+    if (nw) {
+        double ss = 0.0;
+#pragma unroll
+        for (int e = 0; e < kQrMaxE; ++e) ss += (double)x0[e] * (double)x0[e] + (double)x1[e] * (double)x1[e];
+        ss = warp_sum_d(ss);
+        const float mean_sq = (float)(ss / head_dim);
+        const float scale = 1.0f / sqrtf(__fadd_rn(mean_sq, eps));
+#pragma unroll
+        for (int e = 0; e < kQrMaxE; ++e) {
+            const int i = lane + 32 * e;
+            if (i < half) {
+                x0[e] = __fmul_rn(__fmul_rn(x0[e], scale), nw[i]);
+                x1[e] = __fmul_rn(__fmul_rn(x1[e], scale), nw[i + half]);
+            }
+        }
+    }
+    const float *cs = cos_tab + (size_t)pos * half;
+    const float *sn = sin_tab + (size_t)pos * half;
+    float *qd = q + (size_t)h * head_dim;
+    KV *kd = is_q ? nullptr : kcache + ((size_t)(h - n_heads) * max_seq + pos) * head_dim;
+#pragma unroll
+    for (int e = 0; e < kQrMaxE; ++e) {
+        const int i = lane + 32 * e;
+        if (i < half) {
+            const float c = cs[i], sv = sn[i];
+            const float r0 = __fsub_rn(__fmul_rn(x0[e], c), __fmul_rn(x1[e], sv));
+            const float r1 = __fadd_rn(__fmul_rn(x1[e], c), __fmul_rn(x0[e], sv));
+            if (is_q) {
+                qd[i] = r0;
+                qd[i + half] = r1;
+            } else if constexpr (sizeof(KV) == 2) {
+                kd[i] = f2h_ref(r0);
+                kd[i + half] = f2h_ref(r1);
+            } else {
+                kd[i] = r0;
+                kd[i + half] = r1;
+            }
+        }
+    }
+}
+
 // ------------------------------------------------------------------ attention
 __device__ __forceinline__ void load4(const float *p, float o[4]) {
     const float4 v = *reinterpret_cast<const float4 *>(p);
@@ -927,7 +1009,23 @@ int launch_qk_rope_kv(const QkRopeKvArgs &a, cudaStream_t st) {
     TQ_CHECK_ARG(a.head_dim <= 512 && a.head_dim % 2 == 0 && a.head_dim / 2 <= 4 * 128,
                  "head_dim %d", a.head_dim);
     TQ_CHECK_ARG(a.n_tokens >= 1 && a.n_tokens <= 65535, "qk_rope_kv: %d tokens", a.n_tokens);
-    const dim3 blocks(a.n_heads + 2 * a.n_kv_heads, a.n_tokens);
+    const int nh = a.n_heads + 2 * a.n_kv_heads;
+    if (a.head_dim / 2 <= 32 * kQrMaxE) {
+        const dim3 grid((nh + kQrWarps - 1) / kQrWarps, a.n_tokens);
+        if (a.kv_fp16)
+            qk_rope_kv_warp_kernel<uint16_t><<<grid, kQrWarps * 32, 0, st>>>(
+                a.q, a.k, a.v, a.q_norm, a.k_norm, a.eps, a.cos_tab, a.sin_tab, a.pos,
+                (uint16_t *)a.kcache, (uint16_t *)a.vcache, a.n_heads, a.n_kv_heads, a.head_dim,
+                a.max_seq);
+        else
+            qk_rope_kv_warp_kernel<float><<<grid, kQrWarps * 32, 0, st>>>(
+                a.q, a.k, a.v, a.q_norm, a.k_norm, a.eps, a.cos_tab, a.sin_tab, a.pos,
+                (float *)a.kcache, (float *)a.vcache, a.n_heads, a.n_kv_heads, a.head_dim,
+                a.max_seq);
+        TQ_CUDA_TRY(cudaGetLastError());
+        return TQB200_OK;
+    }
+    const dim3 blocks(nh, a.n_tokens);
     if (a.kv_fp16)
         qk_rope_kv_kernel<uint16_t><<<blocks, 128, 0, st>>>(
             a.q, a.k, a.v, a.q_norm, a.k_norm, a.eps, a.cos_tab, a.sin_tab, a.pos,
