@@ -60,6 +60,46 @@ __global__ void rmsnorm_rows_kernel(const float *__restrict__ x, const float *__
     for (int i = threadIdx.x; i < n; i += blockDim.x) yr[i] = __fmul_rn(__fmul_rn(xr[i], scale), w[i]);
 }
 
+// The same with the row held in registers as float4s (n % 4 == 0, n <= 4 * 4 * 256,
+// 16-byte aligned rows): x is read once.  Same double sum of squares and float
+// operations; in place (y == x) is safe, each thread writing only what it read.
+constexpr int kRmsV = 4;  // float4s per thread
+
+__global__ void __launch_bounds__(256) rmsnorm_rows_v4_kernel(const float *__restrict__ x,
+                                                              const float *__restrict__ w,
+                                                              float *__restrict__ y, int n, float eps) {
+    __shared__ double sh[32];
+    const int n4 = n >> 2;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)blockIdx.x * n);
+    float4 *yr = reinterpret_cast<float4 *>(y + (size_t)blockIdx.x * n);
+    const float4 *w4 = reinterpret_cast<const float4 *>(w);
+    float4 v[kRmsV];
+    double ss = 0.0;
+#pragma unroll
+    for (int j = 0; j < kRmsV; ++j) {
+        const int i = threadIdx.x + 256 * j;
+        v[j] = i < n4 ? xr[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        ss += (double)v[j].x * (double)v[j].x;
+        ss += (double)v[j].y * (double)v[j].y;
+        ss += (double)v[j].z * (double)v[j].z;
+        ss += (double)v[j].w * (double)v[j].w;
+    }
+    ss = block_sum_d(ss, sh);
+    const float mean_sq = (float)(ss / n);
+    const float scale = 1.0f / sqrtf(__fadd_rn(mean_sq, eps));
+#pragma unroll
+    for (int j = 0; j < kRmsV; ++j) {
+        const int i = threadIdx.x + 256 * j;
+        if (i < n4) {
+            const float4 g = w4[i];
+            yr[i] = make_float4(__fmul_rn(__fmul_rn(v[j].x, scale), g.x),
+                                __fmul_rn(__fmul_rn(v[j].y, scale), g.y),
+                                __fmul_rn(__fmul_rn(v[j].z, scale), g.z),
+                                __fmul_rn(__fmul_rn(v[j].w, scale), g.w));
+        }
+    }
+}
+
 // Rotate-half RoPE with the position's cos/sin row (per-op entry point).  The row
 // comes from rope_row() on the host: the angle pos * powf(theta, -2i/hd) is so
 // ill-conditioned at long positions (a 1-ulp difference in powf moves cos by
@@ -979,7 +1019,11 @@ int launch_attn_kv(const AttnArgs &a, cudaStream_t st) {
 int launch_rmsnorm(const float *x, const float *w, float *y, int rows, int n, float eps,
                    cudaStream_t st) {
     TQ_CHECK_ARG(n > 0 && rows > 0, "rmsnorm n %d rows %d", n, rows);
-    rmsnorm_rows_kernel<<<rows, 256, 0, st>>>(x, w, y, n, eps);
+    const bool a16 = (((uintptr_t)x | (uintptr_t)w | (uintptr_t)y) & 15u) == 0;
+    if (a16 && n % 4 == 0 && n <= 4 * kRmsV * 256)
+        rmsnorm_rows_v4_kernel<<<rows, 256, 0, st>>>(x, w, y, n, eps);
+    else
+        rmsnorm_rows_kernel<<<rows, 256, 0, st>>>(x, w, y, n, eps);
     TQ_CUDA_TRY(cudaGetLastError());
     return TQB200_OK;
 }
