@@ -822,7 +822,7 @@ Shape plan(int K, int G, bool pair, bool norm, int rows_total, int r_div = 0) {
     // A pass costs a consumer barrier and a reduction, so a CTA's share of up to 100 KB
     // is one pass; larger shares go in at least three passes of at most 80 KB (the first
     // lands sooner and the later ones stream while it is computed; measured against two
-    // passes of 96 KB, four of 48 KB and 64 KB single passes on the config 4 step).
+    // passes of 96 KB, four of 48 KB and 64 KB single passes on the Qwen3-4B decode step).
     if ((size_t)per_cta * RB * np <= 100 * 1024) {
         L.R = per_cta;
     } else {

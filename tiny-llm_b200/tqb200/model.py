@@ -52,7 +52,8 @@ class ModelSpec:
                                       # l % expert_layers (host memory of a large MoE model)
 
 
-# The BASELINE shapes; vocab 151936 everywhere.
+# The benchmark configurations' model shapes (Qwen2.5-0.5B, Qwen3-4B, Qwen3-0.6B VQ2,
+# Qwen3-30B-A3B); vocab 151936 everywhere.
 QWEN25_05B = ModelSpec(name="qwen2.5-0.5b-i4", n_layers=24, hidden=896, inter=4864, n_heads=14,
                        n_kv_heads=2, head_dim=64, vocab=151936, max_seq_len=512, qkv_bias=True)
 QWEN3_4B = ModelSpec(name="qwen3-4b-i4", n_layers=36, hidden=2560, inter=9728, n_heads=32,
