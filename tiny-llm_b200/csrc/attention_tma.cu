@@ -213,8 +213,11 @@ __device__ __forceinline__ void norm_rope_warp(float *x, const float *nw, float 
     __syncwarp();
 }
 
+// 16-bit caches: at most 128 registers, so two CTAs fit an SM with the staged rows; the
+// fp32 instantiations keep the compiler's choice (all <= 127 but G=8 x HD 128 at 156,
+// whose 4-KV-head grids run one CTA per SM anyway).
 template <typename KV, int HD, int G>
-__global__ void __launch_bounds__(kThreads, 2) attn_tma_kernel(const __grid_constant__ TmaAttnParams P) {
+__global__ void __launch_bounds__(kThreads, sizeof(KV) == 2 ? 2 : 1) attn_tma_kernel(const __grid_constant__ TmaAttnParams P) {
     namespace cg = cooperative_groups;
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int RB = HD * (int)sizeof(KV);  // bytes per cached row
