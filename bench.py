@@ -200,6 +200,109 @@ def ref_matvec_rate(seconds: float, threads: int):
 
 
 # ------------------------------------------------------------------ workloads
+def matvec_graph_rate(tq, weights, x, M, K, G, reps: int, warmup: int):
+    """Device time of one tqb200_dev_matvec_i4 launch: a CUDA graph of one launch per
+    weight copy in `weights` (device tensors; together larger than L2, so every launch
+    streams its matrix from HBM), replayed `reps` times between CUDA events on the
+    launching stream.  Returns (us per launch, algorithmic GB/s, launches timed)."""
+    import torch
+    from tqb200 import lib
+    dev = torch.device("cuda")
+    dx = torch.from_numpy(x).to(dev)
+    dy = torch.empty(M, device=dev)
+    stream = torch.cuda.Stream()
+    sp = stream.cuda_stream
+
+    def launch_all():
+        for wi in weights:
+            st = tq.tqb200_dev_matvec_i4(wi.data_ptr(), dx.data_ptr(), dy.data_ptr(), M, K, G, sp)
+            if st:
+                raise lib.TQB200Error(st, tq.tqb200_last_error().decode())
+
+    with torch.cuda.stream(stream):
+        launch_all()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        launch_all()
+    torch.cuda.synchronize()
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    n = reps * len(weights)
+    per_s = e0.elapsed_time(e1) / 1e3 / n
+    algo = weights[0].numel() + K * 4 + M * 4
+    del graph
+    return per_s * 1e6, algo / per_s / 1e9, n
+
+
+def matvec_single_call_us(tq, weights, x, M, K, G, calls: int = 50) -> float:
+    """Median CUDA-event time of one launch by itself (no graph; rotating weight copies,
+    so each call streams a matrix that is not in L2)."""
+    import torch
+    dev = torch.device("cuda")
+    dx = torch.from_numpy(x).to(dev)
+    dy = torch.empty(M, device=dev)
+    stream = torch.cuda.Stream()
+    sp = stream.cuda_stream
+    ts = []
+    with torch.cuda.stream(stream):
+        for i in range(calls + 3):
+            wi = weights[i % len(weights)]
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            assert tq.tqb200_dev_matvec_i4(wi.data_ptr(), dx.data_ptr(), dy.data_ptr(), M, K, G, sp) == 0
+            e1.record(stream)
+            e1.synchronize()
+            if i >= 3:
+                ts.append(e0.elapsed_time(e1) * 1e3)
+    return float(np.median(ts))
+
+
+def matvec_extras(pk, warmup: int) -> dict:
+    """The metric's first clause beside a decode line: BASELINE config 1 (4864x896 g64,
+    64 distinct copies per graph, plus single-call latency) and an lm_head-shaped i4
+    matvec (151936x2560 g64, 218.8 MB per copy, two copies alternating)."""
+    import torch
+    from tqb200 import lib, synth
+    tq = lib.load()
+    dev = torch.device("cuda")
+    out = {}
+    w, x = synth.config1_matvec(0)
+    rng = np.random.default_rng(1)
+    ws = [torch.from_numpy(w).to(dev)] + [
+        torch.from_numpy(synth.random_i4(rng, 4864, 896, 64) if i < 4 else w).to(dev)
+        for i in range(1, 64)]
+    us, gbs, n = matvec_graph_rate(tq, ws, x, 4864, 896, 64, 20, max(3, warmup))
+    out["matvec_config1"] = {
+        "shape": "4864x896 g64", "GB_per_s": round(gbs, 1), "us_per_launch": round(us, 3),
+        "frac_of_hbm": round(gbs / pk["hbm_gbs"], 4), "launches_timed": n,
+        "single_call_us": round(matvec_single_call_us(tq, ws, x, 4864, 896, 64), 3),
+        "how": "CUDA graph of 64 launches over 64 distinct copies of W (157 MB > L2), "
+               "CUDA events around 20 replays; single_call_us = median event time of one "
+               "launch by itself"}
+    del ws
+    M, K = 151936, 2560
+    ws = [torch.from_numpy(synth.random_i4_fast(rng, M, K, 64)).to(dev) for _ in range(2)]
+    xl = rng.normal(size=K).astype(np.float32)
+    us, gbs, n = matvec_graph_rate(tq, ws, xl, M, K, 64, 10, max(3, warmup))
+    out["matvec_lm_head"] = {
+        "shape": "151936x2560 g64", "GB_per_s": round(gbs, 1), "us_per_launch": round(us, 2),
+        "frac_of_hbm": round(gbs / pk["hbm_gbs"], 4), "launches_timed": n,
+        "how": "CUDA graph of 2 launches over 2 distinct copies (218.8 MB each > L2), "
+               "CUDA events around 10 replays"}
+    del ws
+    torch.cuda.empty_cache()
+    return out
+
+
 def bench_matvec(args, rank, pg, pk, pk_kind):
     import torch
     from tqb200 import lib, synth
@@ -483,7 +586,7 @@ def bench_decode(args, rank, pg, pk, pk_kind):
     W, K = args.warmup, args.steps
     wl = DECODE_WORKLOADS[args.workload]
     ctx = args.ctx if args.ctx is not None else wl["ctx"]
-    max_seq = ctx + W + K + 32  # + the e2e (19) and profiled (1) steps after the timed region
+    max_seq = ctx + W + 2 * K + 32  # + the unstamped (K), e2e (19) and profiled (1) steps
     spec = decode_spec(wl, max_seq)
     if args.layers:
         from dataclasses import replace as _replace
@@ -502,7 +605,11 @@ def bench_decode(args, rank, pg, pk, pk_kind):
     first = int(rng.integers(0, spec.vocab))
     toks, _ = eng.generate(first, ctx - W)
     tok = toks[-1]
-    toks, _ = eng.generate(tok, W)   # warm-up steps (also captures the graph)
+    # the timed steps carry the in-graph timeline: every launch stamps the global timer
+    # (first CTA in, first CTA past its dependency wait, last CTA out), so the per-kernel
+    # times below come from the same graph replays as the step time
+    eng.set_timeline(K)
+    toks, _ = eng.generate(tok, W)   # warm-up steps (also captures the stamped graph)
     tok = toks[-1]
     torch.cuda.synchronize()
     clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
@@ -515,6 +622,15 @@ def bench_decode(args, rank, pg, pk, pk_kind):
     clk = clocks.stop()
     dev_ms = max_over_ranks(pg, dev_ms)
     ms_step = dev_ms / K
+    tl_steps, tl_span, tl = eng.timeline()
+    # the same K steps without stamps (the stamps' cost, for the record)
+    eng.set_timeline(0)
+    tok = toks[-1]
+    toks, _ = eng.generate(tok, W)
+    tok = toks[-1]
+    barrier(pg)
+    toks, plain_ms = eng.generate(tok, K)
+    plain_ms = max_over_ranks(pg, plain_ms) / K
 
     # e2e: the C-ABI step call with host token in / host token out, every step
     tok = toks[-1]
@@ -526,13 +642,21 @@ def bench_decode(args, rank, pg, pk, pk_kind):
     for _ in range(n_e2e):
         tok = eng.step(tok)
     e2e_ms = (time.perf_counter() - t0) * 1e3 / n_e2e
-    # live per-kernel times (one step launched kernel by kernel, CUDA events)
+    # serialized per-kernel times (one step launched kernel by kernel, CUDA events between
+    # launches, no PDL overlap): a diagnostic only, not the in-step times
     _, prof = eng.profile_step(tok)
     mvb = matvec_bytes_by_kind(spec)
-    mv_ms = sum(prof[k] for k in mvb)
     mv_bytes = sum(mvb.values())
+    # in-step time of each kind: the timed steps' timeline, max over ranks
+    excl = {k: max_over_ranks(pg, v[0]) for k, v in tl.items()}
+    mv_ms = sum(excl.get(k, 0.0) for k in mvb)
     achieved = mv_bytes / (mv_ms * 1e-3) / 1e9
-    total_bytes = step_bytes(spec, ctx, 2 if wl["kv16"] else 4)
+    kvb = 2 if wl["kv16"] else 4
+    total_bytes = step_bytes(spec, ctx, kvb)
+    kv_bytes = 2 * spec.n_layers * spec.n_kv_heads * ctx * spec.head_dim * kvb
+    attn_io = spec.n_layers * (3 * spec.n_heads * spec.head_dim + 2 * spec.n_kv_heads * spec.head_dim) * 4
+    attn_ms = excl.get("attention", 0.0)
+    step_achieved = total_bytes / (ms_step * 1e-3) / 1e9
     # embed, per layer qkv / attention (QK-norm, RoPE and KV append fused) / o_proj /
     # gate_up / down, lm_head (+argmax), the device-side token feed, and with tensor
     # parallelism the cross-rank argmax (NCCL's all-gather kernels are not counted)
@@ -563,8 +687,36 @@ def bench_decode(args, rank, pg, pk, pk_kind):
                                + " (all matvecs of a step)",
                      "algorithmic_bytes_per_step": int(mv_bytes),
                      "matvec_ms_per_step": round(mv_ms, 4),
+                     "how": "achieved = algorithmic_bytes_per_step / matvec_ms_per_step; "
+                            "matvec_ms_per_step = the matvec launches' in-step time in the timed "
+                            "steps (in-graph global-timer stamps, from the first CTA past the "
+                            "dependency wait to the last CTA out, summed per step, averaged "
+                            "over the timed steps)",
                      "step_vs_hbm_floor": round((total_bytes / (pk["hbm_gbs"] * 1e9) * 1e3) / ms_step, 4)},
-        "kernel_ms_by_kind": {k: round(v, 4) for k, v in prof.items()},
+        "rooflines": {
+            "attention": {"bound": "hbm", "achieved": round((kv_bytes + attn_io) / (attn_ms * 1e-3) / 1e9, 1)
+                          if attn_ms > 0 else None,
+                          "frac": round((kv_bytes + attn_io) / (attn_ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4)
+                          if attn_ms > 0 else None,
+                          "algorithmic_bytes_per_step": int(kv_bytes + attn_io),
+                          "attention_ms_per_step": round(attn_ms, 4),
+                          "kernel": "attn_tma_kernel (QK-norm, RoPE and KV append fused)"},
+            "step": {"bound": "hbm", "achieved": round(step_achieved, 1),
+                     "frac": round(step_achieved / pk["hbm_gbs"], 4),
+                     "algorithmic_bytes_per_step": int(total_bytes),
+                     "note": "every byte a step must read (weights, KV at the context, "
+                             "activations) over ms_per_step"}},
+        "timeline_ms_by_kind": {k: {"in_step_ms": round(v[0], 4), "from_launch_ms": round(v[1], 4),
+                                    "launches": v[2]} for k, v in tl.items()},
+        "timeline": {"steps": tl_steps, "stamped_span_ms": round(tl_span, 4),
+                     "in_step_ms_sum": round(sum(v[0] for v in tl.values()), 4),
+                     "unstamped_ms_per_step": round(plain_ms, 4),
+                     "note": "in_step_ms: first CTA past the dependency wait to last CTA out "
+                             "(no overlap between launches, so the sum <= ms_per_step); "
+                             "from_launch_ms: first CTA in to last CTA out (overlaps the "
+                             "previous kernel under programmatic dependent launch); the "
+                             "embed and token-feed kernels and NCCL's are not stamped"},
+        "kernel_ms_serialized": {k: round(v, 4) for k, v in prof.items() if v > 0},
         "clocks": clk,
         "gpu_launches": launches * K,
         "e2e": {"value": round(e2e_ms, 4), "unit": "ms/token", "h2d_bytes_per_step": 8,
@@ -572,6 +724,9 @@ def bench_decode(args, rank, pg, pk, pk_kind):
                 "note": "tqb200_engine_step per token: token+position H2D, next token+status D2H"},
     }
     eng.close()
+    del eng
+    if world == 1 and args.extras:
+        out.update(matvec_extras(pk, W))
     return out
 
 
@@ -863,6 +1018,8 @@ def main():
                     help="decode context in KV positions (default: the workload's)")
     ap.add_argument("--layers", type=int, default=None,
                     help="decode workloads: fewer layers than the model (small profiling cases)")
+    ap.add_argument("--no-extras", dest="extras", action="store_false",
+                    help="decode workloads: skip the config-1 and lm_head matvec keys")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 

@@ -142,7 +142,11 @@ int tqb200_attention_decode_f16kv(const float *q, const uint16_t *k_cache,
  * 4 MiB for one split or more than 256 KV heads are rejected with TQB200_ERR_INVALID_ARG, as
  * are k/v caches that are not 16-byte aligned.  Every call clears the tickets on its stream.
  * The first call on a device looks up the array's address, so make it outside any stream
- * capture.  All calls share the array: calls that overlap on the GPU race. */
+ * capture.  CUDA loads a library's device code lazily by default, so that first call is
+ * also when the driver loads this library's kernels and places the arrays in device
+ * memory: make it before reserving the rest of the device, or set
+ * CUDA_MODULE_LOADING=EAGER so that the arrays are placed when the library is loaded.
+ * All calls share the array: calls that overlap on the GPU race. */
 int tqb200_dev_attention_decode_noalloc(const float *q, const float *k_cache,
                                         const float *v_cache, int seq_len, int max_seq_len,
                                         int n_heads, int n_kv_heads, int head_dim, float scale,
@@ -231,6 +235,22 @@ int tqb200_engine_set_position(tqb200_engine *e, int pos);
 int tqb200_engine_stream(const tqb200_engine *e, void **stream);
 int tqb200_engine_kv_cache(const tqb200_engine *e, void **kv, size_t *bytes);
 int tqb200_engine_weight_bytes(const tqb200_engine *e, size_t *bytes);
+
+/* In-graph timeline of tqb200_engine_generate (no reference counterpart; the reference
+ * profiles a step op by op on the host, runtime/main.cpp --profile-out).  With a timeline
+ * set, the generate graph is captured again with every projection, attention, router and
+ * combine launch writing global-timer stamps (first CTA in, first CTA past its dependency
+ * wait, last CTA out) for each of the first max_steps steps of every generate() call;
+ * max_steps = 0 turns it off.  Needs use_graph.  The stamps cost two atomics per CTA. */
+int tqb200_engine_set_timeline(tqb200_engine *e, int max_steps);
+/* The last generate() call's timeline, averaged over its recorded steps: per kernel kind
+ * (the kinds of tqb200_engine_profile_step) excl_ms[k] sums, per step, the launches'
+ * times from the first CTA past the dependency wait to the last CTA out (these intervals
+ * do not overlap, so their sum is at most the step), incl_ms[k] the times from the first
+ * CTA in (which overlaps the previous kernel under programmatic dependent launch);
+ * launches[k] = launches of kind k per step; *span_ms = first stamped CTA in to last out. */
+int tqb200_engine_timeline(const tqb200_engine *e, int n_kinds, double *excl_ms, double *incl_ms,
+                           int *launches, int *steps, double *span_ms);
 
 #ifdef __cplusplus
 }

@@ -149,6 +149,8 @@ class Oracle(_Common):
         sig("tqo_model_reset", [_vp])
         sig("tqo_model_destroy", [_vp])
         sig("tqo_model_set_partial", [_vp, _i, _i])
+        sig("tqo_model_kv", [_vp, C.POINTER(C.c_size_t)], _vp)
+        sig("tqo_model_set_position", [_vp, _i], _i)
 
     def set_threads(self, n: int):
         self.lib.tqo_set_threads(n)
@@ -190,6 +192,7 @@ class OracleModel:
         self.orc = orc
         self.sm = sm  # keeps the weights alive
         self.vocab = sm.spec.vocab
+        self.kv_fp16 = kv_fp16
         self.h = orc.lib.tqo_model_create(C.byref(sm.desc), max_seq_len, 1 if kv_fp16 else 0)
 
     def step(self, token: int) -> int:
@@ -204,6 +207,17 @@ class OracleModel:
 
     def reset(self):
         self.orc.lib.tqo_model_reset(self.h)
+
+    def kv(self) -> np.ndarray:
+        """The KV arena as a writable numpy view (uint16 bits for fp16, else float32)."""
+        n = C.c_size_t()
+        p = self.orc.lib.tqo_model_kv(self.h, C.byref(n))
+        raw = np.ctypeslib.as_array(C.cast(p, C.POINTER(C.c_uint8)), shape=(n.value,))
+        return raw.view(np.uint16 if self.kv_fp16 else np.float32)
+
+    def set_position(self, pos: int):
+        if self.orc.lib.tqo_model_set_position(self.h, pos) != 0:
+            raise ValueError(f"position {pos} out of range")
 
     def close(self):
         if self.h:
@@ -244,6 +258,9 @@ class RefLib(_Common):
         self._topk = sig("tqref_topk_softmax", [_f, _i, _i, _i32, _f])
         self._f2h = sig("tqref_float_to_half", [_fl], C.c_uint16)
         self._h2f = sig("tqref_half_to_float", [C.c_uint16], _fl)
+        self._w4a8 = sig("tqref_matvec_i4_w4a8_naive", [_u8, _f, _f, _i, _i, _i])
+        self._pack_sym = sig("tqref_pack_i4_rtn_symmetric", [_f, _i, _i, _i, _u8])
+        self._random_vec = sig("tqref_random_vec", [C.c_size_t, C.c_uint32, _f])
         sig("tqref_model_open", [C.c_char_p, _i, _i, C.c_char_p, _i], _vp)
         sig("tqref_model_step", [_vp, _i], _i)
         sig("tqref_model_logits", [_vp], C.POINTER(C.c_float))
@@ -262,6 +279,25 @@ class RefLib(_Common):
     def float_to_half(self, a) -> np.ndarray:
         a = _f32(a).ravel()
         return np.array([self._f2h(float(v)) for v in a], np.uint16)
+
+    def matvec_i4_w4a8_naive(self, w, x, out_dim, in_dim, group_size):
+        """The reference test's symmetric W4A8 checker (tests/test_matvec_i4.cpp:252-306)."""
+        y = np.zeros(out_dim, np.float32)
+        self._w4a8(_u8a(w), _f32(x), y, out_dim, in_dim, group_size)
+        return y
+
+    def pack_i4_rtn_symmetric(self, w, out_dim, in_dim, group_size):
+        """The reference test's symmetric packer (tests/test_matvec_i4.cpp:403-438)."""
+        ng = (in_dim + group_size - 1) // group_size
+        dst = np.zeros(out_dim * ng * (4 + group_size // 2), np.uint8)
+        self._pack_sym(_f32(w).ravel(), out_dim, in_dim, group_size, dst)
+        return dst.reshape(out_dim, -1)
+
+    def random_vec(self, n, seed):
+        """The reference test's N(0,1) inputs (tests/test_matvec_i4.cpp:144-152)."""
+        out = np.zeros(n, np.float32)
+        self._random_vec(n, seed, out)
+        return out
 
     def open_model(self, path: str, max_seq_len: int, vocab: int, kv_fp16: bool = False):
         err = C.create_string_buffer(512)

@@ -675,6 +675,21 @@ const float *tqo_model_logits(const tqo_model *m) { return m->logits; }
 const float *tqo_model_hidden(const tqo_model *m) { return m->hidden; }
 void tqo_model_reset(tqo_model *m) { m->pos = 0; }
 
+/* The KV arena (KvCache layout [K|V][L][KVH][max_seq][hd], fp32 or binary16 bits) and its
+ * byte size, so a test can compare it with the engine's or load it from there. */
+void *tqo_model_kv(tqo_model *m, size_t *bytes) {
+    const size_t n = 2 * (size_t)m->d.n_layers * m->layer_stride;
+    if (bytes) *bytes = n * (m->kv_fp16 ? 2 : 4);
+    return m->kv_fp16 ? (void *)m->kv16 : (void *)m->kv32;
+}
+
+/* Position of the next step (KvCache::seq_len; rows below it must hold K/V). */
+int tqo_model_set_position(tqo_model *m, int pos) {
+    if (pos < 0 || pos >= m->max_seq_len) return -1;
+    m->pos = pos;
+    return 0;
+}
+
 void tqo_model_destroy(tqo_model *m) {
     if (!m) return;
     free(m->kv32);

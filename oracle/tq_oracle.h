@@ -62,6 +62,8 @@ int tqo_model_step(tqo_model *m, int token_id);           /* returns argmax id, 
 const float *tqo_model_logits(const tqo_model *m);        /* [vocab] of the last step */
 const float *tqo_model_hidden(const tqo_model *m);        /* residual stream after last step */
 void tqo_model_reset(tqo_model *m);
+void *tqo_model_kv(tqo_model *m, size_t *bytes);          /* KV arena, engine layout */
+int tqo_model_set_position(tqo_model *m, int pos);        /* 0, or -1 out of range */
 void tqo_model_destroy(tqo_model *m);
 /* Runs only layers [0, n_layers_run) and skips the head when head == 0: a bounded
  * sample of one step, used by the timed CPU baseline. */

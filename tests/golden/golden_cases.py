@@ -49,6 +49,9 @@ from tqb200 import synth  # noqa: E402
 
 I4_CASES = [(64, 256, 128), (64, 256, 64), (32, 200, 64), (33, 200, 48), (96, 384, 64)]
 VQ2_CASES = [(32, 128), (96, 384), (33, 200)]
+# symmetric W4A8: (rows, cols, weight seed, activation seed) of the reference's sdot5 tests
+# (tests/test_matvec_i4.cpp:441-477), inputs drawn by the reference test's random_vec
+W4A8_CASES = [(96, 384, 9901, 9902), (512, 896, 9903, 9904)]
 BIIP_CASES = [(896, 128, True), (896, 128, False), (4864, 256, True), (256, 64, True),
               (128, 128, False)]
 RMS_CASES = [896, 2560, 128]

@@ -77,6 +77,14 @@ def main():
         out[key + "_sha"] = _s(gc.sha(q, kc, vc))
         out[key + "_o"] = ref.attention(q, kc, vc, seq, maxs, H, KVH, hd,
                                         float(np.float32(1.0) / np.sqrt(np.float32(hd))))
+    # symmetric W4A8 ("sdot5"): the reference test's own inputs, symmetric packer and
+    # checker (tests/test_matvec_i4.cpp:441-477 use these seeds and shapes)
+    for (M, K, sw, sx) in gc.W4A8_CASES:
+        w = ref.pack_i4_rtn_symmetric(ref.random_vec(M * K, sw), M, K, 64)
+        x = ref.random_vec(K, sx)
+        key = f"w4a8_{M}x{K}"
+        out[key + "_w"], out[key + "_x"] = w, x
+        out[key + "_y"] = ref.matvec_i4_w4a8_naive(w, x, M, K, 64)
     g, u = gc.swiglu_case()
     out["swiglu_sha"], out["swiglu_y"] = _s(gc.sha(g, u)), ref.swiglu(g, u)
     l = gc.argmax_case()

@@ -10,7 +10,7 @@ import pytest
 
 import golden_cases as gc
 from conftest import max_rel
-from tqb200.model import QWEN25_05B, QWEN3_06B_VQ2, QWEN3_4B, SynthModel
+from tqb200.model import QWEN25_05B, QWEN3_06B_VQ2, QWEN3_4B, ModelSpec, SynthModel
 from dataclasses import replace
 
 pytestmark = pytest.mark.gpu
@@ -81,25 +81,16 @@ def test_config2_qwen25_05b_64_steps(tq, oracle):
     assert worst < TOL
 
 
-# fp16 KV at 36 layers: every K/V element is rounded to half precision, whose step
-# is 2^-11 of the value.  A last-bit float difference upstream (the engine sums a
-# matvec row in a different order than the oracle) can flip that rounding, a
-# relative change of up to ~4.9e-4 in one cached element; over 36 layers this lifts
-# the logits' max relative error to 1.5e-4 .. 2e-4 (it grows with depth, and is the
-# same with the engine's fp32-math matvec).  The fp16 case therefore keeps exact
-# greedy tokens and a 5e-4 bound; the fp32-KV case keeps 1e-4.
-TOL_F16KV_DEEP = 5e-4
-
-
-@pytest.mark.parametrize("kv16,tol", [(False, TOL), (True, TOL_F16KV_DEEP)], ids=["f32kv", "f16kv"])
-def test_config4_qwen3_4b(tq, oracle, kv16, tol):
-    """BASELINE config 4 shape (36 layers, hidden 2560, 32/8 heads), short run."""
+def test_config4_qwen3_4b_f32kv(tq, oracle):
+    """BASELINE config 4 shape (36 layers, hidden 2560, 32/8 heads) with an fp32 cache,
+    short run; the fp16-cache configuration as benchmarked is covered at length in
+    test_gpu_config4.py."""
     spec = replace(QWEN3_4B, weights="codes")
     sm = SynthModel(spec, seed=0)
     prompt = list(np.random.default_rng(1).integers(0, spec.vocab, 4))
-    toks, otoks, worst = _decode_compare(tq, oracle, sm, prompt, 4, 4096, kv16)
+    toks, otoks, worst = _decode_compare(tq, oracle, sm, prompt, 4, 4096, False)
     assert toks == otoks
-    assert worst < tol, worst
+    assert worst < TOL, worst
 
 
 def test_config3_qwen3_06b_vq2_step(tq, oracle):
@@ -108,5 +99,26 @@ def test_config3_qwen3_06b_vq2_step(tq, oracle):
     sm = SynthModel(QWEN3_06B_VQ2, seed=0)
     prompt = list(np.random.default_rng(3).integers(0, QWEN3_06B_VQ2.vocab, 8))
     toks, otoks, worst = _decode_compare(tq, oracle, sm, prompt, 8, 64, False)
+    assert toks == otoks
+    assert worst < TOL, worst
+
+
+def test_engine_outlier_channels(tq, oracle):
+    """Heavy-tailed activations through every fused prologue: RMSNorm weights of 1e3 and
+    1e4 on a few channels make the q/k/v and gate/up inputs span 4+ decades, and the
+    SwiGLU products feeding down (with its residual) heavier still.  Tokens identical,
+    logits within 1e-4 of the oracle."""
+    spec = ModelSpec(name="outliers", qk_norm=True, n_layers=4, hidden=1024, inter=3072,
+                     n_heads=8, n_kv_heads=2, head_dim=128, vocab=4096)
+    sm = SynthModel(spec, seed=7)
+    rng = np.random.default_rng(70)
+    for li in range(spec.n_layers):
+        for nm in ("input_layernorm", "post_attention_layernorm"):
+            w = sm.tensors[f"model.layers.{li}.{nm}.weight"].data
+            idx = rng.choice(spec.hidden, 6, replace=False)
+            w[idx[:3]] = 1e3
+            w[idx[3:]] = 1e4
+    prompt = [int(t) for t in rng.integers(0, spec.vocab, 6)]
+    toks, otoks, worst = _decode_compare(tq, oracle, sm, prompt, 6, 64, False)
     assert toks == otoks
     assert worst < TOL, worst

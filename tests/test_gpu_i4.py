@@ -70,6 +70,62 @@ def test_symmetric_w4a8_vs_naive(tq, oracle):
         assert np.abs(y.astype(np.float64) - ref).max() < 1e-4
 
 
+@pytest.mark.parametrize("M,K,sw,sx", gc.W4A8_CASES)
+def test_symmetric_w4a8_vs_reference_golden(tq, golden, M, K, sw, sx):
+    # the reference test's own inputs and checker output (golden from oracle/_ref):
+    # tests/test_matvec_i4.cpp:441-477 holds sdot5 to abs err < 1e-4 against it
+    key = f"w4a8_{M}x{K}"
+    y = tq.matvec_i4_sym(golden[key + "_w"], golden[key + "_x"], M, K, 64)
+    assert np.abs(y.astype(np.float64) - golden[key + "_y"]).max() < 1e-4
+
+
+def _heavy_tailed(rng, K, kind):
+    """Activation vectors whose magnitudes span several decades."""
+    x = rng.normal(size=K).astype(np.float32)
+    if kind == "spikes":        # a few channels 1e3x and 1e4x the rest (outlier channels)
+        idx = rng.choice(K, 8, replace=False)
+        x[idx[:4]] *= 1e3
+        x[idx[4:]] *= 1e4
+    elif kind == "swiglu":      # SwiGLU of N(0,3) gate and up: heavy-tailed products
+        g, u = rng.normal(0, 3, K), rng.normal(0, 3, K)
+        x = (g / (1.0 + np.exp(-g)) * u).astype(np.float32)
+    elif kind == "tiny_bulk":   # the bulk 1e-4 of a single large channel
+        x *= 1e-4
+        x[rng.integers(K)] = 1.0
+    return x
+
+
+@pytest.mark.parametrize("kind", ["spikes", "swiglu", "tiny_bulk"])
+@pytest.mark.parametrize("M,K", [(2560, 9728), (4096, 2560), (4864, 896)])
+def test_matvec_i4_heavy_tailed_activations(tq, oracle, kind, M, K):
+    """The kernel's activation digits share one scale per vector (max |x|); inputs
+    spanning 4 decades stay within the 1e-4 bound."""
+    rng = np.random.default_rng(M + K + len(kind))
+    w = synth.random_i4(rng, M, K, 64)
+    x = _heavy_tailed(rng, K, kind)
+    assert max_rel(tq.matvec_i4(w, x, M, K, 64), oracle.matvec_i4(w, x, M, K, 64)) < TOL
+
+
+def test_pair_heavy_tailed_activations(tq, oracle):
+    rng = np.random.default_rng(77)
+    K, M = 2560, 9728
+    g1, g2 = synth.random_i4_fast(rng, M, K, 64), synth.random_i4_fast(rng, M, K, 64)
+    x = _heavy_tailed(rng, K, "spikes")
+    y1, y2 = tq.matvec_pair_i4(g1, g2, x, M, K, 64)
+    assert max_rel(y1, oracle.matvec_i4(g1, x, M, K, 64)) < TOL
+    assert max_rel(y2, oracle.matvec_i4(g2, x, M, K, 64)) < TOL
+
+
+@pytest.mark.parametrize("M,K", [(16384, 2560), (20011, 2560), (151936, 2560)])
+def test_matvec_i4_multi_pass(tq, oracle, M, K):
+    """CTA shares above 100 KB run in several passes (lm_head: 151936 rows, ~1 MB per
+    CTA); 20011 rows leave a ragged last pass."""
+    rng = np.random.default_rng(M)
+    w = synth.random_i4_fast(rng, M, K, 64)
+    x = rng.normal(size=K).astype(np.float32)
+    assert max_rel(tq.matvec_i4(w, x, M, K, 64), oracle.matvec_i4(w, x, M, K, 64)) < TOL
+
+
 def test_resident_weight_cache(tq, oracle):
     rng = np.random.default_rng(3)
     w = synth.random_i4(rng, 256, 512, 64)

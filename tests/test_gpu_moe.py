@@ -12,7 +12,8 @@ import pytest
 
 import golden_cases as gc
 from conftest import max_rel
-from tqb200.model import QWEN3_30B_A3B, SynthModel
+from tqb200 import abi
+from tqb200.model import QWEN3_30B_A3B, ModelSpec, SynthModel
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-4
@@ -78,3 +79,23 @@ def test_moe_engine_profile_kinds(tq):
     _, prof = eng.profile_step(2)
     assert prof["router"] > 0 and prof["moe_combine"] > 0 and prof["gate_up"] > 0
     eng.close()
+
+
+def test_moe_engine_multi_pass_expert_blocks(tq, oracle):
+    """Expert blocks larger than one pass: top-2 of 8 experts with intermediate 4096, so
+    a CTA's share of the paired gate/up rows exceeds 100 KB and its passes (of a row
+    count dividing the 4096-row block) must not straddle two experts' blocks."""
+    spec = ModelSpec(name="moe-wide", model_type=abi.MODEL_QWEN3_MOE, n_layers=2, hidden=2048,
+                     inter=4096, n_heads=16, n_kv_heads=4, head_dim=128, vocab=4096,
+                     qk_norm=True, n_experts=8, experts_per_tok=2, moe_inter=4096, tied=False,
+                     weights="codes")
+    sm = SynthModel(spec, seed=13)
+    eng = tq.Engine(sm, max_seq_len=32)
+    om = oracle.model(sm, 32, False)
+    toks, logits = gc.model_tokens(eng, steps=8)
+    otoks, ologits = gc.model_tokens(om, steps=8)
+    assert toks == otoks
+    for a, b in zip(logits, ologits):
+        assert max_rel(a, b) < TOL
+    eng.close()
+    om.close()

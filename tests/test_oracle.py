@@ -96,6 +96,26 @@ def test_golden_config1(oracle, golden):
     assert np.array_equal(oracle.matvec_i4(w, x, 4864, 896, 64), golden["cfg1_y"])
 
 
+@pytest.mark.parametrize("M,K,sw,sx", gc.W4A8_CASES)
+def test_golden_w4a8_symmetric(oracle, golden, M, K, sw, sx):
+    """The W4A8 (sdot5) restatement against the reference test's own checker
+    matvec_i4_w4a8_naive (tests/test_matvec_i4.cpp:252-306) on that test's inputs and
+    symmetric packing: bit for bit."""
+    key = f"w4a8_{M}x{K}"
+    w, x = golden[key + "_w"], golden[key + "_x"]
+    assert np.array_equal(oracle.matvec_i4_w4a8(w, x, M, K, 64), golden[key + "_y"])
+
+
+def test_w4a8_golden_inputs_are_the_reference_tests(reflib, golden):
+    """The stored inputs are what the reference test's random_vec and
+    pack_i4_rtn_symmetric produce (reference build present only)."""
+    for (M, K, sw, sx) in gc.W4A8_CASES:
+        key = f"w4a8_{M}x{K}"
+        assert np.array_equal(reflib.random_vec(K, sx), golden[key + "_x"])
+        w = reflib.pack_i4_rtn_symmetric(reflib.random_vec(M * K, sw), M, K, 64)
+        assert np.array_equal(w, golden[key + "_w"])
+
+
 def test_golden_matmul(oracle, golden):
     w, X = gc.matmul_case()
     _sha_ok(golden, "mm_sha", w, X)

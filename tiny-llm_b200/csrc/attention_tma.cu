@@ -62,6 +62,7 @@ struct TmaAttnParams {
     int bulk_in;                    // q/k/v and constant vectors 16-byte aligned: bulk copies
     float *out;
     int *status;
+    Stamp stamp;                    // in-graph timeline (off unless the engine records one)
 };
 
 template <typename KV>
@@ -253,6 +254,7 @@ __global__ void __launch_bounds__(kThreads, sizeof(KV) == 2 ? 2 : 1) attn_tma_ke
     __shared__ int s_err, s_issued;
     __shared__ int s_done[kStages];  // warps finished with the slot's current tile
 
+    stamp_mark(P.stamp, 0);
     cg::cluster_group cluster = cg::this_cluster();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int kh = blockIdx.x;
@@ -303,6 +305,7 @@ __global__ void __launch_bounds__(kThreads, sizeof(KV) == 2 ? 2 : 1) attn_tma_ke
         }
     }
     griddep_wait();
+    stamp_mark(P.stamp, 1);
     if (tid == 0 && !fused)
         for (int i = 0; i < min(total, NST); ++i) issue(i);
     // q (and the owner's new k, v) were just written by the projection kernel: plain
@@ -597,6 +600,7 @@ __global__ void __launch_bounds__(kThreads, sizeof(KV) == 2 ? 2 : 1) attn_tma_ke
         for (int s2 = 0; s2 < ns; ++s2) O = fmaf(rcv_o[s2 * per + j], wgt[s2 * G + g], O);
         P.out[(size_t)kh * G * HD + i] = O / s_l[g];
     }
+    stamp_exit(P.stamp);
 }
 
 template <typename KV, int HD, int G>
@@ -657,6 +661,7 @@ int launch_t(const AttnArgs &a, cudaStream_t st) {
                                               (!a.q_norm || (a16(a.q_norm) && a16(a.k_norm)))));
         P.out = a.out;
         P.status = a.status;
+        P.stamp = a.stamp;
         // barriers | ring | new k, v rows (cache type) | krow, vrow, qs, cs+sn, qn, kn
         const size_t smem = 128 + (size_t)P.stage_region + ((2 * (size_t)RB + 15) & ~(size_t)15) +
                             ((size_t)5 * HD + (size_t)G * HD) * 4 +

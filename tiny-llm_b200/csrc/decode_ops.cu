@@ -719,8 +719,9 @@ constexpr int kRouterChunk = 32 * 4 * 16;  // floats of a row one warp loads at 
 __global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(
     const float *__restrict__ h, const float *__restrict__ norm_w, float eps, int H,
     const float *__restrict__ W, int E, int k, float *__restrict__ logits, int *__restrict__ idx,
-    float *__restrict__ wts, unsigned int *ticket) {
+    float *__restrict__ wts, unsigned int *ticket, Stamp stamp) {
     extern __shared__ __align__(16) float xn[];  // [H]
+    stamp_mark(stamp, 0);
     __shared__ double s_red[kRouterWarps];
     __shared__ bool s_last;
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
@@ -736,6 +737,7 @@ __global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(
         wv[j] = (vec && c < H) ? *reinterpret_cast<const float4 *>(row + c) : make_float4(0, 0, 0, 0);
     }
     griddep_wait();
+    stamp_mark(stamp, 1);
     griddep_launch();
     // the hidden vector and the norm weights, every load issued before any is used
     // (a chunk of kRouterHid per thread at a time)
@@ -804,17 +806,23 @@ __global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(
     __syncthreads();
     if (t == 0) s_last = atomicAdd(ticket, 1u) == gridDim.x - 1;
     __syncthreads();
-    if (!s_last) return;
+    if (!s_last) {
+        stamp_mark(stamp, 2);
+        return;
+    }
     __threadfence();
     if (warp == 0) topk_softmax_warp(logits, E, k, idx, wts);
     if (t == 0) *ticket = 0u;  // ready for the next launch (graph replay)
+    stamp_exit(stamp);
 }
 
 // acc = sum_t w_t * o_t in router order, then h += acc, with the reference's fp32
 // rounding points (runtime/qwen_forward_token.cpp:604-609, :627-631).
 __global__ void moe_combine_kernel(float *__restrict__ h, const float *__restrict__ o,
-                                   const float *__restrict__ wts, int k, int H) {
+                                   const float *__restrict__ wts, int k, int H, Stamp stamp) {
+    stamp_mark(stamp, 0);
     griddep_wait();
+    stamp_mark(stamp, 1);
     griddep_launch();
     constexpr int kMax = 16;  // expert outputs loaded at once (k is at most 32)
     for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < H; j += gridDim.x * blockDim.x) {
@@ -834,6 +842,7 @@ __global__ void moe_combine_kernel(float *__restrict__ h, const float *__restric
         }
         h[j] = __fadd_rn(hj, acc);
     }
+    stamp_exit(stamp);
 }
 
 // Expert parallelism: the chosen experts as this rank's local indices (-1: another
@@ -1189,21 +1198,21 @@ int launch_pdl(Kern k, int grid, int block, size_t smem, bool pdl, cudaStream_t 
 
 int launch_moe_router(const float *h, const float *norm_w, float eps, int H, const float *W, int E,
                       int k, float *logits, int *idx, float *wts, unsigned int *ticket, bool pdl,
-                      cudaStream_t st) {
+                      cudaStream_t st, const Stamp &stamp) {
     TQ_CHECK_ARG(E > 0 && E <= 32 * kRouterPer && k > 0 && k <= 32 && k <= E && H > 0,
                  "moe router: E %d k %d H %d", E, k, H);
     const size_t smem = (size_t)H * 4;
     TQ_CHECK_ARG(smem <= 48 * 1024, "moe router: hidden %d too large", H);
     return launch_pdl(moe_router_kernel, (E + kRouterWarps - 1) / kRouterWarps, kRouterWarps * 32,
-                      smem, pdl, st, h, norm_w, eps, H, W, E, k, logits, idx, wts, ticket);
+                      smem, pdl, st, h, norm_w, eps, H, W, E, k, logits, idx, wts, ticket, stamp);
 }
 
 int launch_moe_combine(float *h, const float *o, const float *wts, int k, int H, bool pdl,
-                       cudaStream_t st) {
+                       cudaStream_t st, const Stamp &stamp) {
     TQ_CHECK_ARG(k > 0 && H > 0, "moe combine: k %d H %d", k, H);
     const int threads = 256;
     return launch_pdl(moe_combine_kernel, (H + threads - 1) / threads, threads, 0, pdl, st, h, o,
-                      wts, k, H);
+                      wts, k, H, stamp);
 }
 
 int launch_topk_softmax(const float *logits, int n, int k, int *idx, float *w, cudaStream_t st) {

@@ -148,6 +148,12 @@ struct tqb200_engine {
     int *moe_local = nullptr;  // expert parallelism: chosen experts as local indices (-1: remote)
     unsigned int *moe_ticket = nullptr;
     tqb200::Prefill pf;
+    // in-graph timeline of generate() (tqb200_engine_set_timeline): three global-timer
+    // words per stamped launch and step, the launches' kinds in step order
+    unsigned long long *tl = nullptr;
+    int tl_cap = 0, tl_stride = 0, tl_steps = 0;
+    bool tl_capture = false;  // true while the stamped generate graph is being captured
+    std::vector<int> tl_kind;
 #ifdef TQB200_HAVE_NCCL
     ncclComm_t comm = nullptr;
 #endif
@@ -353,6 +359,21 @@ int mark(tqb200_engine *e, int kind) {
     return TQB200_OK;
 }
 
+// The timeline words of the next stamped launch of kind `kind` (off outside the capture
+// of a stamped generate graph).
+Stamp tl_next(tqb200_engine *e, int kind) {
+    Stamp s;
+    if (!e->tl_capture || !e->tl) return s;
+    const int i = (int)e->tl_kind.size();
+    if (3 * (i + 1) > e->tl_stride) return s;
+    e->tl_kind.push_back(kind);
+    s.base = e->tl + 3 * (size_t)i;
+    s.step = e->gen_count;
+    s.stride = e->tl_stride;
+    s.cap = e->tl_cap;
+    return s;
+}
+
 // Device-side token feed for generate(): records the produced token and makes it
 // (and position + 1) the input of the next step.
 __global__ void feed_next_kernel(int *io_in, const int *io_out, int *tokens, int *count) {
@@ -426,9 +447,10 @@ int launch_forward(tqb200_engine *e) {
             jb.rot_bs = w.rot_bs[p];
             return jb;
         };
-        auto vq_launch = [&](VqLaunch &a) {
+        auto vq_launch = [&](VqLaunch &a, int kind) {
             a.pdl = pdl;
             a.status = status;
+            a.stamp = tl_next(e, kind);
             return launch_vq2_matvec(a, st);
         };
         if (w.vq2) {  // q/k/v (each with its own rotation) after the input RMSNorm
@@ -439,7 +461,7 @@ int launch_forward(tqb200_engine *e) {
             a.n_jobs = 3;
             a.K = H;
             a.x = {X_RMSNORM, e->hidden, w.input_ln, d.rms_eps, nullptr};
-            TQ_TRY(vq_launch(a));
+            TQ_TRY(vq_launch(a, K_QKV));
             TQ_TRY(mark(e, K_QKV));
         } else {   // q/k/v with the input RMSNorm fused into the prologue, biases into the epilogue
             I4Job j[3] = {{w.q, e->q, w.q_bias, nullptr, qdl},
@@ -449,6 +471,7 @@ int launch_forward(tqb200_engine *e) {
             o.x = {X_RMSNORM, e->hidden, w.input_ln, d.rms_eps, nullptr};
             o.pdl = pdl;
             o.status = status;
+            o.stamp = tl_next(e, K_QKV);
             TQ_TRY(launch_i4_matvec_ex(j, 3, H, d.group_size, o, st));
             TQ_TRY(mark(e, K_QKV));
         }
@@ -483,6 +506,7 @@ int launch_forward(tqb200_engine *e) {
             a.sin_tab = e->sin_tab;
             a.pdl = pdl;
             a.status = status;
+            a.stamp = tl_next(e, K_ATTN);
             TQ_TRY(launch_attention(a, st));
             TQ_TRY(allgather(e, e->attn, qdl));
             TQ_TRY(mark(e, K_ATTN));
@@ -492,7 +516,7 @@ int launch_forward(tqb200_engine *e) {
             a.job[0] = vq(w.o, hidden_mine, hidden_mine, Hs, P_O);
             a.K = qd;
             a.x = {X_PLAIN, e->attn, nullptr, 0.0f, nullptr};
-            TQ_TRY(vq_launch(a));
+            TQ_TRY(vq_launch(a, K_OPROJ));
             TQ_TRY(allgather(e, e->hidden, Hs));
             TQ_TRY(mark(e, K_OPROJ));
         } else {   // o_proj, residual fused: hidden = hidden + W_o attn (this rank's rows)
@@ -501,6 +525,7 @@ int launch_forward(tqb200_engine *e) {
             o.x = {X_PLAIN, e->attn, nullptr, 0.0f, nullptr};
             o.pdl = pdl;
             o.status = status;
+            o.stamp = tl_next(e, K_OPROJ);
             TQ_TRY(launch_i4_matvec_ex(&j, 1, qd, d.group_size, o, st));
             TQ_TRY(allgather(e, e->hidden, Hs));
             TQ_TRY(mark(e, K_OPROJ));
@@ -521,13 +546,14 @@ int launch_forward(tqb200_engine *e) {
             if (w.router_f32) {
                 TQ_TRY(launch_moe_router(e->hidden, w.post_ln, d.rms_eps, H, w.router_f32, E, k,
                                          e->moe_logits, e->moe_idx, e->moe_w, e->moe_ticket, pdl,
-                                         st));
+                                         st, tl_next(e, K_ROUTER)));
             } else {
                 I4Job j{w.router_i4, e->moe_logits, nullptr, nullptr, E};
                 I4LaunchOpts o;
                 o.x = {X_RMSNORM, e->hidden, w.post_ln, d.rms_eps, nullptr};
                 o.pdl = pdl;
                 o.status = status;
+                o.stamp = tl_next(e, K_ROUTER);
                 TQ_TRY(launch_i4_matvec_ex(&j, 1, H, d.group_size, o, st));
                 TQ_TRY(launch_topk_softmax(e->moe_logits, E, k, e->moe_idx, e->moe_w, st));
             }
@@ -547,6 +573,7 @@ int launch_forward(tqb200_engine *e) {
                 o.n_experts = El;
                 o.pdl = pdl;
                 o.status = status;
+                o.stamp = tl_next(e, K_GATEUP);
                 TQ_TRY(launch_i4_matvec_ex(j, 2, H, d.group_size, o, st));
                 TQ_TRY(mark(e, K_GATEUP));
             }
@@ -562,11 +589,13 @@ int launch_forward(tqb200_engine *e) {
                 o.xslots = true;
                 o.pdl = pdl;
                 o.status = status;
+                o.stamp = tl_next(e, K_DOWN);
                 TQ_TRY(launch_i4_matvec_ex(&j, 1, mi, d.group_size, o, st));
                 TQ_TRY(allreduce_sum(e, e->moe_o, (size_t)k * H));
                 TQ_TRY(mark(e, K_DOWN));
             }
-            TQ_TRY(launch_moe_combine(e->hidden, e->moe_o, e->moe_w, k, H, pdl, st));
+            TQ_TRY(launch_moe_combine(e->hidden, e->moe_o, e->moe_w, k, H, pdl, st,
+                                      tl_next(e, K_COMBINE)));
             TQ_TRY(mark(e, K_COMBINE));
             continue;
         }
@@ -578,7 +607,7 @@ int launch_forward(tqb200_engine *e) {
             a.pair_swiglu = true;
             a.K = H;
             a.x = {X_RMSNORM, e->hidden, w.post_ln, d.rms_eps, nullptr};
-            TQ_TRY(vq_launch(a));
+            TQ_TRY(vq_launch(a, K_GATEUP));
             TQ_TRY(allgather(e, e->act, Is));
             TQ_TRY(mark(e, K_GATEUP));
         } else {   // gate/up in one pass per row block (post-attention RMSNorm in the prologue),
@@ -590,6 +619,7 @@ int launch_forward(tqb200_engine *e) {
             o.pair_swiglu = true;
             o.pdl = pdl;
             o.status = status;
+            o.stamp = tl_next(e, K_GATEUP);
             TQ_TRY(launch_i4_matvec_ex(j, 2, H, d.group_size, o, st));
             TQ_TRY(allgather(e, e->act, Is));
             TQ_TRY(mark(e, K_GATEUP));
@@ -599,7 +629,7 @@ int launch_forward(tqb200_engine *e) {
             a.job[0] = vq(w.down, hidden_mine, hidden_mine, Hs, P_DOWN);
             a.K = d.inter;
             a.x = {X_PLAIN, e->act, nullptr, 0.0f, nullptr};
-            TQ_TRY(vq_launch(a));
+            TQ_TRY(vq_launch(a, K_DOWN));
             TQ_TRY(allgather(e, e->hidden, Hs));
             TQ_TRY(mark(e, K_DOWN));
         } else {   // down with the residual in the epilogue
@@ -608,6 +638,7 @@ int launch_forward(tqb200_engine *e) {
             o.x = {X_PLAIN, e->act, nullptr, 0.0f, nullptr};
             o.pdl = pdl;
             o.status = status;
+            o.stamp = tl_next(e, K_DOWN);
             TQ_TRY(launch_i4_matvec_ex(&j, 1, d.inter, d.group_size, o, st));
             TQ_TRY(allgather(e, e->hidden, Hs));
             TQ_TRY(mark(e, K_DOWN));
@@ -641,6 +672,7 @@ int launch_lm_head(tqb200_engine *e) {
         }
         o.pdl = pdl;
         o.status = status;
+        o.stamp = tl_next(e, K_LMHEAD);
         TQ_TRY(launch_i4_matvec_ex(&j, 1, H, d.group_size, o, st));
         if (G > 1) {
             TQ_TRY(allgather(e, reinterpret_cast<float *>(e->pairs), 2));
@@ -654,7 +686,11 @@ int launch_lm_head(tqb200_engine *e) {
 
 int capture(tqb200_engine *e, bool with_feed, cudaGraph_t *graph, cudaGraphExec_t *exec) {
     TQ_CUDA_TRY(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+    // the generate graph carries the timeline stamps while a timeline is set
+    e->tl_capture = with_feed && e->tl != nullptr;
+    e->tl_kind.clear();
     int st = launch_forward(e);
+    e->tl_capture = false;
     if (st == TQB200_OK && with_feed) {
         feed_next_kernel<<<1, 1, 0, e->stream>>>(e->io_in, e->io_out, e->gen_tokens, e->gen_count);
         if (cudaGetLastError() != cudaSuccess) st = set_error(TQB200_ERR_CUDA, "feed launch failed");
@@ -696,6 +732,7 @@ void free_engine(tqb200_engine *e) {
     if (e->comm) ncclCommDestroy(e->comm);
 #endif
     for (void *p : e->allocs) cudaFree(p);
+    if (e->tl) cudaFree(e->tl);
     if (e->h_io) cudaFreeHost(e->h_io);
     if (e->stream) cudaStreamDestroy(e->stream);
     delete e;
@@ -1401,6 +1438,10 @@ int tqb200_engine_generate(tqb200_engine *e, int token_id, int n_steps, int *out
     e->h_io[1] = e->pos;
     TQ_CUDA_TRY(cudaMemcpyAsync(e->io_in, e->h_io, 8, cudaMemcpyHostToDevice, e->stream));
     TQ_CUDA_TRY(cudaMemsetAsync(e->gen_count, 0, 4, e->stream));
+    if (e->tl) {  // a fresh timeline record for the first tl_cap steps of this call
+        TQ_CUDA_TRY(cudaMemsetAsync(e->tl, 0xFF, (size_t)e->tl_cap * e->tl_stride * 8, e->stream));
+        e->tl_steps = std::min(n_steps, e->tl_cap);
+    }
     TQ_CUDA_TRY(cudaEventRecord(e->ev[0], e->stream));
     for (int i = 0; i < n_steps; ++i) {
         if (e->o.use_graph) {
@@ -1501,6 +1542,76 @@ int tqb200_engine_kv_cache(const tqb200_engine *e, void **kv, size_t *bytes) {
 int tqb200_engine_weight_bytes(const tqb200_engine *e, size_t *bytes) {
     TQ_CHECK_ARG(e && bytes, "null argument");
     *bytes = e->weight_bytes;
+    return TQB200_OK;
+}
+
+int tqb200_engine_set_timeline(tqb200_engine *e, int max_steps) {
+    TQ_CHECK_ARG(e && max_steps >= 0 && max_steps <= 1 << 16, "bad timeline arguments");
+    TQ_CHECK_ARG(max_steps == 0 || e->o.use_graph, "the timeline needs the graph-replayed step");
+    TQ_CUDA_TRY(cudaSetDevice(e->device));
+    TQ_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    // the generate graph is captured again on its next use, with or without stamps
+    if (e->loop_exec) cudaGraphExecDestroy(e->loop_exec);
+    if (e->loop_graph) cudaGraphDestroy(e->loop_graph);
+    e->loop_exec = nullptr;
+    e->loop_graph = nullptr;
+    if (e->tl) cudaFree(e->tl);
+    e->tl = nullptr;
+    e->tl_cap = e->tl_steps = 0;
+    e->tl_kind.clear();
+    if (max_steps == 0) return TQB200_OK;
+    // room for every launch of a step: at most 8 per layer plus the head
+    e->tl_stride = 3 * (8 * e->d.n_layers + 16);
+    const size_t bytes = (size_t)max_steps * e->tl_stride * 8;
+    TQ_CUDA_TRY(cudaMalloc(&e->tl, bytes));
+    TQ_CUDA_TRY(cudaMemset(e->tl, 0xFF, bytes));
+    e->tl_cap = max_steps;
+    return TQB200_OK;
+}
+
+int tqb200_engine_timeline(const tqb200_engine *e, int n_kinds, double *excl_ms, double *incl_ms,
+                           int *launches, int *steps, double *span_ms) {
+    TQ_CHECK_ARG(e && n_kinds > 0 && excl_ms && incl_ms && launches && steps && span_ms,
+                 "bad timeline arguments");
+    TQ_CHECK_ARG(e->tl, "no timeline set (tqb200_engine_set_timeline)");
+    for (int k = 0; k < n_kinds; ++k) excl_ms[k] = incl_ms[k] = 0.0, launches[k] = 0;
+    *steps = 0;
+    *span_ms = 0.0;
+    const int ns = e->tl_steps, nl = (int)e->tl_kind.size();
+    if (ns == 0 || nl == 0) return TQB200_OK;
+    std::vector<unsigned long long> h((size_t)ns * e->tl_stride);
+    TQ_CUDA_TRY(cudaSetDevice(e->device));
+    TQ_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    TQ_CUDA_TRY(cudaMemcpy(h.data(), e->tl, h.size() * 8, cudaMemcpyDeviceToHost));
+    const unsigned long long none = ~0ull;
+    int good = 0;
+    for (int s = 0; s < ns; ++s) {
+        const unsigned long long *r = h.data() + (size_t)s * e->tl_stride;
+        bool complete = true;
+        for (int i = 0; i < nl && complete; ++i)
+            complete = r[3 * i] != none && r[3 * i + 2] != none;
+        if (!complete) continue;  // a launch left no record (error path): skip the step
+        unsigned long long first = none, last = 0;
+        for (int i = 0; i < nl; ++i) {
+            const unsigned long long entry = r[3 * i];
+            const unsigned long long wait = r[3 * i + 1] != none ? r[3 * i + 1] : entry;
+            const unsigned long long exit = ~r[3 * i + 2];
+            first = std::min(first, entry);
+            last = std::max(last, exit);
+            const int k = e->tl_kind[i];
+            if (k < 0 || k >= n_kinds) continue;
+            excl_ms[k] += exit > wait ? (double)(exit - wait) * 1e-6 : 0.0;
+            incl_ms[k] += exit > entry ? (double)(exit - entry) * 1e-6 : 0.0;
+            if (good == 0) launches[k] += 1;
+        }
+        *span_ms += (double)(last - first) * 1e-6;
+        ++good;
+    }
+    if (good > 0) {
+        for (int k = 0; k < n_kinds; ++k) excl_ms[k] /= good, incl_ms[k] /= good;
+        *span_ms /= good;
+    }
+    *steps = good;
     return TQB200_OK;
 }
 

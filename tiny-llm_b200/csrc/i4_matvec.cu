@@ -66,6 +66,7 @@ struct MvParams {
     long long estride;
     int erows, nslots, n_experts;
     int xslots;
+    Stamp stamp;  // in-graph timeline (off unless the engine records one)
 };
 
 // Pass index of a CTA's i-th pass (>= total when it has none).
@@ -265,6 +266,7 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
     __shared__ int s_bi[32];
     __shared__ bool s_last;
     const bool bulk_x = P.x_bulk != 0;
+    stamp_mark(P.stamp, 0);
 
     if (t == 0) {
         for (int s = 0; s < P.stages; ++s) {
@@ -292,6 +294,7 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
     __syncthreads();  // barrier initialisation visible to every thread
     // weights are in flight; now wait for the producer of x and let our dependents start
     griddep_wait();
+    stamp_mark(P.stamp, 1);
     griddep_launch();
     if (P.eidx && t == 0) {  // expert weights: which ones is known only now
         for (int s = 0; s < P.stages; ++s) {
@@ -630,6 +633,7 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
             }
         }
     }
+    stamp_exit(P.stamp);
 }
 
 // Fallback for odd group sizes or unaligned bases: one warp per row, byte loads.
@@ -943,6 +947,7 @@ int launch_i4_matvec_ex(const I4Job *jobs, int n_jobs, int in_dim, int group_siz
     P.nslots = o.nslots;
     P.n_experts = o.n_experts;
     P.xslots = o.xslots ? 1 : 0;
+    P.stamp = o.stamp;
     const Shape L = plan(in_dim, group_size, pair, o.x.mode == X_RMSNORM, rows_total,
                          o.eidx ? o.erows : 0);
     bool aligned = true;  // the TMA path needs 16-byte aligned matrix bases

@@ -11,6 +11,46 @@ namespace tqb200 {
 
 int num_sms();
 
+// ------------------------------------------------------------------ in-graph timeline
+// Global-timer stamps of one launch, per decode step: word 0 = the first CTA's entry,
+// word 1 = the first CTA past its dependency wait (griddepcontrol.wait returns once the
+// previous kernel has completed), word 2 = the bitwise complement of the last CTA's
+// exit.  All three are kept with atomicMin, so a 0xFF fill clears a record.  With
+// programmatic dependent launch a kernel's entry overlaps its predecessor, but the
+// intervals [word 1, exit] of consecutive launches do not overlap: they partition the
+// step.  base == nullptr turns stamping off (the default everywhere).
+struct Stamp {
+    unsigned long long *base = nullptr;  // this launch's words for step 0
+    const int *step = nullptr;           // device step counter selecting the record
+    int stride = 0;                      // words between consecutive steps' records
+    int cap = 0;                         // steps with a record
+};
+
+#if defined(__CUDACC__)
+__device__ __forceinline__ unsigned long long global_timer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// which = 0 (entry), 1 (past the dependency wait) or 2 (exit); thread (0,0,0) of a CTA.
+__device__ __forceinline__ void stamp_mark(const Stamp &s, int which) {
+    if (s.base != nullptr && threadIdx.x == 0 && threadIdx.y == 0 && threadIdx.z == 0) {
+        const int k = *s.step;
+        if (k >= 0 && k < s.cap) {
+            const unsigned long long t = global_timer_ns();
+            atomicMin(s.base + (size_t)k * s.stride + which, which == 2 ? ~t : t);
+        }
+    }
+}
+// Exit stamp once every thread of the CTA is done (uniform: s.base is a kernel argument).
+__device__ __forceinline__ void stamp_exit(const Stamp &s) {
+    if (s.base != nullptr) {
+        __syncthreads();
+        stamp_mark(s, 2);
+    }
+}
+#endif
+
 // ------------------------------------------------------------------ i4
 // One matrix of a fused i4 matvec launch.  All jobs share x, in_dim and group.
 struct I4Job {
@@ -59,6 +99,7 @@ struct I4LaunchOpts {
     int erows = 0, nslots = 0, n_experts = 0;
     // per-block activations (one plain job): block b uses x.src + b * in_dim
     bool xslots = false;
+    Stamp stamp;                    // in-graph timeline (TMA kernel only)
 };
 
 // y_j = W_j x (+bias_j / +resid_j) for up to 3 jobs in one launch (q/k/v, gate/up, ...).
@@ -190,6 +231,7 @@ struct VqLaunch {
     XSource x;
     bool pdl = false;
     int *status = nullptr;        // device error word (bounded-wait timeouts)
+    Stamp stamp;                  // in-graph timeline
 };
 int launch_vq2_matvec(const VqLaunch &a, cudaStream_t st);
 int launch_biip(const float *x, float *y, int dim, const float *scale, const float *sign, int bs,
@@ -239,6 +281,7 @@ struct AttnArgs {
     const float *cos_tab = nullptr, *sin_tab = nullptr;
     bool pdl = false;         // programmatic dependent launch (TMA kernel only)
     int *status = nullptr;    // device error word (bounded waits, bad position)
+    Stamp stamp;              // in-graph timeline (TMA kernel only)
 };
 int attn_plan(int n_kv_heads, int max_seq, int *nsplit, int *chunk_max);
 size_t attn_partial_floats(int n_heads, int head_dim, int nsplit);
@@ -265,9 +308,9 @@ int launch_topk_softmax(const float *logits, int n, int k, int *idx, float *w, c
 // device word, reset by the kernel); and h += sum_t wts[t] * o[t] in router order.
 int launch_moe_router(const float *h, const float *norm_w, float eps, int H, const float *W, int E,
                       int k, float *logits, int *idx, float *wts, unsigned int *ticket, bool pdl,
-                      cudaStream_t st);
+                      cudaStream_t st, const Stamp &stamp = Stamp());
 int launch_moe_combine(float *h, const float *o, const float *wts, int k, int H, bool pdl,
-                       cudaStream_t st);
+                       cudaStream_t st, const Stamp &stamp = Stamp());
 int launch_embed(const void *table, int dtype, const int *token, int dim, int group_size,
                  float *out, cudaStream_t st, int n_tokens = 1);
 // Expert parallelism: local[j] = idx[j] - e0 when this rank owns that expert, else -1;

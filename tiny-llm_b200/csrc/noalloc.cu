@@ -13,7 +13,11 @@
 // Host code cannot use the arrays' names as device addresses (in host code a
 // __device__ symbol names a host-side stand-in); the device address comes from
 // cudaGetSymbolAddress, looked up once per device, with that device current, by the
-// first call made on it.  Make that first call outside any stream capture.
+// first call made on it.  Make that first call outside any stream capture.  With CUDA's
+// default lazy module loading, that first call is also when the driver loads this
+// library's device code and places the arrays in device memory; a caller that reserves
+// the rest of the device up front makes the first call before reserving it, or sets
+// CUDA_MODULE_LOADING=EAGER so the arrays are placed when the library loads.
 //
 // Every call shares the same arrays and leaves its contents in them.  The tickets
 // must start at zero, so each call clears them on its stream first.  Calls that can

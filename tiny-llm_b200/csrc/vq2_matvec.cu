@@ -45,6 +45,7 @@ struct VqParams {
     int region;        // bytes of one matrix's staging region (codebook + index block)
     XSource x;
     int *status;
+    Stamp stamp;       // in-graph timeline (off unless the engine records one)
 };
 
 // One Hadamard block of BS = 32 * E elements in registers (lane l holds elements
@@ -148,6 +149,7 @@ __global__ void __launch_bounds__(kVqMaxThreads) vq2_matvec_kernel(const __grid_
     float *red = rot + (size_t)nm * 2 * K4 / 4;             // [nm][S][nt]
     __shared__ int s_err;
     __shared__ double s_rd[32];
+    stamp_mark(P.stamp, 0);
 
     int j = 0;
     while (j + 1 < P.n_jobs && (int)blockIdx.x >= P.cta_begin[j + 1]) ++j;
@@ -189,6 +191,7 @@ __global__ void __launch_bounds__(kVqMaxThreads) vq2_matvec_kernel(const __grid_
         }
     }
     griddep_wait();
+    stamp_mark(P.stamp, 1);
     griddep_launch();
     if (t == 0 && P.bulk) {
         const uint32_t xb = (uint32_t)K * 4u;
@@ -351,6 +354,7 @@ __global__ void __launch_bounds__(kVqMaxThreads) vq2_matvec_kernel(const __grid_
         }
         __syncthreads();
     }
+    stamp_exit(P.stamp);
 }
 
 // Standalone BiIP rotation (per-op entry point): one CTA, x -> y.
@@ -382,6 +386,7 @@ int launch_vq2_matvec(const VqLaunch &a, cudaStream_t st) {
     P.K = a.K;
     P.x = a.x;
     P.status = a.status;
+    P.stamp = a.stamp;
     P.nt = (a.K + 15) / 16;
     TQ_CHECK_ARG(P.nt <= kVqMaxThreads, "vq2: in_dim %d above %d", a.K, 16 * kVqMaxThreads);
     P.S = std::max(1, kVqMaxThreads / P.nt);

@@ -24,6 +24,7 @@ _u8 = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
 _f = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
 _u16 = np.ctypeslib.ndpointer(dtype=np.uint16, flags="C_CONTIGUOUS")
 _i32 = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
+_d = np.ctypeslib.ndpointer(dtype=np.float64, flags="C_CONTIGUOUS")
 _i, _fl, _vp = C.c_int, C.c_float, C.c_void_p
 
 
@@ -81,6 +82,8 @@ PROTOTYPES = {
     "tqb200_engine_prefill": ([_vp, _i32, _i, C.POINTER(_i)], _i),
     "tqb200_engine_profile_prefill": ([_vp, _i32, _i, _f, _i, C.POINTER(_i)], _i),
     "tqb200_engine_profile_step": ([_vp, _i, _f, _i, C.POINTER(_i)], _i),
+    "tqb200_engine_set_timeline": ([_vp, _i], _i),
+    "tqb200_engine_timeline": ([_vp, _i, _d, _d, _i32, C.POINTER(_i), C.POINTER(C.c_double)], _i),
 }
 
 _lib = None
@@ -364,6 +367,22 @@ class Engine:
         nxt = C.c_int(-1)
         _check(load().tqb200_engine_profile_step(self.h, int(token), ms, ms.size, C.byref(nxt)))
         return nxt.value, dict(zip(self.KINDS, ms.tolist()))
+
+    def set_timeline(self, max_steps: int):
+        """Stamp every launch of the first max_steps steps of each generate() (0: off)."""
+        _check(load().tqb200_engine_set_timeline(self.h, int(max_steps)))
+
+    def timeline(self):
+        """The last generate()'s in-graph timeline: (steps, span_ms, {kind: (excl_ms,
+        incl_ms, launches)}) per step, for the kinds with launches."""
+        n = len(self.KINDS)
+        ex, inc = np.zeros(n, np.float64), np.zeros(n, np.float64)
+        cnt = np.zeros(n, np.int32)
+        steps, span = C.c_int(0), C.c_double(0.0)
+        _check(load().tqb200_engine_timeline(self.h, n, ex, inc, cnt, C.byref(steps), C.byref(span)))
+        kinds = {k: (float(ex[i]), float(inc[i]), int(cnt[i]))
+                 for i, k in enumerate(self.KINDS) if cnt[i] > 0}
+        return steps.value, span.value, kinds
 
     def reset(self):
         _check(load().tqb200_engine_reset(self.h))
