@@ -586,7 +586,7 @@ def bench_decode(args, rank, pg, pk, pk_kind):
     W, K = args.warmup, args.steps
     wl = DECODE_WORKLOADS[args.workload]
     ctx = args.ctx if args.ctx is not None else wl["ctx"]
-    max_seq = ctx + W + 2 * K + 32  # + the unstamped (K), e2e (19) and profiled (1) steps
+    max_seq = ctx + 2 * W + 2 * K + 32  # + the stamped (W + K), e2e (19) and profiled (1) steps
     spec = decode_spec(wl, max_seq)
     if args.layers:
         from dataclasses import replace as _replace
@@ -605,11 +605,7 @@ def bench_decode(args, rank, pg, pk, pk_kind):
     first = int(rng.integers(0, spec.vocab))
     toks, _ = eng.generate(first, ctx - W)
     tok = toks[-1]
-    # the timed steps carry the in-graph timeline: every launch stamps the global timer
-    # (first CTA in, first CTA past its dependency wait, last CTA out), so the per-kernel
-    # times below come from the same graph replays as the step time
-    eng.set_timeline(K)
-    toks, _ = eng.generate(tok, W)   # warm-up steps (also captures the stamped graph)
+    toks, _ = eng.generate(tok, W)   # warm-up steps (also captures the graph)
     tok = toks[-1]
     torch.cuda.synchronize()
     clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
@@ -622,15 +618,17 @@ def bench_decode(args, rank, pg, pk, pk_kind):
     clk = clocks.stop()
     dev_ms = max_over_ranks(pg, dev_ms)
     ms_step = dev_ms / K
-    tl_steps, tl_span, tl = eng.timeline()
-    # the same K steps without stamps (the stamps' cost, for the record)
-    eng.set_timeline(0)
-    tok = toks[-1]
-    toks, _ = eng.generate(tok, W)
-    tok = toks[-1]
+    # the next K steps again, with the in-graph timeline: every launch in its stamped
+    # form records the global timer (CTA in, past its dependency wait, out), so the
+    # per-kernel in-step times come from graph replays of the same step (the stamps cost
+    # a few percent, so the timed value above is taken without them)
+    eng.set_timeline(K)
+    toks, _ = eng.generate(toks[-1], W)   # also captures the stamped graph
     barrier(pg)
-    toks, plain_ms = eng.generate(tok, K)
-    plain_ms = max_over_ranks(pg, plain_ms) / K
+    toks, tl_ms = eng.generate(toks[-1], K)
+    tl_ms = max_over_ranks(pg, tl_ms) / K
+    tl_steps, tl_span, tl = eng.timeline()
+    eng.set_timeline(0)
 
     # e2e: the C-ABI step call with host token in / host token out, every step
     tok = toks[-1]
@@ -688,10 +686,11 @@ def bench_decode(args, rank, pg, pk, pk_kind):
                      "algorithmic_bytes_per_step": int(mv_bytes),
                      "matvec_ms_per_step": round(mv_ms, 4),
                      "how": "achieved = algorithmic_bytes_per_step / matvec_ms_per_step; "
-                            "matvec_ms_per_step = the matvec launches' in-step time in the timed "
-                            "steps (in-graph global-timer stamps, from the first CTA past the "
-                            "dependency wait to the last CTA out, summed per step, averaged "
-                            "over the timed steps)",
+                            "matvec_ms_per_step = the matvec launches' in-step time (in-graph "
+                            "global-timer stamps: each launch from its first CTA past the "
+                            "dependency wait to the next launch's, summed per step, averaged "
+                            "over K stamped steps timed right after the K unstamped ones, whose "
+                            "step time is in timeline.ms_per_step)",
                      "step_vs_hbm_floor": round((total_bytes / (pk["hbm_gbs"] * 1e9) * 1e3) / ms_step, 4)},
         "rooflines": {
             "attention": {"bound": "hbm", "achieved": round((kv_bytes + attn_io) / (attn_ms * 1e-3) / 1e9, 1)
@@ -708,14 +707,16 @@ def bench_decode(args, rank, pg, pk, pk_kind):
                              "activations) over ms_per_step"}},
         "timeline_ms_by_kind": {k: {"in_step_ms": round(v[0], 4), "from_launch_ms": round(v[1], 4),
                                     "launches": v[2]} for k, v in tl.items()},
-        "timeline": {"steps": tl_steps, "stamped_span_ms": round(tl_span, 4),
+        "timeline": {"steps": tl_steps, "ms_per_step": round(tl_ms, 4),
+                     "stamped_span_ms": round(tl_span, 4),
                      "in_step_ms_sum": round(sum(v[0] for v in tl.values()), 4),
-                     "unstamped_ms_per_step": round(plain_ms, 4),
-                     "note": "in_step_ms: first CTA past the dependency wait to last CTA out "
-                             "(no overlap between launches, so the sum <= ms_per_step); "
-                             "from_launch_ms: first CTA in to last CTA out (overlaps the "
-                             "previous kernel under programmatic dependent launch); the "
-                             "embed and token-feed kernels and NCCL's are not stamped"},
+                     "note": "in_step_ms: a launch's first CTA past its dependency wait to the "
+                             "next stamped launch's (the step's last: to its last CTA out), so "
+                             "the launches do not overlap and the sum <= ms_per_step; the "
+                             "unstamped embed and token-feed kernels (and NCCL's) count with "
+                             "the launch before them; from_launch_ms: first CTA in to last CTA "
+                             "out (overlaps the previous kernel under programmatic dependent "
+                             "launch)"},
         "kernel_ms_serialized": {k: round(v, 4) for k, v in prof.items() if v > 0},
         "clocks": clk,
         "gpu_launches": launches * K,

@@ -239,16 +239,19 @@ int tqb200_engine_weight_bytes(const tqb200_engine *e, size_t *bytes);
 /* In-graph timeline of tqb200_engine_generate (no reference counterpart; the reference
  * profiles a step op by op on the host, runtime/main.cpp --profile-out).  With a timeline
  * set, the generate graph is captured again with every projection, attention, router and
- * combine launch writing global-timer stamps (first CTA in, first CTA past its dependency
- * wait, last CTA out) for each of the first max_steps steps of every generate() call;
- * max_steps = 0 turns it off.  Needs use_graph.  The stamps cost two atomics per CTA. */
+ * combine launch in a stamped form: each CTA's last thread records the global timer when
+ * it enters, when it gets past its dependency wait and when it exits (plain stores at its
+ * exit), for each of the first max_steps steps of every generate() call; max_steps = 0
+ * turns it off and restores the unstamped kernels.  Needs use_graph. */
 int tqb200_engine_set_timeline(tqb200_engine *e, int max_steps);
 /* The last generate() call's timeline, averaged over its recorded steps: per kernel kind
  * (the kinds of tqb200_engine_profile_step) excl_ms[k] sums, per step, the launches'
- * times from the first CTA past the dependency wait to the last CTA out (these intervals
- * do not overlap, so their sum is at most the step), incl_ms[k] the times from the first
- * CTA in (which overlaps the previous kernel under programmatic dependent launch);
- * launches[k] = launches of kind k per step; *span_ms = first stamped CTA in to last out. */
+ * in-step times, each from the launch's first CTA past its dependency wait to the next
+ * stamped launch's (the step's last one: to its last CTA out), so they do not overlap
+ * and the kernels that are not stamped (embed, token feed, NCCL) count with the launch
+ * before them; incl_ms[k] the times from the first CTA in to the last out (overlapping
+ * the previous kernel under programmatic dependent launch); launches[k] = launches of
+ * kind k per step; *span_ms = first stamped CTA in to the last out. */
 int tqb200_engine_timeline(const tqb200_engine *e, int n_kinds, double *excl_ms, double *incl_ms,
                            int *launches, int *steps, double *span_ms);
 

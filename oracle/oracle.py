@@ -151,6 +151,9 @@ class Oracle(_Common):
         sig("tqo_model_set_partial", [_vp, _i, _i])
         sig("tqo_model_kv", [_vp, C.POINTER(C.c_size_t)], _vp)
         sig("tqo_model_set_position", [_vp, _i], _i)
+        sig("tqo_model_set_kv_guide", [_vp, _vp, _fl])
+        sig("tqo_model_kv_guide_counts", [_vp, C.POINTER(C.c_longlong), C.POINTER(C.c_longlong),
+                                           C.POINTER(C.c_double)])
 
     def set_threads(self, n: int):
         self.lib.tqo_set_threads(n)
@@ -214,6 +217,21 @@ class OracleModel:
         p = self.orc.lib.tqo_model_kv(self.h, C.byref(n))
         raw = np.ctypeslib.as_array(C.cast(p, C.POINTER(C.c_uint8)), shape=(n.value,))
         return raw.view(np.uint16 if self.kv_fp16 else np.float32)
+
+    def set_kv_guide(self, guide, tol: float = 1e-5):
+        """Another implementation's fp16 arena (uint16, this model's layout) after the
+        same step: the next steps write their K/V rows from it, measuring how far this
+        model's own rounding is (beyond one ulp, in units of the head row's largest
+        magnitude; above tol is a mismatch).  None: off."""
+        self._guide = None if guide is None else np.ascontiguousarray(guide, np.uint16)
+        self.orc.lib.tqo_model_set_kv_guide(self.h, None if self._guide is None else
+                                            self._guide.ctypes.data, tol)
+
+    def kv_guide_counts(self):
+        """(differing elements, mismatches beyond tol, largest distance beyond one ulp)."""
+        f, m, d = C.c_longlong(0), C.c_longlong(0), C.c_double(0.0)
+        self.orc.lib.tqo_model_kv_guide_counts(self.h, C.byref(f), C.byref(m), C.byref(d))
+        return f.value, m.value, d.value
 
     def set_position(self, pos: int):
         if self.orc.lib.tqo_model_set_position(self.h, pos) != 0:

@@ -475,6 +475,12 @@ struct tqo_model {
     float *hidden, *normed, *q, *k, *v, *attn, *o, *gate, *up, *ffn, *logits, *rot_buf;
     float *router, *acc, *eg, *eu, *eo, *topk_w;
     int *topk_i;
+    /* fp16 cache guide (tests): another implementation's arena for the step; see
+     * tqo_model_set_kv_guide */
+    const uint16_t *guide;
+    float guide_tol;
+    long long guide_flips, guide_mismatches;
+    double guide_max_dev;
 };
 
 /* QwenModel::mv / mv_typed (runtime/qwen_model.cpp:212-221) -> CPUBackend::matvec
@@ -511,6 +517,7 @@ static void mv_rot(const tqo_model *m, const tqb200_matrix *w, const float *x, f
 static float *fz(size_t n) { return (float *)calloc(n ? n : 1, sizeof(float)); }
 
 tqo_model *tqo_model_create(const tqb200_model_desc *desc, int max_seq_len, int kv_fp16) {
+    if (desc->head_dim > 1024) return NULL; /* kv_write's row buffers */
     tqo_model *m = (tqo_model *)calloc(1, sizeof(tqo_model));
     m->d = *desc;
     m->max_seq_len = max_seq_len;
@@ -557,6 +564,39 @@ void tqo_model_set_partial(tqo_model *m, int n_layers_run, int head) {
     m->head = head;
 }
 
+/* Spacing of binary16 values at the magnitude of h (its ulp). */
+static double half_ulp(uint16_t h) {
+    const int e = (h & 0x7FFF) >> 10;
+    return ldexp(1.0, (e == 0 ? 1 : e) - 25);
+}
+
+/* One head row of the current position, n values written at dst[i] (binary16 bits): with
+ * a guide set, the guide's row is taken (every cached element then equals the other
+ * implementation's), and each element's distance from this model's own rounding is
+ * measured beyond one ulp, in units of the row's largest magnitude. */
+static void guided_row(tqo_model *m, uint16_t *dst, size_t idx, const uint16_t *own, int n) {
+    if (!m->guide) {
+        memcpy(dst, own, sizeof(uint16_t) * (size_t)n);
+        return;
+    }
+    double rmax = 0.0;
+    for (int i = 0; i < n; ++i) {
+        const double a = fabs((double)tqo_half_to_float(own[i]));
+        if (a > rmax) rmax = a;
+    }
+    for (int i = 0; i < n; ++i) {
+        const uint16_t g = m->guide[idx + i];
+        dst[i] = g;
+        if (g == own[i]) continue;
+        m->guide_flips += 1;
+        const double d = fabs((double)tqo_half_to_float(g) - (double)tqo_half_to_float(own[i]));
+        const double u = half_ulp(g) > half_ulp(own[i]) ? half_ulp(g) : half_ulp(own[i]);
+        const double dev = rmax > 0.0 ? (d - u) / rmax : (d > u ? INFINITY : 0.0);
+        if (dev > m->guide_max_dev) m->guide_max_dev = dev;
+        if (dev > m->guide_tol) m->guide_mismatches += 1;
+    }
+}
+
 /* KvCache::write_token (runtime/kv_cache.cpp:120-135): layout [K|V][L][KVH][max_seq][hd],
  * fp16 mode stores float_to_half. */
 static void kv_write(tqo_model *m, int layer) {
@@ -564,17 +604,22 @@ static void kv_write(tqo_model *m, int layer) {
     const size_t plane = (size_t)m->max_seq_len * d->head_dim;
     const size_t koff = (size_t)layer * m->layer_stride;
     const size_t voff = ((size_t)d->n_layers + layer) * m->layer_stride;
+    uint16_t hk[1024], hv[1024];
     for (int h = 0; h < d->n_kv_heads; ++h) {
         const size_t base = (size_t)h * plane + (size_t)m->pos * d->head_dim;
         for (int i = 0; i < d->head_dim; ++i) {
             const float kvk = m->k[h * d->head_dim + i], kvv = m->v[h * d->head_dim + i];
             if (m->kv_fp16) {
-                m->kv16[koff + base + i] = tqo_float_to_half(kvk);
-                m->kv16[voff + base + i] = tqo_float_to_half(kvv);
+                hk[i] = tqo_float_to_half(kvk);
+                hv[i] = tqo_float_to_half(kvv);
             } else {
                 m->kv32[koff + base + i] = kvk;
                 m->kv32[voff + base + i] = kvv;
             }
+        }
+        if (m->kv_fp16) {
+            guided_row(m, m->kv16 + koff + base, koff + base, hk, d->head_dim);
+            guided_row(m, m->kv16 + voff + base, voff + base, hv, d->head_dim);
         }
     }
 }
@@ -681,6 +726,24 @@ void *tqo_model_kv(tqo_model *m, size_t *bytes) {
     const size_t n = 2 * (size_t)m->d.n_layers * m->layer_stride;
     if (bytes) *bytes = n * (m->kv_fp16 ? 2 : 4);
     return m->kv_fp16 ? (void *)m->kv16 : (void *)m->kv32;
+}
+
+/* fp16 cache guide, for comparing another implementation's cache with this one step by
+ * step: while set, the K/V rows this model writes are taken from the guide (an arena of
+ * the same layout holding the other implementation's cache after the same step), so
+ * both continue from the same cache.  Each element that differs from this model's own
+ * rounding counts as a flip; its distance beyond one binary16 ulp, in units of its head
+ * row's largest magnitude, is tracked (the maximum), and counts as a mismatch above tol.
+ * NULL turns the guide off; the counts add up over steps. */
+void tqo_model_set_kv_guide(tqo_model *m, const uint16_t *guide, float tol) {
+    m->guide = guide;
+    m->guide_tol = tol;
+}
+void tqo_model_kv_guide_counts(const tqo_model *m, long long *flips, long long *mismatches,
+                               double *max_dev) {
+    if (flips) *flips = m->guide_flips;
+    if (mismatches) *mismatches = m->guide_mismatches;
+    if (max_dev) *max_dev = m->guide_max_dev;
 }
 
 /* Position of the next step (KvCache::seq_len; rows below it must hold K/V). */

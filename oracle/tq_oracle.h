@@ -64,6 +64,10 @@ const float *tqo_model_hidden(const tqo_model *m);        /* residual stream aft
 void tqo_model_reset(tqo_model *m);
 void *tqo_model_kv(tqo_model *m, size_t *bytes);          /* KV arena, engine layout */
 int tqo_model_set_position(tqo_model *m, int pos);        /* 0, or -1 out of range */
+/* fp16 cache guide for comparisons (see tq_oracle.c); NULL = off. */
+void tqo_model_set_kv_guide(tqo_model *m, const uint16_t *guide, float tol);
+void tqo_model_kv_guide_counts(const tqo_model *m, long long *flips, long long *mismatches,
+                               double *max_dev);
 void tqo_model_destroy(tqo_model *m);
 /* Runs only layers [0, n_layers_run) and skips the head when head == 0: a bounded
  * sample of one step, used by the timed CPU baseline. */

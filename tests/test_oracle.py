@@ -202,3 +202,37 @@ def test_oracle_matches_reference_random(oracle, reflib):
     w = synth.random_vq2(rng, 77, 256)
     x = rng.normal(size=256).astype(np.float32)
     assert np.array_equal(oracle.matvec_vq2(w, x, 77, 256), reflib.matvec_vq2(w, x, 77, 256))
+
+
+def test_oracle_kv_guide(oracle):
+    """The fp16 cache guide used by the config-4 comparison: the guided model writes the
+    guide's K/V rows, counts the elements that differ from its own rounding, and
+    measures how far beyond one binary16 ulp they are (in units of the head row's
+    largest magnitude); beyond the tolerance is a mismatch."""
+    from tqb200.model import ModelSpec, SynthModel
+    spec = ModelSpec(name="guide", qk_norm=True, n_layers=2, hidden=128, inter=256, n_heads=4,
+                     n_kv_heads=2, head_dim=32, vocab=500)
+    sm = SynthModel(spec, seed=5)
+    a = oracle.model(sm, 16, True)
+    a.step(7)
+    a.step(9)
+    guide = a.kv().copy()
+    kv = guide.reshape(2, 2, 2, 16, 32)
+    kv[0, 0, 0, 1, 3] ^= 1          # position 1: one rounding step away (a flip)
+    kv[1, 1, 1, 1, 5] ^= 0x0400     # a different binary exponent: far beyond one ulp
+    b = oracle.model(sm, 16, True)
+    b.step(7)
+    b.set_kv_guide(guide, 1e-5)
+    b.step(9)
+    flips, mism, dev = b.kv_guide_counts()
+    # (the adopted elements feed the later layer, whose own rounding may then differ
+    # from the guide's too: those count as flips as well)
+    assert flips >= 2 and mism == 1 and dev > 1e-3
+    assert np.array_equal(b.kv(), guide)
+    c = oracle.model(sm, 16, True)
+    c.step(7)
+    c.set_kv_guide(a.kv().copy(), 1e-5)  # the same computation: nothing differs
+    c.step(9)
+    assert c.kv_guide_counts() == (0, 0, 0.0)
+    for m in (a, b, c):
+        m.close()

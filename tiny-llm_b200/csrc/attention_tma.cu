@@ -217,7 +217,7 @@ __device__ __forceinline__ void norm_rope_warp(float *x, const float *nw, float 
 // 16-bit caches: at most 128 registers, so two CTAs fit an SM with the staged rows; the
 // fp32 instantiations keep the compiler's choice (all <= 127 but G=8 x HD 128 at 156,
 // whose 4-KV-head grids run one CTA per SM anyway).
-template <typename KV, int HD, int G>
+template <typename KV, int HD, int G, bool STAMP>
 __global__ void __launch_bounds__(kThreads, sizeof(KV) == 2 ? 2 : 1) attn_tma_kernel(const __grid_constant__ TmaAttnParams P) {
     namespace cg = cooperative_groups;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -254,7 +254,8 @@ __global__ void __launch_bounds__(kThreads, sizeof(KV) == 2 ? 2 : 1) attn_tma_ke
     __shared__ int s_err, s_issued;
     __shared__ int s_done[kStages];  // warps finished with the slot's current tile
 
-    stamp_mark(P.stamp, 0);
+    StampRegs stamp_r;
+    stamp_enter<STAMP>(P.stamp, stamp_r);
     cg::cluster_group cluster = cg::this_cluster();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int kh = blockIdx.x;
@@ -304,8 +305,9 @@ __global__ void __launch_bounds__(kThreads, sizeof(KV) == 2 ? 2 : 1) attn_tma_ke
             }
         }
     }
+    stamp_step<STAMP>(P.stamp, stamp_r);
     griddep_wait();
-    stamp_mark(P.stamp, 1);
+    stamp_waited<STAMP>(P.stamp, stamp_r);
     if (tid == 0 && !fused)
         for (int i = 0; i < min(total, NST); ++i) issue(i);
     // q (and the owner's new k, v) were just written by the projection kernel: plain
@@ -600,13 +602,13 @@ __global__ void __launch_bounds__(kThreads, sizeof(KV) == 2 ? 2 : 1) attn_tma_ke
         for (int s2 = 0; s2 < ns; ++s2) O = fmaf(rcv_o[s2 * per + j], wgt[s2 * G + g], O);
         P.out[(size_t)kh * G * HD + i] = O / s_l[g];
     }
-    stamp_exit(P.stamp);
+    stamp_exit<STAMP>(P.stamp, stamp_r);
 }
 
-template <typename KV, int HD, int G>
+template <typename KV, int HD, int G, bool STAMP>
 int launch_t(const AttnArgs &a, cudaStream_t st) {
     constexpr int RB = HD * (int)sizeof(KV);
-    auto k = attn_tma_kernel<KV, HD, G>;
+    auto k = attn_tma_kernel<KV, HD, G, STAMP>;
     static KernelSmem attr;
     static std::atomic<unsigned long long> cluster_attr{0};
     int smem_max = 0;
@@ -699,8 +701,9 @@ int launch_t(const AttnArgs &a, cudaStream_t st) {
 template <typename KV>
 int launch_kv(const AttnArgs &a, cudaStream_t st) {
     const int G = a.n_heads / a.n_kv_heads;
-#define TQ_TMA_CASE(HDV, GV) \
-    if (a.head_dim == HDV && G == GV) return launch_t<KV, HDV, GV>(a, st);
+#define TQ_TMA_CASE(HDV, GV)                                                              \
+    if (a.head_dim == HDV && G == GV)                                                      \
+        return a.stamp.base ? launch_t<KV, HDV, GV, true>(a, st) : launch_t<KV, HDV, GV, false>(a, st);
     TQ_TMA_CASE(64, 1) TQ_TMA_CASE(64, 2) TQ_TMA_CASE(64, 4) TQ_TMA_CASE(64, 7)
     TQ_TMA_CASE(64, 8) TQ_TMA_CASE(128, 1) TQ_TMA_CASE(128, 2) TQ_TMA_CASE(128, 4)
     TQ_TMA_CASE(128, 8) TQ_TMA_CASE(32, 1) TQ_TMA_CASE(32, 2) TQ_TMA_CASE(32, 4)

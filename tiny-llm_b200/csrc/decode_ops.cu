@@ -716,12 +716,14 @@ constexpr int kRouterWarps = 4;
 constexpr int kRouterHid = 16;  // hidden elements per thread and chunk (H <= 2048 in one)
 constexpr int kRouterChunk = 32 * 4 * 16;  // floats of a row one warp loads at once
 
+template <bool STAMP>
 __global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(
     const float *__restrict__ h, const float *__restrict__ norm_w, float eps, int H,
     const float *__restrict__ W, int E, int k, float *__restrict__ logits, int *__restrict__ idx,
     float *__restrict__ wts, unsigned int *ticket, Stamp stamp) {
     extern __shared__ __align__(16) float xn[];  // [H]
-    stamp_mark(stamp, 0);
+    StampRegs stamp_r;
+    stamp_enter<STAMP>(stamp, stamp_r);
     __shared__ double s_red[kRouterWarps];
     __shared__ bool s_last;
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
@@ -736,8 +738,9 @@ __global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(
         const int c = 4 * (lane + 32 * j);
         wv[j] = (vec && c < H) ? *reinterpret_cast<const float4 *>(row + c) : make_float4(0, 0, 0, 0);
     }
+    stamp_step<STAMP>(stamp, stamp_r);
     griddep_wait();
-    stamp_mark(stamp, 1);
+    stamp_waited<STAMP>(stamp, stamp_r);
     griddep_launch();
     // the hidden vector and the norm weights, every load issued before any is used
     // (a chunk of kRouterHid per thread at a time)
@@ -807,22 +810,25 @@ __global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(
     if (t == 0) s_last = atomicAdd(ticket, 1u) == gridDim.x - 1;
     __syncthreads();
     if (!s_last) {
-        stamp_mark(stamp, 2);
+        stamp_exit<STAMP>(stamp, stamp_r);
         return;
     }
     __threadfence();
     if (warp == 0) topk_softmax_warp(logits, E, k, idx, wts);
     if (t == 0) *ticket = 0u;  // ready for the next launch (graph replay)
-    stamp_exit(stamp);
+    stamp_exit<STAMP>(stamp, stamp_r);
 }
 
 // acc = sum_t w_t * o_t in router order, then h += acc, with the reference's fp32
 // rounding points (runtime/qwen_forward_token.cpp:604-609, :627-631).
+template <bool STAMP>
 __global__ void moe_combine_kernel(float *__restrict__ h, const float *__restrict__ o,
                                    const float *__restrict__ wts, int k, int H, Stamp stamp) {
-    stamp_mark(stamp, 0);
+    StampRegs stamp_r;
+    stamp_enter<STAMP>(stamp, stamp_r);
+    stamp_step<STAMP>(stamp, stamp_r);
     griddep_wait();
-    stamp_mark(stamp, 1);
+    stamp_waited<STAMP>(stamp, stamp_r);
     griddep_launch();
     constexpr int kMax = 16;  // expert outputs loaded at once (k is at most 32)
     for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < H; j += gridDim.x * blockDim.x) {
@@ -842,7 +848,7 @@ __global__ void moe_combine_kernel(float *__restrict__ h, const float *__restric
         }
         h[j] = __fadd_rn(hj, acc);
     }
-    stamp_exit(stamp);
+    stamp_exit<STAMP>(stamp, stamp_r);
 }
 
 // Expert parallelism: the chosen experts as this rank's local indices (-1: another
@@ -1203,16 +1209,17 @@ int launch_moe_router(const float *h, const float *norm_w, float eps, int H, con
                  "moe router: E %d k %d H %d", E, k, H);
     const size_t smem = (size_t)H * 4;
     TQ_CHECK_ARG(smem <= 48 * 1024, "moe router: hidden %d too large", H);
-    return launch_pdl(moe_router_kernel, (E + kRouterWarps - 1) / kRouterWarps, kRouterWarps * 32,
-                      smem, pdl, st, h, norm_w, eps, H, W, E, k, logits, idx, wts, ticket, stamp);
+    return launch_pdl(stamp.base ? moe_router_kernel<true> : moe_router_kernel<false>,
+                      (E + kRouterWarps - 1) / kRouterWarps, kRouterWarps * 32, smem, pdl, st, h,
+                      norm_w, eps, H, W, E, k, logits, idx, wts, ticket, stamp);
 }
 
 int launch_moe_combine(float *h, const float *o, const float *wts, int k, int H, bool pdl,
                        cudaStream_t st, const Stamp &stamp) {
     TQ_CHECK_ARG(k > 0 && H > 0, "moe combine: k %d H %d", k, H);
     const int threads = 256;
-    return launch_pdl(moe_combine_kernel, (H + threads - 1) / threads, threads, 0, pdl, st, h, o,
-                      wts, k, H, stamp);
+    return launch_pdl(stamp.base ? moe_combine_kernel<true> : moe_combine_kernel<false>,
+                      (H + threads - 1) / threads, threads, 0, pdl, st, h, o, wts, k, H, stamp);
 }
 
 int launch_topk_softmax(const float *logits, int n, int k, int *idx, float *w, cudaStream_t st) {

@@ -365,9 +365,10 @@ Stamp tl_next(tqb200_engine *e, int kind) {
     Stamp s;
     if (!e->tl_capture || !e->tl) return s;
     const int i = (int)e->tl_kind.size();
-    if (3 * (i + 1) > e->tl_stride) return s;
+    const int words = 3 * kStampCtas;  // per launch and step
+    if (words * (i + 1) > e->tl_stride) return s;
     e->tl_kind.push_back(kind);
-    s.base = e->tl + 3 * (size_t)i;
+    s.base = e->tl + (size_t)words * i;
     s.step = e->gen_count;
     s.stride = e->tl_stride;
     s.cap = e->tl_cap;
@@ -1560,8 +1561,9 @@ int tqb200_engine_set_timeline(tqb200_engine *e, int max_steps) {
     e->tl_cap = e->tl_steps = 0;
     e->tl_kind.clear();
     if (max_steps == 0) return TQB200_OK;
-    // room for every launch of a step: at most 8 per layer plus the head
-    e->tl_stride = 3 * (8 * e->d.n_layers + 16);
+    // room for every launch of a step (at most 8 per layer plus the head), kStampCtas
+    // CTAs of three words each
+    e->tl_stride = 3 * kStampCtas * (8 * e->d.n_layers + 16);
     const size_t bytes = (size_t)max_steps * e->tl_stride * 8;
     TQ_CUDA_TRY(cudaMalloc(&e->tl, bytes));
     TQ_CUDA_TRY(cudaMemset(e->tl, 0xFF, bytes));
@@ -1584,24 +1586,34 @@ int tqb200_engine_timeline(const tqb200_engine *e, int n_kinds, double *excl_ms,
     TQ_CUDA_TRY(cudaStreamSynchronize(e->stream));
     TQ_CUDA_TRY(cudaMemcpy(h.data(), e->tl, h.size() * 8, cudaMemcpyDeviceToHost));
     const unsigned long long none = ~0ull;
+    const int words = 3 * kStampCtas;
     int good = 0;
     for (int s = 0; s < ns; ++s) {
-        const unsigned long long *r = h.data() + (size_t)s * e->tl_stride;
+        // per launch: first CTA in, first CTA past its wait, last CTA out
+        std::vector<unsigned long long> entry(nl, none), wait(nl, none), exit(nl, 0);
         bool complete = true;
-        for (int i = 0; i < nl && complete; ++i)
-            complete = r[3 * i] != none && r[3 * i + 2] != none;
+        for (int i = 0; i < nl; ++i) {
+            const unsigned long long *r = h.data() + (size_t)s * e->tl_stride + (size_t)i * words;
+            for (int c = 0; c < kStampCtas; ++c) {
+                if (r[3 * c] == none) continue;
+                entry[i] = std::min(entry[i], r[3 * c]);
+                wait[i] = std::min(wait[i], r[3 * c + 1]);
+                exit[i] = std::max(exit[i], r[3 * c + 2]);
+            }
+            complete = complete && entry[i] != none;
+        }
         if (!complete) continue;  // a launch left no record (error path): skip the step
+        // in-step time of launch i: its first wait to the next launch's first wait (the
+        // last launch: to its last exit); time from launch: first entry to last exit
         unsigned long long first = none, last = 0;
         for (int i = 0; i < nl; ++i) {
-            const unsigned long long entry = r[3 * i];
-            const unsigned long long wait = r[3 * i + 1] != none ? r[3 * i + 1] : entry;
-            const unsigned long long exit = ~r[3 * i + 2];
-            first = std::min(first, entry);
-            last = std::max(last, exit);
+            first = std::min(first, entry[i]);
+            last = std::max(last, exit[i]);
             const int k = e->tl_kind[i];
             if (k < 0 || k >= n_kinds) continue;
-            excl_ms[k] += exit > wait ? (double)(exit - wait) * 1e-6 : 0.0;
-            incl_ms[k] += exit > entry ? (double)(exit - entry) * 1e-6 : 0.0;
+            const unsigned long long end = i + 1 < nl ? wait[i + 1] : exit[i];
+            excl_ms[k] += end > wait[i] ? (double)(end - wait[i]) * 1e-6 : 0.0;
+            incl_ms[k] += exit[i] > entry[i] ? (double)(exit[i] - entry[i]) * 1e-6 : 0.0;
             if (good == 0) launches[k] += 1;
         }
         *span_ms += (double)(last - first) * 1e-6;

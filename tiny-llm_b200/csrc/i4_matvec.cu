@@ -20,10 +20,11 @@
 //    rows slot, slot+S, ... of every pass.  512 threads, one CTA per SM.
 //  * Math: activations split into three int8 digits with one scale for the
 //    whole vector (x ~ (d0 + d1/254 + d2/254^2) * max|x|/127, error
-//    <= 3.1e-8 * max|x|), built once per CTA from activations held in
-//    registers, and the nibble dots run as exact integer dp4a (two masks, no
-//    shift: high nibbles enter as 16x bytes; 6 dp4a per 8 weights, six
-//    independent accumulators), using
+//    <= 6.1e-8 * max|x|; a fourth digit, error / 254, when most of the values
+//    lie below max/64: outlier channels), built once per CTA from
+//    activations held in registers, and the nibble dots run as exact integer
+//    dp4a (two masks, no shift: high nibbles enter as 16x bytes; 6 dp4a per 8
+//    weights, 8 with the fourth digit, independent accumulators), using
 //        sum_i (q_i - z) s x_i = s * (sum_i q_i x_i - z * sum_i x_i).
 //    A pass needs one named barrier among the consumers (partials are
 //    double-buffered); a row's segment partials are summed by one lane, and the
@@ -35,6 +36,7 @@
 // Accumulation is fp32 (the reference accumulates in double); results agree
 // to ~1e-6 relative, inside the 1e-4 max-relative tolerance of the tests.
 #include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -77,6 +79,13 @@ __device__ __forceinline__ int pass_of(const MvParams &P, int i) {
     const int pps = P.erows / P.R;
     const int pl = sub + i * nsub;
     return (pl < pps && sub < nsub) ? slot * pps + pl : INT_MAX;
+}
+
+// Reciprocal to about one ulp (the digit planes below need no exact quotient).
+__device__ __forceinline__ float rcp_approx(float x) {
+    float r;
+    asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
 }
 
 __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
@@ -234,7 +243,7 @@ template <int NW> struct DigitLayout { static constexpr int stride = 6 * NW + 4;
 constexpr int kI4Threads = 512;  // producer warp + 15 consumer warps, one CTA per SM
 constexpr int kI4MaxItems = 3;   // 8-column activation chunks per thread (K <= 12288)
 
-template <int SEG>
+template <int SEG, bool STAMP>
 __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_constant__ MvParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int NW = SEG / 8;
@@ -266,7 +275,8 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
     __shared__ int s_bi[32];
     __shared__ bool s_last;
     const bool bulk_x = P.x_bulk != 0;
-    stamp_mark(P.stamp, 0);
+    StampRegs stamp_r;
+    stamp_enter<STAMP>(P.stamp, stamp_r);
 
     if (t == 0) {
         for (int s = 0; s < P.stages; ++s) {
@@ -293,8 +303,9 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
     }
     __syncthreads();  // barrier initialisation visible to every thread
     // weights are in flight; now wait for the producer of x and let our dependents start
+    stamp_step<STAMP>(P.stamp, stamp_r);
     griddep_wait();
-    stamp_mark(P.stamp, 1);
+    stamp_waited<STAMP>(P.stamp, stamp_r);
     griddep_launch();
     if (P.eidx && t == 0) {  // expert weights: which ones is known only now
         for (int s = 0; s < P.stages; ++s) {
@@ -354,6 +365,10 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
         }
         __syncthreads();  // norm weights in shared memory
     }
+    // pass A: max |value| (under RMSNorm, of x * w: the RMSNorm scale is common to all
+    // columns) and the RMSNorm sum of squares in double as rmsnorm_ref; block-reduced
+    // (one barrier)
+    float am_mine = 0.0f;  // this thread's own max
     {
         double ss = 0.0;
         float am = 0.0f;
@@ -364,14 +379,15 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
                 const float v = xv[it][k];
+                float a = v;
                 if (norm) {
                     ss += (double)v * (double)v;
-                    am = fmaxf(am, fabsf(v * (8 * c + k < K ? wsm[8 * c + k] : 0.0f)));
-                } else {
-                    am = fmaxf(am, fabsf(v));
+                    a = v * (8 * c + k < K ? wsm[8 * c + k] : 0.0f);
                 }
+                am = fmaxf(am, fabsf(a));
             }
         }
+        am_mine = am;
         if (norm) ss = warp_sum_d(ss);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
@@ -382,7 +398,7 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
     }
     __syncthreads();
     float rms_scale = 1.0f, amax = 0.0f;
-    {  // the warps' partials, summed across a warp's lanes (every warp, no extra barrier)
+    {  // the warps' partials, reduced across a warp's lanes (every warp, no extra barrier)
         const int nwp = (int)(blockDim.x >> 5);
         double tot = lane < nwp ? s_rd[lane] : 0.0;
         amax = lane < nwp ? s_am[lane] : 0.0f;
@@ -392,23 +408,34 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
         if (norm) {
             const float mean_sq = (float)(tot / K);
             rms_scale = 1.0f / sqrtf(__fadd_rn(mean_sq, P.x.eps));
-            amax = amax * rms_scale * 1.0000005f;  // bound on |(x*r)*w| after rounding
         }
     }
+    // three digits leave an error of up to 6.1e-8 of max |x| in every element; when the
+    // max stands far out of the bulk of the vector (outlier channels), that is coarse for
+    // the bulk, and a fourth digit (error / 254) is kept: when fewer than half of the
+    // threads holding activations see a value above max/64 among their own (one counting
+    // barrier; the choice is uniform over the CTA)
+    const int holders = min((int)blockDim.x, nchunks);
+    const bool four = 2 * __syncthreads_count(t < holders && am_mine * 64.0f > amax) < holders;
+    if (norm) amax = amax * rms_scale * 1.0000005f;  // bound on |(x*r)*w| after rounding
     // pass B, per chunk: RMSNorm applied, the chunk sum, and the dp4a digit planes of
     // the vector with ONE scale for all of it:
-    //   x ~ (d0 + d1/254 + d2/254^2) * s0,  s0 = max|x| / 127  (error <= 3.1e-8 max|x|);
+    //   x ~ (d0 + d1/254 + d2/254^2 [+ d3/254^3]) * s0,  s0 = max|x| / 127;
     // word order per chunk (lo, hi) x (d0, d1, d2), lo = even columns, hi = odd ones,
-    // matching the nibble order of a weight word.  Rounding to the nearest integer
-    // uses the 1.5*2^23 trick (one FFMA; the digit's byte is the low byte of the
-    // sum's bits), so no float/int conversions; |digit| <= 127 by construction.
-    // (the scales need not be exact quotients: any s0 >= max|x| / 127 to within a
-    // few ulp keeps every digit within +-127)
+    // matching the nibble order of a weight word (the fourth digit's lo, hi words in a
+    // plane of their own).  Rounding to the nearest integer uses the 1.5*2^23 trick (one
+    // FFMA; the digit's byte is the low byte of the sum's bits), so no float/int
+    // conversions; |digit| <= 127 by construction (any s0 >= max|x| / 127 to within a
+    // few ulp keeps every digit within +-127).  Approximate reciprocals suffice: a digit
+    // is round(r * i) of the residual r the digits before it left, so an i off by an ulp
+    // moves |digit| by ~1e-5 (never past 127.5) and the next digit absorbs the rest.
     const float dsc0 = amax > 0.0f ? amax * (1.0f / 127.0f) : 1.0f;
     const float dsc1 = dsc0 * (1.0f / 254.0f), dsc2 = dsc1 * (1.0f / 254.0f);
+    const float dsc3 = four ? dsc2 * (1.0f / 254.0f) : 0.0f;
+    uint2 d3w[kI4MaxItems];  // fourth digit (lo, hi words) of this thread's chunks
     {
         constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
-        const float i0 = __frcp_rn(dsc0), i1 = __frcp_rn(dsc1), i2 = __frcp_rn(dsc2);
+        const float i0 = rcp_approx(dsc0), i1 = i0 * 254.0f, i2 = i1 * 254.0f, i3 = i2 * 254.0f;
 #pragma unroll
         for (int it = 0; it < kI4MaxItems; ++it) {
             const int c = t + it * (int)blockDim.x;
@@ -422,6 +449,7 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
             }
             csum[c] = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
             uint32_t d0[8], d1[8], d2[8];  // digit k of each column, in the low byte
+            float r2s[8];
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
                 const float t0 = fmaf(v[k], i0, kRound);
@@ -432,6 +460,7 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
                 d0[k] = __float_as_uint(t0);
                 d1[k] = __float_as_uint(t1);
                 d2[k] = __float_as_uint(t2);
+                r2s[k] = r2;
             }
             // low bytes of columns (0,2,4,6) -> lo word, (1,3,5,7) -> hi word
             auto pack = [](const uint32_t *d, int o) {
@@ -446,9 +475,50 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
             dst[0] = make_uint2(wd[0], wd[1]);
             dst[1] = make_uint2(wd[2], wd[3]);
             dst[2] = make_uint2(wd[4], wd[5]);
+            if (four) {
+                uint32_t d3[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const float r3 = fmaf(-(__uint_as_float(d2[k]) - kRound), dsc2, r2s[k]);
+                    d3[k] = __float_as_uint(fmaf(r3, i3, kRound));
+                }
+                d3w[it] = make_uint2(pack(d3, 0), pack(d3, 1));
+            }
         }
     }
     __syncthreads();
+
+    // consumer thread (slot, sg) of warps 1.. holds its segment's digit words in
+    // registers for the whole kernel
+    const int tc = t - 32;
+    const int slot = tc / nt;
+    const int sg = tc - slot * nt;
+    const bool active = warp > 0 && slot < S;
+    float X = 0.0f;  // segment sum (zero-point term)
+    uint32_t xd[6 * NW];
+    if (active) {
+#pragma unroll
+        for (int ci = 0; ci < NW; ++ci) X += csum[sg * NW + ci];
+        const uint4 *src = reinterpret_cast<const uint4 *>(dig + (size_t)sg * DS);
+#pragma unroll
+        for (int w = 0; w < 6 * NW / 4; ++w) {
+            const uint4 v4 = src[w];
+            xd[4 * w + 0] = v4.x, xd[4 * w + 1] = v4.y, xd[4 * w + 2] = v4.z, xd[4 * w + 3] = v4.w;
+        }
+    }
+    // outlier channels: with the first three digits in registers the digit rows are free,
+    // and the fourth digit plane goes there (2 words per chunk, segment sg at 2 NW sg),
+    // so it costs no shared memory beyond the three-digit layout
+    uint2 *dig3 = reinterpret_cast<uint2 *>(dig);
+    if (four) {
+        __syncthreads();
+#pragma unroll
+        for (int it = 0; it < kI4MaxItems; ++it) {
+            const int c = t + it * (int)blockDim.x;
+            if (c < nchunks) dig3[c] = d3w[it];
+        }
+        __syncthreads();
+    }
 
     float bv = -INFINITY;
     int bi = INT_MAX;
@@ -471,10 +541,7 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
         }
     } else {
         // ---- consumers: thread (slot, seg) over the rows of every pass
-        const int tc = t - 32, cw = warp - 1;
-        const int slot = tc / nt;
-        const int sg = tc - slot * nt;
-        const bool active = slot < S;
+        const int cw = warp - 1;
         const int GB = 4 + G / 2;
         const size_t RB = (size_t)((K + G - 1) / G) * GB;
         const int spg = G / SEG;
@@ -482,119 +549,137 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
         const uint32_t hdr_off = (uint32_t)g * GB;
         const uint32_t seg_off = hdr_off + 4u + (uint32_t)(sg - g * spg) * (SEG / 2);
         const int ncons = ncw * 32;
-        float X = 0.0f;  // segment sum (zero-point term)
-        uint32_t xd[6 * NW];
-        if (active) {
+        // the pass loop, compiled twice: with and without the fourth digit plane (the
+        // choice is uniform over the CTA, so each thread runs one straight-line version)
+        auto passes = [&](auto four_c) {
+            constexpr bool kFour = decltype(four_c)::value;
+            for (int i_pass = 0;; ++i_pass) {
+                const int p = pass_of(P, i_pass);
+                if (p >= total) break;
+                const int s = i_pass % P.stages;
+                const uint32_t parity = (uint32_t)(i_pass / P.stages) & 1u;
+                int j = 0;
+                while (j + 1 < P.n_jobs && p >= P.pass_begin[j + 1]) ++j;
+                const I4Job &job = P.job[j];
+                const int row0 = (p - P.pass_begin[j]) * P.R;
+                float *rb = red + (size_t)(i_pass & 1) * red_n;  // double-buffered partials
+                // bias / residual of the rows this warp reduces (below), fetched before the
+                // weight wait; chunk c of 32 rows belongs to consumer warp (i_pass + c) % ncw
+                float pre_b0 = 0.0f, pre_b1 = 0.0f, pre_r0 = 0.0f, pre_r1 = 0.0f;
+                if (!P.pair) {
+                    for (int c = 0, k = 0; c * 32 < P.R && k < 2; ++c) {
+                        if ((i_pass + c) % ncw != cw) continue;
+                        const int rl = c * 32 + lane, row = row0 + rl;
+                        if (rl < P.R && row < job.rows) {
+                            const float b = job.bias ? job.bias[row] : 0.0f;
+                            const float r = job.resid ? job.resid[row] : 0.0f;
+                            if (k == 0) pre_b0 = b, pre_r0 = r;
+                            else pre_b1 = b, pre_r1 = r;
+                        }
+                        ++k;
+                    }
+                }
+                const bool ok = mbar_wait(&full[s], parity, kWaitCycles);
+                const size_t half_bytes = P.stage_bytes / 2;
+                // one row's segment partial from the stage (0 past the matrix)
+                auto seg_part = [&](int jb, int rl) -> float {
+                    const uint8_t *sb = stage_base + (size_t)s * P.stage_bytes +
+                                        (jb ? half_bytes + s_head[kMaxStages + s] : s_head[s]);
+                    if (row0 + rl >= job.rows) return 0.0f;
+                    const uint8_t *rp = sb + (size_t)rl * RB;
+                    const uint32_t hv = lds_u32(rp + hdr_off);
+                    const float sc = h2f((uint16_t)(hv & 0xFFFFu));
+                    const float zr = h2f((uint16_t)(hv >> 16));
+                    // low nibbles as bytes, high nibbles as 16x bytes (one mask each, no
+                    // shift): six independent accumulators, the high ones scaled back by 16
+                    int L0 = 0, L1 = 0, L2 = 0, H0 = 0, H1 = 0, H2 = 0;
+                    float dot3 = 0.0f;
+                    if constexpr (!kFour) {
 #pragma unroll
-            for (int ci = 0; ci < NW; ++ci) X += csum[sg * NW + ci];
-            const uint4 *src = reinterpret_cast<const uint4 *>(dig + (size_t)sg * DS);
+                        for (int i = 0; i < NW; ++i) {
+                            const uint32_t wd = lds_u32(rp + seg_off + 4 * i);
+                            const uint32_t lo = wd & 0x0F0F0F0Fu, hi = wd & 0xF0F0F0F0u;
+                            L0 = dp4a_us(lo, xd[6 * i + 0], L0);
+                            H0 = dp4a_us(hi, xd[6 * i + 1], H0);
+                            L1 = dp4a_us(lo, xd[6 * i + 2], L1);
+                            H1 = dp4a_us(hi, xd[6 * i + 3], H1);
+                            L2 = dp4a_us(lo, xd[6 * i + 4], L2);
+                            H2 = dp4a_us(hi, xd[6 * i + 5], H2);
+                        }
+                    } else {  // outlier channels: the fourth digit plane from shared memory
+                        int L3 = 0, H3 = 0;
+                        const uint2 *x3 = dig3 + (size_t)sg * NW;
 #pragma unroll
-            for (int w = 0; w < 6 * NW / 4; ++w) {
-                const uint4 v4 = src[w];
-                xd[4 * w + 0] = v4.x, xd[4 * w + 1] = v4.y, xd[4 * w + 2] = v4.z, xd[4 * w + 3] = v4.w;
-            }
-        }
-        for (int i_pass = 0;; ++i_pass) {
-            const int p = pass_of(P, i_pass);
-            if (p >= total) break;
-            const int s = i_pass % P.stages;
-            const uint32_t parity = (uint32_t)(i_pass / P.stages) & 1u;
-            int j = 0;
-            while (j + 1 < P.n_jobs && p >= P.pass_begin[j + 1]) ++j;
-            const I4Job &job = P.job[j];
-            const int row0 = (p - P.pass_begin[j]) * P.R;
-            float *rb = red + (size_t)(i_pass & 1) * red_n;  // double-buffered partials
-            // bias / residual of the rows this warp reduces (below), fetched before the
-            // weight wait; chunk c of 32 rows belongs to consumer warp (i_pass + c) % ncw
-            float pre_b0 = 0.0f, pre_b1 = 0.0f, pre_r0 = 0.0f, pre_r1 = 0.0f;
-            if (!P.pair) {
-                for (int c = 0, k = 0; c * 32 < P.R && k < 2; ++c) {
+                        for (int i = 0; i < NW; ++i) {
+                            const uint32_t wd = lds_u32(rp + seg_off + 4 * i);
+                            const uint32_t lo = wd & 0x0F0F0F0Fu, hi = wd & 0xF0F0F0F0u;
+                            const uint2 d3 = x3[i];
+                            L0 = dp4a_us(lo, xd[6 * i + 0], L0);
+                            H0 = dp4a_us(hi, xd[6 * i + 1], H0);
+                            L1 = dp4a_us(lo, xd[6 * i + 2], L1);
+                            H1 = dp4a_us(hi, xd[6 * i + 3], H1);
+                            L2 = dp4a_us(lo, xd[6 * i + 4], L2);
+                            H2 = dp4a_us(hi, xd[6 * i + 5], H2);
+                            L3 = dp4a_us(lo, d3.x, L3);
+                            H3 = dp4a_us(hi, d3.y, H3);
+                        }
+                        dot3 = (float)(L3 + (H3 >> 4)) * dsc3;
+                    }
+                    const int D0 = L0 + (H0 >> 4), D1 = L1 + (H1 >> 4), D2 = L2 + (H2 >> 4);
+                    const float dot = fmaf((float)D0, dsc0, fmaf((float)D1, dsc1, fmaf((float)D2, dsc2, dot3)));
+                    return sc * fmaf(-zr, X, dot);
+                };
+                if (active && ok) {
+                    // rows slot, slot+S, ... of each job; two at a time for independent chains
+                    for (int jb = 0; jb < np; ++jb) {
+                        for (int r = 0; r < P.RP; r += 2) {
+                            const int rl0 = slot + r * S, rl1 = rl0 + S;
+                            const bool h0 = rl0 < P.R, h1 = r + 1 < P.RP && rl1 < P.R;
+                            float p0 = 0.0f, p1 = 0.0f;
+                            if (h0) p0 = seg_part(jb, rl0);
+                            if (h1) p1 = seg_part(jb, rl1);
+                            if (h0) rb[(jb * P.R + rl0) * ntp + sg] = p0;
+                            if (h1) rb[(jb * P.R + rl1) * ntp + sg] = p1;
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with stage s
+                // partials of this pass complete; an error anywhere stops every consumer
+                if (consumer_sync_or(ncons, !ok)) {
+                    c_err = true;
+                    break;
+                }
+                // rows of this pass, 32 per warp (a lane per row): the row's segment partials
+                // summed by one lane.
+                // Chunk c of 32 rows goes to consumer warp (i_pass + c) % ncw, so the
+                // reductions of consecutive passes spread over the warps.
+                for (int c = 0, k = 0; c * 32 < P.R; ++c) {
                     if ((i_pass + c) % ncw != cw) continue;
+                    const int kk = k++;
                     const int rl = c * 32 + lane, row = row0 + rl;
-                    if (rl < P.R && row < job.rows) {
-                        const float b = job.bias ? job.bias[row] : 0.0f;
-                        const float r = job.resid ? job.resid[row] : 0.0f;
-                        if (k == 0) pre_b0 = b, pre_r0 = r;
-                        else pre_b1 = b, pre_r1 = r;
+                    if (rl >= P.R || row >= job.rows) continue;
+                    float v = row_sum(rb + (size_t)rl * ntp, nt);
+                    if (P.pair) {
+                        const float u = row_sum(rb + (size_t)(P.R + rl) * ntp, nt);
+                        // swiglu_ref (kernels/silu/swiglu_ref.cpp:41-52) on (gate, up)
+                        v = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), u);
+                    } else {
+                        const float b_ = kk == 0 ? pre_b0 : kk == 1 ? pre_b1 : (job.bias ? job.bias[row] : 0.0f);
+                        const float r_ = kk == 0 ? pre_r0 : kk == 1 ? pre_r1 : (job.resid ? job.resid[row] : 0.0f);
+                        if (job.bias) v += b_;
+                        if (job.resid) v = r_ + v;
                     }
-                    ++k;
+                    if (P.eidx && P.eidx[row / P.erows] == -1) continue;  // another rank's expert
+                    job.y[row] = v;
+                    if (P.am.token && j == 0) better(bv, bi, v, row + P.am.row_offset);
                 }
             }
-            const bool ok = mbar_wait(&full[s], parity, kWaitCycles);
-            const size_t half_bytes = P.stage_bytes / 2;
-            // one row's segment partial from the stage (0 past the matrix)
-            auto seg_part = [&](int jb, int rl) -> float {
-                const uint8_t *sb = stage_base + (size_t)s * P.stage_bytes +
-                                    (jb ? half_bytes + s_head[kMaxStages + s] : s_head[s]);
-                if (row0 + rl >= job.rows) return 0.0f;
-                const uint8_t *rp = sb + (size_t)rl * RB;
-                const uint32_t hv = lds_u32(rp + hdr_off);
-                const float sc = h2f((uint16_t)(hv & 0xFFFFu));
-                const float zr = h2f((uint16_t)(hv >> 16));
-                // low nibbles as bytes, high nibbles as 16x bytes (one mask each, no
-                // shift): six independent accumulators, the high ones scaled back by 16
-                int L0 = 0, L1 = 0, L2 = 0, H0 = 0, H1 = 0, H2 = 0;
-#pragma unroll
-                for (int i = 0; i < NW; ++i) {
-                    const uint32_t wd = lds_u32(rp + seg_off + 4 * i);
-                    const uint32_t lo = wd & 0x0F0F0F0Fu, hi = wd & 0xF0F0F0F0u;
-                    L0 = dp4a_us(lo, xd[6 * i + 0], L0);
-                    H0 = dp4a_us(hi, xd[6 * i + 1], H0);
-                    L1 = dp4a_us(lo, xd[6 * i + 2], L1);
-                    H1 = dp4a_us(hi, xd[6 * i + 3], H1);
-                    L2 = dp4a_us(lo, xd[6 * i + 4], L2);
-                    H2 = dp4a_us(hi, xd[6 * i + 5], H2);
-                }
-                const int D0 = L0 + (H0 >> 4), D1 = L1 + (H1 >> 4), D2 = L2 + (H2 >> 4);
-                const float dot = fmaf((float)D0, dsc0, fmaf((float)D1, dsc1, (float)D2 * dsc2));
-                return sc * fmaf(-zr, X, dot);
-            };
-            if (active && ok) {
-                // rows slot, slot+S, ... of each job; two at a time for independent chains
-                for (int jb = 0; jb < np; ++jb) {
-                    for (int r = 0; r < P.RP; r += 2) {
-                        const int rl0 = slot + r * S, rl1 = rl0 + S;
-                        const bool h0 = rl0 < P.R, h1 = r + 1 < P.RP && rl1 < P.R;
-                        float p0 = 0.0f, p1 = 0.0f;
-                        if (h0) p0 = seg_part(jb, rl0);
-                        if (h1) p1 = seg_part(jb, rl1);
-                        if (h0) rb[(jb * P.R + rl0) * ntp + sg] = p0;
-                        if (h1) rb[(jb * P.R + rl1) * ntp + sg] = p1;
-                    }
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with stage s
-            // partials of this pass complete; an error anywhere stops every consumer
-            if (consumer_sync_or(ncons, !ok)) {
-                c_err = true;
-                break;
-            }
-            // rows of this pass, 32 per warp (a lane per row): the row's segment partials
-            // summed by one lane.
-            // Chunk c of 32 rows goes to consumer warp (i_pass + c) % ncw, so the
-            // reductions of consecutive passes spread over the warps.
-            for (int c = 0, k = 0; c * 32 < P.R; ++c) {
-                if ((i_pass + c) % ncw != cw) continue;
-                const int kk = k++;
-                const int rl = c * 32 + lane, row = row0 + rl;
-                if (rl >= P.R || row >= job.rows) continue;
-                float v = row_sum(rb + (size_t)rl * ntp, nt);
-                if (P.pair) {
-                    const float u = row_sum(rb + (size_t)(P.R + rl) * ntp, nt);
-                    // swiglu_ref (kernels/silu/swiglu_ref.cpp:41-52) on (gate, up)
-                    v = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), u);
-                } else {
-                    const float b_ = kk == 0 ? pre_b0 : kk == 1 ? pre_b1 : (job.bias ? job.bias[row] : 0.0f);
-                    const float r_ = kk == 0 ? pre_r0 : kk == 1 ? pre_r1 : (job.resid ? job.resid[row] : 0.0f);
-                    if (job.bias) v += b_;
-                    if (job.resid) v = r_ + v;
-                }
-                if (P.eidx && P.eidx[row / P.erows] == -1) continue;  // another rank's expert
-                job.y[row] = v;
-                if (P.am.token && j == 0) better(bv, bi, v, row + P.am.row_offset);
-            }
-        }
+        };
+        if (four)
+            passes(std::true_type{});
+        else
+            passes(std::false_type{});
     }
     if (c_err && t == 32) s_err = 1;
     __syncthreads();  // producer and consumers done
@@ -633,7 +718,7 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
             }
         }
     }
-    stamp_exit(P.stamp);
+    stamp_exit<STAMP>(P.stamp, stamp_r);
 }
 
 // Fallback for odd group sizes or unaligned bases: one warp per row, byte loads.
@@ -867,10 +952,10 @@ int grid_for(Kern k, int block, size_t smem, int work) {
     return std::max(1, std::min(work, per_sm * num_sms()));
 }
 
-template <int SEG>
+template <int SEG, bool STAMP>
 int launch_tma(const MvParams &P, const Shape &L, int passes, bool pdl, cudaStream_t st,
                int grid_fixed = 0) {
-    auto k = i4_mv_tma_kernel<SEG>;
+    auto k = i4_mv_tma_kernel<SEG, STAMP>;
     static KernelSmem attr_set;
     int smem_max = 0;
     TQ_CUDA_TRY(smem_limit_once(k, attr_set, &smem_max));
@@ -982,8 +1067,12 @@ int launch_i4_matvec_ex(const I4Job *jobs, int n_jobs, int in_dim, int group_siz
         P.stage_bytes = L.stage_bytes;
         // slot mode: a multiple of nslots CTAs, every block served by the same count
         const int grid = o.xslots ? o.nslots * std::max(1, num_sms() / o.nslots) : 0;
-        if (L.seg == 64) return launch_tma<64>(P, L, acc, o.pdl, stream, grid);
-        return launch_tma<32>(P, L, acc, o.pdl, stream, grid);
+        const bool st = P.stamp.base != nullptr;
+        if (L.seg == 64)
+            return st ? launch_tma<64, true>(P, L, acc, o.pdl, stream, grid)
+                      : launch_tma<64, false>(P, L, acc, o.pdl, stream, grid);
+        return st ? launch_tma<32, true>(P, L, acc, o.pdl, stream, grid)
+                  : launch_tma<32, false>(P, L, acc, o.pdl, stream, grid);
     }
     const int grid = std::max(1, std::min((acc + 7) / 8, num_sms() * 8));
     i4_matvec_generic_kernel<<<grid, 256, 0, stream>>>(P);

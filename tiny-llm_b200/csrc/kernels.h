@@ -12,41 +12,69 @@ namespace tqb200 {
 int num_sms();
 
 // ------------------------------------------------------------------ in-graph timeline
-// Global-timer stamps of one launch, per decode step: word 0 = the first CTA's entry,
-// word 1 = the first CTA past its dependency wait (griddepcontrol.wait returns once the
-// previous kernel has completed), word 2 = the bitwise complement of the last CTA's
-// exit.  All three are kept with atomicMin, so a 0xFF fill clears a record.  With
-// programmatic dependent launch a kernel's entry overlaps its predecessor, but the
-// intervals [word 1, exit] of consecutive launches do not overlap: they partition the
-// step.  base == nullptr turns stamping off (the default everywhere).
+// Global-timer stamps of one launch, per decode step: every CTA (up to kStampCtas of
+// them) writes three words of its own with plain stores (no atomics): when its last
+// thread entered, when that thread got past the dependency wait (griddepcontrol.wait
+// returns once the previous kernel has completed), and when it finished.  The host
+// takes, per launch, the first wait over the CTAs; a launch's in-step time runs from
+// its first wait to the next stamped launch's first wait (the last one's: to its last
+// exit), so the times of a step's launches do not overlap and add up to the step.  The
+// stamps are compiled only into a kernel's ON = true instantiation, which the launchers
+// pick when Stamp::base is set, and the timer values stay in registers until the
+// thread's exit, so a stamped CTA waits on no extra memory access or barrier.
+constexpr int kStampCtas = 256;  // CTAs of a launch with a record (lower linear index)
 struct Stamp {
-    unsigned long long *base = nullptr;  // this launch's words for step 0
+    unsigned long long *base = nullptr;  // this launch's kStampCtas x 3 words for step 0
     const int *step = nullptr;           // device step counter selecting the record
     int stride = 0;                      // words between consecutive steps' records
     int cap = 0;                         // steps with a record
 };
 
 #if defined(__CUDACC__)
+struct StampRegs {
+    unsigned long long t_enter = 0, t_wait = 0;
+    int step = -1;
+};
 __device__ __forceinline__ unsigned long long global_timer_ns() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
-// which = 0 (entry), 1 (past the dependency wait) or 2 (exit); thread (0,0,0) of a CTA.
-__device__ __forceinline__ void stamp_mark(const Stamp &s, int which) {
-    if (s.base != nullptr && threadIdx.x == 0 && threadIdx.y == 0 && threadIdx.z == 0) {
-        const int k = *s.step;
-        if (k >= 0 && k < s.cap) {
-            const unsigned long long t = global_timer_ns();
-            atomicMin(s.base + (size_t)k * s.stride + which, which == 2 ? ~t : t);
-        }
-    }
+// The CTA's last thread stamps: thread 0 of several kernels issues their bulk copies
+// at entry, which a timer read must not delay.
+__device__ __forceinline__ bool stamp_thread() {
+    return threadIdx.x == blockDim.x - 1 && threadIdx.y == blockDim.y - 1 &&
+           threadIdx.z == blockDim.z - 1;
 }
-// Exit stamp once every thread of the CTA is done (uniform: s.base is a kernel argument).
-__device__ __forceinline__ void stamp_exit(const Stamp &s) {
-    if (s.base != nullptr) {
-        __syncthreads();
-        stamp_mark(s, 2);
+// At kernel entry.
+template <bool ON>
+__device__ __forceinline__ void stamp_enter(const Stamp &s, StampRegs &r) {
+    if constexpr (ON)
+        if (stamp_thread()) r.t_enter = global_timer_ns();
+}
+// Just before griddepcontrol.wait: the step counter's load (used at the exit).
+template <bool ON>
+__device__ __forceinline__ void stamp_step(const Stamp &s, StampRegs &r) {
+    if constexpr (ON)
+        if (stamp_thread()) r.step = *s.step;
+}
+// Right after griddepcontrol.wait.
+template <bool ON>
+__device__ __forceinline__ void stamp_waited(const Stamp &s, StampRegs &r) {
+    if constexpr (ON)
+        if (stamp_thread()) r.t_wait = global_timer_ns();
+}
+// At the stamping thread's exit.
+template <bool ON>
+__device__ __forceinline__ void stamp_exit(const Stamp &s, const StampRegs &r) {
+    if constexpr (ON) {
+        const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+        if (stamp_thread() && r.step >= 0 && r.step < s.cap && cta < (unsigned)kStampCtas) {
+            unsigned long long *w = s.base + (size_t)r.step * s.stride + 3 * (size_t)cta;
+            w[0] = r.t_enter;
+            w[1] = r.t_wait;
+            w[2] = global_timer_ns();
+        }
     }
 }
 #endif

@@ -134,6 +134,7 @@ __device__ void biip_smem(float *v, int K, const float *sign, const float *scale
     __syncthreads();
 }
 
+template <bool STAMP>
 __global__ void __launch_bounds__(kVqMaxThreads) vq2_matvec_kernel(const __grid_constant__ VqParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int t = threadIdx.x, K = P.K, nm = 1 + P.pair;  // matrices this CTA reads
@@ -149,7 +150,8 @@ __global__ void __launch_bounds__(kVqMaxThreads) vq2_matvec_kernel(const __grid_
     float *red = rot + (size_t)nm * 2 * K4 / 4;             // [nm][S][nt]
     __shared__ int s_err;
     __shared__ double s_rd[32];
-    stamp_mark(P.stamp, 0);
+    StampRegs stamp_r;
+    stamp_enter<STAMP>(P.stamp, stamp_r);
 
     int j = 0;
     while (j + 1 < P.n_jobs && (int)blockIdx.x >= P.cta_begin[j + 1]) ++j;
@@ -190,8 +192,9 @@ __global__ void __launch_bounds__(kVqMaxThreads) vq2_matvec_kernel(const __grid_
             if (norm) bulk_g2s(wsm, P.x.norm_w, (uint32_t)K * 4u, bar_w);
         }
     }
+    stamp_step<STAMP>(P.stamp, stamp_r);
     griddep_wait();
-    stamp_mark(P.stamp, 1);
+    stamp_waited<STAMP>(P.stamp, stamp_r);
     griddep_launch();
     if (t == 0 && P.bulk) {
         const uint32_t xb = (uint32_t)K * 4u;
@@ -354,7 +357,7 @@ __global__ void __launch_bounds__(kVqMaxThreads) vq2_matvec_kernel(const __grid_
         }
         __syncthreads();
     }
-    stamp_exit(P.stamp);
+    stamp_exit<STAMP>(P.stamp, stamp_r);
 }
 
 // Standalone BiIP rotation (per-op entry point): one CTA, x -> y.
@@ -425,9 +428,11 @@ int launch_vq2_matvec(const VqLaunch &a, cudaStream_t st) {
     const size_t K4 = ((size_t)a.K * 4 + 15) & ~(size_t)15;
     const size_t smem = 128 + (size_t)nm * (kCbDecoded + P.region) + 2 * K4 + (size_t)nm * 3 * K4 +
                         (size_t)nm * P.S * P.nt * 4;
-    static KernelSmem attr;
+    static KernelSmem attr, attr_st;
+    const bool stamped = P.stamp.base != nullptr;
+    auto kern = stamped ? vq2_matvec_kernel<true> : vq2_matvec_kernel<false>;
     int smem_max = 0;
-    TQ_CUDA_TRY(smem_limit_once(vq2_matvec_kernel, attr, &smem_max));
+    TQ_CUDA_TRY(smem_limit_once(kern, stamped ? attr_st : attr, &smem_max));
     TQ_CHECK_ARG(smem <= (size_t)smem_max, "vq2: in_dim %d needs too much shared memory", a.K);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(ctas);
@@ -439,7 +444,7 @@ int launch_vq2_matvec(const VqLaunch &a, cudaStream_t st) {
     attr_l[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr_l;
     cfg.numAttrs = a.pdl ? 1 : 0;
-    TQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, vq2_matvec_kernel, P));
+    TQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, P));
     return TQB200_OK;
 }
 
