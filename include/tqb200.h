@@ -159,6 +159,53 @@ int tqb200_argmax(const float *logits, int n, int *index);
  * kernels/topk_softmax/topk_softmax_ref.cpp:41-78 (n <= 1024, k <= 64; ties -> lower index). */
 int tqb200_topk_softmax(const float *gate_logits, int n, int k, int *indices, float *weights);
 
+/* ---------------------------------------------- Qwen3.5 GDN ops and partial RoPE
+ * Same signatures and meaning as the reference's GDN dispatch entries
+ * (kernels/dispatch.h:389-396, the --ops-impl name) and IBackend::partial_rope
+ * (runtime/backend.h:211); semantics of kernels/gdn/gdn_ops_ref.cpp. */
+
+/* L2normInplaceFn; l2norm_inplace_ref (gdn_ops_ref.cpp:44-57). */
+int tqb200_l2norm_inplace(float *x, int n, float eps);
+/* CausalConv1dUpdateFn; causal_conv1d_update_ref (gdn_ops_ref.cpp:82-105): conv_state
+ * [dim][kernel_size-1] is updated in place, out[dim] = silu(conv). */
+int tqb200_causal_conv1d_update(const float *x, float *conv_state, const float *weight, float *out,
+                                int dim, int kernel_size);
+/* GdnStepFn; gdn_step_ref (gdn_ops_ref.cpp:134-176): one head, S [qk_dim][v_dim] in place,
+ * v_dim <= 512 (TQB200_ERR_INVALID_ARG otherwise). */
+int tqb200_gdn_step(float *S, const float *q, const float *k, const float *v, float g, float beta,
+                    float *o, int qk_dim, int v_dim);
+/* Device twin over n_heads heads at once (S [n_heads][qk_dim][v_dim], q/k [n_heads][qk_dim],
+ * v/o [n_heads][v_dim]); decay[h] = exp(g_h) and beta[h] on the device.  No reference
+ * counterpart (the reference calls gdn_step once per head). */
+int tqb200_dev_gdn_step(float *S, const float *q, const float *k, const float *v,
+                        const float *decay, const float *beta, float *o, int n_heads, int qk_dim,
+                        int v_dim, void *stream);
+/* RmsnormGatedFn; rmsnorm_gated_ref (gdn_ops_ref.cpp:203-218). */
+int tqb200_rmsnorm_gated(const float *x, const float *gate, const float *weight, float *y, int n,
+                         float eps);
+/* IBackend::partial_rope (runtime/backend.h:211); partial_rope_ref (gdn_ops_ref.cpp:233-277):
+ * rotate-half RoPE over the first rotary_dim dimensions of every head. */
+int tqb200_partial_rope(float *q, float *k, int n_heads, int n_kv_heads, int head_dim,
+                        int rotary_dim, int pos, float theta);
+
+/* ------------------------------------------------------ GPTQ-INT4, dense f32 / f16
+ * GPTQ tensor (runtime/tiny_format.h:140-182): [u32 magic][u32 flags][scales f16
+ * [n_groups][out]][qzeros f16 [n_groups][out]][g_idx u32 [in], when flags & 1]
+ * [qweight u32 [in/8][out], column-major]; in % group_size == 0, group_size % 8 == 0. */
+
+/* MatvecGPTQFn (kernels/dispatch.h:211); matvec_gptq_ref (kernels/matvec/matvec_gptq_ref.cpp). */
+int tqb200_matvec_gptq(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim,
+                       int group_size);
+/* MatmulGPTQFn (kernels/dispatch.h:258); matmul_gptq_ref: X [in x n], Y [out x n] column-major. */
+int tqb200_matmul_gptq(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim, int n,
+                       int group_size);
+int tqb200_dev_matvec_gptq(const uint8_t *w, int has_g_idx, const float *x, float *y, int out_dim,
+                           int in_dim, int group_size, void *stream);
+/* MatvecFn (kernels/dispatch.h:45; matvec_f32_ref) and MatvecF16Fn (:98; matvec_f16_ref):
+ * dense row-major weights, double accumulation. */
+int tqb200_matvec_f32(const float *w, const float *x, float *y, int out_dim, int in_dim);
+int tqb200_matvec_f16(const uint16_t *w, const float *x, float *y, int out_dim, int in_dim);
+
 /* -------------------------------------------------- whole-step decode engine
  * Replaces the GPU decode registry entry (GpuDecodeCreateFn / StepFn / ResetFn /
  * DestroyFn / LogitsFn, kernels/dispatch.h:353-378; the reference's engine is

@@ -101,6 +101,51 @@ class _Common:
         l = _f32(logits)
         return int(self._argmax(l, l.size))
 
+    def _bind_gdn_gptq(self, sig, pre):
+        self._gptq = sig(pre + "matvec_gptq", [_u8, _f, _f, _i, _i, _i])
+        self._l2n = sig(pre + "l2norm_inplace", [_f, _i, _fl])
+        self._conv = sig(pre + "causal_conv1d_update", [_f, _f, _f, _f, _i, _i])
+        self._gdn = sig(pre + "gdn_step", [_f, _f, _f, _f, _fl, _fl, _f, _i, _i])
+        self._rmsg = sig(pre + "rmsnorm_gated", [_f, _f, _f, _f, _i, _fl])
+        self._prope = sig(pre + "partial_rope", [_f, _f, _i, _i, _i, _i, _i, _fl])
+
+    def matvec_gptq(self, w, x, out_dim, in_dim, group_size):
+        y = np.zeros(out_dim, np.float32)
+        self._gptq(_u8a(w), _f32(x), y, out_dim, in_dim, group_size)
+        return y
+
+    def matmul_gptq(self, w, x_cols, M, K, N, group_size):
+        """x_cols [N, K]; returns [N, M] (matmul_gptq_ref: one matvec per column)."""
+        return np.stack([self.matvec_gptq(w, x_cols[n], M, K, group_size) for n in range(N)])
+
+    def l2norm_inplace(self, x, eps):
+        x = _f32(x).copy()
+        self._l2n(x, x.size, eps)
+        return x
+
+    def causal_conv1d_update(self, x, state, weight, dim, kernel_size):
+        st = _f32(state).copy()
+        out = np.zeros(dim, np.float32)
+        self._conv(_f32(x), st, _f32(weight), out, dim, kernel_size)
+        return out, st
+
+    def gdn_step(self, S, q, k, v, g, beta, qk_dim, v_dim):
+        S2 = _f32(S).copy()
+        o = np.zeros(v_dim, np.float32)
+        self._gdn(S2, _f32(q), _f32(k), _f32(v), g, beta, o, qk_dim, v_dim)
+        return o, S2
+
+    def rmsnorm_gated(self, x, gate, weight, eps):
+        x = _f32(x)
+        y = np.zeros_like(x)
+        self._rmsg(x, _f32(gate), _f32(weight), y, x.size, eps)
+        return y
+
+    def partial_rope(self, q, k, n_heads, n_kv_heads, head_dim, rotary_dim, pos, theta):
+        q, k = _f32(q).copy(), _f32(k).copy()
+        self._prope(q, k, n_heads, n_kv_heads, head_dim, rotary_dim, pos, theta)
+        return q, k
+
     def topk_softmax(self, logits, k):
         l = _f32(logits)
         idx = np.zeros(k, np.int32)
@@ -141,6 +186,7 @@ class Oracle(_Common):
         self._topk = sig("tqo_topk_softmax", [_f, _i, _i, _i32, _f])
         self._f2h = sig("tqo_float_to_half", [_fl], C.c_uint16)
         self._h2f = sig("tqo_half_to_float", [C.c_uint16], _fl)
+        self._bind_gdn_gptq(sig, "tqo_")
         sig("tqo_set_threads", [_i])
         sig("tqo_model_create", [C.POINTER(abi.ModelDesc), _i, _i], _vp)
         sig("tqo_model_step", [_vp, _i], _i)
@@ -276,6 +322,7 @@ class RefLib(_Common):
         self._topk = sig("tqref_topk_softmax", [_f, _i, _i, _i32, _f])
         self._f2h = sig("tqref_float_to_half", [_fl], C.c_uint16)
         self._h2f = sig("tqref_half_to_float", [C.c_uint16], _fl)
+        self._bind_gdn_gptq(sig, "tqref_")
         self._w4a8 = sig("tqref_matvec_i4_w4a8_naive", [_u8, _f, _f, _i, _i, _i])
         self._pack_sym = sig("tqref_pack_i4_rtn_symmetric", [_f, _i, _i, _i, _u8])
         self._random_vec = sig("tqref_random_vec", [C.c_size_t, C.c_uint32, _f])

@@ -17,6 +17,7 @@
 
 #include "backend_cpu.h"
 #include "dispatch.h"
+#include "gdn_ops.h"
 #include "model_loader.h"
 #include "profiler.h"
 #include "qwen_model.h"
@@ -29,6 +30,9 @@ namespace tinyqwen {
 void matvec_i4_ref(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim,
                    int group_size);
 void matvec_vq2_ref(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim);
+// kernels/matvec/matvec_gptq_ref.cpp, likewise registration-only
+void matvec_gptq_ref(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim,
+                     int group_size);
 }  // namespace tinyqwen
 
 namespace {
@@ -169,6 +173,32 @@ int tqref_argmax(const float *l, int n) { return tinyqwen::argmax_ref(l, n); }
 
 void tqref_topk_softmax(const float *g, int n, int k, int *idx, float *w) {
     tinyqwen::topk_softmax_ref(g, n, k, idx, w);
+}
+
+void tqref_matvec_gptq(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim,
+                       int group_size) {
+    tinyqwen::matvec_gptq_ref(w, x, y, out_dim, in_dim, group_size);
+}
+
+void tqref_l2norm_inplace(float *x, int n, float eps) { tinyqwen::l2norm_inplace_ref(x, n, eps); }
+
+void tqref_causal_conv1d_update(const float *x, float *state, const float *w, float *out, int dim,
+                                int kernel_size) {
+    tinyqwen::causal_conv1d_update_ref(x, state, w, out, dim, kernel_size);
+}
+
+void tqref_gdn_step(float *S, const float *q, const float *k, const float *v, float g, float beta,
+                    float *o, int qk_dim, int v_dim) {
+    tinyqwen::gdn_step_ref(S, q, k, v, g, beta, o, qk_dim, v_dim);
+}
+
+void tqref_rmsnorm_gated(const float *x, const float *gate, const float *w, float *y, int n,
+                         float eps) {
+    tinyqwen::rmsnorm_gated_ref(x, gate, w, y, n, eps);
+}
+
+void tqref_partial_rope(float *q, float *k, int nh, int nkv, int hd, int rd, int pos, float theta) {
+    tinyqwen::partial_rope_ref(q, k, nh, nkv, hd, rd, pos, theta);
 }
 
 uint16_t tqref_float_to_half(float f) { return tinyqwen::float_to_half(f); }

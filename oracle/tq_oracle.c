@@ -462,6 +462,149 @@ void tqo_topk_softmax(const float *gate_logits, int n, int k, int *indices, floa
 }
 
 /* ------------------------------------------------------------------------ */
+/* GPTQ-INT4 (kernels/matvec/matvec_gptq_ref.cpp:52-96, matmul_gptq_ref.cpp;   */
+/* layout runtime/tiny_format.h:140-182)                                       */
+/* ------------------------------------------------------------------------ */
+
+static uint32_t rd_u32(const uint8_t *p) {
+    uint32_t v;
+    memcpy(&v, p, 4);
+    return v;
+}
+static float rd_f16(const uint8_t *p) {
+    uint16_t h;
+    memcpy(&h, p, 2);
+    return tqo_half_to_float(h);
+}
+
+void tqo_matvec_gptq(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim,
+                     int group_size) {
+    const uint32_t flags = rd_u32(w + 4);
+    const int has_g_idx = (flags & 1u) != 0;
+    const int n_groups = in_dim / group_size;
+    const size_t sq = (size_t)n_groups * out_dim * 2;
+    const uint8_t *scales = w + 8, *qzeros = scales + sq;
+    const uint8_t *g_idx = has_g_idx ? qzeros + sq : NULL;
+    const uint8_t *qweight = has_g_idx ? g_idx + (size_t)in_dim * 4 : qzeros + sq;
+#pragma omp parallel for schedule(static)
+    for (int o = 0; o < out_dim; ++o) {
+        double acc = 0.0;
+        for (int c8 = 0; c8 < in_dim / 8; ++c8) {
+            const uint32_t word = rd_u32(qweight + ((size_t)c8 * out_dim + o) * 4);
+            for (int k = 0; k < 8; ++k) {
+                const int c = c8 * 8 + k;
+                const uint32_t nib = (word >> (k * 4)) & 0xFu;
+                const int g = has_g_idx ? (int)rd_u32(g_idx + (size_t)c * 4) : c / group_size;
+                const float s = rd_f16(scales + ((size_t)g * out_dim + o) * 2);
+                const float z = rd_f16(qzeros + ((size_t)g * out_dim + o) * 2);
+                const float dq = ((float)nib - z) * s;
+                acc += (double)dq * (double)x[c];
+            }
+        }
+        y[o] = (float)acc;
+    }
+}
+
+/* matmul_gptq_ref: column n of X/Y (column-major, one token per column) is a matvec. */
+void tqo_matmul_gptq(const uint8_t *w, const float *x, float *y, int M, int K, int N,
+                     int group_size) {
+    for (int n = 0; n < N; ++n)
+        tqo_matvec_gptq(w, x + (size_t)n * K, y + (size_t)n * M, M, K, group_size);
+}
+
+/* ------------------------------------------------------------------------ */
+/* Qwen3.5 GDN ops and partial RoPE (kernels/gdn/gdn_ops_ref.cpp)             */
+/* ------------------------------------------------------------------------ */
+
+static float silu_f(float x) { return x / (1.0f + expf(-x)); }
+
+/* l2norm_inplace_ref (:44-57) */
+void tqo_l2norm_inplace(float *x, int n, float eps) {
+    double sumsq = 0.0;
+    for (int i = 0; i < n; ++i) sumsq += (double)x[i] * (double)x[i];
+    const float inv = 1.0f / sqrtf((float)sumsq + eps);
+    for (int i = 0; i < n; ++i) x[i] *= inv;
+}
+
+/* causal_conv1d_update_ref (:82-105) */
+void tqo_causal_conv1d_update(const float *x, float *state, const float *weight, float *out,
+                              int dim, int kernel_size) {
+    const int sl = kernel_size - 1;
+    for (int c = 0; c < dim; ++c) {
+        float *st = state + (size_t)c * sl;
+        const float *w = weight + (size_t)c * kernel_size;
+        const float xc = x[c];
+        float acc = 0.0f;
+        for (int i = 0; i < sl; ++i) acc += w[i] * st[i];
+        acc += w[sl] * xc;
+        out[c] = silu_f(acc);
+        for (int i = 0; i < sl - 1; ++i) st[i] = st[i + 1];
+        st[sl - 1] = xc;
+    }
+}
+
+/* gdn_step_ref (:134-176) */
+void tqo_gdn_step(float *S, const float *q, const float *k, const float *v, float g, float beta,
+                  float *o, int qk_dim, int v_dim) {
+    if (v_dim <= 0 || v_dim > 512) return;
+    const float decay = expf(g);
+    float kv[512], delta[512];
+    for (int d = 0; d < v_dim; ++d) kv[d] = 0.0f;
+    for (int j = 0; j < qk_dim; ++j) {
+        float *row = S + (size_t)j * v_dim;
+        for (int d = 0; d < v_dim; ++d) {
+            row[d] *= decay;
+            kv[d] += row[d] * k[j];
+        }
+    }
+    for (int d = 0; d < v_dim; ++d) delta[d] = beta * (v[d] - kv[d]);
+    for (int j = 0; j < qk_dim; ++j) {
+        float *row = S + (size_t)j * v_dim;
+        for (int d = 0; d < v_dim; ++d) row[d] += k[j] * delta[d];
+    }
+    for (int d = 0; d < v_dim; ++d) {
+        double acc = 0.0;
+        for (int j = 0; j < qk_dim; ++j) acc += (double)S[(size_t)j * v_dim + d] * (double)q[j];
+        o[d] = (float)acc;
+    }
+}
+
+/* rmsnorm_gated_ref (:203-218) */
+void tqo_rmsnorm_gated(const float *x, const float *gate, const float *weight, float *y, int n,
+                       float eps) {
+    double sumsq = 0.0;
+    for (int i = 0; i < n; ++i) sumsq += (double)x[i] * (double)x[i];
+    const float scale = 1.0f / sqrtf((float)(sumsq / n) + eps);
+    for (int i = 0; i < n; ++i) {
+        const float normed = x[i] * scale * weight[i];
+        y[i] = normed * silu_f(gate[i]);
+    }
+}
+
+/* partial_rope_ref (:233-277) */
+void tqo_partial_rope(float *q, float *k, int n_heads, int n_kv_heads, int head_dim,
+                      int rotary_dim, int pos, float theta) {
+    const int half = rotary_dim / 2;
+    if (rotary_dim <= 0 || rotary_dim > head_dim || rotary_dim % 2 || half > 256) return;
+    float cs[256], sn[256];
+    for (int i = 0; i < half; ++i) {
+        const float exponent = -(float)(2 * i) / (float)rotary_dim;
+        const float inv_freq = powf(theta, exponent);
+        const float angle = (float)pos * inv_freq;
+        cs[i] = cosf(angle);
+        sn[i] = sinf(angle);
+    }
+    for (int h = 0; h < n_heads + n_kv_heads; ++h) {
+        float *v = (h < n_heads) ? q + (size_t)h * head_dim : k + (size_t)(h - n_heads) * head_dim;
+        for (int i = 0; i < half; ++i) {
+            const float x0 = v[i], x1 = v[i + half];
+            v[i] = x0 * cs[i] - x1 * sn[i];
+            v[i + half] = x1 * cs[i] + x0 * sn[i];
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------ */
 /* whole-model decode step (runtime/qwen_forward_token.cpp:83-742)            */
 /* ------------------------------------------------------------------------ */
 

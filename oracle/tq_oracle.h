@@ -55,6 +55,20 @@ void tqo_swiglu(float *gate, const float *up, int n);
 int tqo_argmax(const float *logits, int n);
 void tqo_topk_softmax(const float *gate_logits, int n, int k, int *indices, float *weights);
 
+void tqo_matvec_gptq(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim,
+                     int group_size);
+void tqo_matmul_gptq(const uint8_t *w, const float *x, float *y, int M, int K, int N,
+                     int group_size);
+void tqo_l2norm_inplace(float *x, int n, float eps);
+void tqo_causal_conv1d_update(const float *x, float *state, const float *weight, float *out,
+                              int dim, int kernel_size);
+void tqo_gdn_step(float *S, const float *q, const float *k, const float *v, float g, float beta,
+                  float *o, int qk_dim, int v_dim);
+void tqo_rmsnorm_gated(const float *x, const float *gate, const float *weight, float *y, int n,
+                       float eps);
+void tqo_partial_rope(float *q, float *k, int n_heads, int n_kv_heads, int head_dim,
+                      int rotary_dim, int pos, float theta);
+
 /* Whole-model greedy decode (runtime/qwen_forward_token.cpp:83-742). */
 typedef struct tqo_model tqo_model;
 tqo_model *tqo_model_create(const tqb200_model_desc *desc, int max_seq_len, int kv_fp16);

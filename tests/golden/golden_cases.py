@@ -137,3 +137,30 @@ def f2h_case():
                            [65504, 65519, 65520, 65536, 1e-8, 3e-8, 6e-8, -2.9e-8, 5.9604645e-08,
                             2.9802322e-08, 6.1035156e-05, 6.0975552e-05]])
     return vals.astype(np.float32)
+
+
+# GPTQ-INT4 (rows, cols, group, act-order) and the Qwen3.5 GDN ops
+GPTQ_CASES = [(96, 512, 128, False), (64, 256, 64, True), (33, 384, 128, True)]
+GDN_CONV = (512, 4)          # channels, kernel size
+GDN_HEAD = (128, 128)        # qk_dim, v_dim
+PROPE_CASE = (8, 2, 256, 64, 77, 1e7)  # heads, kv heads, head_dim, rotary_dim, pos, theta
+
+
+def gptq_case(M, K, G, act_order):
+    r = _seed("gptq", M, K, G, int(act_order))
+    return synth.random_gptq(r, M, K, G, act_order), r.normal(size=K).astype(np.float32)
+
+
+def gdn_case():
+    """l2norm vector, conv (x, state, weight), one head (S, q, k, v, g, beta), gated RMSNorm
+    (x, gate, weight), partial RoPE (q, k)."""
+    r = _seed("gdn")
+    dim, ks = GDN_CONV
+    dk, dv = GDN_HEAD
+    H, KVH, hd = PROPE_CASE[:3]
+    f = lambda *s: r.normal(size=s).astype(np.float32)
+    return dict(l2=f(dk), cx=f(dim), cst=f(dim, ks - 1), cw=f(dim, ks) * np.float32(0.5),
+                S=f(dk, dv) * np.float32(0.1), q=f(dk), k=f(dk) * np.float32(0.1), v=f(dv),
+                g=np.float32(-0.25), beta=np.float32(0.6),
+                rx=f(dv), rg=f(dv), rw=(1 + 0.1 * f(dv)).astype(np.float32),
+                pq=f(H * hd), pk=f(KVH * hd))

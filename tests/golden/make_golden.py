@@ -85,6 +85,24 @@ def main():
         key = f"w4a8_{M}x{K}"
         out[key + "_w"], out[key + "_x"] = w, x
         out[key + "_y"] = ref.matvec_i4_w4a8_naive(w, x, M, K, 64)
+    # GPTQ-INT4 and the Qwen3.5 GDN ops (kernels/matvec/matvec_gptq_ref.cpp, kernels/gdn/)
+    for (M, K, G, ao) in gc.GPTQ_CASES:
+        w, x = gc.gptq_case(M, K, G, ao)
+        key = f"gptq_{M}x{K}g{G}_{int(ao)}"
+        out[key + "_sha"] = _s(gc.sha(w, x))
+        out[key + "_y"] = ref.matvec_gptq(w, x, M, K, G)
+    c = gc.gdn_case()
+    out["gdn_sha"] = _s(gc.sha(*[np.asarray(v) for v in c.values()]))
+    out["gdn_l2"] = ref.l2norm_inplace(c["l2"], 1e-6)
+    dim, ks = gc.GDN_CONV
+    out["gdn_conv_out"], out["gdn_conv_state"] = ref.causal_conv1d_update(c["cx"], c["cst"], c["cw"],
+                                                                          dim, ks)
+    dk, dv = gc.GDN_HEAD
+    out["gdn_step_o"], out["gdn_step_S"] = ref.gdn_step(c["S"], c["q"], c["k"], c["v"], float(c["g"]),
+                                                        float(c["beta"]), dk, dv)
+    out["gdn_rmsg"] = ref.rmsnorm_gated(c["rx"], c["rg"], c["rw"], 1e-6)
+    H, KVH, hd, rd, pos, theta = gc.PROPE_CASE
+    out["prope_q"], out["prope_k"] = ref.partial_rope(c["pq"], c["pk"], H, KVH, hd, rd, pos, theta)
     g, u = gc.swiglu_case()
     out["swiglu_sha"], out["swiglu_y"] = _s(gc.sha(g, u)), ref.swiglu(g, u)
     l = gc.argmax_case()

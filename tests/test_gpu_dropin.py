@@ -40,6 +40,43 @@ def test_reference_decode_loop_with_b200_variants(tmp_path, case):
     eng = run("engine")
     assert eng.returncode == 0, eng.stderr
     assert eng.stdout.split() == ref.stdout.split()
+    be = run("backend")  # every IBackend op on the GPU (create_b200_backend)
+    assert be.returncode == 0, be.stderr
+    assert be.stdout.split() == ref.stdout.split()
+
+
+@pytest.mark.parametrize("case", [c for c in gc.MODEL_CASES if c[0] in ("qwen3_f16kv", "moe")],
+                         ids=lambda c: c[0])
+def test_reference_forward_token_on_b200_backend_f16kv(tmp_path, tq, oracle, case):
+    """QwenModel::forward_token with its fp16 KV cache (--kv-f16) on the b200 IBackend: the
+    attention goes through IBackend::attention_decode_f16kv (runtime/backend.h:246-249),
+    which the reference's x86 CPU backend cannot run.  Greedy tokens identical to the
+    b200 engine with an fp16 cache and to the oracle (the reference's method for fp16-KV
+    attention on x86, tests/test_attention.cpp:192)."""
+    if not os.path.exists(BIN):
+        pytest.skip("drop_in_check not built (needs the reference tree at build time)")
+    name, spec, _, seed = case
+    sm = SynthModel(spec, seed=seed)
+    path = str(tmp_path / f"{name}.tqwen")
+    sm.write_tqwen(path)
+    n_new = 8
+    r = subprocess.run([BIN, path, "backend-f16kv", "64", str(n_new)] + [str(t) for t in gc.PROMPT],
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    got = [int(t) for t in r.stdout.split()]
+    eng = tq.Engine(sm, max_seq_len=64, kv_fp16=True)
+    om = oracle.model(sm, 64, True)
+    exp_e, exp_o = [], []
+    ne = no = None
+    for i in range(len(gc.PROMPT) + n_new - 1):
+        t = gc.PROMPT[i] if i < len(gc.PROMPT) else ne
+        to = gc.PROMPT[i] if i < len(gc.PROMPT) else no
+        ne, no = eng.step(t), om.step(to)
+        exp_e.append(ne)
+        exp_o.append(no)
+    eng.close()
+    om.close()
+    assert got == exp_e == exp_o, (got, exp_e, exp_o)
 
 
 def test_reference_matmul_dispatch_reaches_b200(tmp_path, oracle):

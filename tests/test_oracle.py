@@ -236,3 +236,29 @@ def test_oracle_kv_guide(oracle):
     assert c.kv_guide_counts() == (0, 0, 0.0)
     for m in (a, b, c):
         m.close()
+
+
+@pytest.mark.parametrize("M,K,G,ao", gc.GPTQ_CASES)
+def test_golden_gptq(oracle, golden, M, K, G, ao):
+    """GPTQ-INT4 restatement vs matvec_gptq_ref's fixture, with and without act-order."""
+    w, x = gc.gptq_case(M, K, G, ao)
+    key = f"gptq_{M}x{K}g{G}_{int(ao)}"
+    _sha_ok(golden, key + "_sha", w, x)
+    assert np.array_equal(oracle.matvec_gptq(w, x, M, K, G), golden[key + "_y"])
+
+
+def test_golden_gdn_ops(oracle, golden):
+    """The Qwen3.5 GDN ops and partial RoPE vs kernels/gdn/gdn_ops_ref.cpp's fixtures."""
+    c = gc.gdn_case()
+    _sha_ok(golden, "gdn_sha", *[np.asarray(v) for v in c.values()])
+    assert np.array_equal(oracle.l2norm_inplace(c["l2"], 1e-6), golden["gdn_l2"])
+    dim, ks = gc.GDN_CONV
+    out, st = oracle.causal_conv1d_update(c["cx"], c["cst"], c["cw"], dim, ks)
+    assert np.array_equal(out, golden["gdn_conv_out"]) and np.array_equal(st, golden["gdn_conv_state"])
+    dk, dv = gc.GDN_HEAD
+    o, S = oracle.gdn_step(c["S"], c["q"], c["k"], c["v"], float(c["g"]), float(c["beta"]), dk, dv)
+    assert np.array_equal(o, golden["gdn_step_o"]) and np.array_equal(S, golden["gdn_step_S"])
+    assert np.array_equal(oracle.rmsnorm_gated(c["rx"], c["rg"], c["rw"], 1e-6), golden["gdn_rmsg"])
+    H, KVH, hd, rd, pos, theta = gc.PROPE_CASE
+    q, k = oracle.partial_rope(c["pq"], c["pk"], H, KVH, hd, rd, pos, theta)
+    assert np.array_equal(q, golden["prope_q"]) and np.array_equal(k, golden["prope_k"])

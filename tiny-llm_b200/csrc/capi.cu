@@ -4,6 +4,7 @@
 // (kernels/dispatch.h) and are synchronous, like the reference's CPU
 // variants: upload, launch, download, synchronise.  Device-pointer twins
 // (tqb200_dev_*) are stream-ordered and never synchronise.
+#include <cmath>
 #include <cstdarg>
 #include <cstring>
 #include <mutex>
@@ -570,6 +571,173 @@ int tqb200_topk_softmax(const float *gate_logits, int n, int k, int *indices, fl
     TQ_TRY(download(indices, di, (size_t)k * 4));
     TQ_TRY(download(weights, dw, (size_t)k * 4));
     return finish();
+}
+
+// ------------------------------------------------------------------ GDN ops, partial RoPE
+int tqb200_l2norm_inplace(float *x, int n, float eps) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    TQ_CHECK_ARG(x && n > 0, "l2norm_inplace: bad arguments");
+    TQ_TRY(ensure_device());
+    void *dx;
+    TQ_TRY(upload(3, x, (size_t)n * 4, &dx));
+    TQ_TRY(launch_l2norm((float *)dx, 1, n, eps, g_ctx.stream));
+    TQ_TRY(download(x, dx, (size_t)n * 4));
+    return finish();
+}
+
+int tqb200_causal_conv1d_update(const float *x, float *conv_state, const float *weight, float *out,
+                                int dim, int kernel_size) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    TQ_CHECK_ARG(x && conv_state && weight && out && dim > 0,
+                 "causal_conv1d_update: bad arguments");
+    TQ_CHECK_ARG(kernel_size >= 2, "causal_conv1d_update_ref: kernel_size %d < 2", kernel_size);
+    TQ_TRY(ensure_device());
+    const size_t sb = (size_t)dim * (kernel_size - 1) * 4;
+    void *dx, *ds, *dw, *dout;
+    TQ_TRY(upload(3, x, (size_t)dim * 4, &dx));
+    TQ_TRY(upload(7, conv_state, sb, &ds));
+    TQ_TRY(upload_weight(8, weight, (size_t)dim * kernel_size * 4, &dw));
+    TQ_TRY(scratch(4, (size_t)dim * 4, &dout));
+    TQ_TRY(launch_causal_conv1d((const float *)dx, (float *)ds, (const float *)dw, (float *)dout,
+                                dim, kernel_size, g_ctx.stream));
+    TQ_TRY(download(out, dout, (size_t)dim * 4));
+    TQ_TRY(download(conv_state, ds, sb));
+    return finish();
+}
+
+int tqb200_gdn_step(float *S, const float *q, const float *k, const float *v, float g, float beta,
+                    float *o, int qk_dim, int v_dim) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    TQ_CHECK_ARG(S && q && k && v && o && qk_dim > 0, "gdn_step: bad arguments");
+    TQ_CHECK_ARG(v_dim > 0 && v_dim <= 512, "gdn_step_ref: unsupported v_dim %d", v_dim);
+    TQ_TRY(ensure_device());
+    // decay = exp(g) with the host's libm, as gdn_step_ref computes it (std::exp(float))
+    const float dc[2] = {std::exp(g), beta};
+    const size_t sb = (size_t)qk_dim * v_dim * 4;
+    void *dS, *dq, *dk, *dv, *dp, *dout;
+    TQ_TRY(upload(3, S, sb, &dS));
+    TQ_TRY(upload(7, q, (size_t)qk_dim * 4, &dq));
+    TQ_TRY(upload(8, k, (size_t)qk_dim * 4, &dk));
+    TQ_TRY(upload(9, v, (size_t)v_dim * 4, &dv));
+    TQ_TRY(upload(10, dc, sizeof dc, &dp));
+    TQ_TRY(scratch(4, (size_t)v_dim * 4, &dout));
+    TQ_TRY(launch_gdn_step((float *)dS, (const float *)dq, (const float *)dk, (const float *)dv,
+                           (const float *)dp, (const float *)dp + 1, (float *)dout, 1, qk_dim,
+                           v_dim, g_ctx.stream));
+    TQ_TRY(download(o, dout, (size_t)v_dim * 4));
+    TQ_TRY(download(S, dS, sb));
+    return finish();
+}
+
+int tqb200_dev_gdn_step(float *S, const float *q, const float *k, const float *v,
+                        const float *decay, const float *beta, float *o, int n_heads, int qk_dim,
+                        int v_dim, void *stream) {
+    TQ_CHECK_ARG(S && q && k && v && decay && beta && o, "gdn_step: null pointer");
+    return launch_gdn_step(S, q, k, v, decay, beta, o, n_heads, qk_dim, v_dim,
+                           (cudaStream_t)stream);
+}
+
+int tqb200_rmsnorm_gated(const float *x, const float *gate, const float *weight, float *y, int n,
+                         float eps) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    TQ_CHECK_ARG(x && gate && weight && y && n > 0, "rmsnorm_gated: bad arguments");
+    TQ_TRY(ensure_device());
+    void *dx, *dg, *dw, *dy;
+    TQ_TRY(upload(3, x, (size_t)n * 4, &dx));
+    TQ_TRY(upload(7, gate, (size_t)n * 4, &dg));
+    TQ_TRY(upload(8, weight, (size_t)n * 4, &dw));
+    TQ_TRY(scratch(4, (size_t)n * 4, &dy));
+    TQ_TRY(launch_rmsnorm_gated((const float *)dx, (const float *)dg, (const float *)dw, (float *)dy,
+                                1, n, eps, g_ctx.stream));
+    TQ_TRY(download(y, dy, (size_t)n * 4));
+    return finish();
+}
+
+int tqb200_partial_rope(float *q, float *k, int n_heads, int n_kv_heads, int head_dim,
+                        int rotary_dim, int pos, float theta) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    TQ_CHECK_ARG(q && k && n_heads >= 0 && n_kv_heads >= 0 && head_dim > 0 && pos >= 0,
+                 "partial_rope: bad arguments");
+    TQ_CHECK_ARG(rotary_dim > 0 && rotary_dim <= head_dim && rotary_dim % 2 == 0,
+                 "partial_rope_ref: bad rotary_dim %d (head_dim %d)", rotary_dim, head_dim);
+    TQ_CHECK_ARG(rotary_dim / 2 <= 256, "partial_rope_ref: rotary_dim %d too large", rotary_dim);
+    TQ_TRY(ensure_device());
+    // the position's cos/sin with the host libm, the reference's expression with the
+    // rotary width in place of head_dim (kernels/gdn/gdn_ops_ref.cpp:246-254)
+    std::vector<float> tab(rotary_dim);
+    rope_row(theta, rotary_dim, pos, tab.data(), tab.data() + rotary_dim / 2);
+    const size_t qb = (size_t)n_heads * head_dim * 4, kb = (size_t)n_kv_heads * head_dim * 4;
+    void *dq, *dk, *dt;
+    TQ_TRY(upload(3, q, qb, &dq));
+    TQ_TRY(upload(7, k, kb, &dk));
+    TQ_TRY(upload(8, tab.data(), (size_t)rotary_dim * 4, &dt));
+    TQ_TRY(launch_partial_rope((float *)dq, (float *)dk, n_heads, n_kv_heads, head_dim, rotary_dim,
+                               (const float *)dt, (const float *)dt + rotary_dim / 2,
+                               g_ctx.stream));
+    TQ_TRY(download(q, dq, qb));
+    TQ_TRY(download(k, dk, kb));
+    return finish();
+}
+
+// ------------------------------------------------------------------ GPTQ, dense matvec
+static int gptq_host(const uint8_t *w, const float *x, float *y, int out, int in, int n, int G) {
+    TQ_CHECK_ARG(w && x && y && out > 0 && in > 0 && n > 0, "gptq: bad arguments");
+    TQ_CHECK_ARG(G > 0 && in % G == 0 && G % 8 == 0 && in % 8 == 0,
+                 "gptq: in_dim %d / group_size %d (in %% G == 0, G %% 8 == 0)", in, G);
+    TQ_TRY(ensure_device());
+    uint32_t flags = 0;
+    std::memcpy(&flags, w + 4, 4);
+    const bool gidx = (flags & 1u) != 0;
+    void *dw, *dx, *dy;
+    TQ_TRY(upload_weight(2, w, gptq_bytes(out, in, G, gidx), &dw));
+    TQ_TRY(upload(3, x, (size_t)in * n * 4, &dx));
+    TQ_TRY(scratch(4, (size_t)out * n * 4, &dy));
+    TQ_TRY(launch_gptq_matmul((const uint8_t *)dw, gidx, (const float *)dx, (float *)dy, out, in, n,
+                              G, g_ctx.stream));
+    TQ_TRY(download(y, dy, (size_t)out * n * 4));
+    return finish();
+}
+
+int tqb200_matvec_gptq(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim,
+                       int group_size) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    return gptq_host(w, x, y, out_dim, in_dim, 1, group_size);
+}
+
+int tqb200_matmul_gptq(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim, int n,
+                       int group_size) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    return gptq_host(w, x, y, out_dim, in_dim, n, group_size);
+}
+
+int tqb200_dev_matvec_gptq(const uint8_t *w, int has_g_idx, const float *x, float *y, int out_dim,
+                           int in_dim, int group_size, void *stream) {
+    TQ_CHECK_ARG(w && x && y, "gptq: null pointer");
+    return launch_gptq_matmul(w, has_g_idx != 0, x, y, out_dim, in_dim, 1, group_size,
+                              (cudaStream_t)stream);
+}
+
+static int dense_host(const void *w, bool f16, const float *x, float *y, int out, int in) {
+    TQ_CHECK_ARG(w && x && y && out >= 0 && in > 0, "matvec: bad arguments");
+    if (out == 0) return TQB200_OK;
+    TQ_TRY(ensure_device());
+    void *dw, *dx, *dy;
+    TQ_TRY(upload_weight(2, w, (size_t)out * in * (f16 ? 2 : 4), &dw));
+    TQ_TRY(upload(3, x, (size_t)in * 4, &dx));
+    TQ_TRY(scratch(4, (size_t)out * 4, &dy));
+    TQ_TRY(launch_dense_matvec(dw, f16, (const float *)dx, (float *)dy, out, in, g_ctx.stream));
+    TQ_TRY(download(y, dy, (size_t)out * 4));
+    return finish();
+}
+
+int tqb200_matvec_f32(const float *w, const float *x, float *y, int out_dim, int in_dim) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    return dense_host(w, false, x, y, out_dim, in_dim);
+}
+
+int tqb200_matvec_f16(const uint16_t *w, const float *x, float *y, int out_dim, int in_dim) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    return dense_host(w, true, x, y, out_dim, in_dim);
 }
 
 }  // extern "C"

@@ -353,4 +353,27 @@ int launch_topk_rows(const float *logits, int n, int E, int k, int *idx, float *
 int launch_moe_combine_rows(float *h, const float *o, const float *wts, const int *slot, int n,
                             int k, int H, cudaStream_t st);
 
+// ------------------------------------------------------------------ GDN ops (gdn_ops.cu)
+// l2norm_inplace / rmsnorm_gated over n_vec vectors of n floats; gdn_step over n_heads
+// heads (S [n_heads][qk_dim][v_dim], q/k [n_heads][qk_dim], v/o [n_heads][v_dim], decay =
+// exp(g) and beta per head, on the device); partial RoPE with host cos/sin rows.
+int launch_l2norm(float *x, int n_vec, int n, float eps, cudaStream_t st);
+int launch_causal_conv1d(const float *x, float *state, const float *w, float *out, int dim, int ks,
+                         cudaStream_t st);
+int launch_gdn_step(float *S, const float *q, const float *k, const float *v, const float *decay,
+                    const float *beta, float *o, int n_heads, int qk_dim, int v_dim,
+                    cudaStream_t st);
+int launch_rmsnorm_gated(const float *x, const float *gate, const float *w, float *y, int n_vec,
+                         int n, float eps, cudaStream_t st);
+int launch_partial_rope(float *q, float *k, int n_heads, int n_kv_heads, int head_dim,
+                        int rotary_dim, const float *cs, const float *sn, cudaStream_t st);
+
+// ------------------------------------------------------------------ GPTQ, dense (gptq_matvec.cu)
+size_t gptq_bytes(int out, int in, int G, bool g_idx);
+// Y[:, j] = W X[:, j] for n columns (X [in x n], Y [out x n] column-major)
+int launch_gptq_matmul(const uint8_t *w, bool g_idx, const float *x, float *y, int out, int in,
+                       int n, int G, cudaStream_t st);
+int launch_dense_matvec(const void *w, bool f16, const float *x, float *y, int out, int in,
+                        cudaStream_t st);
+
 }  // namespace tqb200

@@ -6,7 +6,13 @@
 //     VQ2 matvec (:187), BiIP rotate (:227) and the ops rmsnorm, rope, attention,
 //     swiglu, argmax, top-k softmax (:298-307), selected by
 //     --matvec-impl b200 / --ops-impl b200;
-//   * the whole-step GPU decode engine (:353-378), selected by --engine b200.
+//   * the Qwen3.5 GDN ops (:389-396, with --ops-impl b200) and the GPTQ-INT4 matvec /
+//     matmul (:211-258, --matvec-gptq-impl b200);
+//   * the whole-step GPU decode engine (:353-378), selected by --engine b200;
+// and defines create_b200_backend() (b200_backend.h): an IBackend
+// (runtime/backend.h:73-392) whose every op runs on the GPU through libtqb200.so,
+// fp16-KV attention (attention_decode_f16kv) included, for QwenModel::create's backend
+// argument (main.cpp's --backend).
 // Per-op calls use host pointers with resident weights: a weight is uploaded the
 // first time its (mmap'd, immutable) host pointer is seen, as the reference's own
 // resident CUDA variants do (kernels/matvec/matvec_f32_cuda_resident.cu).
@@ -19,6 +25,7 @@
 #include <string>
 #include <vector>
 
+#include "b200_backend.h"
 #include "dispatch.h"
 #include "model_loader.h"
 #include "ref_ops.h"
@@ -85,6 +92,126 @@ int argmax_b200(const float *l, int n) {
 void topk_softmax_b200(const float *l, int n, int k, int *idx, float *w) {
     if (tqb200_topk_softmax(l, n, k, idx, w)) die("topk_softmax");
 }
+
+void matvec_gptq_b200(const uint8_t *w, const float *x, float *y, int out, int in, int g) {
+    if (tqb200_matvec_gptq(w, x, y, out, in, g)) die("matvec_gptq");
+}
+void matmul_gptq_b200(const uint8_t *w, const float *x, float *y, int M, int K, int N, int g) {
+    if (tqb200_matmul_gptq(w, x, y, M, K, N, g)) die("matmul_gptq");
+}
+void causal_conv1d_b200(const float *x, float *st, const float *w, float *out, int dim, int ks) {
+    if (tqb200_causal_conv1d_update(x, st, w, out, dim, ks)) die("causal_conv1d_update");
+}
+void l2norm_b200(float *x, int n, float eps) {
+    if (tqb200_l2norm_inplace(x, n, eps)) die("l2norm_inplace");
+}
+void gdn_step_b200(float *S, const float *q, const float *k, const float *v, float g, float beta,
+                   float *o, int dk, int dv) {
+    if (tqb200_gdn_step(S, q, k, v, g, beta, o, dk, dv)) die("gdn_step");
+}
+void rmsnorm_gated_b200(const float *x, const float *gate, const float *w, float *y, int n,
+                        float eps) {
+    if (tqb200_rmsnorm_gated(x, gate, w, y, n, eps)) die("rmsnorm_gated");
+}
+
+// ------------------------------------------------------------------ IBackend
+// Every op on the GPU through the C ABI, weights resident by host pointer: the
+// CUDABackend the reference leaves incomplete (runtime/backend_cuda.cpp:151-154 aborts on
+// i4, :253-258 on partial_rope) and the fp16-KV attention its CPU backend lacks off
+// aarch64 (runtime/backend_cpu.cpp:142-156).
+class B200Backend final : public tinyqwen::IBackend {
+    using WT = tinyqwen::WeightTensor;
+    using QT = tinyqwen::QuantType;
+
+  public:
+    void matvec(const WT &w, const float *x, float *y, int out, int in) override {
+        switch (w.quant_type) {
+            case QT::kI4: matvec_i4_b200(u8(w), x, y, out, in, w.group_size); break;
+            case QT::kVQ2: matvec_vq2_b200(u8(w), x, y, out, in); break;
+            case QT::kGPTQ: matvec_gptq_b200(u8(w), x, y, out, in, w.group_size); break;
+            case QT::kF16:
+                if (tqb200_matvec_f16(static_cast<const uint16_t *>(w.data), x, y, out, in))
+                    die("matvec_f16");
+                break;
+            default:
+                if (tqb200_matvec_f32(static_cast<const float *>(w.data), x, y, out, in))
+                    die("matvec_f32");
+        }
+    }
+    void matvec_pair(const WT &w1, const WT &w2, const float *x, float *y1, float *y2, int out,
+                     int in) override {
+        if (w1.quant_type == QT::kI4 && w2.quant_type == QT::kI4 && w1.group_size == w2.group_size) {
+            matvec_pair_i4_b200(u8(w1), u8(w2), x, y1, y2, out, in, w1.group_size);
+            return;
+        }
+        matvec(w1, x, y1, out, in);
+        matvec(w2, x, y2, out, in);
+    }
+    void matvec_qkv(const WT &wq, const WT &wk, const WT &wv, const float *x, float *yq, float *yk,
+                    float *yv, int qd, int kvd, int in) override {
+        if (wq.quant_type == QT::kI4 && wk.quant_type == QT::kI4 && wv.quant_type == QT::kI4 &&
+            wq.group_size == wk.group_size && wk.group_size == wv.group_size) {
+            matvec_qkv_i4_b200(u8(wq), u8(wk), u8(wv), x, yq, yk, yv, qd, kvd, in, wq.group_size);
+            return;
+        }
+        matvec(wq, x, yq, qd, in);
+        matvec(wk, x, yk, kvd, in);
+        matvec(wv, x, yv, kvd, in);
+    }
+    void matmul(const WT &w, const float *x, float *y, int M, int K, int N) override {
+        if (w.quant_type == QT::kI4) {
+            if (tqb200_matmul_i4(u8(w), x, y, M, K, N, w.group_size)) die("matmul_i4");
+        } else if (w.quant_type == QT::kGPTQ) {
+            matmul_gptq_b200(u8(w), x, y, M, K, N, w.group_size);
+        } else {  // one matvec per column (column-major X / Y), as CUDABackend::matmul
+            for (int c = 0; c < N; ++c) matvec(w, x + (size_t)c * K, y + (size_t)c * M, M, K);
+        }
+    }
+    void rmsnorm(const float *x, const float *w, float *y, int n, float eps) override {
+        rmsnorm_b200(x, w, y, n, eps);
+    }
+    void rope(float *q, float *k, int nh, int nkv, int hd, int pos, float theta) override {
+        rope_b200(q, k, nh, nkv, hd, pos, theta);
+    }
+    void partial_rope(float *q, float *k, int nh, int nkv, int hd, int rd, int pos,
+                      float theta) override {
+        if (tqb200_partial_rope(q, k, nh, nkv, hd, rd, pos, theta)) die("partial_rope");
+    }
+    void attention_decode(const float *q, const float *kc, const float *vc, int seq, int maxs,
+                          int nh, int nkv, int hd, float scale, float *out) override {
+        attention_b200(q, kc, vc, seq, maxs, nh, nkv, hd, scale, out);
+    }
+    void attention_decode_f16kv(const float *q, const uint16_t *kc, const uint16_t *vc, int seq,
+                                int maxs, int nh, int nkv, int hd, float scale,
+                                float *out) override {
+        if (tqb200_attention_decode_f16kv(q, kc, vc, seq, maxs, nh, nkv, hd, scale, out))
+            die("attention_decode_f16kv");
+    }
+    void swiglu(float *g, const float *u, int n) override { swiglu_b200(g, u, n); }
+    int argmax(const float *l, int n) override { return argmax_b200(l, n); }
+    // unused by the reference's decode (CPUBackend::top_k_logits writes nothing either,
+    // runtime/backend_cpu.cpp:168-171)
+    void top_k_logits(const float *, int, int, int *, float *) override {}
+    void topk_softmax(const float *g, int n, int k, int *idx, float *w) override {
+        topk_softmax_b200(g, n, k, idx, w);
+    }
+    void causal_conv1d_update(float *x, float *state, const float *w, float *out, int dim,
+                              int ks) override {
+        causal_conv1d_b200(x, state, w, out, dim, ks);
+    }
+    void l2norm_inplace(float *x, int n, float eps) override { l2norm_b200(x, n, eps); }
+    void gdn_step(float *S, const float *q, const float *k, const float *v, float g, float beta,
+                  float *o, int dk, int dv) override {
+        gdn_step_b200(S, q, k, v, g, beta, o, dk, dv);
+    }
+    void rmsnorm_gated(float *x, const float *gate, const float *w, float *y, int n,
+                       float eps) override {
+        rmsnorm_gated_b200(x, gate, w, y, n, eps);
+    }
+
+  private:
+    static const uint8_t *u8(const WT &w) { return static_cast<const uint8_t *>(w.data); }
+};
 
 // ------------------------------------------------------------------ engine
 // The reference treats GpuDecodeEngine as opaque (kernels/dispatch.h:341-351); this
@@ -236,4 +363,14 @@ TINYQWEN_ATTENTION_DECODE_VARIANT(attention_b200, "b200");
 TINYQWEN_SWIGLU_VARIANT(swiglu_b200, "b200");
 TINYQWEN_ARGMAX_VARIANT(argmax_b200, "b200");
 TINYQWEN_TOPK_SOFTMAX_VARIANT(topk_softmax_b200, "b200");
+TINYQWEN_MATVEC_GPTQ_VARIANT(matvec_gptq_b200, "b200");
+TINYQWEN_MATMUL_GPTQ_VARIANT(matmul_gptq_b200, "b200");
+TINYQWEN_CAUSAL_CONV1D_UPDATE_VARIANT(causal_conv1d_b200, "b200");
+TINYQWEN_L2NORM_INPLACE_VARIANT(l2norm_b200, "b200");
+TINYQWEN_GDN_STEP_VARIANT(gdn_step_b200, "b200");
+TINYQWEN_RMSNORM_GATED_VARIANT(rmsnorm_gated_b200, "b200");
 TINYQWEN_GPU_DECODE_VARIANT("b200", create_b200, step_b200, reset_b200, destroy_b200, logits_b200);
+
+std::unique_ptr<tinyqwen::IBackend> create_b200_backend() {
+    return std::make_unique<B200Backend>();
+}

@@ -1,9 +1,13 @@
 // drop_in_check.cpp — runs the reference's own decode loop with the "b200" variants.
 //
 //   drop_in_check <model.tqwen> <mode> <max_seq> <n_new> <tok0> [tok1 ...]
-//   mode: ref     reference CPU path (matvec/ops "ref")
-//         ops     QwenModel::forward_token with --matvec-impl b200 --ops-impl b200
-//         engine  the GPU decode registry with --engine b200 (gpu_decode_* entries)
+//   mode: ref            reference CPU path (matvec/ops "ref")
+//         ops            QwenModel::forward_token with --matvec-impl b200 --ops-impl b200
+//         engine         the GPU decode registry with --engine b200 (gpu_decode_* entries)
+//         backend        QwenModel::forward_token on create_b200_backend() (every op of the
+//                        IBackend on the GPU), fp32 KV cache
+//         backend-f16kv  the same with QwenModel's fp16 KV cache (--kv-f16: attention
+//                        through IBackend::attention_decode_f16kv)
 // Prints the greedy token after every fed token on one line, as main.cpp's decode
 // loop produces them (runtime/main.cpp:1009-1041).
 //
@@ -19,6 +23,7 @@
 #include <string>
 #include <vector>
 
+#include "b200_backend.h"
 #include "dispatch.h"
 #include "model_loader.h"
 #include "profiler.h"
@@ -86,6 +91,17 @@ int main(int argc, char **argv) {
         for (int t : prompt) out.push_back(next = tinyqwen::gpu_decode_step(eng, t));
         for (int s = 1; s < n_new; ++s) out.push_back(next = tinyqwen::gpu_decode_step(eng, next));
         tinyqwen::gpu_decode_destroy(eng);
+    } else if (mode == "backend" || mode == "backend-f16kv") {
+        tinyqwen::Profiler profiler(false);
+        std::unique_ptr<tinyqwen::QwenModel> model;
+        if (!tinyqwen::QwenModel::create(file, max_seq, profiler, &err, &model, create_b200_backend(),
+                                         mode == "backend-f16kv")) {
+            std::fprintf(stderr, "model create: %s\n", err.c_str());
+            return 1;
+        }
+        int next = -1;
+        for (int t : prompt) out.push_back(next = model->forward_token(t));
+        for (int s = 1; s < n_new; ++s) out.push_back(next = model->forward_token(next));
     } else {
         const char *impl = mode == "ops" ? "b200" : "ref";
         if (!tinyqwen::set_matvec_i4_impl_by_name(impl) ||

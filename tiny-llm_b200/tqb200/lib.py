@@ -83,6 +83,17 @@ PROTOTYPES = {
     "tqb200_engine_profile_prefill": ([_vp, _i32, _i, _f, _i, C.POINTER(_i)], _i),
     "tqb200_engine_profile_step": ([_vp, _i, _f, _i, C.POINTER(_i)], _i),
     "tqb200_engine_set_timeline": ([_vp, _i], _i),
+    "tqb200_l2norm_inplace": ([_f, _i, _fl], _i),
+    "tqb200_causal_conv1d_update": ([_f, _f, _f, _f, _i, _i], _i),
+    "tqb200_gdn_step": ([_f, _f, _f, _f, _fl, _fl, _f, _i, _i], _i),
+    "tqb200_dev_gdn_step": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp], _i),
+    "tqb200_rmsnorm_gated": ([_f, _f, _f, _f, _i, _fl], _i),
+    "tqb200_partial_rope": ([_f, _f, _i, _i, _i, _i, _i, _fl], _i),
+    "tqb200_matvec_gptq": ([_u8, _f, _f, _i, _i, _i], _i),
+    "tqb200_matmul_gptq": ([_u8, _f, _f, _i, _i, _i, _i], _i),
+    "tqb200_dev_matvec_gptq": ([_vp, _i, _vp, _vp, _i, _i, _i, _vp], _i),
+    "tqb200_matvec_f32": ([_f, _f, _f, _i, _i], _i),
+    "tqb200_matvec_f16": ([_u16, _f, _f, _i, _i], _i),
     "tqb200_engine_timeline": ([_vp, _i, _d, _d, _i32, C.POINTER(_i), C.POINTER(C.c_double)], _i),
 }
 
@@ -292,6 +303,70 @@ class EngineOpts(C.Structure):
     _fields_ = [("max_seq_len", C.c_int), ("kv_fp16", C.c_int), ("use_graph", C.c_int),
                 ("pdl", C.c_int), ("device", C.c_int), ("tp_size", C.c_int), ("tp_rank", C.c_int),
                 ("nccl_id", C.c_ubyte * 128), ("reserved", C.c_int * 8)]
+
+
+def l2norm_inplace(x, eps: float) -> np.ndarray:
+    """l2norm_inplace_ref (kernels/gdn/gdn_ops_ref.cpp:44-57); returns the normalised copy."""
+    x = _f32(x).copy()
+    _check(load().tqb200_l2norm_inplace(x, x.size, eps))
+    return x
+
+
+def causal_conv1d_update(x, state, weight, dim: int, kernel_size: int):
+    """causal_conv1d_update_ref (:82-105); returns (out, new state)."""
+    st = _f32(state).copy()
+    out = np.zeros(dim, np.float32)
+    _check(load().tqb200_causal_conv1d_update(_f32(x), st, _f32(weight), out, dim, kernel_size))
+    return out, st
+
+
+def gdn_step(S, q, k, v, g: float, beta: float, qk_dim: int, v_dim: int):
+    """gdn_step_ref (:134-176); returns (o, new S)."""
+    S2 = _f32(S).copy()
+    o = np.zeros(v_dim, np.float32)
+    _check(load().tqb200_gdn_step(S2, _f32(q), _f32(k), _f32(v), g, beta, o, qk_dim, v_dim))
+    return o, S2
+
+
+def rmsnorm_gated(x, gate, weight, eps: float) -> np.ndarray:
+    x = _f32(x)
+    y = np.zeros_like(x)
+    _check(load().tqb200_rmsnorm_gated(x, _f32(gate), _f32(weight), y, x.size, eps))
+    return y
+
+
+def partial_rope(q, k, n_heads: int, n_kv_heads: int, head_dim: int, rotary_dim: int, pos: int,
+                 theta: float):
+    q, k = _f32(q).copy(), _f32(k).copy()
+    _check(load().tqb200_partial_rope(q, k, n_heads, n_kv_heads, head_dim, rotary_dim, pos, theta))
+    return q, k
+
+
+def matvec_gptq(w, x, out_dim: int, in_dim: int, group_size: int) -> np.ndarray:
+    y = np.zeros(out_dim, np.float32)
+    _check(load().tqb200_matvec_gptq(_u8a(w), _f32(x), y, out_dim, in_dim, group_size))
+    return y
+
+
+def matmul_gptq(w, x_cols, M: int, K: int, N: int, group_size: int) -> np.ndarray:
+    """x_cols [N, K] (column-major X [K, N]); returns [N, M]."""
+    y = np.zeros((N, M), np.float32)
+    _check(load().tqb200_matmul_gptq(_u8a(w), _f32(x_cols), y, M, K, N, group_size))
+    return y
+
+
+def matvec_f32(w, x) -> np.ndarray:
+    w = _f32(w)
+    y = np.zeros(w.shape[0], np.float32)
+    _check(load().tqb200_matvec_f32(w, _f32(x), y, w.shape[0], w.shape[1]))
+    return y
+
+
+def matvec_f16(w, x) -> np.ndarray:
+    w = np.ascontiguousarray(w, np.uint16)
+    y = np.zeros(w.shape[0], np.float32)
+    _check(load().tqb200_matvec_f16(w, _f32(x), y, w.shape[0], w.shape[1]))
+    return y
 
 
 def nccl_unique_id() -> bytes:

@@ -160,3 +160,28 @@ def hadamard_block_size(dim: int) -> int:
         if dim % bs == 0:
             return bs
     return 1
+
+
+GPTQ_MAGIC = 0x47505451  # 'GPTQ' little-endian (runtime/tiny_format.h:135)
+
+
+def random_gptq(rng: np.random.Generator, rows: int, cols: int, group_size: int,
+                act_order: bool = False) -> np.ndarray:
+    """A GPTQ-INT4 tensor in the reference's in-band layout (runtime/tiny_format.h:108-182):
+    [magic][flags][scales f16 [ng][rows]][qzeros f16 [ng][rows]][g_idx u32 [cols] when
+    act_order][qweight u32 [cols/8][rows], column k of a word in bits 4k..4k+3].  Codes
+    U{0..15}, scales |N(0,0.02)|/7.5, zeros U[0,15] (stored as the real zero point);
+    act-order assigns the columns to groups by a seeded permutation."""
+    G = group_size
+    assert cols % G == 0 and cols % 8 == 0
+    ng = cols // G
+    hdr = np.array([GPTQ_MAGIC, 1 if act_order else 0], np.uint32).view(np.uint8)
+    scales = (np.abs(rng.normal(0.0, 0.02, (ng, rows))) / 7.5).astype(np.float16).view(np.uint8)
+    zeros = rng.uniform(0.0, 15.0, (ng, rows)).astype(np.float16).view(np.uint8)
+    parts = [hdr, scales.ravel(), zeros.ravel()]
+    if act_order:
+        g_idx = (rng.permutation(cols) // G).astype(np.uint32)
+        parts.append(g_idx.view(np.uint8))
+    qw = np.frombuffer(rng.bytes(cols // 8 * rows * 4), np.uint32)
+    parts.append(qw.view(np.uint8))
+    return np.ascontiguousarray(np.concatenate(parts))
