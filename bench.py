@@ -307,15 +307,21 @@ def bench_matvec(args, rank, pg, pk, pk_kind):
     import torch
     from tqb200 import lib, synth
     tq = lib.load()
-    M, K, G = 4864, 896, 64
-    NCOPY = 64
-    w, x = synth.config1_matvec(0)
+    G = 64
+    cfg1 = args.rows is None and args.cols is None
+    M, K = (4864, 896) if cfg1 else (args.rows or 4864, args.cols or 896)
+    NCOPY = args.copies or (64 if cfg1 else 2)
+    rng = np.random.default_rng(1)
+    if cfg1:
+        w, x = synth.config1_matvec(0)
+    else:
+        w, x = synth.random_i4_fast(rng, M, K, G), rng.normal(size=K).astype(np.float32)
     algo_bytes = w.nbytes + x.nbytes + M * 4
     dev = torch.device("cuda")
-    rng = np.random.default_rng(1)
     ws = [torch.from_numpy(w).to(dev)]
     for i in range(1, NCOPY):   # distinct copies (same distribution) so L2 never holds W
-        ws.append(torch.from_numpy(synth.random_i4(rng, M, K, G) if i < 4 else w).to(dev))
+        ws.append(torch.from_numpy(synth.random_i4(rng, M, K, G) if (i < 4 and cfg1) else
+                                   synth.random_i4_fast(rng, M, K, G) if not cfg1 else w).to(dev))
     dx = torch.from_numpy(x).to(dev)
     dy = torch.empty(M, device=dev)
     stream = torch.cuda.Stream()
@@ -374,19 +380,22 @@ def bench_matvec(args, rank, pg, pk, pk_kind):
         e2e = {"value": algo_bytes / dt / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(w.nbytes + x.nbytes),
                "d2h_bytes_per_step": int(M * 4), "note": "one tqb200_matvec_i4 host-pointer call per step"}
     out = {
-        "metric": "i4 matvec HBM GB/s (BASELINE config 1, 4864x896 g64)",
+        "metric": ("i4 matvec HBM GB/s (BASELINE config 1, 4864x896 g64)" if cfg1 else
+                   f"i4 matvec HBM GB/s ({M}x{K} g64)"),
         "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "u4 weights, f32 activations",
         "data": "synthetic (seeded, BASELINE config 1 distributions)",
-        "config": {"workload": "matvec-i4 (config 1)", "rows": M, "cols": K, "group_size": G,
+        "config": {"workload": "matvec-i4 (config 1)" if cfg1 else f"matvec-i4 ({M}x{K})",
+                   "rows": M, "cols": K, "group_size": G,
                    "launches_per_step": NCOPY, "distinct_weight_copies": NCOPY,
-                   "l2": "inputs larger than L2 (64 distinct W copies, 157 MB)",
+                   "l2": f"inputs larger than L2 ({NCOPY} distinct W copies, "
+                         f"{NCOPY * w.nbytes / 1e6:.0f} MB)",
                    "parallelism": f"replicas x{world}"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
                      "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
                      "traffic": None, "peak_source": pk_kind,
-                     "kernel": "i4_matvec_kernel<64,2>",
+                     "kernel": "i4_mv_tma_kernel<64>",
                      "algorithmic_bytes_per_launch": int(algo_bytes)},
         "clocks": clk,
         "gpu_launches": NCOPY * args.steps,
@@ -1019,6 +1028,10 @@ def main():
                     help="decode context in KV positions (default: the workload's)")
     ap.add_argument("--layers", type=int, default=None,
                     help="decode workloads: fewer layers than the model (small profiling cases)")
+    ap.add_argument("--rows", type=int, default=None, help="matvec-i4: rows (default config 1)")
+    ap.add_argument("--cols", type=int, default=None, help="matvec-i4: columns (default config 1)")
+    ap.add_argument("--copies", type=int, default=None,
+                    help="matvec-i4: distinct weight copies per graph (default 64 for config 1, else 2)")
     ap.add_argument("--no-extras", dest="extras", action="store_false",
                     help="decode workloads: skip the config-1 and lm_head matvec keys")
     args = ap.parse_args()

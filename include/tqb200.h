@@ -301,6 +301,11 @@ int tqb200_engine_set_timeline(tqb200_engine *e, int max_steps);
  * kind k per step; *span_ms = first stamped CTA in to the last out. */
 int tqb200_engine_timeline(const tqb200_engine *e, int n_kinds, double *excl_ms, double *incl_ms,
                            int *launches, int *steps, double *span_ms);
+/* One recorded step of that timeline launch by launch: kinds[i] and, in us[6 i .. 6 i + 5],
+ * the first and last CTA's entry, wait and exit of launch i in microseconds from the
+ * step's first stamp (-1 where no CTA stamped).  *n_launches = launches reported. */
+int tqb200_engine_timeline_launches(const tqb200_engine *e, int step, int max_launches,
+                                    int *kinds, double *us, int *n_launches);
 
 #ifdef __cplusplus
 }

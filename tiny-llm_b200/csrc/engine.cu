@@ -8,13 +8,15 @@
 //            -> attention -> o_proj + residual -> rmsnorm -> gate/up -> SwiGLU
 //            -> down + residual ] -> final rmsnorm -> lm_head -> argmax
 //
-// as 2 + 6 * n_layers kernels:
-//   embed | qkv (RMSNorm prologue, bias epilogue) | qk-norm+rope+kv-append | split-K
-//   attention | o_proj (residual epilogue) | gate/up (RMSNorm prologue) | down (SwiGLU
-//   prologue, residual epilogue) | ... | lm_head (RMSNorm prologue, argmax epilogue)
-// captured once into a CUDA graph whose nodes are linked by programmatic
-// dependent launch, so each matvec streams its weights while its predecessor
-// finishes.  Per step the host moves 8 bytes in (token, position) and 8 bytes
+// as 2 + 5 * n_layers kernels for a dense model:
+//   embed | qkv (RMSNorm prologue, bias epilogue) | attention (QK-norm, RoPE and KV append
+//   fused; split-K over the positions, merged in a cluster) | o_proj (residual epilogue)
+//   | gate/up (RMSNorm prologue, SwiGLU epilogue) | down (residual epilogue) | ... |
+//   lm_head (RMSNorm prologue, argmax epilogue)
+// (a MoE layer: qkv | attention | o_proj | router + top-k | expert gate/up | expert down
+// | ordered combine), captured once into a CUDA graph whose nodes are linked by
+// programmatic dependent launch, so a kernel's CTAs start (and stream their weights)
+// on the SMs its predecessor has left.  Per step the host moves 8 bytes in (token, position) and 8 bytes
 // out (next token, device status) through pinned memory, like the reference
 // engine's 2 x 4 B H2D + 4 B D2H (kernels/cuda/gpu_engine.cu:332-371).
 //
@@ -1568,6 +1570,40 @@ int tqb200_engine_set_timeline(tqb200_engine *e, int max_steps) {
     TQ_CUDA_TRY(cudaMalloc(&e->tl, bytes));
     TQ_CUDA_TRY(cudaMemset(e->tl, 0xFF, bytes));
     e->tl_cap = max_steps;
+    return TQB200_OK;
+}
+
+int tqb200_engine_timeline_launches(const tqb200_engine *e, int step, int max_launches,
+                                    int *kinds, double *us, int *n_launches) {
+    TQ_CHECK_ARG(e && kinds && us && n_launches && max_launches > 0, "bad timeline arguments");
+    TQ_CHECK_ARG(e->tl && step >= 0 && step < e->tl_steps, "no timeline record for step %d", step);
+    const int nl = std::min((int)e->tl_kind.size(), max_launches);
+    const int words = 3 * kStampCtas;
+    std::vector<unsigned long long> h((size_t)e->tl_stride);
+    TQ_CUDA_TRY(cudaSetDevice(e->device));
+    TQ_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    TQ_CUDA_TRY(cudaMemcpy(h.data(), e->tl + (size_t)step * e->tl_stride, h.size() * 8,
+                           cudaMemcpyDeviceToHost));
+    const unsigned long long none = ~0ull;
+    unsigned long long t0 = none;
+    for (int i = 0; i < nl; ++i)
+        for (int c = 0; c < kStampCtas; ++c)
+            if (h[(size_t)i * words + 3 * c] != none) t0 = std::min(t0, h[(size_t)i * words + 3 * c]);
+    for (int i = 0; i < nl; ++i) {
+        unsigned long long v[6] = {none, 0, none, 0, none, 0};  // entry, wait, exit: min, max
+        for (int c = 0; c < kStampCtas; ++c) {
+            const unsigned long long *r = h.data() + (size_t)i * words + 3 * c;
+            if (r[0] == none) continue;
+            for (int j = 0; j < 3; ++j) {
+                v[2 * j] = std::min(v[2 * j], r[j]);
+                v[2 * j + 1] = std::max(v[2 * j + 1], r[j]);
+            }
+        }
+        kinds[i] = e->tl_kind[i];
+        for (int j = 0; j < 6; ++j)
+            us[6 * i + j] = v[j] == none || t0 == none ? -1.0 : (double)(v[j] - t0) * 1e-3;
+    }
+    *n_launches = nl;
     return TQB200_OK;
 }
 

@@ -95,6 +95,7 @@ PROTOTYPES = {
     "tqb200_matvec_f32": ([_f, _f, _f, _i, _i], _i),
     "tqb200_matvec_f16": ([_u16, _f, _f, _i, _i], _i),
     "tqb200_engine_timeline": ([_vp, _i, _d, _d, _i32, C.POINTER(_i), C.POINTER(C.c_double)], _i),
+    "tqb200_engine_timeline_launches": ([_vp, _i, _i, _i32, _d, C.POINTER(_i)], _i),
 }
 
 _lib = None
@@ -458,6 +459,16 @@ class Engine:
         kinds = {k: (float(ex[i]), float(inc[i]), int(cnt[i]))
                  for i, k in enumerate(self.KINDS) if cnt[i] > 0}
         return steps.value, span.value, kinds
+
+    def timeline_launches(self, step: int = 0, max_launches: int = 4096):
+        """[(kind, entry_first, entry_last, wait_first, wait_last, exit_first, exit_last)] in
+        microseconds from the step's first stamp, for one recorded step."""
+        kinds = np.zeros(max_launches, np.int32)
+        us = np.zeros(6 * max_launches, np.float64)
+        n = C.c_int(0)
+        _check(load().tqb200_engine_timeline_launches(self.h, step, max_launches, kinds, us,
+                                                      C.byref(n)))
+        return [(self.KINDS[kinds[i]],) + tuple(us[6 * i: 6 * i + 6]) for i in range(n.value)]
 
     def reset(self):
         _check(load().tqb200_engine_reset(self.h))
