@@ -77,7 +77,7 @@ def test_gdn_ops_vs_reference_golden(tq, oracle, golden):
     assert np.array_equal(q, golden["prope_q"]) and np.array_equal(k, golden["prope_k"])
 
 
-@pytest.mark.parametrize("dk,dv", [(128, 128), (64, 256), (100, 512), (16, 7)])
+@pytest.mark.parametrize("dk,dv", [(128, 128), (64, 256), (100, 512), (16, 7), (200, 64)])
 def test_gdn_step_shapes_bit_exact(tq, oracle, dk, dv):
     rng = np.random.default_rng(dk * 1000 + dv)
     S = (rng.normal(size=(dk, dv)) * 0.1).astype(np.float32)

@@ -19,8 +19,12 @@
 // ties).  gdn_step's decay = exp(g) is computed on the host with the host libm (the
 // launcher takes the decay), so gdn_step is bit-exact.
 //
-// The decode ops are tiny (one head: 128 x 128 state, 64 KB); the launches use one CTA
-// per vector or head and are latency-bound.
+// The decode ops are tiny (one head: 128 x 128 state, 64 KB) and latency-bound.  gdn_step
+// on 128 x 128 heads (Qwen3.5's) gives each warp 32 value columns of one head, copies
+// them to shared memory with every row's 128 bytes in flight at once, runs both passes
+// there and stores each column element once; the grid is heads x ceil(v_dim / 32)
+// one-warp CTAs.  Other shapes use the two-pass kernel that reads the column from global
+// memory in each pass.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -111,6 +115,57 @@ __global__ void gdn_step_kernel(float *__restrict__ S, const float *__restrict__
     }
 }
 
+// The same step with the warp's 32 columns of S staged in shared memory by 4-byte
+// cp.async copies (all qk_dim rows in flight at once, no registers held), for qk_dim ==
+// QK and v_dim == V known at compile time: one warp per 32 value columns of a head,
+// identical rounding points and summation order.
+template <int QK, int V>
+__global__ void __launch_bounds__(32) gdn_step_warp_kernel(
+    float *__restrict__ S, const float *__restrict__ q, const float *__restrict__ k,
+    const float *__restrict__ v, const float *__restrict__ decay, const float *__restrict__ beta,
+    float *__restrict__ o) {
+    __shared__ float s_q[QK], s_k[QK];
+    __shared__ float s_col[QK * 32];  // [j][lane]
+    const int h = blockIdx.x, lane = threadIdx.x, d = blockIdx.y * 32 + lane;
+    const bool live = d < V;
+    float *const col_p = S + (size_t)h * QK * V + d;
+    if (live) {
+        const uint32_t dst = (uint32_t)__cvta_generic_to_shared(s_col + lane);
+#pragma unroll 16
+        for (int j = 0; j < QK; ++j)
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst + 128u * j),
+                         "l"(col_p + (size_t)j * V) : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    q += (size_t)h * QK;
+    k += (size_t)h * QK;
+    for (int j = lane; j < QK; j += 32) {
+        s_q[j] = q[j];
+        s_k[j] = k[j];
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncwarp();
+    if (!live) return;
+    const float dc = decay[h], bt = beta[h];
+    float *col = s_col + lane;
+    float kv = 0.0f;
+#pragma unroll 8
+    for (int j = 0; j < QK; ++j) {
+        const float sv = __fmul_rn(col[32 * j], dc);
+        col[32 * j] = sv;
+        kv = __fadd_rn(kv, __fmul_rn(sv, s_k[j]));
+    }
+    const float delta = __fmul_rn(bt, __fsub_rn(v[(size_t)h * V + d], kv));
+    double acc = 0.0;
+#pragma unroll 8
+    for (int j = 0; j < QK; ++j) {
+        const float sv = __fadd_rn(col[32 * j], __fmul_rn(s_k[j], delta));
+        col_p[(size_t)j * V] = sv;
+        acc += (double)sv * (double)s_q[j];
+    }
+    o[(size_t)h * V + d] = (float)acc;
+}
+
 // One vector per CTA.
 __global__ void rmsnorm_gated_kernel(const float *__restrict__ x, const float *__restrict__ gate,
                                      const float *__restrict__ w, float *__restrict__ y, int n,
@@ -163,9 +218,14 @@ int launch_gdn_step(float *S, const float *q, const float *k, const float *v, co
     TQ_CHECK_ARG(n_heads > 0 && n_heads <= 65535 && qk_dim > 0 && qk_dim <= 4096 && v_dim > 0 &&
                      v_dim <= 512,
                  "gdn_step: %d heads, qk_dim %d, v_dim %d (v_dim 1..512)", n_heads, qk_dim, v_dim);
-    const int threads = ((v_dim + 31) / 32) * 32;
-    gdn_step_kernel<<<n_heads, threads, (size_t)2 * qk_dim * 4, st>>>(S, q, k, v, decay, beta, o,
-                                                                      qk_dim, v_dim);
+    const dim3 grid(n_heads, (v_dim + 31) / 32);
+    if (qk_dim == 128 && v_dim == 128) {  // every Qwen3.5 linear-attention head
+        gdn_step_warp_kernel<128, 128><<<grid, 32, 0, st>>>(S, q, k, v, decay, beta, o);
+    } else {
+        const int threads = ((v_dim + 31) / 32) * 32;
+        gdn_step_kernel<<<n_heads, threads, (size_t)2 * qk_dim * 4, st>>>(S, q, k, v, decay, beta,
+                                                                          o, qk_dim, v_dim);
+    }
     TQ_CUDA_TRY(cudaGetLastError());
     return TQB200_OK;
 }
