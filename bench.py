@@ -608,6 +608,14 @@ def bench_decode(args, rank, pg, pk, pk_kind):
     if world > 1:  # tensor parallel: every projection's output rows sharded over the ranks
         tp = {"tp_size": world, "tp_rank": rank, "nccl_id": share_nccl_id(pg, rank)}
     eng = lib.Engine(sm, max_seq_len=max_seq, kv_fp16=wl["kv16"], **tp)
+    exchange_mode = "none"
+    if world > 1:
+        exchange_mode = "nccl"
+        if args.exchange == "p2p" and spec.weight_dtype != "vq2":
+            # the all-gathers fused into the producing kernels (peer stores over NVLink)
+            from tqb200 import exchange
+            exchange.open_exchange(eng, exchange.gather_over_pg(eng.exchange_handle(), pg))
+            exchange_mode = "p2p"
     del sm.tensors  # host copy no longer needed
     # KV for the context: run the engine itself over positions 0..ctx-W-1 (greedy)
     rng = np.random.default_rng(1)
@@ -666,7 +674,8 @@ def bench_decode(args, rank, pg, pk, pk_kind):
     step_achieved = total_bytes / (ms_step * 1e-3) / 1e9
     # embed, per layer qkv / attention (QK-norm, RoPE and KV append fused) / o_proj /
     # gate_up / down, lm_head (+argmax), the device-side token feed, and with tensor
-    # parallelism the cross-rank argmax (NCCL's all-gather kernels are not counted)
+    # parallelism the cross-rank argmax (NCCL's all-gather kernels are not counted; with
+    # the peer exchange there are none)
     # MoE layers: qkv, attention, o_proj, router (+ top-k), gate/up, down, combine
     per_layer = 7 if spec.n_experts else 5
     launches = 2 + per_layer * spec.n_layers + 1 + (1 if world > 1 else 0)
@@ -683,6 +692,7 @@ def bench_decode(args, rank, pg, pk, pk_kind):
                    "context": ctx, "global_batch": 1,
                    "l2": "inputs larger than L2 (%.2f GB read per step)" % (total_bytes / 1e9),
                    "parallelism": "single GPU" if world == 1 else f"tp{world}",
+                   "exchange": exchange_mode,
                    "bytes_per_step": int(total_bytes),
                    "hbm_floor_ms": round(total_bytes / (pk["hbm_gbs"] * 1e9) * 1e3, 4),
                    "model_build_s": round(t_build, 1)},
@@ -1032,6 +1042,9 @@ def main():
     ap.add_argument("--cols", type=int, default=None, help="matvec-i4: columns (default config 1)")
     ap.add_argument("--copies", type=int, default=None,
                     help="matvec-i4: distinct weight copies per graph (default 64 for config 1, else 2)")
+    ap.add_argument("--exchange", choices=("p2p", "nccl"), default="p2p",
+                    help="tensor-parallel decode: all-gathers fused into the producing kernels "
+                         "over peer memory (p2p, i4 models) or NCCL all-gather launches")
     ap.add_argument("--no-extras", dest="extras", action="store_false",
                     help="decode workloads: skip the config-1 and lm_head matvec keys")
     args = ap.parse_args()

@@ -236,6 +236,19 @@ typedef struct tqb200_engine_opts {
  * library was built without NCCL). */
 int tqb200_nccl_unique_id(unsigned char id[128]);
 
+/* Peer exchange (no reference counterpart; the reference is single-device).  Every rank
+ * exports its activation arena (a CUDA IPC handle, 64 bytes) after tqb200_engine_create,
+ * the ranks share the handles (rank r's at handles + 64 r), and every rank then opens the
+ * others' arenas.  From the next step on, each layer's all-gathers run inside the kernels
+ * that produce the rows: attention, o_proj, gate/up and down (a MoE layer's expert down)
+ * store their rows into every rank's buffer over NVLink and release a per-exchange counter
+ * there; the consuming kernel waits for it (bounded: 20 s, then status
+ * TQB200_ERR_TIMEOUT) instead of an NCCL launch.  Results are bit-identical to the NCCL
+ * path.  i4 models only (VQ2 models keep NCCL); at most 8 ranks; all ranks must open
+ * before any steps. */
+int tqb200_engine_exchange_handle(tqb200_engine *e, unsigned char handle[64]);
+int tqb200_engine_open_exchange(tqb200_engine *e, const unsigned char *handles, int n_ranks);
+
 void tqb200_engine_default_opts(tqb200_engine_opts *opts);
 /* GpuDecodeCreateFn (kernels/dispatch.h:356). */
 int tqb200_engine_create(const tqb200_model_desc *desc, const tqb200_engine_opts *opts,

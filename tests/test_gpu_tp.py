@@ -1,6 +1,8 @@
-"""Tensor-parallel engine (tp_size 2, one process per GPU, NCCL all-gather per layer;
-MoE layers expert-parallel) against the single-GPU oracle: identical greedy tokens and logits within 1e-4 on
-every rank.  Needs two visible GPUs (skipped otherwise)."""
+"""Tensor-parallel engine (tp_size 2, one process per GPU; MoE layers expert-parallel)
+against the single-GPU oracle: identical greedy tokens and logits within 1e-4 on every
+rank, with the activations all-gathered over NCCL and with the peer exchange (the
+all-gathers fused into the producing kernels over NVLink; i4 models).  Needs two visible
+GPUs (skipped otherwise)."""
 from __future__ import annotations
 
 import os
@@ -21,8 +23,11 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 TP_CASES = [c for c in gc.MODEL_CASES if c[0] in ("qwen2_bias", "qwen3_f16kv", "vq2_rot", "moe")]
 
 
-@pytest.mark.parametrize("case", TP_CASES, ids=[c[0] for c in TP_CASES])
-def test_tp2_engine_matches_oracle(tq, oracle, tmp_path, case):
+MODES = [(c, m) for c in TP_CASES for m in ("nccl", "p2p") if not (m == "p2p" and c[0] == "vq2_rot")]
+
+
+@pytest.mark.parametrize("case,mode", MODES, ids=[f"{c[0]}-{m}" for c, m in MODES])
+def test_tp2_engine_matches_oracle(tq, oracle, tmp_path, case, mode):
     import torch
     world = 2
     if torch.cuda.device_count() < world:
@@ -32,7 +37,7 @@ def test_tp2_engine_matches_oracle(tq, oracle, tmp_path, case):
     outs = [str(tmp_path / f"r{r}.npz") for r in range(world)]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     procs = [subprocess.Popen([sys.executable, os.path.join(HERE, "tp_worker.py"), str(r),
-                               str(world), nid, name, outs[r]], env=env,
+                               str(world), nid, name, outs[r], mode, str(tmp_path)], env=env,
                               stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
              for r in range(world)]
     logs = []

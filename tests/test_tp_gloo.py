@@ -111,8 +111,52 @@ def _nccl_id_broadcast(rank):
     return bytes(nid.numpy().tobytes()) == bytes((np.arange(128) * 3 % 256).astype(np.uint8))
 
 
-@pytest.mark.parametrize("fn", [_sharded_matvecs, _sharded_argmax, _nccl_id_broadcast],
-                         ids=["row_shards_allgather", "vocab_shard_argmax", "nccl_id_broadcast"])
+def _handle(rank):
+    return ((np.arange(64) * (rank + 3) + rank) % 256).astype(np.uint8).tobytes()
+
+
+def _exchange_path():
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                                    "tiny-llm_b200"))
+
+
+def _exchange_handles_pg(rank):
+    """The peer exchange's handle sharing over a process group: every rank gets every
+    rank's 64-byte arena handle in rank order."""
+    _exchange_path()
+    from tqb200 import exchange
+    got = exchange.gather_over_pg(_handle(rank), dist)
+    return got == [_handle(r) for r in range(WORLD)]
+
+
+def _exchange_handles_dir(directory, rank):
+    """The same through files in a shared directory (the test workers' rendezvous)."""
+    _exchange_path()
+    from tqb200 import exchange
+    got = exchange.gather_over_dir(_handle(rank), rank, WORLD, directory, timeout_s=60)
+    return got == [_handle(r) for r in range(WORLD)]
+
+
+@pytest.mark.parametrize("fn", [_sharded_matvecs, _sharded_argmax, _nccl_id_broadcast,
+                                _exchange_handles_pg],
+                         ids=["row_shards_allgather", "vocab_shard_argmax", "nccl_id_broadcast",
+                              "exchange_handles_pg"])
 def test_tp_host_logic_world2_gloo(fn):
     out = _run(fn)
     assert out == {0: True, 1: True}, out
+
+
+def test_exchange_handles_dir_world2(tmp_path):
+    import functools
+    out = _run(functools.partial(_exchange_handles_dir, str(tmp_path)))
+    assert out == {0: True, 1: True}, out
+
+
+def test_exchange_handles_dir_times_out_without_peer(tmp_path):
+    _exchange_path()
+    from tqb200 import exchange
+    with pytest.raises(TimeoutError, match=r"ranks \[1\]"):
+        exchange.gather_over_dir(_handle(0), 0, 2, str(tmp_path), timeout_s=0.2)
+    with pytest.raises(AssertionError):
+        exchange.gather_over_dir(b"short", 0, 2, str(tmp_path), timeout_s=0.2)

@@ -63,6 +63,8 @@ struct TmaAttnParams {
     float *out;
     int *status;
     Stamp stamp;                    // in-graph timeline (off unless the engine records one)
+    const XPut *put;                // tensor parallelism (device descriptor, XCHG instance
+                                    // only): out rows also go to every peer
 };
 
 template <typename KV>
@@ -217,7 +219,7 @@ __device__ __forceinline__ void norm_rope_warp(float *x, const float *nw, float 
 // 16-bit caches: at most 128 registers, so two CTAs fit an SM with the staged rows; the
 // fp32 instantiations keep the compiler's choice (all <= 127 but G=8 x HD 128 at 156,
 // whose 4-KV-head grids run one CTA per SM anyway).
-template <typename KV, int HD, int G, bool STAMP>
+template <typename KV, int HD, int G, bool STAMP, bool XCHG>
 __global__ void __launch_bounds__(kThreads, sizeof(KV) == 2 ? 2 : 1) attn_tma_kernel(const __grid_constant__ TmaAttnParams P) {
     namespace cg = cooperative_groups;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -600,15 +602,22 @@ __global__ void __launch_bounds__(kThreads, sizeof(KV) == 2 ? 2 : 1) attn_tma_ke
         const int g = i / HD, j = i - split * per;
         float O = 0.0f;
         for (int s2 = 0; s2 < ns; ++s2) O = fmaf(rcv_o[s2 * per + j], wgt[s2 * G + g], O);
-        P.out[(size_t)kh * G * HD + i] = O / s_l[g];
+        if constexpr (XCHG) {
+            if (P.put) xput_val(*P.put, P.out + (size_t)kh * G * HD + i, O / s_l[g]);
+            else P.out[(size_t)kh * G * HD + i] = O / s_l[g];
+        } else {
+            P.out[(size_t)kh * G * HD + i] = O / s_l[g];
+        }
     }
+    if constexpr (XCHG)
+        if (P.put) xput_arrive(*P.put);
     stamp_exit<STAMP>(P.stamp, stamp_r);
 }
 
-template <typename KV, int HD, int G, bool STAMP>
+template <typename KV, int HD, int G, bool STAMP, bool XCHG>
 int launch_t(const AttnArgs &a, cudaStream_t st) {
     constexpr int RB = HD * (int)sizeof(KV);
-    auto k = attn_tma_kernel<KV, HD, G, STAMP>;
+    auto k = attn_tma_kernel<KV, HD, G, STAMP, XCHG>;
     static KernelSmem attr;
     static std::atomic<unsigned long long> cluster_attr{0};
     int smem_max = 0;
@@ -664,6 +673,7 @@ int launch_t(const AttnArgs &a, cudaStream_t st) {
         P.out = a.out;
         P.status = a.status;
         P.stamp = a.stamp;
+        P.put = a.put;
         // barriers | ring | new k, v rows (cache type) | krow, vrow, qs, cs+sn, qn, kn
         const size_t smem = 128 + (size_t)P.stage_region + ((2 * (size_t)RB + 15) & ~(size_t)15) +
                             ((size_t)5 * HD + (size_t)G * HD) * 4 +
@@ -703,7 +713,10 @@ int launch_kv(const AttnArgs &a, cudaStream_t st) {
     const int G = a.n_heads / a.n_kv_heads;
 #define TQ_TMA_CASE(HDV, GV)                                                              \
     if (a.head_dim == HDV && G == GV)                                                      \
-        return a.stamp.base ? launch_t<KV, HDV, GV, true>(a, st) : launch_t<KV, HDV, GV, false>(a, st);
+        return a.put ? (a.stamp.base ? launch_t<KV, HDV, GV, true, true>(a, st)                \
+                                     : launch_t<KV, HDV, GV, false, true>(a, st))              \
+                     : (a.stamp.base ? launch_t<KV, HDV, GV, true, false>(a, st)               \
+                                     : launch_t<KV, HDV, GV, false, false>(a, st));
     TQ_TMA_CASE(64, 1) TQ_TMA_CASE(64, 2) TQ_TMA_CASE(64, 4) TQ_TMA_CASE(64, 7)
     TQ_TMA_CASE(64, 8) TQ_TMA_CASE(128, 1) TQ_TMA_CASE(128, 2) TQ_TMA_CASE(128, 4)
     TQ_TMA_CASE(128, 8) TQ_TMA_CASE(32, 1) TQ_TMA_CASE(32, 2) TQ_TMA_CASE(32, 4)

@@ -226,6 +226,7 @@ enum : int {
     kDevBadToken = 3,     // token id outside [0, vocab)
     kDevBadPosition = 4,  // position outside [0, max_seq)
     kDevBadExpert = 5,    // expert index outside [0, n_experts)
+    kDevTimeoutPeer = 6,  // a peer rank's exchanged rows did not arrive within the bound
 };
 
 }  // namespace tqb200

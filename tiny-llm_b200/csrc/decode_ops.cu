@@ -584,11 +584,13 @@ __global__ void argmax_kernel(const float *__restrict__ l, int n, float *__restr
 }
 
 // Global greedy token from per-rank (max, index) pairs: largest value, then lowest index.
-__global__ void argmax_pairs_kernel(const ArgPair *__restrict__ pairs, int n, int *__restrict__ out) {
+__global__ void argmax_pairs_kernel(const ArgPair *__restrict__ pairs, int n, int *__restrict__ out,
+                                    XWait xw, int *status) {
+    xwait(xw, status);  // peer exchange: every rank's pair has landed
     if (threadIdx.x != 0) return;
     float bv = -INFINITY;
     int bi = INT_MAX;
-    for (int r = 0; r < n; ++r) better(bv, bi, pairs[r].v, pairs[r].i);
+    for (int r = 0; r < n; ++r) better(bv, bi, __ldcg(&pairs[r].v), __ldcg(&pairs[r].i));
     *out = bi == INT_MAX ? 0 : bi;
 }
 
@@ -720,7 +722,7 @@ template <bool STAMP>
 __global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(
     const float *__restrict__ h, const float *__restrict__ norm_w, float eps, int H,
     const float *__restrict__ W, int E, int k, float *__restrict__ logits, int *__restrict__ idx,
-    float *__restrict__ wts, unsigned int *ticket, Stamp stamp) {
+    float *__restrict__ wts, unsigned int *ticket, Stamp stamp, XWait xw, int *status) {
     extern __shared__ __align__(16) float xn[];  // [H]
     StampRegs stamp_r;
     stamp_enter<STAMP>(stamp, stamp_r);
@@ -742,6 +744,7 @@ __global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(
     griddep_wait();
     stamp_waited<STAMP>(stamp, stamp_r);
     griddep_launch();
+    xwait(xw, status);  // tensor parallelism: the peers' rows of h have landed
     // the hidden vector and the norm weights, every load issued before any is used
     // (a chunk of kRouterHid per thread at a time)
     double ss = 0.0;
@@ -823,13 +826,15 @@ __global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(
 // rounding points (runtime/qwen_forward_token.cpp:604-609, :627-631).
 template <bool STAMP>
 __global__ void moe_combine_kernel(float *__restrict__ h, const float *__restrict__ o,
-                                   const float *__restrict__ wts, int k, int H, Stamp stamp) {
+                                   const float *__restrict__ wts, int k, int H, Stamp stamp,
+                                   XWait xw, int *status) {
     StampRegs stamp_r;
     stamp_enter<STAMP>(stamp, stamp_r);
     stamp_step<STAMP>(stamp, stamp_r);
     griddep_wait();
     stamp_waited<STAMP>(stamp, stamp_r);
     griddep_launch();
+    xwait(xw, status);  // expert parallelism: every owner's slot rows have landed
     constexpr int kMax = 16;  // expert outputs loaded at once (k is at most 32)
     for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < H; j += gridDim.x * blockDim.x) {
         float acc = 0.0f;
@@ -863,12 +868,17 @@ __global__ void moe_ep_local_kernel(const int *__restrict__ idx, int k, int e0, 
         const int e = idx[i] - e0;
         local[i] = (e >= 0 && e < e_local) ? e : -1;
     }
-    for (int j = i; j < n; j += gridDim.x * blockDim.x) o[j] = 0.0f;
+    if (o)
+        for (int j = i; j < n; j += gridDim.x * blockDim.x) o[j] = 0.0f;
 }
 
 // ------------------------------------------------------------------ embed
 __global__ void embed_kernel(const void *__restrict__ table, int dtype, const int *__restrict__ token,
-                             int dim, int group_size, float *__restrict__ out) {
+                             int dim, int group_size, float *__restrict__ out,
+                             unsigned int *__restrict__ epoch) {
+    // the decode step's epoch for the peer exchanges (launched without PDL: every kernel
+    // of the previous step has completed, none of this step's has started)
+    if (epoch && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *epoch += 1u;
     const int tok = token[blockIdx.y];  // batched: row blockIdx.y
     out += (size_t)blockIdx.y * dim;
     for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < dim; c += gridDim.x * blockDim.x) {
@@ -1118,6 +1128,8 @@ int launch_attention(const AttnArgs &a, cudaStream_t st) {
     TQ_CHECK_ARG(!a.k_new || (a.pos && a.v_new && a.cos_tab && a.sin_tab), "fused attention args");
     const int rc = launch_attention_tma(a, st);
     if (rc != TQB200_ERR_UNSUPPORTED) return rc;
+    TQ_CHECK_ARG(!a.put, "peer exchange needs the TMA attention kernel (head_dim %d, group %d)",
+                 a.head_dim, a.n_heads / a.n_kv_heads);
     // no TMA shape: the split kernel (global partials), after the per-head
     // QK-norm / RoPE / KV-append kernel in fused mode
     TQ_CHECK_ARG(a.chunk_max >= (a.max_seq + a.nsplit - 1) / a.nsplit, "chunk plan");
@@ -1170,8 +1182,9 @@ int launch_swiglu_out(const float *g, const float *u, float *out, int n, cudaStr
     return TQB200_OK;
 }
 
-int launch_argmax_pairs(const ArgPair *pairs, int n, int *out, cudaStream_t st) {
-    argmax_pairs_kernel<<<1, 32, 0, st>>>(pairs, n, out);
+int launch_argmax_pairs(const ArgPair *pairs, int n, int *out, cudaStream_t st, const XWait &xw,
+                        int *status) {
+    argmax_pairs_kernel<<<1, 32, 0, st>>>(pairs, n, out, xw, status);
     TQ_CUDA_TRY(cudaGetLastError());
     return TQB200_OK;
 }
@@ -1204,22 +1217,23 @@ int launch_pdl(Kern k, int grid, int block, size_t smem, bool pdl, cudaStream_t 
 
 int launch_moe_router(const float *h, const float *norm_w, float eps, int H, const float *W, int E,
                       int k, float *logits, int *idx, float *wts, unsigned int *ticket, bool pdl,
-                      cudaStream_t st, const Stamp &stamp) {
+                      cudaStream_t st, const Stamp &stamp, const XWait &xw, int *status) {
     TQ_CHECK_ARG(E > 0 && E <= 32 * kRouterPer && k > 0 && k <= 32 && k <= E && H > 0,
                  "moe router: E %d k %d H %d", E, k, H);
     const size_t smem = (size_t)H * 4;
     TQ_CHECK_ARG(smem <= 48 * 1024, "moe router: hidden %d too large", H);
     return launch_pdl(stamp.base ? moe_router_kernel<true> : moe_router_kernel<false>,
                       (E + kRouterWarps - 1) / kRouterWarps, kRouterWarps * 32, smem, pdl, st, h,
-                      norm_w, eps, H, W, E, k, logits, idx, wts, ticket, stamp);
+                      norm_w, eps, H, W, E, k, logits, idx, wts, ticket, stamp, xw, status);
 }
 
 int launch_moe_combine(float *h, const float *o, const float *wts, int k, int H, bool pdl,
-                       cudaStream_t st, const Stamp &stamp) {
+                       cudaStream_t st, const Stamp &stamp, const XWait &xw, int *status) {
     TQ_CHECK_ARG(k > 0 && H > 0, "moe combine: k %d H %d", k, H);
     const int threads = 256;
     return launch_pdl(stamp.base ? moe_combine_kernel<true> : moe_combine_kernel<false>,
-                      (H + threads - 1) / threads, threads, 0, pdl, st, h, o, wts, k, H, stamp);
+                      (H + threads - 1) / threads, threads, 0, pdl, st, h, o, wts, k, H, stamp, xw,
+                      status);
 }
 
 int launch_topk_softmax(const float *logits, int n, int k, int *idx, float *w, cudaStream_t st) {
@@ -1258,16 +1272,16 @@ int launch_moe_combine_rows(float *h, const float *o, const float *wts, const in
 int launch_moe_ep_local(const int *idx, int k, int e0, int e_local, int *local, float *o, int H,
                         bool pdl, cudaStream_t st) {
     TQ_CHECK_ARG(k > 0 && k <= 1024 && H > 0 && e_local > 0, "moe ep: k %d H %d", k, H);
-    const int n = k * H, threads = 256;
+    const int n = o ? k * H : k, threads = 256;
     const int grid = std::max(1, std::min((n + threads - 1) / threads, 64));
     return launch_pdl(moe_ep_local_kernel, grid, threads, 0, pdl, st, idx, k, e0, e_local, local, o, n);
 }
 
 int launch_embed(const void *table, int dtype, const int *token, int dim, int group_size,
-                 float *out, cudaStream_t st, int n_tokens) {
+                 float *out, cudaStream_t st, int n_tokens, unsigned int *epoch) {
     TQ_CHECK_ARG(n_tokens >= 1 && n_tokens <= 65535, "embed: %d tokens", n_tokens);
     const dim3 grid(std::max(1, std::min((dim + 255) / 256, 16)), n_tokens);
-    embed_kernel<<<grid, 256, 0, st>>>(table, dtype, token, dim, group_size, out);
+    embed_kernel<<<grid, 256, 0, st>>>(table, dtype, token, dim, group_size, out, epoch);
     TQ_CUDA_TRY(cudaGetLastError());
     return TQB200_OK;
 }

@@ -23,8 +23,10 @@
 // Tensor parallelism (tp_size > 1, one process per GPU): every projection's
 // output rows are split evenly (q/k/v by head, o/down by hidden row, gate/up by
 // intermediate row, lm_head by vocabulary row); each rank runs the same kernels
-// on its rows and the activations are all-gathered in place over NCCL (inside
-// the CUDA graph) after attention, o_proj, SwiGLU and down.  Every output
+// on its rows and the activations are all-gathered after attention, o_proj,
+// SwiGLU and down: by the producing kernels themselves over the ranks' mapped
+// arenas once the peer exchange is open (tqb200_engine_open_exchange), else in
+// place over NCCL inside the CUDA graph.  Every output
 // element is computed by exactly the kernel and order the single-GPU engine
 // uses, so tokens and logits do not depend on the number of GPUs.  The greedy
 // token is the first maximum over the ranks' (max, index) pairs.
@@ -159,6 +161,23 @@ struct tqb200_engine {
 #ifdef TQB200_HAVE_NCCL
     ncclComm_t comm = nullptr;
 #endif
+    // peer exchange (tqb200_engine_open_exchange): the all-gathers fused into the
+    // producing kernels over the ranks' mapped arenas instead of NCCL
+    void *xarena = nullptr;              // activations, then counters, tickets and epoch
+    bool p2p = false;
+    int n_peers = 0;
+    long long xdelta[tqb200::kMaxPeers] = {};
+    std::vector<void *> peer_maps;       // the other ranks' arenas, mapped here
+    unsigned long long *xcnt = nullptr;  // [n_xslots] arrival counters
+    unsigned int *xticket = nullptr;     // [n_xslots] CTA tickets
+    unsigned int *epoch = nullptr;       // decode steps since the exchange opened
+    // per exchange slot: the consumer and producer descriptors, on the host (kernels that
+    // take them by value) and on the device (the matvec and attention kernels' exchange
+    // instances read them from there)
+    std::vector<tqb200::XWait> xw_host;
+    std::vector<tqb200::XPut> xp_host;
+    tqb200::XWait *xw_dev = nullptr;
+    tqb200::XPut *xp_dev = nullptr;
 };
 
 namespace tqb200 {
@@ -387,9 +406,24 @@ __global__ void feed_next_kernel(int *io_in, const int *io_out, int *tokens, int
     *count = c + 1;
 }
 
+// Peer-exchange slots: four per layer (a MoE layer uses three: its FFN slot carries the
+// experts' output slots and the combine runs whole on every rank), then lm_head's.
+enum XSlot { XS_ATTN, XS_HID_O, XS_FFN, XS_HID_D, XS_PER_LAYER };
+int n_xslots(const tqb200_model_desc &d) { return d.n_layers * XS_PER_LAYER + 1; }
+int xslot_lm(const tqb200_model_desc &d) { return d.n_layers * XS_PER_LAYER; }
+
+// The producer and consumer descriptors of exchange `slot` (device copies for the matvec
+// and attention kernels, values for the others; none without an open exchange).
+const XPut *xput(const tqb200_engine *e, int slot) { return e->p2p ? e->xp_dev + slot : nullptr; }
+const XWait *xwait_of(const tqb200_engine *e, int slot) {
+    return e->p2p ? e->xw_dev + slot : nullptr;
+}
+XWait xwait_val(const tqb200_engine *e, int slot) { return e->p2p ? e->xw_host[slot] : XWait(); }
+
 // In-place all-gather of `count` floats per rank (rank r's slice at buf + r * count).
+// With the peer exchange open the producing kernel has already stored the rows.
 int allgather(tqb200_engine *e, float *buf, size_t count) {
-    if (e->tp == 1) return TQB200_OK;
+    if (e->tp == 1 || e->p2p) return TQB200_OK;
 #ifdef TQB200_HAVE_NCCL
     const ncclResult_t nr =
         ncclAllGather(buf + (size_t)e->rank * count, buf, count, ncclFloat, e->comm, e->stream);
@@ -403,9 +437,10 @@ int allgather(tqb200_engine *e, float *buf, size_t count) {
 #endif
 }
 
-// In-place sum over the ranks of `count` floats.
+// In-place sum over the ranks of `count` floats (with the peer exchange open every
+// owner has stored its slots in every rank's buffer instead).
 int allreduce_sum(tqb200_engine *e, float *buf, size_t count) {
-    if (e->tp == 1) return TQB200_OK;
+    if (e->tp == 1 || e->p2p) return TQB200_OK;
 #ifdef TQB200_HAVE_NCCL
     const ncclResult_t nr = ncclAllReduce(buf, buf, count, ncclFloat, ncclSum, e->comm, e->stream);
     if (nr != ncclSuccess)
@@ -434,7 +469,8 @@ int launch_forward(tqb200_engine *e) {
     float *attn_mine = e->attn + (size_t)r * qdl;
     float *hidden_mine = e->hidden + (size_t)r * Hs;
     TQ_TRY(mark(e, -1));
-    TQ_TRY(launch_embed(e->embed, e->embed_dtype, e->io_in, H, d.group_size, e->hidden, st));
+    TQ_TRY(launch_embed(e->embed, e->embed_dtype, e->io_in, H, d.group_size, e->hidden, st, 1,
+                        e->p2p ? e->epoch : nullptr));
     TQ_TRY(mark(e, K_EMBED));
     for (int l = 0; l < d.n_layers; ++l) {
         const DLayer &w = e->layers[l];
@@ -475,6 +511,8 @@ int launch_forward(tqb200_engine *e) {
             o.pdl = pdl;
             o.status = status;
             o.stamp = tl_next(e, K_QKV);
+            // the previous dense layer's down rows (a MoE layer's combine is local)
+            if (l > 0 && !e->layers[l - 1].moe) o.xwait = xwait_of(e, (l - 1) * XS_PER_LAYER + XS_HID_D);
             TQ_TRY(launch_i4_matvec_ex(j, 3, H, d.group_size, o, st));
             TQ_TRY(mark(e, K_QKV));
         }
@@ -510,6 +548,7 @@ int launch_forward(tqb200_engine *e) {
             a.pdl = pdl;
             a.status = status;
             a.stamp = tl_next(e, K_ATTN);
+            a.put = xput(e, l * XS_PER_LAYER + XS_ATTN);
             TQ_TRY(launch_attention(a, st));
             TQ_TRY(allgather(e, e->attn, qdl));
             TQ_TRY(mark(e, K_ATTN));
@@ -529,6 +568,8 @@ int launch_forward(tqb200_engine *e) {
             o.pdl = pdl;
             o.status = status;
             o.stamp = tl_next(e, K_OPROJ);
+            o.xwait = xwait_of(e, l * XS_PER_LAYER + XS_ATTN);
+            o.put = xput(e, l * XS_PER_LAYER + XS_HID_O);
             TQ_TRY(launch_i4_matvec_ex(&j, 1, qd, d.group_size, o, st));
             TQ_TRY(allgather(e, e->hidden, Hs));
             TQ_TRY(mark(e, K_OPROJ));
@@ -549,7 +590,8 @@ int launch_forward(tqb200_engine *e) {
             if (w.router_f32) {
                 TQ_TRY(launch_moe_router(e->hidden, w.post_ln, d.rms_eps, H, w.router_f32, E, k,
                                          e->moe_logits, e->moe_idx, e->moe_w, e->moe_ticket, pdl,
-                                         st, tl_next(e, K_ROUTER)));
+                                         st, tl_next(e, K_ROUTER),
+                                         xwait_val(e, l * XS_PER_LAYER + XS_HID_O), status));
             } else {
                 I4Job j{w.router_i4, e->moe_logits, nullptr, nullptr, E};
                 I4LaunchOpts o;
@@ -557,11 +599,13 @@ int launch_forward(tqb200_engine *e) {
                 o.pdl = pdl;
                 o.status = status;
                 o.stamp = tl_next(e, K_ROUTER);
+                o.xwait = xwait_of(e, l * XS_PER_LAYER + XS_HID_O);
                 TQ_TRY(launch_i4_matvec_ex(&j, 1, H, d.group_size, o, st));
                 TQ_TRY(launch_topk_softmax(e->moe_logits, E, k, e->moe_idx, e->moe_w, st));
             }
             if (G > 1)
-                TQ_TRY(launch_moe_ep_local(e->moe_idx, k, r * El, El, e->moe_local, e->moe_o, H, pdl, st));
+                TQ_TRY(launch_moe_ep_local(e->moe_idx, k, r * El, El, e->moe_local,
+                                           e->p2p ? nullptr : e->moe_o, H, pdl, st));
             TQ_TRY(mark(e, K_ROUTER));
             {
                 I4Job j[2] = {{w.ex_gate, e->moe_h, nullptr, nullptr, k * mi},
@@ -577,6 +621,7 @@ int launch_forward(tqb200_engine *e) {
                 o.pdl = pdl;
                 o.status = status;
                 o.stamp = tl_next(e, K_GATEUP);
+                o.xwait = xwait_of(e, l * XS_PER_LAYER + XS_HID_O);
                 TQ_TRY(launch_i4_matvec_ex(j, 2, H, d.group_size, o, st));
                 TQ_TRY(mark(e, K_GATEUP));
             }
@@ -593,12 +638,14 @@ int launch_forward(tqb200_engine *e) {
                 o.pdl = pdl;
                 o.status = status;
                 o.stamp = tl_next(e, K_DOWN);
+                o.put = xput(e, l * XS_PER_LAYER + XS_FFN);
                 TQ_TRY(launch_i4_matvec_ex(&j, 1, mi, d.group_size, o, st));
                 TQ_TRY(allreduce_sum(e, e->moe_o, (size_t)k * H));
                 TQ_TRY(mark(e, K_DOWN));
             }
             TQ_TRY(launch_moe_combine(e->hidden, e->moe_o, e->moe_w, k, H, pdl, st,
-                                      tl_next(e, K_COMBINE)));
+                                      tl_next(e, K_COMBINE),
+                                      xwait_val(e, l * XS_PER_LAYER + XS_FFN), status));
             TQ_TRY(mark(e, K_COMBINE));
             continue;
         }
@@ -623,6 +670,8 @@ int launch_forward(tqb200_engine *e) {
             o.pdl = pdl;
             o.status = status;
             o.stamp = tl_next(e, K_GATEUP);
+            o.xwait = xwait_of(e, l * XS_PER_LAYER + XS_HID_O);
+            o.put = xput(e, l * XS_PER_LAYER + XS_FFN);
             TQ_TRY(launch_i4_matvec_ex(j, 2, H, d.group_size, o, st));
             TQ_TRY(allgather(e, e->act, Is));
             TQ_TRY(mark(e, K_GATEUP));
@@ -642,6 +691,8 @@ int launch_forward(tqb200_engine *e) {
             o.pdl = pdl;
             o.status = status;
             o.stamp = tl_next(e, K_DOWN);
+            o.xwait = xwait_of(e, l * XS_PER_LAYER + XS_FFN);
+            o.put = xput(e, l * XS_PER_LAYER + XS_HID_D);
             TQ_TRY(launch_i4_matvec_ex(&j, 1, d.inter, d.group_size, o, st));
             TQ_TRY(allgather(e, e->hidden, Hs));
             TQ_TRY(mark(e, K_DOWN));
@@ -676,11 +727,15 @@ int launch_lm_head(tqb200_engine *e) {
         o.pdl = pdl;
         o.status = status;
         o.stamp = tl_next(e, K_LMHEAD);
+        const int L = d.n_layers;
+        if (!e->layers[L - 1].moe) o.xwait = xwait_of(e, (L - 1) * XS_PER_LAYER + XS_HID_D);
+        o.put = xput(e, xslot_lm(d));
         TQ_TRY(launch_i4_matvec_ex(&j, 1, H, d.group_size, o, st));
         if (G > 1) {
             TQ_TRY(allgather(e, reinterpret_cast<float *>(e->pairs), 2));
             TQ_TRY(allgather(e, e->logits, Vs));
-            TQ_TRY(launch_argmax_pairs(e->pairs, G, e->io_out, st));
+            TQ_TRY(launch_argmax_pairs(e->pairs, G, e->io_out, st, xwait_val(e, xslot_lm(d)),
+                                       status));
         }
         TQ_TRY(mark(e, K_LMHEAD));
     }
@@ -734,6 +789,7 @@ void free_engine(tqb200_engine *e) {
 #ifdef TQB200_HAVE_NCCL
     if (e->comm) ncclCommDestroy(e->comm);
 #endif
+    for (void *p : e->peer_maps) cudaIpcCloseMemHandle(p);
     for (void *p : e->allocs) cudaFree(p);
     if (e->tl) cudaFree(e->tl);
     if (e->h_io) cudaFreeHost(e->h_io);
@@ -866,9 +922,24 @@ int create_impl(const tqb200_model_desc *desc, const tqb200_engine_opts *opts, t
     TQ_TRY(up_vec(e, d.final_norm, H, &e->final_norm));
     TQ_TRY(build_rope_tables(e));
 
+    // The exchange arena (one allocation, the same layout on every rank, mapped by the
+    // peers when the peer exchange opens): the activations, the MoE buffers, then the
+    // exchange counters, tickets and epoch.
     void *p;
-    const size_t act = (size_t)H * 2 + qd * 2 + kvd * 2 + (size_t)d.inter * 3 + d.vocab + 64;
-    TQ_TRY(dev_alloc(e, act * 4, &p));
+    const size_t act = ((size_t)H * 2 + qd * 2 + kvd * 2 + (size_t)d.inter * 3 + d.vocab + 64 + 63) &
+                       ~(size_t)63;
+    const bool moe_model = d.model_type == TQB200_MODEL_QWEN3_MOE;
+    const size_t moe_n = moe_model ? ((size_t)d.n_experts + 2 * (size_t)d.experts_per_tok * d.moe_inter +
+                                      (size_t)d.experts_per_tok * H + 4 * 64 + 63) & ~(size_t)63
+                                   : 0;
+    const size_t nx = (size_t)n_xslots(d);
+    const size_t arena = (act + moe_n) * 4 + nx * 8 + nx * 4 + 256;
+    TQ_TRY(dev_alloc(e, arena, &p));
+    TQ_CUDA_TRY(cudaMemset(p, 0, arena));
+    e->xarena = p;
+    e->xcnt = reinterpret_cast<unsigned long long *>((char *)p + (act + moe_n) * 4);
+    e->xticket = reinterpret_cast<unsigned int *>(e->xcnt + nx);
+    e->epoch = e->xticket + nx;
     float *f = (float *)p;
     e->hidden = f, f += H;
     e->q = f, f += qd;
@@ -881,12 +952,9 @@ int create_impl(const tqb200_model_desc *desc, const tqb200_engine_opts *opts, t
     e->logits = f, f += d.vocab;
     e->pairs = reinterpret_cast<ArgPair *>(f);
     TQ_CHECK_ARG(G <= 32, "tp_size %d above 32", G);
-    if (d.model_type == TQB200_MODEL_QWEN3_MOE) {
+    if (moe_model) {
         const int k = d.experts_per_tok, mi = d.moe_inter;
-        const size_t n = (size_t)d.n_experts + 2 * (size_t)k * mi + (size_t)k * H + 4 * 64;
-        TQ_TRY(dev_alloc(e, n * 4 + 256, &p));
-        TQ_CUDA_TRY(cudaMemset(p, 0, n * 4 + 256));
-        float *m = (float *)p;
+        float *m = (float *)e->xarena + act;  // 256-byte aligned
         e->moe_h = m, m += (size_t)k * mi;       // 16-byte aligned rows of mi floats
         e->moe_u = m, m += (size_t)k * mi;
         e->moe_o = m, m += (size_t)k * H;
@@ -1545,6 +1613,74 @@ int tqb200_engine_kv_cache(const tqb200_engine *e, void **kv, size_t *bytes) {
 int tqb200_engine_weight_bytes(const tqb200_engine *e, size_t *bytes) {
     TQ_CHECK_ARG(e && bytes, "null argument");
     *bytes = e->weight_bytes;
+    return TQB200_OK;
+}
+
+int tqb200_engine_exchange_handle(tqb200_engine *e, unsigned char handle[64]) {
+    TQ_CHECK_ARG(e && handle, "null argument");
+    TQ_CUDA_TRY(cudaSetDevice(e->device));
+    TQ_CUDA_TRY(cudaDeviceSynchronize());  // the arena's zeroed counters are in place
+    cudaIpcMemHandle_t h;
+    static_assert(sizeof(h) == 64, "CUDA IPC handle size");
+    TQ_CUDA_TRY(cudaIpcGetMemHandle(&h, e->xarena));
+    memcpy(handle, &h, 64);
+    return TQB200_OK;
+}
+
+int tqb200_engine_open_exchange(tqb200_engine *e, const unsigned char *handles, int n_ranks) {
+    TQ_CHECK_ARG(e && handles, "null argument");
+    TQ_CHECK_ARG(n_ranks == e->tp && e->tp > 1, "open_exchange: %d handles for tp_size %d",
+                 n_ranks, e->tp);
+    TQ_CHECK_ARG(e->tp - 1 <= kMaxPeers, "open_exchange: tp_size %d above %d", e->tp,
+                 kMaxPeers + 1);
+    TQ_CHECK_ARG(!e->p2p, "open_exchange: already open");
+    TQ_CHECK_ARG(!e->layers[0].vq2, "open_exchange: VQ2 models keep the NCCL all-gathers");
+    TQ_CUDA_TRY(cudaSetDevice(e->device));
+    TQ_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    int np = 0;
+    for (int r = 0; r < n_ranks; ++r) {
+        if (r == e->rank) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, handles + 64 * (size_t)r, 64);
+        void *peer = nullptr;
+        const cudaError_t ce = cudaIpcOpenMemHandle(&peer, h, cudaIpcMemLazyEnablePeerAccess);
+        if (ce != cudaSuccess) {
+            for (void *q : e->peer_maps) cudaIpcCloseMemHandle(q);
+            e->peer_maps.clear();
+            return set_error(TQB200_ERR_CUDA, "open_exchange: rank %d's arena: %s", r,
+                             cudaGetErrorString(ce));
+        }
+        e->peer_maps.push_back(peer);
+        e->xdelta[np++] = (long long)((char *)peer - (char *)e->xarena);
+    }
+    e->n_peers = np;
+    const int nx = n_xslots(e->d);
+    e->xw_host.assign(nx, XWait());
+    e->xp_host.assign(nx, XPut());
+    for (int s = 0; s < nx; ++s) {
+        XWait &w = e->xw_host[s];
+        w.arrive = e->xcnt + s;
+        w.epoch = e->epoch;
+        w.ranks = (unsigned int)e->tp;
+        XPut &p = e->xp_host[s];
+        p.n_peers = np;
+        for (int i = 0; i < np; ++i) p.delta[i] = e->xdelta[i];
+        p.arrive = e->xcnt + s;
+        p.ticket = e->xticket + s;
+    }
+    void *dw = nullptr, *dp = nullptr;
+    TQ_TRY(dev_alloc(e, sizeof(XWait) * nx, &dw));
+    TQ_TRY(dev_alloc(e, sizeof(XPut) * nx, &dp));
+    TQ_CUDA_TRY(cudaMemcpy(dw, e->xw_host.data(), sizeof(XWait) * nx, cudaMemcpyHostToDevice));
+    TQ_CUDA_TRY(cudaMemcpy(dp, e->xp_host.data(), sizeof(XPut) * nx, cudaMemcpyHostToDevice));
+    e->xw_dev = (XWait *)dw;
+    e->xp_dev = (XPut *)dp;
+    e->p2p = true;
+    // the step graphs are captured again on their next use, with the exchange
+    for (cudaGraphExec_t *x : {&e->exec, &e->loop_exec})
+        if (*x) cudaGraphExecDestroy(*x), *x = nullptr;
+    for (cudaGraph_t *g : {&e->graph, &e->loop_graph})
+        if (*g) cudaGraphDestroy(*g), *g = nullptr;
     return TQB200_OK;
 }
 

@@ -69,6 +69,8 @@ struct MvParams {
     int erows, nslots, n_experts;
     int xslots;
     Stamp stamp;  // in-graph timeline (off unless the engine records one)
+    const XWait *xw;  // tensor parallelism (device descriptors, XCHG instance only): x's
+    const XPut *xp;   // exchange before reading x; written rows also to every peer
 };
 
 // Pass index of a CTA's i-th pass (>= total when it has none).
@@ -243,7 +245,7 @@ template <int NW> struct DigitLayout { static constexpr int stride = 6 * NW + 4;
 constexpr int kI4Threads = 512;  // producer warp + 15 consumer warps, one CTA per SM
 constexpr int kI4MaxItems = 3;   // 8-column activation chunks per thread (K <= 12288)
 
-template <int SEG, bool STAMP>
+template <int SEG, bool STAMP, bool XCHG>
 __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_constant__ MvParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int NW = SEG / 8;
@@ -316,6 +318,9 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
             }
         }
     }
+    // x gathered from the peers (tensor parallelism): their rows have landed
+    if constexpr (XCHG)
+        if (P.xw) xwait(*P.xw, P.status);
     // this CTA's activation vector (slot mode: its block's own)
     const float *xsrc = P.x.src + (P.xslots ? (size_t)(blockIdx.x % P.nslots) * K : 0);
 
@@ -549,98 +554,112 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
         const uint32_t hdr_off = (uint32_t)g * GB;
         const uint32_t seg_off = hdr_off + 4u + (uint32_t)(sg - g * spg) * (SEG / 2);
         const int ncons = ncw * 32;
-        // the pass loop, compiled twice: with and without the fourth digit plane (the
-        // choice is uniform over the CTA, so each thread runs one straight-line version)
-        auto passes = [&](auto four_c) {
+        // this thread's rows of a full pass: slot, slot + S, ... below R (the same in every
+        // pass); row pointers and partial slots advance by fixed strides
+        const int my_rows = active ? (P.R - slot + S - 1) / S : 0;
+        const size_t rstride = (size_t)S * RB;
+        const int pstride = S * ntp;
+        // one row's segment partial from its bytes in the stage
+        auto seg_part = [&](const uint8_t *rp, auto four_c) -> float {
             constexpr bool kFour = decltype(four_c)::value;
+            const uint32_t hv = lds_u32(rp + hdr_off);
+            const float sc = h2f((uint16_t)(hv & 0xFFFFu));
+            const float zr = h2f((uint16_t)(hv >> 16));
+            // low nibbles as bytes, high nibbles as 16x bytes (one mask each, no shift): six
+            // independent accumulators, the high ones scaled back by 16
+            int L0 = 0, L1 = 0, L2 = 0, H0 = 0, H1 = 0, H2 = 0;
+            float dot3 = 0.0f;
+            if constexpr (!kFour) {
+#pragma unroll
+                for (int i = 0; i < NW; ++i) {
+                    const uint32_t wd = lds_u32(rp + seg_off + 4 * i);
+                    const uint32_t lo = wd & 0x0F0F0F0Fu, hi = wd & 0xF0F0F0F0u;
+                    L0 = dp4a_us(lo, xd[6 * i + 0], L0);
+                    H0 = dp4a_us(hi, xd[6 * i + 1], H0);
+                    L1 = dp4a_us(lo, xd[6 * i + 2], L1);
+                    H1 = dp4a_us(hi, xd[6 * i + 3], H1);
+                    L2 = dp4a_us(lo, xd[6 * i + 4], L2);
+                    H2 = dp4a_us(hi, xd[6 * i + 5], H2);
+                }
+            } else {  // outlier channels: the fourth digit plane from shared memory
+                int L3 = 0, H3 = 0;
+                const uint2 *x3 = dig3 + (size_t)sg * NW;
+#pragma unroll
+                for (int i = 0; i < NW; ++i) {
+                    const uint32_t wd = lds_u32(rp + seg_off + 4 * i);
+                    const uint32_t lo = wd & 0x0F0F0F0Fu, hi = wd & 0xF0F0F0F0u;
+                    const uint2 d3 = x3[i];
+                    L0 = dp4a_us(lo, xd[6 * i + 0], L0);
+                    H0 = dp4a_us(hi, xd[6 * i + 1], H0);
+                    L1 = dp4a_us(lo, xd[6 * i + 2], L1);
+                    H1 = dp4a_us(hi, xd[6 * i + 3], H1);
+                    L2 = dp4a_us(lo, xd[6 * i + 4], L2);
+                    H2 = dp4a_us(hi, xd[6 * i + 5], H2);
+                    L3 = dp4a_us(lo, d3.x, L3);
+                    H3 = dp4a_us(hi, d3.y, H3);
+                }
+                dot3 = (float)(L3 + (H3 >> 4)) * dsc3;
+            }
+            const int D0 = L0 + (H0 >> 4), D1 = L1 + (H1 >> 4), D2 = L2 + (H2 >> 4);
+            const float dot = fmaf((float)D0, dsc0, fmaf((float)D1, dsc1, fmaf((float)D2, dsc2, dot3)));
+            return sc * fmaf(-zr, X, dot);
+        };
+        // the pass loop, compiled twice: with and without the fourth digit plane (the
+        // choice is uniform over the CTA, so each thread runs one straight-line version).
+        // Per pass: stage s and its phase, and the consumer warp that reduces the pass's
+        // first chunk of 32 rows (chunk c goes to warp (first + c) mod ncw, so the
+        // reductions of consecutive passes spread over the warps), all advanced
+        // incrementally; the pass's job index only grows.
+        auto passes = [&](auto four_c) {
+            int s = 0, first = 0, j = 0;
+            uint32_t parity = 0;
             for (int i_pass = 0;; ++i_pass) {
                 const int p = pass_of(P, i_pass);
                 if (p >= total) break;
-                const int s = i_pass % P.stages;
-                const uint32_t parity = (uint32_t)(i_pass / P.stages) & 1u;
-                int j = 0;
                 while (j + 1 < P.n_jobs && p >= P.pass_begin[j + 1]) ++j;
                 const I4Job &job = P.job[j];
                 const int row0 = (p - P.pass_begin[j]) * P.R;
+                const int rows_here = min(P.R, job.rows - row0);  // a job's last pass may be short
                 float *rb = red + (size_t)(i_pass & 1) * red_n;  // double-buffered partials
                 // bias / residual of the rows this warp reduces (below), fetched before the
-                // weight wait; chunk c of 32 rows belongs to consumer warp (i_pass + c) % ncw
+                // weight wait
                 float pre_b0 = 0.0f, pre_b1 = 0.0f, pre_r0 = 0.0f, pre_r1 = 0.0f;
-                if (!P.pair) {
-                    for (int c = 0, k = 0; c * 32 < P.R && k < 2; ++c) {
-                        if ((i_pass + c) % ncw != cw) continue;
-                        const int rl = c * 32 + lane, row = row0 + rl;
-                        if (rl < P.R && row < job.rows) {
-                            const float b = job.bias ? job.bias[row] : 0.0f;
-                            const float r = job.resid ? job.resid[row] : 0.0f;
-                            if (k == 0) pre_b0 = b, pre_r0 = r;
-                            else pre_b1 = b, pre_r1 = r;
+                if (!P.pair && (job.bias || job.resid)) {
+                    for (int c = 0, k = 0, w = first; c * 32 < rows_here && k < 2; ++c) {
+                        if (w == cw) {
+                            const int row = row0 + c * 32 + lane;
+                            if (c * 32 + lane < rows_here) {
+                                const float b = job.bias ? job.bias[row] : 0.0f;
+                                const float r = job.resid ? job.resid[row] : 0.0f;
+                                if (k == 0) pre_b0 = b, pre_r0 = r;
+                                else pre_b1 = b, pre_r1 = r;
+                            }
+                            ++k;
                         }
-                        ++k;
+                        if (++w == ncw) w = 0;
                     }
                 }
                 const bool ok = mbar_wait(&full[s], parity, kWaitCycles);
-                const size_t half_bytes = P.stage_bytes / 2;
-                // one row's segment partial from the stage (0 past the matrix)
-                auto seg_part = [&](int jb, int rl) -> float {
-                    const uint8_t *sb = stage_base + (size_t)s * P.stage_bytes +
-                                        (jb ? half_bytes + s_head[kMaxStages + s] : s_head[s]);
-                    if (row0 + rl >= job.rows) return 0.0f;
-                    const uint8_t *rp = sb + (size_t)rl * RB;
-                    const uint32_t hv = lds_u32(rp + hdr_off);
-                    const float sc = h2f((uint16_t)(hv & 0xFFFFu));
-                    const float zr = h2f((uint16_t)(hv >> 16));
-                    // low nibbles as bytes, high nibbles as 16x bytes (one mask each, no
-                    // shift): six independent accumulators, the high ones scaled back by 16
-                    int L0 = 0, L1 = 0, L2 = 0, H0 = 0, H1 = 0, H2 = 0;
-                    float dot3 = 0.0f;
-                    if constexpr (!kFour) {
-#pragma unroll
-                        for (int i = 0; i < NW; ++i) {
-                            const uint32_t wd = lds_u32(rp + seg_off + 4 * i);
-                            const uint32_t lo = wd & 0x0F0F0F0Fu, hi = wd & 0xF0F0F0F0u;
-                            L0 = dp4a_us(lo, xd[6 * i + 0], L0);
-                            H0 = dp4a_us(hi, xd[6 * i + 1], H0);
-                            L1 = dp4a_us(lo, xd[6 * i + 2], L1);
-                            H1 = dp4a_us(hi, xd[6 * i + 3], H1);
-                            L2 = dp4a_us(lo, xd[6 * i + 4], L2);
-                            H2 = dp4a_us(hi, xd[6 * i + 5], H2);
-                        }
-                    } else {  // outlier channels: the fourth digit plane from shared memory
-                        int L3 = 0, H3 = 0;
-                        const uint2 *x3 = dig3 + (size_t)sg * NW;
-#pragma unroll
-                        for (int i = 0; i < NW; ++i) {
-                            const uint32_t wd = lds_u32(rp + seg_off + 4 * i);
-                            const uint32_t lo = wd & 0x0F0F0F0Fu, hi = wd & 0xF0F0F0F0u;
-                            const uint2 d3 = x3[i];
-                            L0 = dp4a_us(lo, xd[6 * i + 0], L0);
-                            H0 = dp4a_us(hi, xd[6 * i + 1], H0);
-                            L1 = dp4a_us(lo, xd[6 * i + 2], L1);
-                            H1 = dp4a_us(hi, xd[6 * i + 3], H1);
-                            L2 = dp4a_us(lo, xd[6 * i + 4], L2);
-                            H2 = dp4a_us(hi, xd[6 * i + 5], H2);
-                            L3 = dp4a_us(lo, d3.x, L3);
-                            H3 = dp4a_us(hi, d3.y, H3);
-                        }
-                        dot3 = (float)(L3 + (H3 >> 4)) * dsc3;
-                    }
-                    const int D0 = L0 + (H0 >> 4), D1 = L1 + (H1 >> 4), D2 = L2 + (H2 >> 4);
-                    const float dot = fmaf((float)D0, dsc0, fmaf((float)D1, dsc1, fmaf((float)D2, dsc2, dot3)));
-                    return sc * fmaf(-zr, X, dot);
-                };
                 if (active && ok) {
                     // rows slot, slot+S, ... of each job; two at a time for independent chains
+                    const int n = rows_here == P.R ? my_rows
+                                                   : (rows_here > slot ? (rows_here - slot + S - 1) / S : 0);
+                    const uint8_t *stage = stage_base + (size_t)s * P.stage_bytes;
                     for (int jb = 0; jb < np; ++jb) {
-                        for (int r = 0; r < P.RP; r += 2) {
-                            const int rl0 = slot + r * S, rl1 = rl0 + S;
-                            const bool h0 = rl0 < P.R, h1 = r + 1 < P.RP && rl1 < P.R;
-                            float p0 = 0.0f, p1 = 0.0f;
-                            if (h0) p0 = seg_part(jb, rl0);
-                            if (h1) p1 = seg_part(jb, rl1);
-                            if (h0) rb[(jb * P.R + rl0) * ntp + sg] = p0;
-                            if (h1) rb[(jb * P.R + rl1) * ntp + sg] = p1;
+                        const uint8_t *rp = stage + (jb ? P.stage_bytes / 2 + s_head[kMaxStages + s]
+                                                        : s_head[s]) +
+                                            (size_t)slot * RB;
+                        float *pp = rb + (size_t)(jb * P.R + slot) * ntp + sg;
+                        int r = 0;
+                        for (; r + 2 <= n; r += 2) {
+                            const float p0 = seg_part(rp, four_c);
+                            const float p1 = seg_part(rp + rstride, four_c);
+                            pp[0] = p0;
+                            pp[pstride] = p1;
+                            rp += 2 * rstride;
+                            pp += 2 * pstride;
                         }
+                        if (r < n) pp[0] = seg_part(rp, four_c);
                     }
                 }
                 __syncwarp();
@@ -651,14 +670,14 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
                     break;
                 }
                 // rows of this pass, 32 per warp (a lane per row): the row's segment partials
-                // summed by one lane.
-                // Chunk c of 32 rows goes to consumer warp (i_pass + c) % ncw, so the
-                // reductions of consecutive passes spread over the warps.
-                for (int c = 0, k = 0; c * 32 < P.R; ++c) {
-                    if ((i_pass + c) % ncw != cw) continue;
+                // summed by one lane
+                for (int c = 0, k = 0, w = first; c * 32 < rows_here; ++c) {
+                    const bool mine = w == cw;
+                    if (++w == ncw) w = 0;
+                    if (!mine) continue;
                     const int kk = k++;
                     const int rl = c * 32 + lane, row = row0 + rl;
-                    if (rl >= P.R || row >= job.rows) continue;
+                    if (rl >= rows_here) continue;
                     float v = row_sum(rb + (size_t)rl * ntp, nt);
                     if (P.pair) {
                         const float u = row_sum(rb + (size_t)(P.R + rl) * ntp, nt);
@@ -671,9 +690,16 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
                         if (job.resid) v = r_ + v;
                     }
                     if (P.eidx && P.eidx[row / P.erows] == -1) continue;  // another rank's expert
-                    job.y[row] = v;
+                    if constexpr (XCHG) {
+                        if (P.xp) xput_val(*P.xp, job.y + row, v);
+                        else job.y[row] = v;
+                    } else {
+                        job.y[row] = v;
+                    }
                     if (P.am.token && j == 0) better(bv, bi, v, row + P.am.row_offset);
                 }
+                if (++s == P.stages) s = 0, parity ^= 1u;
+                if (++first == ncw) first = 0;
             }
         };
         if (four)
@@ -712,12 +738,25 @@ __global__ void __launch_bounds__(kI4Threads, 1) i4_mv_tma_kernel(const __grid_c
                 better(bv, bi, __ldcg(P.am.part_v + b), __ldcg(P.am.part_i + b));
             block_argmax(bv, bi, s_bv, s_bi);
             if (t == 0) {
-                *P.am.token = bi == INT_MAX ? P.am.row_offset : bi;
-                if (P.am.value) *P.am.value = bv;
+                const int tok = bi == INT_MAX ? P.am.row_offset : bi;
+                if constexpr (XCHG) {
+                    if (P.xp) {
+                        xput_val(*P.xp, P.am.token, tok);
+                        if (P.am.value) xput_val(*P.xp, P.am.value, bv);
+                    } else {
+                        *P.am.token = tok;
+                        if (P.am.value) *P.am.value = bv;
+                    }
+                } else {
+                    *P.am.token = tok;
+                    if (P.am.value) *P.am.value = bv;
+                }
                 *P.am.ticket = 0u;
             }
         }
     }
+    if constexpr (XCHG)
+        if (P.xp) xput_arrive(*P.xp);
     stamp_exit<STAMP>(P.stamp, stamp_r);
 }
 
@@ -917,6 +956,13 @@ Shape plan(int K, int G, bool pair, bool norm, int rows_total, int r_div = 0) {
     } else {
         const size_t cap = 80 * 1024 / (RB * np);
         L.R = (int)std::max<size_t>(1, std::min<size_t>((per_cta + 2) / 3, cap));
+        // a multiple of the slots S: every consumer thread then has the same number of
+        // rows in a pass and no warp idles at the pass barrier (rounded up while a pass
+        // stays within the 80 KB, else down)
+        if (L.R > L.S) {
+            const int up = (L.R + L.S - 1) / L.S * L.S;
+            L.R = (size_t)up <= cap ? up : L.R / L.S * L.S;
+        }
     }
     if (r_div > 0) {  // passes must not straddle r_div-row blocks
         L.R = std::min(L.R, r_div);
@@ -952,10 +998,10 @@ int grid_for(Kern k, int block, size_t smem, int work) {
     return std::max(1, std::min(work, per_sm * num_sms()));
 }
 
-template <int SEG, bool STAMP>
+template <int SEG, bool STAMP, bool XCHG>
 int launch_tma(const MvParams &P, const Shape &L, int passes, bool pdl, cudaStream_t st,
                int grid_fixed = 0) {
-    auto k = i4_mv_tma_kernel<SEG, STAMP>;
+    auto k = i4_mv_tma_kernel<SEG, STAMP, XCHG>;
     static KernelSmem attr_set;
     int smem_max = 0;
     TQ_CUDA_TRY(smem_limit_once(k, attr_set, &smem_max));
@@ -1033,15 +1079,18 @@ int launch_i4_matvec_ex(const I4Job *jobs, int n_jobs, int in_dim, int group_siz
     P.n_experts = o.n_experts;
     P.xslots = o.xslots ? 1 : 0;
     P.stamp = o.stamp;
+    P.xw = o.xwait;
+    P.xp = o.put;
     const Shape L = plan(in_dim, group_size, pair, o.x.mode == X_RMSNORM, rows_total,
                          o.eidx ? o.erows : 0);
     bool aligned = true;  // the TMA path needs 16-byte aligned matrix bases
     for (int j = 0; j < n_jobs; ++j) aligned = aligned && ((uintptr_t)jobs[j].w % 16u == 0);
     const bool fast = (group_size % 32 == 0) && L.seg != 0 && aligned;
     if (!fast) {
-        TQ_CHECK_ARG(o.x.mode == X_PLAIN && !o.argmax.token && !pair && !o.eidx,
-                     "fused prologue/epilogue and expert mode need group_size %% 32 == 0 and "
-                     "aligned weights");
+        TQ_CHECK_ARG(o.x.mode == X_PLAIN && !o.argmax.token && !pair && !o.eidx && !o.put &&
+                         !o.xwait,
+                     "fused prologue/epilogue, expert mode and peer exchange need group_size "
+                     "%% 32 == 0 and aligned weights");
     }
     const int R = fast ? L.R : 1;
     int acc = 0;
@@ -1057,6 +1106,7 @@ int launch_i4_matvec_ex(const I4Job *jobs, int n_jobs, int in_dim, int group_siz
     P.x_bulk = (in_dim % 4 == 0) && a16(o.x.src) && (o.x.mode != X_RMSNORM || a16(o.x.norm_w)) &&
                (o.x.mode != X_SWIGLU || a16(o.x.up));
     TQ_CHECK_ARG(!o.xslots || P.x_bulk, "per-slot activations need 16-byte aligned rows of x");
+    TQ_CHECK_ARG(acc > 0 || !o.put, "peer exchange: a launch with no rows never arrives");
     if (acc == 0) return TQB200_OK;
     if (fast) {
         P.nt = L.nt;
@@ -1067,12 +1117,17 @@ int launch_i4_matvec_ex(const I4Job *jobs, int n_jobs, int in_dim, int group_siz
         P.stage_bytes = L.stage_bytes;
         // slot mode: a multiple of nslots CTAs, every block served by the same count
         const int grid = o.xslots ? o.nslots * std::max(1, num_sms() / o.nslots) : 0;
-        const bool st = P.stamp.base != nullptr;
-        if (L.seg == 64)
-            return st ? launch_tma<64, true>(P, L, acc, o.pdl, stream, grid)
-                      : launch_tma<64, false>(P, L, acc, o.pdl, stream, grid);
-        return st ? launch_tma<32, true>(P, L, acc, o.pdl, stream, grid)
-                  : launch_tma<32, false>(P, L, acc, o.pdl, stream, grid);
+        const int mode = (P.stamp.base != nullptr ? 1 : 0) | (P.xw || P.xp ? 2 : 0);
+#define TQ_I4_LAUNCH(SEGV)                                                              \
+    switch (mode) {                                                                    \
+        case 0: return launch_tma<SEGV, false, false>(P, L, acc, o.pdl, stream, grid); \
+        case 1: return launch_tma<SEGV, true, false>(P, L, acc, o.pdl, stream, grid);  \
+        case 2: return launch_tma<SEGV, false, true>(P, L, acc, o.pdl, stream, grid);  \
+        default: return launch_tma<SEGV, true, true>(P, L, acc, o.pdl, stream, grid); \
+    }
+        if (L.seg == 64) TQ_I4_LAUNCH(64)
+        TQ_I4_LAUNCH(32)
+#undef TQ_I4_LAUNCH
     }
     const int grid = std::max(1, std::min((acc + 7) / 8, num_sms() * 8));
     i4_matvec_generic_kernel<<<grid, 256, 0, stream>>>(P);

@@ -79,6 +79,93 @@ __device__ __forceinline__ void stamp_exit(const Stamp &s, const StampRegs &r) {
 }
 #endif
 
+// ------------------------------------------------------------------ peer exchange
+// Tensor-parallel all-gather fused into the kernel that produces the rows (one process
+// per GPU; every rank's exchange arena has the same layout and is mapped into every
+// other rank's address space).  The producer stores each of its output rows into its
+// own buffer and, at the same offset, into every peer's (NVLink stores); each CTA then
+// fences (system scope) and takes a ticket, and the launch's last CTA adds 1 to the
+// exchange's arrival counter on every rank (a system-scope release).  A consumer waits,
+// after its dependency wait and before reading the buffer, until its own counter reaches
+// epoch x ranks (one thread of each CTA polls with an acquire load, bounded in time).
+// The counters only grow: epoch counts decode steps (the embed kernel advances it), so
+// no counter is ever reset while a peer may still add to it.
+constexpr int kMaxPeers = 7;  // up to 8 ranks
+struct XPut {
+    int n_peers = 0;
+    long long delta[kMaxPeers] = {};       // peer arena address minus local (bytes)
+    unsigned long long *arrive = nullptr;  // local address of this exchange's counter
+    unsigned int *ticket = nullptr;        // local CTA-completion ticket of this exchange
+};
+struct XWait {
+    const unsigned long long *arrive = nullptr;  // this rank's counter of the exchange
+    const unsigned int *epoch = nullptr;         // decode steps so far (device)
+    unsigned int ranks = 0;                      // arrivals per step
+};
+
+#if defined(__CUDACC__)
+constexpr unsigned long long kXWaitNs = 20000000000ull;  // 20 s: ranks may start apart
+
+// Stores v at p and at p's offset in every peer's arena.
+template <typename T>
+__device__ __forceinline__ void xput_val(const XPut &x, T *p, T v) {
+    *p = v;
+    for (int i = 0; i < x.n_peers; ++i)
+        *reinterpret_cast<T *>(reinterpret_cast<char *>(p) + x.delta[i]) = v;
+}
+// Called by every thread of the CTA after its last store of exchanged rows.
+__device__ __forceinline__ void xput_arrive(const XPut &x) {
+    if (!x.arrive) return;
+    __syncthreads();
+    if (threadIdx.x == 0 && threadIdx.y == 0 && threadIdx.z == 0) {
+        __threadfence_system();  // this CTA's stores, local and remote, before its ticket
+        const unsigned int n = gridDim.x * gridDim.y * gridDim.z;
+        if ((atomicAdd(x.ticket, 1u) + 1u) % n == 0u) {  // the launch's last CTA
+            __threadfence_system();
+            asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(x.arrive) : "memory");
+            for (int i = 0; i < x.n_peers; ++i) {
+                unsigned long long *a = reinterpret_cast<unsigned long long *>(
+                    reinterpret_cast<char *>(x.arrive) + x.delta[i]);
+                asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(a) : "memory");
+            }
+        }
+    }
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+// Called by every thread of the CTA; thread 0 polls.  false (and *status set) when the
+// peers' rows did not arrive within kXWaitNs or another wait already failed.
+__device__ __forceinline__ bool xwait(const XWait &w, int *status) {
+    __shared__ int s_xok;
+    if (!w.arrive) return true;
+    if (threadIdx.x == 0 && threadIdx.y == 0 && threadIdx.z == 0) {
+        const unsigned long long need =
+            (unsigned long long)__ldcg(reinterpret_cast<const unsigned int *>(w.epoch)) * w.ranks;
+        int ok = 1;
+        if (ld_acquire_sys_u64(w.arrive) < need) {
+            const unsigned long long t0 = global_timer_ns();
+            for (unsigned int it = 1;; ++it) {
+                if (ld_acquire_sys_u64(w.arrive) >= need) break;
+                if ((it & 63u) == 0u &&
+                    (global_timer_ns() - t0 > kXWaitNs || it > (1u << 30) ||
+                     (status && *(volatile int *)status != 0))) {
+                    ok = 0;
+                    break;
+                }
+                __nanosleep(100);
+            }
+        }
+        if (!ok && status) atomicCAS(status, 0, kDevTimeoutPeer);
+        s_xok = ok;
+    }
+    __syncthreads();
+    return s_xok != 0;
+}
+#endif
+
 // ------------------------------------------------------------------ i4
 // One matrix of a fused i4 matvec launch.  All jobs share x, in_dim and group.
 struct I4Job {
@@ -128,6 +215,12 @@ struct I4LaunchOpts {
     // per-block activations (one plain job): block b uses x.src + b * in_dim
     bool xslots = false;
     Stamp stamp;                    // in-graph timeline (TMA kernel only)
+    // tensor parallelism over peer memory (TMA kernel only; DEVICE descriptors, so the
+    // single-GPU kernel instance carries neither their parameters nor their code): wait
+    // for x's exchange before reading it; store the written rows (and the argmax pair)
+    // into every peer
+    const XWait *xwait = nullptr;
+    const XPut *put = nullptr;
 };
 
 // y_j = W_j x (+bias_j / +resid_j) for up to 3 jobs in one launch (q/k/v, gate/up, ...).
@@ -310,6 +403,8 @@ struct AttnArgs {
     bool pdl = false;         // programmatic dependent launch (TMA kernel only)
     int *status = nullptr;    // device error word (bounded waits, bad position)
     Stamp stamp;              // in-graph timeline (TMA kernel only)
+    const XPut *put = nullptr;  // tensor parallelism (device descriptor): out rows also go
+                                // to every peer (TMA kernel only)
 };
 int attn_plan(int n_kv_heads, int max_seq, int *nsplit, int *chunk_max);
 size_t attn_partial_floats(int n_heads, int head_dim, int nsplit);
@@ -327,7 +422,8 @@ struct ArgPair {
     float v;
     int i;
 };
-int launch_argmax_pairs(const ArgPair *pairs, int n, int *out, cudaStream_t st);
+int launch_argmax_pairs(const ArgPair *pairs, int n, int *out, cudaStream_t st,
+                        const XWait &xw = XWait(), int *status = nullptr);
 int argmax_blocks(int n);
 int launch_argmax(const float *l, int n, float *pv, int *pi, unsigned int *ticket, int *out,
                   cudaStream_t st);
@@ -336,13 +432,17 @@ int launch_topk_softmax(const float *logits, int n, int k, int *idx, float *w, c
 // device word, reset by the kernel); and h += sum_t wts[t] * o[t] in router order.
 int launch_moe_router(const float *h, const float *norm_w, float eps, int H, const float *W, int E,
                       int k, float *logits, int *idx, float *wts, unsigned int *ticket, bool pdl,
-                      cudaStream_t st, const Stamp &stamp = Stamp());
+                      cudaStream_t st, const Stamp &stamp = Stamp(), const XWait &xw = XWait(),
+                      int *status = nullptr);
 int launch_moe_combine(float *h, const float *o, const float *wts, int k, int H, bool pdl,
-                       cudaStream_t st, const Stamp &stamp = Stamp());
+                       cudaStream_t st, const Stamp &stamp = Stamp(), const XWait &xw = XWait(),
+                       int *status = nullptr);
+// epoch (optional): advanced by one, the decode step count of the peer exchanges
 int launch_embed(const void *table, int dtype, const int *token, int dim, int group_size,
-                 float *out, cudaStream_t st, int n_tokens = 1);
+                 float *out, cudaStream_t st, int n_tokens = 1, unsigned int *epoch = nullptr);
 // Expert parallelism: local[j] = idx[j] - e0 when this rank owns that expert, else -1;
-// o[0 .. k*H) = 0 (the cross-rank sum of the slots then equals each owner's output).
+// o[0 .. k*H) = 0 when o is given (the cross-rank sum of the slots then equals each
+// owner's output; the peer exchange, where each owner stores its slots, passes none).
 int launch_moe_ep_local(const int *idx, int k, int e0, int e_local, int *local, float *o, int H,
                         bool pdl, cudaStream_t st);
 // MoE prefill: router logits of n tokens (f32 router, xn normalised rows), top-k softmax

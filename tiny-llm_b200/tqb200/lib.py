@@ -83,6 +83,8 @@ PROTOTYPES = {
     "tqb200_engine_profile_prefill": ([_vp, _i32, _i, _f, _i, C.POINTER(_i)], _i),
     "tqb200_engine_profile_step": ([_vp, _i, _f, _i, C.POINTER(_i)], _i),
     "tqb200_engine_set_timeline": ([_vp, _i], _i),
+    "tqb200_engine_exchange_handle": ([_vp, _vp], _i),
+    "tqb200_engine_open_exchange": ([_vp, _vp, _i], _i),
     "tqb200_l2norm_inplace": ([_f, _i, _fl], _i),
     "tqb200_causal_conv1d_update": ([_f, _f, _f, _f, _i, _i], _i),
     "tqb200_gdn_step": ([_f, _f, _f, _f, _fl, _fl, _f, _i, _i], _i),
@@ -443,6 +445,20 @@ class Engine:
         nxt = C.c_int(-1)
         _check(load().tqb200_engine_profile_step(self.h, int(token), ms, ms.size, C.byref(nxt)))
         return nxt.value, dict(zip(self.KINDS, ms.tolist()))
+
+    def exchange_handle(self) -> bytes:
+        """This rank's activation arena as a 64-byte CUDA IPC handle (peer exchange)."""
+        buf = (C.c_ubyte * 64)()
+        _check(load().tqb200_engine_exchange_handle(self.h, buf))
+        return bytes(buf)
+
+    def open_exchange(self, handles):
+        """Maps every other rank's arena (handles[r] = rank r's exchange_handle()); from the
+        next step on the all-gathers run inside the producing kernels over NVLink."""
+        blob = b"".join(handles)
+        assert len(blob) == 64 * len(handles)
+        buf = (C.c_ubyte * len(blob)).from_buffer_copy(blob)
+        _check(load().tqb200_engine_open_exchange(self.h, buf, len(handles)))
 
     def set_timeline(self, max_steps: int):
         """Stamp every launch of the first max_steps steps of each generate() (0: off)."""
