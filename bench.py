@@ -200,8 +200,9 @@ def ref_matvec_rate(seconds: float, threads: int):
 
 
 # ------------------------------------------------------------------ workloads
-def matvec_graph_rate(tq, weights, x, M, K, G, reps: int, warmup: int):
-    """Device time of one tqb200_dev_matvec_i4 launch: a CUDA graph of one launch per
+def matvec_graph_rate(tq, weights, x, M, K, G, reps: int, warmup: int, pdl: bool = True):
+    """Device time of one tqb200_dev_matvec_i4_pdl launch (tqb200_dev_matvec_i4 with
+    pdl=False: fully serialised launches): a CUDA graph of one launch per
     weight copy in `weights` (device tensors; together larger than L2, so every launch
     streams its matrix from HBM), replayed `reps` times between CUDA events on the
     launching stream.  Returns (us per launch, algorithmic GB/s, launches timed)."""
@@ -213,9 +214,11 @@ def matvec_graph_rate(tq, weights, x, M, K, G, reps: int, warmup: int):
     stream = torch.cuda.Stream()
     sp = stream.cuda_stream
 
+    entry = tq.tqb200_dev_matvec_i4_pdl if pdl else tq.tqb200_dev_matvec_i4
+
     def launch_all():
         for wi in weights:
-            st = tq.tqb200_dev_matvec_i4(wi.data_ptr(), dx.data_ptr(), dy.data_ptr(), M, K, G, sp)
+            st = entry(wi.data_ptr(), dx.data_ptr(), dy.data_ptr(), M, K, G, sp)
             if st:
                 raise lib.TQB200Error(st, tq.tqb200_last_error().decode())
 
@@ -281,13 +284,17 @@ def matvec_extras(pk, warmup: int) -> dict:
         torch.from_numpy(synth.random_i4(rng, 4864, 896, 64) if i < 4 else w).to(dev)
         for i in range(1, 64)]
     us, gbs, n = matvec_graph_rate(tq, ws, x, 4864, 896, 64, 20, max(3, warmup))
+    us_s, gbs_s, _ = matvec_graph_rate(tq, ws, x, 4864, 896, 64, 20, max(3, warmup), pdl=False)
     out["matvec_config1"] = {
         "shape": "4864x896 g64", "GB_per_s": round(gbs, 1), "us_per_launch": round(us, 3),
         "frac_of_hbm": round(gbs / pk["hbm_gbs"], 4), "launches_timed": n,
+        "serialised_GB_per_s": round(gbs_s, 1), "serialised_us_per_launch": round(us_s, 3),
         "single_call_us": round(matvec_single_call_us(tq, ws, x, 4864, 896, 64), 3),
-        "how": "CUDA graph of 64 launches over 64 distinct copies of W (157 MB > L2), "
-               "CUDA events around 20 replays; single_call_us = median event time of one "
-               "launch by itself"}
+        "how": "CUDA graph of 64 tqb200_dev_matvec_i4_pdl launches over 64 distinct copies "
+               "of W (157 MB > L2; each launch may read its weights while the previous "
+               "finishes), CUDA events around 20 replays; serialised_*: the same with "
+               "tqb200_dev_matvec_i4; single_call_us = median event time of one launch by "
+               "itself"}
     del ws
     M, K = 151936, 2560
     ws = [torch.from_numpy(synth.random_i4_fast(rng, M, K, 64)).to(dev) for _ in range(2)]
@@ -327,40 +334,49 @@ def bench_matvec(args, rank, pg, pk, pk_kind):
     stream = torch.cuda.Stream()
     sp = stream.cuda_stream
 
-    def launch_all():
-        for wi in ws:
-            st = tq.tqb200_dev_matvec_i4(wi.data_ptr(), dx.data_ptr(), dy.data_ptr(), M, K, G, sp)
-            if st:
-                raise lib.TQB200Error(st, tq.tqb200_last_error().decode())
+    def graph_ms(entry):
+        """Device ms of one replay of a graph of NCOPY launches of `entry`, over args.steps
+        replays (clocks sampled during the timed replays)."""
+        def launch_all():
+            for wi in ws:
+                st = entry(wi.data_ptr(), dx.data_ptr(), dy.data_ptr(), M, K, G, sp)
+                if st:
+                    raise lib.TQB200Error(st, tq.tqb200_last_error().decode())
 
-    with torch.cuda.stream(stream):
-        launch_all()
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        launch_all()
-    torch.cuda.synchronize()
-    for _ in range(args.warmup):
-        graph.replay()
-    torch.cuda.synchronize()
-    clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
-    clocks.start()
-    barrier(pg)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        e0.record(stream)
-        for _ in range(args.steps):
+        with torch.cuda.stream(stream):
+            launch_all()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            launch_all()
+        torch.cuda.synchronize()
+        for _ in range(args.warmup):
             graph.replay()
-        e1.record(stream)
-    torch.cuda.synchronize()
-    barrier(pg)
-    ms = e0.elapsed_time(e1)
-    clk = clocks.stop()
-    ms = max_over_ranks(pg, ms)
-    ms_step = ms / args.steps
+        torch.cuda.synchronize()
+        clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
+        clocks.start()
+        barrier(pg)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        barrier(pg)
+        ms = e0.elapsed_time(e1)
+        clk = clocks.stop()
+        del graph
+        return max_over_ranks(pg, ms) / args.steps, clk
+
+    # each launch with programmatic dependent launch (its weight loads start while the
+    # previous launch finishes, as in a decode step), and each fully serialised
+    ms_step, clk = graph_ms(tq.tqb200_dev_matvec_i4_pdl)
+    ms_plain, _ = graph_ms(tq.tqb200_dev_matvec_i4)
     per_launch_s = ms_step / 1e3 / NCOPY
     achieved = algo_bytes / per_launch_s / 1e9
+    plain_gbs = algo_bytes / (ms_plain / 1e3 / NCOPY) / 1e9
     world = int(os.environ.get("WORLD_SIZE", "1"))
     value = achieved * world  # replicas: every rank streams its own copies
 
@@ -395,8 +411,14 @@ def bench_matvec(args, rank, pg, pk, pk_kind):
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
                      "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
                      "traffic": None, "peak_source": pk_kind,
-                     "kernel": "i4_mv_tma_kernel<64>",
-                     "algorithmic_bytes_per_launch": int(algo_bytes)},
+                     "kernel": ("i4_mv_direct_kernel" if K <= 1800 and w.nbytes <= (8 << 20)
+                                else "i4_mv_tma_kernel<64>"),
+                     "algorithmic_bytes_per_launch": int(algo_bytes),
+                     "how": "a CUDA graph of one tqb200_dev_matvec_i4_pdl launch per distinct "
+                            "weight copy (each launch may read its weights while the previous "
+                            "finishes; x and y after it), CUDA events around the replays"},
+        "serialised": {"value": round(plain_gbs * world, 2), "unit": "GB/s",
+                       "how": "the same graph of tqb200_dev_matvec_i4 launches (no overlap)"},
         "clocks": clk,
         "gpu_launches": NCOPY * args.steps,
         "e2e": e2e,

@@ -78,6 +78,14 @@ int tqb200_dev_matvec_i4(const uint8_t *w, const float *x, float *y, int out_dim
                          int group_size, void *stream);
 int tqb200_dev_matvec_i4_sym(const uint8_t *w, const float *x, float *y, int out_dim,
                              int in_dim, int group_size, void *stream);
+/* tqb200_dev_matvec_i4 launched with programmatic dependent launch (no reference
+ * counterpart): the kernel may start while the preceding kernel on the stream still runs
+ * and read W then (its first weight loads overlap that kernel's tail, as the engine's
+ * matvecs do); x is read, and y written, only after that kernel has completed.  For
+ * weights that the preceding kernel does not write, such as the reference's immutable
+ * model tensors. */
+int tqb200_dev_matvec_i4_pdl(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim,
+                             int group_size, void *stream);
 int tqb200_dev_dequant_i4(const uint8_t *w, int rows, int dim, int group_size, float *out,
                           void *stream);
 

@@ -153,3 +153,51 @@ def test_device_pointer_path(tq, oracle):
     tq.dev_matvec_i4(dw.data_ptr(), dx.data_ptr(), dy.data_ptr(), M, K, G)
     torch.cuda.synchronize()
     assert max_rel(dy.cpu().numpy(), oracle.matvec_i4(w, x, M, K, G)) < TOL
+
+
+@pytest.mark.parametrize("M,K", [(4864, 896), (2048, 2560)])
+def test_pdl_launch_after_producer(tq, oracle, M, K):
+    """tqb200_dev_matvec_i4_pdl right after a kernel that writes x: the matvec may start
+    early and read its weights, but must read the x that kernel wrote (small rows: the
+    direct kernel; K = 2560: the TMA kernel)."""
+    import torch
+    from tqb200 import lib
+    rng = np.random.default_rng(M + K)
+    G = 64
+    w = synth.random_i4(rng, M, K, G)
+    x = rng.normal(size=K).astype(np.float32)
+    dw = torch.from_numpy(w).cuda()
+    src = torch.from_numpy(x).cuda()
+    dx = torch.zeros(K, device="cuda", dtype=torch.float32)
+    dy = torch.empty(M, device="cuda", dtype=torch.float32)
+    s = torch.cuda.current_stream()
+    for _ in range(2):
+        dx.zero_()
+        torch.cuda.synchronize()
+        dx.copy_(src * 1.0)  # a kernel on the stream that produces x
+        st = lib.load().tqb200_dev_matvec_i4_pdl(dw.data_ptr(), dx.data_ptr(), dy.data_ptr(), M,
+                                                 K, G, s.cuda_stream)
+        assert st == 0
+        torch.cuda.synchronize()
+        assert max_rel(dy.cpu().numpy(), oracle.matvec_i4(w, x, M, K, G)) < TOL
+
+
+@pytest.mark.parametrize("K", [64, 896, 1792])
+def test_direct_kernel_shapes_and_jobs(tq, oracle, K):
+    """The small-row kernel over its row-width range (K = 1792: 252 words per row) for
+    one, paired and q/k/v launches, against the oracle."""
+    rng = np.random.default_rng(K)
+    G = 64
+    M = 333
+    w1, w2, w3 = (synth.random_i4(rng, M, K, G) for _ in range(3))
+    x = rng.normal(size=K).astype(np.float32)
+    assert max_rel(tq.matvec_i4(w1, x, M, K, G), oracle.matvec_i4(w1, x, M, K, G)) < TOL
+    y1, y2 = tq.matvec_pair_i4(w1, w2, x, M, K, G)
+    assert max_rel(y1, oracle.matvec_i4(w1, x, M, K, G)) < TOL
+    assert max_rel(y2, oracle.matvec_i4(w2, x, M, K, G)) < TOL
+    wk = synth.random_i4(rng, 77, K, G)
+    wv = synth.random_i4(rng, 77, K, G)
+    q, k, v = tq.matvec_qkv_i4(w1, wk, wv, x, M, 77, K, G)
+    assert max_rel(q, oracle.matvec_i4(w1, x, M, K, G)) < TOL
+    assert max_rel(k, oracle.matvec_i4(wk, x, 77, K, G)) < TOL
+    assert max_rel(v, oracle.matvec_i4(wv, x, 77, K, G)) < TOL

@@ -290,6 +290,18 @@ int tqb200_dev_matvec_i4(const uint8_t *w, const float *x, float *y, int out_dim
     return launch_i4_matvec(&j, 1, x, in_dim, group_size, (cudaStream_t)stream);
 }
 
+int tqb200_dev_matvec_i4_pdl(const uint8_t *w, const float *x, float *y, int out_dim, int in_dim,
+                             int group_size, void *stream) {
+    TQ_TRY(check_i4(out_dim, in_dim, group_size));
+    TQ_CHECK_ARG(w && x && y, "null pointer");
+    I4Job j{w, y, nullptr, nullptr, out_dim};
+    I4LaunchOpts o;
+    o.x.mode = X_PLAIN;
+    o.x.src = x;
+    o.pdl = true;  // W may be read before the preceding kernel completes; x only after
+    return launch_i4_matvec_ex(&j, 1, in_dim, group_size, o, (cudaStream_t)stream);
+}
+
 int tqb200_dev_matvec_i4_sym(const uint8_t *w, const float *x, float *y, int out_dim,
                              int in_dim, int group_size, void *stream) {
     TQ_TRY(check_i4(out_dim, in_dim, group_size));

@@ -48,6 +48,7 @@ PROTOTYPES = {
     "tqb200_matvec_i4_sym": ([_u8, _f, _f, _i, _i, _i], _i),
     "tqb200_dequant_i4": ([_u8, _i, _i, _i, _f], _i),
     "tqb200_dev_matvec_i4": ([_vp, _vp, _vp, _i, _i, _i, _vp], _i),
+    "tqb200_dev_matvec_i4_pdl": ([_vp, _vp, _vp, _i, _i, _i, _vp], _i),
     "tqb200_dev_matvec_i4_sym": ([_vp, _vp, _vp, _i, _i, _i, _vp], _i),
     "tqb200_dev_dequant_i4": ([_vp, _i, _i, _i, _vp, _vp], _i),
     "tqb200_matmul_i4": ([_u8, _f, _f, _i, _i, _i, _i], _i),
