@@ -411,8 +411,7 @@ def bench_matvec(args, rank, pg, pk, pk_kind):
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
                      "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
                      "traffic": None, "peak_source": pk_kind,
-                     "kernel": ("i4_mv_direct_kernel" if K <= 1800 and w.nbytes <= (8 << 20)
-                                else "i4_mv_tma_kernel<64>"),
+                     "kernel": "i4_mv_tma_kernel<64>",
                      "algorithmic_bytes_per_launch": int(algo_bytes),
                      "how": "a CUDA graph of one tqb200_dev_matvec_i4_pdl launch per distinct "
                             "weight copy (each launch may read its weights while the previous "

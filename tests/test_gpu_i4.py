@@ -158,8 +158,7 @@ def test_device_pointer_path(tq, oracle):
 @pytest.mark.parametrize("M,K", [(4864, 896), (2048, 2560)])
 def test_pdl_launch_after_producer(tq, oracle, M, K):
     """tqb200_dev_matvec_i4_pdl right after a kernel that writes x: the matvec may start
-    early and read its weights, but must read the x that kernel wrote (small rows: the
-    direct kernel; K = 2560: the TMA kernel)."""
+    early and read its weights, but must read the x that kernel wrote."""
     import torch
     from tqb200 import lib
     rng = np.random.default_rng(M + K)
@@ -183,9 +182,9 @@ def test_pdl_launch_after_producer(tq, oracle, M, K):
 
 
 @pytest.mark.parametrize("K", [64, 896, 1792])
-def test_direct_kernel_shapes_and_jobs(tq, oracle, K):
-    """The small-row kernel over its row-width range (K = 1792: 252 words per row) for
-    one, paired and q/k/v launches, against the oracle."""
+def test_small_rows_single_pair_qkv(tq, oracle, K):
+    """Short rows (one to 28 groups) in single, paired and q/k/v launches, against the
+    oracle."""
     rng = np.random.default_rng(K)
     G = 64
     M = 333

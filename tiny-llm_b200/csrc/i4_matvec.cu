@@ -920,155 +920,6 @@ __global__ void i4_dequant_kernel(const uint8_t *__restrict__ w, int rows, int d
 }
 
 int g_num_sms = 0;
-// ------------------------------------------------------------------ direct kernel
-// Small-row matvecs (a row of at most 8 x 32 words: K <= ~1800 at G = 64) without the
-// TMA ring and the digit-plane prologue: a warp owns RW rows (of each of np jobs), lane l
-// the row's 32-bit words l, l + 32, ...  The words are loaded into registers before the
-// dependency wait (weights do not depend on the previous kernel, so under PDL they
-// arrive while it finishes); after it, x (RMSNorm applied in the reference's rounding
-// order, as the TMA kernel's prologue does) and its 8-column sums go to shared memory,
-// and each code word contributes s (sum_k q_k x_k - z X8) in fp32, s and z read from
-// the group's header word (an L1 hit: the warp loaded the row's line), then one warp sum
-// per row.  Its fixed cost is one x load and two block barriers, against the TMA kernel's
-// activation prologue and ring set-up, which dominate a matrix of a few MB.
-struct DirectParams {
-    I4Job job[3];
-    int row_end[3];  // cumulative rows of the jobs (pair: job 0's rows, shared with job 1)
-    int n_jobs;
-    int K, G, WG, WPR;  // in_dim, group size, words per group, words per row
-    size_t RB;          // bytes per row
-    int pair;           // y0 = silu(W0 x) * (W1 x)
-    XSource x;
-    Stamp stamp;
-};
-
-constexpr int kDirectThreads = 256;
-constexpr int kDirectWarps = kDirectThreads / 32;
-constexpr int kDirectMaxWords = 8 * 32;  // words per row the register prefetch covers
-
-template <int WPL, int RW, int NP, bool STAMP>
-__global__ void __launch_bounds__(kDirectThreads) i4_mv_direct_kernel(const __grid_constant__ DirectParams P) {
-    extern __shared__ __align__(16) float s_x[];  // [KP] x, then [KP / 8] 8-column sums
-    __shared__ double s_rd[kDirectWarps];
-    StampRegs stamp_r;
-    stamp_enter<STAMP>(P.stamp, stamp_r);
-    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    const int total = P.row_end[P.n_jobs - 1];
-    const int row_base = (blockIdx.x * kDirectWarps + warp) * RW;
-    // the row's job and its local row (pair mode: job jb of the same row)
-    auto row_ptr = [&](int row, int jb, int *j_out, int *lr_out) -> const uint8_t * {
-        int j = 0;
-        while (j + 1 < P.n_jobs && row >= P.row_end[j]) ++j;
-        if (NP == 2) j = jb;
-        const int lr = row - (NP == 2 ? 0 : (j ? P.row_end[j - 1] : 0));
-        *j_out = j;
-        *lr_out = lr;
-        return P.job[j].w + (size_t)lr * P.RB;
-    };
-    uint32_t wr[NP][RW][WPL];
-#pragma unroll
-    for (int jb = 0; jb < NP; ++jb)
-#pragma unroll
-        for (int r = 0; r < RW; ++r) {
-            const int row = row_base + r;
-            int j, lr;
-            const unsigned int *rp =
-                row < total ? reinterpret_cast<const unsigned int *>(row_ptr(row, jb, &j, &lr)) : nullptr;
-#pragma unroll
-            for (int i = 0; i < WPL; ++i) {
-                const int wi = lane + 32 * i;
-                wr[jb][r][i] = (rp && wi < P.WPR) ? __ldg(rp + wi) : 0u;
-            }
-        }
-    stamp_step<STAMP>(P.stamp, stamp_r);
-    griddep_wait();
-    stamp_waited<STAMP>(P.stamp, stamp_r);
-    griddep_launch();
-    const int K = P.K, G = P.G, WG = P.WG;
-    const int KP = (P.WPR / WG) * G;
-    float *xs8 = s_x + KP;
-    const bool norm = P.x.mode == X_RMSNORM;
-    double ss = 0.0;
-    for (int i = t; i < KP; i += kDirectThreads) {
-        const float v = i < K ? P.x.src[i] : 0.0f;
-        s_x[i] = v;
-        if (norm) ss += (double)v * (double)v;
-    }
-    if (norm) {  // rmsnorm_ref: the sum of squares in double, y = (x * scale) * w
-        ss = warp_sum_d(ss);
-        if (lane == 0) s_rd[warp] = ss;
-        __syncthreads();
-        double tot = lane < kDirectWarps ? s_rd[lane] : 0.0;
-        tot = warp_sum_d(tot);
-        const float mean_sq = (float)(tot / K);
-        const float scale = 1.0f / sqrtf(__fadd_rn(mean_sq, P.x.eps));
-        for (int i = t; i < K; i += kDirectThreads)
-            s_x[i] = __fmul_rn(__fmul_rn(s_x[i], scale), P.x.norm_w[i]);
-    }
-    __syncthreads();
-    for (int c = t; c < KP / 8; c += kDirectThreads) {
-        const float *v = s_x + 8 * c;
-        xs8[c] = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
-    }
-    __syncthreads();
-    // this lane's words: group and position within the group (the same in every row)
-    int gi[WPL], pi[WPL];
-#pragma unroll
-    for (int i = 0; i < WPL; ++i) {
-        const int wi = lane + 32 * i;
-        gi[i] = wi / WG;
-        pi[i] = wi < P.WPR ? wi - gi[i] * WG : 0;  // 0: header word or none
-    }
-#pragma unroll
-    for (int r = 0; r < RW; ++r) {
-        const int row = row_base + r;
-        if (row >= total) break;  // uniform over the warp
-        float res[NP];
-        int j = 0, lr = 0;
-#pragma unroll
-        for (int jb = 0; jb < NP; ++jb) {
-            const unsigned int *rp = reinterpret_cast<const unsigned int *>(row_ptr(row, jb, &j, &lr));
-            float acc = 0.0f;
-#pragma unroll
-            for (int i = 0; i < WPL; ++i) {
-                if (pi[i] == 0) continue;
-                const uint32_t wd = wr[jb][r][i];
-                const uint32_t hv = __ldg(rp + gi[i] * WG);
-                const float sc = h2f((uint16_t)(hv & 0xFFFFu));
-                const float z = h2f((uint16_t)(hv >> 16));
-                const int c0 = gi[i] * G + 8 * (pi[i] - 1);
-                const float4 xa = *reinterpret_cast<const float4 *>(s_x + c0);
-                const float4 xb = *reinterpret_cast<const float4 *>(s_x + c0 + 4);
-                float a0 = (float)(wd & 15u) * xa.x, a1 = (float)((wd >> 4) & 15u) * xa.y;
-                a0 = fmaf((float)((wd >> 8) & 15u), xa.z, a0);
-                a1 = fmaf((float)((wd >> 12) & 15u), xa.w, a1);
-                a0 = fmaf((float)((wd >> 16) & 15u), xb.x, a0);
-                a1 = fmaf((float)((wd >> 20) & 15u), xb.y, a1);
-                a0 = fmaf((float)((wd >> 24) & 15u), xb.z, a0);
-                a1 = fmaf((float)(wd >> 28), xb.w, a1);
-                acc = fmaf(sc, fmaf(-z, xs8[c0 >> 3], a0 + a1), acc);
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-            res[jb] = acc;
-        }
-        if (lane == 0) {
-            float v = res[0];
-            if constexpr (NP == 2) {
-                // swiglu_ref (kernels/silu/swiglu_ref.cpp:41-52) on (gate, up)
-                v = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), res[NP - 1]);
-                P.job[0].y[lr] = v;
-            } else {
-                const I4Job &job = P.job[j];
-                if (job.bias) v += job.bias[lr];
-                if (job.resid) v = job.resid[lr] + v;
-                job.y[lr] = v;
-            }
-        }
-    }
-    stamp_exit<STAMP>(P.stamp, stamp_r);
-}
-
 struct Shape {
     int seg = 0, nt = 0, S = 0, RP = 0, R = 0, block = 0, stages = 0;
     uint32_t stage_bytes = 0;
@@ -1192,75 +1043,6 @@ int i4_argmax_slots(int rows, int in_dim, int group_size) {
     return 8 * num_sms();  // >= any grid the launcher picks (<= per_sm * SMs, per_sm <= 8)
 }
 
-// The direct kernel's launch: RW rows per warp so that about a CTA per SM or more run,
-// the register prefetch capped at 32 words per lane.
-constexpr size_t kDirectMaxBytes = 8u << 20;  // larger matrices stream through the TMA ring
-
-template <int WPL, int RW, int NP>
-int launch_direct_t(const DirectParams &P, int rows_total, bool pdl, cudaStream_t st) {
-    const int grid = (rows_total + kDirectWarps * RW - 1) / (kDirectWarps * RW);
-    const int KP = (P.WPR / P.WG) * P.G;
-    const size_t smem = ((size_t)KP + KP / 8) * 4;
-    auto k = P.stamp.base ? i4_mv_direct_kernel<WPL, RW, NP, true> : i4_mv_direct_kernel<WPL, RW, NP, false>;
-    if (smem > 48 * 1024) {
-        static KernelSmem attr;
-        int smem_max = 0;
-        TQ_CUDA_TRY(smem_limit_once(k, attr, &smem_max));
-        TQ_CHECK_ARG(smem <= (size_t)smem_max, "i4 direct: %zu B of shared memory", smem);
-    }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kDirectThreads);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr_l[1];
-    attr_l[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr_l[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr_l;
-    cfg.numAttrs = pdl ? 1 : 0;
-    TQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, k, P));
-    return TQB200_OK;
-}
-
-int launch_direct(const I4Job *jobs, int n_jobs, int in_dim, int group_size, const I4LaunchOpts &o,
-                  bool pair, cudaStream_t st) {
-    DirectParams P{};
-    P.n_jobs = n_jobs;
-    int acc = 0;
-    for (int j = 0; j < n_jobs; ++j) {
-        TQ_CHECK_ARG(jobs[j].rows >= 0, "rows %d", jobs[j].rows);
-        P.job[j] = jobs[j];
-        if (!pair || j == 0) acc += jobs[j].rows;
-        P.row_end[j] = acc;
-    }
-    if (pair) P.row_end[1] = acc;
-    if (acc == 0) return TQB200_OK;
-    P.K = in_dim;
-    P.G = group_size;
-    P.WG = 1 + group_size / 8;
-    P.WPR = ((in_dim + group_size - 1) / group_size) * P.WG;
-    P.RB = (size_t)P.WPR * 4;
-    P.pair = pair ? 1 : 0;
-    P.x = o.x;
-    P.stamp = o.stamp;
-    const int wpl = (P.WPR + 31) / 32;  // <= 8
-    const int np = pair ? 2 : 1;
-    // rows per warp: the most (up to 4, <= 32 prefetched words per lane) that still gives
-    // at least one CTA per SM
-    int rw = 4;
-    const int cap = 32 / (((wpl + 3) / 4) * 4 * np);
-    rw = std::min(rw, std::max(1, cap));
-    while (rw > 1 && (acc + kDirectWarps * rw - 1) / (kDirectWarps * rw) < num_sms()) rw /= 2;
-#define TQ_DIRECT(WPLV, RWV, NPV) \
-    if (wpl <= WPLV && rw == RWV && np == NPV) return launch_direct_t<WPLV, RWV, NPV>(P, acc, o.pdl, st);
-    TQ_DIRECT(4, 4, 1) TQ_DIRECT(4, 2, 1) TQ_DIRECT(4, 1, 1)
-    TQ_DIRECT(8, 4, 1) TQ_DIRECT(8, 2, 1) TQ_DIRECT(8, 1, 1)
-    TQ_DIRECT(4, 4, 2) TQ_DIRECT(4, 2, 2) TQ_DIRECT(4, 1, 2)
-    TQ_DIRECT(8, 2, 2) TQ_DIRECT(8, 1, 2)
-#undef TQ_DIRECT
-    return set_error(TQB200_ERR_INVALID_ARG, "i4 direct: no instance for %d words, %d rows", wpl, rw);
-}
-
 int launch_i4_matvec_ex(const I4Job *jobs, int n_jobs, int in_dim, int group_size,
                         const I4LaunchOpts &o, cudaStream_t stream) {
     TQ_CHECK_ARG(n_jobs >= 1 && n_jobs <= 3, "n_jobs %d", n_jobs);
@@ -1299,16 +1081,6 @@ int launch_i4_matvec_ex(const I4Job *jobs, int n_jobs, int in_dim, int group_siz
     P.stamp = o.stamp;
     P.xw = o.xwait;
     P.xp = o.put;
-    {   // small rows, plain or RMSNorm x, no argmax / experts / exchange: the direct kernel
-        const int ng = (in_dim + group_size - 1) / group_size;
-        const int WG = 1 + group_size / 8, WPR = ng * WG;
-        bool direct = group_size % 8 == 0 && WPR <= kDirectMaxWords &&
-                      (o.x.mode == X_PLAIN || o.x.mode == X_RMSNORM) && !o.argmax.token &&
-                      !o.eidx && !o.xslots && !o.put && !o.xwait && (!pair || n_jobs == 2) &&
-                      (size_t)rows_total * ng * (4 + group_size / 2) * (pair ? 2 : 1) <= kDirectMaxBytes;
-        for (int jx = 0; jx < n_jobs; ++jx) direct = direct && ((uintptr_t)jobs[jx].w % 4u == 0);
-        if (direct) return launch_direct(jobs, n_jobs, in_dim, group_size, o, pair, stream);
-    }
     const Shape L = plan(in_dim, group_size, pair, o.x.mode == X_RMSNORM, rows_total,
                          o.eidx ? o.erows : 0);
     bool aligned = true;  // the TMA path needs 16-byte aligned matrix bases
