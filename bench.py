@@ -814,7 +814,13 @@ def bench_prefill(args, rank, pg, pk, pk_kind):
     sm = SynthModel(spec, seed=0)
     t_build = time.time() - t0
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    eng = lib.Engine(sm, max_seq_len=spec.max_seq_len, kv_fp16=False)
+    tp = {}
+    if world > 1:  # expert parallelism: experts sharded, attention whole on every rank
+        tp = {"tp_size": world, "tp_rank": rank, "nccl_id": share_nccl_id(pg, rank)}
+    eng = lib.Engine(sm, max_seq_len=spec.max_seq_len, kv_fp16=False, **tp)
+    if world > 1 and args.exchange == "p2p":  # the decode steps' expert-slot exchange
+        from tqb200 import exchange
+        exchange.open_exchange(eng, exchange.gather_over_pg(eng.exchange_handle(), pg))
     del sm.tensors
     rng = np.random.default_rng(2)
     prompt = rng.integers(0, spec.vocab, n).astype(np.int32)
@@ -875,7 +881,10 @@ def bench_prefill(args, rank, pg, pk, pk_kind):
                    "prompt_tokens": n, "global_batch": 1,
                    "l2": "inputs larger than L2 (%.1f GB of expert weights read per prompt)"
                          % (L * spec.n_experts * 3 * spec.moe_inter * spec.hidden * 0.5625 / 1e9),
-                   "parallelism": "single GPU", "model_build_s": round(t_build, 1),
+                   "parallelism": ("single GPU" if world == 1 else
+                                   f"ep{world}: experts sharded, attention whole on every rank; "
+                                   "the prompt's expert rows summed over NCCL"),
+                   "model_build_s": round(t_build, 1),
                    "prefill_tflop": round(total_fl / 1e12, 4),
                    "prefill_tflops_whole_step": round(total_fl / (ms * 1e-3) / 1e12, 2),
                    "decode_after_prefill_ms_per_token": round(dec_ms / PREFILL_DECODE_STEPS, 4)},

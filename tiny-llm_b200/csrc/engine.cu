@@ -143,6 +143,10 @@ struct tqb200_engine {
     size_t weight_bytes = 0;
     // tensor parallelism
     int tp = 1, rank = 0;
+    // attention shards: tp for dense models; 1 for MoE models, whose attention runs whole
+    // on every rank (expert parallelism shards only the experts), and rank ra in them
+    int ga = 1, ra = 0;
+    bool xoff = false;  // the batched prefill's exchanges go over NCCL even with p2p open
     float *act = nullptr;              // [inter] SwiGLU output, all-gathered (tp > 1)
     tqb200::ArgPair *pairs = nullptr;  // [tp] per-rank (max, index)
     // MoE decode state: router logits, chosen experts and weights, expert activations
@@ -414,16 +418,17 @@ int xslot_lm(const tqb200_model_desc &d) { return d.n_layers * XS_PER_LAYER; }
 
 // The producer and consumer descriptors of exchange `slot` (device copies for the matvec
 // and attention kernels, values for the others; none without an open exchange).
-const XPut *xput(const tqb200_engine *e, int slot) { return e->p2p ? e->xp_dev + slot : nullptr; }
+bool p2p_on(const tqb200_engine *e) { return e->p2p && !e->xoff; }
+const XPut *xput(const tqb200_engine *e, int slot) { return p2p_on(e) ? e->xp_dev + slot : nullptr; }
 const XWait *xwait_of(const tqb200_engine *e, int slot) {
-    return e->p2p ? e->xw_dev + slot : nullptr;
+    return p2p_on(e) ? e->xw_dev + slot : nullptr;
 }
-XWait xwait_val(const tqb200_engine *e, int slot) { return e->p2p ? e->xw_host[slot] : XWait(); }
+XWait xwait_val(const tqb200_engine *e, int slot) { return p2p_on(e) ? e->xw_host[slot] : XWait(); }
 
 // In-place all-gather of `count` floats per rank (rank r's slice at buf + r * count).
 // With the peer exchange open the producing kernel has already stored the rows.
 int allgather(tqb200_engine *e, float *buf, size_t count) {
-    if (e->tp == 1 || e->p2p) return TQB200_OK;
+    if (e->tp == 1 || p2p_on(e)) return TQB200_OK;
 #ifdef TQB200_HAVE_NCCL
     const ncclResult_t nr =
         ncclAllGather(buf + (size_t)e->rank * count, buf, count, ncclFloat, e->comm, e->stream);
@@ -440,7 +445,7 @@ int allgather(tqb200_engine *e, float *buf, size_t count) {
 // In-place sum over the ranks of `count` floats (with the peer exchange open every
 // owner has stored its slots in every rank's buffer instead).
 int allreduce_sum(tqb200_engine *e, float *buf, size_t count) {
-    if (e->tp == 1 || e->p2p) return TQB200_OK;
+    if (e->tp == 1 || p2p_on(e)) return TQB200_OK;
 #ifdef TQB200_HAVE_NCCL
     const ncclResult_t nr = ncclAllReduce(buf, buf, count, ncclFloat, ncclSum, e->comm, e->stream);
     if (nr != ncclSuccess)
@@ -459,18 +464,19 @@ int launch_lm_head(tqb200_engine *e);
 int launch_forward(tqb200_engine *e) {
     const tqb200_model_desc &d = e->d;
     cudaStream_t st = e->stream;
-    const int G = e->tp, r = e->rank;
+    const int G = e->tp, r = e->rank, Ga = e->ga;
     const int H = d.hidden, hd = d.head_dim;
     const int qd = d.n_heads * hd;
-    const int Hl = d.n_heads / G, KVl = d.n_kv_heads / G;
-    const int qdl = Hl * hd, kvdl = KVl * hd, Hs = H / G, Is = d.inter / G, Vs = d.vocab / G;
+    const int Hl = d.n_heads / Ga, KVl = d.n_kv_heads / Ga;
+    const int qdl = Hl * hd, kvdl = KVl * hd, Hs = H / Ga, Is = d.inter / G, Vs = d.vocab / G;
     const bool pdl = e->o.pdl != 0;
+    const bool xa = Ga > 1;  // attention sharded: its rows and o_proj's are exchanged
     int *status = e->io_out + 1;
-    float *attn_mine = e->attn + (size_t)r * qdl;
-    float *hidden_mine = e->hidden + (size_t)r * Hs;
+    float *attn_mine = e->attn + (size_t)e->ra * qdl;
+    float *hidden_mine = e->hidden + (size_t)e->ra * Hs;
     TQ_TRY(mark(e, -1));
     TQ_TRY(launch_embed(e->embed, e->embed_dtype, e->io_in, H, d.group_size, e->hidden, st, 1,
-                        e->p2p ? e->epoch : nullptr));
+                        p2p_on(e) ? e->epoch : nullptr));
     TQ_TRY(mark(e, K_EMBED));
     for (int l = 0; l < d.n_layers; ++l) {
         const DLayer &w = e->layers[l];
@@ -548,9 +554,9 @@ int launch_forward(tqb200_engine *e) {
             a.pdl = pdl;
             a.status = status;
             a.stamp = tl_next(e, K_ATTN);
-            a.put = xput(e, l * XS_PER_LAYER + XS_ATTN);
+            a.put = xa ? xput(e, l * XS_PER_LAYER + XS_ATTN) : nullptr;
             TQ_TRY(launch_attention(a, st));
-            TQ_TRY(allgather(e, e->attn, qdl));
+            if (xa) TQ_TRY(allgather(e, e->attn, qdl));
             TQ_TRY(mark(e, K_ATTN));
         }
         if (w.vq2) {
@@ -559,7 +565,7 @@ int launch_forward(tqb200_engine *e) {
             a.K = qd;
             a.x = {X_PLAIN, e->attn, nullptr, 0.0f, nullptr};
             TQ_TRY(vq_launch(a, K_OPROJ));
-            TQ_TRY(allgather(e, e->hidden, Hs));
+            if (xa) TQ_TRY(allgather(e, e->hidden, Hs));
             TQ_TRY(mark(e, K_OPROJ));
         } else {   // o_proj, residual fused: hidden = hidden + W_o attn (this rank's rows)
             I4Job j{w.o, hidden_mine, nullptr, hidden_mine, Hs};
@@ -568,10 +574,12 @@ int launch_forward(tqb200_engine *e) {
             o.pdl = pdl;
             o.status = status;
             o.stamp = tl_next(e, K_OPROJ);
-            o.xwait = xwait_of(e, l * XS_PER_LAYER + XS_ATTN);
-            o.put = xput(e, l * XS_PER_LAYER + XS_HID_O);
+            if (xa) {
+                o.xwait = xwait_of(e, l * XS_PER_LAYER + XS_ATTN);
+                o.put = xput(e, l * XS_PER_LAYER + XS_HID_O);
+            }
             TQ_TRY(launch_i4_matvec_ex(&j, 1, qd, d.group_size, o, st));
-            TQ_TRY(allgather(e, e->hidden, Hs));
+            if (xa) TQ_TRY(allgather(e, e->hidden, Hs));
             TQ_TRY(mark(e, K_OPROJ));
         }
         if (w.moe) {
@@ -591,7 +599,8 @@ int launch_forward(tqb200_engine *e) {
                 TQ_TRY(launch_moe_router(e->hidden, w.post_ln, d.rms_eps, H, w.router_f32, E, k,
                                          e->moe_logits, e->moe_idx, e->moe_w, e->moe_ticket, pdl,
                                          st, tl_next(e, K_ROUTER),
-                                         xwait_val(e, l * XS_PER_LAYER + XS_HID_O), status));
+                                         xa ? xwait_val(e, l * XS_PER_LAYER + XS_HID_O) : XWait(),
+                                         status));
             } else {
                 I4Job j{w.router_i4, e->moe_logits, nullptr, nullptr, E};
                 I4LaunchOpts o;
@@ -599,7 +608,7 @@ int launch_forward(tqb200_engine *e) {
                 o.pdl = pdl;
                 o.status = status;
                 o.stamp = tl_next(e, K_ROUTER);
-                o.xwait = xwait_of(e, l * XS_PER_LAYER + XS_HID_O);
+                if (xa) o.xwait = xwait_of(e, l * XS_PER_LAYER + XS_HID_O);
                 TQ_TRY(launch_i4_matvec_ex(&j, 1, H, d.group_size, o, st));
                 TQ_TRY(launch_topk_softmax(e->moe_logits, E, k, e->moe_idx, e->moe_w, st));
             }
@@ -621,7 +630,7 @@ int launch_forward(tqb200_engine *e) {
                 o.pdl = pdl;
                 o.status = status;
                 o.stamp = tl_next(e, K_GATEUP);
-                o.xwait = xwait_of(e, l * XS_PER_LAYER + XS_HID_O);
+                if (xa) o.xwait = xwait_of(e, l * XS_PER_LAYER + XS_HID_O);
                 TQ_TRY(launch_i4_matvec_ex(j, 2, H, d.group_size, o, st));
                 TQ_TRY(mark(e, K_GATEUP));
             }
@@ -820,11 +829,15 @@ int create_impl(const tqb200_model_desc *desc, const tqb200_engine_opts *opts, t
     e->rank = e->o.tp_rank;
     const int G = e->tp, r = e->rank;
     TQ_CHECK_ARG(r >= 0 && r < G, "tp_rank %d outside tp_size %d", r, G);
-    TQ_CHECK_ARG(d.n_heads % G == 0 && d.n_kv_heads % G == 0 && H % G == 0 && d.inter % G == 0 &&
-                     d.vocab % G == 0,
+    e->ga = d.model_type == TQB200_MODEL_QWEN3_MOE ? 1 : G;
+    e->ra = e->ga > 1 ? r : 0;
+    const int Ga = e->ga;
+    TQ_CHECK_ARG(d.n_heads % Ga == 0 && d.n_kv_heads % Ga == 0 && H % Ga == 0 &&
+                     (Ga == 1 || d.inter % G == 0) && d.vocab % G == 0,
                  "tp_size %d must divide heads %d, kv heads %d, hidden %d, inter %d, vocab %d", G,
                  d.n_heads, d.n_kv_heads, H, d.inter, d.vocab);
-    const int qdl = qd / G, kvdl = kvd / G, Hs = H / G, Is = d.inter / G, Vs = d.vocab / G;
+    const int ra = e->ra;
+    const int qdl = qd / Ga, kvdl = kvd / Ga, Hs = H / Ga, Is = d.inter / G, Vs = d.vocab / G;
 #ifdef TQB200_HAVE_NCCL
     if (G > 1) {
         ncclUniqueId id;
@@ -896,10 +909,10 @@ int create_impl(const tqb200_model_desc *desc, const tqb200_engine_opts *opts, t
         auto up_rows = [&](const tqb200_matrix &m, int r0, int n, const uint8_t **o) {
             return w.vq2 ? up_vq2_rows(e, m, r0, n, o) : up_i4_rows(e, m, r0, n, o);
         };
-        TQ_TRY(up_rows(s.q_proj, r * qdl, qdl, &w.q));
-        TQ_TRY(up_rows(s.k_proj, r * kvdl, kvdl, &w.k));
-        TQ_TRY(up_rows(s.v_proj, r * kvdl, kvdl, &w.v));
-        TQ_TRY(up_rows(s.o_proj, r * Hs, Hs, &w.o));
+        TQ_TRY(up_rows(s.q_proj, ra * qdl, qdl, &w.q));
+        TQ_TRY(up_rows(s.k_proj, ra * kvdl, kvdl, &w.k));
+        TQ_TRY(up_rows(s.v_proj, ra * kvdl, kvdl, &w.v));
+        TQ_TRY(up_rows(s.o_proj, ra * Hs, Hs, &w.o));
         if (w.moe) {
             TQ_TRY(up_experts(e, s, d, w));
         } else {
@@ -907,9 +920,9 @@ int create_impl(const tqb200_model_desc *desc, const tqb200_engine_opts *opts, t
             TQ_TRY(up_rows(s.up_proj, r * Is, Is, &w.up));
             TQ_TRY(up_rows(s.down_proj, r * Hs, Hs, &w.down));
         }
-        TQ_TRY(up_vec(e, s.q_bias ? s.q_bias + r * qdl : nullptr, qdl, &w.q_bias));
-        TQ_TRY(up_vec(e, s.k_bias ? s.k_bias + r * kvdl : nullptr, kvdl, &w.k_bias));
-        TQ_TRY(up_vec(e, s.v_bias ? s.v_bias + r * kvdl : nullptr, kvdl, &w.v_bias));
+        TQ_TRY(up_vec(e, s.q_bias ? s.q_bias + ra * qdl : nullptr, qdl, &w.q_bias));
+        TQ_TRY(up_vec(e, s.k_bias ? s.k_bias + ra * kvdl : nullptr, kvdl, &w.k_bias));
+        TQ_TRY(up_vec(e, s.v_bias ? s.v_bias + ra * kvdl : nullptr, kvdl, &w.v_bias));
         TQ_TRY(up_vec(e, s.q_norm, hd, &w.q_norm));
         TQ_TRY(up_vec(e, s.k_norm, hd, &w.k_norm));
     }
@@ -964,11 +977,11 @@ int create_impl(const tqb200_model_desc *desc, const tqb200_engine_opts *opts, t
         e->moe_local = (int *)m, m += 64;
         e->moe_ticket = (unsigned int *)m;
     }
-    e->layer_stride = (size_t)(d.n_kv_heads / G) * e->o.max_seq_len * hd;
+    e->layer_stride = (size_t)(d.n_kv_heads / Ga) * e->o.max_seq_len * hd;
     const size_t kv_bytes = 2 * (size_t)d.n_layers * e->layer_stride * (e->o.kv_fp16 ? 2 : 4);
     TQ_TRY(dev_alloc(e, kv_bytes, &e->kv));
     TQ_CUDA_TRY(cudaMemset(e->kv, 0, kv_bytes));
-    TQ_TRY(attn_plan(d.n_kv_heads / G, e->o.max_seq_len, &e->attn_nsplit, &e->attn_chunk));
+    TQ_TRY(attn_plan(d.n_kv_heads / Ga, e->o.max_seq_len, &e->attn_nsplit, &e->attn_chunk));
     TQ_TRY(dev_alloc(e, attn_partial_floats(d.n_heads, hd, e->attn_nsplit) * 4, &p));
     e->attn_part = (float *)p;
     const int slots = i4_argmax_slots(d.vocab, H, d.group_size);
@@ -1005,7 +1018,9 @@ constexpr int kPrefillChunk = 512;
 
 bool prefill_batched(const tqb200_engine *e) {
     const tqb200_model_desc &d = e->d;
-    return e->tp == 1 && !e->layers[0].vq2 && mm_group_supported(d.group_size) &&
+    // tensor parallelism: MoE models only (attention whole on every rank, the experts
+    // sharded); dense models under tensor parallelism run the prompt as decode steps
+    return (e->tp == 1 || e->ga == 1) && !e->layers[0].vq2 && mm_group_supported(d.group_size) &&
            attn_prefill_supported(d.n_heads, d.n_kv_heads, d.head_dim);
 }
 
@@ -1047,6 +1062,7 @@ int prefill_setup(tqb200_engine *e) {
     const int G = d.group_size;
     const bool moe = d.model_type == TQB200_MODEL_QWEN3_MOE;
     const int k = moe ? d.experts_per_tok : 1, E = moe ? d.n_experts : 0, mi = d.moe_inter;
+    const int El = E / e->tp;  // this rank's experts (expert parallelism)
     P.cap = std::min(kPrefillChunk, e->o.max_seq_len);
     if (moe)  // the plan kernel holds the chunk's n*k assignments in shared memory
         while (P.cap > 1 && moe_plan_smem_bytes(P.cap, k, E) > kMoePlanMaxSmem) P.cap /= 2;
@@ -1060,9 +1076,9 @@ int prefill_setup(tqb200_engine *e) {
         TQ_TRY(repack(e, w.v, kvd, H, &pl.v));
         TQ_TRY(repack(e, w.o, H, qd, &pl.o));
         if (w.moe) {
-            TQ_TRY(repack_experts(e, w.ex_gate, w.ex_gu_stride, E, mi, H, &pl.ex_gate, &pl.ex_gu_stride));
-            TQ_TRY(repack_experts(e, w.ex_up, w.ex_gu_stride, E, mi, H, &pl.ex_up, &pl.ex_gu_stride));
-            TQ_TRY(repack_experts(e, w.ex_down, w.ex_down_stride, E, H, mi, &pl.ex_down,
+            TQ_TRY(repack_experts(e, w.ex_gate, w.ex_gu_stride, El, mi, H, &pl.ex_gate, &pl.ex_gu_stride));
+            TQ_TRY(repack_experts(e, w.ex_up, w.ex_gu_stride, El, mi, H, &pl.ex_up, &pl.ex_gu_stride));
+            TQ_TRY(repack_experts(e, w.ex_down, w.ex_down_stride, El, H, mi, &pl.ex_down,
                                   &pl.ex_down_stride));
             if (w.router_i4) TQ_TRY(repack(e, w.router_i4, E, H, &pl.router));
         } else {
@@ -1332,6 +1348,10 @@ int prefill_chunk(tqb200_engine *e, int n, int p0) {
         a.pack_dn = P.pack_dn;
         a.pack_map = P.pack_map;
         a.status = status;
+        if (e->tp > 1) {  // expert parallelism: this rank's experts only
+            a.e0 = e->rank * (E / e->tp);
+            a.e_local = E / e->tp;
+        }
         TQ_TRY(launch_moe_plan(a, st));
         TQ_TRY(mark(e, K_PLAN));
         const int nbk = moe_plan_max_cols(n, k, E) / 8;
@@ -1344,8 +1364,12 @@ int prefill_chunk(tqb200_engine *e, int n, int p0) {
         TQ_TRY(mark(e, K_GATEUP));
         TQ_TRY(launch_mm_pack_x_mapped(P.pack_dn, P.pack_map, P.ntiles + 2, nbk, mi, G, P.bhi, P.blo, st));
         TQ_TRY(mark(e, K_PACK));
+        // expert parallelism: the bucket rows of other ranks' experts stay zero here, and
+        // a cross-rank sum (exact: one non-zero term per row) gives every rank all rows
+        if (e->tp > 1) TQ_CUDA_TRY(cudaMemsetAsync(P.mo, 0, (size_t)n * k * H * 4, st));
         TQ_TRY(launch_matmul_i4_planned(P.jobs_dn, P.tile_dn, P.ntiles + 1, tdn, mi, G, P.moe_nt,
                                         P.bhi, P.blo, status, st));
+        if (e->tp > 1) TQ_TRY(allreduce_sum(e, P.mo, (size_t)n * k * H));
         TQ_TRY(mark(e, K_DOWN));
         TQ_TRY(launch_moe_combine_rows(P.hidden, P.mo, P.wts, P.slot, n, k, H, st));
         TQ_TRY(mark(e, K_COMBINE));
@@ -1472,6 +1496,13 @@ int tqb200_engine_prefill(tqb200_engine *e, const int *tokens, int n, int *next_
     TQ_CUDA_TRY(cudaSetDevice(e->device));
     TQ_TRY(prefill_setup(e));
     Prefill &P = e->pf;
+    // expert parallelism: the prompt's cross-rank sums go over NCCL (the decode step's
+    // peer-exchange counters stay in step with its epoch)
+    struct XOff {
+        tqb200_engine *e;
+        explicit XOff(tqb200_engine *x) : e(x) { e->xoff = true; }
+        ~XOff() { e->xoff = false; }
+    } xoff_guard(e);
     std::vector<int> io((size_t)P.cap + 1);
     for (int c0 = 0; c0 < n; c0 += P.cap) {
         const int m = std::min(P.cap, n - c0);

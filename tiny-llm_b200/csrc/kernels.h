@@ -311,6 +311,10 @@ struct MoePlanArgs {
     MmPackJob *pack_gu, *pack_dn; // [E] each
     int *pack_map;                // 8-column block -> expert (moe_plan_max_cols / 8 entries)
     int *status;
+    // expert parallelism: only experts [e0, e0 + e_local) get matmul jobs, their weights at
+    // (e - e0) * stride (e_local = 0: every expert); the bucket layout stays that of all E
+    // experts, so obuf rows line up across the ranks
+    int e0 = 0, e_local = 0;
 };
 int launch_moe_plan(const MoePlanArgs &a, cudaStream_t st);
 // upper bounds for the buffers of a plan: tiles of one job kind of M rows at width nt,

@@ -334,6 +334,7 @@ __global__ void __launch_bounds__(kPlanThreads) moe_plan_kernel(const MoePlanArg
     const int mt_gu = (a.mi + kMmTileRows - 1) / kMmTileRows;
     const int mt_dn = (a.H + kMmTileRows - 1) / kMmTileRows;
     int c = 0;
+    const bool loc = tid < E && (a.e_local == 0 || (tid >= a.e0 && tid < a.e0 + a.e_local));
     if (tid < E) {  // slice offsets inside the bucket, and the bucket size
         for (int w = 0; w < kPlanWarps; ++w) {
             const int x = s_wc[w * E + tid];
@@ -343,18 +344,18 @@ __global__ void __launch_bounds__(kPlanThreads) moe_plan_kernel(const MoePlanArg
         const int npad = (c + 15) & ~15, ct = (npad + a.nt - 1) / a.nt;
         v[0] = c;
         v[1] = npad;
-        v[2] = 2 * mt_gu * ct;
-        v[3] = mt_dn * ct;
+        v[2] = loc ? 2 * mt_gu * ct : 0;  // another rank's expert: no tiles here
+        v[3] = loc ? mt_dn * ct : 0;
     }
     plan_scan4(v, tot, s_wt);
-    int jv[4] = {tid < E && c > 0 ? 1 : 0, 0, 0, 0}, jt[4];
+    int jv[4] = {loc && c > 0 ? 1 : 0, 0, 0, 0}, jt[4];
     plan_scan4(jv, jt, s_wt);
     if (tid < E) {
         s_off[tid] = v[0];
         s_npre[tid] = v[1];
         s_tgu[tid] = v[2];
         s_tdn[tid] = v[3];
-        s_job[tid] = c > 0 ? jv[0] : -1;
+        s_job[tid] = loc && c > 0 ? jv[0] : -1;
     }
     if (tid == 0) {
         a.ntiles[0] = tot[2];
@@ -392,7 +393,7 @@ __global__ void __launch_bounds__(kPlanThreads) moe_plan_kernel(const MoePlanArg
         const int ct = (((cnt + 15) & ~15) + a.nt - 1) / a.nt;
         for (int h = 0; h < 2; ++h) {
             MmJob j;
-            j.w = (h ? a.wu : a.wg) + (size_t)e * a.wgu_stride;
+            j.w = (h ? a.wu : a.wg) + (size_t)(e - (a.e_local ? a.e0 : 0)) * a.wgu_stride;
             j.y = (h ? a.ubuf : a.hbuf) + (size_t)off * a.mi;
             j.M = a.mi;
             j.N = cnt;
@@ -405,7 +406,7 @@ __global__ void __launch_bounds__(kPlanThreads) moe_plan_kernel(const MoePlanArg
             for (int i = 0; i < mt_gu * ct; ++i) a.tile_gu[j.tile_begin + i] = 2 * jx + h;
         }
         MmJob j;
-        j.w = a.wd + (size_t)e * a.wd_stride;
+        j.w = a.wd + (size_t)(e - (a.e_local ? a.e0 : 0)) * a.wd_stride;
         j.y = a.obuf + (size_t)off * a.H;
         j.M = a.H;
         j.N = cnt;
@@ -473,6 +474,8 @@ long long moe_plan_plane_elems(int n, int k, int E, int K, int G) {
 int launch_moe_plan(const MoePlanArgs &a, cudaStream_t st) {
     TQ_CHECK_ARG(a.E > 0 && a.E <= kMoePlanMaxExperts && a.k > 0 && a.n > 0,
                  "moe plan: E %d k %d n %d", a.E, a.k, a.n);
+    TQ_CHECK_ARG(a.e_local >= 0 && a.e0 >= 0 && a.e0 + a.e_local <= a.E,
+                 "moe plan: local experts [%d, %d) outside %d", a.e0, a.e0 + a.e_local, a.E);
     const size_t smem = moe_plan_smem_bytes(a.n, a.k, a.E);
     TQ_CHECK_ARG(smem <= kMoePlanMaxSmem, "moe plan: %d assignments over %d experts", a.n * a.k, a.E);
     static KernelSmem once;
