@@ -231,9 +231,13 @@ typedef struct tqb200_engine_opts {
     int pdl;           /* programmatic dependent launch between kernels (default 1) */
     int device;        /* CUDA device ordinal; -1 = current */
     /* Column-parallel sharding over tp_size GPUs, one process per GPU (new in this build;
-     * the reference is single-device).  Every projection's output rows, the attention
-     * heads and lm_head's vocabulary rows are split; activations are all-gathered over
-     * NCCL at each layer boundary.  All ranks call create/step/generate in lockstep. */
+     * the reference is single-device).  Dense models: every projection's output rows, the
+     * attention heads and lm_head's vocabulary rows are split, and the activations are
+     * all-gathered at each layer boundary (NCCL, or the peer exchange below).  MoE models:
+     * expert parallelism (each rank holds tp_size-th of the experts; the attention runs
+     * whole on every rank; the chosen experts' outputs are exchanged once per layer) with
+     * lm_head split by vocabulary.  All ranks call create/step/generate/prefill in
+     * lockstep. */
     int tp_size;       /* 1 = single GPU */
     int tp_rank;
     unsigned char nccl_id[128];  /* from tqb200_nccl_unique_id() on one rank, shared to all */
@@ -267,8 +271,10 @@ int tqb200_engine_step(tqb200_engine *e, int token_id, int *next_token);
  * feeds the n prompt tokens at positions pos .. pos+n-1 as one batch (projections and
  * experts on the tensor-core matmul, causal attention over the cache), leaves their K/V
  * in the cache and the last token's logits in the engine, and returns the greedy next
- * token.  Falls back to n decode steps where the batched path does not apply (tp_size > 1,
- * VQ2 projections, head_dim other than 64/128), as the reference falls back to
+ * token.  Under expert parallelism (MoE, tp_size > 1) each rank's grouped GEMM covers its
+ * own experts and the expert rows are summed across the ranks.  Falls back to n decode
+ * steps where the batched path does not apply (dense models with tp_size > 1, VQ2
+ * projections, head_dim other than 64/128), as the reference falls back to
  * forward_token. */
 int tqb200_engine_prefill(tqb200_engine *e, const int *tokens, int n, int *next_token);
 /* tqb200_engine_prefill launched kernel by kernel with a CUDA event after each launch:
