@@ -309,6 +309,11 @@ int tqb200_engine_set_position(tqb200_engine *e, int pos);
 int tqb200_engine_stream(const tqb200_engine *e, void **stream);
 int tqb200_engine_kv_cache(const tqb200_engine *e, void **kv, size_t *bytes);
 int tqb200_engine_weight_bytes(const tqb200_engine *e, size_t *bytes);
+/* Device bytes the batched prefill holds in addition to the weights (no reference
+ * counterpart): repacked copies of the matrices its tensor-core matmul cannot read in
+ * place (those with in_dim / group_size not a multiple of 4); 0 before the first prefill
+ * and when every matrix is read in place through a tensor map. */
+int tqb200_engine_prefill_copy_bytes(const tqb200_engine *e, size_t *bytes);
 
 /* In-graph timeline of tqb200_engine_generate (no reference counterpart; the reference
  * profiles a step op by op on the host, runtime/main.cpp --profile-out).  With a timeline

@@ -36,6 +36,15 @@ CASES = [
 ]
 
 
+def _read_in_place(spec):
+    """Whether the prefill's matmul reads every matrix in place through a tensor map:
+    only matrices whose in_dim / group_size is a multiple of 4 have one (their rows are a
+    multiple of 16 bytes long); the others get a repacked copy."""
+    ffn = spec.moe_inter if spec.model_type == 3 else spec.inter
+    dims = (spec.hidden, spec.n_heads * spec.head_dim, ffn)
+    return all((k // spec.group_size) % 4 == 0 for k in dims)
+
+
 def _prompt(n, vocab, seed):
     return np.random.default_rng(seed).integers(0, vocab, n).astype(np.int32).tolist()
 
@@ -67,6 +76,7 @@ def test_prefill_matches_token_by_token(tq, oracle, name, spec, kv16):
     assert eng.position == len(prompt)
     assert max_rel(eng.logits(), om.logits()) < TOL
     assert nxt == onxt
+    assert (eng.prefill_copy_bytes() == 0) == _read_in_place(spec)
     toks, logits = _continue(eng, nxt, 8)
     otoks, ologits = _continue(om, onxt, 8)
     assert toks == otoks
@@ -128,6 +138,7 @@ def test_prefill_config5_shape(tq, oracle):
     onxt = _oracle_feed(om, prompt)
     assert max_rel(eng.logits(), om.logits()) < TOL
     assert nxt == onxt
+    assert eng.prefill_copy_bytes() == 0  # every matrix read in place: i4 bytes held once
     toks, _ = _continue(eng, nxt, 3)
     otoks, _ = _continue(om, onxt, 3)
     assert toks == otoks

@@ -65,12 +65,20 @@ struct DLayer {
     size_t ex_gu_stride = 0, ex_down_stride = 0;  // bytes between experts
 };
 
-// Prefill copies of a layer's i4 matrices in the tensor-core matmul's tile-contiguous
-// order (launch_mm_repack_w); experts back to back, expert x at x * stride.
+// A weight operand of the prefill's tensor-core matmul: a tensor map (device copy)
+// over the decode matrix itself, read in place, or, for a matrix no map can cover (K / G
+// not a multiple of 4), a tile-contiguous repacked copy (launch_mm_repack_w).
+struct PW {
+    const uint8_t *w = nullptr;  // repacked copy (null with a map)
+    const void *tm = nullptr;    // CUtensorMap in device memory
+    explicit operator bool() const { return w || tm; }
+};
+
+// A layer's prefill weight operands; experts of a kind under one map (expert x at z = x)
+// or repacked back to back, expert x at x * stride.
 struct PLayer {
-    const uint8_t *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr;
-    const uint8_t *gate = nullptr, *up = nullptr, *down = nullptr, *router = nullptr;
-    const uint8_t *ex_gate = nullptr, *ex_up = nullptr, *ex_down = nullptr;
+    PW q, k, v, o, gate, up, down, router;
+    PW ex_gate, ex_up, ex_down;
     size_t ex_gu_stride = 0, ex_down_stride = 0;
 };
 
@@ -96,6 +104,12 @@ struct Prefill {
     MmJob *jobs_gu = nullptr, *jobs_dn = nullptr;
     MmPackJob *pack_gu = nullptr, *pack_dn = nullptr;
     int max_tiles_gu = 0, max_tiles_dn = 0, moe_nt = 64;
+    // tensor maps of every layer's matrices (device; 128 bytes each) and the bytes of the
+    // repacked copies made for matrices without one
+    uint8_t *maps = nullptr;
+    size_t n_maps = 0, cap_maps = 0;
+    std::vector<uint8_t> hmaps;
+    size_t copy_bytes = 0;
 };
 
 }  // namespace
@@ -1024,23 +1038,45 @@ bool prefill_batched(const tqb200_engine *e) {
            attn_prefill_supported(d.n_heads, d.n_kv_heads, d.head_dim);
 }
 
-int repack(tqb200_engine *e, const uint8_t *w, int M, int K, const uint8_t **out) {
+// A tensor map over E matrices of M x K (matrix x at w + x * stride) into the next slot
+// of the device map array; false when the layout admits none.
+bool weight_map(tqb200_engine *e, const uint8_t *w, int M, int K, int E, size_t stride, PW *out) {
+    Prefill &P = e->pf;
+    if (P.n_maps >= P.cap_maps) return false;
+    uint8_t *h = P.hmaps.data() + P.n_maps * 128;
+    if (!mm_encode_weight_map(w, M, K, e->d.group_size, E, stride, h)) return false;
+    out->w = nullptr;
+    out->tm = P.maps + P.n_maps * 128;
+    ++P.n_maps;
+    return true;
+}
+
+int repack(tqb200_engine *e, const uint8_t *w, int M, int K, PW *out) {
+    if (weight_map(e, w, M, K, 1, 0, out)) return TQB200_OK;
     const int G = e->d.group_size;
     void *p;
     TQ_TRY(dev_alloc(e, mm_repacked_bytes(M, K, G), &p));
     TQ_TRY(launch_mm_repack_w(w, M, K, G, (uint8_t *)p, e->stream));
-    *out = (const uint8_t *)p;
+    e->pf.copy_bytes += mm_repacked_bytes(M, K, G);
+    out->w = (const uint8_t *)p;
+    out->tm = nullptr;
     return TQB200_OK;
 }
 
-// E experts of M x K at `stride` bytes apart -> one buffer, expert x at x * *ostride.
+// E experts of M x K at `stride` bytes apart: one map over all of them, or one repacked
+// buffer, expert x at x * *ostride.
 int repack_experts(tqb200_engine *e, const uint8_t *w, size_t stride, int E, int M, int K,
-                   const uint8_t **out, size_t *ostride) {
+                   PW *out, size_t *ostride) {
+    if (weight_map(e, w, M, K, E, stride, out)) {
+        *ostride = stride;
+        return TQB200_OK;
+    }
     const int G = e->d.group_size;
     const size_t one = (mm_repacked_bytes(M, K, G) + 255) & ~(size_t)255;
     const size_t rb = tqb200_i4_row_bytes(K, G);
     void *p;
     TQ_TRY(dev_alloc(e, one * E, &p));
+    e->pf.copy_bytes += one * E;
     if (stride == (size_t)M * rb && M % kMmTileRows == 0 && one == mm_repacked_bytes(M, K, G)) {
         // rows of consecutive experts are contiguous and no tile straddles two experts
         TQ_TRY(launch_mm_repack_w(w, M * E, K, G, (uint8_t *)p, e->stream));
@@ -1049,7 +1085,8 @@ int repack_experts(tqb200_engine *e, const uint8_t *w, size_t stride, int E, int
             TQ_TRY(launch_mm_repack_w(w + (size_t)x * stride, M, K, G, (uint8_t *)p + (size_t)x * one,
                                       e->stream));
     }
-    *out = (const uint8_t *)p;
+    out->w = (const uint8_t *)p;
+    out->tm = nullptr;
     *ostride = one;
     return TQB200_OK;
 }
@@ -1068,6 +1105,13 @@ int prefill_setup(tqb200_engine *e) {
         while (P.cap > 1 && moe_plan_smem_bytes(P.cap, k, E) > kMoePlanMaxSmem) P.cap /= 2;
     const int cap = P.cap;
     P.layers.resize(d.n_layers);
+    void *p;
+    P.cap_maps = (size_t)11 * d.n_layers;  // q k v o + gate up down router + 3 expert kinds
+    P.hmaps.assign(P.cap_maps * 128, 0);
+    TQ_TRY(dev_alloc(e, P.cap_maps * 128, &p));
+    P.maps = (uint8_t *)p;
+    P.n_maps = 0;
+    P.copy_bytes = 0;
     for (int l = 0; l < d.n_layers; ++l) {
         const DLayer &w = e->layers[l];
         PLayer &pl = P.layers[l];
@@ -1087,9 +1131,10 @@ int prefill_setup(tqb200_engine *e) {
             TQ_TRY(repack(e, w.down, H, d.inter, &pl.down));
         }
     }
+    if (P.n_maps)
+        TQ_CUDA_TRY(cudaMemcpy(P.maps, P.hmaps.data(), P.n_maps * 128, cudaMemcpyHostToDevice));
     const int I = moe ? 0 : d.inter;
     const size_t f = (size_t)cap * (2 * (size_t)H + 2 * (size_t)qd + 2 * (size_t)kvd + 2 * (size_t)I);
-    void *p;
     TQ_TRY(dev_alloc(e, f * 4 + 16 * 64, &p));
     float *a = (float *)p;
     auto take = [&](size_t n) {  // 64-byte aligned carve
@@ -1184,9 +1229,10 @@ int prefill_plan(tqb200_engine *e, int n) {
             P.nt[(size_t)4 * l + launch] = nt;
             P.tiles[(size_t)4 * l + launch] = t;
         };
-        auto job = [](const uint8_t *wt, float *y, int M, const float *resid, const float *bias) {
+        auto job = [](const PW &wt, float *y, int M, const float *resid, const float *bias) {
             MmJob x{};
-            x.w = wt;
+            x.w = wt.w;
+            x.tmap = wt.tm;
             x.y = y;
             x.M = M;
             x.ldy = M;
@@ -1328,9 +1374,12 @@ int prefill_chunk(tqb200_engine *e, int n, int p0) {
         a.H = H;
         a.mi = mi;
         a.nt = P.moe_nt;
-        a.wg = pl.ex_gate;
-        a.wu = pl.ex_up;
-        a.wd = pl.ex_down;
+        a.wg = pl.ex_gate.w;
+        a.wu = pl.ex_up.w;
+        a.wd = pl.ex_down.w;
+        a.tmg = pl.ex_gate.tm;
+        a.tmu = pl.ex_up.tm;
+        a.tmd = pl.ex_down.tm;
         a.wgu_stride = (long long)pl.ex_gu_stride;
         a.wd_stride = (long long)pl.ex_down_stride;
         a.xn = P.xn;
@@ -1644,6 +1693,12 @@ int tqb200_engine_kv_cache(const tqb200_engine *e, void **kv, size_t *bytes) {
 int tqb200_engine_weight_bytes(const tqb200_engine *e, size_t *bytes) {
     TQ_CHECK_ARG(e && bytes, "null argument");
     *bytes = e->weight_bytes;
+    return TQB200_OK;
+}
+
+int tqb200_engine_prefill_copy_bytes(const tqb200_engine *e, size_t *bytes) {
+    TQ_CHECK_ARG(e && bytes, "null argument");
+    *bytes = e->pf.copy_bytes;
     return TQB200_OK;
 }
 

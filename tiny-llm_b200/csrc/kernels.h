@@ -238,16 +238,29 @@ int launch_i4_dequant(const uint8_t *w, int rows, int dim, int group_size, float
 
 // ------------------------------------------------------------------ i4 matmul (tensor cores)
 // One weight matrix of a (grouped) tcgen05 matmul: Y[:, n] = W X[:, n] for N columns.
+// The weights come either through a tensor map over the interleaved rows themselves
+// (tmap set: the decode copy, read in place) or from a tile-contiguous repacked copy (w).
 struct MmJob {
-    const uint8_t *w;     // tile-contiguous weights (launch_mm_repack_w)
+    const uint8_t *w;     // tile-contiguous weights (launch_mm_repack_w); unused with tmap
     float *y;             // column n at y + n * ldy
     int M, N, ldy;
     int tile_begin;       // first CTA of this job (jobs in CTA order)
     long long b_off;      // offset (bf16 elements) of this job's X planes
     const float *resid = nullptr;  // optional: y = resid + W x (same layout as y)
     const float *bias = nullptr;   // optional: y = W x + bias[row]
+    const void *tmap = nullptr;    // optional: CUtensorMap in device memory (mm_encode_weight_map)
+    int tz = 0;                    // the map's matrix index (expert e of a layer: e)
 };
 constexpr int kMmTileRows = 256;  // weight rows per matmul CTA
+constexpr int kMmGroupsPerBlock = 4;  // quantisation groups per staged weight block
+// Tensor map (a 128-byte CUtensorMap written to map128) over E matrices of M interleaved
+// i4 rows of K columns, matrix x at w + x * stride, for the matmul's weight blocks (256
+// rows x kMmGroupsPerBlock groups).  False (nothing written) when the layout cannot be
+// mapped: K / G not a multiple of kMmGroupsPerBlock (a row's byte length is then not a
+// multiple of 16), w or stride not 16-byte aligned, or the driver refuses the map; the
+// caller then repacks.
+bool mm_encode_weight_map(const uint8_t *w, int M, int K, int G, int E, size_t stride,
+                          void *map128);
 // One source of a grouped X pack: column n of the job is x + (cols ? cols[n] : n) * ldx.
 struct MmPackJob {
     const float *x;
@@ -300,6 +313,9 @@ struct MoePlanArgs {
     int G, H, mi, nt;      // group size, hidden, expert intermediate, tile width
     const uint8_t *wg, *wu, *wd;  // tile-contiguous expert weights, expert e at e * stride
     long long wgu_stride, wd_stride;
+    // or tensor maps over the experts' interleaved rows (expert e: coordinate z = e), which
+    // take precedence when set
+    const void *tmg = nullptr, *tmu = nullptr, *tmd = nullptr;
     const float *xn;       // [n][H] normalised hidden rows (gate/up input)
     float *hbuf, *ubuf;    // [n*k][mi] gate / up outputs in bucket order (down's input is
                            // SwiGLU(h, u), formed by its X pack)

@@ -22,9 +22,13 @@
 //    accumulators, so the MMAs of group g+1 overlap the read of group g) and fold
 //    y += s_g * (P_hi + P_lo) in fp32 registers.
 //  * Roles: warps 0-7 build the A operand (thread = weight row of the 256-row tile) from
-//    the weight blocks that warp 17 stages with 1-D bulk copies (TMA) a few groups ahead,
+//    the weight blocks (256 rows x 4 groups) that warp 17 stages a few blocks ahead,
 //    together with the stage's X planes, which a pre-pass kernel lays out in the MMA's
-//    shared-memory order.  Warps 8-15 are the epilogue; warp 16 allocates TMEM and one
+//    shared-memory order.  A weight block comes by one 3-D tensor copy (TMA) straight out
+//    of the interleaved rows (runtime/tiny_format.h:66-77) the decode matvec reads, so the
+//    model's i4 bytes are held once; where a row's byte length is not a multiple of 16
+//    (K / G not a multiple of 4) no tensor map exists for it, and the block comes by 1-D
+//    bulk copies from a tile-contiguous repacked copy instead.  Warps 8-15 are the epilogue; warp 16 allocates TMEM and one
 //    lane issues the MMAs; warp 18 does the MMA warp's barrier waits.  Stages (one quantisation group each) are handed over with
 //    mbarriers: full (8 producer warps + the X-plane copy bytes), empty (tcgen05.commit),
 //    tmem_full per row half (commit) and tmem_empty per row half (its 4 epilogue warps);
@@ -39,10 +43,12 @@
 //    waits (bounded) for what it issued and frees its TMEM before returning.
 // Accuracy: products carry the x residue (~2^-17 relative), the zero term ~2^-24, and
 // accumulation is fp32 (the reference's is double): ~1e-5 relative, inside 1e-4.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <string.h>
+
 #include <algorithm>
 #include <atomic>
-
-#include <cuda_bf16.h>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -72,6 +78,7 @@ constexpr int kMmMaxCols = 64;     // tile width limit (epilogue registers)
 // for the epilogue's drain of group i-S-2)
 constexpr int kSclRing = kMmMaxStages + 3;
 constexpr int kMaxRaw = 8;         // weight blocks staged ahead, at most
+constexpr int kGpb = kMmGroupsPerBlock;  // quantisation groups per weight block
 constexpr int kTmemCols = 512;     // the CTA's TMEM allocation (one CTA per SM: registers)
 
 struct MmParams {
@@ -105,15 +112,6 @@ __device__ __forceinline__ uint32_t umma_idesc_bf16(int n) {
            ((uint32_t)(kMmRows >> 4) << 24);
 }
 
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
-                                          uint32_t accumulate) {
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
-        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
 // D (TMEM) (+)= A (TMEM, lane = row, 8 columns = 16 bf16 of K) x B (shared memory).
 __device__ __forceinline__ void umma_bf16_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t b,
                                              uint32_t idesc, uint32_t accumulate) {
@@ -145,6 +143,21 @@ __device__ __forceinline__ void tc_fence_before() {
 }
 __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// One box of a 3-D tensor map in global memory -> shared memory, completion on `bar`.
+// The map was written by the host before the launch; the acquire fence orders this
+// thread's use of it through the tensor-map proxy.
+__device__ __forceinline__ void tmap_acquire(const void *tmap) {
+    asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(tmap) : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(void *dst, const void *tmap, int x, int y, int z,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+        "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive_plain(uint64_t *bar) {
@@ -324,10 +337,10 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
     constexpr int CK = (G + 16) / 8;          // 16-byte chunks per row of a stage
     constexpr uint32_t SBO = CK * 128;        // bytes between 8-row groups (B operand)
     constexpr int KS = G / 16 + 1;            // MMA K steps per group (the last: zero term)
-    constexpr int NW = G / 8;                 // nibble words per row of a group
     constexpr int GB = 4 + G / 2;             // bytes per group of a weight row
     constexpr int WR = GB / 4;                // words per row of a group (odd)
-    constexpr uint32_t kRawBytes = kTileRows * GB;
+    constexpr uint32_t kRawBytes = kTileRows * GB;  // one group of the tile's rows
+    constexpr uint32_t kBlkBytes = kGpb * kRawBytes;  // one staged weight block
     extern __shared__ __align__(1024) uint8_t smem[];
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);  // [kMmMaxStages] A built
@@ -367,6 +380,12 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
     const uint32_t stage_bytes = P.stage_bytes;
     const int ng = P.ng, S = P.stages, RD = P.raw_depth;
     uint8_t *raw = stage_base + (size_t)S * stage_bytes;  // [RD] weight blocks
+    // a block holds groups 4b .. 4b+3 of the tile's 256 rows: from the tensor map as
+    // [row][4 groups] (row t's group c at word t * 4 WR + c * WR), repacked as
+    // [group][row] (at word c * 256 WR + t * WR)
+    const bool tmw = job.tmap != nullptr;
+    const int nblk = (ng + kGpb - 1) / kGpb;
+    const int w_rs = tmw ? kGpb * WR : WR, w_gs = tmw ? WR : kTileRows * WR;
 
     if (t == 0) {
         for (int s = 0; s < S; ++s) {
@@ -406,21 +425,22 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
         const int half = t >> 7;
         const __nv_bfloat162 k128 = __floats2bfloat162_rn(128.0f, 128.0f);
         for (int i = 0; i < ng; ++i) {
-            const int s = i % S, r = i % RD;
+            const int s = i % S, b = i / kGpb, r = b % RD, c = i - b * kGpb;
             bool ok = true;
             if (i >= S) ok = mbar_wait_sleep(&empty[s], (uint32_t)((i / S) - 1) & 1u, kWaitCycles);
-            if (ok) ok = mbar_wait_sleep(&rawbar[r], (uint32_t)(i / RD) & 1u, kWaitCycles);
+            if (ok) ok = mbar_wait_sleep(&rawbar[r], (uint32_t)(b / RD) & 1u, kWaitCycles);
             if (!__all_sync(0xffffffffu, ok)) {  // warp-uniform stop; the MMA side times out
                 if (lane == 0) s_err = 1;
                 break;
             }
             tc_fence_after();  // the MMAs that read this stage's TMEM columns are complete
-            const uint32_t *d = reinterpret_cast<const uint32_t *>(raw + (size_t)r * kRawBytes) + t * WR;
+            const uint32_t *d =
+                reinterpret_cast<const uint32_t *>(raw + (size_t)r * kBlkBytes) + t * w_rs + c * w_gs;
             uint32_t wv[WR];
 #pragma unroll
             for (int q = 0; q < WR; ++q) wv[q] = d[q];  // [0] header, then nibble words
             __syncwarp();
-            if (lane == 0) mbar_arrive_plain(&rawfree[r]);  // block slot r read
+            if (lane == 0 && (c == kGpb - 1 || i == ng - 1)) mbar_arrive_plain(&rawfree[r]);  // slot r read
             const uint32_t ta = a_lane + (uint32_t)(P.a_col + (s * 2 + half) * KS * 8);
 #pragma unroll
             for (int kk = 0; kk < G / 16; ++kk) {  // 16 codes -> 8 words: (q0,q4) (q1,q5) ...
@@ -557,25 +577,35 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
         if (bad && lane == 0) s_err = 1;
     } else if (lane == 0) {
         // ---------------- loader: weight blocks RD - 1 groups ahead, X planes per stage
-        const uint8_t *wblk = job.w + (size_t)(local % mt) * ng * kRawBytes;  // this row tile
-        auto issue_raw = [&](int g) {
-            uint64_t *bar = &rawbar[g % RD];
-            uint8_t *dst = raw + (size_t)(g % RD) * kRawBytes;
-            const uint8_t *src = wblk + (size_t)g * kRawBytes;
-            mbar_arrive_expect_tx(bar, kRawBytes);
-            for (uint32_t o = 0; o < kRawBytes; o += 16384u)
-                bulk_g2s(dst + o, src + o, min(16384u, kRawBytes - o), bar);
+        // weight block b: groups 4b .. 4b+3 of this row tile.  Tensor map: the box at
+        // word 4b * WR of rows m0 .. m0+255 of matrix tz (x a multiple of 16 bytes; rows past
+        // M read as zeros).  Repacked: the tile's groups are back to back, one bulk copy.
+        const uint8_t *wblk = job.w + (size_t)(local % mt) * ng * kRawBytes;
+        if (tmw) tmap_acquire(job.tmap);
+        auto issue_raw = [&](int b) {
+            uint64_t *bar = &rawbar[b % RD];
+            uint8_t *dst = raw + (size_t)(b % RD) * kBlkBytes;
+            if (tmw) {
+                mbar_arrive_expect_tx(bar, kBlkBytes);
+                tma_load_3d(dst, job.tmap, b * kGpb * WR, m0, job.tz, bar);
+            } else {
+                const uint32_t bytes = (uint32_t)min(kGpb, ng - b * kGpb) * kRawBytes;
+                const uint8_t *src = wblk + (size_t)b * kBlkBytes;
+                mbar_arrive_expect_tx(bar, bytes);
+                for (uint32_t o = 0; o < bytes; o += 16384u)
+                    bulk_g2s(dst + o, src + o, min(16384u, bytes - o), bar);
+            }
         };
         int raw_issued = 0, b_issued = 0;
         bool ok = true;
-        for (int g = 0; g < RD - 1 && g < ng; ++g) issue_raw(g), raw_issued = g + 1;
+        for (int b = 0; b < RD - 1 && b < nblk; ++b) issue_raw(b), raw_issued = b + 1;
         for (int g = 0; g < ng && ok; ++g) {
-            const int gr = g + RD - 1;  // weight block into the slot group g - 1 used
-            if (gr < ng) {
-                if (g >= 1) ok = mbar_wait_sleep(&rawfree[(g - 1) % RD], (uint32_t)((g - 1) / RD) & 1u, kWaitCycles);
+            const int b = g / kGpb, br = b + RD - 1;  // block br into the slot block b - 1 used
+            if (g == b * kGpb && br < nblk) {
+                if (b >= 1) ok = mbar_wait_sleep(&rawfree[(b - 1) % RD], (uint32_t)((b - 1) / RD) & 1u, kWaitCycles);
                 if (!ok) break;
-                issue_raw(gr);
-                raw_issued = gr + 1;
+                issue_raw(br);
+                raw_issued = br + 1;
             }
             const int s = g % S;  // X planes of group g into stage s
             if (g >= S) ok = mbar_wait_sleep(&empty[s], (uint32_t)((g / S) - 1) & 1u, kWaitCycles);
@@ -589,8 +619,8 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
         }
         if (!ok) s_err = 1;
         // copies still in flight land before shared memory is released
-        for (int g = max(0, raw_issued - RD); g < raw_issued; ++g)
-            if (!mbar_wait_sleep(&rawbar[g % RD], (uint32_t)(g / RD) & 1u, kWaitCycles)) s_err = 1;
+        for (int b = max(0, raw_issued - RD); b < raw_issued; ++b)
+            if (!mbar_wait_sleep(&rawbar[b % RD], (uint32_t)(b / RD) & 1u, kWaitCycles)) s_err = 1;
         for (int g = max(0, b_issued - S); g < b_issued; ++g)
             if (!mbar_wait_sleep(&full[g % S], (uint32_t)(g / S) & 1u, kWaitCycles)) s_err = 1;
     }
@@ -618,7 +648,7 @@ int launch_grouped_g(MmParams &P, int total_tiles, cudaStream_t st, int gi) {
     int limit = 0;
     TQ_CUDA_TRY(smem_limit_once(mm_i4_tc_kernel<G>, g_mm_smem_set[gi], &limit));
     const int fixed = 1024 + kSclRing * kTileRows * 4;
-    const int raw_group = kTileRows * (4 + G / 2);  // bytes of one staged weight block
+    const int raw_group = kGpb * kTileRows * (4 + G / 2);  // bytes of one staged weight block
     // TMEM: 4 nt accumulator columns (two row halves of [hi | lo]), then per stage two row
     // halves of (G/16 + 1) K steps of 8 columns of A
     const int a_stage_cols = 2 * (G / 16 + 1) * 8;
@@ -660,6 +690,50 @@ size_t mm_repacked_bytes(int M, int K, int G) {
     const size_t ng = (size_t)(K + G - 1) / G;
     const size_t mt = (size_t)(M + kTileRows - 1) / kTileRows;
     return mt * ng * kTileRows * (size_t)(4 + G / 2);
+}
+
+bool mm_encode_weight_map(const uint8_t *w, int M, int K, int G, int E, size_t stride,
+                          void *map128) {
+    if (!mm_group_supported(G) || M <= 0 || K <= 0 || E <= 0) return false;
+    const int ng = (K + G - 1) / G, wr = (4 + G / 2) / 4;
+    const size_t row = (size_t)ng * wr * 4;  // bytes of one interleaved row
+    if (ng % kGpb != 0 || row % 16 != 0 || (((uintptr_t)w) & 15) != 0) return false;
+    // matrices apart by `stride` (one matrix: its own length, rounded up to 16 bytes)
+    const size_t zs = E > 1 ? stride : ((row * (size_t)M + 15) & ~(size_t)15);
+    if (zs % 16 != 0 || zs < row * (size_t)M) return false;
+    // 32-bit words: x over a row's ng * WR words, y over rows, z over matrices; the box is
+    // kGpb groups (a multiple of 16 bytes for every supported G) of 256 rows
+    const cuuint64_t dims[3] = {(cuuint64_t)ng * wr, (cuuint64_t)M, (cuuint64_t)E};
+    const cuuint64_t strides[2] = {(cuuint64_t)row, (cuuint64_t)zs};
+    const cuuint32_t box[3] = {(cuuint32_t)(kGpb * wr), (cuuint32_t)kTileRows, 1u};
+    const cuuint32_t elem[3] = {1u, 1u, 1u};
+    // the driver's encoder, looked up at run time (the library links no driver API, so it
+    // loads on hosts without a GPU driver)
+    using Encode = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+    static Encode encode = [] {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault,
+                                             &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            cudaGetLastError();
+            fn = nullptr;
+        }
+        return reinterpret_cast<Encode>(fn);
+    }();
+    if (!encode) return false;
+    CUtensorMap m;
+    const CUresult r = encode(
+        &m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<uint8_t *>(w), dims, strides, box, elem,
+        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return false;
+    static_assert(sizeof(CUtensorMap) == 128, "CUtensorMap size");
+    memcpy(map128, &m, sizeof(m));
+    return true;
 }
 
 int launch_mm_repack_w(const uint8_t *w, int M, int K, int G, uint8_t *out, cudaStream_t st) {

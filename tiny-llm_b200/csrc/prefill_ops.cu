@@ -393,7 +393,10 @@ __global__ void __launch_bounds__(kPlanThreads) moe_plan_kernel(const MoePlanArg
         const int ct = (((cnt + 15) & ~15) + a.nt - 1) / a.nt;
         for (int h = 0; h < 2; ++h) {
             MmJob j;
-            j.w = (h ? a.wu : a.wg) + (size_t)(e - (a.e_local ? a.e0 : 0)) * a.wgu_stride;
+            const int el = e - (a.e_local ? a.e0 : 0);  // the rank's copy of expert e
+            j.w = (h ? a.wu : a.wg) + (size_t)el * a.wgu_stride;
+            j.tmap = h ? a.tmu : a.tmg;
+            j.tz = el;
             j.y = (h ? a.ubuf : a.hbuf) + (size_t)off * a.mi;
             j.M = a.mi;
             j.N = cnt;
@@ -406,7 +409,10 @@ __global__ void __launch_bounds__(kPlanThreads) moe_plan_kernel(const MoePlanArg
             for (int i = 0; i < mt_gu * ct; ++i) a.tile_gu[j.tile_begin + i] = 2 * jx + h;
         }
         MmJob j;
-        j.w = a.wd + (size_t)(e - (a.e_local ? a.e0 : 0)) * a.wd_stride;
+        const int el = e - (a.e_local ? a.e0 : 0);
+        j.w = a.wd + (size_t)el * a.wd_stride;
+        j.tmap = a.tmd;
+        j.tz = el;
         j.y = a.obuf + (size_t)off * a.H;
         j.M = a.H;
         j.N = cnt;

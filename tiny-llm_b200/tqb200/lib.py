@@ -79,6 +79,7 @@ PROTOTYPES = {
     "tqb200_engine_stream": ([_vp, C.POINTER(_vp)], _i),
     "tqb200_engine_kv_cache": ([_vp, C.POINTER(_vp), C.POINTER(C.c_size_t)], _i),
     "tqb200_engine_weight_bytes": ([_vp, C.POINTER(C.c_size_t)], _i),
+    "tqb200_engine_prefill_copy_bytes": ([_vp, C.POINTER(C.c_size_t)], _i),
     "tqb200_engine_generate": ([_vp, _i, _i, _i32, C.POINTER(_fl)], _i),
     "tqb200_engine_prefill": ([_vp, _i32, _i, C.POINTER(_i)], _i),
     "tqb200_engine_profile_prefill": ([_vp, _i32, _i, _f, _i, C.POINTER(_i)], _i),
@@ -510,6 +511,12 @@ class Engine:
     def weight_bytes(self) -> int:
         n = C.c_size_t()
         _check(load().tqb200_engine_weight_bytes(self.h, C.byref(n)))
+        return n.value
+
+    def prefill_copy_bytes(self) -> int:
+        """Bytes of repacked weight copies the batched prefill made (0: all read in place)."""
+        n = C.c_size_t()
+        _check(load().tqb200_engine_prefill_copy_bytes(self.h, C.byref(n)))
         return n.value
 
     def close(self):
