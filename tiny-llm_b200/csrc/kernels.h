@@ -281,9 +281,12 @@ int mm_tile_width(int M, int N);
 // X [K x N] (column n at x + (cols ? cols[n] : n) * ldx) -> the bf16 hi/lo planes
 int launch_mm_pack_x(const float *x, const int *cols, int ldx, int K, int N, int G,
                      uint16_t *bhi, uint16_t *blo, cudaStream_t st, const float *u = nullptr);
+// map128: optional tensor map (host copy) of a single job's weights, passed in the
+// kernel's parameters (the job's tmap is then ignored)
 int launch_matmul_i4_grouped(const MmJob *host_jobs, const MmJob *dev_jobs, int n_jobs, int K,
                              int G, int nt, const uint16_t *bhi, const uint16_t *blo,
-                             int total_tiles, int *status, cudaStream_t st);
+                             int total_tiles, int *status, cudaStream_t st,
+                             const void *map128 = nullptr);
 // Device-planned launch: the job of tile i is dev_tile_job[i]; tiles at or beyond
 // *dev_n_tiles (written on the device, <= max_tiles) return at once.
 int launch_matmul_i4_planned(const MmJob *dev_jobs, const int *dev_tile_job, const int *dev_n_tiles,

@@ -96,6 +96,10 @@ struct MmParams {
     uint32_t tmem_cols;
     int a_col;             // first TMEM column of the A stages (after the accumulators)
     int *status;
+    // single-job launch: the weight tensor map itself (used when tm0_set; a map in the
+    // kernel's parameters needs no proxy fence)
+    int tm0_set;
+    alignas(64) uint8_t tm0[128];
 };
 
 // ---------------------------------------------------------------- tcgen05 wrappers
@@ -383,7 +387,8 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
     // a block holds groups 4b .. 4b+3 of the tile's 256 rows: from the tensor map as
     // [row][4 groups] (row t's group c at word t * 4 WR + c * WR), repacked as
     // [group][row] (at word c * 256 WR + t * WR)
-    const bool tmw = job.tmap != nullptr;
+    const void *tmap = P.tm0_set ? static_cast<const void *>(P.tm0) : job.tmap;
+    const bool tmw = tmap != nullptr;
     const int nblk = (ng + kGpb - 1) / kGpb;
     const int w_rs = tmw ? kGpb * WR : WR, w_gs = tmw ? WR : kTileRows * WR;
 
@@ -581,13 +586,13 @@ __global__ void __launch_bounds__(kMmThreads, 1) mm_i4_tc_kernel(const __grid_co
         // word 4b * WR of rows m0 .. m0+255 of matrix tz (x a multiple of 16 bytes; rows past
         // M read as zeros).  Repacked: the tile's groups are back to back, one bulk copy.
         const uint8_t *wblk = job.w + (size_t)(local % mt) * ng * kRawBytes;
-        if (tmw) tmap_acquire(job.tmap);
+        if (tmw && !P.tm0_set) tmap_acquire(tmap);  // written to global memory by the host
         auto issue_raw = [&](int b) {
             uint64_t *bar = &rawbar[b % RD];
             uint8_t *dst = raw + (size_t)(b % RD) * kBlkBytes;
             if (tmw) {
                 mbar_arrive_expect_tx(bar, kBlkBytes);
-                tma_load_3d(dst, job.tmap, b * kGpb * WR, m0, job.tz, bar);
+                tma_load_3d(dst, tmap, b * kGpb * WR, m0, job.tz, bar);
             } else {
                 const uint32_t bytes = (uint32_t)min(kGpb, ng - b * kGpb) * kRawBytes;
                 const uint8_t *src = wblk + (size_t)b * kBlkBytes;
@@ -780,7 +785,7 @@ int mm_tile_width(int M, int N) {
 
 int launch_matmul_i4_grouped(const MmJob *host_jobs, const MmJob *dev_jobs, int n_jobs, int K,
                              int G, int nt, const uint16_t *bhi, const uint16_t *blo, int total_tiles,
-                             int *status, cudaStream_t st) {
+                             int *status, cudaStream_t st, const void *map128) {
     TQ_CHECK_ARG(n_jobs >= 1, "matmul_i4: no jobs");
     TQ_CHECK_ARG(mm_group_supported(G), "matmul_i4 (tensor cores): group_size %d not 32, 64 or 128", G);
     TQ_CHECK_ARG(nt % 16 == 0 && nt >= 16 && nt <= kMmMaxCols, "matmul_i4: bad tile width %d", nt);
@@ -788,6 +793,11 @@ int launch_matmul_i4_grouped(const MmJob *host_jobs, const MmJob *dev_jobs, int 
     if (total_tiles == 0) return TQB200_OK;
     MmParams P{};
     if (dev_jobs == nullptr) P.job0 = host_jobs[0];
+    if (map128) {
+        TQ_CHECK_ARG(dev_jobs == nullptr, "matmul_i4: a parameter tensor map serves one job");
+        memcpy(P.tm0, map128, sizeof(P.tm0));
+        P.tm0_set = 1;
+    }
     P.jobs = dev_jobs;
     P.n_jobs = dev_jobs ? n_jobs : 1;
     P.K = K;
@@ -888,7 +898,11 @@ int launch_matmul_i4(const uint8_t *w, const float *x, float *y, int M, int K, i
     const size_t plane = mm_x_planes_bytes(K, N, G) / 2;
     uint16_t *bhi = reinterpret_cast<uint16_t *>(wt + wbytes);
     uint16_t *blo = reinterpret_cast<uint16_t *>(wt + wbytes + plane);
-    int r = launch_mm_repack_w(w, M, K, G, wt, st);
+    // the weights in place through a tensor map where their rows allow one, else a
+    // repacked copy in the scratch
+    alignas(64) uint8_t map[128];
+    const bool mapped = mm_encode_weight_map(w, M, K, G, 1, 0, map);
+    int r = mapped ? TQB200_OK : launch_mm_repack_w(w, M, K, G, wt, st);
     if (r != TQB200_OK) return r;
     r = launch_mm_pack_x(x, nullptr, K, K, N, G, bhi, blo, st);
     if (r != TQB200_OK) return r;
@@ -902,7 +916,8 @@ int launch_matmul_i4(const uint8_t *w, const float *x, float *y, int M, int K, i
     j.tile_begin = 0;
     j.b_off = 0;
     const int tiles = ((M + kTileRows - 1) / kTileRows) * ((npad + nt - 1) / nt);
-    return launch_matmul_i4_grouped(&j, nullptr, 1, K, G, nt, bhi, blo, tiles, status, st);
+    return launch_matmul_i4_grouped(&j, nullptr, 1, K, G, nt, bhi, blo, tiles, status, st,
+                                    mapped ? map : nullptr);
 }
 
 }  // namespace tqb200
