@@ -310,6 +310,36 @@ def matvec_extras(pk, warmup: int) -> dict:
     return out
 
 
+def config_extras(args, pk, pk_kind) -> dict:
+    """BASELINE configs 2, 3 and 5 beside the config-4 decode line, each through its own
+    workload's bench at a short run (its main numbers only; the full lines come from
+    --workload <name>)."""
+    import argparse as _ap
+    out = {}
+    runs = (("config2_decode", "decode-qwen2.5-0.5b", bench_decode),
+            ("config3_decode", "decode-qwen3-0.6b-vq2", bench_decode),
+            ("config5_prefill", "prefill-qwen3-30b-a3b", bench_prefill))
+    for key, workload, fn in runs:
+        sub = _ap.Namespace(**vars(args))
+        sub.workload, sub.extras, sub.ctx, sub.layers = workload, False, None, None
+        sub.steps, sub.warmup = 5, 3
+        try:
+            r = fn(sub, 0, None, pk, pk_kind)
+        except Exception as ex:  # the main line still prints; the failure is recorded
+            out[key] = {"workload": workload, "error": f"{type(ex).__name__}: {ex}"[:300]}
+            continue
+        e = {"workload": workload, "metric": r["metric"], "value": r["value"],
+             "unit": r["unit"], "steps": sub.steps, "warmup": sub.warmup,
+             "e2e": r["e2e"]["value"], "roofline_frac": r["roofline"]["frac"],
+             "roofline_kernel": r["roofline"]["kernel"], "clocks": r["clocks"]}
+        if "context" in r["config"]:
+            e["context"] = r["config"]["context"]
+        if "decode_after_prefill_ms_per_token" in r["config"]:
+            e["decode_after_prefill_ms_per_token"] = r["config"]["decode_after_prefill_ms_per_token"]
+        out[key] = e
+    return out
+
+
 def bench_matvec(args, rank, pg, pk, pk_kind):
     import torch
     from tqb200 import lib, synth
@@ -768,6 +798,8 @@ def bench_decode(args, rank, pg, pk, pk_kind):
     del eng
     if world == 1 and args.extras:
         out.update(matvec_extras(pk, W))
+        if args.workload == "decode-qwen3-4b":
+            out.update(config_extras(args, pk, pk_kind))
     return out
 
 
@@ -827,7 +859,7 @@ def bench_prefill(args, rank, pg, pk, pk_kind):
     ptr = C.c_void_p()
     lib._check(lib.load().tqb200_engine_stream(eng.h, C.byref(ptr)))
     stream = torch.cuda.ExternalStream(ptr.value)
-    for _ in range(W):  # the first one also makes the tile-contiguous weight copies
+    for _ in range(W):  # the first one also writes the prefill's weight tensor maps
         eng.reset()
         eng.prefill(prompt)
     torch.cuda.synchronize()
