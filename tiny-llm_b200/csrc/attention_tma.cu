@@ -583,30 +583,44 @@ __global__ void __launch_bounds__(kThreads, sizeof(KV) == 2 ? 2 : 1) attn_tma_ke
         *cluster.map_shared_rank(rcv_l + split * G + g, r) = pl[g];
     }
     cluster.sync();  // every push has landed
-    if (tid < G) {
-        const int g = tid;
-        float M = -INFINITY;
-        for (int s2 = 0; s2 < ns; ++s2) M = fmaxf(M, rcv_m[s2 * G + g]);
-        float L = 0.0f;
-        for (int s2 = 0; s2 < ns; ++s2) {
-            const float m = rcv_m[s2 * G + g];
-            const float w = m == -INFINITY ? 0.0f : expf(m - M);
-            wgt[s2 * G + g] = w;
-            L = fmaf(rcv_l[s2 * G + g], w, L);
-        }
-        s_l[g] = L;
+    // the splits' weights exp(m_s - M) per head: 16 lanes per head (lane s2 = split s2),
+    // the max and the weighted sum of l as shuffle trees
+    static_assert(kMaxSplit == 16 && G * 16 <= kThreads, "one 16-lane group per head");
+    if (tid < ((G * 16 + 31) & ~31)) {  // whole warps: every lane takes the shuffles
+        const int g = tid >> 4, s2 = tid & 15;
+        const bool ok = g < G && s2 < ns;
+        const float m = ok ? rcv_m[s2 * G + g] : -INFINITY;
+        float M = m;
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        const float w = m == -INFINITY ? 0.0f : expf(m - M);
+        float L = ok ? rcv_l[s2 * G + g] * w : 0.0f;
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        if (ok) wgt[s2 * G + g] = w;
+        if (g < G && s2 == 0) s_l[g] = L;
     }
     __syncthreads();
-    const int i_end = min(G * HD, (split + 1) * per);
-    for (int i = split * per + tid; i < i_end; i += kThreads) {
-        const int g = i / HD, j = i - split * per;
+    // this rank's slice of the output: 8 lanes per value, each over every 8th split,
+    // then a 3-level shuffle sum
+    const int cnt = max(0, min(G * HD, (split + 1) * per) - split * per);
+    for (int base = 0; base < cnt; base += kThreads / 8) {  // uniform over the CTA
+        const int j = base + (tid >> 3), sub = tid & 7;
+        const int i = split * per + j;
+        const int g = i / HD;
         float O = 0.0f;
-        for (int s2 = 0; s2 < ns; ++s2) O = fmaf(rcv_o[s2 * per + j], wgt[s2 * G + g], O);
-        if constexpr (XCHG) {
-            if (P.put) xput_val(*P.put, P.out + (size_t)kh * G * HD + i, O / s_l[g]);
-            else P.out[(size_t)kh * G * HD + i] = O / s_l[g];
-        } else {
-            P.out[(size_t)kh * G * HD + i] = O / s_l[g];
+        if (j < cnt)
+            for (int s2 = sub; s2 < ns; s2 += 8) O = fmaf(rcv_o[s2 * per + j], wgt[s2 * G + g], O);
+        O += __shfl_xor_sync(0xffffffffu, O, 4);
+        O += __shfl_xor_sync(0xffffffffu, O, 2);
+        O += __shfl_xor_sync(0xffffffffu, O, 1);
+        if (j < cnt && sub == 0) {
+            if constexpr (XCHG) {
+                if (P.put) xput_val(*P.put, P.out + (size_t)kh * G * HD + i, O / s_l[g]);
+                else P.out[(size_t)kh * G * HD + i] = O / s_l[g];
+            } else {
+                P.out[(size_t)kh * G * HD + i] = O / s_l[g];
+            }
         }
     }
     if constexpr (XCHG)
