@@ -312,8 +312,8 @@ def matvec_extras(pk, warmup: int) -> dict:
 
 def config_extras(args, pk, pk_kind) -> dict:
     """BASELINE configs 2, 3 and 5 beside the config-4 decode line, each through its own
-    workload's bench at a short run (its main numbers only; the full lines come from
-    --workload <name>)."""
+    workload's bench at a short run (20 decode steps after 5 warm-up, or 5 prompts after
+    3; its main numbers only; the full lines come from --workload <name>)."""
     import argparse as _ap
     out = {}
     runs = (("config2_decode", "decode-qwen2.5-0.5b", bench_decode),
@@ -322,7 +322,7 @@ def config_extras(args, pk, pk_kind) -> dict:
     for key, workload, fn in runs:
         sub = _ap.Namespace(**vars(args))
         sub.workload, sub.extras, sub.ctx, sub.layers = workload, False, None, None
-        sub.steps, sub.warmup = 5, 3
+        sub.steps, sub.warmup = (5, 3) if fn is bench_prefill else (20, 5)
         try:
             r = fn(sub, 0, None, pk, pk_kind)
         except Exception as ex:  # the main line still prints; the failure is recorded
